@@ -1,0 +1,167 @@
+/*
+ * libsupra_attn — C ABI of the B200 (sm_100a) fused attention operator of Supra2-Img.
+ *
+ * The operator surface mirrors the reference's JavaScript entry point
+ *   attention(gpu, {q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff, kOff, vOff, oOff, scale, bias, out})
+ * (app/gpu/ops.js:103-149) and the runtime it records into (app/gpu/device.js:41-269):
+ *
+ *   - q is [Lq, ldq] row-major fp32; head h of query row i is q[qOff + i*ldq + h*D + 0..D).
+ *     k / v likewise with ldk / ldv and kOff / vOff, over Lk key rows.
+ *   - The output row i is written at out[oOff + i*(H*D) + h*D + 0..D): row stride H*D.
+ *   - scale multiplies the scores; the reference's default is 1/sqrt(D) (app/gpu/ops.js:109).
+ *   - bias, when present, is an additive score bias laid out [H, Lq, Lk] (T5 relative
+ *     positions, app/models/t5.js:55-65); it is added after scaling (app/gpu/kernels.js:34).
+ *   - All offsets, strides and sizes are in ELEMENTS (floats), never bytes.
+ *
+ * Execution model ("record now, submit at flush", app/gpu/device.js:1-5,207-253):
+ *   supra_attn_enqueue() validates a problem synchronously and records it; nothing runs yet.
+ *   supra_attn_flush() groups every recorded problem by kernel configuration and issues one
+ *   grouped launch per group on the context's stream; supra_attn_sync() waits and reports
+ *   device-side failures (the reference surfaces asynchronous errors at read/sync,
+ *   app/gpu/device.js:186,258,262-268). A recorded problem that reads memory written by an
+ *   earlier recorded problem (or writes memory an earlier one touches) flushes the queue
+ *   first, so results never depend on grouping.
+ *
+ * Every function returns a status code (SUPRA_ATTN_OK on success) and never throws or aborts.
+ * supra_attn_last_error() returns the message of the most recent failure on a context.
+ * A context is bound to one device and is not thread-safe (one context per host thread),
+ * like the reference's single-threaded GPU object.
+ */
+#ifndef SUPRA_ATTN_H
+#define SUPRA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SUPRA_ATTN_API __attribute__((visibility("default")))
+#else
+#define SUPRA_ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define SUPRA_ATTN_OK 0
+#define SUPRA_ATTN_EINVAL 1   /* bad argument: sizes, alignment, bounds, aliasing, unknown flag */
+#define SUPRA_ATTN_ENOMEM 2   /* device or pinned host allocation failed                      */
+#define SUPRA_ATTN_ECUDA 3    /* a CUDA runtime/driver call failed                            */
+#define SUPRA_ATTN_ETIMEOUT 4 /* a device-side bounded wait ran out (reported at sync)        */
+#define SUPRA_ATTN_EDEVICE 5  /* the device reported an error status (reported at sync)       */
+#define SUPRA_ATTN_ESTATE 6   /* call not allowed in the context's current state              */
+
+/* ---- numeric variants -------------------------------------------------------------------- */
+#define SUPRA_ATTN_FP32 0 /* FFMA kernel, fp32 throughout: matches torch CPU fp32 to <=1e-5 */
+#define SUPRA_ATTN_TF32 1 /* tcgen05 tensor-core kernel with TF32 operands, fp32 accumulate */
+
+/* ---- descriptor flags -------------------------------------------------------------------- */
+#define SUPRA_ATTN_F_DEFAULT_SCALE 0x1u /* ignore .scale, use 1/sqrt(D) (ops.js:109 default) */
+
+typedef struct supra_attn_ctx supra_attn_ctx;
+
+/*
+ * One attention problem: all H heads of one call of ops.attention (app/gpu/ops.js:109).
+ * The *_size fields give the number of floats the caller owns at each pointer; every
+ * element the problem reads or writes is checked against them at enqueue, so an
+ * out-of-range offset is an EINVAL instead of a device fault. Pass 0 only for bias when
+ * bias is NULL.
+ */
+typedef struct supra_attn_desc {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* out;
+  const float* bias; /* NULL, or [H, Lq, Lk] additive score bias */
+  int64_t q_size, k_size, v_size, out_size, bias_size;
+  int64_t ldq, ldk, ldv;
+  int64_t q_off, k_off, v_off, o_off;
+  int32_t Lq, Lk, H, D;
+  float scale;
+  int32_t variant; /* SUPRA_ATTN_FP32 or SUPRA_ATTN_TF32 */
+  uint32_t flags;  /* SUPRA_ATTN_F_* */
+  uint32_t reserved;
+} supra_attn_desc;
+
+/* ---- context ----------------------------------------------------------------------------- */
+/* Replaces GPU.create (app/gpu/device.js:92-118): binds a context to a CUDA device and
+ * creates its stream, descriptor ring and device status word. */
+SUPRA_ATTN_API int supra_attn_create(int device, supra_attn_ctx** out);
+/* Flushes, synchronises and frees everything the context owns. NULL is a no-op. */
+SUPRA_ATTN_API int supra_attn_destroy(supra_attn_ctx* ctx);
+/* Runs subsequent launches and copies on a caller-owned cudaStream_t (NULL = the context's
+ * own stream). Flushes pending work on the previous stream first. */
+SUPRA_ATTN_API int supra_attn_set_stream(supra_attn_ctx* ctx, void* cuda_stream);
+SUPRA_ATTN_API const char* supra_attn_last_error(const supra_attn_ctx* ctx);
+/* Message for a status code. */
+SUPRA_ATTN_API const char* supra_attn_status_string(int status);
+
+/* ---- tensors (the Tensor/BufferPool surface, app/gpu/device.js:41-88,144-191) ------------ */
+/* gpu.empty(shape): a pooled device buffer of n floats (size-bucketed like BufferPool.round). */
+SUPRA_ATTN_API int supra_attn_tensor_alloc(supra_attn_ctx* ctx, int64_t n, float** dptr);
+/* Tensor.release(): flushes recorded work, then returns the buffer to the pool. */
+SUPRA_ATTN_API int supra_attn_tensor_free(supra_attn_ctx* ctx, float* dptr);
+/* fromArray / write: flushes, then copies n floats host->device (stream-ordered). */
+SUPRA_ATTN_API int supra_attn_upload(supra_attn_ctx* ctx, float* dst, const float* src, int64_t n);
+/* read(): flushes, copies n floats device->host and waits for them. */
+SUPRA_ATTN_API int supra_attn_download(supra_attn_ctx* ctx, float* dst, const float* src, int64_t n);
+/* Page-locked host memory for fast upload/download (freed with supra_attn_host_free). */
+SUPRA_ATTN_API int supra_attn_host_alloc(supra_attn_ctx* ctx, int64_t n, float** hptr);
+SUPRA_ATTN_API int supra_attn_host_free(supra_attn_ctx* ctx, float* hptr);
+
+/* ---- the operator (app/gpu/ops.js:103-149) ------------------------------------------------ */
+/* Validates and records one problem. Synchronous EINVAL mirrors the reference's synchronous
+ * throw (app/gpu/ops.js:122, app/gpu/device.js:208). */
+SUPRA_ATTN_API int supra_attn_enqueue(supra_attn_ctx* ctx, const supra_attn_desc* desc);
+/* Validates a descriptor exactly as supra_attn_enqueue does, without a context or a device
+ * (pure host function). Writes the message of a failure into msg (cap bytes, may be NULL). */
+SUPRA_ATTN_API int supra_attn_check_desc(const supra_attn_desc* desc, char* msg, int32_t cap);
+/* Records n problems (an explicit varlen batch); all or none are recorded. */
+SUPRA_ATTN_API int supra_attn_enqueue_batch(supra_attn_ctx* ctx, const supra_attn_desc* descs, int32_t n);
+/* GPU.flush (app/gpu/device.js:243-253): one grouped launch per kernel configuration. */
+SUPRA_ATTN_API int supra_attn_flush(supra_attn_ctx* ctx);
+/* GPU.sync (app/gpu/device.js:255-259): flush, wait, and check the device status word.
+ * *device_status (may be NULL) receives the raw device status (0 = clean). */
+SUPRA_ATTN_API int supra_attn_sync(supra_attn_ctx* ctx, int32_t* device_status);
+/* Number of problems recorded and not yet flushed. */
+SUPRA_ATTN_API int supra_attn_pending(const supra_attn_ctx* ctx, int32_t* n);
+
+/* ---- T5 relative-position bias (app/models/t5.js:14-23,55-65) ----------------------------- */
+/* relativeBucket(rel, buckets, maxDistance) (app/models/t5.js:14-23), bidirectional, with the
+ * same float32 rounding steps. Pure host function. Returns the bucket, or -1 on bad input. */
+SUPRA_ATTN_API int32_t supra_attn_relative_bucket(int32_t rel, int32_t buckets, int32_t max_distance);
+/* T5Encoder.positionBias(L) (app/models/t5.js:55-65) computed on the device:
+ *   out[(h*L + i)*L + j] = table[relativeBucket(j - i)*H + h]
+ * table is a DEVICE pointer to table_size >= buckets*H floats laid out [buckets, H]
+ * (encoder.block.0...relative_attention_bias.weight, app/models/t5.js:44); out is a device
+ * pointer to out_size >= H*L*L floats. Stream-ordered with the context's other work
+ * (recorded attention is flushed first). */
+SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* table, int64_t table_size,
+                                            int32_t buckets, int32_t max_distance, int32_t H, int32_t L,
+                                            float* out, int64_t out_size);
+
+/* ---- profiling (the reference's Profiler, app/gpu/device.js:91-99,222-233,272-325) -------- */
+/* When on, every grouped launch is bracketed by CUDA events on the launching stream and
+ * aggregated by kernel name with its algorithmic FLOPs (4*Lq*Lk*D*H, app/gpu/ops.js:116) and
+ * bytes (Q+K+V+O read/written once, plus the bias). */
+SUPRA_ATTN_API int supra_attn_profile_enable(supra_attn_ctx* ctx, int32_t on);
+typedef struct supra_attn_profile_entry {
+  char name[48];
+  int64_t launches;
+  double ms;    /* summed device time */
+  double flops; /* summed algorithmic FLOPs */
+  double bytes; /* summed algorithmic bytes */
+} supra_attn_profile_entry;
+/* Synchronises, then copies up to cap entries (sorted by time) and sets *n. */
+SUPRA_ATTN_API int supra_attn_profile_report(supra_attn_ctx* ctx, supra_attn_profile_entry* entries,
+                              int32_t cap, int32_t* n);
+SUPRA_ATTN_API int supra_attn_profile_reset(supra_attn_ctx* ctx);
+/* Total kernels this context has launched since creation (all kinds). */
+SUPRA_ATTN_API int supra_attn_launch_count(const supra_attn_ctx* ctx, int64_t* n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SUPRA_ATTN_H */

@@ -1,0 +1,89 @@
+// Internal interface between the host runtime (supra_attn.cpp) and the CUDA kernels.
+// Plain structs that the host packs into the descriptor ring and the kernels read from HBM.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace supra {
+
+// Device status codes written to the context's status word (status[0]).
+enum DevStatus : int32_t {
+  DEV_OK = 0,
+  DEV_TIMEOUT = 1,   // a bounded mbarrier / copy wait ran out
+  DEV_BAD_TILE = 2,  // a tile index outside the launch's problem list
+};
+
+// One attention problem (all heads of one ops.attention call) as the fused kernels see it.
+// Element offsets already include the caller's qOff/kOff/vOff/oOff; head h adds h*D.
+struct alignas(16) AttnProb {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;
+  const float* bias;  // [H, Lq, Lk] or nullptr
+  int64_t q_off, k_off, v_off, o_off;
+  int64_t ldq, ldk, ldv, ldo;
+  int32_t Lq, Lk, H, D;
+  float scale;       // score multiplier
+  float scale_log2;  // scale * log2(e): scores are exponentiated with exp2
+  int32_t q_tiles;   // ceil(Lq / tile rows)
+  int32_t pad;
+};
+static_assert(sizeof(AttnProb) % 16 == 0, "AttnProb is packed into the descriptor ring");
+
+// A grouped launch: `n` problems, tile t belongs to the problem p with begin[p] <= t < begin[p+1].
+struct AttnLaunch {
+  const AttnProb* probs;
+  const int32_t* begin;  // n + 1 entries, begin[n] = total tiles
+  int32_t n;
+  int32_t total;
+  int32_t* status;
+};
+
+// One (problem, head, row chunk) unit of the score-materialising path used for D > 128: the
+// scores of `rows` query rows starting at row0 live in scratch at s_off with row stride ldS.
+struct alignas(16) GemmUnit {
+  int64_t s_off;
+  int32_t prob, h, row0, rows;
+  int32_t ldS;
+  int32_t qk_begin;  // prefix of QK^T tiles
+  int32_t pv_begin;  // prefix of PV tiles
+  int32_t row_begin; // prefix of softmax rows
+};
+static_assert(sizeof(GemmUnit) % 16 == 0, "GemmUnit is packed into the descriptor ring");
+
+struct GemmLaunch {
+  const AttnProb* probs;
+  const GemmUnit* units;
+  const int32_t* qk_begin;  // n_units + 1
+  const int32_t* pv_begin;  // n_units + 1
+  const int32_t* row_begin; // n_units + 1
+  float* scratch;
+  int32_t n_units;
+  int32_t qk_total, pv_total, row_total;
+  int32_t* status;
+};
+
+// Fused FP32 kernel configurations (head-dim capacity DT, query rows per CTA MQ).
+enum FusedCfg : int32_t {
+  CFG_D64_Q128 = 0,
+  CFG_D64_Q64 = 1,
+  CFG_D128_Q64 = 2,
+  CFG_COUNT = 3,
+};
+int fused_cfg_tile_rows(int cfg);
+int fused_cfg_head_dim(int cfg);
+
+// Launchers. Each returns the cudaError_t of the launch (cudaSuccess on success).
+cudaError_t launch_attn_fp32(int cfg, bool bias, bool aligned, const AttnLaunch& L, cudaStream_t s);
+const char* attn_fp32_name(int cfg, bool bias, bool aligned);
+
+cudaError_t launch_gemm_qk(bool bias, bool aligned, const GemmLaunch& L, cudaStream_t s);
+cudaError_t launch_softmax_rows(const GemmLaunch& L, cudaStream_t s);
+cudaError_t launch_gemm_pv(bool aligned, const GemmLaunch& L, cudaStream_t s);
+
+cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L,
+                                 float* out, cudaStream_t s);
+
+}  // namespace supra

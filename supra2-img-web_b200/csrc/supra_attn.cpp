@@ -1,0 +1,970 @@
+// libsupra_attn host runtime: the C ABI declared in include/supra_attn.h.
+//
+// It replaces, for the attention operator, the reference's WebGPU runtime (app/gpu/device.js):
+//   - GPU/Tensor/BufferPool  -> context, pooled device buffers with the same size bucketing
+//                               (BufferPool.round, app/gpu/device.js:64-70)
+//   - dispatch + flush       -> enqueue records validated problems; flush issues one grouped
+//                               launch per kernel configuration (app/gpu/device.js:207-253)
+//   - uniform ring           -> a pinned/device descriptor ring, two halves fenced by events
+//                               (app/gpu/device.js:7-8,128-130,210-218)
+//   - checkErrors / lost     -> a device status word read at sync/download
+//                               (app/gpu/device.js:134,186,258,262-268)
+//   - Profiler               -> CUDA events per grouped launch, aggregated by kernel name with
+//                               FLOPs and bytes (app/gpu/device.js:272-325, app/gpu/ops.js:116)
+// and the operator itself (app/gpu/ops.js:103-149): the same arguments, the same defaults,
+// and synchronous errors for invalid calls.
+#include "supra_attn.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+#include "kernels.h"
+
+using supra::AttnLaunch;
+using supra::AttnProb;
+using supra::GemmLaunch;
+using supra::GemmUnit;
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Disjoint, merged [begin, end) byte ranges.
+class IntervalSet {
+ public:
+  void clear() { m_.clear(); }
+  bool empty() const { return m_.empty(); }
+  bool overlaps(uintptr_t b, uintptr_t e) const {
+    if (b >= e || m_.empty()) return false;
+    auto it = m_.upper_bound(b);
+    if (it != m_.end() && it->first < e) return true;
+    if (it != m_.begin()) {
+      --it;
+      if (it->second > b) return true;
+    }
+    return false;
+  }
+  void add(uintptr_t b, uintptr_t e) {
+    if (b >= e) return;
+    auto it = m_.upper_bound(b);
+    if (it != m_.begin()) {
+      auto pv = std::prev(it);
+      if (pv->second >= b) {
+        b = pv->first;
+        e = std::max(e, pv->second);
+        it = m_.erase(pv);
+      }
+    }
+    while (it != m_.end() && it->first <= e) {
+      e = std::max(e, it->second);
+      it = m_.erase(it);
+    }
+    m_.emplace(b, e);
+  }
+
+ private:
+  std::map<uintptr_t, uintptr_t> m_;
+};
+
+struct ByteRange {
+  uintptr_t b = 0, e = 0;
+};
+
+enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1 };
+
+struct Queued {
+  AttnProb p;
+  int path;
+  int cfg;
+  bool bias;
+  bool aligned;
+  double flops;
+  double bytes;
+};
+
+struct ProfStat {
+  int64_t launches = 0;
+  double ms = 0, flops = 0, bytes = 0;
+};
+
+struct PendingEvt {
+  std::string name;
+  double flops, bytes;
+  cudaEvent_t a, b;
+};
+
+size_t pool_round(size_t bytes) {  // BufferPool.round (app/gpu/device.js:64-70)
+  size_t b = std::max<size_t>(256, bytes);
+  size_t p = 1;
+  while (p * 2 <= b) p *= 2;
+  const size_t step = std::max<size_t>(256, p / 8);
+  return (b + step - 1) / step * step;
+}
+
+size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+}  // namespace
+
+struct supra_attn_ctx {
+  int device = 0;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  int32_t* d_status = nullptr;
+  int32_t* h_status = nullptr;
+
+  // descriptor ring: two halves of pinned staging + device memory
+  char* ring_h = nullptr;
+  char* ring_d = nullptr;
+  size_t ring_half = 0;
+  int ring_cur = 0;
+  size_t ring_head = 0;
+  cudaEvent_t ring_ev[2] = {nullptr, nullptr};
+  bool ring_ev_used[2] = {false, false};
+
+  std::vector<Queued> queue;
+  IntervalSet qreads, qwrites;
+
+  std::map<size_t, std::vector<void*>> pool_free;
+  std::unordered_map<void*, size_t> pool_live;
+  std::unordered_set<void*> host_live;
+
+  float* scratch = nullptr;
+  size_t scratch_cap = 0;
+  size_t scratch_budget = size_t(64) << 20;  // per chunk of score-materialising units
+
+  bool profile = false;
+  std::vector<PendingEvt> pend;
+  std::vector<cudaEvent_t> evt_free;
+  std::map<std::string, ProfStat> stats;
+
+  int64_t launches = 0;
+  std::string err;
+};
+
+namespace {
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+    if (prev_ != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev_ >= 0) {
+      int cur = -1;
+      if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+    }
+  }
+
+ private:
+  int prev_ = -1;
+};
+
+int set_err(supra_attn_ctx* c, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return code;
+}
+
+int cuda_err(supra_attn_ctx* c, cudaError_t e, const char* what) {
+  return set_err(c, SUPRA_ATTN_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// ---- descriptor ring ---------------------------------------------------------------------------
+int ring_reserve(supra_attn_ctx* c, size_t bytes, char** host, char** dev) {
+  bytes = align16(bytes);
+  if (bytes > c->ring_half) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_err(c, e, "ring grow: stream sync");
+    size_t half = std::max<size_t>(c->ring_half * 2, align16(bytes));
+    char *nh = nullptr, *nd = nullptr;
+    if (cudaMallocHost(&nh, 2 * half) != cudaSuccess) return set_err(c, SUPRA_ATTN_ENOMEM, "ring: pinned alloc");
+    if (cudaMalloc(&nd, 2 * half) != cudaSuccess) {
+      cudaFreeHost(nh);
+      return set_err(c, SUPRA_ATTN_ENOMEM, "ring: device alloc");
+    }
+    cudaFreeHost(c->ring_h);
+    cudaFree(c->ring_d);
+    c->ring_h = nh;
+    c->ring_d = nd;
+    c->ring_half = half;
+    c->ring_cur = 0;
+    c->ring_head = 0;
+    c->ring_ev_used[0] = c->ring_ev_used[1] = false;
+  }
+  if (c->ring_head + bytes > c->ring_half) {
+    c->ring_cur ^= 1;
+    c->ring_head = 0;
+    if (c->ring_ev_used[c->ring_cur]) {
+      cudaError_t e = cudaEventSynchronize(c->ring_ev[c->ring_cur]);
+      if (e != cudaSuccess) return cuda_err(c, e, "ring: event sync");
+    }
+  }
+  const size_t off = c->ring_cur * c->ring_half + c->ring_head;
+  *host = c->ring_h + off;
+  *dev = c->ring_d + off;
+  c->ring_head += bytes;
+  return SUPRA_ATTN_OK;
+}
+
+// Copies bytes staged at host (inside the ring) to dev, stream-ordered.
+int ring_commit(supra_attn_ctx* c, char* host, char* dev, size_t bytes) {
+  cudaError_t e = cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "ring: upload");
+  e = cudaEventRecord(c->ring_ev[c->ring_cur], c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "ring: event record");
+  c->ring_ev_used[c->ring_cur] = true;
+  return SUPRA_ATTN_OK;
+}
+
+// ---- profiling -------------------------------------------------------------------------------
+cudaEvent_t take_event(supra_attn_ctx* c) {
+  if (!c->evt_free.empty()) {
+    cudaEvent_t e = c->evt_free.back();
+    c->evt_free.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+struct ProfScope {
+  supra_attn_ctx* c;
+  PendingEvt pe;
+  bool on;
+  ProfScope(supra_attn_ctx* ctx, const char* name, double flops, double bytes) : c(ctx), on(ctx->profile) {
+    if (!on) return;
+    pe.name = name;
+    pe.flops = flops;
+    pe.bytes = bytes;
+    pe.a = take_event(c);
+    pe.b = take_event(c);
+    if (!pe.a || !pe.b) {
+      on = false;
+      return;
+    }
+    cudaEventRecord(pe.a, c->stream);
+  }
+  ~ProfScope() {
+    if (!on) return;
+    cudaEventRecord(pe.b, c->stream);
+    c->pend.push_back(pe);
+  }
+};
+
+int collect_profile(supra_attn_ctx* c) {
+  for (auto& pe : c->pend) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(pe.b);
+    if (e != cudaSuccess) return cuda_err(c, e, "profile: event sync");
+    cudaEventElapsedTime(&ms, pe.a, pe.b);
+    ProfStat& s = c->stats[pe.name];
+    s.launches += 1;
+    s.ms += ms;
+    s.flops += pe.flops;
+    s.bytes += pe.bytes;
+    c->evt_free.push_back(pe.a);
+    c->evt_free.push_back(pe.b);
+  }
+  c->pend.clear();
+  return SUPRA_ATTN_OK;
+}
+
+// ---- validation --------------------------------------------------------------------------------
+struct Checked {
+  Queued q;
+  ByteRange reads[4];
+  int nreads = 0;
+  ByteRange write;
+  bool empty = false;  // Lq == 0: nothing to do
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
+  if (!d) return set_err(c, SUPRA_ATTN_EINVAL, "descriptor is NULL");
+  if (d->flags & ~SUPRA_ATTN_F_DEFAULT_SCALE) return set_err(c, SUPRA_ATTN_EINVAL, "unknown flag bits 0x%x", d->flags);
+  if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
+    return set_err(c, SUPRA_ATTN_EINVAL, "unknown variant %d", d->variant);
+  if (d->variant == SUPRA_ATTN_TF32)
+    return set_err(c, SUPRA_ATTN_EINVAL, "the TF32 variant is not available in this build");
+  if (d->Lq < 0 || d->Lq > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lq=%d out of range [0, 2^30]", d->Lq);
+  if (d->Lk < 1 || d->Lk > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lk=%d out of range [1, 2^30]", d->Lk);
+  if (d->H < 1 || d->H > 65536) return set_err(c, SUPRA_ATTN_EINVAL, "H=%d out of range [1, 65536]", d->H);
+  if (d->D < 1 || d->D > 65536) return set_err(c, SUPRA_ATTN_EINVAL, "D=%d out of range [1, 65536]", d->D);
+  if ((int64_t)d->H * d->D > (int64_t(1) << 24)) return set_err(c, SUPRA_ATTN_EINVAL, "H*D too large");
+  const int64_t lim = int64_t(1) << 46;
+  const int64_t lds[3] = {d->ldq, d->ldk, d->ldv};
+  const int64_t offs[4] = {d->q_off, d->k_off, d->v_off, d->o_off};
+  for (int i = 0; i < 3; ++i)
+    if (lds[i] < 0 || lds[i] > lim) return set_err(c, SUPRA_ATTN_EINVAL, "leading dimension out of range");
+  for (int i = 0; i < 4; ++i)
+    if (offs[i] < 0 || offs[i] > lim) return set_err(c, SUPRA_ATTN_EINVAL, "offset out of range (negative?)");
+  if (!d->q || !d->k || !d->v || !d->out) return set_err(c, SUPRA_ATTN_EINVAL, "q, k, v and out must be non-NULL");
+  const void* ptrs[5] = {d->q, d->k, d->v, d->out, d->bias};
+  for (int i = 0; i < 5; ++i)
+    if (ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 3u))
+      return set_err(c, SUPRA_ATTN_EINVAL, "pointers must be 4-byte aligned float arrays");
+  float scale = d->scale;
+  if (d->flags & SUPRA_ATTN_F_DEFAULT_SCALE) scale = (float)(1.0 / std::sqrt((double)d->D));  // ops.js:109
+  if (!std::isfinite(scale)) return set_err(c, SUPRA_ATTN_EINVAL, "scale must be finite");
+
+  const int64_t HD = (int64_t)d->H * d->D;
+  out->empty = (d->Lq == 0);
+  // bounds: the last element each operand touches (app/gpu/ops.js:104-105)
+  auto last = [&](int64_t off, int64_t rows, int64_t ld) { return off + (rows - 1) * ld + HD - 1; };
+  if (!out->empty && last(d->q_off, d->Lq, d->ldq) >= d->q_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "q out of bounds: needs %lld floats, q_size=%lld",
+                   (long long)(last(d->q_off, d->Lq, d->ldq) + 1), (long long)d->q_size);
+  if (last(d->k_off, d->Lk, d->ldk) >= d->k_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "k out of bounds: needs %lld floats, k_size=%lld",
+                   (long long)(last(d->k_off, d->Lk, d->ldk) + 1), (long long)d->k_size);
+  if (last(d->v_off, d->Lk, d->ldv) >= d->v_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "v out of bounds: needs %lld floats, v_size=%lld",
+                   (long long)(last(d->v_off, d->Lk, d->ldv) + 1), (long long)d->v_size);
+  if (d->o_off + (int64_t)d->Lq * HD > d->out_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "out out of bounds: needs %lld floats, out_size=%lld",
+                   (long long)(d->o_off + (int64_t)d->Lq * HD), (long long)d->out_size);
+  const int64_t nbias = (int64_t)d->H * d->Lq * d->Lk;
+  if (d->bias && nbias > d->bias_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "bias must hold H*Lq*Lk=%lld floats, bias_size=%lld", (long long)nbias,
+                   (long long)d->bias_size);
+
+  // byte ranges for hazard tracking; the output may not alias an input of the same problem
+  // (a writable binding may not alias a read-only one in one WebGPU dispatch)
+  auto rng = [](const float* base, int64_t first, int64_t lastidx) {
+    ByteRange r;
+    r.b = reinterpret_cast<uintptr_t>(base + first);
+    r.e = reinterpret_cast<uintptr_t>(base + lastidx + 1);
+    return r;
+  };
+  out->nreads = 0;
+  if (!out->empty) {
+    out->reads[out->nreads++] = rng(d->q, d->q_off, last(d->q_off, d->Lq, d->ldq));
+    out->reads[out->nreads++] = rng(d->k, d->k_off, last(d->k_off, d->Lk, d->ldk));
+    out->reads[out->nreads++] = rng(d->v, d->v_off, last(d->v_off, d->Lk, d->ldv));
+    if (d->bias) out->reads[out->nreads++] = rng(d->bias, 0, nbias - 1);
+    out->write = rng(d->out, d->o_off, d->o_off + (int64_t)d->Lq * HD - 1);
+    for (int i = 0; i < out->nreads; ++i)
+      if (out->reads[i].b < out->write.e && out->write.b < out->reads[i].e)
+        return set_err(c, SUPRA_ATTN_EINVAL, "out overlaps an input of the same call");
+  }
+
+  Queued& q = out->q;
+  std::memset(&q.p, 0, sizeof(q.p));
+  q.p.q = d->q;
+  q.p.k = d->k;
+  q.p.v = d->v;
+  q.p.o = d->out;
+  q.p.bias = d->bias;
+  q.p.q_off = d->q_off;
+  q.p.k_off = d->k_off;
+  q.p.v_off = d->v_off;
+  q.p.o_off = d->o_off;
+  q.p.ldq = d->ldq;
+  q.p.ldk = d->ldk;
+  q.p.ldv = d->ldv;
+  q.p.ldo = HD;
+  q.p.Lq = d->Lq;
+  q.p.Lk = d->Lk;
+  q.p.H = d->H;
+  q.p.D = d->D;
+  q.p.scale = scale;
+  q.p.scale_log2 = scale * kLog2e;
+  q.bias = d->bias != nullptr;
+  // 16-byte aligned rows for the bulk-copy engine (the reference's fused path needs the same
+  // %4 alignment of every stride and offset, app/gpu/ops.js:111)
+  q.aligned = (d->D % 4 == 0) && (d->ldq % 4 == 0) && (d->ldk % 4 == 0) && (d->ldv % 4 == 0) &&
+              aligned16(d->q + d->q_off) && aligned16(d->k + d->k_off) && aligned16(d->v + d->v_off) &&
+              aligned16(d->out + d->o_off);
+  if (d->D <= 64) {
+    q.path = PATH_FUSED;
+    q.cfg = d->Lq <= 64 ? supra::CFG_D64_Q64 : supra::CFG_D64_Q128;
+  } else if (d->D <= 128) {
+    q.path = PATH_FUSED;
+    q.cfg = supra::CFG_D128_Q64;
+  } else {
+    q.path = PATH_GEMM;
+    q.cfg = 0;
+  }
+  q.flops = 4.0 * d->Lq * (double)d->Lk * d->D * d->H;  // app/gpu/ops.js:116
+  q.bytes = 4.0 * ((double)d->Lq * HD * 2 + (double)d->Lk * HD * 2 + (d->bias ? (double)nbias : 0.0));
+  return SUPRA_ATTN_OK;
+}
+
+// ---- flush ---------------------------------------------------------------------------------------
+int flush_fused(supra_attn_ctx* c, std::vector<const Queued*>& g) {
+  const Queued& first = *g[0];
+  const int mq = supra::fused_cfg_tile_rows(first.cfg);
+  // longest-first (work per tile grows with the number of key blocks)
+  std::stable_sort(g.begin(), g.end(), [](const Queued* a, const Queued* b) { return a->p.Lk > b->p.Lk; });
+  const int n = (int)g.size();
+  int64_t total = 0;
+  double flops = 0, bytes = 0;
+  std::vector<int32_t> begin(n + 1);
+  for (int i = 0; i < n; ++i) {
+    begin[i] = (int32_t)total;
+    const int qt = (g[i]->p.Lq + mq - 1) / mq;
+    total += (int64_t)qt * g[i]->p.H;
+    flops += g[i]->flops;
+    bytes += g[i]->bytes;
+  }
+  if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
+  begin[n] = (int32_t)total;
+  const size_t pbytes = align16(sizeof(AttnProb) * n);
+  const size_t bbytes = sizeof(int32_t) * (n + 1);
+  char *h = nullptr, *dv = nullptr;
+  int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
+  if (rc) return rc;
+  AttnProb* hp = reinterpret_cast<AttnProb*>(h);
+  for (int i = 0; i < n; ++i) {
+    hp[i] = g[i]->p;
+    hp[i].q_tiles = (g[i]->p.Lq + mq - 1) / mq;
+  }
+  std::memcpy(h + pbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pbytes + bbytes);
+  if (rc) return rc;
+  AttnLaunch L;
+  L.probs = reinterpret_cast<const AttnProb*>(dv);
+  L.begin = reinterpret_cast<const int32_t*>(dv + pbytes);
+  L.n = n;
+  L.total = (int32_t)total;
+  L.status = c->d_status;
+  const char* name = supra::attn_fp32_name(first.cfg, first.bias, first.aligned);
+  cudaError_t e;
+  {
+    ProfScope ps(c, name, flops, bytes);
+    e = supra::launch_attn_fp32(first.cfg, first.bias, first.aligned, L, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, name);
+  c->launches += 1;
+  return SUPRA_ATTN_OK;
+}
+
+int ensure_scratch(supra_attn_ctx* c, size_t bytes) {
+  if (bytes <= c->scratch_cap) return SUPRA_ATTN_OK;
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "scratch: stream sync");
+  if (c->scratch) cudaFree(c->scratch);
+  c->scratch = nullptr;
+  c->scratch_cap = 0;
+  if (cudaMalloc(&c->scratch, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(c, SUPRA_ATTN_ENOMEM, "scratch: cudaMalloc(%zu) failed", bytes);
+  }
+  c->scratch_cap = bytes;
+  return SUPRA_ATTN_OK;
+}
+
+int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::vector<GemmUnit>& units,
+                   size_t scratch_bytes, bool bias, bool aligned) {
+  if (units.empty()) return SUPRA_ATTN_OK;
+  int rc = ensure_scratch(c, scratch_bytes);
+  if (rc) return rc;
+  const int np = (int)g.size();
+  const int nu = (int)units.size();
+  std::vector<int32_t> qk(nu + 1), pv(nu + 1), rw(nu + 1);
+  int64_t tq = 0, tp = 0, tr = 0;
+  double fl = 0, by_qk = 0, by_sm = 0, by_pv = 0;
+  for (int i = 0; i < nu; ++i) {
+    GemmUnit& u = units[i];
+    const AttnProb& P = g[u.prob]->p;
+    u.qk_begin = (int32_t)tq;
+    u.pv_begin = (int32_t)tp;
+    u.row_begin = (int32_t)tr;
+    qk[i] = u.qk_begin;
+    pv[i] = u.pv_begin;
+    rw[i] = u.row_begin;
+    const int rt = (u.rows + 127) / 128;
+    tq += (int64_t)rt * ((P.Lk + 127) / 128);
+    tp += (int64_t)rt * ((P.D + 127) / 128);
+    tr += u.rows;
+    fl += 2.0 * u.rows * (double)P.Lk * P.D;
+    const double s = 4.0 * u.rows * (double)P.Lk;
+    by_qk += 4.0 * ((double)u.rows * P.D + (double)P.Lk * P.D) + s + (P.bias ? s : 0.0);
+    by_sm += 2 * s;
+    by_pv += s + 4.0 * ((double)P.Lk * P.D + (double)u.rows * P.D);
+  }
+  if (tq > INT32_MAX || tp > INT32_MAX || tr > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "chunk too large");
+  qk[nu] = (int32_t)tq;
+  pv[nu] = (int32_t)tp;
+  rw[nu] = (int32_t)tr;
+  const size_t pbytes = align16(sizeof(AttnProb) * np);
+  const size_t ubytes = align16(sizeof(GemmUnit) * nu);
+  const size_t ibytes = align16(sizeof(int32_t) * (nu + 1));
+  char *h = nullptr, *dv = nullptr;
+  rc = ring_reserve(c, pbytes + ubytes + 3 * ibytes, &h, &dv);
+  if (rc) return rc;
+  AttnProb* hp = reinterpret_cast<AttnProb*>(h);
+  for (int i = 0; i < np; ++i) hp[i] = g[i]->p;
+  std::memcpy(h + pbytes, units.data(), sizeof(GemmUnit) * nu);
+  std::memcpy(h + pbytes + ubytes, qk.data(), sizeof(int32_t) * (nu + 1));
+  std::memcpy(h + pbytes + ubytes + ibytes, pv.data(), sizeof(int32_t) * (nu + 1));
+  std::memcpy(h + pbytes + ubytes + 2 * ibytes, rw.data(), sizeof(int32_t) * (nu + 1));
+  rc = ring_commit(c, h, dv, pbytes + ubytes + 3 * ibytes);
+  if (rc) return rc;
+  GemmLaunch L;
+  L.probs = reinterpret_cast<const AttnProb*>(dv);
+  L.units = reinterpret_cast<const GemmUnit*>(dv + pbytes);
+  L.qk_begin = reinterpret_cast<const int32_t*>(dv + pbytes + ubytes);
+  L.pv_begin = reinterpret_cast<const int32_t*>(dv + pbytes + ubytes + ibytes);
+  L.row_begin = reinterpret_cast<const int32_t*>(dv + pbytes + ubytes + 2 * ibytes);
+  L.scratch = c->scratch;
+  L.n_units = nu;
+  L.qk_total = (int32_t)tq;
+  L.pv_total = (int32_t)tp;
+  L.row_total = (int32_t)tr;
+  L.status = c->d_status;
+  cudaError_t e;
+  {
+    ProfScope ps(c, bias ? "attn_gemm_qk_bias" : "attn_gemm_qk", fl, by_qk);
+    e = supra::launch_gemm_qk(bias, aligned, L, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, "attn_gemm_qk");
+  {
+    ProfScope ps(c, "attn_softmax_rows", 0.0, by_sm);
+    e = supra::launch_softmax_rows(L, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, "attn_softmax_rows");
+  {
+    ProfScope ps(c, "attn_gemm_pv", fl, by_pv);
+    e = supra::launch_gemm_pv(aligned, L, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, "attn_gemm_pv");
+  c->launches += 3;
+  return SUPRA_ATTN_OK;
+}
+
+int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
+  const bool bias = g[0]->bias, aligned = g[0]->aligned;
+  std::vector<GemmUnit> units;
+  size_t used = 0;
+  for (int pi = 0; pi < (int)g.size(); ++pi) {
+    const AttnProb& P = g[pi]->p;
+    const int ldS = (P.Lk + 3) & ~3;
+    const size_t row_bytes = (size_t)ldS * 4;
+    // rows per unit: the whole problem when it fits the budget, else multiples of 128 rows
+    int64_t rows_max = (int64_t)(c->scratch_budget / row_bytes);
+    if (rows_max >= 128) rows_max = rows_max / 128 * 128;
+    if (rows_max < 1) rows_max = 1;
+    for (int h = 0; h < P.H; ++h) {
+      for (int r0 = 0; r0 < P.Lq; r0 += (int)std::min<int64_t>(rows_max, P.Lq)) {
+        const int rows = (int)std::min<int64_t>(rows_max, P.Lq - r0);
+        const size_t ub = align16((size_t)rows * row_bytes);
+        if (used + ub > c->scratch_budget && !units.empty()) {
+          int rc = run_gemm_chunk(c, g, units, used, bias, aligned);
+          if (rc) return rc;
+          units.clear();
+          used = 0;
+        }
+        GemmUnit u;
+        std::memset(&u, 0, sizeof u);
+        u.s_off = (int64_t)(used / 4);
+        u.prob = pi;
+        u.h = h;
+        u.row0 = r0;
+        u.rows = rows;
+        u.ldS = ldS;
+        units.push_back(u);
+        used += ub;
+      }
+    }
+  }
+  return run_gemm_chunk(c, g, units, used, bias, aligned);
+}
+
+int do_flush(supra_attn_ctx* c) {
+  if (c->queue.empty()) return SUPRA_ATTN_OK;
+  std::map<int, std::vector<const Queued*>> groups;
+  for (const Queued& q : c->queue) {
+    const int key = q.path * 1024 + q.cfg * 4 + (q.bias ? 2 : 0) + (q.aligned ? 1 : 0);
+    groups[key].push_back(&q);
+  }
+  int rc = SUPRA_ATTN_OK;
+  for (auto& kv : groups) {
+    rc = kv.second[0]->path == PATH_FUSED ? flush_fused(c, kv.second) : flush_gemm(c, kv.second);
+    if (rc) break;
+  }
+  c->queue.clear();
+  c->qreads.clear();
+  c->qwrites.clear();
+  return rc;
+}
+
+int check_device_status(supra_attn_ctx* c, int32_t* device_status) {
+  cudaError_t e = cudaMemcpyAsync(c->h_status, c->d_status, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "sync");
+  const int32_t code = c->h_status[0];
+  if (device_status) *device_status = code;
+  if (code == 0) return SUPRA_ATTN_OK;
+  const int32_t blk = c->h_status[1], stage = c->h_status[2];
+  cudaMemsetAsync(c->d_status, 0, 4 * sizeof(int32_t), c->stream);
+  cudaStreamSynchronize(c->stream);
+  if (code == supra::DEV_TIMEOUT)
+    return set_err(c, SUPRA_ATTN_ETIMEOUT, "device wait timed out (block %d, stage %d)", blk, stage);
+  return set_err(c, SUPRA_ATTN_EDEVICE, "device status %d (block %d, stage %d)", code, blk, stage);
+}
+
+int do_sync(supra_attn_ctx* c, int32_t* device_status) {
+  int rc = do_flush(c);
+  if (rc) return rc;
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "stream sync");
+  return check_device_status(c, device_status);
+}
+
+int record(supra_attn_ctx* c, const Checked& ck) {
+  if (ck.empty) return SUPRA_ATTN_OK;
+  bool hazard = c->qwrites.overlaps(ck.write.b, ck.write.e) || c->qreads.overlaps(ck.write.b, ck.write.e);
+  for (int i = 0; i < ck.nreads && !hazard; ++i) hazard = c->qwrites.overlaps(ck.reads[i].b, ck.reads[i].e);
+  if (hazard) {
+    int rc = do_flush(c);
+    if (rc) return rc;
+  }
+  for (int i = 0; i < ck.nreads; ++i) c->qreads.add(ck.reads[i].b, ck.reads[i].e);
+  c->qwrites.add(ck.write.b, ck.write.e);
+  c->queue.push_back(ck.q);
+  return SUPRA_ATTN_OK;
+}
+
+}  // namespace
+
+// ==================================================================================================
+extern "C" {
+
+const char* supra_attn_status_string(int status) {
+  switch (status) {
+    case SUPRA_ATTN_OK: return "ok";
+    case SUPRA_ATTN_EINVAL: return "invalid argument";
+    case SUPRA_ATTN_ENOMEM: return "out of memory";
+    case SUPRA_ATTN_ECUDA: return "CUDA error";
+    case SUPRA_ATTN_ETIMEOUT: return "device wait timed out";
+    case SUPRA_ATTN_EDEVICE: return "device error";
+    case SUPRA_ATTN_ESTATE: return "invalid state";
+    default: return "unknown status";
+  }
+}
+
+const char* supra_attn_last_error(const supra_attn_ctx* ctx) { return ctx ? ctx->err.c_str() : "NULL context"; }
+
+int supra_attn_create(int device, supra_attn_ctx** out) {
+  if (!out) return SUPRA_ATTN_EINVAL;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return SUPRA_ATTN_ECUDA;
+  }
+  if (device < 0 || device >= n) return SUPRA_ATTN_EINVAL;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return SUPRA_ATTN_ECUDA;
+  if (prop.major != 10) return SUPRA_ATTN_ECUDA;  // kernels are built for sm_100a only
+  DeviceGuard g(device);
+  supra_attn_ctx* c = new supra_attn_ctx();
+  c->device = device;
+  bool ok = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking) == cudaSuccess;
+  c->stream = c->own;
+  ok = ok && cudaMalloc(&c->d_status, 4 * sizeof(int32_t)) == cudaSuccess;
+  ok = ok && cudaMemset(c->d_status, 0, 4 * sizeof(int32_t)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&c->h_status, 4 * sizeof(int32_t)) == cudaSuccess;
+  ok = ok && cudaEventCreateWithFlags(&c->ring_ev[0], cudaEventDisableTiming) == cudaSuccess;
+  ok = ok && cudaEventCreateWithFlags(&c->ring_ev[1], cudaEventDisableTiming) == cudaSuccess;
+  if (ok) {
+    c->ring_half = size_t(2) << 20;
+    ok = cudaMallocHost(&c->ring_h, 2 * c->ring_half) == cudaSuccess &&
+         cudaMalloc(&c->ring_d, 2 * c->ring_half) == cudaSuccess;
+  }
+  if (!ok) {
+    cudaGetLastError();
+    supra_attn_destroy(c);
+    return SUPRA_ATTN_ENOMEM;
+  }
+  *out = c;
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_destroy(supra_attn_ctx* c) {
+  if (!c) return SUPRA_ATTN_OK;
+  DeviceGuard g(c->device);
+  if (c->stream) {
+    do_flush(c);
+    cudaStreamSynchronize(c->stream);
+  }
+  for (auto& pe : c->pend) {
+    cudaEventDestroy(pe.a);
+    cudaEventDestroy(pe.b);
+  }
+  for (cudaEvent_t e : c->evt_free) cudaEventDestroy(e);
+  for (auto& kv : c->pool_free)
+    for (void* p : kv.second) cudaFree(p);
+  for (auto& kv : c->pool_live) cudaFree(kv.first);
+  for (void* p : c->host_live) cudaFreeHost(p);
+  if (c->scratch) cudaFree(c->scratch);
+  if (c->ring_h) cudaFreeHost(c->ring_h);
+  if (c->ring_d) cudaFree(c->ring_d);
+  for (int i = 0; i < 2; ++i)
+    if (c->ring_ev[i]) cudaEventDestroy(c->ring_ev[i]);
+  if (c->d_status) cudaFree(c->d_status);
+  if (c->h_status) cudaFreeHost(c->h_status);
+  if (c->own) cudaStreamDestroy(c->own);
+  delete c;
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_set_stream(supra_attn_ctx* c, void* s) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  DeviceGuard g(c->device);
+  int rc = do_sync(c, nullptr);
+  if (rc) return rc;
+  c->stream = s ? static_cast<cudaStream_t>(s) : c->own;
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_tensor_alloc(supra_attn_ctx* c, int64_t n, float** dptr) {
+  if (!c || !dptr || n < 0) return c ? set_err(c, SUPRA_ATTN_EINVAL, "tensor_alloc: bad arguments") : SUPRA_ATTN_EINVAL;
+  DeviceGuard g(c->device);
+  const size_t size = pool_round((size_t)n * 4);
+  auto it = c->pool_free.find(size);
+  void* p = nullptr;
+  if (it != c->pool_free.end() && !it->second.empty()) {
+    p = it->second.back();
+    it->second.pop_back();
+  } else if (cudaMalloc(&p, size) != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(c, SUPRA_ATTN_ENOMEM, "tensor_alloc: cudaMalloc(%zu) failed", size);
+  }
+  c->pool_live[p] = size;
+  *dptr = static_cast<float*>(p);
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_tensor_free(supra_attn_ctx* c, float* dptr) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  if (!dptr) return SUPRA_ATTN_OK;
+  auto it = c->pool_live.find(dptr);
+  if (it == c->pool_live.end()) return set_err(c, SUPRA_ATTN_EINVAL, "tensor_free: pointer not from this context");
+  DeviceGuard g(c->device);
+  int rc = do_flush(c);  // recorded work may still read it; later reuse is stream-ordered after it
+  c->pool_free[it->second].push_back(dptr);
+  c->pool_live.erase(it);
+  return rc;
+}
+
+int supra_attn_upload(supra_attn_ctx* c, float* dst, const float* src, int64_t n) {
+  if (!c || n < 0 || (n > 0 && (!dst || !src))) return c ? set_err(c, SUPRA_ATTN_EINVAL, "upload: bad arguments") : 1;
+  DeviceGuard g(c->device);
+  int rc = do_flush(c);  // as fromArray: recorded work that reads dst runs first (app/gpu/device.js:150-157)
+  if (rc) return rc;
+  if (n == 0) return SUPRA_ATTN_OK;
+  cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream);
+  return e == cudaSuccess ? SUPRA_ATTN_OK : cuda_err(c, e, "upload");
+}
+
+int supra_attn_download(supra_attn_ctx* c, float* dst, const float* src, int64_t n) {
+  if (!c || n < 0 || (n > 0 && (!dst || !src))) return c ? set_err(c, SUPRA_ATTN_EINVAL, "download: bad arguments") : 1;
+  DeviceGuard g(c->device);
+  int rc = do_flush(c);
+  if (rc) return rc;
+  if (n > 0) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e != cudaSuccess) return cuda_err(c, e, "download");
+  }
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "download: sync");
+  return check_device_status(c, nullptr);  // read() surfaces pending errors (app/gpu/device.js:186)
+}
+
+int supra_attn_host_alloc(supra_attn_ctx* c, int64_t n, float** hptr) {
+  if (!c || !hptr || n < 0) return c ? set_err(c, SUPRA_ATTN_EINVAL, "host_alloc: bad arguments") : 1;
+  DeviceGuard g(c->device);
+  void* p = nullptr;
+  if (cudaMallocHost(&p, std::max<size_t>(16, (size_t)n * 4)) != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(c, SUPRA_ATTN_ENOMEM, "host_alloc failed");
+  }
+  c->host_live.insert(p);
+  *hptr = static_cast<float*>(p);
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_host_free(supra_attn_ctx* c, float* hptr) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  if (!hptr) return SUPRA_ATTN_OK;
+  auto it = c->host_live.find(hptr);
+  if (it == c->host_live.end()) return set_err(c, SUPRA_ATTN_EINVAL, "host_free: pointer not from this context");
+  DeviceGuard g(c->device);
+  int rc = do_sync(c, nullptr);
+  cudaFreeHost(hptr);
+  c->host_live.erase(it);
+  return rc;
+}
+
+int supra_attn_enqueue(supra_attn_ctx* c, const supra_attn_desc* d) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  Checked ck;
+  int rc = validate(c, d, &ck);
+  if (rc) return rc;
+  DeviceGuard g(c->device);
+  return record(c, ck);
+}
+
+int supra_attn_check_desc(const supra_attn_desc* d, char* msg, int32_t cap) {
+  supra_attn_ctx tmp;  // only its message field is used; no device state is touched
+  Checked ck;
+  const int rc = validate(&tmp, d, &ck);
+  if (msg && cap > 0) std::snprintf(msg, (size_t)cap, "%s", rc ? tmp.err.c_str() : "");
+  return rc;
+}
+
+int supra_attn_enqueue_batch(supra_attn_ctx* c, const supra_attn_desc* descs, int32_t n) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  if (n < 0 || (n > 0 && !descs)) return set_err(c, SUPRA_ATTN_EINVAL, "enqueue_batch: bad arguments");
+  std::vector<Checked> cks((size_t)n);
+  for (int32_t i = 0; i < n; ++i) {
+    int rc = validate(c, descs + i, &cks[i]);
+    if (rc) {
+      c->err = "problem " + std::to_string(i) + ": " + c->err;
+      return rc;
+    }
+  }
+  DeviceGuard g(c->device);
+  for (int32_t i = 0; i < n; ++i) {
+    int rc = record(c, cks[i]);
+    if (rc) return rc;
+  }
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_flush(supra_attn_ctx* c) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  DeviceGuard g(c->device);
+  return do_flush(c);
+}
+
+int supra_attn_sync(supra_attn_ctx* c, int32_t* device_status) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  DeviceGuard g(c->device);
+  return do_sync(c, device_status);
+}
+
+int supra_attn_pending(const supra_attn_ctx* c, int32_t* n) {
+  if (!c || !n) return SUPRA_ATTN_EINVAL;
+  *n = (int32_t)c->queue.size();
+  return SUPRA_ATTN_OK;
+}
+
+int32_t supra_attn_relative_bucket(int32_t rel, int32_t buckets, int32_t max_distance) {
+  // relativeBucket (app/models/t5.js:14-23), float32 rounding at every step like Math.fround
+  if (buckets < 4 || (buckets & 1)) return -1;
+  const int32_t nb = buckets / 2;
+  const int32_t max_exact = nb / 2;
+  if (max_distance <= max_exact) return -1;
+  int32_t bucket = rel > 0 ? nb : 0;
+  const int64_t n = rel < 0 ? -(int64_t)rel : (int64_t)rel;
+  if (n < max_exact) return bucket + (int32_t)n;
+  const float a = (float)((double)n / (double)max_exact);
+  const float b = (float)std::log((double)a);
+  const float cc = (float)std::log((double)max_distance / (double)max_exact);
+  const float dd = (float)((double)b / (double)cc);
+  const float e = (float)((double)dd * (double)(nb - max_exact));
+  const int64_t large = (int64_t)max_exact + (int64_t)std::trunc((double)e);
+  return bucket + (int32_t)std::min<int64_t>(large, nb - 1);
+}
+
+int supra_attn_position_bias(supra_attn_ctx* c, const float* table, int64_t table_size, int32_t buckets,
+                             int32_t max_distance, int32_t H, int32_t L, float* out, int64_t out_size) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  if (!table || !out) return set_err(c, SUPRA_ATTN_EINVAL, "position_bias: table and out must be non-NULL");
+  if (H < 1 || H > 65536 || L < 1 || L > (1 << 14)) return set_err(c, SUPRA_ATTN_EINVAL, "position_bias: bad H or L");
+  if (supra_attn_relative_bucket(0, buckets, max_distance) < 0)
+    return set_err(c, SUPRA_ATTN_EINVAL, "position_bias: buckets must be even and >= 4, max_distance > buckets/4");
+  if ((int64_t)buckets * H > table_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "position_bias: table holds fewer than buckets*H floats");
+  if ((int64_t)H * L * L > out_size) return set_err(c, SUPRA_ATTN_EINVAL, "position_bias: out holds fewer than H*L*L");
+  if (reinterpret_cast<uintptr_t>(out) < reinterpret_cast<uintptr_t>(table + table_size) &&
+      reinterpret_cast<uintptr_t>(table) < reinterpret_cast<uintptr_t>(out + (int64_t)H * L * L))
+    return set_err(c, SUPRA_ATTN_EINVAL, "position_bias: out overlaps table");
+  DeviceGuard g(c->device);
+  int rc = do_flush(c);
+  if (rc) return rc;
+  const size_t n = 2 * (size_t)L - 1;
+  char *h = nullptr, *dv = nullptr;
+  rc = ring_reserve(c, n * sizeof(int32_t), &h, &dv);
+  if (rc) return rc;
+  int32_t* lut = reinterpret_cast<int32_t*>(h);
+  for (int32_t r = -(L - 1); r <= L - 1; ++r) lut[r + L - 1] = supra_attn_relative_bucket(r, buckets, max_distance);
+  rc = ring_commit(c, h, dv, n * sizeof(int32_t));
+  if (rc) return rc;
+  cudaError_t e;
+  {
+    ProfScope ps(c, "position_bias", 0.0, 4.0 * (double)H * L * L);
+    e = supra::launch_position_bias(table, reinterpret_cast<const int32_t*>(dv), H, L, out, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, "position_bias");
+  c->launches += 1;
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_profile_enable(supra_attn_ctx* c, int32_t on) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  c->profile = on != 0;
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_profile_report(supra_attn_ctx* c, supra_attn_profile_entry* entries, int32_t cap, int32_t* n) {
+  if (!c || !n || cap < 0 || (cap > 0 && !entries)) return SUPRA_ATTN_EINVAL;
+  DeviceGuard g(c->device);
+  int rc = do_sync(c, nullptr);
+  if (rc) return rc;
+  rc = collect_profile(c);
+  if (rc) return rc;
+  std::vector<std::pair<std::string, ProfStat>> v(c->stats.begin(), c->stats.end());
+  std::sort(v.begin(), v.end(), [](const auto& a, const auto& b) { return a.second.ms > b.second.ms; });
+  int32_t k = 0;
+  for (auto& kv : v) {
+    if (k >= cap) break;
+    supra_attn_profile_entry& e = entries[k++];
+    std::memset(&e, 0, sizeof e);
+    std::snprintf(e.name, sizeof e.name, "%s", kv.first.c_str());
+    e.launches = kv.second.launches;
+    e.ms = kv.second.ms;
+    e.flops = kv.second.flops;
+    e.bytes = kv.second.bytes;
+  }
+  *n = k;
+  return SUPRA_ATTN_OK;
+}
+
+int supra_attn_profile_reset(supra_attn_ctx* c) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  DeviceGuard g(c->device);
+  int rc = do_sync(c, nullptr);
+  if (rc) return rc;
+  rc = collect_profile(c);
+  c->stats.clear();
+  return rc;
+}
+
+int supra_attn_launch_count(const supra_attn_ctx* c, int64_t* n) {
+  if (!c || !n) return SUPRA_ATTN_EINVAL;
+  *n = c->launches;
+  return SUPRA_ATTN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,266 @@
+"""Python mirror of the reference's attention operator surface over libsupra_attn.
+
+  GPU / Tensor      -- the device half of app/gpu/device.js (empty, fromArray, read, flush,
+                       sync, Tensor.release, the Profiler), one libsupra_attn context each.
+  attention()       -- ops.attention (app/gpu/ops.js:103-149): same keyword arguments, same
+                       defaults (scale = 1/sqrt(D), out allocated as [Lq, H*D] when omitted),
+                       a synchronous ValueError where the reference throws.
+  relative_bucket() -- relativeBucket (app/models/t5.js:14-23).
+  position_bias()   -- T5Encoder.positionBias + upload (app/models/t5.js:55-65,73), on the device.
+
+Operands may be Tensors of a GPU or CUDA float32 torch tensors (contiguous); in the latter
+case run the GPU on torch's current stream (GPU(stream=torch.cuda.current_stream())) so the
+work is ordered with torch's. Every call goes through the C ABI; nothing computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+
+from . import _lib
+from ._lib import Desc, ProfileEntry, check, lib
+
+VARIANTS = {"fp32": _lib.FP32, "tf32": _lib.TF32}
+
+
+class Tensor:
+    """app/gpu/device.js:41-55 — {buf, shape, size, release()} over a device address."""
+
+    def __init__(self, gpu: "GPU", buf: int, shape, capacity: int, owned: bool = True, keepalive=None):
+        self.gpu = gpu
+        self.buf = buf
+        self.shape = list(shape)
+        self.capacity = capacity  # floats addressable at buf (bounds for every call)
+        self.owned = owned
+        self._keep = keepalive
+
+    @property
+    def size(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+    def release(self):
+        if self.buf and self.owned:
+            check(lib.supra_attn_tensor_free(self.gpu.ctx, C.c_void_p(self.buf)), self.gpu.ctx)
+        self.buf = None
+        self._keep = None
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(getattr(stream, "cuda_stream"))
+
+
+class GPU:
+    """A libsupra_attn context bound to one CUDA device (GPU.create, app/gpu/device.js:92-118)."""
+
+    def __init__(self, device: int = 0, stream=None):
+        ctx = C.c_void_p()
+        st = lib.supra_attn_create(int(device), C.byref(ctx))
+        if st != _lib.OK:
+            raise _lib.SupraAttnError(st, f"supra_attn_create(device={device}) failed "
+                                          "(needs an sm_100 GPU and the CUDA driver)")
+        self.ctx = ctx
+        self.device = int(device)
+        if stream is not None:
+            self.set_stream(stream)
+
+    # ---- lifetime -------------------------------------------------------------------------------
+    def close(self):
+        if self.ctx:
+            lib.supra_attn_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream):
+        check(lib.supra_attn_set_stream(self.ctx, C.c_void_p(_stream_handle(stream))), self.ctx)
+
+    # ---- tensors ----------------------------------------------------------------------------------
+    def empty(self, shape) -> Tensor:
+        n = 1
+        for s in shape:
+            n *= int(s)
+        p = C.c_void_p()
+        check(lib.supra_attn_tensor_alloc(self.ctx, n, C.byref(p)), self.ctx)
+        return Tensor(self, p.value, shape, n)
+
+    def from_array(self, arr, shape=None) -> Tensor:
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32)).reshape(-1)
+        t = self.empty(list(shape) if shape is not None else [a.size])
+        if t.size != a.size:
+            t.release()
+            raise ValueError(f"from_array: {a.size} values for shape {shape}")
+        check(lib.supra_attn_upload(self.ctx, C.c_void_p(t.buf), a.ctypes.data_as(C.c_void_p), a.size), self.ctx)
+        return t
+
+    fromArray = from_array
+
+    def write(self, t: Tensor, arr, offset: int = 0):
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32)).reshape(-1)
+        if offset < 0 or offset + a.size > t.capacity:
+            raise ValueError("write: out of bounds")
+        check(lib.supra_attn_upload(self.ctx, C.c_void_p(t.buf + 4 * offset), a.ctypes.data_as(C.c_void_p), a.size),
+              self.ctx)
+
+    def read(self, t, count: int | None = None) -> np.ndarray:
+        buf, cap = _as_buf(t)
+        n = cap if count is None and not isinstance(t, Tensor) else (t.size if count is None else int(count))
+        if n > cap:
+            raise ValueError("read: count exceeds the tensor")
+        out = np.empty(n, dtype=np.float32)
+        check(lib.supra_attn_download(self.ctx, out.ctypes.data_as(C.c_void_p), C.c_void_p(buf), n), self.ctx)
+        return out
+
+    def wrap(self, x, shape=None) -> Tensor:
+        """A non-owning Tensor over a CUDA float32 torch tensor (kept alive by the Tensor)."""
+        buf, cap = _as_buf(x)
+        return Tensor(self, buf, shape if shape is not None else list(x.shape), cap, owned=False, keepalive=x)
+
+    # ---- execution ----------------------------------------------------------------------------------
+    def enqueue(self, desc: Desc):
+        check(lib.supra_attn_enqueue(self.ctx, C.byref(desc)), self.ctx)
+
+    def enqueue_batch(self, descs):
+        """descs: a ctypes array of Desc (see make_desc); recorded all-or-none."""
+        check(lib.supra_attn_enqueue_batch(self.ctx, descs, len(descs)), self.ctx)
+
+    def flush(self):
+        check(lib.supra_attn_flush(self.ctx), self.ctx)
+
+    def sync(self) -> int:
+        st = C.c_int32(0)
+        check(lib.supra_attn_sync(self.ctx, C.byref(st)), self.ctx)
+        return st.value
+
+    def pending(self) -> int:
+        n = C.c_int32(0)
+        check(lib.supra_attn_pending(self.ctx, C.byref(n)), self.ctx)
+        return n.value
+
+    def launch_count(self) -> int:
+        n = C.c_int64(0)
+        check(lib.supra_attn_launch_count(self.ctx, C.byref(n)), self.ctx)
+        return n.value
+
+    # ---- profiler (app/gpu/device.js:272-325) -------------------------------------------------------
+    def profile(self, on: bool = True):
+        check(lib.supra_attn_profile_enable(self.ctx, 1 if on else 0), self.ctx)
+
+    def profile_report(self):
+        arr = (ProfileEntry * 64)()
+        n = C.c_int32(0)
+        check(lib.supra_attn_profile_report(self.ctx, arr, 64, C.byref(n)), self.ctx)
+        return [{"name": e.name.decode(), "count": e.launches, "ms": e.ms, "flops": e.flops, "bytes": e.bytes}
+                for e in arr[: n.value]]
+
+    def profile_reset(self):
+        check(lib.supra_attn_profile_reset(self.ctx), self.ctx)
+
+
+def _as_buf(x):
+    """(device address, capacity in floats) of a Tensor or a CUDA float32 torch tensor."""
+    if isinstance(x, Tensor):
+        if not x.buf:
+            raise ValueError("tensor was released")
+        return x.buf, x.capacity
+    if hasattr(x, "data_ptr") and hasattr(x, "is_cuda"):
+        import torch
+
+        if not x.is_cuda:
+            raise ValueError("torch tensors must live on a CUDA device")
+        if x.dtype != torch.float32:
+            raise ValueError("torch tensors must be float32")
+        if not x.is_contiguous():
+            raise ValueError("torch tensors must be contiguous")
+        return x.data_ptr(), x.numel()
+    raise TypeError(f"unsupported operand type {type(x).__name__}")
+
+
+def make_desc(*, q, k, v, out, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff=0, oOff=0, scale=None,
+              bias=None, variant="fp32") -> Desc:
+    """Packs one ops.attention call into a supra_attn_desc (no validation; the library does it)."""
+    d = Desc()
+    d.q, d.q_size = _as_buf(q)
+    d.k, d.k_size = _as_buf(k)
+    d.v, d.v_size = _as_buf(v)
+    d.out, d.out_size = _as_buf(out)
+    if bias is not None:
+        d.bias, d.bias_size = _as_buf(bias)
+    d.ldq, d.ldk, d.ldv = int(ldq), int(ldk), int(ldv)
+    d.q_off, d.k_off, d.v_off, d.o_off = int(qOff), int(kOff), int(vOff), int(oOff)
+    d.Lq, d.Lk, d.H, d.D = int(Lq), int(Lk), int(H), int(D)
+    if scale is None:
+        d.flags = _lib.F_DEFAULT_SCALE
+        d.scale = 0.0
+    else:
+        d.scale = float(scale)
+    if variant not in VARIANTS:
+        raise ValueError(f"variant must be one of {sorted(VARIANTS)}")
+    d.variant = VARIANTS[variant]
+    return d
+
+
+def attention(gpu: GPU, *, q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff=0, oOff=0, scale=None,
+              bias=None, out=None, variant="fp32"):
+    """ops.attention (app/gpu/ops.js:109): records the call and returns the output tensor.
+
+    q: [Lq, ldq] with head h at column qOff + h*D; k, v: [Lk, ldk] / [Lk, ldv] with head h at
+    kOff / vOff + h*D. The output rows [Lq, H*D] are written at element offset oOff of `out`
+    (allocated as gpu.empty([Lq, H*D]) when omitted). scale defaults to 1/sqrt(D). bias is an
+    additive score bias [H, Lq, Lk]. Work runs at the next flush/sync/read.
+    """
+    o = out if out is not None else gpu.empty([Lq, H * D])
+    try:
+        d = make_desc(q=q, k=k, v=v, out=o, Lq=Lq, Lk=Lk, H=H, D=D, ldq=ldq, ldk=ldk, ldv=ldv, qOff=qOff, kOff=kOff,
+                      vOff=vOff, oOff=oOff, scale=scale, bias=bias, variant=variant)
+        gpu.enqueue(d)
+    except Exception:
+        if out is None:
+            o.release()
+        raise
+    return o
+
+
+def relative_bucket(rel: int, buckets: int = 32, max_distance: int = 128) -> int:
+    """relativeBucket (app/models/t5.js:14-23)."""
+    b = lib.supra_attn_relative_bucket(int(rel), int(buckets), int(max_distance))
+    if b < 0:
+        raise ValueError("buckets must be even and >= 4, and max_distance > buckets/4")
+    return b
+
+
+def position_bias(gpu: GPU, table, L: int, H: int = 12, buckets: int = 32, max_distance: int = 128, out=None):
+    """T5Encoder.positionBias(L) uploaded as [H, L, L] (app/models/t5.js:55-65,73), built on the device.
+
+    table: device [buckets, H] (Tensor or CUDA torch tensor).
+    """
+    tb, tcap = _as_buf(table)
+    if tcap < buckets * H:
+        raise ValueError("table must hold buckets*H floats")
+    o = out if out is not None else gpu.empty([H, L, L])
+    ob, ocap = _as_buf(o)
+    try:
+        check(lib.supra_attn_position_bias(gpu.ctx, C.c_void_p(tb), int(tcap), int(buckets), int(max_distance), int(H), int(L),
+                                           C.c_void_p(ob), int(ocap)), gpu.ctx)
+    except Exception:
+        if out is None:
+            o.release()
+        raise
+    return o
+
+
+def default_scale(D: int) -> float:
+    return 1.0 / math.sqrt(D)

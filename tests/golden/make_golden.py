@@ -1,0 +1,171 @@
+"""Generate the golden vectors in this folder from the reference's own CPU oracles.
+
+Run in a checkout that has the reference mounted (it imports it at run time; nothing is
+copied):
+
+    python tests/golden/make_golden.py --reference /path/to/supra2-img-web
+
+Sources of truth:
+  - DiT self / cross attention and the single-head VAE attention come from the reference's
+    PyTorch oracle `attention()` (tools/reference.py:72-79), called exactly as its
+    dit_forward calls it (tools/reference.py:96-100) with heads=9, and with heads=1 for the
+    VAE shape (the app's VAE attention is ops.attention with H=1, D=512, app/models/vae.js:86).
+  - The cross-attention ragged case is produced both per sequence at its true length (as the
+    app runs it, app/models/dit.js:184) and padded+masked (as tools/reference.py:167-171 does).
+  - T5 attention comes from Hugging Face transformers' T5Attention (the module
+    tools/reference.py:129 runs): q/k/v projections with seeded weights, o = identity, and the
+    relative-attention-bias embedding set to a seeded [32, 12] table; its compute_bias gives
+    the [H, L, L] bias. transformers is not vendored by the reference (version recorded below).
+  - Bucket vectors come from T5Attention._relative_position_bucket, which
+    app/models/t5.js:13-23 restates.
+
+Output format is the reference's dump format (tools/reference.py:41-54): one raw
+little-endian float32 file per tensor plus index.json with shapes and metadata.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+class Dump:
+    def __init__(self, out):
+        self.out = out
+        self.index = {}
+
+    def __call__(self, name, t, **meta):
+        a = t.detach().float().contiguous().cpu().numpy() if torch.is_tensor(t) else np.asarray(t, dtype=np.float32)
+        a.astype("<f4").tofile(os.path.join(self.out, name + ".bin"))
+        self.index[name] = {"shape": list(a.shape), **meta}
+
+    def save(self, **extra):
+        with open(os.path.join(self.out, "index.json"), "w") as f:
+            json.dump({**extra, "tensors": self.index}, f, indent=1, sort_keys=True)
+
+
+def sha(t):
+    return hashlib.sha256(t.detach().float().contiguous().numpy().astype("<f4").tobytes()).hexdigest()
+
+
+@torch.no_grad()
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("SUPRA_REFERENCE", ""))
+    ap.add_argument("--out", default=HERE)
+    args = ap.parse_args()
+    if not args.reference:
+        sys.exit("pass --reference <path to the reference checkout>")
+    sys.path.insert(0, os.path.join(args.reference, "tools"))
+    import reference  # tools/reference.py (imports only torch/numpy at module level)
+    import transformers
+    from transformers import T5Config
+    from transformers.models.t5.modeling_t5 import T5Attention
+
+    torch.set_num_threads(1)
+    d = Dump(args.out)
+    meta = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__,
+            "transformers": transformers.__version__, "cases": {}}
+
+    # ---- DiT self-attention, interleaved qkv [B, N, 1728] (app/models/dit.js:172) ----------
+    for name, B, N, seed in (("dit_self", 2, 40, 11),):
+        g = torch.Generator().manual_seed(seed)
+        qkv = torch.randn(B, N, 3 * 576, generator=g)
+        v3 = qkv.view(B, N, 3, 576)
+        out = reference.attention(v3[:, :, 0], v3[:, :, 1], v3[:, :, 2], 9)
+        d(f"{name}_qkv", qkv, seed=seed)
+        d(f"{name}_out", out)
+        meta["cases"][name] = {"B": B, "N": N, "H": 9, "D": 64, "seed": seed}
+
+    # ---- config-1 size (B=2, 256 tokens): inputs regenerated from the seed, output stored ---
+    g = torch.Generator().manual_seed(1)
+    qkv = torch.randn(2, 256, 1728, generator=g)
+    v3 = qkv.view(2, 256, 3, 576)
+    out = reference.attention(v3[:, :, 0], v3[:, :, 1], v3[:, :, 2], 9)
+    d("dit_self_cfg1_out", out, input_sha256=sha(qkv),
+      inputs="torch.Generator().manual_seed(1); torch.randn(2, 256, 1728) as interleaved qkv")
+    meta["cases"]["dit_self_cfg1"] = {"B": 2, "N": 256, "H": 9, "D": 64, "seed": 1}
+
+    # ---- DiT cross-attention, ragged cached K/V [L, 1152] (app/models/dit.js:137-144,184) ---
+    Ls = [1, 7, 77, 128]
+    g = torch.Generator().manual_seed(22)
+    B, N = len(Ls), 48
+    q = torch.randn(B, N, 576, generator=g)
+    kvs = [torch.randn(L, 1152, generator=g) for L in Ls]
+    d("dit_cross_q", q, seed=22)
+    per_seq = []
+    for b, (L, kv) in enumerate(zip(Ls, kvs)):
+        d(f"dit_cross_kv{b}", kv)
+        o = reference.attention(q[b:b + 1], kv[None, :, :576], kv[None, :, 576:], 9)[0]
+        per_seq.append(o)
+    d("dit_cross_out", torch.stack(per_seq))
+    # padded + masked form of the same batch (tools/reference.py:167-171)
+    Lm = max(Ls)
+    kp = torch.zeros(B, Lm, 576)
+    vp = torch.zeros(B, Lm, 576)
+    mask = torch.zeros(B, Lm)
+    for b, (L, kv) in enumerate(zip(Ls, kvs)):
+        kp[b, :L] = kv[:, :576]
+        vp[b, :L] = kv[:, 576:]
+        mask[b, :L] = 1
+    d("dit_cross_out_masked", reference.attention(q, kp, vp, 9, mask))
+    meta["cases"]["dit_cross"] = {"Ls": Ls, "N": N, "H": 9, "D": 64, "seed": 22}
+
+    # ---- T5 encoder attention with relative-position bias (app/models/t5.js:73-80) ---------
+    cfg = T5Config(d_model=768, d_kv=64, num_heads=12, relative_attention_num_buckets=32,
+                   relative_attention_max_distance=128, dropout_rate=0.0, is_decoder=False)
+    att = T5Attention(cfg, has_relative_attention_bias=True).eval()
+    g = torch.Generator().manual_seed(33)
+    for lin in (att.q, att.k, att.v):
+        lin.weight.copy_(torch.randn(768, 768, generator=g) / 768 ** 0.5)
+    att.o.weight.copy_(torch.eye(768))
+    table = torch.randn(32, 12, generator=g) * 0.1
+    att.relative_attention_bias.weight.copy_(table)
+    d("t5_table", table, seed=33)
+    t5_Ls = [1, 5, 37, 128]
+    for L in t5_Ls:
+        x = torch.randn(1, L, 768, generator=g)
+        y = att(x)[0][0]
+        d(f"t5_L{L}_q", att.q(x)[0])
+        d(f"t5_L{L}_k", att.k(x)[0])
+        d(f"t5_L{L}_v", att.v(x)[0])
+        d(f"t5_L{L}_bias", att.compute_bias(L, L)[0])
+        d(f"t5_L{L}_out", y)
+    meta["cases"]["t5"] = {"Ls": t5_Ls, "H": 12, "D": 64, "scale": 1.0, "buckets": 32, "max_distance": 128}
+
+    # ---- HF bucket function over a wide range of relative positions -------------------------
+    rel = torch.arange(-1000, 1001)
+    for nb, md in ((32, 128), (32, 64), (16, 32), (64, 256)):
+        bk = T5Attention._relative_position_bucket(rel, bidirectional=True, num_buckets=nb, max_distance=md)
+        d(f"bucket_{nb}_{md}", bk.float(), rel_first=-1000)
+    meta["cases"]["buckets"] = {"rel": [-1000, 1000], "configs": [[32, 128], [32, 64], [16, 32], [64, 256]]}
+
+    # ---- VAE mid-block single-head attention, D=512 (app/models/vae.js:77-94) ---------------
+    g = torch.Generator().manual_seed(44)
+    for name, T in (("vae_small", 96),):
+        x = torch.randn(T, 512, generator=g)
+        bound = (6.0 / 1024) ** 0.5
+        W = [(torch.rand(512, 512, generator=g) * 2 - 1) * bound for _ in range(3)]
+        bvec = [(torch.rand(512, generator=g) * 2 - 1) / 512 ** 0.5 for _ in range(3)]
+        qv, kv_, vv = [x @ w.T + b for w, b in zip(W, bvec)]
+        out = reference.attention(qv[None], kv_[None], vv[None], 1)[0]
+        d(f"{name}_q", qv)
+        d(f"{name}_k", kv_)
+        d(f"{name}_v", vv)
+        d(f"{name}_out", out)
+        meta["cases"][name] = {"T": T, "H": 1, "D": 512, "seed": 44}
+
+    d.save(**meta)
+    print("wrote", args.out, len(d.index), "tensors")
+
+
+if __name__ == "__main__":
+    main()

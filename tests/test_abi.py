@@ -1,0 +1,151 @@
+"""CPU-side checks of the C ABI: the library loads, exports every declared symbol, and its pure
+host functions (descriptor validation, the T5 bucket function) behave like the reference."""
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+import supra_attn
+from supra_attn import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "supra_attn.h")
+
+
+def header_functions():
+    txt = open(HEADER).read()
+    return set(re.findall(r"SUPRA_ATTN_API\s+[\w\s\*]+?\b(supra_attn_\w+)\s*\(", txt))
+
+
+def test_exports_every_declared_symbol():
+    declared = header_functions()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(_lib.lib, name), name
+    assert {s[0] for s in _lib.SIGNATURES} == declared
+
+
+def test_library_path_is_in_tree():
+    assert os.path.exists(_lib.LIB_PATH)
+    assert "supra2-img-web_b200" in os.path.abspath(_lib.LIB_PATH)
+
+
+def test_status_strings():
+    for st in range(7):
+        assert _lib.lib.supra_attn_status_string(st).decode()
+
+
+@pytest.mark.parametrize("nb,md", [(32, 128), (32, 64), (16, 32), (64, 256)])
+def test_relative_bucket_matches_hf(golden, nb, md):
+    ref = golden(f"bucket_{nb}_{md}").astype(np.int64)
+    got = np.array([supra_attn.relative_bucket(r, nb, md) for r in range(-1000, 1001)])
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_relative_bucket_rejects_bad_config():
+    assert _lib.lib.supra_attn_relative_bucket(3, 3, 128) == -1
+    assert _lib.lib.supra_attn_relative_bucket(3, 2, 128) == -1
+    assert _lib.lib.supra_attn_relative_bucket(3, 32, 8) == -1
+    with pytest.raises(ValueError):
+        supra_attn.relative_bucket(1, 31, 128)
+
+
+# ---- descriptor validation (pure host; fake, never dereferenced device addresses) ----------------
+BASE_Q = 0x7F0000000000
+BASE_O = 0x7F1000000000
+BASE_B = 0x7F2000000000
+
+
+def dit_self_desc(**kw):
+    """DiT self-attention for sample b=1 of B=2 (app/models/dit.js:172)."""
+    d = _lib.Desc()
+    d.q = d.k = d.v = BASE_Q
+    d.out = BASE_O
+    d.q_size = d.k_size = d.v_size = 2 * 256 * 1728
+    d.out_size = 2 * 256 * 576
+    d.ldq = d.ldk = d.ldv = 1728
+    r = 256 * 1728
+    d.q_off, d.k_off, d.v_off, d.o_off = r, r + 576, r + 1152, 256 * 576
+    d.Lq, d.Lk, d.H, d.D = 256, 256, 9, 64
+    d.flags = _lib.F_DEFAULT_SCALE
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def check(d):
+    msg = C.create_string_buffer(512)
+    st = _lib.lib.supra_attn_check_desc(C.byref(d), msg, 512)
+    return st, msg.value.decode()
+
+
+def test_valid_descriptors():
+    assert check(dit_self_desc()) == (_lib.OK, "")
+    # T5 with bias
+    d = dit_self_desc(q_off=0, k_off=0, v_off=0, o_off=0, ldq=768, ldk=768, ldv=768, Lq=37, Lk=37, H=12, D=64)
+    d.q_size = d.k_size = d.v_size = 37 * 768
+    d.out_size = 37 * 768
+    d.bias = BASE_B
+    d.bias_size = 12 * 37 * 37
+    d.flags = 0
+    d.scale = 1.0
+    assert check(d)[0] == _lib.OK
+    # Lq = 0 records nothing and is valid
+    assert check(dit_self_desc(Lq=0))[0] == _lib.OK
+
+
+@pytest.mark.parametrize(
+    "kw,needle",
+    [
+        (dict(Lk=0), "Lk"),
+        (dict(H=0), "H="),
+        (dict(D=0), "D="),
+        (dict(Lq=-1), "Lq"),
+        (dict(q_off=-4), "offset"),
+        (dict(ldq=-1), "leading"),
+        (dict(v_size=2 * 256 * 1728 - 1), "v out of bounds"),  # v's last read is the buffer's last float
+        (dict(q_size=511 * 1728 + 575), "q out of bounds"),
+        (dict(out_size=2 * 256 * 576 - 1), "out out of bounds"),
+        (dict(o_off=256 * 576 + 4), "out out of bounds"),
+        (dict(flags=0x10), "flag"),
+        (dict(variant=7), "variant"),
+        (dict(q=0), "non-NULL"),
+        (dict(q=BASE_Q + 2, k=BASE_Q + 2, v=BASE_Q + 2), "aligned"),
+        (dict(flags=0, scale=float("inf")), "finite"),
+    ],
+)
+def test_invalid_descriptors(kw, needle):
+    st, msg = check(dit_self_desc(**kw))
+    assert st == _lib.EINVAL
+    assert needle in msg, msg
+
+
+def test_bias_too_small():
+    d = dit_self_desc()
+    d.bias = BASE_B
+    d.bias_size = 9 * 256 * 256 - 1
+    st, msg = check(d)
+    assert st == _lib.EINVAL and "bias" in msg
+
+
+def test_out_may_not_alias_inputs():
+    d = dit_self_desc()
+    d.out = BASE_Q  # writes over rows that q/k/v of this call read
+    d.out_size = d.q_size
+    d.o_off = 256 * 1728
+    st, msg = check(d)
+    assert st == _lib.EINVAL and "overlaps" in msg
+
+
+def test_create_without_gpu_fails_cleanly():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    ctx = C.c_void_p()
+    st = _lib.lib.supra_attn_create(0, C.byref(ctx))
+    assert st != _lib.OK and not ctx.value
+    with pytest.raises(supra_attn.SupraAttnError):
+        supra_attn.GPU(0)

@@ -1,0 +1,289 @@
+"""CUDA kernels (through the C ABI) against the pinned CPU oracle and the golden vectors.
+
+FP32 bar: normwise max-relative error max|got - ref| / max|ref| <= 1e-5 and rel-L2 <= 1e-5 per
+output tensor (the reference's rel-L2 metric, tools/check.js:31-44).
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def dev(a):
+    return _torch().from_numpy(np.ascontiguousarray(np.asarray(a, dtype=np.float32)).reshape(-1)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy().reshape(-1)
+
+
+def assert_close(got, ref, tol=TOL):
+    mr, rl = oracle.max_rel(got, ref), oracle.rel_l2(got, ref)
+    assert mr <= tol and rl <= tol, f"max_rel={mr:.3e} rel_l2={rl:.3e} (tol {tol})"
+
+
+def attn(gpu, **kw):
+    import supra_attn
+
+    return supra_attn.attention(gpu, **kw)
+
+
+# ---- the four call sites against the reference's golden outputs --------------------------------
+def test_dit_self_golden(gpu, golden):
+    c = golden.cases["dit_self"]
+    B, N, H, D = c["B"], c["N"], c["H"], c["D"]
+    qkv = dev(golden("dit_self_qkv"))
+    out = dev(np.zeros(B * N * H * D))
+    for b in range(B):  # one call per sample, as app/models/dit.js:170-173
+        r = b * N * 3 * H * D
+        attn(gpu, q=qkv, k=qkv, v=qkv, Lq=N, Lk=N, H=H, D=D, ldq=3 * H * D, ldk=3 * H * D, ldv=3 * H * D,
+             qOff=r, kOff=r + H * D, vOff=r + 2 * H * D, oOff=b * N * H * D, out=out)
+    assert gpu.pending() == B
+    gpu.sync()
+    assert_close(host(out), golden("dit_self_out"))
+
+
+def test_dit_self_config1(gpu, golden):
+    torch = _torch()
+    g = torch.Generator().manual_seed(1)
+    qkv = torch.randn(2, 256, 1728, generator=g).reshape(-1).cuda()
+    out = torch.zeros(2 * 256 * 576, device="cuda")
+    for b in range(2):
+        r = b * 256 * 1728
+        attn(gpu, q=qkv, k=qkv, v=qkv, Lq=256, Lk=256, H=9, D=64, ldq=1728, ldk=1728, ldv=1728, qOff=r,
+             kOff=r + 576, vOff=r + 1152, oOff=b * 256 * 576, out=out)
+    gpu.sync()
+    assert_close(host(out), golden("dit_self_cfg1_out"))
+
+
+def test_dit_cross_ragged_golden(gpu, golden):
+    c = golden.cases["dit_cross"]
+    N = c["N"]
+    q = dev(golden("dit_cross_q"))
+    out = dev(np.zeros(len(c["Ls"]) * N * 576))
+    kvs = []
+    for b, L in enumerate(c["Ls"]):  # app/models/dit.js:182-185, K/V cached per prompt [L, 1152]
+        kv = dev(golden(f"dit_cross_kv{b}"))
+        kvs.append(kv)
+        attn(gpu, q=q, k=kv, v=kv, Lq=N, Lk=L, H=9, D=64, ldq=576, ldk=1152, ldv=1152, qOff=b * N * 576, kOff=0,
+             vOff=576, oOff=b * N * 576, out=out)
+    gpu.sync()
+    assert_close(host(out), golden("dit_cross_out"))
+
+
+@pytest.mark.parametrize("L", [1, 5, 37, 128])
+def test_t5_golden(gpu, golden, L):
+    import supra_attn
+
+    table = dev(golden("t5_table"))
+    bias = supra_attn.position_bias(gpu, table, L, H=12, buckets=32, max_distance=128)
+    q, k, v = (dev(golden(f"t5_L{L}_{n}")) for n in "qkv")
+    o = attn(gpu, q=q, k=k, v=v, Lq=L, Lk=L, H=12, D=64, ldq=768, ldk=768, ldv=768, scale=1.0, bias=bias)
+    got = gpu.read(o)
+    np.testing.assert_array_equal(gpu.read(bias), golden(f"t5_L{L}_bias").reshape(-1))  # bit-exact
+    assert_close(got, golden(f"t5_L{L}_out"))
+    o.release()
+    bias.release()
+
+
+def test_vae_golden(gpu, golden):
+    T = golden.cases["vae_small"]["T"]
+    q, k, v = (dev(golden(f"vae_small_{n}")) for n in "qkv")
+    o = attn(gpu, q=q, k=k, v=v, Lq=T, Lk=T, H=1, D=512, ldq=512, ldk=512, ldv=512)  # app/models/vae.js:86
+    assert_close(gpu.read(o), golden("vae_small_out"))
+    o.release()
+
+
+def vae_inputs(n_img, seed):
+    """Config 4: x ~ N(0,1) per channel, Q/K/V = x W^T + b, W Xavier-uniform, b ~ U(+-1/sqrt(512))."""
+    rng = np.random.default_rng(seed)
+    bound = (6.0 / 1024) ** 0.5
+    W = [rng.uniform(-bound, bound, (512, 512)).astype(np.float32) for _ in range(3)]
+    bv = [rng.uniform(-1 / 512 ** 0.5, 1 / 512 ** 0.5, 512).astype(np.float32) for _ in range(3)]
+    x = rng.standard_normal((n_img, 1024, 512)).astype(np.float32)
+    return [(x @ w.T + b).astype(np.float32) for w, b in zip(W, bv)]
+
+
+def test_vae_full_size(gpu):
+    q, k, v = vae_inputs(2, 4)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = dev(np.zeros(2 * 1024 * 512))
+    for i in range(2):
+        o = i * 1024 * 512
+        attn(gpu, q=qd, k=kd, v=vd, Lq=1024, Lk=1024, H=1, D=512, ldq=512, ldk=512, ldv=512, qOff=o, kOff=o, vOff=o,
+             oOff=o, out=out)
+    gpu.sync()
+    got = host(out).reshape(2, 1024, 512)
+    for i in range(2):
+        assert_close(got[i], oracle.attention_heads(q[i], k[i], v[i], 1))
+
+
+# ---- edge cases ---------------------------------------------------------------------------------
+def rand_problem(rng, Lq, Lk, H, D, ldq=None, ldk=None, ldv=None, qOff=0, kOff=0, vOff=0, oOff=0, bias=False):
+    ldq = ldq or H * D
+    ldk = ldk or H * D
+    ldv = ldv or H * D
+    q = rng.standard_normal(qOff + (Lq - 1) * ldq + H * D if Lq else 1).astype(np.float32)
+    k = rng.standard_normal(kOff + (Lk - 1) * ldk + H * D).astype(np.float32)
+    v = rng.standard_normal(vOff + (Lk - 1) * ldv + H * D).astype(np.float32)
+    b = rng.standard_normal(H * Lq * Lk).astype(np.float32) if bias else None
+    return dict(q=q, k=k, v=v, bias=b, Lq=Lq, Lk=Lk, H=H, D=D, ldq=ldq, ldk=ldk, ldv=ldv, qOff=qOff, kOff=kOff,
+                vOff=vOff, oOff=oOff)
+
+
+def run_and_check(gpu, p, scale=None, tol=TOL):
+    q, k, v = dev(p["q"]), dev(p["k"]), dev(p["v"])
+    bias = dev(p["bias"]) if p["bias"] is not None else None
+    n_out = p["oOff"] + p["Lq"] * p["H"] * p["D"]
+    out = dev(np.full(max(n_out, 1), 7.0))
+    kw = {kk: p[kk] for kk in ("Lq", "Lk", "H", "D", "ldq", "ldk", "ldv", "qOff", "kOff", "vOff", "oOff")}
+    attn(gpu, q=q, k=k, v=v, bias=bias, out=out, scale=scale, **kw)
+    gpu.sync()
+    ref = np.full(max(n_out, 1), 7.0, dtype=np.float32)
+    oracle.attention_ops(p["q"], p["k"], p["v"], scale=scale, bias=p["bias"], out=ref, **kw)
+    got = host(out)
+    assert np.all(got[: p["oOff"]] == 7.0), "wrote before oOff"
+    assert_close(got, ref, tol)
+
+
+@pytest.mark.parametrize(
+    "Lq,Lk,H,D",
+    [
+        (1, 1, 1, 64), (1, 300, 2, 64), (63, 65, 3, 64), (64, 64, 1, 64), (65, 129, 2, 64), (129, 63, 1, 64),
+        (200, 1000, 2, 64), (256, 4096, 1, 64), (17, 33, 2, 16), (40, 40, 2, 32), (50, 70, 3, 60),
+        (70, 130, 2, 96), (100, 100, 2, 128), (33, 77, 1, 192), (130, 260, 2, 256), (64, 96, 1, 512),
+    ],
+)
+def test_shapes(gpu, Lq, Lk, H, D):
+    rng = np.random.default_rng(Lq * 1000 + Lk * 10 + D)
+    run_and_check(gpu, rand_problem(rng, Lq, Lk, H, D))
+
+
+@pytest.mark.parametrize("D", [64, 128, 512])
+def test_strided_and_unaligned(gpu, D):
+    rng = np.random.default_rng(D)
+    H = 2
+    # 16-byte aligned strides/offsets (bulk-copy path) with padding between rows
+    run_and_check(gpu, rand_problem(rng, 70, 90, H, D, ldq=H * D + 4, ldk=H * D + 8, ldv=H * D + 12, qOff=4, kOff=8,
+                                    vOff=12, oOff=4))
+    # misaligned offsets and strides (the reference's own unfused fallback case, app/gpu/ops.js:111)
+    run_and_check(gpu, rand_problem(rng, 70, 90, H, D, ldq=H * D + 1, ldk=H * D + 3, ldv=H * D + 5, qOff=1, kOff=3,
+                                    vOff=5, oOff=1))
+
+
+@pytest.mark.parametrize("D", [64, 128, 512])
+@pytest.mark.parametrize("Lq,Lk", [(1, 1), (37, 37), (65, 130)])
+def test_bias(gpu, D, Lq, Lk):
+    rng = np.random.default_rng(D + Lq)
+    run_and_check(gpu, rand_problem(rng, Lq, Lk, 3, D, bias=True), scale=1.0)
+
+
+def test_custom_scale_and_lq_zero(gpu):
+    rng = np.random.default_rng(5)
+    run_and_check(gpu, rand_problem(rng, 33, 45, 2, 64), scale=0.37)
+    p = rand_problem(rng, 0, 5, 1, 64)
+    torch = _torch()
+    out = torch.zeros(1, device="cuda")
+    attn(gpu, q=dev(p["q"]), k=dev(p["k"]), v=dev(p["v"]), Lq=0, Lk=5, H=1, D=64, ldq=64, ldk=64, ldv=64, out=out)
+    assert gpu.pending() == 0
+    gpu.sync()
+
+
+def test_known_answers(gpu):
+    rng = np.random.default_rng(7)
+    v = rng.standard_normal(64).astype(np.float32)
+    q = rng.standard_normal(5 * 64).astype(np.float32)
+    k = rng.standard_normal(64).astype(np.float32)
+    o = attn(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=5, Lk=1, H=1, D=64, ldq=64, ldk=64, ldv=64)
+    np.testing.assert_array_equal(gpu.read(o).reshape(5, 64), np.tile(v, (5, 1)))  # L = 1: exactly V
+    vv = rng.standard_normal(9 * 64).astype(np.float32)
+    o2 = attn(gpu, q=dev(np.zeros(3 * 64)), k=dev(rng.standard_normal(9 * 64)), v=dev(vv), Lq=3, Lk=9, H=1, D=64,
+              ldq=64, ldk=64, ldv=64)
+    np.testing.assert_allclose(gpu.read(o2).reshape(3, 64), np.tile(vv.reshape(9, 64).mean(0), (3, 1)), atol=2e-6)
+
+
+def test_hazard_ordering(gpu):
+    """A call that reads an earlier recorded call's output sees it (auto-flush on the hazard)."""
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal(40 * 128).astype(np.float32)
+    k = rng.standard_normal(50 * 128).astype(np.float32)
+    v = rng.standard_normal(50 * 128).astype(np.float32)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    o1 = dev(np.zeros(40 * 128))
+    o2 = dev(np.zeros(40 * 128))
+    attn(gpu, q=qd, k=kd, v=vd, Lq=40, Lk=50, H=2, D=64, ldq=128, ldk=128, ldv=128, out=o1)
+    attn(gpu, q=o1, k=kd, v=vd, Lq=40, Lk=50, H=2, D=64, ldq=128, ldk=128, ldv=128, out=o2)
+    gpu.sync()
+    r1 = oracle.attention_ops(q, k, v, 40, 50, 2, 64, 128, 128, 128)
+    r2 = oracle.attention_ops(r1, k, v, 40, 50, 2, 64, 128, 128, 128)
+    assert_close(host(o2), r2)
+
+
+def test_invalid_call_raises_and_records_nothing(gpu):
+    rng = np.random.default_rng(3)
+    q = dev(rng.standard_normal(64))
+    before = gpu.pending()
+    with pytest.raises(ValueError):
+        attn(gpu, q=q, k=q, v=q, Lq=2, Lk=1, H=1, D=64, ldq=64, ldk=64, ldv=64)  # q too short for Lq=2
+    assert gpu.pending() == before
+
+
+def test_determinism_and_profile(gpu):
+    rng = np.random.default_rng(9)
+    p = rand_problem(rng, 256, 256, 9, 64)
+    q, k, v = dev(p["q"]), dev(p["k"]), dev(p["v"])
+    gpu.profile(True)
+    n0 = gpu.launch_count()
+    outs = []
+    for _ in range(2):
+        o = attn(gpu, q=q, k=k, v=v, Lq=256, Lk=256, H=9, D=64, ldq=576, ldk=576, ldv=576)
+        outs.append(gpu.read(o))
+        o.release()
+    np.testing.assert_array_equal(outs[0], outs[1])
+    rep = gpu.profile_report()
+    gpu.profile(False)
+    assert gpu.launch_count() - n0 == 2
+    names = [r["name"] for r in rep]
+    assert any(n.startswith("attn_fp32_d64") for n in names), names
+
+
+# ---- BASELINE config sizes --------------------------------------------------------------------
+def test_config2_cross_full(gpu):
+    """Config 2: 128 sequences, L ~ U{1..128}, Q [128, 256, 576], K/V packed [L, 1152] per sequence."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(2)
+    Ls = torch.randint(1, 129, (128,), generator=g).tolist()
+    q = torch.randn(128 * 256 * 576, generator=g)
+    kvs = [torch.randn(L * 1152, generator=g) for L in Ls]
+    qd = q.cuda()
+    kvd = [x.cuda() for x in kvs]
+    out = torch.zeros(128 * 256 * 576, device="cuda")
+    import supra_attn
+
+    descs = (supra_attn.Desc * 128)()
+    for b, L in enumerate(Ls):
+        descs[b] = supra_attn.make_desc(q=qd, k=kvd[b], v=kvd[b], out=out, Lq=256, Lk=L, H=9, D=64, ldq=576,
+                                        ldk=1152, ldv=1152, qOff=b * 256 * 576, kOff=0, vOff=576, oOff=b * 256 * 576)
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    got = host(out).reshape(128, 256, 576)
+    qn = q.numpy().reshape(128, 256, 576)
+    for b in range(0, 128, 9):  # every 9th sequence against the float64 oracle
+        kv = kvs[b].numpy().reshape(-1, 1152)
+        assert_close(got[b], oracle.attention_heads(qn[b], kv[:, :576], kv[:, 576:], 9))
+    # every row of every sequence is a convex combination of its V rows
+    for b in range(128):
+        kv = kvs[b].numpy().reshape(-1, 1152)
+        vmin = kv[:, 576:].min(0) - 1e-5
+        vmax = kv[:, 576:].max(0) + 1e-5
+        assert np.all(got[b] >= vmin) and np.all(got[b] <= vmax)

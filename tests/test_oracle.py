@@ -1,0 +1,119 @@
+"""Pins the CPU oracle against the golden vectors made from the reference's own oracles.
+
+The golden outputs come from tools/reference.py:72-79 (DiT and VAE shapes) and from Hugging
+Face's T5Attention (T5 with relative-position bias); see tests/golden/make_golden.py.
+"""
+
+import hashlib
+
+import numpy as np
+import pytest
+
+import oracle
+
+# oracle (float64) vs the reference's float32 torch CPU outputs: the gap is torch's own fp32
+# rounding (largest for T5, whose scores are unscaled), 2x tighter than the kernels' 1e-5 bar
+TOL = 5e-6
+
+
+def test_dit_self_interleaved(golden):
+    c = golden.cases["dit_self"]
+    B, N, H, D = c["B"], c["N"], c["H"], c["D"]
+    qkv = golden("dit_self_qkv").reshape(-1)
+    ref = golden("dit_self_out")
+    out = np.zeros(B * N * H * D, dtype=np.float32)
+    for b in range(B):  # app/models/dit.js:170-173
+        r = b * N * 3 * H * D
+        oracle.attention_ops(qkv, qkv, qkv, N, N, H, D, 3 * H * D, 3 * H * D, 3 * H * D,
+                             qOff=r, kOff=r + H * D, vOff=r + 2 * H * D, oOff=b * N * H * D, out=out)
+    assert oracle.max_rel(out, ref) < TOL
+    assert oracle.rel_l2(out, ref) < TOL
+
+
+def test_dit_self_config1(golden):
+    import torch
+
+    meta = golden.meta("dit_self_cfg1_out")
+    g = torch.Generator().manual_seed(1)
+    qkv = torch.randn(2, 256, 1728, generator=g)
+    assert hashlib.sha256(qkv.numpy().astype("<f4").tobytes()).hexdigest() == meta["input_sha256"]
+    ref = golden("dit_self_cfg1_out")
+    for b in range(2):
+        o = oracle.attention_heads(qkv[b, :, :576].numpy(), qkv[b, :, 576:1152].numpy(), qkv[b, :, 1152:].numpy(), 9)
+        assert oracle.max_rel(o, ref[b]) < TOL
+
+
+def test_dit_cross_ragged(golden):
+    c = golden.cases["dit_cross"]
+    q = golden("dit_cross_q")
+    ref = golden("dit_cross_out")
+    for b, L in enumerate(c["Ls"]):
+        kv = golden(f"dit_cross_kv{b}")
+        assert kv.shape == (L, 1152)
+        qf = q[b].reshape(-1)
+        kvf = kv.reshape(-1)
+        out = oracle.attention_ops(qf, kvf, kvf, c["N"], L, 9, 64, 576, 1152, 1152, kOff=0, vOff=576)
+        assert oracle.max_rel(out, ref[b]) < TOL
+
+
+def test_ragged_equals_masked_padding(golden):
+    # the reference's only evidence that true-length K/V equals masked padding (tools/check.js:130-131)
+    a = golden("dit_cross_out")
+    b = golden("dit_cross_out_masked")
+    assert oracle.rel_l2(a, b) < 1e-6
+
+
+@pytest.mark.parametrize("L", [1, 5, 37, 128])
+def test_t5_bias_and_attention(golden, L):
+    table = golden("t5_table")
+    bias = oracle.position_bias(table, L, 12)
+    np.testing.assert_array_equal(bias.reshape(12, L, L), golden(f"t5_L{L}_bias"))  # bit-exact
+    q, k, v = (golden(f"t5_L{L}_{n}").reshape(-1) for n in "qkv")
+    out = oracle.attention_ops(q, k, v, L, L, 12, 64, 768, 768, 768, scale=1.0, bias=bias)
+    ref = golden(f"t5_L{L}_out")
+    assert oracle.max_rel(out, ref) < TOL
+
+
+@pytest.mark.parametrize("nb,md", [(32, 128), (32, 64), (16, 32), (64, 256)])
+def test_relative_bucket_matches_hf(golden, nb, md):
+    ref = golden(f"bucket_{nb}_{md}").astype(np.int64)
+    got = np.array([oracle.relative_bucket(r, nb, md) for r in range(-1000, 1001)])
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_vae_single_head(golden):
+    c = golden.cases["vae_small"]
+    T = c["T"]
+    q, k, v = (golden(f"vae_small_{n}").reshape(-1) for n in "qkv")
+    out = oracle.attention_ops(q, k, v, T, T, 1, 512, 512, 512, 512)  # default scale 1/sqrt(512)
+    assert oracle.max_rel(out, golden("vae_small_out")) < TOL
+
+
+def test_known_answers():
+    rng = np.random.default_rng(0)
+    # L = 1: the output is V exactly
+    q = rng.standard_normal(7 * 64).astype(np.float32)
+    k = rng.standard_normal(64).astype(np.float32)
+    v = rng.standard_normal(64).astype(np.float32)
+    out = oracle.attention_ops(q, k, v, 7, 1, 1, 64, 64, 64, 64)
+    np.testing.assert_allclose(out.reshape(7, 64), np.tile(v, (7, 1)), rtol=0, atol=0)
+    # uniform scores (q = 0): the mean of V
+    kk = rng.standard_normal(9 * 64).astype(np.float32)
+    vv = rng.standard_normal(9 * 64).astype(np.float32)
+    out = oracle.attention_ops(np.zeros(3 * 64, np.float32), kk, vv, 3, 9, 1, 64, 64, 64, 64)
+    np.testing.assert_allclose(out.reshape(3, 64), np.tile(vv.reshape(9, 64).mean(0), (3, 1)), rtol=1e-6, atol=1e-6)
+    # a dominant bias selects one key
+    bias = np.full(3 * 9, -1e4, np.float32)
+    bias[[4, 9 + 2, 18 + 8]] = 0
+    out = oracle.attention_ops(np.zeros(3 * 64, np.float32), kk, vv, 3, 9, 1, 64, 64, 64, 64, bias=bias)
+    np.testing.assert_allclose(out.reshape(3, 64), vv.reshape(9, 64)[[4, 2, 8]], rtol=1e-6, atol=1e-6)
+
+
+def test_sdpa_port_matches_golden(golden):
+    import torch
+
+    qkv = torch.from_numpy(golden("dit_self_qkv").copy())
+    B, N = qkv.shape[:2]
+    v3 = qkv.view(B, N, 3, 576)
+    out = oracle.sdpa_port(v3[:, :, 0], v3[:, :, 1], v3[:, :, 2], 9)
+    assert oracle.max_rel(out.numpy(), golden("dit_self_out")) < 1e-6
