@@ -1,0 +1,476 @@
+"""Benchmark: SupraDiT attention workload per Euler step on 1..8 B200.
+
+One step = one Euler step of the DiT's attention: 14 blocks x (self-attention over 256 patch
+tokens + cross-attention to the sequence's cached projected T5 K/V of ragged length L ~ U{1..128}),
+9 heads x 64, for 1024 prompts with CFG (2048 sequences), sharded by prompt across the ranks
+(strong scaling), outputs of each step gathered to rank 0. Each attention call is issued as the
+reference issues it (one ops.attention per sample, app/models/dit.js:170-173,182-185) through
+the C ABI; the library groups the 2048 calls of a block into one launch. Self and cross
+attention of a block are flushed separately because the model's cross-attention query depends
+on the self-attention output.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0. `value` = sequence-attentions per second over all ranks
+(one sequence-attention = one sample's all-head attention at one call; a step has
+2048 x 14 x 2 of them), inputs resident in HBM. `e2e` = the same metric through the public API
+with the step's inputs uploaded from pinned host memory and its output read back inside the
+timed region. `roofline` = the fused FP32 kernel's algorithmic FLOPs per launch over its
+CUDA-event launch time, against the FP32 FFMA peak. `cpu_baseline` = tools/reference.py's CPU
+attention (restated in oracle/) on this host's cores, on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "supra2-img-web_b200"))
+sys.path.insert(0, ROOT)
+
+N_HEADS, HEAD_DIM, TOKENS, DIM = 9, 64, 256, 576
+BLOCKS = 14
+METRIC = "dit_attention_sequences_per_s"
+UNIT = "seq/s"
+
+
+# ---------------------------------------------------------------------------------------------
+def workload_lengths(prompts: int, seed: int):
+    """Cross-attention K/V length of every sequence (2 per prompt: cond, uncond), L ~ U{1..128}."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(1, 129, (2 * prompts,), generator=g).tolist()
+
+
+def shard_prompts(lengths, world: int, rank: int):
+    """Prompts dealt to ranks longest-first in a snake order so that every rank gets the same
+    number of prompts and near-equal sum of K/V lengths (the cross-attention work)."""
+    prompts = len(lengths) // 2
+    order = sorted(range(prompts), key=lambda p: -(lengths[2 * p] + lengths[2 * p + 1]))
+    mine = []
+    for i, p in enumerate(order):
+        r = i % (2 * world)
+        r = r if r < world else 2 * world - 1 - r
+        if r == rank:
+            mine.append(p)
+    return sorted(mine)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/power/throttle reasons every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.lines = []
+        self.t_begin = None
+        self.t_end = None
+
+    def mark_begin(self):
+        self.t_begin = time.monotonic()
+
+    def mark_end(self):
+        self.t_end = time.monotonic()
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append((time.monotonic(), ln.strip()))
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, power, reasons = [], None, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ts, ln in self.lines:
+            if (self.t_begin and ts < self.t_begin) or (self.t_end and ts > self.t_end + 0.25):
+                continue  # only samples taken while the timed region ran
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 10 or (self.uuid and self.uuid not in f[1]):
+                continue
+            try:
+                sm.append(float(f[2]))
+                smax = float(f[3])
+                power.append(float(f[4]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[6:10]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ---------------------------------------------------------------------------------------------
+def cpu_port_rate(seq_sample: int, seconds: float, seed: int, lengths):
+    """tools/reference.py:72-79 restated (oracle.sdpa_port) on all host cores over a bounded
+    sample: `seq_sample` sequences through one block (self + ragged cross attention), repeated
+    until `seconds` have passed. Returns (sequence-attentions/s, threads, sample text)."""
+    import torch
+
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    n = seq_sample
+    qkv = torch.randn(n, TOKENS, 3 * DIM, generator=g)
+    qx = torch.randn(n, TOKENS, DIM, generator=g)
+    kvs = [torch.randn(1, lengths[i], 2 * DIM, generator=g) for i in range(n)]
+    v3 = qkv.view(n, TOKENS, 3, DIM)
+
+    def one():
+        for b in range(0, n, 2):  # CFG pairs run together as in tools/reference.py:173
+            oracle.sdpa_port(v3[b:b + 2, :, 0], v3[b:b + 2, :, 1], v3[b:b + 2, :, 2], N_HEADS)
+        for i in range(n):  # each sequence at its true length (app/models/dit.js:184)
+            oracle.sdpa_port(qx[i:i + 1], kvs[i][:, :, :DIM], kvs[i][:, :, DIM:], N_HEADS)
+
+    one()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        one()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    rate = reps * 2 * n / el
+    cpu = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu = next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), "")
+    except OSError:
+        pass
+    sample = (f"{n} sequences x 1 block (self 256x256 + cross 256xL, L~U{{1..128}}), 9x64 heads, "
+              f"torch CPU fp32 SDPA, {reps} repetitions in {el:.1f} s; CPU: {cpu}")
+    return rate, threads, sample
+
+
+def run_reference(args, rank, world):
+    """`--impl reference`: the reference's CPU attention (oracle port of tools/reference.py:72-79)
+    on this host's cores, rank 0 only; each step is a bounded sample of the same workload."""
+    if rank != 0:
+        return
+    import torch
+
+    lengths = workload_lengths(args.prompts, args.seed)
+    n = 32
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_port_rate(n, 0.0, args.seed, lengths)
+    rates = []
+    t0 = time.perf_counter()
+    sample = ""
+    threads = os.cpu_count() or 1
+    for _ in range(args.steps):
+        r, threads, sample = cpu_port_rate(n, 0.0, args.seed, lengths)
+        rates.append(r)
+    el = time.perf_counter() - t0
+    value = statistics.median(rates)
+    per_step = 2048 * BLOCKS * 2
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_step / value * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "supradit_attention_step (configs[4]): 2048 seqs x 14 blocks x (self 256 + cross L~U{1..128})",
+                   "prompts": args.prompts, "global_batch": 2 * args.prompts, "seq_len": TOKENS,
+                   "parallelism": f"cpu x{threads} threads", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": el,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prompts", type=int, default=1024)
+    ap.add_argument("--seed", type=int, default=5)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import supra_attn
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    # one compute stream for torch's copies/events and the library's launches
+    torch.cuda.set_stream(torch.cuda.Stream(device=dev))
+
+    # ---- workload shard --------------------------------------------------------------------
+    lengths = workload_lengths(args.prompts, args.seed)
+    mine = shard_prompts(lengths, world, rank)
+    seqs = [s for p in mine for s in (2 * p, 2 * p + 1)]
+    S = len(seqs)
+    Ls = [lengths[s] for s in seqs]
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
+    qkv = torch.randn(S * TOKENS * 3 * DIM, device=dev, generator=gen)
+    qx = torch.randn(S * TOKENS * DIM, device=dev, generator=gen)
+    out_self = torch.empty(S * TOKENS * DIM, device=dev)
+    out_cross = torch.empty(S * TOKENS * DIM, device=dev)
+    kv_off = [0]
+    for L in Ls:
+        kv_off.append(kv_off[-1] + L * 2 * DIM)
+    kv = [torch.randn(kv_off[-1], device=dev, generator=gen) for _ in range(BLOCKS)]  # cached per block
+
+    gpu = supra_attn.GPU(local_rank, stream=torch.cuda.current_stream())
+    self_d = (supra_attn.Desc * S)()
+    for i in range(S):  # app/models/dit.js:172
+        r = i * TOKENS * 3 * DIM
+        self_d[i] = supra_attn.make_desc(q=qkv, k=qkv, v=qkv, out=out_self, Lq=TOKENS, Lk=TOKENS, H=N_HEADS,
+                                         D=HEAD_DIM, ldq=3 * DIM, ldk=3 * DIM, ldv=3 * DIM, qOff=r, kOff=r + DIM,
+                                         vOff=r + 2 * DIM, oOff=i * TOKENS * DIM)
+    cross_d = []
+    for b in range(BLOCKS):  # app/models/dit.js:184, K/V [L, 1152] cached per prompt and block
+        arr = (supra_attn.Desc * S)()
+        for i in range(S):
+            arr[i] = supra_attn.make_desc(q=qx, k=kv[b], v=kv[b], out=out_cross, Lq=TOKENS, Lk=Ls[i], H=N_HEADS,
+                                          D=HEAD_DIM, ldq=DIM, ldk=2 * DIM, ldv=2 * DIM, qOff=i * TOKENS * DIM,
+                                          kOff=kv_off[i], vOff=kv_off[i] + DIM, oOff=i * TOKENS * DIM)
+        cross_d.append(arr)
+
+    flops_step = sum(4.0 * TOKENS * TOKENS * HEAD_DIM * N_HEADS + 4.0 * TOKENS * L * HEAD_DIM * N_HEADS for L in Ls) * BLOCKS
+    flops_total = 0.0
+    for L in lengths:
+        flops_total += (4.0 * TOKENS * TOKENS + 4.0 * TOKENS * L) * HEAD_DIM * N_HEADS * BLOCKS
+
+    # gather of each step's output to rank 0 (a separate stream, overlapped with the next step)
+    # (double-buffered send buffers: step s copies into buffer s%2 on the compute stream once the
+    # gather that last read that buffer has finished, then the gather stream sends it)
+    gather_stream = torch.cuda.Stream(device=dev) if world > 1 else None
+    shard_max = max(len(shard_prompts(lengths, world, r)) for r in range(world)) * 2 * TOKENS * DIM
+    send_bufs = [torch.empty(shard_max, device=dev) for _ in range(2)] if world > 1 else None
+    sent = [None, None]
+    recv = [torch.empty(shard_max, device=dev) for _ in range(world)] if (world > 1 and rank == 0) else None
+    nstep = [0]
+
+    def gather_step():
+        if world == 1:
+            return
+        i = nstep[0] % 2
+        nstep[0] += 1
+        cur = torch.cuda.current_stream()
+        if sent[i] is not None:
+            cur.wait_event(sent[i])
+        send_bufs[i][: out_cross.numel()].copy_(out_cross)
+        gather_stream.wait_stream(cur)
+        with torch.cuda.stream(gather_stream):
+            dist.gather(send_bufs[i], recv if rank == 0 else None, dst=0)
+            ev = torch.cuda.Event()
+            ev.record(gather_stream)
+        sent[i] = ev
+
+    def step():
+        for b in range(BLOCKS):
+            gpu.enqueue_batch(self_d)
+            gpu.flush()
+            gpu.enqueue_batch(cross_d[b])
+            gpu.flush()
+        gather_step()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if gather_stream is not None:
+        gather_stream.synchronize()
+
+    # ---- timed region (device time, max over ranks) ---------------------------------------------
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local_rank).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    gpu.profile(True)
+    gpu.profile_reset()
+    launches0 = gpu.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.5)  # nvidia-smi is sampling before the timed region starts
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    clocks.mark_begin()
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    if gather_stream is not None:
+        torch.cuda.current_stream().wait_stream(gather_stream)
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    time.sleep(0.3)
+    clk = clocks.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    launches = gpu.launch_count() - launches0
+    prof = gpu.profile_report()
+    gpu.profile(False)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    seq_calls = 2 * args.prompts * BLOCKS * 2 * args.steps
+    value = seq_calls / (ms_max / 1e3)
+
+    # ---- roofline of the dominant kernel ---------------------------------------------------------
+    top = max(prof, key=lambda r: r["ms"]) if prof else None
+    peaks = measured_peaks()
+    sm_max = float(peaks.get("sm_max_mhz", 1965.0))
+    fp32_peak = 148 * 128 * 2 * sm_max * 1e6 / 1e12  # TFLOP/s: SMs x FP32 lanes x FMA x clock
+    roofline = None
+    if top:
+        achieved = top["flops"] / (top["ms"] / 1e3) / 1e12
+        traffic = None
+        tf = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tf):
+            with open(tf) as f:
+                tj = json.load(f).get(top["name"])
+            if tj:  # ncu DRAM bytes per algorithmic byte, applied to this bench's launch
+                traffic = tj["dram_bytes_per_alg_byte"] * top["bytes"] / top["count"]
+        roofline = {"bound": "fp32", "kernel": top["name"], "achieved": achieved, "peak": fp32_peak,
+                    "unit": "TFLOP/s", "frac": achieved / fp32_peak, "traffic": traffic,
+                    "alg_bytes_per_launch": top["bytes"] / top["count"],
+                    "alg_flops_per_launch": top["flops"] / top["count"],
+                    "launch_ms": top["ms"] / top["count"],
+                    "peak_source": f"nominal FP32 FFMA: 148 SMs x 128 lanes x 2 x {sm_max:.0f} MHz "
+                                   "(MEASURED_PEAKS.json has no FP32 figure)",
+                    "hbm_gbs_achieved": top["bytes"] / (top["ms"] / 1e3) / 1e9,
+                    "hbm_peak_gbs": peaks.get("hbm_gbs")}
+
+    # ---- end to end through the public API with host buffers ------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        h_qkv = torch.empty(qkv.numel(), dtype=torch.float32, pin_memory=True)
+        h_qx = torch.empty(qx.numel(), dtype=torch.float32, pin_memory=True)
+        h_out = torch.empty(out_cross.numel(), dtype=torch.float32, pin_memory=True)
+        h_qkv.copy_(qkv)
+        h_qx.copy_(qx)
+
+        up, down = supra_attn.lib.supra_attn_upload, supra_attn.lib.supra_attn_download
+
+        def e2e_step():
+            # the step's inputs host -> device, the steps, the result device -> host (read())
+            supra_attn._lib.check(up(gpu.ctx, qkv.data_ptr(), h_qkv.data_ptr(), qkv.numel()), gpu.ctx)
+            supra_attn._lib.check(up(gpu.ctx, qx.data_ptr(), h_qx.data_ptr(), qx.numel()), gpu.ctx)
+            step()
+            supra_attn._lib.check(down(gpu.ctx, h_out.data_ptr(), out_cross.data_ptr(), out_cross.numel()), gpu.ctx)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        if gather_stream is not None:
+            torch.cuda.current_stream().wait_stream(gather_stream)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        t2 = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e = {"value": seq_calls / (float(t2.item()) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": 4 * (qkv.numel() + qx.numel()) * world,
+               "d2h_bytes_per_step": 4 * out_cross.numel() * world,
+               "ms_per_step": float(t2.item()) / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, threads, sample = cpu_port_rate(32, args.cpu_seconds, args.seed, lengths)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, L~U{1..128})",
+            "config": {"workload": "supradit_attention_step (configs[4]): 1024 prompts x CFG = 2048 seqs, 14 blocks x "
+                                   "(self 256x256 + cross 256xL, L~U{1..128}), 9x64 heads, fp32 kernel",
+                       "prompts": args.prompts, "global_batch": 2 * args.prompts, "seq_len": TOKENS,
+                       "parallelism": f"prompt-sharded x{world}, outputs gathered to rank 0",
+                       "l2": "inputs larger than L2 (qkv 3.6 GB, K/V 8.5 GB per step at N=1)"},
+            "tflops": flops_total * args.steps / (ms_max / 1e3) / 1e12,
+            "gpu_launches": launches,
+            "clocks": clk,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "kernels": prof,
+        }
+        print(json.dumps(line), flush=True)
+
+    gpu.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -91,7 +91,8 @@ SUPRA_ATTN_API int supra_attn_create(int device, supra_attn_ctx** out);
 /* Flushes, synchronises and frees everything the context owns. NULL is a no-op. */
 SUPRA_ATTN_API int supra_attn_destroy(supra_attn_ctx* ctx);
 /* Runs subsequent launches and copies on a caller-owned cudaStream_t (NULL = the context's
- * own stream). Flushes pending work on the previous stream first. */
+ * own non-blocking stream; pass cudaStreamLegacy, (void*)1, for the legacy default stream).
+ * Flushes and waits for pending work on the previous stream first. */
 SUPRA_ATTN_API int supra_attn_set_stream(supra_attn_ctx* ctx, void* cuda_stream);
 SUPRA_ATTN_API const char* supra_attn_last_error(const supra_attn_ctx* ctx);
 /* Message for a status code. */

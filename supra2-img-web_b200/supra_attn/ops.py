@@ -51,12 +51,18 @@ class Tensor:
         self._keep = None
 
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream as an explicit handle
+
+
 def _stream_handle(stream) -> int:
+    """None -> 0 (the context's own stream); an int is passed through; a torch stream object
+    maps to its handle, with torch's default stream (handle 0) mapped to cudaStreamLegacy."""
     if stream is None:
         return 0
     if isinstance(stream, int):
         return stream
-    return int(getattr(stream, "cuda_stream"))
+    h = int(getattr(stream, "cuda_stream"))
+    return h if h != 0 else CUDA_STREAM_LEGACY
 
 
 class GPU:

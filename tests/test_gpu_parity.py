@@ -184,8 +184,11 @@ def test_strided_and_unaligned(gpu, D):
 @pytest.mark.parametrize("D", [64, 128, 512])
 @pytest.mark.parametrize("Lq,Lk", [(1, 1), (37, 37), (65, 130)])
 def test_bias(gpu, D, Lq, Lk):
+    # T5 runs unscaled at D = 64 (app/models/t5.js:80); wider heads keep the same score spread
+    # (N(0,1) inputs at D = 512 and scale 1 give scores of std 22, where fp32 accumulation alone
+    # is ~1e-5 off float64)
     rng = np.random.default_rng(D + Lq)
-    run_and_check(gpu, rand_problem(rng, Lq, Lk, 3, D, bias=True), scale=1.0)
+    run_and_check(gpu, rand_problem(rng, Lq, Lk, 3, D, bias=True), scale=(64.0 / D) ** 0.5)
 
 
 def test_custom_scale_and_lq_zero(gpu):
