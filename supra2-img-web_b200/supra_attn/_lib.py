@@ -62,6 +62,7 @@ SIGNATURES = [
     ("supra_attn_profile_report", C.c_int, [C.c_void_p, C.POINTER(ProfileEntry), C.c_int32, C.POINTER(C.c_int32)]),
     ("supra_attn_profile_reset", C.c_int, [C.c_void_p]),
     ("supra_attn_launch_count", C.c_int, [C.c_void_p, C.POINTER(C.c_int64)]),
+    ("supra_attn_attention_noalloc", C.c_int, [C.POINTER(Desc), C.c_void_p, C.c_char_p, C.c_int32]),
 ]
 
 
