@@ -39,6 +39,8 @@ struct AttnLaunch {
   int32_t n;
   int32_t total;
   int32_t* status;
+  int32_t uniform;  // > 0: every problem has this many tiles (tile -> problem by division)
+  int32_t pad;
 };
 
 // One (problem, head, row chunk) unit of the score-materialising path used for D > 128: the
@@ -70,7 +72,8 @@ enum FusedCfg : int32_t {
   CFG_D64_Q128 = 0,
   CFG_D64_Q64 = 1,
   CFG_D128_Q64 = 2,
-  CFG_COUNT = 3,
+  CFG_D64_W4 = 3,  // warp-independent pipeline (attn_fp32_warp.cu): D <= 64, no bias, aligned
+  CFG_COUNT = 4,
 };
 int fused_cfg_tile_rows(int cfg);
 int fused_cfg_head_dim(int cfg);
@@ -78,6 +81,8 @@ int fused_cfg_head_dim(int cfg);
 // Launchers. Each returns the cudaError_t of the launch (cudaSuccess on success).
 cudaError_t launch_attn_fp32(int cfg, bool bias, bool aligned, const AttnLaunch& L, cudaStream_t s);
 const char* attn_fp32_name(int cfg, bool bias, bool aligned);
+cudaError_t launch_attn_fp32_w4(const AttnLaunch& L, cudaStream_t s);
+int attn_fp32_w4_tile_rows();
 
 cudaError_t launch_gemm_qk(bool bias, bool aligned, const GemmLaunch& L, cudaStream_t s);
 cudaError_t launch_softmax_rows(const GemmLaunch& L, cudaStream_t s);

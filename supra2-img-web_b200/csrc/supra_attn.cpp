@@ -394,7 +394,8 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
               aligned16(d->out + d->o_off);
   if (d->D <= 64) {
     q.path = PATH_FUSED;
-    q.cfg = d->Lq <= 64 ? supra::CFG_D64_Q64 : supra::CFG_D64_Q128;
+    if (d->Lq <= 64) q.cfg = supra::CFG_D64_Q64;
+    else q.cfg = (q.aligned && !q.bias && scale > 0.f) ? supra::CFG_D64_W4 : supra::CFG_D64_Q128;
   } else if (d->D <= 128) {
     q.path = PATH_FUSED;
     q.cfg = supra::CFG_D128_Q64;
@@ -445,6 +446,14 @@ int flush_fused(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   L.n = n;
   L.total = (int32_t)total;
   L.status = c->d_status;
+  L.uniform = 0;
+  L.pad = 0;
+  {
+    const int64_t t0 = begin[1] - begin[0];
+    bool uni = t0 > 0;
+    for (int i = 1; i < n && uni; ++i) uni = (begin[i + 1] - begin[i]) == t0;
+    if (uni) L.uniform = (int32_t)t0;
+  }
   const char* name = supra::attn_fp32_name(first.cfg, first.bias, first.aligned);
   cudaError_t e;
   {

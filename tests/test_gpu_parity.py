@@ -162,6 +162,10 @@ def run_and_check(gpu, p, scale=None, tol=TOL):
         (1, 1, 1, 64), (1, 300, 2, 64), (63, 65, 3, 64), (64, 64, 1, 64), (65, 129, 2, 64), (129, 63, 1, 64),
         (200, 1000, 2, 64), (256, 4096, 1, 64), (17, 33, 2, 16), (40, 40, 2, 32), (50, 70, 3, 60),
         (70, 130, 2, 96), (100, 100, 2, 128), (33, 77, 1, 192), (130, 260, 2, 256), (64, 96, 1, 512),
+        # warp-pipelined D<=64 kernel: idle warps (Lq % 128), partial key blocks, head-dim padding,
+        # single key, many ring refills
+        (100, 50, 2, 32), (97, 31, 3, 48), (130, 1, 1, 64), (300, 97, 2, 64), (129, 33, 2, 64),
+        (160, 2000, 1, 64), (65, 8, 4, 8),
     ],
 )
 def test_shapes(gpu, Lq, Lk, H, D):
@@ -194,6 +198,8 @@ def test_bias(gpu, D, Lq, Lk):
 def test_custom_scale_and_lq_zero(gpu):
     rng = np.random.default_rng(5)
     run_and_check(gpu, rand_problem(rng, 33, 45, 2, 64), scale=0.37)
+    run_and_check(gpu, rand_problem(rng, 100, 70, 2, 64), scale=-0.2)  # non-positive scales
+    run_and_check(gpu, rand_problem(rng, 100, 70, 2, 64), scale=0.0)
     p = rand_problem(rng, 0, 5, 1, 64)
     torch = _torch()
     out = torch.zeros(1, device="cuda")
