@@ -2,6 +2,7 @@
 // Plain structs that the host packs into the descriptor ring and the kernels read from HBM.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the library calls the driver only through cudaGetDriverEntryPoint)
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -87,6 +88,32 @@ int attn_fp32_w4_tile_rows();
 cudaError_t launch_gemm_qk(bool bias, bool aligned, const GemmLaunch& L, cudaStream_t s);
 cudaError_t launch_softmax_rows(const GemmLaunch& L, cudaStream_t s);
 cudaError_t launch_gemm_pv(bool aligned, const GemmLaunch& L, cudaStream_t s);
+
+// TF32 tensor-core path (attn_tf32.cu): one problem with its TMA tensor-map indices and the
+// TMA coordinates (x = column, y = row) of head 0 / row 0 of each operand.
+struct alignas(16) Tf32Prob {
+  float* o;
+  int64_t o_off;
+  int64_t ldo;
+  int32_t Lq, Lk, H, D;
+  int32_t mq, mk, mv;
+  int32_t qx, qy, kx, ky, vx, vy;
+  float scale_log2;
+  int32_t q_tiles;
+  int32_t pad;
+};
+static_assert(sizeof(Tf32Prob) % 16 == 0, "Tf32Prob is packed into the descriptor ring");
+
+struct Tf32Launch {
+  const Tf32Prob* probs;
+  const CUtensorMap* maps;
+  const int32_t* begin;
+  int32_t n, total, uniform;
+  int32_t* status;
+};
+
+cudaError_t launch_attn_tf32(const Tf32Launch& L, cudaStream_t s);
+int attn_tf32_tile_rows();
 
 cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L,
                                  float* out, cudaStream_t s);

@@ -80,7 +80,7 @@ struct ByteRange {
   uintptr_t b = 0, e = 0;
 };
 
-enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1 };
+enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1, PATH_TF32 = 2 };
 
 struct Queued {
   AttnProb p;
@@ -90,6 +90,27 @@ struct Queued {
   bool aligned;
   double flops;
   double bytes;
+  int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TF32 tensor maps)
+};
+
+// A tensor map over a whole operand buffer: [rows, ld] fp32, boxes of 32 columns x box_rows rows.
+struct MapKey {
+  uintptr_t base;
+  int64_t ld, rows;
+  int32_t box_rows;
+  int32_t swz;  // CUtensorMapSwizzle
+  bool operator==(const MapKey& o) const {
+    return base == o.base && ld == o.ld && rows == o.rows && box_rows == o.box_rows && swz == o.swz;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<uintptr_t>()(k.base);
+    h ^= std::hash<int64_t>()(k.ld) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= std::hash<int64_t>()(k.rows) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= std::hash<int32_t>()(k.box_rows * 8 + k.swz) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    return h;
+  }
 };
 
 struct ProfStat {
@@ -147,11 +168,55 @@ struct supra_attn_ctx {
   std::vector<cudaEvent_t> evt_free;
   std::map<std::string, ProfStat> stats;
 
+  // encoded TMA tensor maps of the TF32 path, reused across flushes (keyed by buffer and box)
+  std::unordered_map<MapKey, CUtensorMap, MapKeyHash> map_cache;
+
   int64_t launches = 0;
   std::string err;
 };
 
 namespace {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda dependency).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// [rows, ld] fp32 buffer, boxes of 32 columns (128 bytes) x box_rows rows with the key's swizzle
+// (SWIZZLE_128B for K-major operands, SWIZZLE_128B_ATOM_32B for the MN-major V operand), zero
+// fill outside. The TMA unit rounds the fp32 values to TF32 on the way in when the driver
+// accepts that type.
+bool encode_map(CUtensorMap* m, const MapKey& k) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)k.ld, (cuuint64_t)k.rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)k.ld * 4};
+  const cuuint32_t box[2] = {32, (cuuint32_t)k.box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  for (CUtensorMapDataType t : {CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32}) {
+    if (fn(m, t, 2, reinterpret_cast<void*>(k.base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           static_cast<CUtensorMapSwizzle>(k.swz), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      return true;
+  }
+  return false;
+}
 
 class DeviceGuard {
  public:
@@ -301,8 +366,6 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   if (d->flags & ~SUPRA_ATTN_F_DEFAULT_SCALE) return set_err(c, SUPRA_ATTN_EINVAL, "unknown flag bits 0x%x", d->flags);
   if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
     return set_err(c, SUPRA_ATTN_EINVAL, "unknown variant %d", d->variant);
-  if (d->variant == SUPRA_ATTN_TF32)
-    return set_err(c, SUPRA_ATTN_EINVAL, "the TF32 variant is not available in this build");
   if (d->Lq < 0 || d->Lq > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lq=%d out of range [0, 2^30]", d->Lq);
   if (d->Lk < 1 || d->Lk > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lk=%d out of range [1, 2^30]", d->Lk);
   if (d->H < 1 || d->H > 65536) return set_err(c, SUPRA_ATTN_EINVAL, "H=%d out of range [1, 65536]", d->H);
@@ -402,6 +465,27 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   } else {
     q.path = PATH_GEMM;
     q.cfg = 0;
+  }
+  q.rows_q = d->ldq > 0 ? d->q_size / d->ldq : 0;
+  q.rows_k = d->ldk > 0 ? d->k_size / d->ldk : 0;
+  q.rows_v = d->ldv > 0 ? d->v_size / d->ldv : 0;
+  if (d->variant == SUPRA_ATTN_TF32) {
+    // The tensor-core kernel reads whole 32-column slabs of full buffer rows through TMA tensor
+    // maps: head dim 64, no bias, 16-byte aligned rows, every row of the problem a whole row of
+    // its buffer, and the heads inside one row. Other TF32 requests run the FP32 kernels, which
+    // are at least as accurate.
+    auto rows_ok = [](int64_t off, int64_t ld, int64_t rows, int64_t nrows, int64_t HDc) {
+      return ld >= 32 && ld <= (int64_t(1) << 30) && (off % ld) + HDc <= ld && off / ld + nrows <= rows &&
+             rows <= (int64_t(1) << 31) - 1;
+    };
+    const bool ok = d->D == 64 && !d->bias && q.aligned && d->Lq > 0 && aligned16(d->q) && aligned16(d->k) &&
+                    aligned16(d->v) && d->q_off % 4 == 0 && d->k_off % 4 == 0 && d->v_off % 4 == 0 &&
+                    rows_ok(d->q_off, d->ldq, q.rows_q, d->Lq, HD) && rows_ok(d->k_off, d->ldk, q.rows_k, d->Lk, HD) &&
+                    rows_ok(d->v_off, d->ldv, q.rows_v, d->Lk, HD);
+    if (ok) {
+      q.path = PATH_TF32;
+      q.cfg = 0;
+    }
   }
   q.flops = 4.0 * d->Lq * (double)d->Lk * d->D * d->H;  // app/gpu/ops.js:116
   q.bytes = 4.0 * ((double)d->Lq * HD * 2 + (double)d->Lk * HD * 2 + (d->bias ? (double)nbias : 0.0));
@@ -597,6 +681,114 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   return run_gemm_chunk(c, g, units, used, bias, aligned);
 }
 
+// TF32 tensor-core group: one tensor map per distinct (buffer, ld, rows, box) in the flush,
+// encoded once per context and cached; problems refer to maps by index.
+int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
+  const int mrows = supra::attn_tf32_tile_rows();
+  std::stable_sort(g.begin(), g.end(), [](const Queued* a, const Queued* b) { return a->p.Lk > b->p.Lk; });
+  const int n = (int)g.size();
+  std::vector<supra::Tf32Prob> probs((size_t)n);
+  std::vector<CUtensorMap> maps;
+  std::unordered_map<MapKey, int32_t, MapKeyHash> index;
+  MapKey last_key{0, 0, 0, 0, 0};
+  int32_t last_idx = -1;
+  auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box, CUtensorMapSwizzle swz,
+                       int32_t* out) -> int {
+    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, box, (int32_t)swz};
+    if (last_idx >= 0 && k == last_key) {
+      *out = last_idx;
+      return SUPRA_ATTN_OK;
+    }
+    auto it = index.find(k);
+    if (it == index.end()) {
+      auto ct = c->map_cache.find(k);
+      if (ct == c->map_cache.end()) {
+        CUtensorMap m;
+        if (!encode_map(&m, k)) return set_err(c, SUPRA_ATTN_ECUDA, "cuTensorMapEncodeTiled failed");
+        if (c->map_cache.size() > 65536) c->map_cache.clear();
+        ct = c->map_cache.emplace(k, m).first;
+      }
+      it = index.emplace(k, (int32_t)maps.size()).first;
+      maps.push_back(ct->second);
+    }
+    last_key = k;
+    last_idx = it->second;
+    *out = it->second;
+    return SUPRA_ATTN_OK;
+  };
+  std::vector<int32_t> begin(n + 1);
+  int64_t total = 0;
+  double flops = 0, bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    const Queued& q = *g[i];
+    const AttnProb& P = q.p;
+    supra::Tf32Prob& t = probs[i];
+    std::memset(&t, 0, sizeof t);
+    t.o = P.o;
+    t.o_off = P.o_off;
+    t.ldo = P.ldo;
+    t.Lq = P.Lq;
+    t.Lk = P.Lk;
+    t.H = P.H;
+    t.D = P.D;
+    int rc = map_index(P.q, P.ldq, q.rows_q, mrows, CU_TENSOR_MAP_SWIZZLE_128B, &t.mq);
+    if (!rc) rc = map_index(P.k, P.ldk, q.rows_k, 64, CU_TENSOR_MAP_SWIZZLE_128B, &t.mk);
+    if (!rc) rc = map_index(P.v, P.ldv, q.rows_v, 64, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, &t.mv);
+    if (rc) return rc;
+    t.qx = (int32_t)(P.q_off % P.ldq);
+    t.qy = (int32_t)(P.q_off / P.ldq);
+    t.kx = (int32_t)(P.k_off % P.ldk);
+    t.ky = (int32_t)(P.k_off / P.ldk);
+    t.vx = (int32_t)(P.v_off % P.ldv);
+    t.vy = (int32_t)(P.v_off / P.ldv);
+    t.scale_log2 = P.scale_log2;
+    t.q_tiles = (P.Lq + mrows - 1) / mrows;
+    begin[i] = (int32_t)total;
+    total += (int64_t)t.q_tiles * P.H;
+    flops += q.flops;
+    bytes += q.bytes;
+  }
+  if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
+  begin[n] = (int32_t)total;
+  const size_t pbytes = align16(sizeof(supra::Tf32Prob) * n);
+  const size_t mbytes = sizeof(CUtensorMap) * maps.size();
+  const size_t bbytes = sizeof(int32_t) * (n + 1);
+  char *h = nullptr, *dv = nullptr;
+  int rc = ring_reserve(c, 64 + pbytes + mbytes + bbytes, &h, &dv);
+  if (rc) return rc;
+  // tensor maps must sit on a 64-byte boundary in device memory
+  const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
+  char* hm = h + pad;
+  char* dm = dv + pad;
+  std::memcpy(hm, maps.data(), mbytes);
+  std::memcpy(hm + mbytes, probs.data(), sizeof(supra::Tf32Prob) * n);
+  std::memcpy(hm + mbytes + pbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
+  if (rc) return rc;
+  supra::Tf32Launch L;
+  L.maps = reinterpret_cast<const CUtensorMap*>(dm);
+  L.probs = reinterpret_cast<const supra::Tf32Prob*>(dm + mbytes);
+  L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes);
+  L.n = n;
+  L.total = (int32_t)total;
+  L.uniform = 0;
+  {
+    const int64_t t0 = begin[1] - begin[0];
+    bool uni = t0 > 0;
+    for (int i = 1; i < n && uni; ++i) uni = (begin[i + 1] - begin[i]) == t0;
+    if (uni) L.uniform = (int32_t)t0;
+  }
+  L.status = c->d_status;
+  cudaError_t e;
+  {
+    ProfScope ps(c, "attn_tf32_d64", flops, bytes);
+    e = supra::launch_attn_tf32(L, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, "attn_tf32_d64");
+  c->launches += 1;
+  return SUPRA_ATTN_OK;
+}
+
 int do_flush(supra_attn_ctx* c) {
   if (c->queue.empty()) return SUPRA_ATTN_OK;
   std::map<int, std::vector<const Queued*>> groups;
@@ -606,7 +798,10 @@ int do_flush(supra_attn_ctx* c) {
   }
   int rc = SUPRA_ATTN_OK;
   for (auto& kv : groups) {
-    rc = kv.second[0]->path == PATH_FUSED ? flush_fused(c, kv.second) : flush_gemm(c, kv.second);
+    const int path = kv.second[0]->path;
+    rc = path == PATH_FUSED ? flush_fused(c, kv.second)
+         : path == PATH_TF32 ? flush_tf32(c, kv.second)
+                             : flush_gemm(c, kv.second);
     if (rc) break;
   }
   c->queue.clear();

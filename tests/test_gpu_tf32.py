@@ -1,0 +1,139 @@
+"""TF32 tensor-core kernel (tcgen05) through the C ABI against the oracle and golden vectors.
+
+TF32 bar (its own stated tolerance): max|got - ref| / max|ref| <= 2e-3 and rel-L2 <= 2e-3 per output
+tensor. Requests the tensor-core kernel does not cover (head dim other than 64, a bias, rows
+that are not whole buffer rows) run the FP32 kernels and are held to the FP32 bar (1e-5).
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+TOL_TF32 = 2e-3
+TOL_FP32 = 1e-5
+
+
+def dev(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, dtype=np.float32)).reshape(-1)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy().reshape(-1)
+
+
+def check(got, ref, tol):
+    mr, rl = oracle.max_rel(got, ref), oracle.rel_l2(got, ref)
+    assert mr <= tol and rl <= tol, f"max_rel={mr:.3e} rel_l2={rl:.3e} (tol {tol})"
+    return mr, rl
+
+
+def kernel_names(gpu):
+    return {r["name"] for r in gpu.profile_report()}
+
+
+def test_dit_self_config1_tf32(gpu, golden):
+    import torch
+
+    import supra_attn
+
+    g = torch.Generator().manual_seed(1)
+    qkv = torch.randn(2, 256, 1728, generator=g).reshape(-1).cuda()
+    out = torch.zeros(2 * 256 * 576, device="cuda")
+    gpu.profile(True)
+    gpu.profile_reset()
+    for b in range(2):
+        r = b * 256 * 1728
+        supra_attn.attention(gpu, q=qkv, k=qkv, v=qkv, Lq=256, Lk=256, H=9, D=64, ldq=1728, ldk=1728, ldv=1728,
+                             qOff=r, kOff=r + 576, vOff=r + 1152, oOff=b * 256 * 576, out=out, variant="tf32")
+    gpu.sync()
+    names = kernel_names(gpu)
+    gpu.profile(False)
+    assert "attn_tf32_d64" in names, names
+    check(host(out), golden("dit_self_cfg1_out"), TOL_TF32)
+
+
+def test_dit_cross_ragged_tf32(gpu, golden):
+    import supra_attn
+
+    c = golden.cases["dit_cross"]
+    N = c["N"]
+    q = dev(golden("dit_cross_q"))
+    out = dev(np.zeros(len(c["Ls"]) * N * 576))
+    kvs = [dev(golden(f"dit_cross_kv{b}")) for b in range(len(c["Ls"]))]
+    for b, L in enumerate(c["Ls"]):
+        supra_attn.attention(gpu, q=q, k=kvs[b], v=kvs[b], Lq=N, Lk=L, H=9, D=64, ldq=576, ldk=1152, ldv=1152,
+                             qOff=b * N * 576, kOff=0, vOff=576, oOff=b * N * 576, out=out, variant="tf32")
+    gpu.sync()
+    ref = golden("dit_cross_out")
+    got = host(out).reshape(ref.shape)
+    for b in range(len(c["Ls"])):
+        check(got[b], ref[b], TOL_TF32)
+
+
+@pytest.mark.parametrize(
+    "Lq,Lk,H",
+    [(1, 1, 1), (100, 63, 2), (128, 64, 1), (129, 65, 3), (256, 256, 9), (300, 1000, 2), (64, 4096, 1), (7, 200, 4)],
+)
+def test_shapes_tf32(gpu, Lq, Lk, H):
+    import supra_attn
+
+    rng = np.random.default_rng(Lq * 7 + Lk)
+    HD = H * 64
+    q = rng.standard_normal(Lq * HD).astype(np.float32)
+    k = rng.standard_normal(Lk * HD).astype(np.float32)
+    v = rng.standard_normal(Lk * HD).astype(np.float32)
+    o = supra_attn.attention(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=Lq, Lk=Lk, H=H, D=64, ldq=HD, ldk=HD, ldv=HD,
+                             variant="tf32")
+    got = gpu.read(o)
+    o.release()
+    check(got, oracle.attention_ops(q, k, v, Lq, Lk, H, 64, HD, HD, HD), TOL_TF32)
+
+
+def test_tf32_requests_outside_the_tensor_core_kernel_run_fp32(gpu):
+    """Head dim 32, a bias, and a last row shorter than ld all run the FP32 kernels (1e-5)."""
+    import supra_attn
+
+    rng = np.random.default_rng(3)
+    gpu.profile(True)
+    gpu.profile_reset()
+    # head dim 32
+    q, k, v = (rng.standard_normal(n).astype(np.float32) for n in (70 * 64, 90 * 64, 90 * 64))
+    o = supra_attn.attention(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=70, Lk=90, H=2, D=32, ldq=64, ldk=64, ldv=64,
+                             variant="tf32")
+    check(gpu.read(o), oracle.attention_ops(q, k, v, 70, 90, 2, 32, 64, 64, 64), TOL_FP32)
+    # a bias
+    b = rng.standard_normal(2 * 70 * 90).astype(np.float32)
+    q, k, v = (rng.standard_normal(n).astype(np.float32) for n in (70 * 128, 90 * 128, 90 * 128))
+    o2 = supra_attn.attention(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=70, Lk=90, H=2, D=64, ldq=128, ldk=128, ldv=128,
+                              bias=dev(b), scale=1.0, variant="tf32")
+    check(gpu.read(o2), oracle.attention_ops(q, k, v, 70, 90, 2, 64, 128, 128, 128, scale=1.0, bias=b), TOL_FP32)
+    # padded rows with a short last row (buffer of (Lq-1)*ld + H*D floats)
+    q = rng.standard_normal(69 * 132 + 128).astype(np.float32)
+    k = rng.standard_normal(89 * 132 + 128).astype(np.float32)
+    v = rng.standard_normal(89 * 132 + 128).astype(np.float32)
+    o3 = supra_attn.attention(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=70, Lk=90, H=2, D=64, ldq=132, ldk=132, ldv=132,
+                              variant="tf32")
+    check(gpu.read(o3), oracle.attention_ops(q, k, v, 70, 90, 2, 64, 132, 132, 132), TOL_FP32)
+    names = kernel_names(gpu)
+    gpu.profile(False)
+    assert "attn_tf32_d64" not in names, names
+    for t in (o, o2, o3):
+        t.release()
+
+
+def test_tf32_determinism(gpu):
+    import supra_attn
+
+    rng = np.random.default_rng(8)
+    q, k, v = (dev(rng.standard_normal(300 * 576)) for _ in range(3))
+    outs = []
+    for _ in range(2):
+        o = supra_attn.attention(gpu, q=q, k=k, v=v, Lq=300, Lk=300, H=9, D=64, ldq=576, ldk=576, ldv=576,
+                                 variant="tf32")
+        outs.append(gpu.read(o))
+        o.release()
+    np.testing.assert_array_equal(outs[0], outs[1])
