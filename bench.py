@@ -229,6 +229,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-tf32", action="store_true", help="skip the TF32 tensor-core pass")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -442,6 +443,75 @@ def main():
                "d2h_bytes_per_step": 4 * out_cross.numel() * world,
                "ms_per_step": float(t2.item()) / args.steps}
 
+    # ---- the TF32 tensor-core variant on the same workload (its own tolerance, 2e-3) --------------
+    tf32 = None
+    if not args.no_tf32:
+        for arr in [self_d] + cross_d:
+            for i in range(S):
+                arr[i].variant = supra_attn._lib.TF32
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        if gather_stream is not None:
+            gather_stream.synchronize()
+        clocks_tf = ClockSampler(uuid)
+        gpu.profile(True)
+        gpu.profile_reset()
+        l0 = gpu.launch_count()
+        barrier()
+        torch.cuda.synchronize()
+        clocks_tf.start()
+        time.sleep(0.5)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        clocks_tf.mark_begin()
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        if gather_stream is not None:
+            torch.cuda.current_stream().wait_stream(gather_stream)
+        t1.record()
+        torch.cuda.synchronize()
+        clocks_tf.mark_end()
+        time.sleep(0.3)
+        clk_tf = clocks_tf.stop()
+        barrier()
+        ltf = gpu.launch_count() - l0
+        prof_tf = gpu.profile_report()
+        gpu.profile(False)
+        tt = torch.tensor([t0.elapsed_time(t1)], device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_tf = float(tt.item())
+        top_tf = max(prof_tf, key=lambda r: r["ms"]) if prof_tf else None
+        roof_tf = None
+        if top_tf:
+            gbs = top_tf["bytes"] / (top_tf["ms"] / 1e3) / 1e9
+            hbm = float(peaks.get("hbm_gbs", 6650.0))
+            tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0  # TF32 dense rate is half of bf16
+            traffic = None
+            tf = os.path.join(ROOT, "profiles", "traffic.json")
+            if os.path.exists(tf):
+                with open(tf) as f:
+                    tj = json.load(f).get(top_tf["name"])
+                if tj:
+                    traffic = tj["dram_bytes_per_alg_byte"] * top_tf["bytes"] / top_tf["count"]
+            roof_tf = {"bound": "hbm", "kernel": top_tf["name"], "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                       "frac": gbs / hbm, "traffic": traffic,
+                       "alg_bytes_per_launch": top_tf["bytes"] / top_tf["count"],
+                       "launch_ms": top_tf["ms"] / top_tf["count"],
+                       "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s",
+                       "tensor_tflops": top_tf["flops"] / (top_tf["ms"] / 1e3) / 1e12,
+                       "tensor_peak_tflops": tf_peak,
+                       "tensor_peak_source": "half of MEASURED_PEAKS.json bf16_tflops (TF32 dense = bf16 dense / 2)"}
+        tf32 = {"value": seq_calls / (ms_tf / 1e3), "unit": UNIT, "ms_per_step": ms_tf / args.steps,
+                "dtype": "tf32 operands, f32 accumulate", "tolerance": "max|d|/max|ref| and rel-L2 <= 2e-3",
+                "tflops": flops_total * args.steps / (ms_tf / 1e3) / 1e12, "gpu_launches": ltf, "clocks": clk_tf,
+                "roofline": roof_tf, "kernels": prof_tf}
+        for arr in [self_d] + cross_d:
+            for i in range(S):
+                arr[i].variant = supra_attn._lib.FP32
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, threads, sample = cpu_port_rate(32, args.cpu_seconds, args.seed, lengths)
@@ -464,6 +534,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "kernels": prof,
+            "variants": {"tf32": tf32} if tf32 else {},
         }
         print(json.dumps(line), flush=True)
 

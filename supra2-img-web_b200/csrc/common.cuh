@@ -11,11 +11,13 @@ namespace supra {
 
 // ---- device status word ----------------------------------------------------------------------
 // status[0] = first error code (DEV_* in kernels.h), status[1] = blockIdx.x of the reporter,
-// status[2] = stage tag. The first reporter wins; the host reads and clears it at sync.
-__device__ __forceinline__ void report_error(int32_t* status, int32_t code, int32_t stage) {
+// status[2] = stage tag, status[3] = a detail word (e.g. the block counter a wait was for).
+// The first reporter wins; the host reads and clears it at sync.
+__device__ __forceinline__ void report_error(int32_t* status, int32_t code, int32_t stage, int32_t detail = 0) {
   if (atomicCAS(status, 0, code) == 0) {
     status[1] = (int32_t)blockIdx.x;
     status[2] = stage;
+    status[3] = detail;
   }
 }
 

@@ -817,12 +817,13 @@ int check_device_status(supra_attn_ctx* c, int32_t* device_status) {
   const int32_t code = c->h_status[0];
   if (device_status) *device_status = code;
   if (code == 0) return SUPRA_ATTN_OK;
-  const int32_t blk = c->h_status[1], stage = c->h_status[2];
+  const int32_t blk = c->h_status[1], stage = c->h_status[2], detail = c->h_status[3];
   cudaMemsetAsync(c->d_status, 0, 4 * sizeof(int32_t), c->stream);
   cudaStreamSynchronize(c->stream);
   if (code == supra::DEV_TIMEOUT)
-    return set_err(c, SUPRA_ATTN_ETIMEOUT, "device wait timed out (block %d, stage %d)", blk, stage);
-  return set_err(c, SUPRA_ATTN_EDEVICE, "device status %d (block %d, stage %d)", code, blk, stage);
+    return set_err(c, SUPRA_ATTN_ETIMEOUT, "device wait timed out (block %d, stage %d, detail %d)", blk, stage,
+                   detail);
+  return set_err(c, SUPRA_ATTN_EDEVICE, "device status %d (block %d, stage %d, detail %d)", code, blk, stage, detail);
 }
 
 int do_sync(supra_attn_ctx* c, int32_t* device_status) {

@@ -137,3 +137,31 @@ def test_tf32_determinism(gpu):
         outs.append(gpu.read(o))
         o.release()
     np.testing.assert_array_equal(outs[0], outs[1])
+
+
+def test_config2_cross_tf32(gpu):
+    """Config 2 at full size through the TF32 kernel: 128 ragged sequences, 2304 tiles, so every
+    persistent CTA runs several tiles back to back with key blocks flowing across tile boundaries."""
+    import torch
+
+    import supra_attn
+
+    g = torch.Generator().manual_seed(12)
+    Ls = torch.randint(1, 129, (128,), generator=g).tolist()
+    q = torch.randn(128 * 256 * 576, generator=g)
+    kvs = [torch.randn(L * 1152, generator=g) for L in Ls]
+    qd = q.cuda()
+    kvd = [x.cuda() for x in kvs]
+    out = torch.zeros(128 * 256 * 576, device="cuda")
+    descs = (supra_attn.Desc * 128)()
+    for b, L in enumerate(Ls):
+        descs[b] = supra_attn.make_desc(q=qd, k=kvd[b], v=kvd[b], out=out, Lq=256, Lk=L, H=9, D=64, ldq=576,
+                                        ldk=1152, ldv=1152, qOff=b * 256 * 576, kOff=0, vOff=576, oOff=b * 256 * 576,
+                                        variant="tf32")
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    got = host(out).reshape(128, 256, 576)
+    qn = q.numpy().reshape(128, 256, 576)
+    for b in range(0, 128, 7):
+        kv = kvs[b].numpy().reshape(-1, 1152)
+        check(got[b], oracle.attention_heads(qn[b], kv[:, :576], kv[:, 576:], 9), TOL_TF32)
