@@ -15,7 +15,7 @@
 //  * Q, K and V tiles are staged by the bulk-copy (TMA) engine: one cp.async.bulk per row into a
 //    padded shared-memory row (stride D+4 floats keeps the float4 fragment loads conflict-free),
 //    completion on mbarriers with bounded waits. K for block j+1 streams in during PV of block j
-//    and V for block j+1 during QK^T/softmax of block j+1. No tensor map, no multicast.
+//    and V for block j+1 during QK^T/softmax of block j+1. No tensor map; each CTA loads only into its own shared memory.
 //  * Scores are exponentiated with exp2 and scale*log2(e) folded into one multiply.
 //  * Row max is reduced with three xor-shuffles across the 8 lanes that share a row; row sums
 //    stay per thread and are reduced once at the end.

@@ -23,7 +23,7 @@
 // rescale O in TMEM. The first PV of a tile overwrites O once the previous tile's epilogue has
 // read it.
 // Q and K tiles are loaded with the 128-byte swizzle (K-major operands), V tiles with the
-// 128-byte / 32-byte-atom swizzle (the MN-major TF32 operand layout); no multicast.
+// 128-byte / 32-byte-atom swizzle (the MN-major TF32 operand layout); every CTA loads only its own tiles.
 // Every wait is bounded; on a timeout the CTA records the failure, drains the MMAs it issued,
 // frees its TMEM and leaves.
 #include "tcgen05.cuh"

@@ -76,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// ---- bulk async copy global -> shared (no tensor map, no multicast) --------------------------------
+// ---- bulk async copy global -> shared (no tensor map, this CTA only) --------------------------------
 // Both addresses 16-byte aligned, bytes a multiple of 16. Completion is signalled on `bar` as
 // transaction bytes.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {

@@ -125,7 +125,7 @@ __device__ __forceinline__ void tmem_st64(uint32_t taddr, const float (&v)[64]) 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// ---- tiled TMA load (2-D, no multicast), completion as transaction bytes on `bar` ---------------
+// ---- tiled TMA load (2-D, into this CTA only), completion as transaction bytes on `bar` ---------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar) {
   asm volatile(
