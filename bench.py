@@ -218,6 +218,125 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------------------------------------
+def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
+    """BASELINE.json configs[0..3] as extra figures: DiT self (B=2), DiT cross (128 ragged
+    sequences), T5 (256 prompts, ragged L, bias), VAE mid-block (1, 8, 64 images). Each rep is one
+    flush of the call site's calls, timed with CUDA events after the L2 is flushed; FP32 and TF32
+    requests both reported with the kernels that ran (TF32 requests the tensor-core kernel does
+    not cover run the FP32 kernels)."""
+    import supra_attn
+
+    peaks = measured_peaks()
+    fp32_peak = 148 * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MB > L2
+    g = torch.Generator(device=dev).manual_seed(seed)
+    gc = torch.Generator().manual_seed(seed)
+    out = {}
+
+    def run(name, units, unit_name, make_descs, flops, bytes_):
+        res = {}
+        for variant in ("fp32", "tf32"):
+            descs = make_descs(variant)
+            gpu.enqueue_batch(descs)
+            gpu.sync()
+            gpu.profile(True)
+            gpu.profile_reset()
+            times = []
+            for _ in range(reps):
+                flush.fill_(1.0)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                gpu.enqueue_batch(descs)
+                gpu.flush()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            prof = gpu.profile_report()
+            gpu.profile(False)
+            ms = statistics.median(times)
+            res[variant] = {"ms": ms, f"{unit_name}_per_s": units / (ms / 1e3),
+                            "tflops": flops / (ms / 1e3) / 1e12, "gbs": bytes_ / (ms / 1e3) / 1e9,
+                            "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                            "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
+                            "kernels": sorted({p["name"] for p in prof})}
+        out[name] = res
+
+    # configs[0]: DiT self-attention, B = 2, interleaved qkv
+    qkv = torch.randn(2 * 256 * 1728, device=dev, generator=g)
+    o1 = torch.empty(2 * 256 * 576, device=dev)
+
+    def c1(variant):
+        arr = (supra_attn.Desc * 2)()
+        for b in range(2):
+            r = b * 256 * 1728
+            arr[b] = supra_attn.make_desc(q=qkv, k=qkv, v=qkv, out=o1, Lq=256, Lk=256, H=9, D=64, ldq=1728, ldk=1728,
+                                          ldv=1728, qOff=r, kOff=r + 576, vOff=r + 1152, oOff=b * 256 * 576,
+                                          variant=variant)
+        return arr
+
+    f1 = 2 * 4.0 * 256 * 256 * 64 * 9
+    run("dit_self_b2", 2, "seq", c1, f1, 2 * 4.0 * (2 * 256 * 576 + 2 * 256 * 576))
+
+    # configs[1]: DiT cross-attention, 64 prompts x CFG, ragged L
+    Ls = torch.randint(1, 129, (128,), generator=gc).tolist()
+    q2 = torch.randn(128 * 256 * 576, device=dev, generator=g)
+    kv2 = [torch.randn(L * 1152, device=dev, generator=g) for L in Ls]
+    o2 = torch.empty_like(q2)
+
+    def c2(variant):
+        arr = (supra_attn.Desc * 128)()
+        for b, L in enumerate(Ls):
+            arr[b] = supra_attn.make_desc(q=q2, k=kv2[b], v=kv2[b], out=o2, Lq=256, Lk=L, H=9, D=64, ldq=576,
+                                          ldk=1152, ldv=1152, qOff=b * 256 * 576, kOff=0, vOff=576,
+                                          oOff=b * 256 * 576, variant=variant)
+        return arr
+
+    run("dit_cross_128", 128, "seq", c2, sum(4.0 * 256 * L * 64 * 9 for L in Ls),
+        sum(4.0 * (2 * 256 * 576 + 2 * L * 576) for L in Ls))
+
+    # configs[2]: T5 encoder attention, 256 prompts, ragged L, relative-position bias, scale 1
+    Lt = torch.randint(1, 129, (256,), generator=gc).tolist()
+    table = (torch.randn(32 * 12, generator=gc) * 0.1).to(dev)
+    qs = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
+    ks = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
+    vs = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
+    os_ = [torch.empty(L * 768, device=dev) for L in Lt]
+    biases = [gpu.wrap(torch.empty(12 * L * L, device=dev)) for L in Lt]
+    for L, bt in zip(Lt, biases):
+        supra_attn.position_bias(gpu, table, L, H=12, out=bt)
+    gpu.sync()
+
+    def c3(variant):
+        arr = (supra_attn.Desc * 256)()
+        for i, L in enumerate(Lt):
+            arr[i] = supra_attn.make_desc(q=qs[i], k=ks[i], v=vs[i], out=os_[i], bias=biases[i], Lq=L, Lk=L, H=12, D=64,
+                                          ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
+        return arr
+
+    run("t5_256", 256, "prompt", c3, sum(4.0 * L * L * 64 * 12 for L in Lt),
+        sum(4.0 * (4 * L * 768 + 12 * L * L) for L in Lt))
+
+    # configs[3]: VAE mid-block single-head attention, 1024 tokens x 512 channels
+    for nimg in (1, 8, 64):
+        qv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
+        kvv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
+        vv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
+        ov = torch.empty_like(qv)
+
+        def c4(variant, nimg=nimg, qv=qv, kvv=kvv, vv=vv, ov=ov):
+            arr = (supra_attn.Desc * nimg)()
+            for i in range(nimg):
+                o = i * 1024 * 512
+                arr[i] = supra_attn.make_desc(q=qv, k=kvv, v=vv, out=ov, Lq=1024, Lk=1024, H=1, D=512, ldq=512,
+                                              ldk=512, ldv=512, qOff=o, kOff=o, vOff=o, oOff=o, variant=variant)
+            return arr
+
+        run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -230,6 +349,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tf32", action="store_true", help="skip the TF32 tensor-core pass")
+    ap.add_argument("--no-sites", action="store_true", help="skip the per-call-site figures (configs[0..3])")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -245,6 +365,9 @@ def main():
         return
 
     import datetime
+
+    # NCCL would print its version line on stdout, which must carry exactly one JSON line
+    os.environ["NCCL_DEBUG"] = "WARN"
 
     import torch
     import torch.distributed as dist
@@ -512,6 +635,10 @@ def main():
             for i in range(S):
                 arr[i].variant = supra_attn._lib.FP32
 
+    sites = None
+    if rank == 0 and world == 1 and not args.no_sites:
+        sites = measure_call_sites(gpu, torch, dev, args.seed)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, threads, sample = cpu_port_rate(32, args.cpu_seconds, args.seed, lengths)
@@ -535,6 +662,7 @@ def main():
             "e2e": e2e,
             "kernels": prof,
             "variants": {"tf32": tf32} if tf32 else {},
+            "call_sites": sites,
         }
         print(json.dumps(line), flush=True)
 
