@@ -1,5 +1,7 @@
 // TF32 tensor-core attention for sm_100a: tcgen05.mma with TMEM accumulators, TMA-staged tiles.
-// Head dim 64, no bias (the DiT self/cross-attention call sites, app/models/dit.js:172,184).
+// Head dim 64 (the DiT self/cross-attention call sites, app/models/dit.js:172,184, and the T5
+// encoder attention, app/models/t5.js:80, whose [H, Lq, Lk] relative-position bias the softmax
+// warps add to the scores read from TMEM).
 //
 // Same math as the reference's fused kernel (app/gpu/kernels.js:164-316: online softmax over key
 // blocks, O / l at the end), with both contractions on the 5th-generation tensor cores:
@@ -109,6 +111,7 @@ __device__ __forceinline__ Tile tile_of(const Tf32Launch& L, int t) {
   return r;
 }
 
+template <bool BIAS>
 __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_constant__ Tf32Launch L) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -282,11 +285,22 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
         tc::tmem_wait_ld();
         const int nk = min(kN, Lk - j * kN);
         float mx = -INFINITY;
+        if (BIAS && T.q0 + row < Lq) {
+          // this thread's query row of the bias, keys j*64 .. j*64 + nk (exp2 domain: times log2 e)
+          const float* brow = pp->bias + ((int64_t)T.h * Lq + T.q0 + row) * Lk + (int64_t)j * kN;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float x = (c < nk) ? v[c] * sl2 : -INFINITY;
-          v[c] = x;
-          mx = fmaxf(mx, x);
+          for (int c = 0; c < 64; ++c) {
+            const float x = (c < nk) ? fmaf(__ldg(brow + c), 1.4426950408889634f, v[c] * sl2) : -INFINITY;
+            v[c] = x;
+            mx = fmaxf(mx, x);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            const float x = (c < nk) ? v[c] * sl2 : -INFINITY;
+            v[c] = x;
+            mx = fmaxf(mx, x);
+          }
         }
         const bool move = mx > m + 8.f;
         if (j > 0 && __any_sync(0xffffffffu, move)) {
@@ -360,14 +374,15 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
 
 int attn_tf32_tile_rows() { return kM; }
 
-cudaError_t launch_attn_tf32(const Tf32Launch& L, cudaStream_t s) {
+cudaError_t launch_attn_tf32(const Tf32Launch& L, bool bias, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(attn_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  auto k = bias ? attn_tf32_kernel<true> : attn_tf32_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = L.total < 2 * sms ? L.total : 2 * sms;  // persistent: two CTAs per SM
-  attn_tf32_kernel<<<grid, kThreads, SMEM_BYTES, s>>>(L);
+  k<<<grid, kThreads, SMEM_BYTES, s>>>(L);
   return cudaGetLastError();
 }
 

@@ -95,12 +95,12 @@ struct alignas(16) Tf32Prob {
   float* o;
   int64_t o_off;
   int64_t ldo;
+  const float* bias;  // [H, Lq, Lk] additive score bias, or nullptr
   int32_t Lq, Lk, H, D;
   int32_t mq, mk, mv;
   int32_t qx, qy, kx, ky, vx, vy;
   float scale_log2;
   int32_t q_tiles;
-  int32_t pad;
 };
 static_assert(sizeof(Tf32Prob) % 16 == 0, "Tf32Prob is packed into the descriptor ring");
 
@@ -112,7 +112,7 @@ struct Tf32Launch {
   int32_t* status;
 };
 
-cudaError_t launch_attn_tf32(const Tf32Launch& L, cudaStream_t s);
+cudaError_t launch_attn_tf32(const Tf32Launch& L, bool bias, cudaStream_t s);
 int attn_tf32_tile_rows();
 
 cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L,

@@ -471,14 +471,14 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   q.rows_v = d->ldv > 0 ? d->v_size / d->ldv : 0;
   if (d->variant == SUPRA_ATTN_TF32) {
     // The tensor-core kernel reads whole 32-column slabs of full buffer rows through TMA tensor
-    // maps: head dim 64, no bias, 16-byte aligned rows, every row of the problem a whole row of
-    // its buffer, and the heads inside one row. Other TF32 requests run the FP32 kernels, which
-    // are at least as accurate.
+    // maps: head dim 64, 16-byte aligned rows, every row of the problem a whole row of its
+    // buffer, and the heads inside one row (a bias is read directly). Other TF32 requests run
+    // the FP32 kernels, which are at least as accurate.
     auto rows_ok = [](int64_t off, int64_t ld, int64_t rows, int64_t nrows, int64_t HDc) {
       return ld >= 32 && ld <= (int64_t(1) << 30) && (off % ld) + HDc <= ld && off / ld + nrows <= rows &&
              rows <= (int64_t(1) << 31) - 1;
     };
-    const bool ok = d->D == 64 && !d->bias && q.aligned && d->Lq > 0 && aligned16(d->q) && aligned16(d->k) &&
+    const bool ok = d->D == 64 && q.aligned && d->Lq > 0 && aligned16(d->q) && aligned16(d->k) &&
                     aligned16(d->v) && d->q_off % 4 == 0 && d->k_off % 4 == 0 && d->v_off % 4 == 0 &&
                     rows_ok(d->q_off, d->ldq, q.rows_q, d->Lq, HD) && rows_ok(d->k_off, d->ldk, q.rows_k, d->Lk, HD) &&
                     rows_ok(d->v_off, d->ldv, q.rows_v, d->Lk, HD);
@@ -727,6 +727,7 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     t.o = P.o;
     t.o_off = P.o_off;
     t.ldo = P.ldo;
+    t.bias = P.bias;
     t.Lq = P.Lq;
     t.Lk = P.Lk;
     t.H = P.H;
@@ -781,8 +782,8 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   L.status = c->d_status;
   cudaError_t e;
   {
-    ProfScope ps(c, "attn_tf32_d64", flops, bytes);
-    e = supra::launch_attn_tf32(L, c->stream);
+    ProfScope ps(c, g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64", flops, bytes);
+    e = supra::launch_attn_tf32(L, g[0]->bias, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, "attn_tf32_d64");
   c->launches += 1;
