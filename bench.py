@@ -428,7 +428,7 @@ def main():
     recv = [torch.empty(shard_max, device=dev) for _ in range(world)] if (world > 1 and rank == 0) else None
     nstep = [0]
 
-    def gather_step():
+    def gather_step(oc):
         if world == 1:
             return
         i = nstep[0] % 2
@@ -436,7 +436,7 @@ def main():
         cur = torch.cuda.current_stream()
         if sent[i] is not None:
             cur.wait_event(sent[i])
-        send_bufs[i][: out_cross.numel()].copy_(out_cross)
+        send_bufs[i][: oc.numel()].copy_(oc)
         gather_stream.wait_stream(cur)
         with torch.cuda.stream(gather_stream):
             dist.gather(send_bufs[i], recv if rank == 0 else None, dst=0)
@@ -444,13 +444,13 @@ def main():
             ev.record(gather_stream)
         sent[i] = ev
 
-    def step():
+    def step(sd=self_d, cd=cross_d, oc=out_cross):
         for b in range(BLOCKS):
-            gpu.enqueue_batch(self_d)
+            gpu.enqueue_batch(sd)
             gpu.flush()
-            gpu.enqueue_batch(cross_d[b])
+            gpu.enqueue_batch(cd[b])
             gpu.flush()
-        gather_step()
+        gather_step(oc)
 
     def barrier():
         if world > 1:
@@ -527,6 +527,12 @@ def main():
                     "hbm_peak_gbs": peaks.get("hbm_gbs")}
 
     # ---- end to end through the public API with host buffers ------------------------------------
+    # Every step uploads its inputs (Q/K/V of the self-attention, Q of the cross-attention) from
+    # pinned host memory with supra_attn_upload and reads its result back with supra_attn_download
+    # (fromArray / read of app/gpu/device.js). The copies go through two more library contexts on
+    # their own streams, and the inputs and outputs are double-buffered, so step s computes while
+    # step s+1's inputs arrive and step s-1's output leaves. All copies of all K steps lie inside
+    # the timed region: it starts before the first upload and ends after the last read-back.
     e2e = None
     if not args.no_e2e:
         h_qkv = torch.empty(qkv.numel(), dtype=torch.float32, pin_memory=True)
@@ -535,27 +541,77 @@ def main():
         h_qkv.copy_(qkv)
         h_qx.copy_(qx)
 
+        sets = [(qkv, qx, out_cross, self_d, cross_d)]
+        qkv2, qx2, oc2 = torch.empty_like(qkv), torch.empty_like(qx), torch.empty_like(out_cross)
+        sd2 = (supra_attn.Desc * S)()
+        for i in range(S):
+            sd2[i] = self_d[i]
+            sd2[i].q = sd2[i].k = sd2[i].v = qkv2.data_ptr()
+        cd2 = []
+        for b in range(BLOCKS):
+            arr = (supra_attn.Desc * S)()
+            for i in range(S):
+                arr[i] = cross_d[b][i]
+                arr[i].q = qx2.data_ptr()
+                arr[i].out = oc2.data_ptr()
+            cd2.append(arr)
+        sets.append((qkv2, qx2, oc2, sd2, cd2))
+
+        up_stream = torch.cuda.Stream(device=dev)
+        down_stream = torch.cuda.Stream(device=dev)
+        up_gpu = supra_attn.GPU(local_rank, stream=up_stream)
+        down_gpu = supra_attn.GPU(local_rank, stream=down_stream)
         up, down = supra_attn.lib.supra_attn_upload, supra_attn.lib.supra_attn_download
+        comp = torch.cuda.current_stream()
 
-        def e2e_step():
-            # the step's inputs host -> device, the steps, the result device -> host (read())
-            supra_attn._lib.check(up(gpu.ctx, qkv.data_ptr(), h_qkv.data_ptr(), qkv.numel()), gpu.ctx)
-            supra_attn._lib.check(up(gpu.ctx, qx.data_ptr(), h_qx.data_ptr(), qx.numel()), gpu.ctx)
-            step()
-            supra_attn._lib.check(down(gpu.ctx, h_out.data_ptr(), out_cross.data_ptr(), out_cross.numel()), gpu.ctx)
+        def run_e2e(nsteps):
+            """Uploads, steps and read-backs of `nsteps` steps, pipelined over the two sets."""
+            computed = [None, None]
+            arrived = [None, None]
 
-        e2e_step()
+            def upload(s):
+                q_s, x_s = sets[s % 2][0], sets[s % 2][1]
+                if computed[s % 2] is not None:  # step s-2 read this set
+                    up_stream.wait_event(computed[s % 2])
+                supra_attn._lib.check(up(up_gpu.ctx, q_s.data_ptr(), h_qkv.data_ptr(), q_s.numel()), up_gpu.ctx)
+                supra_attn._lib.check(up(up_gpu.ctx, x_s.data_ptr(), h_qx.data_ptr(), x_s.numel()), up_gpu.ctx)
+                ev = torch.cuda.Event()
+                ev.record(up_stream)
+                arrived[s % 2] = ev
+
+            upload(0)
+            for s in range(nsteps + 1):
+                if s + 1 < nsteps:  # issued before step s is recorded: it lands while step s computes
+                    upload(s + 1)
+                if s < nsteps:
+                    _, _, o_s, sd_s, cd_s = sets[s % 2]
+                    comp.wait_event(arrived[s % 2])
+                    step(sd_s, cd_s, o_s)
+                    done = torch.cuda.Event()
+                    done.record(comp)
+                    computed[s % 2] = done
+                if s > 0:  # read back step s-1 while step s computes (blocks the host)
+                    o_p = sets[(s - 1) % 2][2]
+                    down_stream.wait_event(computed[(s - 1) % 2])
+                    supra_attn._lib.check(down(down_gpu.ctx, h_out.data_ptr(), o_p.data_ptr(), o_p.numel()),
+                                          down_gpu.ctx)
+            comp.wait_stream(down_stream)
+
+        run_e2e(2)
         torch.cuda.synchronize()
+        if gather_stream is not None:
+            gather_stream.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            e2e_step()
+        e0.record(comp)
+        up_stream.wait_event(e0)
+        down_stream.wait_event(e0)
+        run_e2e(args.steps)
         if gather_stream is not None:
-            torch.cuda.current_stream().wait_stream(gather_stream)
-        e1.record()
+            comp.wait_stream(gather_stream)
+        e1.record(comp)
         torch.cuda.synchronize()
         barrier()
         t2 = torch.tensor([e0.elapsed_time(e1)], device=dev)
@@ -564,7 +620,11 @@ def main():
         e2e = {"value": seq_calls / (float(t2.item()) / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": 4 * (qkv.numel() + qx.numel()) * world,
                "d2h_bytes_per_step": 4 * out_cross.numel() * world,
-               "ms_per_step": float(t2.item()) / args.steps}
+               "ms_per_step": float(t2.item()) / args.steps,
+               "pipeline": "inputs and outputs double-buffered; uploads, compute and read-backs on three streams"}
+        up_gpu.close()
+        down_gpu.close()
+        del qkv2, qx2, oc2
 
     # ---- the TF32 tensor-core variant on the same workload (its own tolerance, 2e-3) --------------
     tf32 = None

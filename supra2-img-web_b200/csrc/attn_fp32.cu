@@ -359,7 +359,7 @@ cudaError_t launch_cfg(bool bias, bool aligned, const AttnLaunch& L, cudaStream_
 }  // namespace
 
 int fused_cfg_tile_rows(int cfg) {
-  return cfg == CFG_D64_Q128 ? 128 : cfg == CFG_D64_W4 ? attn_fp32_w4_tile_rows() : 64;
+  return cfg == CFG_D64_Q128 ? 128 : 64;
 }
 int fused_cfg_head_dim(int cfg) { return cfg == CFG_D128_Q64 ? 128 : 64; }
 
@@ -369,7 +369,6 @@ cudaError_t launch_attn_fp32(int cfg, bool bias, bool aligned, const AttnLaunch&
     case CFG_D64_Q128: return launch_cfg<64, 128>(bias, aligned, L, s);
     case CFG_D64_Q64: return launch_cfg<64, 64>(bias, aligned, L, s);
     case CFG_D128_Q64: return launch_cfg<128, 64>(bias, aligned, L, s);
-    case CFG_D64_W4: return (bias || !aligned) ? cudaErrorInvalidValue : launch_attn_fp32_w4(L, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -379,7 +378,6 @@ const char* attn_fp32_name(int cfg, bool bias, bool aligned) {
       {{"attn_fp32_d64_q128_u", "attn_fp32_d64_q128"}, {"attn_fp32_d64_q128_bias_u", "attn_fp32_d64_q128_bias"}},
       {{"attn_fp32_d64_q64_u", "attn_fp32_d64_q64"}, {"attn_fp32_d64_q64_bias_u", "attn_fp32_d64_q64_bias"}},
       {{"attn_fp32_d128_q64_u", "attn_fp32_d128_q64"}, {"attn_fp32_d128_q64_bias_u", "attn_fp32_d128_q64_bias"}},
-      {{"attn_fp32_d64_w4_?", "attn_fp32_d64_w4"}, {"attn_fp32_d64_w4_?", "attn_fp32_d64_w4_?"}},
   };
   if (cfg < 0 || cfg >= CFG_COUNT) return "attn_fp32_?";
   return names[cfg][bias ? 1 : 0][aligned ? 1 : 0];

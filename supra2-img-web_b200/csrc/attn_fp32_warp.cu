@@ -1,45 +1,132 @@
-// Fused FP32 attention, warp-independent pipeline (sm_100a): D <= 64, no bias, 16-byte aligned rows.
+// Fused FP32 attention, persistent warp-pipelined kernel (sm_100a): D = 64, no bias, scale > 0.
 // The DiT self/cross-attention kernel (app/models/dit.js:172,184).
 //
 // Same algorithm as attn_fp32.cu (online softmax over key blocks, app/gpu/kernels.js:164-316),
-// reorganised so that the main loop has no block-wide barrier:
-//  * 4 warps x 32 query rows (128-row tile). Lane (rg = lane/8, cg = lane%8) of warp w owns rows
-//    32w + rg + 4i (i < 8), keys cg + 8j (j < 4) of each 32-key block and output columns
-//    4*(cg + 8u) .. +3 (u < 2): 8x4 score and 8x8 output register blocks.
-//  * Each warp stages its own 32 Q rows (bulk copies, its own mbarrier) and keeps its own P tile,
-//    so softmax -> PV needs only __syncwarp.
-//  * K/V blocks flow through a 3-stage ring of shared-memory stages filled by the bulk-copy (TMA)
-//    engine with one "full" mbarrier per stage (expect_tx). A warp that has finished a stage
-//    counts itself out on the stage's counter; the last warp out issues the refill for the block
-//    three ahead, so no warp ever waits for a producer and warps drift freely.
+// organised so that the main loop has no block-wide barrier and no start-up gap between tiles:
+//  * Persistent CTAs (two per SM): CTA c runs tiles c, c + grid, c + 2*grid, ... A tile is 128
+//    query rows of one head of one problem; the host orders problems longest-Lk first.
+//  * 4 warps x 32 query rows. Lane (rg = lane/8, cg = lane%8) of warp w owns rows 32w + rg + 4i
+//    (i < 8), keys cg + 8j (j < 4) of each 32-key block and output columns 4*(cg + 8u) .. +3
+//    (u < 2): 8x4 score and 8x8 output register blocks (FFMA only, fp32 throughout).
+//  * All operands arrive by TMA tensor copies (fp32 tensor maps, no rounding): one box per warp
+//    for its Q rows, one box each for the K and V rows of a 32-key block. Q and K boxes are 68
+//    columns wide, so their shared-memory rows are 68 floats apart and the fragment reads are
+//    free of bank conflicts; the 4 extra columns (the next head, or zero fill past the buffer)
+//    are never read.
+//  * The K/V blocks of all of a CTA's tiles form one sequence flowing through a 3-stage ring
+//    (one "full" mbarrier per stage, expect_tx). A warp that has finished a stage counts itself
+//    out on the stage's counter; the last warp out issues the block three ahead, which may
+//    belong to the CTA's next tile, through a cursor kept in shared memory. No warp waits for
+//    a producer, warps drift freely, and the next tile's first blocks are already in flight
+//    while the current tile finishes.
+//  * Each warp fetches its Q rows of the next tile as soon as it has finished the last QK^T of
+//    the current tile (its own Q rows are read by no other warp).
 //  * Lazy rescaling: the running row maximum used as the exp2 offset is only moved when a block
-//    exceeds it by more than 8 (a factor 256), so the O/l rescale is skipped on almost every block;
-//    the result is the same softmax (O and l always share one offset).
+//    exceeds it by more than 8 (a factor 256), so the O/l rescale is skipped on almost every
+//    block; the result is the same softmax (O and l always share one offset).
 //  * exp2 via ex2.approx.ftz (relative error ~2^-22), scale*log2(e) folded into the scores.
-//  * Ragged last blocks: whole 8-key groups past Lk are skipped in QK^T and PV; the rest are masked.
-//  * All waits are bounded (2 s); a timeout sets the device status word and the warp leaves.
+//  * Boxes are always whole (32 rows). Rows past Lq or Lk hold other rows of the buffer or zero
+//    fill: scores of keys past Lk are replaced (not multiplied) by -inf, V rows past Lk are not
+//    read, and rows past Lq are never stored, so no value there can reach a stored output.
+//  * All waits are bounded (2 s); a timeout sets the device status word and the CTA leaves.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace supra {
 namespace {
 
-constexpr int kW = 4;           // consumer warps per CTA
-constexpr int kRows = 32 * kW;  // query rows per tile
-constexpr int kNK = 32;         // keys per block
-constexpr int kNS = 3;          // K/V stages
-constexpr int kD = 64;          // head-dim capacity
-constexpr int kQS = kD + 4;     // Q row stride (floats)
-constexpr int kKS = kD + 4;     // K row stride
-constexpr int kVS = kD;         // V row stride
-constexpr int kPS = kNK + 8;    // P row stride: conflict-free scalar writes and float4 reads
+constexpr int kW = 4;             // warps per CTA
+constexpr int kRI = 8;            // query rows per lane
+constexpr int kRowsW = 4 * kRI;   // query rows per warp
+constexpr int kRows = kW * kRowsW;
+constexpr int kNK = kFwBoxRows;   // keys per block
+constexpr int kNS = 3;            // K/V stages
+constexpr int kD = 64;            // head dim
+constexpr int kQS = kFwBoxWide;   // Q row stride in shared memory (floats)
+constexpr int kKS = kFwBoxWide;   // K row stride
+constexpr int kVS = kFwBoxNarrow; // V row stride
+constexpr int kPS = kNK + 8;      // P row stride: conflict-free scalar writes and float4 reads
+static_assert(kRowsW == kFwBoxRows, "one Q box per warp");
+static_assert(kVS == kD && kQS >= kD, "box widths");
+
+constexpr uint32_t kQBytes = kRowsW * kQS * 4;
+constexpr uint32_t kKBytes = kNK * kKS * 4;
+constexpr uint32_t kVBytes = kNK * kVS * 4;
 
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + kRows * kQS;
 constexpr int OFF_V = OFF_K + kNS * kNK * kKS;
 constexpr int OFF_P = OFF_V + kNS * kNK * kVS;
-constexpr int FLOATS = OFF_P + kW * 32 * kPS;
-// barriers: qbar[kW], full[kNS] (8 B each), then the stage counters cnt[kNS] (4 B each)
-constexpr int BYTES = FLOATS * 4 + (kW + kNS) * 8 + kNS * 4 + 4;
+constexpr int FLOATS = OFF_P + kW * kRowsW * kPS;
+static_assert((OFF_K * 4) % 128 == 0 && (OFF_V * 4) % 128 == 0 && kQBytes % 128 == 0 && kKBytes % 128 == 0 &&
+                  kVBytes % 128 == 0,
+              "TMA destinations are 128-byte aligned");
+
+// Next K/V block of this CTA's block sequence: tile t, block b of its nblk, and the tile's TMA
+// coordinates (head column already added).
+struct Cursor {
+  int32_t t, b, nblk, mk, mv, kx, ky, vx, vy, pad;
+};
+struct Ctl {
+  uint64_t qbar[kW];
+  uint64_t full[kNS];
+  int32_t cnt[kNS];
+  int32_t pad;
+  Cursor cur;
+};
+constexpr int BYTES = FLOATS * 4 + (int)sizeof(Ctl) + 128;  // + slack for the 128-byte alignment
+
+struct Tile {
+  const TmaProb* p;
+  int h, q0, nblk;
+};
+
+__device__ __forceinline__ Tile tile_of(const TmaLaunch& L, int t) {
+  Tile r;
+  const int pidx = L.uniform > 0 ? t / L.uniform : find_problem(L.begin, L.n, t);
+  r.p = L.probs + pidx;
+  const int local = t - (L.uniform > 0 ? pidx * L.uniform : __ldg(L.begin + pidx));
+  const int qt = r.p->q_tiles;
+  r.h = local / qt;
+  r.q0 = (local - r.h * qt) * kRows;
+  r.nblk = (r.p->Lk + kNK - 1) / kNK;
+  return r;
+}
+
+__device__ __forceinline__ void cursor_at(const TmaLaunch& L, Cursor& c, int t) {
+  const Tile T = tile_of(L, t);
+  c.t = t;
+  c.b = 0;
+  c.nblk = T.nblk;
+  c.mk = T.p->mk;
+  c.mv = T.p->mv;
+  c.kx = T.p->kx + T.h * kD;
+  c.ky = T.p->ky;
+  c.vx = T.p->vx + T.h * kD;
+  c.vy = T.p->vy;
+}
+
+// Issues the cursor's block into stage s and advances the cursor (one thread). Past the CTA's
+// last tile it issues nothing: no warp will wait for that stage again.
+__device__ __forceinline__ void issue_next(const TmaLaunch& L, Ctl* C, float* Ks, float* Vs, int s) {
+  Cursor& c = C->cur;
+  if (c.t >= L.total) return;
+  uint64_t* bar = &C->full[s];
+  mbar_arrive_expect_tx(bar, kKBytes + kVBytes);
+  tc::tma_load_2d(Ks + s * kNK * kKS, L.maps + c.mk, c.kx, c.ky + c.b * kNK, bar);
+  tc::tma_load_2d(Vs + s * kNK * kVS, L.maps + c.mv, c.vx, c.vy + c.b * kNK, bar);
+  if (++c.b == c.nblk) {
+    const int tn = c.t + (int)gridDim.x;
+    if (tn < L.total) cursor_at(L, c, tn);
+    else c.t = tn;
+  }
+}
+
+// This warp's 32 Q rows of tile T into its Q region (one thread).
+__device__ __forceinline__ void issue_q(const TmaLaunch& L, const Tile& T, int w, float* dst, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, kQBytes);
+  tc::tma_load_2d(dst, L.maps + T.p->mq, T.p->qx + T.h * kD, T.p->qy + T.q0 + w * kRowsW, bar);
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -47,222 +134,186 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(kW * 32, 2) attn_fp32_w4_kernel(const AttnLaunch L) {
-  extern __shared__ __align__(128) float smem[];
+__global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid_constant__ TmaLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  float* smem = reinterpret_cast<float*>(smem_raw + (((raw + 127u) & ~127u) - raw));
   float* Qs = smem + OFF_Q;
   float* Ks = smem + OFF_K;
   float* Vs = smem + OFF_V;
-  uint64_t* qbar = reinterpret_cast<uint64_t*>(smem + FLOATS);
-  uint64_t* full = qbar + kW;
-  int* cnt = reinterpret_cast<int*>(full + kNS);
+  Ctl* C = reinterpret_cast<Ctl*>(smem + FLOATS);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int w = tid >> 5;
   const int rg = lane >> 3;
   const int cg = lane & 7;
-  float* Pw = smem + OFF_P + w * 32 * kPS;
+  float* Pw = smem + OFF_P + w * kRowsW * kPS;
+  float* Qw = Qs + w * kRowsW * kQS;
 
-  const int t = blockIdx.x;
-  if (t >= L.total) {
-    if (tid == 0) report_error(L.status, DEV_BAD_TILE, 0);
+  const int t0 = blockIdx.x;
+  if (t0 >= L.total) {  // the host sizes the grid to at most one CTA per tile
+    if (tid == 0) report_error(L.status, DEV_BAD_TILE, 20);
     return;
   }
-  const int pidx = L.uniform > 0 ? t / L.uniform : find_problem(L.begin, L.n, t);
-  const AttnProb* __restrict__ pp = L.probs + pidx;
-  const int local = t - (L.uniform > 0 ? pidx * L.uniform : __ldg(L.begin + pidx));
-  const int q_tiles = pp->q_tiles;
-  const int h = local / q_tiles;
-  const int q0 = (local - h * q_tiles) * kRows;
-  const int Lq = pp->Lq, Lk = pp->Lk, D = pp->D;
-  const int rows_q = min(kRows, Lq - q0);
-  const int nwa = (rows_q + 31) >> 5;  // warps with at least one valid row
-  const int nblk = (Lk + kNK - 1) / kNK;
-  const int64_t ldq = pp->ldq, ldk = pp->ldk, ldv = pp->ldv;
-  const float* qsrc = pp->q + pp->q_off + (int64_t)q0 * ldq + (int64_t)h * D;
-  const float* ksrc = pp->k + pp->k_off + (int64_t)h * D;
-  const float* vsrc = pp->v + pp->v_off + (int64_t)h * D;
-  const float sl2 = pp->scale_log2;
-  const uint32_t row_bytes = (uint32_t)D * 4u;
-
-  // ---- set-up (the kernel's only block-wide barrier) ------------------------------------------------
   if (tid == 0) {
-    for (int i = 0; i < kW; ++i) mbar_init(&qbar[i], 1);
+    for (int i = 0; i < kW; ++i) mbar_init(&C->qbar[i], 1);
     for (int s = 0; s < kNS; ++s) {
-      mbar_init(&full[s], 1);
-      cnt[s] = 0;
+      mbar_init(&C->full[s], 1);
+      C->cnt[s] = 0;
     }
     mbar_fence_init();
   }
-  if (D < kD) {  // padding columns of Q and K take part in the dot products: zero them
-    for (int idx = tid; idx < kRows * (kD - D); idx += kW * 32) {
-      const int r = idx / (kD - D);
-      Qs[r * kQS + D + (idx - r * (kD - D))] = 0.f;
-    }
-    for (int idx = tid; idx < kNS * kNK * (kD - D); idx += kW * 32) {
-      const int r = idx / (kD - D);
-      Ks[r * kKS + D + (idx - r * (kD - D))] = 0.f;
-    }
+  __syncthreads();  // the kernel's only block-wide barrier
+  if (tid == 0) {
+    cursor_at(L, C->cur, t0);
+    for (int s = 0; s < kNS; ++s) issue_next(L, C, Ks, Vs, s);
   }
-  if (rows_q < kRows) {  // query rows past Lq: keep their (never stored) scores finite
-    for (int idx = tid; idx < (kRows - rows_q) * kD; idx += kW * 32) {
-      const int r = rows_q + idx / kD;
-      Qs[r * kQS + (idx % kD)] = 0.f;
-    }
-  }
-  if (Lk % kNK != 0) {  // V rows past Lk meet P == 0 and must hold finite values
-    float4* V4 = reinterpret_cast<float4*>(Vs);
-    for (int idx = tid; idx < kNS * kNK * kVS / 4; idx += kW * 32) V4[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (w >= nwa) return;  // no valid rows: this warp takes no part (nwa counts the stage users)
+  Tile T = tile_of(L, t0);
+  if (lane == 0) issue_q(L, T, w, Qw, &C->qbar[w]);
 
-  // K and V rows of block b into stage s, issued by one warp
-  auto issue_block = [&](int b, int s) {
-    const int k0 = b * kNK;
-    const int nk = min(kNK, Lk - k0);
-    if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * row_bytes * (uint32_t)nk);
-    __syncwarp();
-    float* kd = Ks + s * kNK * kKS;
-    float* vd = Vs + s * kNK * kVS;
-    for (int r = lane; r < nk; r += 32) {
-      bulk_g2s(kd + r * kKS, ksrc + (int64_t)(k0 + r) * ldk, row_bytes, &full[s]);
-      bulk_g2s(vd + r * kVS, vsrc + (int64_t)(k0 + r) * ldv, row_bytes, &full[s]);
-    }
-  };
+  const float4* Q4 = reinterpret_cast<const float4*>(Qw) + rg * (kQS / 4);
+  const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
+  uint32_t g = 0;  // position in the CTA's K/V block sequence
+  uint32_t k = 0;  // position in the CTA's tile sequence
+  for (int t = t0; t < L.total; t += (int)gridDim.x, ++k) {
+    const TmaProb* __restrict__ pp = T.p;
+    const int Lk = pp->Lk;
+    const float sl2 = pp->scale_log2;
+    const int nblk = T.nblk;
+    Tile Tn = T;
 
-  // own Q rows
-  const int my_rows = min(32, rows_q - 32 * w);
-  if (lane == 0) mbar_arrive_expect_tx(&qbar[w], row_bytes * (uint32_t)my_rows);
-  __syncwarp();
-  for (int r = lane; r < my_rows; r += 32)
-    bulk_g2s(Qs + (32 * w + r) * kQS, qsrc + (int64_t)(32 * w + r) * ldq, row_bytes, &qbar[w]);
-  if (w == 0)
-    for (int b = 0; b < min(kNS, nblk); ++b) issue_block(b, b);
-
-  float4 o[8][2];
-  float mo[8], l[8];
+    float4 o[kRI][2];
+    float mo[kRI], l[kRI];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    mo[i] = -INFINITY;
-    l[i] = 0.f;
-    o[i][0] = o[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-
-  if (!mbar_wait_bounded(&qbar[w], 0)) {
-    if (lane == 0) report_error(L.status, DEV_TIMEOUT, 10);
-    return;
-  }
-  const float4* Q4 = reinterpret_cast<const float4*>(Qs) + (32 * w + rg) * (kQS / 4);
-
-  for (int j = 0; j < nblk; ++j) {
-    const int s = j % kNS;
-    const uint32_t par = (uint32_t)((j / kNS) & 1);
-    const int nk = min(kNK, Lk - j * kNK);
-    if (!mbar_wait_bounded(&full[s], par)) {
-      if (lane == 0) report_error(L.status, DEV_TIMEOUT, 11);
+    for (int i = 0; i < kRI; ++i) {
+      mo[i] = -INFINITY;
+      l[i] = 0.f;
+      o[i][0] = o[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (!mbar_wait_bounded(&C->qbar[w], k & 1u)) {
+      if (lane == 0) report_error(L.status, DEV_TIMEOUT, 21, (int32_t)k);
       return;
     }
-    const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
-    const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
 
-    // ---- S = Q K^T. Component-major order: for each 4-deep slice of the head dim, the 32
-    // products of one component are independent FFMAs, so no accumulator waits on its previous
-    // update. Keys past Lk in a partial block are computed from stale rows and masked below.
-    float sc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.f;
-#pragma unroll 2
-    for (int d4 = 0; d4 < kD / 4; ++d4) {
-      float4 kf[4], qf[8];
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) kf[jj] = K4[jj * 8 * (kKS / 4) + d4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) qf[i] = Q4[i * 4 * (kQS / 4) + d4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].x, kf[jj].x, sc[i][jj]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].y, kf[jj].y, sc[i][jj]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].z, kf[jj].z, sc[i][jj]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].w, kf[jj].w, sc[i][jj]);
-    }
-    if (nk < kNK) {  // partial block (warp-uniform): mask the keys past Lk
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = (cg + 8 * jj < nk) ? sc[i][jj] : -INFINITY;
-    }
-
-    // ---- softmax with a lazily moved offset (exp2 domain). scale > 0 (host-checked), so the
-    // maximum of the raw scores times scale*log2(e) is the maximum of the scaled scores.
-    bool any_move = false;
-    float mprev[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float mr = fmaxf(fmaxf(sc[i][0], sc[i][1]), fmaxf(sc[i][2], sc[i][3]));
-      mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
-      mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
-      mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
-      const float mx = mr * sl2;
-      mprev[i] = mo[i];
-      if (mx > mo[i] + 8.f) {
-        mo[i] = mx;
-        any_move = true;
+    for (int j = 0; j < nblk; ++j, ++g) {
+      const int s = (int)(g % kNS);
+      const uint32_t par = (g / kNS) & 1u;
+      const int nk = min(kNK, Lk - j * kNK);
+      if (!mbar_wait_bounded(&C->full[s], par)) {
+        if (lane == 0) report_error(L.status, DEV_TIMEOUT, 22, (int32_t)g);
+        return;
       }
-    }
-    if (__any_sync(0xffffffffu, any_move)) {
+      const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
+      const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
+
+      // ---- S = Q K^T. Component-major order: for each 4-deep slice of the head dim, the 32
+      // products of one component are independent FFMAs, so no accumulator waits on its
+      // previous update.
+      float sc[kRI][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float alpha = ex2(mprev[i] - mo[i]);
-        l[i] *= alpha;
+      for (int i = 0; i < kRI; ++i)
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          o[i][u].x *= alpha;
-          o[i][u].y *= alpha;
-          o[i][u].z *= alpha;
-          o[i][u].w *= alpha;
+        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.f;
+#pragma unroll 2
+      for (int d4 = 0; d4 < kD / 4; ++d4) {
+        float4 kf[4], qf[kRI];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) kf[jj] = K4[jj * 8 * (kKS / 4) + d4];
+#pragma unroll
+        for (int i = 0; i < kRI; ++i) qf[i] = Q4[i * 4 * (kQS / 4) + d4];
+#pragma unroll
+        for (int i = 0; i < kRI; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].x, kf[jj].x, sc[i][jj]);
+#pragma unroll
+        for (int i = 0; i < kRI; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].y, kf[jj].y, sc[i][jj]);
+#pragma unroll
+        for (int i = 0; i < kRI; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].z, kf[jj].z, sc[i][jj]);
+#pragma unroll
+        for (int i = 0; i < kRI; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].w, kf[jj].w, sc[i][jj]);
+      }
+      if (j == nblk - 1) {  // this warp's Q rows are done: fetch its rows of the next tile
+        const int tn = t + (int)gridDim.x;
+        if (tn < L.total) {
+          Tn = tile_of(L, tn);
+          __syncwarp();
+          if (lane == 0) {
+            fence_proxy_async_smem();
+            issue_q(L, Tn, w, Qw, &C->qbar[w]);
+          }
         }
       }
-    }
+      if (nk < kNK) {  // partial block (warp-uniform): keys past Lk get -inf (a select, not a product)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kRI; ++i)
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const float pe = ex2(fmaf(sc[i][jj], sl2, -mo[i]));
-        l[i] += pe;
-        Pw[(rg + 4 * i) * kPS + cg + 8 * jj] = pe;
+          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = (cg + 8 * jj < nk) ? sc[i][jj] : -INFINITY;
       }
-    }
-    __syncwarp();
 
-    // ---- O += P V ----------------------------------------------------------------------------
-    {
-      const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
-      const int k4end = (nk + 3) >> 2;  // groups of 4 keys with a valid key (8 in full blocks)
-#pragma unroll 2
-      for (int k4 = 0; k4 < k4end; ++k4) {
-        float4 pf[8];
+      // ---- softmax with a lazily moved offset (exp2 domain). scale > 0 (host-checked), so the
+      // maximum of the raw scores times scale*log2(e) is the maximum of the scaled scores.
+      bool any_move = false;
+      float mprev[kRI];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pf[i] = P4[i * 4 * (kPS / 4) + k4];
+      for (int i = 0; i < kRI; ++i) {
+        float mr = fmaxf(fmaxf(sc[i][0], sc[i][1]), fmaxf(sc[i][2], sc[i][3]));
+        mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
+        mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
+        mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
+        const float mx = mr * sl2;
+        mprev[i] = mo[i];
+        if (mx > mo[i] + 8.f) {
+          mo[i] = mx;
+          any_move = true;
+        }
+      }
+      if (__any_sync(0xffffffffu, any_move)) {
+#pragma unroll
+        for (int i = 0; i < kRI; ++i) {
+          const float alpha = ex2(mprev[i] - mo[i]);
+          l[i] *= alpha;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            o[i][u].x *= alpha;
+            o[i][u].y *= alpha;
+            o[i][u].z *= alpha;
+            o[i][u].w *= alpha;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRI; ++i) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const float pe = ex2(fmaf(sc[i][jj], sl2, -mo[i]));
+          l[i] += pe;
+          Pw[(rg + 4 * i) * kPS + cg + 8 * jj] = pe;
+        }
+      }
+      __syncwarp();
+
+      // ---- O += P V: whole groups of 4 valid keys, then the ragged group, whose V rows past
+      // Lk are replaced by zeros (they may hold anything, and 0 * inf is not 0).
+      auto pv_group = [&](int k4, int valid) {
+        float4 pf[kRI];
+#pragma unroll
+        for (int i = 0; i < kRI; ++i) pf[i] = P4[i * 4 * (kPS / 4) + k4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float4 v0 = V4[(k4 * 4 + e) * (kVS / 4)];
-          const float4 v1 = V4[(k4 * 4 + e) * (kVS / 4) + 8];
+          float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+          if (e < valid) {
+            v0 = V4[(k4 * 4 + e) * (kVS / 4)];
+            v1 = V4[(k4 * 4 + e) * (kVS / 4) + 8];
+          }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < kRI; ++i) {
             const float pe = e == 0 ? pf[i].x : e == 1 ? pf[i].y : e == 2 ? pf[i].z : pf[i].w;
             o[i][0].x = fmaf(pe, v0.x, o[i][0].x);
             o[i][0].y = fmaf(pe, v0.y, o[i][0].y);
@@ -274,58 +325,60 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_w4_kernel(const AttnLaun
             o[i][1].w = fmaf(pe, v1.w, o[i][1].w);
           }
         }
-      }
-    }
-    __syncwarp();  // every lane is done with P and with stage s
+      };
+      const int nfull = nk >> 2;
+#pragma unroll 2
+      for (int k4 = 0; k4 < nfull; ++k4) pv_group(k4, 4);
+      if (nk & 3) pv_group(nfull, nk & 3);
+      __syncwarp();  // every lane is done with P and with stage s
 
-    // ---- release stage s; the last warp out refills it with block j + kNS ------------------------
-    int last = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      last = (atomicAdd(&cnt[s], 1) == nwa - 1);
-      if (last) {
-        atomicExch(&cnt[s], 0);
+      // ---- release stage s; the last warp out loads the block three ahead into it -----------
+      if (lane == 0) {
         __threadfence_block();
+        if (atomicAdd(&C->cnt[s], 1) == kW - 1) {
+          atomicExch(&C->cnt[s], 0);
+          __threadfence_block();
+          fence_proxy_async_smem();
+          issue_next(L, C, Ks, Vs, s);
+        }
       }
     }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last && j + kNS < nblk) {
-      fence_proxy_async_smem();
-      issue_block(j + kNS, s);
-    }
-  }
 
-  // ---- O / l, rows < Lq ----------------------------------------------------------------------
+    // ---- O / l, rows < Lq ------------------------------------------------------------------
+    const int rows_q = min(kRows, pp->Lq - T.q0);
+    float* obase = pp->o + pp->o_off + (int64_t)T.q0 * pp->ldo + (int64_t)T.h * kD;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float ls = l[i];
-    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 4);
-    const float inv = 1.0f / ls;
-    const int r = 32 * w + rg + 4 * i;
-    if (r < rows_q) {
-      float* dst = pp->o + pp->o_off + (int64_t)(q0 + r) * pp->ldo + (int64_t)h * D;
+    for (int i = 0; i < kRI; ++i) {
+      float ls = l[i];
+      ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+      ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+      const float inv = 1.0f / ls;
+      const int r = kRowsW * w + rg + 4 * i;
+      if (r < rows_q) {
+        float* dst = obase + (int64_t)r * pp->ldo;
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = 4 * (cg + 8 * u);
-        if (c < D)
-          *reinterpret_cast<float4*>(dst + c) =
+        for (int u = 0; u < 2; ++u)
+          *reinterpret_cast<float4*>(dst + 4 * (cg + 8 * u)) =
               make_float4(o[i][u].x * inv, o[i][u].y * inv, o[i][u].z * inv, o[i][u].w * inv);
       }
     }
+    T = Tn;
   }
 }
 
 }  // namespace
 
-int attn_fp32_w4_tile_rows() { return kRows; }
+int attn_fp32_warp_tile_rows() { return kRows; }
 
-cudaError_t launch_attn_fp32_w4(const AttnLaunch& L, cudaStream_t s) {
+cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(attn_fp32_w4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+  cudaError_t e = cudaFuncSetAttribute(attn_fp32_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
   if (e != cudaSuccess) return e;
-  attn_fp32_w4_kernel<<<L.total, kW * 32, BYTES, s>>>(L);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = L.total < 2 * sms ? L.total : 2 * sms;  // persistent: two CTAs per SM
+  attn_fp32_warp_kernel<<<grid, kW * 32, BYTES, s>>>(L);
   return cudaGetLastError();
 }
 

@@ -96,10 +96,10 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 
 // A tile of the launch: problem, head and first query row.
 struct Tile {
-  const Tf32Prob* p;
+  const TmaProb* p;
   int h, q0, nblk;
 };
-__device__ __forceinline__ Tile tile_of(const Tf32Launch& L, int t) {
+__device__ __forceinline__ Tile tile_of(const TmaLaunch& L, int t) {
   Tile r;
   const int pidx = L.uniform > 0 ? t / L.uniform : find_problem(L.begin, L.n, t);
   r.p = L.probs + pidx;
@@ -112,7 +112,7 @@ __device__ __forceinline__ Tile tile_of(const Tf32Launch& L, int t) {
 }
 
 template <bool BIAS>
-__global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_constant__ Tf32Launch L) {
+__global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_constant__ TmaLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned for the swizzle atoms
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
       int n = 0, k = 0;
       for (int t = blockIdx.x; t < L.total; t += gridDim.x, ++k) {
         const Tile T = tile_of(L, t);
-        const Tf32Prob* pp = T.p;
+        const TmaProb* pp = T.p;
         const CUtensorMap* mq = L.maps + pp->mq;
         const CUtensorMap* mk = L.maps + pp->mk;
         const CUtensorMap* mv = L.maps + pp->mv;
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
     float v[64];
     for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
       const Tile T = tile_of(L, t);
-      const Tf32Prob* pp = T.p;
+      const TmaProb* pp = T.p;
       const int Lk = pp->Lk, Lq = pp->Lq;
       const float sl2 = pp->scale_log2;
       float m = -INFINITY, l = 0.f;
@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
 
 int attn_tf32_tile_rows() { return kM; }
 
-cudaError_t launch_attn_tf32(const Tf32Launch& L, bool bias, cudaStream_t s) {
+cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
   auto k = bias ? attn_tf32_kernel<true> : attn_tf32_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);

@@ -73,8 +73,7 @@ enum FusedCfg : int32_t {
   CFG_D64_Q128 = 0,
   CFG_D64_Q64 = 1,
   CFG_D128_Q64 = 2,
-  CFG_D64_W4 = 3,  // warp-independent pipeline (attn_fp32_warp.cu): D <= 64, no bias, aligned
-  CFG_COUNT = 4,
+  CFG_COUNT = 3,
 };
 int fused_cfg_tile_rows(int cfg);
 int fused_cfg_head_dim(int cfg);
@@ -82,16 +81,15 @@ int fused_cfg_head_dim(int cfg);
 // Launchers. Each returns the cudaError_t of the launch (cudaSuccess on success).
 cudaError_t launch_attn_fp32(int cfg, bool bias, bool aligned, const AttnLaunch& L, cudaStream_t s);
 const char* attn_fp32_name(int cfg, bool bias, bool aligned);
-cudaError_t launch_attn_fp32_w4(const AttnLaunch& L, cudaStream_t s);
-int attn_fp32_w4_tile_rows();
 
 cudaError_t launch_gemm_qk(bool bias, bool aligned, const GemmLaunch& L, cudaStream_t s);
 cudaError_t launch_softmax_rows(const GemmLaunch& L, cudaStream_t s);
 cudaError_t launch_gemm_pv(bool aligned, const GemmLaunch& L, cudaStream_t s);
 
-// TF32 tensor-core path (attn_tf32.cu): one problem with its TMA tensor-map indices and the
+// Problems read through TMA tensor maps (the TF32 tensor-core kernel, attn_tf32.cu, and the
+// persistent FP32 kernel, attn_fp32_warp.cu): one problem with its tensor-map indices and the
 // TMA coordinates (x = column, y = row) of head 0 / row 0 of each operand.
-struct alignas(16) Tf32Prob {
+struct alignas(16) TmaProb {
   float* o;
   int64_t o_off;
   int64_t ldo;
@@ -102,18 +100,27 @@ struct alignas(16) Tf32Prob {
   float scale_log2;
   int32_t q_tiles;
 };
-static_assert(sizeof(Tf32Prob) % 16 == 0, "Tf32Prob is packed into the descriptor ring");
+static_assert(sizeof(TmaProb) % 16 == 0, "TmaProb is packed into the descriptor ring");
 
-struct Tf32Launch {
-  const Tf32Prob* probs;
+struct TmaLaunch {
+  const TmaProb* probs;
   const CUtensorMap* maps;
   const int32_t* begin;
   int32_t n, total, uniform;
   int32_t* status;
 };
 
-cudaError_t launch_attn_tf32(const Tf32Launch& L, bool bias, cudaStream_t s);
+cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, cudaStream_t s);
 int attn_tf32_tile_rows();
+
+// Persistent FP32 kernel (attn_fp32_warp.cu): D = 64, no bias, scale > 0. Q and K tensor maps
+// have boxes of kFwBoxWide columns x 32 rows, V maps kFwBoxNarrow columns x 32 rows (fp32, no
+// swizzle): the 4 extra Q/K columns pad the shared-memory rows against bank conflicts.
+constexpr int kFwBoxWide = 68;
+constexpr int kFwBoxNarrow = 64;
+constexpr int kFwBoxRows = 32;
+cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s);
+int attn_fp32_warp_tile_rows();
 
 cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L,
                                  float* out, cudaStream_t s);

@@ -80,7 +80,7 @@ struct ByteRange {
   uintptr_t b = 0, e = 0;
 };
 
-enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1, PATH_TF32 = 2 };
+enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1, PATH_TF32 = 2, PATH_FP32_TMA = 3 };
 
 struct Queued {
   AttnProb p;
@@ -90,17 +90,21 @@ struct Queued {
   bool aligned;
   double flops;
   double bytes;
-  int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TF32 tensor maps)
+  int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TMA tensor maps)
 };
 
-// A tensor map over a whole operand buffer: [rows, ld] fp32, boxes of 32 columns x box_rows rows.
+// A tensor map over a whole operand buffer: [rows, ld] fp32, boxes of box_cols columns x
+// box_rows rows. tf32: the TMA unit may round to TF32 on the way in (tensor-core operands);
+// otherwise the values arrive unchanged (FP32 kernel).
 struct MapKey {
   uintptr_t base;
   int64_t ld, rows;
-  int32_t box_rows;
+  int32_t box_cols, box_rows;
   int32_t swz;  // CUtensorMapSwizzle
+  int32_t tf32;
   bool operator==(const MapKey& o) const {
-    return base == o.base && ld == o.ld && rows == o.rows && box_rows == o.box_rows && swz == o.swz;
+    return base == o.base && ld == o.ld && rows == o.rows && box_cols == o.box_cols && box_rows == o.box_rows &&
+           swz == o.swz && tf32 == o.tf32;
   }
 };
 struct MapKeyHash {
@@ -108,7 +112,8 @@ struct MapKeyHash {
     size_t h = std::hash<uintptr_t>()(k.base);
     h ^= std::hash<int64_t>()(k.ld) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
     h ^= std::hash<int64_t>()(k.rows) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
-    h ^= std::hash<int32_t>()(k.box_rows * 8 + k.swz) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= std::hash<int64_t>()(((int64_t)k.box_cols << 32) ^ (k.box_rows * 16 + k.swz * 2 + k.tf32)) +
+         0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
     return h;
   }
 };
@@ -168,7 +173,7 @@ struct supra_attn_ctx {
   std::vector<cudaEvent_t> evt_free;
   std::map<std::string, ProfStat> stats;
 
-  // encoded TMA tensor maps of the TF32 path, reused across flushes (keyed by buffer and box)
+  // encoded TMA tensor maps, reused across flushes (keyed by buffer, box and element handling)
   std::unordered_map<MapKey, CUtensorMap, MapKeyHash> map_cache;
 
   int64_t launches = 0;
@@ -198,18 +203,19 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [rows, ld] fp32 buffer, boxes of 32 columns (128 bytes) x box_rows rows with the key's swizzle
-// (SWIZZLE_128B for K-major operands, SWIZZLE_128B_ATOM_32B for the MN-major V operand), zero
-// fill outside. The TMA unit rounds the fp32 values to TF32 on the way in when the driver
-// accepts that type.
+// [rows, ld] fp32 buffer, boxes of box_cols x box_rows with the key's swizzle, zero fill outside.
+// The TF32 kernel uses 32-column (128-byte) boxes with SWIZZLE_128B for K-major operands and
+// SWIZZLE_128B_ATOM_32B for the MN-major V operand, and lets the TMA unit round to TF32 when the
+// driver accepts that type; the FP32 kernel uses unswizzled FLOAT32 boxes (exact copies).
 bool encode_map(CUtensorMap* m, const MapKey& k) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)k.ld, (cuuint64_t)k.rows};
   const cuuint64_t strides[1] = {(cuuint64_t)k.ld * 4};
-  const cuuint32_t box[2] = {32, (cuuint32_t)k.box_rows};
+  const cuuint32_t box[2] = {(cuuint32_t)k.box_cols, (cuuint32_t)k.box_rows};
   const cuuint32_t estr[2] = {1, 1};
   for (CUtensorMapDataType t : {CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32}) {
+    if (t == CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 && !k.tf32) continue;
     if (fn(m, t, 2, reinterpret_cast<void*>(k.base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
            static_cast<CUtensorMapSwizzle>(k.swz), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
@@ -457,8 +463,7 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
               aligned16(d->out + d->o_off);
   if (d->D <= 64) {
     q.path = PATH_FUSED;
-    if (d->Lq <= 64) q.cfg = supra::CFG_D64_Q64;
-    else q.cfg = (q.aligned && !q.bias && scale > 0.f) ? supra::CFG_D64_W4 : supra::CFG_D64_Q128;
+    q.cfg = d->Lq <= 64 ? supra::CFG_D64_Q64 : supra::CFG_D64_Q128;
   } else if (d->D <= 128) {
     q.path = PATH_FUSED;
     q.cfg = supra::CFG_D128_Q64;
@@ -469,23 +474,29 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   q.rows_q = d->ldq > 0 ? d->q_size / d->ldq : 0;
   q.rows_k = d->ldk > 0 ? d->k_size / d->ldk : 0;
   q.rows_v = d->ldv > 0 ? d->v_size / d->ldv : 0;
+  // The TMA kernels read whole boxes of full buffer rows through tensor maps: head dim 64,
+  // 16-byte aligned rows, every row of the problem a whole row of its buffer, and the heads
+  // inside one row.
+  auto rows_ok = [](int64_t off, int64_t ld, int64_t rows, int64_t nrows, int64_t HDc) {
+    return ld >= 32 && ld <= (int64_t(1) << 30) && (off % ld) + HDc <= ld && off / ld + nrows <= rows &&
+           rows <= (int64_t(1) << 31) - 1;
+  };
+  const bool tma_ok = d->D == 64 && q.aligned && d->Lq > 0 && aligned16(d->q) && aligned16(d->k) &&
+                      aligned16(d->v) && d->q_off % 4 == 0 && d->k_off % 4 == 0 && d->v_off % 4 == 0 &&
+                      rows_ok(d->q_off, d->ldq, q.rows_q, d->Lq, HD) && rows_ok(d->k_off, d->ldk, q.rows_k, d->Lk, HD) &&
+                      rows_ok(d->v_off, d->ldv, q.rows_v, d->Lk, HD);
   if (d->variant == SUPRA_ATTN_TF32) {
-    // The tensor-core kernel reads whole 32-column slabs of full buffer rows through TMA tensor
-    // maps: head dim 64, 16-byte aligned rows, every row of the problem a whole row of its
-    // buffer, and the heads inside one row (a bias is read directly). Other TF32 requests run
-    // the FP32 kernels, which are at least as accurate.
-    auto rows_ok = [](int64_t off, int64_t ld, int64_t rows, int64_t nrows, int64_t HDc) {
-      return ld >= 32 && ld <= (int64_t(1) << 30) && (off % ld) + HDc <= ld && off / ld + nrows <= rows &&
-             rows <= (int64_t(1) << 31) - 1;
-    };
-    const bool ok = d->D == 64 && q.aligned && d->Lq > 0 && aligned16(d->q) && aligned16(d->k) &&
-                    aligned16(d->v) && d->q_off % 4 == 0 && d->k_off % 4 == 0 && d->v_off % 4 == 0 &&
-                    rows_ok(d->q_off, d->ldq, q.rows_q, d->Lq, HD) && rows_ok(d->k_off, d->ldk, q.rows_k, d->Lk, HD) &&
-                    rows_ok(d->v_off, d->ldv, q.rows_v, d->Lk, HD);
-    if (ok) {
+    // Other TF32 requests run the FP32 kernels, which are at least as accurate (a bias is read
+    // directly by the tensor-core kernel).
+    if (tma_ok) {
       q.path = PATH_TF32;
       q.cfg = 0;
     }
+  } else if (tma_ok && !q.bias && scale > 0.f && d->Lq > 64 && d->ldq >= supra::kFwBoxWide &&
+             d->ldk >= supra::kFwBoxWide) {
+    // persistent FP32 kernel: its Q/K boxes are kFwBoxWide columns wide
+    q.path = PATH_FP32_TMA;
+    q.cfg = 0;
   }
   q.flops = 4.0 * d->Lq * (double)d->Lk * d->D * d->H;  // app/gpu/ops.js:116
   q.bytes = 4.0 * ((double)d->Lq * HD * 2 + (double)d->Lk * HD * 2 + (d->bias ? (double)nbias : 0.0));
@@ -681,20 +692,21 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   return run_gemm_chunk(c, g, units, used, bias, aligned);
 }
 
-// TF32 tensor-core group: one tensor map per distinct (buffer, ld, rows, box) in the flush,
-// encoded once per context and cached; problems refer to maps by index.
-int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
-  const int mrows = supra::attn_tf32_tile_rows();
+// A group read through TMA tensor maps (the TF32 tensor-core kernel or the persistent FP32
+// kernel): one tensor map per distinct (buffer, ld, rows, box) in the flush, encoded once per
+// context and cached; problems refer to maps by index.
+int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
+  const int mrows = tf32 ? supra::attn_tf32_tile_rows() : supra::attn_fp32_warp_tile_rows();
   std::stable_sort(g.begin(), g.end(), [](const Queued* a, const Queued* b) { return a->p.Lk > b->p.Lk; });
   const int n = (int)g.size();
-  std::vector<supra::Tf32Prob> probs((size_t)n);
+  std::vector<supra::TmaProb> probs((size_t)n);
   std::vector<CUtensorMap> maps;
   std::unordered_map<MapKey, int32_t, MapKeyHash> index;
-  MapKey last_key{0, 0, 0, 0, 0};
+  MapKey last_key{0, 0, 0, 0, 0, 0, 0};
   int32_t last_idx = -1;
-  auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box, CUtensorMapSwizzle swz,
-                       int32_t* out) -> int {
-    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, box, (int32_t)swz};
+  auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box_cols, int32_t box_rows,
+                       CUtensorMapSwizzle swz, int32_t* out) -> int {
+    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, box_cols, box_rows, (int32_t)swz, tf32 ? 1 : 0};
     if (last_idx >= 0 && k == last_key) {
       *out = last_idx;
       return SUPRA_ATTN_OK;
@@ -722,7 +734,7 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   for (int i = 0; i < n; ++i) {
     const Queued& q = *g[i];
     const AttnProb& P = q.p;
-    supra::Tf32Prob& t = probs[i];
+    supra::TmaProb& t = probs[i];
     std::memset(&t, 0, sizeof t);
     t.o = P.o;
     t.o_off = P.o_off;
@@ -732,9 +744,21 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     t.Lk = P.Lk;
     t.H = P.H;
     t.D = P.D;
-    int rc = map_index(P.q, P.ldq, q.rows_q, mrows, CU_TENSOR_MAP_SWIZZLE_128B, &t.mq);
-    if (!rc) rc = map_index(P.k, P.ldk, q.rows_k, 64, CU_TENSOR_MAP_SWIZZLE_128B, &t.mk);
-    if (!rc) rc = map_index(P.v, P.ldv, q.rows_v, 64, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, &t.mv);
+    int rc;
+    if (tf32) {
+      rc = map_index(P.q, P.ldq, q.rows_q, 32, mrows, CU_TENSOR_MAP_SWIZZLE_128B, &t.mq);
+      if (!rc) rc = map_index(P.k, P.ldk, q.rows_k, 32, 64, CU_TENSOR_MAP_SWIZZLE_128B, &t.mk);
+      if (!rc) rc = map_index(P.v, P.ldv, q.rows_v, 32, 64, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, &t.mv);
+    } else {
+      rc = map_index(P.q, P.ldq, q.rows_q, supra::kFwBoxWide, supra::kFwBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     &t.mq);
+      if (!rc)
+        rc = map_index(P.k, P.ldk, q.rows_k, supra::kFwBoxWide, supra::kFwBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       &t.mk);
+      if (!rc)
+        rc = map_index(P.v, P.ldv, q.rows_v, supra::kFwBoxNarrow, supra::kFwBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       &t.mv);
+    }
     if (rc) return rc;
     t.qx = (int32_t)(P.q_off % P.ldq);
     t.qy = (int32_t)(P.q_off / P.ldq);
@@ -751,7 +775,7 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   }
   if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
   begin[n] = (int32_t)total;
-  const size_t pbytes = align16(sizeof(supra::Tf32Prob) * n);
+  const size_t pbytes = align16(sizeof(supra::TmaProb) * n);
   const size_t mbytes = sizeof(CUtensorMap) * maps.size();
   const size_t bbytes = sizeof(int32_t) * (n + 1);
   char *h = nullptr, *dv = nullptr;
@@ -762,13 +786,13 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   char* hm = h + pad;
   char* dm = dv + pad;
   std::memcpy(hm, maps.data(), mbytes);
-  std::memcpy(hm + mbytes, probs.data(), sizeof(supra::Tf32Prob) * n);
+  std::memcpy(hm + mbytes, probs.data(), sizeof(supra::TmaProb) * n);
   std::memcpy(hm + mbytes + pbytes, begin.data(), bbytes);
   rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
   if (rc) return rc;
-  supra::Tf32Launch L;
+  supra::TmaLaunch L;
   L.maps = reinterpret_cast<const CUtensorMap*>(dm);
-  L.probs = reinterpret_cast<const supra::Tf32Prob*>(dm + mbytes);
+  L.probs = reinterpret_cast<const supra::TmaProb*>(dm + mbytes);
   L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes);
   L.n = n;
   L.total = (int32_t)total;
@@ -780,12 +804,13 @@ int flush_tf32(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     if (uni) L.uniform = (int32_t)t0;
   }
   L.status = c->d_status;
+  const char* name = !tf32 ? "attn_fp32_d64_tma" : g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64";
   cudaError_t e;
   {
-    ProfScope ps(c, g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64", flops, bytes);
-    e = supra::launch_attn_tf32(L, g[0]->bias, c->stream);
+    ProfScope ps(c, name, flops, bytes);
+    e = tf32 ? supra::launch_attn_tf32(L, g[0]->bias, c->stream) : supra::launch_attn_fp32_warp(L, c->stream);
   }
-  if (e != cudaSuccess) return cuda_err(c, e, "attn_tf32_d64");
+  if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;
   return SUPRA_ATTN_OK;
 }
@@ -801,7 +826,8 @@ int do_flush(supra_attn_ctx* c) {
   for (auto& kv : groups) {
     const int path = kv.second[0]->path;
     rc = path == PATH_FUSED ? flush_fused(c, kv.second)
-         : path == PATH_TF32 ? flush_tf32(c, kv.second)
+         : path == PATH_TF32 ? flush_tma(c, kv.second, true)
+         : path == PATH_FP32_TMA ? flush_tma(c, kv.second, false)
                              : flush_gemm(c, kv.second);
     if (rc) break;
   }

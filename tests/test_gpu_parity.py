@@ -263,7 +263,68 @@ def test_determinism_and_profile(gpu):
     gpu.profile(False)
     assert gpu.launch_count() - n0 == 2
     names = [r["name"] for r in rep]
-    assert any(n.startswith("attn_fp32_d64") for n in names), names
+    assert names == ["attn_fp32_d64_tma"], names  # the persistent TMA kernel serves the DiT shapes
+
+
+# ---- persistent FP32 kernel (TMA boxes, K/V ring across tiles) ------------------------------------
+def test_fp32_tma_nan_past_lengths(gpu):
+    """Whole 32-row boxes read rows past Lq and Lk. Fill those rows with NaN/inf: no output may
+    change (scores past Lk are replaced by -inf, V rows past Lk are not read, rows past Lq are
+    not stored)."""
+    rng = np.random.default_rng(21)
+    H, D, Lq, Lk = 3, 64, 200, 45  # 200 = 128 + 72 rows; 45 keys = 1 block + 13 (a ragged group of 1)
+    ld = H * D
+    q = rng.standard_normal((Lq + 40) * ld).astype(np.float32)
+    k = rng.standard_normal((Lk + 40) * ld).astype(np.float32)
+    v = rng.standard_normal((Lk + 40) * ld).astype(np.float32)
+    q[Lq * ld:] = np.nan
+    k[Lk * ld:] = np.inf
+    v[Lk * ld:] = np.nan
+    out = dev(np.full((Lq + 40) * ld, 7.0))
+    gpu.profile(True)
+    gpu.profile_reset()
+    attn(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=Lq, Lk=Lk, H=H, D=D, ldq=ld, ldk=ld, ldv=ld, out=out)
+    gpu.sync()
+    names = [r["name"] for r in gpu.profile_report()]
+    gpu.profile(False)
+    assert names == ["attn_fp32_d64_tma"], names
+    got = host(out)
+    ref = oracle.attention_ops(q[: Lq * ld], k[: Lk * ld], v[: Lk * ld], Lq, Lk, H, D, ld, ld, ld)
+    assert_close(got[: Lq * ld], ref)
+    assert np.all(got[Lq * ld:] == 7.0), "wrote past Lq"
+
+
+def test_fp32_tma_many_ragged_tiles(gpu):
+    """600 problems with 1..70 keys (1-3 key blocks per tile): every CTA runs several tiles and the
+    K/V ring carries blocks of the next tiles; one launch."""
+    torch = _torch()
+    import supra_attn
+
+    g = torch.Generator().manual_seed(22)
+    n, H, D, Lq = 600, 2, 64, 130
+    Ls = torch.randint(1, 71, (n,), generator=g).tolist()
+    q = torch.randn(n * Lq * H * D, generator=g)
+    kv_off = np.concatenate([[0], np.cumsum([L * 2 * H * D for L in Ls])]).astype(np.int64)
+    kv = torch.randn(int(kv_off[-1]), generator=g)
+    qd, kvd = q.cuda(), kv.cuda()
+    out = torch.zeros(n * Lq * H * D, device="cuda")
+    descs = (supra_attn.Desc * n)()
+    for b, L in enumerate(Ls):
+        descs[b] = supra_attn.make_desc(q=qd, k=kvd, v=kvd, out=out, Lq=Lq, Lk=L, H=H, D=D, ldq=H * D,
+                                        ldk=2 * H * D, ldv=2 * H * D, qOff=b * Lq * H * D, kOff=int(kv_off[b]),
+                                        vOff=int(kv_off[b]) + H * D, oOff=b * Lq * H * D)
+    n0 = gpu.launch_count()
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    assert gpu.launch_count() - n0 == 1
+    got = host(out).reshape(n, Lq, H * D)
+    qn, kvn = q.numpy().reshape(n, Lq, H * D), kv.numpy()
+    for b in list(range(0, n, 37)) + [n - 1]:
+        x = kvn[kv_off[b]: kv_off[b + 1]].reshape(-1, 2 * H * D)
+        assert_close(got[b], oracle.attention_heads(qn[b], x[:, : H * D], x[:, H * D:], H))
+    for b in range(n):  # every row a convex combination of its V rows
+        x = kvn[kv_off[b]: kv_off[b + 1]].reshape(-1, 2 * H * D)[:, H * D:]
+        assert np.all(got[b] >= x.min(0) - 1e-5) and np.all(got[b] <= x.max(0) + 1e-5)
 
 
 # ---- BASELINE config sizes --------------------------------------------------------------------
