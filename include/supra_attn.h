@@ -158,7 +158,8 @@ typedef struct supra_attn_profile_entry {
 SUPRA_ATTN_API int supra_attn_profile_report(supra_attn_ctx* ctx, supra_attn_profile_entry* entries,
                               int32_t cap, int32_t* n);
 SUPRA_ATTN_API int supra_attn_profile_reset(supra_attn_ctx* ctx);
-/* Total kernels this context has launched since creation (all kinds). */
+/* Total kernels this context has launched since creation, all kinds: every flushed group is one
+ * descriptor-staging kernel plus its attention kernel(s). */
 SUPRA_ATTN_API int supra_attn_launch_count(const supra_attn_ctx* ctx, int64_t* n);
 
 /* ---- attention without allocation ---------------------------------------------------------- */

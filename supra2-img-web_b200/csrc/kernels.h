@@ -122,6 +122,10 @@ constexpr int kFwBoxRows = 32;
 cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s);
 int attn_fp32_warp_tile_rows();
 
+// Copies bytes (a multiple of 16, both addresses 16-byte aligned) from src, which may be pinned
+// host memory addressable by the device, to device memory dst (stage.cu).
+cudaError_t launch_stage_copy(const void* src, void* dst, size_t bytes, cudaStream_t s);
+
 cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L,
                                  float* out, cudaStream_t s);
 

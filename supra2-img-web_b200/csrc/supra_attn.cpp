@@ -150,6 +150,7 @@ struct supra_attn_ctx {
 
   // descriptor ring: two halves of pinned staging + device memory
   char* ring_h = nullptr;
+  char* ring_hd = nullptr;  // ring_h as the device addresses it (pinned, mapped)
   char* ring_d = nullptr;
   size_t ring_half = 0;
   int ring_cur = 0;
@@ -268,9 +269,17 @@ int ring_reserve(supra_attn_ctx* c, size_t bytes, char** host, char** dev) {
       cudaFreeHost(nh);
       return set_err(c, SUPRA_ATTN_ENOMEM, "ring: device alloc");
     }
+    void* nhd = nullptr;
+    if (cudaHostGetDevicePointer(&nhd, nh, 0) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFreeHost(nh);
+      cudaFree(nd);
+      return set_err(c, SUPRA_ATTN_ENOMEM, "ring: pinned buffer not addressable by the device");
+    }
     cudaFreeHost(c->ring_h);
     cudaFree(c->ring_d);
     c->ring_h = nh;
+    c->ring_hd = static_cast<char*>(nhd);
     c->ring_d = nd;
     c->ring_half = half;
     c->ring_cur = 0;
@@ -292,10 +301,13 @@ int ring_reserve(supra_attn_ctx* c, size_t bytes, char** host, char** dev) {
   return SUPRA_ATTN_OK;
 }
 
-// Copies bytes staged at host (inside the ring) to dev, stream-ordered.
+// Copies bytes staged at host (inside the ring) to dev, stream-ordered, with the staging kernel
+// (stage.cu) rather than the copy engine, so that large uploads on other streams cannot hold
+// the descriptors back.
 int ring_commit(supra_attn_ctx* c, char* host, char* dev, size_t bytes) {
-  cudaError_t e = cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, c->stream);
-  if (e != cudaSuccess) return cuda_err(c, e, "ring: upload");
+  cudaError_t e = supra::launch_stage_copy(c->ring_hd + (host - c->ring_h), dev, align16(bytes), c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, "ring: stage");
+  c->launches += 1;
   e = cudaEventRecord(c->ring_ev[c->ring_cur], c->stream);
   if (e != cudaSuccess) return cuda_err(c, e, "ring: event record");
   c->ring_ev_used[c->ring_cur] = true;
@@ -918,9 +930,13 @@ int supra_attn_create(int device, supra_attn_ctx** out) {
   ok = ok && cudaEventCreateWithFlags(&c->ring_ev[0], cudaEventDisableTiming) == cudaSuccess;
   ok = ok && cudaEventCreateWithFlags(&c->ring_ev[1], cudaEventDisableTiming) == cudaSuccess;
   if (ok) {
-    c->ring_half = size_t(2) << 20;
+    // 8 MiB halves: the host may record about one DiT step (28 flushes of 2048 problems) ahead
+    c->ring_half = size_t(8) << 20;
+    void* hd = nullptr;
     ok = cudaMallocHost(&c->ring_h, 2 * c->ring_half) == cudaSuccess &&
-         cudaMalloc(&c->ring_d, 2 * c->ring_half) == cudaSuccess;
+         cudaMalloc(&c->ring_d, 2 * c->ring_half) == cudaSuccess &&
+         cudaHostGetDevicePointer(&hd, c->ring_h, 0) == cudaSuccess;
+    c->ring_hd = static_cast<char*>(hd);
   }
   if (!ok) {
     cudaGetLastError();

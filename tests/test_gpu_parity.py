@@ -261,7 +261,7 @@ def test_determinism_and_profile(gpu):
     np.testing.assert_array_equal(outs[0], outs[1])
     rep = gpu.profile_report()
     gpu.profile(False)
-    assert gpu.launch_count() - n0 == 2
+    assert gpu.launch_count() - n0 == 4  # per flush: descriptor staging + the attention kernel
     names = [r["name"] for r in rep]
     assert names == ["attn_fp32_d64_tma"], names  # the persistent TMA kernel serves the DiT shapes
 
@@ -316,7 +316,7 @@ def test_fp32_tma_many_ragged_tiles(gpu):
     n0 = gpu.launch_count()
     gpu.enqueue_batch(descs)
     gpu.sync()
-    assert gpu.launch_count() - n0 == 1
+    assert gpu.launch_count() - n0 == 2  # descriptor staging + one attention launch
     got = host(out).reshape(n, Lq, H * D)
     qn, kvn = q.numpy().reshape(n, Lq, H * D), kv.numpy()
     for b in list(range(0, n, 37)) + [n - 1]:
