@@ -27,7 +27,9 @@
 //  * exp2 via ex2.approx.ftz (relative error ~2^-22), scale*log2(e) folded into the scores.
 //  * Boxes are always whole (32 rows). Rows past Lq or Lk hold other rows of the buffer or zero
 //    fill: scores of keys past Lk are replaced (not multiplied) by -inf, V rows past Lk are not
-//    read, and rows past Lq are never stored, so no value there can reach a stored output.
+//    read, and rows past Lq are never stored, so no value there can reach a stored output. In a
+//    ragged last block the 8-key groups wholly past Lk are skipped in QK^T and the 4-key groups
+//    in PV.
 //  * All waits are bounded (2 s); a timeout sets the device status word and the CTA leaves.
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -128,6 +130,43 @@ __device__ __forceinline__ void issue_q(const TmaLaunch& L, const Tile& T, int w
   tc::tma_load_2d(dst, L.maps + T.p->mq, T.p->qx + T.h * kD, T.p->qy + T.q0 + w * kRowsW, bar);
 }
 
+// S = Q K^T for keys cg + 8jj, jj < NJ, of one block (NJ < 4 for a ragged last block: the key
+// groups past Lk are not computed). Component-major order: for each 4-deep slice of the head
+// dim, the products of one component are independent FFMAs, so no accumulator waits on its
+// previous update.
+template <int NJ>
+__device__ __forceinline__ void qk_block(const float4* __restrict__ Q4, const float4* __restrict__ K4,
+                                         float (&sc)[kRI][4]) {
+#pragma unroll
+  for (int i = 0; i < kRI; ++i)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.f;
+#pragma unroll 2
+  for (int d4 = 0; d4 < kD / 4; ++d4) {
+    float4 kf[NJ], qf[kRI];
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) kf[jj] = K4[jj * 8 * (kKS / 4) + d4];
+#pragma unroll
+    for (int i = 0; i < kRI; ++i) qf[i] = Q4[i * 4 * (kQS / 4) + d4];
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].x, kf[jj].x, sc[i][jj]);
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].y, kf[jj].y, sc[i][jj]);
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].z, kf[jj].z, sc[i][jj]);
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].w, kf[jj].w, sc[i][jj]);
+  }
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -207,37 +246,16 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
       const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
       const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
 
-      // ---- S = Q K^T. Component-major order: for each 4-deep slice of the head dim, the 32
-      // products of one component are independent FFMAs, so no accumulator waits on its
-      // previous update.
+      // ---- S = Q K^T
       float sc[kRI][4];
-#pragma unroll
-      for (int i = 0; i < kRI; ++i)
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.f;
-#pragma unroll 2
-      for (int d4 = 0; d4 < kD / 4; ++d4) {
-        float4 kf[4], qf[kRI];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) kf[jj] = K4[jj * 8 * (kKS / 4) + d4];
-#pragma unroll
-        for (int i = 0; i < kRI; ++i) qf[i] = Q4[i * 4 * (kQS / 4) + d4];
-#pragma unroll
-        for (int i = 0; i < kRI; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].x, kf[jj].x, sc[i][jj]);
-#pragma unroll
-        for (int i = 0; i < kRI; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].y, kf[jj].y, sc[i][jj]);
-#pragma unroll
-        for (int i = 0; i < kRI; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].z, kf[jj].z, sc[i][jj]);
-#pragma unroll
-        for (int i = 0; i < kRI; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = fmaf(qf[i].w, kf[jj].w, sc[i][jj]);
+      if (nk == kNK) {
+        qk_block<4>(Q4, K4, sc);
+      } else {
+        const int nj = (nk + 7) >> 3;
+        if (nj == 1) qk_block<1>(Q4, K4, sc);
+        else if (nj == 2) qk_block<2>(Q4, K4, sc);
+        else if (nj == 3) qk_block<3>(Q4, K4, sc);
+        else qk_block<4>(Q4, K4, sc);
       }
       if (j == nblk - 1) {  // this warp's Q rows are done: fetch its rows of the next tile
         const int tn = t + (int)gridDim.x;
@@ -250,7 +268,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
           }
         }
       }
-      if (nk < kNK) {  // partial block (warp-uniform): keys past Lk get -inf (a select, not a product)
+      if (nk < kNK) {  // ragged block (warp-uniform): keys past Lk get -inf (a select, not a product)
 #pragma unroll
         for (int i = 0; i < kRI; ++i)
 #pragma unroll

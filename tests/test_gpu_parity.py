@@ -166,6 +166,8 @@ def run_and_check(gpu, p, scale=None, tol=TOL):
         # single key, many ring refills
         (100, 50, 2, 32), (97, 31, 3, 48), (130, 1, 1, 64), (300, 97, 2, 64), (129, 33, 2, 64),
         (160, 2000, 1, 64), (65, 8, 4, 8),
+        # persistent TMA kernel: ragged last blocks with 1, 2, 3 and 4 key groups of 8
+        (100, 37, 2, 64), (100, 44, 2, 64), (100, 52, 2, 64), (100, 60, 2, 64), (257, 31, 3, 64),
     ],
 )
 def test_shapes(gpu, Lq, Lk, H, D):
