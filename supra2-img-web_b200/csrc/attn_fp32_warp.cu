@@ -220,6 +220,10 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     const int Lk = pp->Lk;
     const float sl2 = pp->scale_log2;
     const int nblk = T.nblk;
+    // this lane's first output row, read now rather than behind the last block
+    const int64_t ldo = pp->ldo;
+    const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
+    float* const orow = pp->o + pp->o_off + ((int64_t)T.q0 + kRowsW * w + rg) * ldo + (int64_t)T.h * kD + 4 * cg;
     Tile Tn = T;
 
     float4 o[kRI][2];
@@ -292,7 +296,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
           any_move = true;
         }
       }
-      if (__any_sync(0xffffffffu, any_move)) {
+      if (j > 0 && __any_sync(0xffffffffu, any_move)) {  // (block 0: O and l are still zero)
 #pragma unroll
         for (int i = 0; i < kRI; ++i) {
           const float alpha = ex2(mprev[i] - mo[i]);
@@ -363,21 +367,19 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     }
 
     // ---- O / l, rows < Lq ------------------------------------------------------------------
-    const int rows_q = min(kRows, pp->Lq - T.q0);
-    float* obase = pp->o + pp->o_off + (int64_t)T.q0 * pp->ldo + (int64_t)T.h * kD;
 #pragma unroll
     for (int i = 0; i < kRI; ++i) {
       float ls = l[i];
       ls += __shfl_xor_sync(0xffffffffu, ls, 1);
       ls += __shfl_xor_sync(0xffffffffu, ls, 2);
       ls += __shfl_xor_sync(0xffffffffu, ls, 4);
-      const float inv = 1.0f / ls;
-      const int r = kRowsW * w + rg + 4 * i;
-      if (r < rows_q) {
-        float* dst = obase + (int64_t)r * pp->ldo;
+      float inv;
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(ls));  // within 1 ulp; l >= 1 here
+      if (4 * i < rows_q) {
+        float* dst = orow + (int64_t)(4 * i) * ldo;
 #pragma unroll
         for (int u = 0; u < 2; ++u)
-          *reinterpret_cast<float4*>(dst + 4 * (cg + 8 * u)) =
+          *reinterpret_cast<float4*>(dst + 32 * u) =
               make_float4(o[i][u].x * inv, o[i][u].y * inv, o[i][u].z * inv, o[i][u].w * inv);
       }
     }
