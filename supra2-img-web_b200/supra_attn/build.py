@@ -1,7 +1,9 @@
 """Build libsupra_attn.so in-tree for sm_100a with nvcc.
 
-    python -m supra_attn.build            (from supra2-img-web_b200/)
-    python supra2-img-web_b200/supra_attn/build.py
+    python supra2-img-web_b200/supra_attn/build.py [--force] [-v]
+
+(Run it as a script or load it by path, as __graft_entry__.build() does: importing it as
+supra_attn.build would first run the package's __init__, which loads the library.)
 
 Every csrc/*.cu and csrc/*.cpp is compiled to an object under _build/ (skipped when the object
 is newer than its source and the headers), then linked into supra_attn/libsupra_attn.so.
