@@ -124,10 +124,16 @@ __device__ __forceinline__ void issue_next(const TmaLaunch& L, Ctl* C, float* Ks
   }
 }
 
-// This warp's 32 Q rows of tile T into its Q region (one thread).
-__device__ __forceinline__ void issue_q(const TmaLaunch& L, const Tile& T, int w, float* dst, uint64_t* bar) {
+// A warp's 32 Q rows of a tile: tensor map and TMA coordinates.
+struct QBox {
+  int32_t m, x, y;
+};
+__device__ __forceinline__ QBox qbox_of(const Tile& T, int w) {
+  return QBox{T.p->mq, T.p->qx + T.h * kD, T.p->qy + T.q0 + w * kRowsW};
+}
+__device__ __forceinline__ void issue_q(const TmaLaunch& L, const QBox& q, float* dst, uint64_t* bar) {
   mbar_arrive_expect_tx(bar, kQBytes);
-  tc::tma_load_2d(dst, L.maps + T.p->mq, T.p->qx + T.h * kD, T.p->qy + T.q0 + w * kRowsW, bar);
+  tc::tma_load_2d(dst, L.maps + q.m, q.x, q.y, bar);
 }
 
 // S = Q K^T for keys cg + 8jj, jj < NJ, of one block (NJ < 4 for a ragged last block: the key
@@ -209,7 +215,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     for (int s = 0; s < kNS; ++s) issue_next(L, C, Ks, Vs, s);
   }
   Tile T = tile_of(L, t0);
-  if (lane == 0) issue_q(L, T, w, Qw, &C->qbar[w]);
+  if (lane == 0) issue_q(L, qbox_of(T, w), Qw, &C->qbar[w]);
 
   const float4* Q4 = reinterpret_cast<const float4*>(Qw) + rg * (kQS / 4);
   const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
@@ -224,7 +230,10 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     const int64_t ldo = pp->ldo;
     const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
     float* const orow = pp->o + pp->o_off + ((int64_t)T.q0 + kRowsW * w + rg) * ldo + (int64_t)T.h * kD + 4 * cg;
-    Tile Tn = T;
+    // the next tile, looked up now: its Q rows are requested right after this tile's last QK^T
+    const int tn = t + (int)gridDim.x;
+    const Tile Tn = tn < L.total ? tile_of(L, tn) : T;
+    const QBox qn = qbox_of(Tn, w);
 
     float4 o[kRI][2];
     float mo[kRI], l[kRI];
@@ -261,15 +270,11 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         else if (nj == 3) qk_block<3>(Q4, K4, sc);
         else qk_block<4>(Q4, K4, sc);
       }
-      if (j == nblk - 1) {  // this warp's Q rows are done: fetch its rows of the next tile
-        const int tn = t + (int)gridDim.x;
-        if (tn < L.total) {
-          Tn = tile_of(L, tn);
-          __syncwarp();
-          if (lane == 0) {
-            fence_proxy_async_smem();
-            issue_q(L, Tn, w, Qw, &C->qbar[w]);
-          }
+      if (j == nblk - 1 && tn < L.total) {  // this warp's Q rows are done: fetch its next ones
+        __syncwarp();
+        if (lane == 0) {
+          fence_proxy_async_smem();
+          issue_q(L, qn, Qw, &C->qbar[w]);
         }
       }
       if (nk < kNK) {  // ragged block (warp-uniform): keys past Lk get -inf (a select, not a product)
