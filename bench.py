@@ -129,6 +129,30 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
+def sgemm_tflops(torch, dev, n=8192, reps=5):
+    """Measured FP32 reference rate on this GPU: cuBLAS SGEMM (torch.matmul, TF32 off) on n^3,
+    best of `reps`, CUDA events. The FP32 counterpart of MEASURED_PEAKS.json's cuBLAS bf16 figure."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        c = torch.empty(n, n, device=dev)
+        torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        return 2.0 * n ** 3 / (best / 1e3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -525,6 +549,9 @@ def main():
                                    "(MEASURED_PEAKS.json has no FP32 figure)",
                     "hbm_gbs_achieved": top["bytes"] / (top["ms"] / 1e3) / 1e9,
                     "hbm_peak_gbs": peaks.get("hbm_gbs")}
+        sg = sgemm_tflops(torch, dev)  # after the timed regions: nothing of it is timed
+        roofline["sgemm_tflops_measured"] = sg
+        roofline["frac_of_sgemm"] = achieved / sg
 
     # ---- end to end through the public API with host buffers ------------------------------------
     # Every step uploads its inputs (Q/K/V of the self-attention, Q of the cross-attention) from

@@ -286,32 +286,44 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
 
       // ---- softmax with a lazily moved offset (exp2 domain). scale > 0 (host-checked), so the
       // maximum of the raw scores times scale*log2(e) is the maximum of the scaled scores.
-      bool any_move = false;
-      float mprev[kRI];
+      // Cheap test first: does any lane hold a score more than 8 above its row's offset? Only
+      // then (every tile's first block, rarely afterwards) are the row maxima reduced across
+      // the row's 8 lanes and the offsets moved.
+      float lmax[kRI];
+      bool need = false;
 #pragma unroll
       for (int i = 0; i < kRI; ++i) {
-        float mr = fmaxf(fmaxf(sc[i][0], sc[i][1]), fmaxf(sc[i][2], sc[i][3]));
-        mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
-        mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
-        mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
-        const float mx = mr * sl2;
-        mprev[i] = mo[i];
-        if (mx > mo[i] + 8.f) {
-          mo[i] = mx;
-          any_move = true;
-        }
+        lmax[i] = fmaxf(fmaxf(sc[i][0], sc[i][1]), fmaxf(sc[i][2], sc[i][3]));
+        need |= fmaf(lmax[i], sl2, -mo[i]) > 8.f;
       }
-      if (j > 0 && __any_sync(0xffffffffu, any_move)) {  // (block 0: O and l are still zero)
+      if (__any_sync(0xffffffffu, need)) {
+        bool moved = false;
+        float mprev[kRI];
 #pragma unroll
         for (int i = 0; i < kRI; ++i) {
-          const float alpha = ex2(mprev[i] - mo[i]);
-          l[i] *= alpha;
+          float mr = lmax[i];
+          mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
+          mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
+          mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
+          const float mx = mr * sl2;  // the same value in all 8 lanes of the row
+          mprev[i] = mo[i];
+          if (mx > mo[i] + 8.f) {
+            mo[i] = mx;
+            moved = true;
+          }
+        }
+        if (j > 0 && __any_sync(0xffffffffu, moved)) {  // (block 0: O and l are still zero)
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            o[i][u].x *= alpha;
-            o[i][u].y *= alpha;
-            o[i][u].z *= alpha;
-            o[i][u].w *= alpha;
+          for (int i = 0; i < kRI; ++i) {
+            const float alpha = ex2(mprev[i] - mo[i]);
+            l[i] *= alpha;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              o[i][u].x *= alpha;
+              o[i][u].y *= alpha;
+              o[i][u].z *= alpha;
+              o[i][u].w *= alpha;
+            }
           }
         }
       }
