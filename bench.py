@@ -342,6 +342,18 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
     run("t5_256", 256, "prompt", c3, sum(4.0 * L * L * 64 * 12 for L in Lt),
         sum(4.0 * (4 * L * 768 + 12 * L * L) for L in Lt))
 
+    # the same T5 calls with the [32, 12] table in place of the expanded bias (the kernels form
+    # the bias; the host's per-prompt bias build and its 48*L^2 bytes drop out)
+    def c3t(variant):
+        arr = (supra_attn.Desc * 256)()
+        for i, L in enumerate(Lt):
+            arr[i] = supra_attn.make_desc(q=qs[i], k=ks[i], v=vs[i], out=os_[i], t5_table=table, Lq=L, Lk=L, H=12,
+                                          D=64, ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
+        return arr
+
+    run("t5_256_table", 256, "prompt", c3t, sum(4.0 * L * L * 64 * 12 for L in Lt),
+        sum(4.0 * (4 * L * 768 + 32 * 12) for L in Lt))
+
     # VAE mid-block single-head attention, 1024 tokens x 512 channels
     for nimg in (1, 8, 64):
         qv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)

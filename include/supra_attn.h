@@ -58,6 +58,15 @@ extern "C" {
 
 /* ---- descriptor flags -------------------------------------------------------------------- */
 #define SUPRA_ATTN_F_DEFAULT_SCALE 0x1u /* ignore .scale, use 1/sqrt(D) (ops.js:109 default) */
+/* .bias is T5's relative-attention-bias TABLE, not an expanded bias: bias points at
+ * bias_size >= buckets*H floats laid out [buckets, H] (encoder.block.0...relative_attention_bias
+ * .weight, app/models/t5.js:44), and the kernels form the score bias themselves as
+ *   bias[h, i, j] = table[relativeBucket(j - i)*H + h]   (app/models/t5.js:14-23,55-65)
+ * with the bidirectional bucket of supra_attn_relative_bucket. .bias_param carries the bucket
+ * parameters: buckets in bits 0-15, max_distance in bits 16-31. Not in the reference: its T5
+ * builds the [H, L, L] bias on the host and uploads it per encode (app/models/t5.js:73); this
+ * saves those 4*H*L*L bytes per prompt and the host loop. */
+#define SUPRA_ATTN_F_T5_TABLE 0x2u
 
 typedef struct supra_attn_ctx supra_attn_ctx;
 
@@ -73,7 +82,7 @@ typedef struct supra_attn_desc {
   const float* k;
   const float* v;
   float* out;
-  const float* bias; /* NULL, or [H, Lq, Lk] additive score bias */
+  const float* bias; /* NULL, [H, Lq, Lk] additive score bias, or a T5 table (SUPRA_ATTN_F_T5_TABLE) */
   int64_t q_size, k_size, v_size, out_size, bias_size;
   int64_t ldq, ldk, ldv;
   int64_t q_off, k_off, v_off, o_off;
@@ -81,7 +90,7 @@ typedef struct supra_attn_desc {
   float scale;
   int32_t variant; /* SUPRA_ATTN_FP32 or SUPRA_ATTN_TF32 */
   uint32_t flags;  /* SUPRA_ATTN_F_* */
-  uint32_t reserved;
+  uint32_t bias_param; /* with SUPRA_ATTN_F_T5_TABLE: buckets | max_distance << 16; else 0 */
 } supra_attn_desc;
 
 /* ---- context ----------------------------------------------------------------------------- */

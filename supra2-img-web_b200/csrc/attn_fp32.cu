@@ -47,8 +47,10 @@ struct Geom {
   static constexpr int BYTES = FLOATS * 4 + 4 * 8;  // + 3 mbarriers (8-byte aligned)
 };
 
-template <int DT, int MQ, bool BIAS, bool ALIGNED>
+// BM: bias mode, 0 none, 1 an expanded [H, Lq, Lk] bias, 2 a T5 relative-bias table.
+template <int DT, int MQ, int BM, bool ALIGNED>
 __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L) {
+  constexpr bool BIAS = BM != 0;
   using G = Geom<DT, MQ>;
   constexpr int TM = G::TM;
   constexpr int U = G::U;
@@ -83,7 +85,11 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
   const float* qsrc = pp->q + pp->q_off + (int64_t)q0 * ldq + (int64_t)h * D;
   const float* ksrc = pp->k + pp->k_off + (int64_t)h * D;
   const float* vsrc = pp->v + pp->v_off + (int64_t)h * D;
-  const float* bsrc = BIAS ? pp->bias + ((int64_t)h * Lq + q0) * Lk : nullptr;
+  // bias: the expanded [H, Lq, Lk] array (staged per block), or a T5 table read per score
+  const float* bsrc = BM == 1 ? pp->bias + ((int64_t)h * Lq + q0) * Lk : nullptr;
+  const float* tab_h = BM == 2 ? pp->bias + h : nullptr;
+  const int32_t* lut_c = BM == 2 ? pp->rel_lut + pp->rel_max : nullptr;
+  const int32_t rel_max = BM == 2 ? pp->rel_max : 0;
   const float sl2 = pp->scale_log2;
 
   // ---- set-up: barriers and the zero padding the bulk copies never write -------------------------
@@ -149,7 +155,7 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
     if (tid == 0) report_error(L.status, DEV_TIMEOUT, stage);
     // drain the copies that may still target this CTA's shared memory (bounded again)
     mbar_wait_bounded(bar, parity);
-    if (BIAS) cp_async_wait<0>();
+    if (BM == 1) cp_async_wait<0>();
   };
 
   if (ALIGNED && warp == 0) {
@@ -157,7 +163,7 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
     issue_rows(Ks, G::KS, ksrc, ldk, min(kNK, Lk), &bars[1]);
     issue_rows(Vs, G::VS, vsrc, ldv, min(kNK, Lk), &bars[2]);
   }
-  if (BIAS) issue_bias(0);
+  if (BM == 1) issue_bias(0);
 
   float4 o[TM][U];
   float m[TM], l[TM];
@@ -218,7 +224,7 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
     }
 
     // ---- online softmax (exp2 domain) --------------------------------------------------------
-    if (BIAS) cp_async_wait<0>();  // this thread's own staged bias slots
+    if (BM == 1) cp_async_wait<0>();  // this thread's own staged bias slots
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
       const int r = rg + 16 * i;
@@ -226,7 +232,11 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
         float x = s[i][jj] * sl2;
-        if (BIAS) x = fmaf(Ps[r * kPS + cg + 8 * jj], kLog2e, x);
+        if (BIAS) {
+          const float b = BM == 2 ? t5_table_bias(tab_h, lut_c, rel_max, (uint32_t)pp->H, k0 + cg + 8 * jj - (q0 + r))
+                                  : Ps[r * kPS + cg + 8 * jj];
+          x = fmaf(b, kLog2e, x);
+        }
         x = (cg + 8 * jj < nk) ? x : -INFINITY;
         s[i][jj] = x;
         mx = fmaxf(mx, x);
@@ -308,7 +318,7 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
         fence_proxy_async_smem();
         issue_rows(Vs, G::VS, vsrc + (int64_t)(k0 + kNK) * ldv, ldv, min(kNK, Lk - k0 - kNK), &bars[2]);
       }
-      if (BIAS) issue_bias(k0 + kNK);
+      if (BM == 1) issue_bias(k0 + kNK);
     }
   }
 
@@ -340,10 +350,10 @@ __global__ void __launch_bounds__(kThreads) attn_fp32_kernel(const AttnLaunch L)
   }
 }
 
-template <int DT, int MQ, bool BIAS, bool ALIGNED>
+template <int DT, int MQ, int BM, bool ALIGNED>
 cudaError_t launch_one(const AttnLaunch& L, cudaStream_t s) {
   using G = Geom<DT, MQ>;
-  auto k = attn_fp32_kernel<DT, MQ, BIAS, ALIGNED>;
+  auto k = attn_fp32_kernel<DT, MQ, BM, ALIGNED>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::BYTES);
   if (e != cudaSuccess) return e;
   k<<<L.total, kThreads, G::BYTES, s>>>(L);
@@ -351,9 +361,10 @@ cudaError_t launch_one(const AttnLaunch& L, cudaStream_t s) {
 }
 
 template <int DT, int MQ>
-cudaError_t launch_cfg(bool bias, bool aligned, const AttnLaunch& L, cudaStream_t s) {
-  if (bias) return aligned ? launch_one<DT, MQ, true, true>(L, s) : launch_one<DT, MQ, true, false>(L, s);
-  return aligned ? launch_one<DT, MQ, false, true>(L, s) : launch_one<DT, MQ, false, false>(L, s);
+cudaError_t launch_cfg(int bm, bool aligned, const AttnLaunch& L, cudaStream_t s) {
+  if (bm == 2) return aligned ? launch_one<DT, MQ, 2, true>(L, s) : launch_one<DT, MQ, 2, false>(L, s);
+  if (bm == 1) return aligned ? launch_one<DT, MQ, 1, true>(L, s) : launch_one<DT, MQ, 1, false>(L, s);
+  return aligned ? launch_one<DT, MQ, 0, true>(L, s) : launch_one<DT, MQ, 0, false>(L, s);
 }
 
 }  // namespace
@@ -363,24 +374,31 @@ int fused_cfg_tile_rows(int cfg) {
 }
 int fused_cfg_head_dim(int cfg) { return cfg == CFG_D128_Q64 ? 128 : 64; }
 
-cudaError_t launch_attn_fp32(int cfg, bool bias, bool aligned, const AttnLaunch& L, cudaStream_t s) {
+cudaError_t launch_attn_fp32(int cfg, int bias_mode, bool aligned, const AttnLaunch& L, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
+  if (bias_mode < 0 || bias_mode > 2) return cudaErrorInvalidValue;
   switch (cfg) {
-    case CFG_D64_Q128: return launch_cfg<64, 128>(bias, aligned, L, s);
-    case CFG_D64_Q64: return launch_cfg<64, 64>(bias, aligned, L, s);
-    case CFG_D128_Q64: return launch_cfg<128, 64>(bias, aligned, L, s);
+    case CFG_D64_Q128: return launch_cfg<64, 128>(bias_mode, aligned, L, s);
+    case CFG_D64_Q64: return launch_cfg<64, 64>(bias_mode, aligned, L, s);
+    case CFG_D128_Q64: return launch_cfg<128, 64>(bias_mode, aligned, L, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
-const char* attn_fp32_name(int cfg, bool bias, bool aligned) {
-  static const char* names[CFG_COUNT][2][2] = {
-      {{"attn_fp32_d64_q128_u", "attn_fp32_d64_q128"}, {"attn_fp32_d64_q128_bias_u", "attn_fp32_d64_q128_bias"}},
-      {{"attn_fp32_d64_q64_u", "attn_fp32_d64_q64"}, {"attn_fp32_d64_q64_bias_u", "attn_fp32_d64_q64_bias"}},
-      {{"attn_fp32_d128_q64_u", "attn_fp32_d128_q64"}, {"attn_fp32_d128_q64_bias_u", "attn_fp32_d128_q64_bias"}},
+const char* attn_fp32_name(int cfg, int bias_mode, bool aligned) {
+  static const char* names[CFG_COUNT][3][2] = {
+      {{"attn_fp32_d64_q128_u", "attn_fp32_d64_q128"},
+       {"attn_fp32_d64_q128_bias_u", "attn_fp32_d64_q128_bias"},
+       {"attn_fp32_d64_q128_t5_u", "attn_fp32_d64_q128_t5"}},
+      {{"attn_fp32_d64_q64_u", "attn_fp32_d64_q64"},
+       {"attn_fp32_d64_q64_bias_u", "attn_fp32_d64_q64_bias"},
+       {"attn_fp32_d64_q64_t5_u", "attn_fp32_d64_q64_t5"}},
+      {{"attn_fp32_d128_q64_u", "attn_fp32_d128_q64"},
+       {"attn_fp32_d128_q64_bias_u", "attn_fp32_d128_q64_bias"},
+       {"attn_fp32_d128_q64_t5_u", "attn_fp32_d128_q64_t5"}},
   };
-  if (cfg < 0 || cfg >= CFG_COUNT) return "attn_fp32_?";
-  return names[cfg][bias ? 1 : 0][aligned ? 1 : 0];
+  if (cfg < 0 || cfg >= CFG_COUNT || bias_mode < 0 || bias_mode > 2) return "attn_fp32_?";
+  return names[cfg][bias_mode][aligned ? 1 : 0];
 }
 
 }  // namespace supra

@@ -131,7 +131,9 @@ __global__ void __launch_bounds__(kGT) gemm_qk_kernel(const GemmLaunch L) {
       const int c = cg + 16 * j;
       if (c >= nc) continue;
       float x = acc[i][j] * scale;
-      if (BIAS) x += __ldg(P.bias + ((int64_t)u.h * P.Lq + grow) * P.Lk + c0 + c);
+      if (BIAS)
+        x += P.rel_lut ? t5_table_bias(P.bias + u.h, P.rel_lut + P.rel_max, P.rel_max, (uint32_t)P.H, c0 + c - grow)
+                       : __ldg(P.bias + ((int64_t)u.h * P.Lq + grow) * P.Lk + c0 + c);
       S[(int64_t)(r0 + r) * u.ldS + c0 + c] = x;
     }
   }

@@ -140,6 +140,8 @@ extern "C" int supra_attn_attention_noalloc(const supra_attn_desc* d, void* stre
   };
   int rc = supra_attn_check_desc(d, msg, cap);  // same checks as supra_attn_enqueue
   if (rc) return rc;
+  if (d->flags & SUPRA_ATTN_F_T5_TABLE)
+    return fail(SUPRA_ATTN_EINVAL, "the no-alloc entry point takes an expanded [H, Lq, Lk] bias, not a T5 table");
   if (msg && cap > 0) msg[0] = 0;
   if (d->Lq == 0) return SUPRA_ATTN_OK;
   const int ldS = (d->Lk + 3) & ~3;

@@ -285,7 +285,21 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
         tc::tmem_wait_ld();
         const int nk = min(kN, Lk - j * kN);
         float mx = -INFINITY;
-        if (BIAS && T.q0 + row < Lq) {
+        if (BIAS && T.q0 + row < Lq && pp->rel_lut) {
+          // T5 table bias: this thread's query row, keys j*64 .. j*64 + nk (exp2 domain)
+          const float* tab_h = pp->bias + T.h;
+          const int32_t* lut_c = pp->rel_lut + pp->rel_max;
+          const int32_t rel_max = pp->rel_max;
+          const uint32_t Hu = (uint32_t)pp->H;
+          const int32_t rel0 = j * kN - (T.q0 + row);
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            const float b = t5_table_bias(tab_h, lut_c, rel_max, Hu, rel0 + c);
+            const float x = (c < nk) ? fmaf(b, 1.4426950408889634f, v[c] * sl2) : -INFINITY;
+            v[c] = x;
+            mx = fmaxf(mx, x);
+          }
+        } else if (BIAS && T.q0 + row < Lq) {
           // this thread's query row of the bias, keys j*64 .. j*64 + nk (exp2 domain: times log2 e)
           const float* brow = pp->bias + ((int64_t)T.h * Lq + T.q0 + row) * Lk + (int64_t)j * kN;
 #pragma unroll

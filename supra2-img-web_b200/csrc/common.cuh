@@ -105,6 +105,17 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Score bias of a (query row i, key j) pair of one head from a T5 relative-bias table, in 32-bit
+// index arithmetic: tab_h = table + h (the table is [buckets, H], buckets * H < 2^32), lut_c =
+// rel_lut + rel_max (the bucket of relative position r at lut_c[r]), rel = j - i. Buckets of
+// relative positions beyond rel_max equal those at +-rel_max (the bucket saturates at
+// max_distance), so rel is clamped.
+__device__ __forceinline__ float t5_table_bias(const float* __restrict__ tab_h, const int32_t* __restrict__ lut_c,
+                                               int32_t rel_max, uint32_t H, int32_t rel) {
+  rel = max(-rel_max, min(rel_max, rel));
+  return __ldg(tab_h + (uint32_t)__ldg(lut_c + rel) * H);
+}
+
 // Tile index -> problem index: the largest p with begin[p] <= t (begin[0] == 0, ascending).
 __device__ __forceinline__ int find_problem(const int32_t* __restrict__ begin, int n, int t) {
   int lo = 0, hi = n - 1;

@@ -29,7 +29,9 @@ struct alignas(16) AttnProb {
   float scale;       // score multiplier
   float scale_log2;  // scale * log2(e): scores are exponentiated with exp2
   int32_t q_tiles;   // ceil(Lq / tile rows)
-  int32_t pad;
+  int32_t rel_max;   // T5 table bias: relative positions are clamped to [-rel_max, rel_max]
+  const int32_t* rel_lut;  // T5 table bias: bucket of relative position r at rel_lut[r + rel_max]
+                           // (bias is then the [buckets, H] table); nullptr: bias is [H, Lq, Lk]
 };
 static_assert(sizeof(AttnProb) % 16 == 0, "AttnProb is packed into the descriptor ring");
 
@@ -79,8 +81,9 @@ int fused_cfg_tile_rows(int cfg);
 int fused_cfg_head_dim(int cfg);
 
 // Launchers. Each returns the cudaError_t of the launch (cudaSuccess on success).
-cudaError_t launch_attn_fp32(int cfg, bool bias, bool aligned, const AttnLaunch& L, cudaStream_t s);
-const char* attn_fp32_name(int cfg, bool bias, bool aligned);
+// bias_mode: 0 none, 1 an expanded [H, Lq, Lk] bias, 2 a T5 relative-bias table (AttnProb::rel_lut)
+cudaError_t launch_attn_fp32(int cfg, int bias_mode, bool aligned, const AttnLaunch& L, cudaStream_t s);
+const char* attn_fp32_name(int cfg, int bias_mode, bool aligned);
 
 cudaError_t launch_gemm_qk(bool bias, bool aligned, const GemmLaunch& L, cudaStream_t s);
 cudaError_t launch_softmax_rows(const GemmLaunch& L, cudaStream_t s);
@@ -99,6 +102,9 @@ struct alignas(16) TmaProb {
   int32_t qx, qy, kx, ky, vx, vy;
   float scale_log2;
   int32_t q_tiles;
+  const int32_t* rel_lut;  // T5 table bias (as AttnProb): bias is then the [buckets, H] table
+  int32_t rel_max;
+  int32_t pad;
 };
 static_assert(sizeof(TmaProb) % 16 == 0, "TmaProb is packed into the descriptor ring");
 

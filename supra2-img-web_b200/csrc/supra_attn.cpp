@@ -91,6 +91,7 @@ struct Queued {
   double flops;
   double bytes;
   int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TMA tensor maps)
+  int32_t t5_buckets, t5_maxd;      // T5 table bias (SUPRA_ATTN_F_T5_TABLE), else 0
 };
 
 // A tensor map over a whole operand buffer: [rows, ld] fp32, boxes of box_cols columns x
@@ -381,7 +382,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   if (!d) return set_err(c, SUPRA_ATTN_EINVAL, "descriptor is NULL");
-  if (d->flags & ~SUPRA_ATTN_F_DEFAULT_SCALE) return set_err(c, SUPRA_ATTN_EINVAL, "unknown flag bits 0x%x", d->flags);
+  if (d->flags & ~(SUPRA_ATTN_F_DEFAULT_SCALE | SUPRA_ATTN_F_T5_TABLE))
+    return set_err(c, SUPRA_ATTN_EINVAL, "unknown flag bits 0x%x", d->flags);
   if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
     return set_err(c, SUPRA_ATTN_EINVAL, "unknown variant %d", d->variant);
   if (d->Lq < 0 || d->Lq > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lq=%d out of range [0, 2^30]", d->Lq);
@@ -421,10 +423,23 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   if (d->o_off + (int64_t)d->Lq * HD > d->out_size)
     return set_err(c, SUPRA_ATTN_EINVAL, "out out of bounds: needs %lld floats, out_size=%lld",
                    (long long)(d->o_off + (int64_t)d->Lq * HD), (long long)d->out_size);
-  const int64_t nbias = (int64_t)d->H * d->Lq * d->Lk;
+  const bool t5 = (d->flags & SUPRA_ATTN_F_T5_TABLE) != 0;
+  const int32_t t5_buckets = t5 ? (int32_t)(d->bias_param & 0xffffu) : 0;
+  const int32_t t5_maxd = t5 ? (int32_t)(d->bias_param >> 16) : 0;
+  if (t5) {
+    if (!d->bias) return set_err(c, SUPRA_ATTN_EINVAL, "SUPRA_ATTN_F_T5_TABLE: bias must point at the table");
+    if (supra_attn_relative_bucket(0, t5_buckets, t5_maxd) < 0)
+      return set_err(c, SUPRA_ATTN_EINVAL,
+                     "T5 table: buckets (bias_param bits 0-15) must be even and >= 4 and max_distance "
+                     "(bits 16-31) > buckets/4; got buckets=%d max_distance=%d", t5_buckets, t5_maxd);
+  } else if (d->bias_param != 0) {
+    return set_err(c, SUPRA_ATTN_EINVAL, "bias_param must be 0 without SUPRA_ATTN_F_T5_TABLE");
+  }
+  const int64_t nbias = t5 ? (int64_t)t5_buckets * d->H : (int64_t)d->H * d->Lq * d->Lk;
   if (d->bias && nbias > d->bias_size)
-    return set_err(c, SUPRA_ATTN_EINVAL, "bias must hold H*Lq*Lk=%lld floats, bias_size=%lld", (long long)nbias,
-                   (long long)d->bias_size);
+    return set_err(c, SUPRA_ATTN_EINVAL, t5 ? "T5 table must hold buckets*H=%lld floats, bias_size=%lld"
+                                            : "bias must hold H*Lq*Lk=%lld floats, bias_size=%lld",
+                   (long long)nbias, (long long)d->bias_size);
 
   // byte ranges for hazard tracking; the output may not alias an input of the same problem
   // (a writable binding may not alias a read-only one in one WebGPU dispatch)
@@ -468,6 +483,9 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   q.p.scale = scale;
   q.p.scale_log2 = scale * kLog2e;
   q.bias = d->bias != nullptr;
+  q.t5_buckets = t5_buckets;
+  q.t5_maxd = t5_maxd;
+  q.p.rel_max = t5_maxd;
   // 16-byte aligned rows for the bulk-copy engine (the reference's fused path needs the same
   // %4 alignment of every stride and offset, app/gpu/ops.js:111)
   q.aligned = (d->D % 4 == 0) && (d->ldq % 4 == 0) && (d->ldk % 4 == 0) && (d->ldv % 4 == 0) &&
@@ -516,6 +534,32 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
 }
 
 // ---- flush ---------------------------------------------------------------------------------------
+// T5 table bias: one bucket table per distinct (buckets, max_distance) among a launch's
+// problems, over relative positions [-max_distance, max_distance] (app/models/t5.js:14-23; the
+// bucket saturates at max_distance, so the kernels clamp beyond it). off[i] is problem i's
+// table offset in ints within blob, or -1 (no T5 table). Returns the blob's bytes, 16-aligned.
+size_t t5_luts(const std::vector<const Queued*>& g, std::vector<int32_t>& blob, std::vector<int64_t>& off) {
+  blob.clear();
+  off.assign(g.size(), -1);
+  std::vector<std::pair<int64_t, int64_t>> seen;  // (buckets | maxd << 32, offset)
+  for (size_t i = 0; i < g.size(); ++i) {
+    const Queued& q = *g[i];
+    if (q.t5_buckets == 0) continue;
+    const int64_t key = (int64_t)q.t5_buckets | ((int64_t)q.t5_maxd << 32);
+    int64_t at = -1;
+    for (auto& kv : seen)
+      if (kv.first == key) at = kv.second;
+    if (at < 0) {
+      at = (int64_t)blob.size();
+      seen.emplace_back(key, at);
+      for (int32_t r = -q.t5_maxd; r <= q.t5_maxd; ++r)
+        blob.push_back(supra_attn_relative_bucket(r, q.t5_buckets, q.t5_maxd));
+    }
+    off[i] = at;
+  }
+  return align16(blob.size() * sizeof(int32_t));
+}
+
 int flush_fused(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   const Queued& first = *g[0];
   const int mq = supra::fused_cfg_tile_rows(first.cfg);
@@ -534,22 +578,27 @@ int flush_fused(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   }
   if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
   begin[n] = (int32_t)total;
+  std::vector<int32_t> lut;
+  std::vector<int64_t> loff;
   const size_t pbytes = align16(sizeof(AttnProb) * n);
+  const size_t lbytes = t5_luts(g, lut, loff);
   const size_t bbytes = sizeof(int32_t) * (n + 1);
   char *h = nullptr, *dv = nullptr;
-  int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
+  int rc = ring_reserve(c, pbytes + lbytes + bbytes, &h, &dv);
   if (rc) return rc;
   AttnProb* hp = reinterpret_cast<AttnProb*>(h);
   for (int i = 0; i < n; ++i) {
     hp[i] = g[i]->p;
     hp[i].q_tiles = (g[i]->p.Lq + mq - 1) / mq;
+    hp[i].rel_lut = loff[i] < 0 ? nullptr : reinterpret_cast<const int32_t*>(dv + pbytes) + loff[i];
   }
-  std::memcpy(h + pbytes, begin.data(), bbytes);
-  rc = ring_commit(c, h, dv, pbytes + bbytes);
+  if (!lut.empty()) std::memcpy(h + pbytes, lut.data(), lut.size() * sizeof(int32_t));
+  std::memcpy(h + pbytes + lbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pbytes + lbytes + bbytes);
   if (rc) return rc;
   AttnLaunch L;
   L.probs = reinterpret_cast<const AttnProb*>(dv);
-  L.begin = reinterpret_cast<const int32_t*>(dv + pbytes);
+  L.begin = reinterpret_cast<const int32_t*>(dv + pbytes + lbytes);
   L.n = n;
   L.total = (int32_t)total;
   L.status = c->d_status;
@@ -561,11 +610,12 @@ int flush_fused(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     for (int i = 1; i < n && uni; ++i) uni = (begin[i + 1] - begin[i]) == t0;
     if (uni) L.uniform = (int32_t)t0;
   }
-  const char* name = supra::attn_fp32_name(first.cfg, first.bias, first.aligned);
+  const int bias_mode = first.t5_buckets ? 2 : first.bias ? 1 : 0;
+  const char* name = supra::attn_fp32_name(first.cfg, bias_mode, first.aligned);
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = supra::launch_attn_fp32(first.cfg, first.bias, first.aligned, L, c->stream);
+    e = supra::launch_attn_fp32(first.cfg, bias_mode, first.aligned, L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;
@@ -620,14 +670,22 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
   qk[nu] = (int32_t)tq;
   pv[nu] = (int32_t)tp;
   rw[nu] = (int32_t)tr;
-  const size_t pbytes = align16(sizeof(AttnProb) * np);
+  std::vector<int32_t> lut;
+  std::vector<int64_t> loff;
+  const size_t lbytes = t5_luts(g, lut, loff);
+  const size_t pbytes = align16(sizeof(AttnProb) * np) + lbytes;  // problems, then T5 bucket tables
   const size_t ubytes = align16(sizeof(GemmUnit) * nu);
   const size_t ibytes = align16(sizeof(int32_t) * (nu + 1));
   char *h = nullptr, *dv = nullptr;
   rc = ring_reserve(c, pbytes + ubytes + 3 * ibytes, &h, &dv);
   if (rc) return rc;
   AttnProb* hp = reinterpret_cast<AttnProb*>(h);
-  for (int i = 0; i < np; ++i) hp[i] = g[i]->p;
+  const size_t lut_at = pbytes - lbytes;
+  for (int i = 0; i < np; ++i) {
+    hp[i] = g[i]->p;
+    hp[i].rel_lut = loff[i] < 0 ? nullptr : reinterpret_cast<const int32_t*>(dv + lut_at) + loff[i];
+  }
+  if (!lut.empty()) std::memcpy(h + lut_at, lut.data(), lut.size() * sizeof(int32_t));
   std::memcpy(h + pbytes, units.data(), sizeof(GemmUnit) * nu);
   std::memcpy(h + pbytes + ubytes, qk.data(), sizeof(int32_t) * (nu + 1));
   std::memcpy(h + pbytes + ubytes + ibytes, pv.data(), sizeof(int32_t) * (nu + 1));
@@ -752,6 +810,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     t.o_off = P.o_off;
     t.ldo = P.ldo;
     t.bias = P.bias;
+    t.rel_max = P.rel_max;
     t.Lq = P.Lq;
     t.Lk = P.Lk;
     t.H = P.H;
@@ -787,25 +846,31 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   }
   if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
   begin[n] = (int32_t)total;
+  std::vector<int32_t> lut;
+  std::vector<int64_t> loff;
   const size_t pbytes = align16(sizeof(supra::TmaProb) * n);
+  const size_t lbytes = t5_luts(g, lut, loff);
   const size_t mbytes = sizeof(CUtensorMap) * maps.size();
   const size_t bbytes = sizeof(int32_t) * (n + 1);
   char *h = nullptr, *dv = nullptr;
-  int rc = ring_reserve(c, 64 + pbytes + mbytes + bbytes, &h, &dv);
+  int rc = ring_reserve(c, 64 + pbytes + mbytes + lbytes + bbytes, &h, &dv);
   if (rc) return rc;
   // tensor maps must sit on a 64-byte boundary in device memory
   const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
   char* hm = h + pad;
   char* dm = dv + pad;
+  for (int i = 0; i < n; ++i)
+    probs[i].rel_lut = loff[i] < 0 ? nullptr : reinterpret_cast<const int32_t*>(dm + mbytes + pbytes) + loff[i];
   std::memcpy(hm, maps.data(), mbytes);
   std::memcpy(hm + mbytes, probs.data(), sizeof(supra::TmaProb) * n);
-  std::memcpy(hm + mbytes + pbytes, begin.data(), bbytes);
-  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
+  if (!lut.empty()) std::memcpy(hm + mbytes + pbytes, lut.data(), lut.size() * sizeof(int32_t));
+  std::memcpy(hm + mbytes + pbytes + lbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + lbytes + bbytes);
   if (rc) return rc;
   supra::TmaLaunch L;
   L.maps = reinterpret_cast<const CUtensorMap*>(dm);
   L.probs = reinterpret_cast<const supra::TmaProb*>(dm + mbytes);
-  L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes);
+  L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes + lbytes);
   L.n = n;
   L.total = (int32_t)total;
   L.uniform = 0;
@@ -831,7 +896,8 @@ int do_flush(supra_attn_ctx* c) {
   if (c->queue.empty()) return SUPRA_ATTN_OK;
   std::map<int, std::vector<const Queued*>> groups;
   for (const Queued& q : c->queue) {
-    const int key = q.path * 1024 + q.cfg * 4 + (q.bias ? 2 : 0) + (q.aligned ? 1 : 0);
+    // (a T5 table and an expanded bias run as different kernel forms)
+    const int key = q.path * 1024 + q.cfg * 8 + (q.t5_buckets ? 4 : 0) + (q.bias ? 2 : 0) + (q.aligned ? 1 : 0);
     groups[key].push_back(&q);
   }
   int rc = SUPRA_ATTN_OK;

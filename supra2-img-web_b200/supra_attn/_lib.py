@@ -15,6 +15,7 @@ LIB_PATH = os.environ.get("SUPRA_ATTN_LIB", os.path.join(_HERE, "libsupra_attn.s
 OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, EDEVICE, ESTATE = range(7)
 FP32, TF32 = 0, 1
 F_DEFAULT_SCALE = 0x1
+F_T5_TABLE = 0x2
 
 
 class Desc(C.Structure):
@@ -27,7 +28,7 @@ class Desc(C.Structure):
         ("ldq", C.c_int64), ("ldk", C.c_int64), ("ldv", C.c_int64),
         ("q_off", C.c_int64), ("k_off", C.c_int64), ("v_off", C.c_int64), ("o_off", C.c_int64),
         ("Lq", C.c_int32), ("Lk", C.c_int32), ("H", C.c_int32), ("D", C.c_int32),
-        ("scale", C.c_float), ("variant", C.c_int32), ("flags", C.c_uint32), ("reserved", C.c_uint32),
+        ("scale", C.c_float), ("variant", C.c_int32), ("flags", C.c_uint32), ("bias_param", C.c_uint32),
     ]
 
 

@@ -196,8 +196,13 @@ def _as_buf(x):
 
 
 def make_desc(*, q, k, v, out, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff=0, oOff=0, scale=None,
-              bias=None, variant="fp32") -> Desc:
-    """Packs one ops.attention call into a supra_attn_desc (no validation; the library does it)."""
+              bias=None, t5_table=None, t5_buckets=32, t5_max_distance=128, variant="fp32") -> Desc:
+    """Packs one ops.attention call into a supra_attn_desc (no validation; the library does it).
+
+    t5_table (instead of bias): T5's [buckets, H] relative-attention-bias table; the kernels form
+    the [H, Lq, Lk] bias from it (SUPRA_ATTN_F_T5_TABLE)."""
+    if t5_table is not None and bias is not None:
+        raise ValueError("pass either bias or t5_table, not both")
     d = Desc()
     d.q, d.q_size = _as_buf(q)
     d.k, d.k_size = _as_buf(k)
@@ -205,6 +210,11 @@ def make_desc(*, q, k, v, out, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff
     d.out, d.out_size = _as_buf(out)
     if bias is not None:
         d.bias, d.bias_size = _as_buf(bias)
+    if t5_table is not None:
+        d.bias, d.bias_size = _as_buf(t5_table)
+        if not (0 <= int(t5_buckets) < 1 << 16 and 0 <= int(t5_max_distance) < 1 << 16):
+            raise ValueError("t5_buckets and t5_max_distance must fit in 16 bits")
+        d.bias_param = int(t5_buckets) | (int(t5_max_distance) << 16)
     d.ldq, d.ldk, d.ldv = int(ldq), int(ldk), int(ldv)
     d.q_off, d.k_off, d.v_off, d.o_off = int(qOff), int(kOff), int(vOff), int(oOff)
     d.Lq, d.Lk, d.H, d.D = int(Lq), int(Lk), int(H), int(D)
@@ -213,6 +223,8 @@ def make_desc(*, q, k, v, out, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff
         d.scale = 0.0
     else:
         d.scale = float(scale)
+    if t5_table is not None:
+        d.flags |= _lib.F_T5_TABLE
     if variant not in VARIANTS:
         raise ValueError(f"variant must be one of {sorted(VARIANTS)}")
     d.variant = VARIANTS[variant]
@@ -220,18 +232,22 @@ def make_desc(*, q, k, v, out, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff
 
 
 def attention(gpu: GPU, *, q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0, vOff=0, oOff=0, scale=None,
-              bias=None, out=None, variant="fp32"):
+              bias=None, out=None, variant="fp32", t5_table=None, t5_buckets=32, t5_max_distance=128):
     """ops.attention (app/gpu/ops.js:109): records the call and returns the output tensor.
 
     q: [Lq, ldq] with head h at column qOff + h*D; k, v: [Lk, ldk] / [Lk, ldv] with head h at
     kOff / vOff + h*D. The output rows [Lq, H*D] are written at element offset oOff of `out`
     (allocated as gpu.empty([Lq, H*D]) when omitted). scale defaults to 1/sqrt(D). bias is an
-    additive score bias [H, Lq, Lk]. Work runs at the next flush/sync/read.
+    additive score bias [H, Lq, Lk]. Alternatively t5_table, T5's [buckets, H] relative-bias
+    table, makes the kernels form that bias themselves (bias[h, i, j] = table[bucket(j - i), h],
+    app/models/t5.js:55-65) instead of reading an expanded one. Work runs at the next
+    flush/sync/read.
     """
     o = out if out is not None else gpu.empty([Lq, H * D])
     try:
         d = make_desc(q=q, k=k, v=v, out=o, Lq=Lq, Lk=Lk, H=H, D=D, ldq=ldq, ldk=ldk, ldv=ldv, qOff=qOff, kOff=kOff,
-                      vOff=vOff, oOff=oOff, scale=scale, bias=bias, variant=variant)
+                      vOff=vOff, oOff=oOff, scale=scale, bias=bias, t5_table=t5_table, t5_buckets=t5_buckets,
+                      t5_max_distance=t5_max_distance, variant=variant)
         gpu.enqueue(d)
     except Exception:
         if out is None:

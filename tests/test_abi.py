@@ -130,6 +130,36 @@ def test_bias_too_small():
     assert st == _lib.EINVAL and "bias" in msg
 
 
+def t5_table_desc(**kw):
+    """T5 encoder attention (app/models/t5.js:80) with the [32, 12] table in place of the bias."""
+    d = dit_self_desc(q_off=0, k_off=0, v_off=0, o_off=0, ldq=768, ldk=768, ldv=768, Lq=37, Lk=37, H=12, D=64)
+    d.q_size = d.k_size = d.v_size = 37 * 768
+    d.out_size = 37 * 768
+    d.bias = BASE_B
+    d.bias_size = 32 * 12
+    d.flags = _lib.F_T5_TABLE
+    d.bias_param = 32 | (128 << 16)
+    d.scale = 1.0
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def test_t5_table_descriptors():
+    assert check(t5_table_desc()) == (_lib.OK, "")
+    assert check(t5_table_desc(flags=_lib.F_T5_TABLE | _lib.F_DEFAULT_SCALE))[0] == _lib.OK
+    cases = [
+        (dict(bias=0), "table"),                             # the flag needs the table pointer
+        (dict(bias_size=32 * 12 - 1), "buckets*H"),          # table too small
+        (dict(bias_param=31 | (128 << 16)), "buckets"),      # odd bucket count
+        (dict(bias_param=32 | (8 << 16)), "max_distance"),   # max_distance <= buckets/4
+        (dict(flags=0), "bias_param"),                       # parameters without the flag
+    ]
+    for kw, needle in cases:
+        st, msg = check(t5_table_desc(**kw))
+        assert st == _lib.EINVAL and needle in msg, (kw, msg)
+
+
 def test_out_may_not_alias_inputs():
     d = dit_self_desc()
     d.out = BASE_Q  # writes over rows that q/k/v of this call read

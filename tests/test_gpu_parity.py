@@ -96,6 +96,75 @@ def test_t5_golden(gpu, golden, L):
     bias.release()
 
 
+@pytest.mark.parametrize("L", [1, 5, 37, 128])
+def test_t5_table_golden(gpu, golden, L):
+    """The T5 call site with the [32, 12] table in place of the expanded bias: the kernel forms
+    the bias itself and gives the same bits as the expanded-bias call."""
+    import supra_attn
+
+    table = dev(golden("t5_table"))
+    bias = supra_attn.position_bias(gpu, table, L, H=12, buckets=32, max_distance=128)
+    q, k, v = (dev(golden(f"t5_L{L}_{n}")) for n in "qkv")
+    kw = dict(q=q, k=k, v=v, Lq=L, Lk=L, H=12, D=64, ldq=768, ldk=768, ldv=768, scale=1.0)
+    o_tab = attn(gpu, t5_table=table, t5_buckets=32, t5_max_distance=128, **kw)
+    o_exp = attn(gpu, bias=bias, **kw)
+    got = gpu.read(o_tab)
+    np.testing.assert_array_equal(got, gpu.read(o_exp))
+    assert_close(got, golden(f"t5_L{L}_out"))
+    for t in (o_tab, o_exp, bias):
+        t.release()
+
+
+@pytest.mark.parametrize("L,H,D", [(300, 12, 64), (70, 2, 128), (70, 2, 512)])
+def test_t5_table_long_and_wide(gpu, L, H, D):
+    """Relative positions beyond max_distance (the bucket saturates; the kernels clamp) and the
+    D = 128 and D = 512 kernels, against the float64 oracle and the expanded-bias call."""
+    import supra_attn
+
+    rng = np.random.default_rng(L + D)
+    table = (0.5 * rng.standard_normal(32 * H)).astype(np.float32)
+    q, k, v = (rng.standard_normal(L * H * D).astype(np.float32) for _ in range(3))
+    scale = (64.0 / D) ** 0.5
+    ref_bias = oracle.position_bias(table, L, H, 32, 128).reshape(-1)
+    ref = oracle.attention_ops(q, k, v, L, L, H, D, H * D, H * D, H * D, scale=scale, bias=ref_bias)
+    td = dev(table)
+    kw = dict(q=dev(q), k=dev(k), v=dev(v), Lq=L, Lk=L, H=H, D=D, ldq=H * D, ldk=H * D, ldv=H * D, scale=scale)
+    o_tab = attn(gpu, t5_table=td, **kw)
+    bias = supra_attn.position_bias(gpu, td, L, H=H, buckets=32, max_distance=128)
+    o_exp = attn(gpu, bias=bias, **kw)
+    got = gpu.read(o_tab)
+    assert_close(got, ref)
+    np.testing.assert_array_equal(got, gpu.read(o_exp))
+    for t in (o_tab, o_exp, bias):
+        t.release()
+
+
+def test_t5_table_ragged_batch(gpu):
+    """256 prompts of ragged length (config 3) in one flush, table mode, against the oracle."""
+    import supra_attn
+
+    rng = np.random.default_rng(33)
+    Ls = rng.integers(1, 129, 256)
+    table = (0.1 * rng.standard_normal(32 * 12)).astype(np.float32)
+    offs = np.concatenate([[0], np.cumsum(Ls * 768)]).astype(np.int64)
+    q, k, v = (rng.standard_normal(int(offs[-1])).astype(np.float32) for _ in range(3))
+    qd, kd, vd, td = dev(q), dev(k), dev(v), dev(table)
+    out = dev(np.zeros(int(offs[-1])))
+    descs = (supra_attn.Desc * 256)()
+    for i, L in enumerate(Ls):
+        descs[i] = supra_attn.make_desc(q=qd, k=kd, v=vd, out=out, Lq=int(L), Lk=int(L), H=12, D=64, ldq=768, ldk=768,
+                                        ldv=768, qOff=int(offs[i]), kOff=int(offs[i]), vOff=int(offs[i]),
+                                        oOff=int(offs[i]), scale=1.0, t5_table=td)
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    got = host(out)
+    for i in list(range(0, 256, 17)) + [255]:
+        L, a, b = int(Ls[i]), int(offs[i]), int(offs[i + 1])
+        bias = oracle.position_bias(table, L, 12, 32, 128).reshape(-1)
+        assert_close(got[a:b], oracle.attention_ops(q[a:b], k[a:b], v[a:b], L, L, 12, 64, 768, 768, 768, scale=1.0,
+                                                    bias=bias))
+
+
 def test_vae_golden(gpu, golden):
     T = golden.cases["vae_small"]["T"]
     q, k, v = (dev(golden(f"vae_small_{n}")) for n in "qkv")

@@ -158,6 +158,34 @@ def test_t5_golden_tf32(gpu, golden, L):
     bias.release()
 
 
+@pytest.mark.parametrize("L", [5, 128, 300])
+def test_t5_table_tf32(gpu, golden, L):
+    """The T5 table in place of the expanded bias on the tensor-core kernel: same bits as the
+    expanded-bias call, and within the TF32 bar of the oracle (L = 300 clamps beyond max_distance)."""
+    import supra_attn
+
+    rng = np.random.default_rng(L)
+    table = golden("t5_table").reshape(-1).astype(np.float32)
+    q, k, v = (rng.standard_normal(L * 768).astype(np.float32) for _ in range(3))
+    td = dev(table)
+    kw = dict(q=dev(q), k=dev(k), v=dev(v), Lq=L, Lk=L, H=12, D=64, ldq=768, ldk=768, ldv=768, scale=0.125,
+              variant="tf32")
+    gpu.profile(True)
+    gpu.profile_reset()
+    o_tab = supra_attn.attention(gpu, t5_table=td, **kw)
+    got = gpu.read(o_tab)
+    names = [r["name"] for r in gpu.profile_report()]
+    gpu.profile(False)
+    assert names == ["attn_tf32_d64_bias"], names
+    bias = supra_attn.position_bias(gpu, td, L, H=12)
+    o_exp = supra_attn.attention(gpu, bias=bias, **kw)
+    np.testing.assert_array_equal(got, gpu.read(o_exp))
+    ref_bias = oracle.position_bias(table, L, 12, 32, 128).reshape(-1)
+    check(got, oracle.attention_ops(q, k, v, L, L, 12, 64, 768, 768, 768, scale=0.125, bias=ref_bias), TOL_TF32)
+    for t in (o_tab, o_exp, bias):
+        t.release()
+
+
 def test_tf32_determinism(gpu):
     import supra_attn
 
