@@ -44,7 +44,9 @@ constexpr uint32_t kKVBytes = 2 * kKVSlab;  // one K (or V) block
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_K = OFF_Q + kQBytes;
 constexpr uint32_t OFF_V = OFF_K + kNS * kKVBytes;
-constexpr uint32_t OFF_BAR = OFF_V + kNS * kKVBytes;
+constexpr uint32_t OFF_O = OFF_V + kNS * kKVBytes;  // epilogue staging: 2 KB per softmax warp
+constexpr uint32_t kOStage = 16 * 32 * 4;            // 16 rows x 32 columns of O
+constexpr uint32_t OFF_BAR = OFF_O + 4 * kOStage;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;  // barriers + alignment slack for the 1024-B base
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t COL_S0 = 0, COL_S1 = 64, COL_O = 128;
@@ -119,6 +121,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
   uint8_t* Qs = base + OFF_Q;
   uint8_t* Ks = base + OFF_K;
   uint8_t* Vs = base + OFF_V;
+  float* Os = reinterpret_cast<float*>(base + OFF_O);
   Bars* B = reinterpret_cast<Bars*>(base + OFF_BAR);
   volatile int32_t* abort = &B->abort;
 
@@ -357,12 +360,38 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
       tc::tmem_wait_ld();
       tc::fence_before_sync();
       mbar_arrive(&B->o_empty);  // the next tile's first PV may overwrite O
+      // O / l, stored coalesced: each thread holds its own row, so the warp's 32 x 64 block goes
+      // through a 16 x 32 shared-memory slot (16-byte chunks swizzled by row) in four rounds and
+      // every store instruction writes four whole 128-byte row segments.
       const float inv = 1.0f / l;
-      if (T.q0 + row < Lq) {
-        float* dst = pp->o + pp->o_off + (int64_t)(T.q0 + row) * pp->ldo + (int64_t)T.h * kD;
+      const int64_t ldo = pp->ldo;
+      float* orow0 = pp->o + pp->o_off + (int64_t)(T.q0 + 32 * q4) * ldo + (int64_t)T.h * kD;
+      const int vrows = Lq - (T.q0 + 32 * q4);  // rows of this warp's 32 that exist
+      float* stg = Os + q4 * (kOStage / 4);
 #pragma unroll
-        for (int c = 0; c < 64; c += 4)
-          *reinterpret_cast<float4*>(dst + c) = make_float4(v[c] * inv, v[c + 1] * inv, v[c + 2] * inv, v[c + 3] * inv);
+      for (int hr = 0; hr < 2; ++hr) {
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          if ((lane >> 4) == hr) {
+            const int r = lane & 15;
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const int c = 32 * hc + 4 * c4;
+              *reinterpret_cast<float4*>(stg + r * 32 + ((c4 ^ (r & 7)) << 2)) =
+                  make_float4(v[c] * inv, v[c + 1] * inv, v[c + 2] * inv, v[c + 3] * inv);
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = 4 * i + (lane >> 3);
+            const int c4 = lane & 7;
+            const float4 val = *reinterpret_cast<const float4*>(stg + r * 32 + ((c4 ^ (r & 7)) << 2));
+            if (16 * hr + r < vrows)
+              *reinterpret_cast<float4*>(orow0 + (int64_t)(16 * hr + r) * ldo + 32 * hc + 4 * c4) = val;
+          }
+          __syncwarp();
+        }
       }
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 22, n);
