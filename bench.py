@@ -370,6 +370,54 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
             return arr
 
         run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512)
+        del qv, kvv, vv, ov
+
+    # Cross-attention K/V preparation for configs[4]'s 2048 sequences (app/models/dit.js:137-144):
+    # ctx_proj over every sequence's T5 rows at once, then the 14 blocks' kv projections as one
+    # product with the stacked [14*1152, 576] weights (the cross attention reads its K/V in place).
+    # Two flushes (the second reads the first's output); fp32 FFMA (a TF32 request runs the same).
+    Lc = workload_lengths(1024, seed)
+    rows = sum(Lc)
+    ctx = torch.randn(rows * 768, device=dev, generator=g)
+    wp = torch.randn(576 * 768, device=dev, generator=g) * 768 ** -0.5
+    bp = torch.randn(576, device=dev, generator=g) * 0.1
+    wkv = torch.randn(14 * 1152 * 576, device=dev, generator=g) * 576 ** -0.5
+    bkv = torch.randn(14 * 1152, device=dev, generator=g) * 0.1
+    p = torch.empty(rows * 576, device=dev)
+    kv_all = torch.empty(rows * 14 * 1152, device=dev)
+    d1 = supra_attn.make_linear_desc(x=ctx, w=wp, bias=bp, y=p, M=rows, N=576, K=768)
+    d2 = supra_attn.make_linear_desc(x=p, w=wkv, bias=bkv, y=kv_all, M=rows, N=14 * 1152, K=576)
+    enq = supra_attn.lib.supra_attn_enqueue_linear
+
+    def prep():
+        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d1)), gpu.ctx)
+        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d2)), gpu.ctx)  # hazard: flushes d1 first
+        gpu.flush()
+
+    prep()
+    gpu.sync()
+    gpu.profile(True)
+    gpu.profile_reset()
+    times = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        prep()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    prof = gpu.profile_report()
+    gpu.profile(False)
+    ms = statistics.median(times)
+    flops = 2.0 * rows * (768 * 576 + 576 * 14 * 1152)
+    bytes_ = 4.0 * (rows * 768 + 576 * 768 + rows * 576 * 2 + 14 * 1152 * 576 + rows * 14 * 1152)
+    out["ctx_prep_2048"] = {"fp32": {"ms": ms, "seq_per_s": 2048 / (ms / 1e3), "rows": rows,
+                                     "tflops": flops / (ms / 1e3) / 1e12, "gbs": bytes_ / (ms / 1e3) / 1e9,
+                                     "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                                     "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
+                                     "kernels": sorted({r["name"] for r in prof})}}
     return out
 
 

@@ -151,6 +151,34 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
                                             int32_t buckets, int32_t max_distance, int32_t H, int32_t L,
                                             float* out, int64_t out_size);
 
+/* ---- linear: the projections beside the attention (ops.linear, app/gpu/ops.js:35-43) -------- */
+/* One y = x W^T (+ bias) problem, recorded like an attention problem (same queue, same hazard
+ * tracking, one grouped launch per flush). x: M rows of K floats, row stride ldx, first row at
+ * x_off; w: [N, K] row-major with row stride ldw >= K (the reference's weight layout, x @ W^T);
+ * bias: N floats or NULL; y: M rows of N floats, row stride ldy >= N, first row at y_off. All
+ * counts in floats. Computed in fp32 with FFMA (a TF32 request runs the same kernel). The
+ * reference's optional activation, residual and gate (app/gpu/ops.js:33-43) are not part of
+ * this entry point; flags and reserved must be 0.
+ * Cross-attention K/V preparation (app/models/dit.js:137-144) is two calls: ctx_proj, then ONE
+ * product with the 14 blocks' kv weights stacked [14*1152, 576]; block b's cross attention then
+ * reads K at column 1152*b and V at 1152*b + 576 of rows of stride 14*1152, without a copy. */
+typedef struct supra_attn_linear_desc {
+  const float* x;
+  const float* w;
+  const float* bias;
+  float* y;
+  int64_t x_size, w_size, bias_size, y_size;
+  int64_t ldx, ldw, ldy;
+  int64_t x_off, y_off;
+  int32_t M, N, K;
+  int32_t variant;
+  uint32_t flags;
+  uint32_t reserved;
+} supra_attn_linear_desc;
+SUPRA_ATTN_API int supra_attn_enqueue_linear(supra_attn_ctx* ctx, const supra_attn_linear_desc* desc);
+/* Validates a linear descriptor as supra_attn_enqueue_linear does (pure host function). */
+SUPRA_ATTN_API int supra_attn_check_linear_desc(const supra_attn_linear_desc* desc, char* msg, int32_t cap);
+
 /* ---- profiling (the reference's Profiler, app/gpu/device.js:91-99,222-233,272-325) -------- */
 /* When on, every grouped launch is bracketed by CUDA events on the launching stream and
  * aggregated by kernel name with its algorithmic FLOPs (4*Lq*Lk*D*H, app/gpu/ops.js:116) and

@@ -1,0 +1,45 @@
+"""CPU restatement of the reference's linear layer and the cross-attention K/V preparation.
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): never imported by the product.
+
+  linear           -- ops.linear (app/gpu/ops.js:35-43): y = x @ W^T (+ bias) with W in the
+                      reference's [N, K] layout, on flat float32 arrays with row strides and
+                      element offsets, computed in float64.
+  prepare_context  -- DiT.prepareContext (app/models/dit.js:137-144): p = ctx_proj(ctx), then
+                      each block's kv projection of p ([L, 1152]: K at columns 0..575, V at
+                      576..1151), as tools/reference.py:92,99 computes them.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def linear(x, w, M, N, K, bias=None, ldx=None, ldw=None, ldy=None, x_off=0, y_off=0, out=None):
+    """Flat-array ops.linear; returns the flat float32 `out` (allocated [M, N] when None)."""
+    ldx = K if ldx is None else ldx
+    ldw = K if ldw is None else ldw
+    ldy = N if ldy is None else ldy
+    xa = np.asarray(x, dtype=np.float32).reshape(-1)
+    wa = np.asarray(w, dtype=np.float32).reshape(-1)
+    rows = x_off + np.arange(M, dtype=np.int64)[:, None] * ldx + np.arange(K, dtype=np.int64)[None, :]
+    wrows = np.arange(N, dtype=np.int64)[:, None] * ldw + np.arange(K, dtype=np.int64)[None, :]
+    y = xa[rows].astype(np.float64) @ wa[wrows].astype(np.float64).T
+    if bias is not None:
+        y = y + np.asarray(bias, dtype=np.float64).reshape(-1)[:N][None, :]
+    if out is None:
+        out = np.zeros(y_off + (M - 1) * ldy + N if M else 1, dtype=np.float32)
+    if M:
+        idx = y_off + np.arange(M, dtype=np.int64)[:, None] * ldy + np.arange(N, dtype=np.int64)[None, :]
+        out[idx] = y.astype(np.float32)
+    return out
+
+
+def prepare_context(ctx, w_proj, b_proj, w_kv, b_kv):
+    """ctx [L, Kc]; w_proj [D, Kc], b_proj [D]; w_kv / b_kv lists of [2D, D] / [2D] per block.
+    Returns (p [L, D], [kv_b [L, 2D] for each block]) in float32."""
+    ctx = np.asarray(ctx, dtype=np.float64)
+    p = ctx @ np.asarray(w_proj, dtype=np.float64).T + np.asarray(b_proj, dtype=np.float64)[None, :]
+    kvs = [(p @ np.asarray(w, dtype=np.float64).T + np.asarray(b, dtype=np.float64)[None, :]).astype(np.float32)
+           for w, b in zip(w_kv, b_kv)]
+    return p.astype(np.float32), kvs

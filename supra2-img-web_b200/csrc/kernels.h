@@ -128,6 +128,30 @@ constexpr int kFwBoxRows = 32;
 cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s);
 int attn_fp32_warp_tile_rows();
 
+// y = x W^T (+ bias) for one ops.linear call (app/gpu/ops.js:35-43), linear_fp32.cu. x rows of
+// stride ldx (the caller's x offset already applied), W [N, K] row-major with row stride ldw,
+// y rows of stride ldy (offset applied).
+struct alignas(16) LinProb {
+  const float* x;
+  const float* w;
+  const float* bias;  // [N] or nullptr
+  float* y;
+  int64_t ldx, ldw, ldy;
+  int32_t M, N, K;
+  int32_t n_tiles;  // column tiles of 128: ceil(N / 128)
+};
+static_assert(sizeof(LinProb) % 16 == 0, "LinProb is packed into the descriptor ring");
+
+// A grouped linear launch: tile t (a 128x128 block of one problem's y) belongs to the problem p
+// with begin[p] <= t < begin[p+1]; within a problem, row tiles outer, column tiles inner.
+struct LinLaunch {
+  const LinProb* probs;
+  const int32_t* begin;
+  int32_t n, total;
+  int32_t* status;
+};
+cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cudaStream_t s);
+
 // Copies bytes (a multiple of 16, both addresses 16-byte aligned) from src, which may be pinned
 // host memory addressable by the device, to device memory dst (stage.cu).
 cudaError_t launch_stage_copy(const void* src, void* dst, size_t bytes, cudaStream_t s);

@@ -1,0 +1,147 @@
+// FP32 linear layer y = x W^T (+ bias): the projections on either side of the attention path
+// (ops.linear, app/gpu/ops.js:35-43; the cross-attention K/V preparation of
+// app/models/dit.js:137-144 runs ctx_proj and then the 14 blocks' kv projections).
+//
+// One grouped launch per flush over every recorded problem: 128x128 output tiles over 256
+// threads, each thread an 8x8 register block (rows rg + 16i, columns cg + 16j), x and W both
+// read along K (W is [N, K] row-major, the reference's weight layout) and staged 16 deep through
+// double-buffered padded shared memory by cp.async, zero-filled past every edge. FFMA only, fp32
+// throughout. Within a problem the row tiles are outer and the column tiles inner, so CTAs that
+// run together share x rows and sweep W, which stays in L2 (the 14 stacked kv weights are
+// 37 MB).
+#include "common.cuh"
+
+namespace supra {
+namespace {
+
+constexpr int kT = 256;   // threads
+constexpr int kBM = 128;  // rows per tile
+constexpr int kBN = 128;  // columns per tile
+constexpr int kBK = 16;   // reduction depth per stage
+constexpr int kS = kBK + 4;  // row stride of the stage buffers (conflict-free float4 reads)
+
+template <bool BIAS, bool ALIGNED>
+__global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
+  __shared__ __align__(16) float As[2][kBM * kS];
+  __shared__ __align__(16) float Bs[2][kBN * kS];
+  const int t = blockIdx.x;
+  if (t >= L.total) {
+    if (threadIdx.x == 0) report_error(L.status, DEV_BAD_TILE, 30);
+    return;
+  }
+  const int pi = find_problem(L.begin, L.n, t);
+  const LinProb& P = L.probs[pi];
+  const int local = t - __ldg(L.begin + pi);
+  const int rt = local / P.n_tiles;
+  const int r0 = rt * kBM;
+  const int c0 = (local - rt * P.n_tiles) * kBN;
+  const int K = P.K;
+  const float* abase = P.x + (int64_t)r0 * P.ldx;
+  const float* bbase = P.w + (int64_t)c0 * P.ldw;
+  const int nr = min(kBM, P.M - r0);
+  const int nc = min(kBN, P.N - c0);
+
+  const int tid = threadIdx.x;
+  const int rg = tid >> 4, cg = tid & 15;
+
+  auto load_stage = [&](int buf, int k0) {
+    if (ALIGNED) {
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {  // 512 float4 per operand
+        const int idx = tid + it * kT;
+        const int r = idx >> 2, c4 = idx & 3;
+        const int k = k0 + c4 * 4;
+        const bool okA = (r < nr) && (k < K);
+        cp_async16(&As[buf][r * kS + c4 * 4], okA ? (const void*)(abase + (int64_t)r * P.ldx + k) : (const void*)abase,
+                   okA ? 16u : 0u);
+        const bool okB = (r < nc) && (k < K);
+        cp_async16(&Bs[buf][r * kS + c4 * 4], okB ? (const void*)(bbase + (int64_t)r * P.ldw + k) : (const void*)bbase,
+                   okB ? 16u : 0u);
+      }
+    } else {
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int idx = tid + it * kT;
+        const int r = idx >> 4, c = idx & 15;
+        const int k = k0 + c;
+        const bool okA = (r < nr) && (k < K);
+        cp_async4(&As[buf][r * kS + c], okA ? (const void*)(abase + (int64_t)r * P.ldx + k) : (const void*)abase,
+                  okA ? 4u : 0u);
+        const bool okB = (r < nc) && (k < K);
+        cp_async4(&Bs[buf][r * kS + c], okB ? (const void*)(bbase + (int64_t)r * P.ldw + k) : (const void*)bbase,
+                  okB ? 4u : 0u);
+      }
+    }
+    cp_async_commit();
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  const int nstage = (K + kBK - 1) / kBK;
+  load_stage(0, 0);
+  for (int st = 0; st < nstage; ++st) {
+    if (st + 1 < nstage) {
+      load_stage((st + 1) & 1, (st + 1) * kBK);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float4* A4 = reinterpret_cast<const float4*>(As[st & 1]) + rg * (kS / 4);
+    const float4* B4 = reinterpret_cast<const float4*>(Bs[st & 1]) + cg * (kS / 4);
+#pragma unroll
+    for (int k4 = 0; k4 < kBK / 4; ++k4) {
+      float4 bf[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 af = A4[i * 16 * (kS / 4) + k4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc[i][j] = fmaf(af.x, bf[j].x, acc[i][j]);
+          acc[i][j] = fmaf(af.y, bf[j].y, acc[i][j]);
+          acc[i][j] = fmaf(af.z, bf[j].z, acc[i][j]);
+          acc[i][j] = fmaf(af.w, bf[j].w, acc[i][j]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
+  float bias[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = rg + 16 * i;
+    if (r >= nr) continue;
+    float* yrow = P.y + (int64_t)(r0 + r) * P.ldy + c0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = cg + 16 * j;
+      if (c < nc) yrow[c] = acc[i][j] + bias[j];
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
+  if (bias) {
+    if (aligned) linear_fp32_kernel<true, true><<<L.total, kT, 0, s>>>(L);
+    else linear_fp32_kernel<true, false><<<L.total, kT, 0, s>>>(L);
+  } else {
+    if (aligned) linear_fp32_kernel<false, true><<<L.total, kT, 0, s>>>(L);
+    else linear_fp32_kernel<false, false><<<L.total, kT, 0, s>>>(L);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace supra

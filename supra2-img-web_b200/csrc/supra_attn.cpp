@@ -80,7 +80,7 @@ struct ByteRange {
   uintptr_t b = 0, e = 0;
 };
 
-enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1, PATH_TF32 = 2, PATH_FP32_TMA = 3 };
+enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1, PATH_TF32 = 2, PATH_FP32_TMA = 3, PATH_LINEAR = 4 };
 
 struct Queued {
   AttnProb p;
@@ -92,6 +92,7 @@ struct Queued {
   double bytes;
   int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TMA tensor maps)
   int32_t t5_buckets, t5_maxd;      // T5 table bias (SUPRA_ATTN_F_T5_TABLE), else 0
+  supra::LinProb lin;               // PATH_LINEAR: the linear problem (p unused)
 };
 
 // A tensor map over a whole operand buffer: [rows, ld] fp32, boxes of box_cols columns x
@@ -533,6 +534,84 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   return SUPRA_ATTN_OK;
 }
 
+int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked* out) {
+  if (!d) return set_err(c, SUPRA_ATTN_EINVAL, "linear descriptor is NULL");
+  if (d->flags || d->reserved) return set_err(c, SUPRA_ATTN_EINVAL, "linear: flags and reserved must be 0");
+  if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: unknown variant %d", d->variant);
+  if (d->M < 0 || d->M > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "linear: M=%d out of range [0, 2^30]", d->M);
+  if (d->N < 1 || d->N > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "linear: N=%d out of range [1, 2^30]", d->N);
+  if (d->K < 1 || d->K > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "linear: K=%d out of range [1, 2^30]", d->K);
+  const int64_t lim = int64_t(1) << 46;
+  if (d->ldx < d->K || d->ldw < d->K || d->ldy < d->N || d->ldx > lim || d->ldw > lim || d->ldy > lim)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: need ldx >= K, ldw >= K, ldy >= N");
+  if (d->x_off < 0 || d->y_off < 0 || d->x_off > lim || d->y_off > lim)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: offset out of range (negative?)");
+  if (!d->x || !d->w || !d->y) return set_err(c, SUPRA_ATTN_EINVAL, "linear: x, w and y must be non-NULL");
+  const void* ptrs[4] = {d->x, d->w, d->y, d->bias};
+  for (int i = 0; i < 4; ++i)
+    if (ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 3u))
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: pointers must be 4-byte aligned float arrays");
+  out->empty = (d->M == 0);
+  const int64_t x_last = d->x_off + (int64_t)(d->M - 1) * d->ldx + d->K - 1;
+  const int64_t w_last = (int64_t)(d->N - 1) * d->ldw + d->K - 1;
+  const int64_t y_last = d->y_off + (int64_t)(d->M - 1) * d->ldy + d->N - 1;
+  if (!out->empty && x_last >= d->x_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: x out of bounds: needs %lld floats, x_size=%lld",
+                   (long long)(x_last + 1), (long long)d->x_size);
+  if (w_last >= d->w_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: w out of bounds: needs %lld floats, w_size=%lld",
+                   (long long)(w_last + 1), (long long)d->w_size);
+  if (d->bias && d->N > d->bias_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: bias must hold N=%d floats, bias_size=%lld", d->N,
+                   (long long)d->bias_size);
+  if (!out->empty && y_last >= d->y_size)
+    return set_err(c, SUPRA_ATTN_EINVAL, "linear: y out of bounds: needs %lld floats, y_size=%lld",
+                   (long long)(y_last + 1), (long long)d->y_size);
+  const int64_t tiles = ((int64_t)d->M + 127) / 128 * (((int64_t)d->N + 127) / 128);
+  if (tiles > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "linear: too many 128x128 tiles");
+  auto rng = [](const float* base, int64_t first, int64_t lastidx) {
+    ByteRange r;
+    r.b = reinterpret_cast<uintptr_t>(base + first);
+    r.e = reinterpret_cast<uintptr_t>(base + lastidx + 1);
+    return r;
+  };
+  out->nreads = 0;
+  if (!out->empty) {
+    out->reads[out->nreads++] = rng(d->x, d->x_off, x_last);
+    out->reads[out->nreads++] = rng(d->w, 0, w_last);
+    if (d->bias) out->reads[out->nreads++] = rng(d->bias, 0, d->N - 1);
+    out->write = rng(d->y, d->y_off, y_last);
+    for (int i = 0; i < out->nreads; ++i)
+      if (out->reads[i].b < out->write.e && out->write.b < out->reads[i].e)
+        return set_err(c, SUPRA_ATTN_EINVAL, "linear: y overlaps an input of the same call");
+  }
+  Queued& q = out->q;
+  std::memset(&q.p, 0, sizeof(q.p));
+  std::memset(&q.lin, 0, sizeof(q.lin));
+  q.lin.x = d->x + d->x_off;
+  q.lin.w = d->w;
+  q.lin.bias = d->bias;
+  q.lin.y = d->y + d->y_off;
+  q.lin.ldx = d->ldx;
+  q.lin.ldw = d->ldw;
+  q.lin.ldy = d->ldy;
+  q.lin.M = d->M;
+  q.lin.N = d->N;
+  q.lin.K = d->K;
+  q.lin.n_tiles = (d->N + 127) / 128;
+  q.path = PATH_LINEAR;
+  q.cfg = 0;
+  q.bias = d->bias != nullptr;
+  q.aligned = (d->K % 4 == 0) && (d->ldx % 4 == 0) && (d->ldw % 4 == 0) && aligned16(d->x + d->x_off) &&
+              aligned16(d->w);
+  q.t5_buckets = q.t5_maxd = 0;
+  q.rows_q = q.rows_k = q.rows_v = 0;
+  q.flops = 2.0 * d->M * (double)d->N * d->K;
+  q.bytes = 4.0 * ((double)d->M * d->K + (double)d->N * d->K + (double)d->M * d->N + (d->bias ? d->N : 0));
+  return SUPRA_ATTN_OK;
+}
+
 // ---- flush ---------------------------------------------------------------------------------------
 // T5 table bias: one bucket table per distinct (buckets, max_distance) among a launch's
 // problems, over relative positions [-max_distance, max_distance] (app/models/t5.js:14-23; the
@@ -892,6 +971,47 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   return SUPRA_ATTN_OK;
 }
 
+// Linear group: one launch over the 128x128 output tiles of every recorded problem.
+int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
+  const int n = (int)g.size();
+  std::vector<int32_t> begin(n + 1);
+  int64_t total = 0;
+  double flops = 0, bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    begin[i] = (int32_t)total;
+    total += (int64_t)((g[i]->lin.M + 127) / 128) * g[i]->lin.n_tiles;
+    flops += g[i]->flops;
+    bytes += g[i]->bytes;
+    if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
+  }
+  begin[n] = (int32_t)total;
+  const size_t pbytes = align16(sizeof(supra::LinProb) * n);
+  const size_t bbytes = sizeof(int32_t) * (n + 1);
+  char *h = nullptr, *dv = nullptr;
+  int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
+  if (rc) return rc;
+  supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(h);
+  for (int i = 0; i < n; ++i) hp[i] = g[i]->lin;
+  std::memcpy(h + pbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pbytes + bbytes);
+  if (rc) return rc;
+  supra::LinLaunch L;
+  L.probs = reinterpret_cast<const supra::LinProb*>(dv);
+  L.begin = reinterpret_cast<const int32_t*>(dv + pbytes);
+  L.n = n;
+  L.total = (int32_t)total;
+  L.status = c->d_status;
+  const char* name = g[0]->bias ? "linear_fp32_bias" : "linear_fp32";
+  cudaError_t e;
+  {
+    ProfScope ps(c, name, flops, bytes);
+    e = supra::launch_linear_fp32(g[0]->bias, g[0]->aligned, L, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, name);
+  c->launches += 1;
+  return SUPRA_ATTN_OK;
+}
+
 int do_flush(supra_attn_ctx* c) {
   if (c->queue.empty()) return SUPRA_ATTN_OK;
   std::map<int, std::vector<const Queued*>> groups;
@@ -906,6 +1026,7 @@ int do_flush(supra_attn_ctx* c) {
     rc = path == PATH_FUSED ? flush_fused(c, kv.second)
          : path == PATH_TF32 ? flush_tma(c, kv.second, true)
          : path == PATH_FP32_TMA ? flush_tma(c, kv.second, false)
+         : path == PATH_LINEAR ? flush_linear(c, kv.second)
                              : flush_gemm(c, kv.second);
     if (rc) break;
   }
@@ -1142,6 +1263,23 @@ int supra_attn_check_desc(const supra_attn_desc* d, char* msg, int32_t cap) {
   supra_attn_ctx tmp;  // only its message field is used; no device state is touched
   Checked ck;
   const int rc = validate(&tmp, d, &ck);
+  if (msg && cap > 0) std::snprintf(msg, (size_t)cap, "%s", rc ? tmp.err.c_str() : "");
+  return rc;
+}
+
+int supra_attn_enqueue_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d) {
+  if (!c) return SUPRA_ATTN_EINVAL;
+  Checked ck;
+  int rc = validate_linear(c, d, &ck);
+  if (rc) return rc;
+  DeviceGuard g(c->device);
+  return record(c, ck);
+}
+
+int supra_attn_check_linear_desc(const supra_attn_linear_desc* d, char* msg, int32_t cap) {
+  supra_attn_ctx tmp;  // only its message field is used; no device state is touched
+  Checked ck;
+  const int rc = validate_linear(&tmp, d, &ck);
   if (msg && cap > 0) std::snprintf(msg, (size_t)cap, "%s", rc ? tmp.err.c_str() : "");
   return rc;
 }

@@ -5,20 +5,24 @@ app/gpu/device.js); see ops.py. Importing this package loads libsupra_attn.so an
 ImportError if it has not been built; there is no fallback implementation.
 """
 
-from ._lib import LIB_PATH, SupraAttnError, SupraAttnValueError, Desc, SIGNATURES, lib
-from .ops import GPU, Tensor, attention, make_desc, position_bias, relative_bucket, default_scale
+from ._lib import LIB_PATH, SupraAttnError, SupraAttnValueError, Desc, LinearDesc, SIGNATURES, lib
+from .ops import (GPU, Tensor, attention, make_desc, linear, make_linear_desc, position_bias, relative_bucket,
+                  default_scale)
 
 __all__ = [
     "LIB_PATH",
     "SupraAttnError",
     "SupraAttnValueError",
     "Desc",
+    "LinearDesc",
     "SIGNATURES",
     "lib",
     "GPU",
     "Tensor",
     "attention",
     "make_desc",
+    "linear",
+    "make_linear_desc",
     "position_bias",
     "relative_bucket",
     "default_scale",

@@ -32,6 +32,18 @@ class Desc(C.Structure):
     ]
 
 
+class LinearDesc(C.Structure):
+    """supra_attn_linear_desc (include/supra_attn.h)."""
+
+    _fields_ = [
+        ("x", C.c_void_p), ("w", C.c_void_p), ("bias", C.c_void_p), ("y", C.c_void_p),
+        ("x_size", C.c_int64), ("w_size", C.c_int64), ("bias_size", C.c_int64), ("y_size", C.c_int64),
+        ("ldx", C.c_int64), ("ldw", C.c_int64), ("ldy", C.c_int64), ("x_off", C.c_int64), ("y_off", C.c_int64),
+        ("M", C.c_int32), ("N", C.c_int32), ("K", C.c_int32),
+        ("variant", C.c_int32), ("flags", C.c_uint32), ("reserved", C.c_uint32),
+    ]
+
+
 class ProfileEntry(C.Structure):
     _fields_ = [("name", C.c_char * 48), ("launches", C.c_int64), ("ms", C.c_double), ("flops", C.c_double),
                 ("bytes", C.c_double)]
@@ -64,6 +76,8 @@ SIGNATURES = [
     ("supra_attn_profile_reset", C.c_int, [C.c_void_p]),
     ("supra_attn_launch_count", C.c_int, [C.c_void_p, C.POINTER(C.c_int64)]),
     ("supra_attn_attention_noalloc", C.c_int, [C.POINTER(Desc), C.c_void_p, C.c_char_p, C.c_int32]),
+    ("supra_attn_enqueue_linear", C.c_int, [C.c_void_p, C.POINTER(LinearDesc)]),
+    ("supra_attn_check_linear_desc", C.c_int, [C.POINTER(LinearDesc), C.c_char_p, C.c_int32]),
 ]
 
 

@@ -5,6 +5,9 @@
   attention()       -- ops.attention (app/gpu/ops.js:103-149): same keyword arguments, same
                        defaults (scale = 1/sqrt(D), out allocated as [Lq, H*D] when omitted),
                        a synchronous ValueError where the reference throws.
+  linear()          -- ops.linear (app/gpu/ops.js:35-43): y = x @ W^T (+ bias), the projections
+                       beside the attention (the cross-attention K/V preparation,
+                       app/models/dit.js:137-144).
   relative_bucket() -- relativeBucket (app/models/t5.js:14-23).
   position_bias()   -- T5Encoder.positionBias + upload (app/models/t5.js:55-65,73), on the device.
 
@@ -21,7 +24,7 @@ import math
 import numpy as np
 
 from . import _lib
-from ._lib import Desc, ProfileEntry, check, lib
+from ._lib import Desc, LinearDesc, ProfileEntry, check, lib
 
 VARIANTS = {"fp32": _lib.FP32, "tf32": _lib.TF32}
 
@@ -254,6 +257,49 @@ def attention(gpu: GPU, *, q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0,
             o.release()
         raise
     return o
+
+
+def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
+                     variant="fp32") -> LinearDesc:
+    """Packs one linear call y = x W^T (+ bias) into a supra_attn_linear_desc (validated by the library)."""
+    d = LinearDesc()
+    d.x, d.x_size = _as_buf(x)
+    d.w, d.w_size = _as_buf(w)
+    d.y, d.y_size = _as_buf(y)
+    if bias is not None:
+        d.bias, d.bias_size = _as_buf(bias)
+    d.M, d.N, d.K = int(M), int(N), int(K)
+    d.ldx = int(K if ldx is None else ldx)
+    d.ldw = int(K if ldw is None else ldw)
+    d.ldy = int(N if ldy is None else ldy)
+    d.x_off, d.y_off = int(xOff), int(yOff)
+    if variant not in VARIANTS:
+        raise ValueError(f"variant must be one of {sorted(VARIANTS)}")
+    d.variant = VARIANTS[variant]
+    return d
+
+
+def linear(gpu: GPU, x, w, *, N, K, M=None, bias=None, out=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
+           variant="fp32"):
+    """ops.linear (app/gpu/ops.js:35-43): y = x @ W^T (+ bias), recorded; returns y.
+
+    x: M rows of K floats (row stride ldx, first row at xOff; M defaults to x.size / K as in the
+    reference); w: [N, K] row-major weights; bias: N floats. y is allocated as gpu.empty([M, N])
+    when `out` is omitted. fp32 FFMA; runs at the next flush/sync/read.
+    """
+    if M is None:  # the reference's x.size / W.K (app/gpu/ops.js:36), from the logical size
+        n = x.size if isinstance(x, Tensor) else _as_buf(x)[1]
+        M = (n - int(xOff)) // int(K)
+    y = out if out is not None else gpu.empty([int(M), int(N)])
+    try:
+        d = make_linear_desc(x=x, w=w, y=y, M=M, N=N, K=K, bias=bias, ldx=ldx, ldw=ldw, ldy=ldy, xOff=xOff,
+                             yOff=yOff, variant=variant)
+        check(lib.supra_attn_enqueue_linear(gpu.ctx, C.byref(d)), gpu.ctx)
+    except Exception:
+        if out is None:
+            y.release()
+        raise
+    return y
 
 
 def relative_bucket(rel: int, buckets: int = 32, max_distance: int = 128) -> int:

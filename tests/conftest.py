@@ -43,6 +43,28 @@ def golden():
     return Golden()
 
 
+def ctxprep_inputs():
+    """Inputs of the golden 'ctxprep' case (cross-attention K/V preparation), regenerated from
+    its seed in tests/golden/make_golden.py's order: ctx, ctx_proj weight and bias, then each
+    block's kv weight and bias, then the cross-attention query."""
+    import torch
+
+    g = torch.Generator().manual_seed(55)
+    L, nblk = 37, 3
+    ctx = torch.randn(L, 768, generator=g)
+    wp = torch.randn(576, 768, generator=g) / 768 ** 0.5
+    bp = torch.randn(576, generator=g) * 0.1
+    wkv, bkv = [], []
+    for _ in range(nblk):
+        wkv.append(torch.randn(1152, 576, generator=g) / 576 ** 0.5)
+        bkv.append(torch.randn(1152, generator=g) * 0.1)
+    qx = torch.randn(1, 48, 576, generator=g)
+    flat = torch.cat([ctx.reshape(-1), wp.reshape(-1), bp.reshape(-1)] +
+                     [t.reshape(-1) for pair in zip(wkv, bkv) for t in pair])
+    return {"L": L, "ctx": ctx.numpy(), "wp": wp.numpy(), "bp": bp.numpy(), "wkv": [w.numpy() for w in wkv],
+            "bkv": [b.numpy() for b in bkv], "q": qx[0].numpy(), "flat": flat.numpy(), "q_flat": qx.reshape(-1).numpy()}
+
+
 @pytest.fixture(scope="session")
 def gpu():
     """One libsupra_attn context on cuda:0, running on torch's current stream."""

@@ -18,6 +18,8 @@ Sources of truth:
     the [H, L, L] bias. transformers is not vendored by the reference (version recorded below).
   - Bucket vectors come from T5Attention._relative_position_bucket, which
     app/models/t5.js:13-23 restates.
+  - The cross-attention K/V preparation (ctx_proj, then each block's cross_attn.kv) comes from
+    the reference's `linear` (tools/reference.py:67-68), called as dit_forward calls it.
 
 Output format is the reference's dump format (tools/reference.py:41-54): one raw
 little-endian float32 file per tensor plus index.json with shapes and metadata.
@@ -162,6 +164,29 @@ def main():
         d(f"{name}_v", vv)
         d(f"{name}_out", out)
         meta["cases"][name] = {"T": T, "H": 1, "D": 512, "seed": 44}
+
+    # ---- cross-attention K/V preparation (app/models/dit.js:137-144): ctx_proj, then each block's
+    # cross_attn.kv, through the reference's own `linear` (tools/reference.py:67-68) as its
+    # dit_forward calls it (tools/reference.py:92,99); then one cross attention on block 1's K/V.
+    # Inputs are regenerated from the seed in the order below (their SHA-256 is recorded).
+    g = torch.Generator().manual_seed(55)
+    L, nblk = 37, 3
+    ctx = torch.randn(L, 768, generator=g)
+    sd = {"ctx_proj.weight": torch.randn(576, 768, generator=g) / 768 ** 0.5,
+          "ctx_proj.bias": torch.randn(576, generator=g) * 0.1}
+    for i in range(nblk):
+        sd[f"blocks.{i}.cross_attn.kv.weight"] = torch.randn(1152, 576, generator=g) / 576 ** 0.5
+        sd[f"blocks.{i}.cross_attn.kv.bias"] = torch.randn(1152, generator=g) * 0.1
+    qx = torch.randn(1, 48, 576, generator=g)
+    p = reference.linear(sd, "ctx_proj", ctx)
+    d("ctxprep_p", p, input_sha256=sha(torch.cat([ctx.reshape(-1)] + [t.reshape(-1) for t in sd.values()])))
+    for i in range(nblk):
+        d(f"ctxprep_kv{i}", reference.linear(sd, f"blocks.{i}.cross_attn.kv", p))
+    kv1 = reference.linear(sd, "blocks.1.cross_attn.kv", p).view(1, L, 2, 576)
+    d("ctxprep_cross_out", reference.attention(qx, kv1[:, :, 0], kv1[:, :, 1], 9)[0], q_sha256=sha(qx))
+    meta["cases"]["ctxprep"] = {"L": L, "blocks": nblk, "seed": 55, "N": 48,
+                                "inputs": "torch.Generator().manual_seed(55): ctx [37,768]; ctx_proj W [576,768]/sqrt(768), "
+                                          "b [576]*0.1; per block kv W [1152,576]/sqrt(576), b [1152]*0.1; q [1,48,576]"}
 
     d.save(**meta)
     print("wrote", args.out, len(d.index), "tensors")

@@ -179,3 +179,48 @@ def test_create_without_gpu_fails_cleanly():
     assert st != _lib.OK and not ctx.value
     with pytest.raises(supra_attn.SupraAttnError):
         supra_attn.GPU(0)
+
+
+# ---- linear descriptors (pure host) ----------------------------------------------------------
+def linear_desc(**kw):
+    """ctx_proj of one prompt (app/models/dit.js:139): x [37, 768], W [576, 768], bias [576]."""
+    d = _lib.LinearDesc()
+    d.x, d.w, d.bias, d.y = BASE_Q, BASE_B, BASE_B + 4 * 576 * 768, BASE_O
+    d.x_size, d.w_size, d.bias_size, d.y_size = 37 * 768, 576 * 768, 576, 37 * 576
+    d.ldx, d.ldw, d.ldy = 768, 768, 576
+    d.M, d.N, d.K = 37, 576, 768
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def check_linear(d):
+    msg = C.create_string_buffer(512)
+    st = _lib.lib.supra_attn_check_linear_desc(C.byref(d), msg, 512)
+    return st, msg.value.decode()
+
+
+def test_linear_descriptors():
+    assert check_linear(linear_desc()) == (_lib.OK, "")
+    assert check_linear(linear_desc(bias=0, bias_size=0))[0] == _lib.OK
+    assert check_linear(linear_desc(M=0))[0] == _lib.OK  # nothing to do
+    cases = [
+        (dict(N=0), "N="),
+        (dict(K=0), "K="),
+        (dict(M=-1), "M="),
+        (dict(ldx=700), "ldx >= K"),
+        (dict(ldy=500), "ldy >= N"),
+        (dict(x_size=37 * 768 - 1), "x out of bounds"),
+        (dict(w_size=576 * 768 - 1), "w out of bounds"),
+        (dict(bias_size=575), "bias"),
+        (dict(y_size=37 * 576 - 1), "y out of bounds"),
+        (dict(x_off=-4), "offset"),
+        (dict(flags=1), "flags"),
+        (dict(variant=9), "variant"),
+        (dict(w=0), "non-NULL"),
+        (dict(x=BASE_Q + 2), "aligned"),
+        (dict(y=BASE_Q, y_size=37 * 768), "overlaps"),
+    ]
+    for kw, needle in cases:
+        st, msg = check_linear(linear_desc(**kw))
+        assert st == _lib.EINVAL and needle in msg, (kw, msg)

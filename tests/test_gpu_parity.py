@@ -323,6 +323,7 @@ def test_determinism_and_profile(gpu):
     p = rand_problem(rng, 256, 256, 9, 64)
     q, k, v = dev(p["q"]), dev(p["k"]), dev(p["v"])
     gpu.profile(True)
+    gpu.profile_reset()
     n0 = gpu.launch_count()
     outs = []
     for _ in range(2):

@@ -117,3 +117,27 @@ def test_sdpa_port_matches_golden(golden):
     v3 = qkv.view(B, N, 3, 576)
     out = oracle.sdpa_port(v3[:, :, 0], v3[:, :, 1], v3[:, :, 2], 9)
     assert oracle.max_rel(out.numpy(), golden("dit_self_out")) < 1e-6
+
+
+def test_context_preparation(golden):
+    """oracle.prepare_context / oracle.linear against the reference's own linear (ctx_proj, then
+    each block's cross_attn.kv) and the cross attention on block 1's K/V."""
+    from conftest import ctxprep_inputs
+
+    x = ctxprep_inputs()
+    sha = lambda a: hashlib.sha256(np.asarray(a, dtype="<f4").tobytes()).hexdigest()
+    assert sha(x["flat"]) == golden.meta("ctxprep_p")["input_sha256"]
+    assert sha(x["q_flat"]) == golden.meta("ctxprep_cross_out")["q_sha256"]
+    p, kvs = oracle.prepare_context(x["ctx"], x["wp"], x["bp"], x["wkv"], x["bkv"])
+    assert oracle.max_rel(p, golden("ctxprep_p")) <= TOL
+    for i, kv in enumerate(kvs):
+        assert oracle.max_rel(kv, golden(f"ctxprep_kv{i}")) <= TOL
+    # the flat-array operator with offsets and strides gives the same
+    L = x["L"]
+    y = oracle.linear(np.concatenate([np.zeros(8, np.float32), x["ctx"].reshape(-1)]), x["wp"], L, 576, 768,
+                      bias=x["bp"], x_off=8, ldy=600)
+    yy = y[np.arange(L)[:, None] * 600 + np.arange(576)[None, :]]
+    assert oracle.max_rel(yy, golden("ctxprep_p")) <= TOL
+    kv1 = kvs[1]
+    out = oracle.attention_heads(x["q"], kv1[:, :576], kv1[:, 576:], 9)
+    assert oracle.max_rel(out, golden("ctxprep_cross_out")) <= TOL
