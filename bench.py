@@ -372,6 +372,61 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
         run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512)
         del qv, kvv, vv, ov
 
+    # VAE mid-block attention, whole block fused (app/models/vae.js:77-94), 8 images of 32x32:
+    # GroupNorm folded into one stacked q/k/v product, attention reading q/k/v in place, residual
+    # folded into the output projection.
+    nimg, hw, C = 8, 1024, 512
+    xv = torch.randn(nimg * hw * C, device=dev, generator=g)
+    gam = 1 + 0.1 * torch.randn(C, device=dev, generator=g)
+    bet = 0.1 * torch.randn(C, device=dev, generator=g)
+    wqkv = torch.randn(3 * C * C, device=dev, generator=g) * C ** -0.5
+    bqkv = 0.1 * torch.randn(3 * C, device=dev, generator=g)
+    wo = torch.randn(C * C, device=dev, generator=g) * C ** -0.5
+    bo = 0.1 * torch.randn(C, device=dev, generator=g)
+    qkv_v = torch.empty(nimg * hw * 3 * C, device=dev)
+    a_v = torch.empty(nimg * hw * C, device=dev)
+    y_v = torch.empty(nimg * hw * C, device=dev)
+    dq = supra_attn.make_linear_desc(x=xv, w=wqkv, bias=bqkv, y=qkv_v, M=nimg * hw, N=3 * C, K=C,
+                                     groupnorm=dict(gamma=gam, beta=bet, groups=32, rows_per_image=hw))
+    do = supra_attn.make_linear_desc(x=a_v, w=wo, bias=bo, y=y_v, M=nimg * hw, N=C, K=C, resid=xv)
+    da = (supra_attn.Desc * nimg)()
+    for i in range(nimg):
+        r = i * hw
+        da[i] = supra_attn.make_desc(q=qkv_v, k=qkv_v, v=qkv_v, out=a_v, Lq=hw, Lk=hw, H=1, D=C, ldq=3 * C,
+                                     ldk=3 * C, ldv=3 * C, qOff=r * 3 * C, kOff=r * 3 * C + C, vOff=r * 3 * C + 2 * C,
+                                     oOff=r * C)
+    enq = supra_attn.lib.supra_attn_enqueue_linear
+
+    def vae_block():
+        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(dq)), gpu.ctx)
+        gpu.enqueue_batch(da)  # reads qkv: flushes the projection first
+        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(do)), gpu.ctx)
+        gpu.flush()
+
+    vae_block()
+    gpu.sync()
+    gpu.profile(True)
+    gpu.profile_reset()
+    times = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        vae_block()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    prof = gpu.profile_report()
+    gpu.profile(False)
+    ms = statistics.median(times)
+    flops = nimg * (2.0 * hw * C * 3 * C + 4.0 * hw * hw * C + 2.0 * hw * C * C)
+    out["vae_block_8"] = {"fp32": {"ms": ms, "image_per_s": nimg / (ms / 1e3),
+                                   "tflops": flops / (ms / 1e3) / 1e12,
+                                   "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                                   "kernels": sorted({r["name"] for r in prof})}}
+    del xv, qkv_v, a_v, y_v
+
     # Cross-attention K/V preparation for configs[4]'s 2048 sequences (app/models/dit.js:137-144):
     # ctx_proj over every sequence's T5 rows at once, then the 14 blocks' kv projections as one
     # product with the stacked [14*1152, 576] weights (the cross attention reads its K/V in place).

@@ -156,12 +156,29 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  * tracking, one grouped launch per flush). x: M rows of K floats, row stride ldx, first row at
  * x_off; w: [N, K] row-major with row stride ldw >= K (the reference's weight layout, x @ W^T);
  * bias: N floats or NULL; y: M rows of N floats, row stride ldy >= N, first row at y_off. All
- * counts in floats. Computed in fp32 with FFMA (a TF32 request runs the same kernel). The
- * reference's optional activation, residual and gate (app/gpu/ops.js:33-43) are not part of
- * this entry point; flags and reserved must be 0.
+ * counts in floats. Computed in fp32 with FFMA (a TF32 request runs the same kernel).
+ * Two optional fusions (the VAE mid-block attention, app/models/vae.js:77-94):
+ *   - gn != NULL: x is GroupNorm-ed on the way in (ops.groupnorm, app/gpu/ops.js:82-92,
+ *     app/gpu/kernels.js:117-162): x rows form images of gn->rows_per_image rows; per image and
+ *     group of K / gn->groups channels the library computes (mean, 1/sqrt(var + eps)) in an extra
+ *     launch, and the product uses (x - mean) * rstd * gamma[k] + beta[k] (then SiLU if
+ *     gn->silu) in place of x. Needs x_off == 0 and ldx == K.
+ *   - resid != NULL: y = x W^T + bias + resid, resid rows of stride ldr at r_off (the residual
+ *     add of app/models/vae.js:91; resid may not overlap y).
+ * The reference's gated residual and activations on y (app/gpu/ops.js:33-43) are not covered;
+ * flags and reserved must be 0.
  * Cross-attention K/V preparation (app/models/dit.js:137-144) is two calls: ctx_proj, then ONE
  * product with the 14 blocks' kv weights stacked [14*1152, 576]; block b's cross attention then
  * reads K at column 1152*b and V at 1152*b + 576 of rows of stride 14*1152, without a copy. */
+typedef struct supra_attn_groupnorm {
+  const float* gamma; /* K floats */
+  const float* beta;  /* K floats */
+  int32_t groups;     /* K % groups == 0 */
+  int32_t rows_per_image; /* M % rows_per_image == 0 */
+  float eps;          /* the reference uses 1e-6 */
+  int32_t silu;       /* nonzero: SiLU after the affine (ops.groupnorm's silu flag) */
+} supra_attn_groupnorm;
+
 typedef struct supra_attn_linear_desc {
   const float* x;
   const float* w;
@@ -174,6 +191,9 @@ typedef struct supra_attn_linear_desc {
   int32_t variant;
   uint32_t flags;
   uint32_t reserved;
+  const supra_attn_groupnorm* gn; /* NULL, or GroupNorm x on the way in (copied at enqueue) */
+  const float* resid;             /* NULL, or y += resid (rows of stride ldr at r_off) */
+  int64_t resid_size, ldr, r_off;
 } supra_attn_linear_desc;
 SUPRA_ATTN_API int supra_attn_enqueue_linear(supra_attn_ctx* ctx, const supra_attn_linear_desc* desc);
 /* Validates a linear descriptor as supra_attn_enqueue_linear does (pure host function). */

@@ -8,6 +8,9 @@ TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): never imported by the product
   prepare_context  -- DiT.prepareContext (app/models/dit.js:137-144): p = ctx_proj(ctx), then
                       each block's kv projection of p ([L, 1152]: K at columns 0..575, V at
                       576..1151), as tools/reference.py:92,99 computes them.
+  groupnorm        -- ops.groupnorm (app/gpu/ops.js:82-92, app/gpu/kernels.js:117-162).
+  vae_attention_block -- VAE.attention (app/models/vae.js:77-94): GroupNorm, q/k/v, attention,
+                      output projection, residual.
 """
 
 from __future__ import annotations
@@ -43,3 +46,34 @@ def prepare_context(ctx, w_proj, b_proj, w_kv, b_kv):
     kvs = [(p @ np.asarray(w, dtype=np.float64).T + np.asarray(b, dtype=np.float64)[None, :]).astype(np.float32)
            for w, b in zip(w_kv, b_kv)]
     return p.astype(np.float32), kvs
+
+
+def groupnorm(x, gamma, beta, groups, eps=1e-6, silu=False):
+    """ops.groupnorm (app/gpu/ops.js:82-92; app/gpu/kernels.js:117-162) of one NHWC image
+    x [pixels, C]: per group of C/groups channels the mean, then the variance around it (biased),
+    y = (x - mean) * (var + eps)^-1/2 * gamma[c] + beta[c], then SiLU if asked. float64."""
+    x = np.asarray(x, dtype=np.float64)
+    P, Cn = x.shape
+    cg = Cn // groups
+    xg = x.reshape(P, groups, cg)
+    mean = xg.mean(axis=(0, 2), keepdims=True)
+    var = ((xg - mean) ** 2).mean(axis=(0, 2), keepdims=True)
+    y = ((xg - mean) / np.sqrt(var + eps)).reshape(P, Cn) * np.asarray(gamma, np.float64) + np.asarray(beta, np.float64)
+    if silu:
+        y = y / (1.0 + np.exp(-y))
+    return y
+
+
+def vae_attention_block(x, gn_gamma, gn_beta, wq, bq, wk, bk, wv, bv, wo, bo, groups=32, eps=1e-6):
+    """VAE.attention (app/models/vae.js:77-94) on one image x [hw, C]: GroupNorm (no SiLU), q/k/v
+    projections, single-head attention with scale 1/sqrt(C) (app/gpu/ops.js:109), output
+    projection, residual add. float64 throughout; returns float32 [hw, C]."""
+    x64 = np.asarray(x, dtype=np.float64)
+    n = groupnorm(x64, gn_gamma, gn_beta, groups, eps)
+    f = lambda a, w, b: a @ np.asarray(w, np.float64).T + np.asarray(b, np.float64)
+    q, k, v = f(n, wq, bq), f(n, wk, bk), f(n, wv, bv)
+    s = q @ k.T / np.sqrt(q.shape[1])
+    s -= s.max(axis=1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=1, keepdims=True)
+    return (x64 + f(p @ v, wo, bo)).astype(np.float32)

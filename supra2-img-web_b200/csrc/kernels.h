@@ -139,6 +139,16 @@ struct alignas(16) LinProb {
   int64_t ldx, ldw, ldy;
   int32_t M, N, K;
   int32_t n_tiles;  // column tiles of 128: ceil(N / 128)
+  const float* resid;  // y += resid[row * ldr + col], or nullptr
+  int64_t ldr;
+  // GroupNorm of x on the way in (gn_stats != nullptr): stats[image * groups + g] = (mean, rstd)
+  const float2* gn_stats;
+  const float* gamma;
+  const float* beta;
+  int32_t gn_cg;     // channels per group
+  int32_t gn_rows;   // rows per image
+  int32_t gn_groups;
+  int32_t gn_silu;
 };
 static_assert(sizeof(LinProb) % 16 == 0, "LinProb is packed into the descriptor ring");
 
@@ -151,6 +161,11 @@ struct LinLaunch {
   int32_t* status;
 };
 cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cudaStream_t s);
+// GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
+// group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
+// mean in a second pass (app/gpu/kernels.js:117-139).
+cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
+                            float eps, float2* stats, cudaStream_t s);
 
 // Copies bytes (a multiple of 16, both addresses 16-byte aligned) from src, which may be pinned
 // host memory addressable by the device, to device memory dst (stage.cu).

@@ -9,6 +9,9 @@
 // throughout. Within a problem the row tiles are outer and the column tiles inner, so CTAs that
 // run together share x rows and sweep W, which stays in L2 (the 14 stacked kv weights are
 // 37 MB).
+// Two optional fusions for the VAE mid-block attention (app/models/vae.js:77-94): GroupNorm of
+// x applied to each staged x tile in shared memory before it is used (statistics from
+// gn_stats_kernel, an earlier launch in the same flush), and a residual added in the epilogue.
 #include "common.cuh"
 
 namespace supra {
@@ -91,6 +94,25 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
       cp_async_wait<0>();
     }
     __syncthreads();
+    if (P.gn_stats) {
+      // GroupNorm (+ SiLU) of the staged x tile: (x - mean) * rstd * gamma + beta per element of
+      // a valid row and column (padding stays zero); app/gpu/kernels.js:141-162
+      float* a = As[st & 1];
+      const int k0 = st * kBK;
+#pragma unroll
+      for (int it = 0; it < kBM * kBK / kT; ++it) {
+        const int idx = tid + it * kT;
+        const int r = idx >> 4, kk = idx & 15;
+        const int k = k0 + kk;
+        if (r < nr && k < K) {
+          const float2 ms = __ldg(P.gn_stats + (int64_t)((r0 + r) / P.gn_rows) * P.gn_groups + k / P.gn_cg);
+          float v = (a[r * kS + kk] - ms.x) * ms.y * __ldg(P.gamma + k) + __ldg(P.beta + k);
+          if (P.gn_silu) v = v / (1.f + __expf(-v));
+          a[r * kS + kk] = v;
+        }
+      }
+      __syncthreads();
+    }
     const float4* A4 = reinterpret_cast<const float4*>(As[st & 1]) + rg * (kS / 4);
     const float4* B4 = reinterpret_cast<const float4*>(Bs[st & 1]) + cg * (kS / 4);
 #pragma unroll
@@ -122,15 +144,58 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
     const int r = rg + 16 * i;
     if (r >= nr) continue;
     float* yrow = P.y + (int64_t)(r0 + r) * P.ldy + c0;
+    const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = cg + 16 * j;
-      if (c < nc) yrow[c] = acc[i][j] + bias[j];
+      if (c < nc) yrow[c] = acc[i][j] + bias[j] + (rrow ? __ldg(rrow + c) : 0.f);
     }
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// One CTA per (image, group): mean, then the variance around it (two passes for accuracy, as the
+// reference's groupnormStatsShader), over rows_per_image rows x cg channels.
+__global__ void __launch_bounds__(256) gn_stats_kernel(const float* __restrict__ x, int32_t K, int32_t rows,
+                                                       int32_t groups, float eps, float2* __restrict__ stats) {
+  __shared__ float red[8];
+  const int img = blockIdx.x / groups;
+  const int g = blockIdx.x - img * groups;
+  const int cg = K / groups;
+  const int64_t n = (int64_t)rows * cg;
+  const float* base = x + (int64_t)img * rows * K + (int64_t)g * cg;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  auto block_sum = [&](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w];
+    __syncthreads();
+    return t;
+  };
+  float s = 0.f;
+  for (int64_t i = tid; i < n; i += 256) s += __ldg(base + (i / cg) * K + i % cg);
+  const float mean = block_sum(s) / (float)n;
+  float v = 0.f;
+  for (int64_t i = tid; i < n; i += 256) {
+    const float d = __ldg(base + (i / cg) * K + i % cg) - mean;
+    v = fmaf(d, d, v);
+  }
+  const float var = block_sum(v) / (float)n;
+  if (tid == 0) stats[blockIdx.x] = make_float2(mean, rsqrtf(var + eps));
+}
+
 }  // namespace
+
+cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
+                            float eps, float2* stats, cudaStream_t s) {
+  if (images <= 0) return cudaSuccess;
+  gn_stats_kernel<<<images * groups, 256, 0, s>>>(x, K, rows_per_image, groups, eps, stats);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;

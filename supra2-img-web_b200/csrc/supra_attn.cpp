@@ -93,6 +93,7 @@ struct Queued {
   int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TMA tensor maps)
   int32_t t5_buckets, t5_maxd;      // T5 table bias (SUPRA_ATTN_F_T5_TABLE), else 0
   supra::LinProb lin;               // PATH_LINEAR: the linear problem (p unused)
+  float gn_eps;                     // PATH_LINEAR with GroupNorm of x
 };
 
 // A tensor map over a whole operand buffer: [rows, ld] fp32, boxes of box_cols columns x
@@ -163,6 +164,8 @@ struct supra_attn_ctx {
   std::vector<Queued> queue;
   IntervalSet qreads, qwrites;
 
+  float2* gn_stats = nullptr;  // GroupNorm statistics of the linear problems of a flush
+  size_t gn_cap = 0;             // in float2
   std::map<size_t, std::vector<void*>> pool_free;
   std::unordered_map<void*, size_t> pool_live;
   std::unordered_set<void*> host_live;
@@ -373,7 +376,7 @@ int collect_profile(supra_attn_ctx* c) {
 // ---- validation --------------------------------------------------------------------------------
 struct Checked {
   Queued q;
-  ByteRange reads[4];
+  ByteRange reads[8];
   int nreads = 0;
   ByteRange write;
   bool empty = false;  // Lq == 0: nothing to do
@@ -570,6 +573,30 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
                    (long long)(y_last + 1), (long long)d->y_size);
   const int64_t tiles = ((int64_t)d->M + 127) / 128 * (((int64_t)d->N + 127) / 128);
   if (tiles > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "linear: too many 128x128 tiles");
+  const supra_attn_groupnorm* gn = d->gn;
+  if (gn) {
+    if (!gn->gamma || !gn->beta || (reinterpret_cast<uintptr_t>(gn->gamma) & 3u) ||
+        (reinterpret_cast<uintptr_t>(gn->beta) & 3u))
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: groupnorm gamma and beta must be non-NULL float arrays");
+    if (gn->groups < 1 || d->K % gn->groups)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: groupnorm groups=%d must divide K=%d", gn->groups, d->K);
+    if (gn->rows_per_image < 1 || (d->M % gn->rows_per_image))
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: groupnorm rows_per_image=%d must divide M=%d", gn->rows_per_image,
+                     d->M);
+    if (!std::isfinite(gn->eps) || gn->eps < 0.f) return set_err(c, SUPRA_ATTN_EINVAL, "linear: groupnorm eps");
+    if (d->x_off != 0 || d->ldx != d->K)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: groupnorm needs contiguous x rows (x_off == 0, ldx == K)");
+    if ((int64_t)(d->M / gn->rows_per_image) * gn->groups > INT32_MAX)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: too many groupnorm groups");
+  }
+  if (d->resid) {
+    if (reinterpret_cast<uintptr_t>(d->resid) & 3u)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: resid must be a 4-byte aligned float array");
+    if (d->ldr < d->N || d->ldr > lim || d->r_off < 0 || d->r_off > lim)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: resid needs ldr >= N and a non-negative r_off");
+    if (!out->empty && d->r_off + (int64_t)(d->M - 1) * d->ldr + d->N - 1 >= d->resid_size)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: resid out of bounds: resid_size=%lld", (long long)d->resid_size);
+  }
   auto rng = [](const float* base, int64_t first, int64_t lastidx) {
     ByteRange r;
     r.b = reinterpret_cast<uintptr_t>(base + first);
@@ -581,6 +608,11 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
     out->reads[out->nreads++] = rng(d->x, d->x_off, x_last);
     out->reads[out->nreads++] = rng(d->w, 0, w_last);
     if (d->bias) out->reads[out->nreads++] = rng(d->bias, 0, d->N - 1);
+    if (gn) {
+      out->reads[out->nreads++] = rng(gn->gamma, 0, d->K - 1);
+      out->reads[out->nreads++] = rng(gn->beta, 0, d->K - 1);
+    }
+    if (d->resid) out->reads[out->nreads++] = rng(d->resid, d->r_off, d->r_off + (int64_t)(d->M - 1) * d->ldr + d->N - 1);
     out->write = rng(d->y, d->y_off, y_last);
     for (int i = 0; i < out->nreads; ++i)
       if (out->reads[i].b < out->write.e && out->write.b < out->reads[i].e)
@@ -600,6 +632,18 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   q.lin.N = d->N;
   q.lin.K = d->K;
   q.lin.n_tiles = (d->N + 127) / 128;
+  q.lin.resid = d->resid ? d->resid + d->r_off : nullptr;
+  q.lin.ldr = d->resid ? d->ldr : 0;
+  q.gn_eps = 0.f;
+  if (gn) {
+    q.lin.gamma = gn->gamma;
+    q.lin.beta = gn->beta;
+    q.lin.gn_groups = gn->groups;
+    q.lin.gn_cg = d->K / gn->groups;
+    q.lin.gn_rows = gn->rows_per_image;
+    q.lin.gn_silu = gn->silu ? 1 : 0;
+    q.gn_eps = gn->eps;
+  }
   q.path = PATH_LINEAR;
   q.cfg = 0;
   q.bias = d->bias != nullptr;
@@ -608,7 +652,8 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   q.t5_buckets = q.t5_maxd = 0;
   q.rows_q = q.rows_k = q.rows_v = 0;
   q.flops = 2.0 * d->M * (double)d->N * d->K;
-  q.bytes = 4.0 * ((double)d->M * d->K + (double)d->N * d->K + (double)d->M * d->N + (d->bias ? d->N : 0));
+  q.bytes = 4.0 * ((double)d->M * d->K + (double)d->N * d->K + (double)d->M * d->N + (d->bias ? d->N : 0) +
+                   (d->resid ? (double)d->M * d->N : 0.0) + (gn ? 2.0 * d->K : 0.0));
   return SUPRA_ATTN_OK;
 }
 
@@ -990,8 +1035,40 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   char *h = nullptr, *dv = nullptr;
   int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
   if (rc) return rc;
+  // GroupNorm statistics of the problems that normalise x, in a context buffer, one launch each
+  size_t nstats = 0;
+  for (int i = 0; i < n; ++i)
+    if (g[i]->lin.gamma) nstats += (size_t)(g[i]->lin.M / g[i]->lin.gn_rows) * g[i]->lin.gn_groups;
+  if (nstats > c->gn_cap) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return cuda_err(c, e, "groupnorm stats: stream sync");
+    if (c->gn_stats) cudaFree(c->gn_stats);
+    c->gn_stats = nullptr;
+    c->gn_cap = 0;
+    if (cudaMalloc(&c->gn_stats, nstats * sizeof(float2)) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(c, SUPRA_ATTN_ENOMEM, "groupnorm stats: cudaMalloc failed");
+    }
+    c->gn_cap = nstats;
+  }
   supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(h);
-  for (int i = 0; i < n; ++i) hp[i] = g[i]->lin;
+  size_t at = 0;
+  for (int i = 0; i < n; ++i) {
+    hp[i] = g[i]->lin;
+    if (hp[i].gamma) {
+      const int32_t images = hp[i].M / hp[i].gn_rows;
+      hp[i].gn_stats = c->gn_stats + at;
+      cudaError_t e;
+      {
+        ProfScope ps(c, "groupnorm_stats", 0.0, 4.0 * (double)hp[i].M * hp[i].K);
+        e = supra::launch_gn_stats(hp[i].x, hp[i].K, hp[i].gn_rows, images, hp[i].gn_groups, g[i]->gn_eps,
+                                   c->gn_stats + at, c->stream);
+      }
+      if (e != cudaSuccess) return cuda_err(c, e, "groupnorm_stats");
+      c->launches += 1;
+      at += (size_t)images * hp[i].gn_groups;
+    }
+  }
   std::memcpy(h + pbytes, begin.data(), bbytes);
   rc = ring_commit(c, h, dv, pbytes + bbytes);
   if (rc) return rc;
@@ -1151,6 +1228,7 @@ int supra_attn_destroy(supra_attn_ctx* c) {
   for (auto& kv : c->pool_live) cudaFree(kv.first);
   for (void* p : c->host_live) cudaFreeHost(p);
   if (c->scratch) cudaFree(c->scratch);
+  if (c->gn_stats) cudaFree(c->gn_stats);
   if (c->ring_h) cudaFreeHost(c->ring_h);
   if (c->ring_d) cudaFree(c->ring_d);
   for (int i = 0; i < 2; ++i)

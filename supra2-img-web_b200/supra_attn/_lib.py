@@ -32,6 +32,13 @@ class Desc(C.Structure):
     ]
 
 
+class GroupNorm(C.Structure):
+    """supra_attn_groupnorm (include/supra_attn.h)."""
+
+    _fields_ = [("gamma", C.c_void_p), ("beta", C.c_void_p), ("groups", C.c_int32), ("rows_per_image", C.c_int32),
+                ("eps", C.c_float), ("silu", C.c_int32)]
+
+
 class LinearDesc(C.Structure):
     """supra_attn_linear_desc (include/supra_attn.h)."""
 
@@ -41,6 +48,8 @@ class LinearDesc(C.Structure):
         ("ldx", C.c_int64), ("ldw", C.c_int64), ("ldy", C.c_int64), ("x_off", C.c_int64), ("y_off", C.c_int64),
         ("M", C.c_int32), ("N", C.c_int32), ("K", C.c_int32),
         ("variant", C.c_int32), ("flags", C.c_uint32), ("reserved", C.c_uint32),
+        ("gn", C.POINTER(GroupNorm)), ("resid", C.c_void_p), ("resid_size", C.c_int64), ("ldr", C.c_int64),
+        ("r_off", C.c_int64),
     ]
 
 

@@ -24,7 +24,7 @@ import math
 import numpy as np
 
 from . import _lib
-from ._lib import Desc, LinearDesc, ProfileEntry, check, lib
+from ._lib import Desc, GroupNorm, LinearDesc, ProfileEntry, check, lib
 
 VARIANTS = {"fp32": _lib.FP32, "tf32": _lib.TF32}
 
@@ -260,9 +260,25 @@ def attention(gpu: GPU, *, q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0,
 
 
 def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
-                     variant="fp32") -> LinearDesc:
-    """Packs one linear call y = x W^T (+ bias) into a supra_attn_linear_desc (validated by the library)."""
+                     groupnorm=None, resid=None, ldr=None, rOff=0, variant="fp32") -> LinearDesc:
+    """Packs one linear call y = x W^T (+ bias) (+ resid) into a supra_attn_linear_desc (validated by
+    the library). groupnorm: dict(gamma, beta, groups, rows_per_image, eps=1e-6, silu=False) to
+    GroupNorm x on the way in. The returned descriptor keeps the GroupNorm block alive."""
     d = LinearDesc()
+    if groupnorm is not None:
+        gnb = GroupNorm()
+        gnb.gamma = _as_buf(groupnorm["gamma"])[0]
+        gnb.beta = _as_buf(groupnorm["beta"])[0]
+        gnb.groups = int(groupnorm["groups"])
+        gnb.rows_per_image = int(groupnorm["rows_per_image"])
+        gnb.eps = float(groupnorm.get("eps", 1e-6))
+        gnb.silu = 1 if groupnorm.get("silu", False) else 0
+        d._gn = gnb
+        d.gn = C.pointer(gnb)
+    if resid is not None:
+        d.resid, d.resid_size = _as_buf(resid)
+        d.ldr = int(N if ldr is None else ldr)
+        d.r_off = int(rOff)
     d.x, d.x_size = _as_buf(x)
     d.w, d.w_size = _as_buf(w)
     d.y, d.y_size = _as_buf(y)
@@ -280,12 +296,14 @@ def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=Non
 
 
 def linear(gpu: GPU, x, w, *, N, K, M=None, bias=None, out=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
-           variant="fp32"):
+           groupnorm=None, resid=None, ldr=None, rOff=0, variant="fp32"):
     """ops.linear (app/gpu/ops.js:35-43): y = x @ W^T (+ bias), recorded; returns y.
 
     x: M rows of K floats (row stride ldx, first row at xOff; M defaults to x.size / K as in the
     reference); w: [N, K] row-major weights; bias: N floats. y is allocated as gpu.empty([M, N])
-    when `out` is omitted. fp32 FFMA; runs at the next flush/sync/read.
+    when `out` is omitted. groupnorm (dict, see make_linear_desc) normalises x on the way in
+    (ops.groupnorm, app/gpu/ops.js:82-92); resid is added to y (the residual add of
+    app/models/vae.js:91). fp32 FFMA; runs at the next flush/sync/read.
     """
     if M is None:  # the reference's x.size / W.K (app/gpu/ops.js:36), from the logical size
         n = x.size if isinstance(x, Tensor) else _as_buf(x)[1]
@@ -293,7 +311,7 @@ def linear(gpu: GPU, x, w, *, N, K, M=None, bias=None, out=None, ldx=None, ldw=N
     y = out if out is not None else gpu.empty([int(M), int(N)])
     try:
         d = make_linear_desc(x=x, w=w, y=y, M=M, N=N, K=K, bias=bias, ldx=ldx, ldw=ldw, ldy=ldy, xOff=xOff,
-                             yOff=yOff, variant=variant)
+                             yOff=yOff, groupnorm=groupnorm, resid=resid, ldr=ldr, rOff=rOff, variant=variant)
         check(lib.supra_attn_enqueue_linear(gpu.ctx, C.byref(d)), gpu.ctx)
     except Exception:
         if out is None:

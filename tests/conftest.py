@@ -77,3 +77,20 @@ def gpu():
     g = supra_attn.GPU(0, stream=torch.cuda.current_stream())
     yield g
     g.close()
+
+
+def vae_block_inputs():
+    """Inputs of the golden 'vae_block' case (VAE mid-block attention), regenerated from its seed
+    in tests/golden/make_golden.py's order: x, the norm's weight and bias, then q, k, v, o weights
+    and biases."""
+    import torch
+
+    g = torch.Generator().manual_seed(66)
+    hw, C = 64, 512
+    x = torch.randn(hw, C, generator=g)
+    sd = {"gamma": 1.0 + 0.1 * torch.randn(C, generator=g), "beta": 0.1 * torch.randn(C, generator=g)}
+    for nm in ("q", "k", "v", "o"):
+        sd["w" + nm] = torch.randn(C, C, generator=g) / C ** 0.5
+        sd["b" + nm] = 0.1 * torch.randn(C, generator=g)
+    flat = torch.cat([x.reshape(-1)] + [t.reshape(-1) for t in sd.values()])
+    return {"hw": hw, "C": C, "x": x.numpy(), **{k: v.numpy() for k, v in sd.items()}, "flat": flat.numpy()}

@@ -35,6 +35,7 @@ import sys
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -187,6 +188,27 @@ def main():
     meta["cases"]["ctxprep"] = {"L": L, "blocks": nblk, "seed": 55, "N": 48,
                                 "inputs": "torch.Generator().manual_seed(55): ctx [37,768]; ctx_proj W [576,768]/sqrt(768), "
                                           "b [576]*0.1; per block kv W [1152,576]/sqrt(576), b [1152]*0.1; q [1,48,576]"}
+
+    # ---- VAE mid-block attention (app/models/vae.js:77-94) as diffusers' attention block runs it:
+    # GroupNorm(32, eps 1e-6) over the image, q/k/v linears, single-head attention (the
+    # reference's own oracle, heads=1), output linear, residual add. torch's group_norm stands in
+    # for diffusers (not installed); linears through the reference's `linear`. Inputs regenerated
+    # from the seed in the order below (their SHA-256 recorded); only the output is stored.
+    g = torch.Generator().manual_seed(66)
+    hw, C = 64, 512
+    x = torch.randn(hw, C, generator=g)
+    vsd = {"norm.weight": 1.0 + 0.1 * torch.randn(C, generator=g), "norm.bias": 0.1 * torch.randn(C, generator=g)}
+    for nm in ("q", "k", "v", "o"):
+        vsd[nm + ".weight"] = torch.randn(C, C, generator=g) / C ** 0.5
+        vsd[nm + ".bias"] = 0.1 * torch.randn(C, generator=g)
+    n = F.group_norm(x.T[None], 32, vsd["norm.weight"], vsd["norm.bias"], eps=1e-6)[0].T
+    qv, kv_, vv = (reference.linear(vsd, nm, n) for nm in ("q", "k", "v"))
+    a = reference.attention(qv[None], kv_[None], vv[None], 1)[0]
+    out = x + reference.linear(vsd, "o", a)
+    d("vae_block_out", out, input_sha256=sha(torch.cat([x.reshape(-1)] + [t.reshape(-1) for t in vsd.values()])))
+    meta["cases"]["vae_block"] = {"hw": hw, "C": C, "groups": 32, "eps": 1e-6, "seed": 66,
+                                  "inputs": "torch.Generator().manual_seed(66): x [64,512]; norm weight 1+0.1*randn, "
+                                            "bias 0.1*randn; q,k,v,o: W randn/sqrt(512), b 0.1*randn"}
 
     d.save(**meta)
     print("wrote", args.out, len(d.index), "tensors")

@@ -224,3 +224,24 @@ def test_linear_descriptors():
     for kw, needle in cases:
         st, msg = check_linear(linear_desc(**kw))
         assert st == _lib.EINVAL and needle in msg, (kw, msg)
+
+
+def test_linear_groupnorm_and_residual_descriptors():
+    gn = _lib.GroupNorm()
+    gn.gamma, gn.beta, gn.groups, gn.rows_per_image, gn.eps = BASE_B + 4 * 600000, BASE_B + 4 * 700000, 32, 37, 1e-6
+    assert check_linear(linear_desc(gn=C.pointer(gn)))[0] == _lib.OK
+    for field, value, needle in [("groups", 7, "groups"), ("rows_per_image", 5, "rows_per_image"),
+                                 ("eps", -1.0, "eps"), ("gamma", 0, "gamma")]:
+        bad = _lib.GroupNorm()
+        C.pointer(bad)[0] = gn
+        setattr(bad, field, value)
+        st, msg = check_linear(linear_desc(gn=C.pointer(bad)))
+        assert st == _lib.EINVAL and needle in msg, (field, msg)
+    st, msg = check_linear(linear_desc(gn=C.pointer(gn), x_off=4, x_size=37 * 768 + 4))
+    assert st == _lib.EINVAL and "contiguous" in msg
+    ok = linear_desc(resid=BASE_O + 4 * 10 ** 6, resid_size=37 * 576, ldr=576)
+    assert check_linear(ok)[0] == _lib.OK
+    st, msg = check_linear(linear_desc(resid=BASE_O + 4 * 10 ** 6, resid_size=37 * 576 - 1, ldr=576))
+    assert st == _lib.EINVAL and "resid" in msg
+    st, msg = check_linear(linear_desc(resid=BASE_O, resid_size=37 * 576, ldr=576))
+    assert st == _lib.EINVAL and "overlaps" in msg

@@ -125,3 +125,81 @@ def test_linear_batch_one_launch(gpu):
     for i, (m, n, k) in enumerate(shapes):
         assert_close(gpu.read(outs[i]), oracle.linear(xs[i], ws[i], m, n, k, bias=bs[i]))
         outs[i].release()
+
+
+# ---- VAE mid-block attention, fused (app/models/vae.js:77-94) --------------------------------------
+def vae_block(gpu, x, p, nimg, hw, C, stacked):
+    """GroupNorm folded into the stacked q/k/v product, attention reading q/k/v in place, and the
+    residual folded into the output projection: three launches (plus the statistics)."""
+    import supra_attn
+
+    qkv = supra_attn.linear(gpu, x, stacked["w"], N=3 * C, K=C, bias=stacked["b"],
+                            groupnorm=dict(gamma=p["gamma"], beta=p["beta"], groups=32, rows_per_image=hw))
+    a = gpu.empty([nimg * hw, C])
+    for i in range(nimg):
+        r = i * hw
+        supra_attn.attention(gpu, q=qkv, k=qkv, v=qkv, Lq=hw, Lk=hw, H=1, D=C, ldq=3 * C, ldk=3 * C, ldv=3 * C,
+                             qOff=r * 3 * C, kOff=r * 3 * C + C, vOff=r * 3 * C + 2 * C, oOff=r * C, out=a)
+    out = supra_attn.linear(gpu, a, p["wo"], N=C, K=C, bias=p["bo"], resid=x)
+    return out, (qkv, a)
+
+
+def stack_qkv(x):
+    return {"w": dev(np.concatenate([x["wq"], x["wk"], x["wv"]], 0)), "b": dev(np.concatenate([x["bq"], x["bk"], x["bv"]]))}
+
+
+def test_vae_block_golden(gpu, golden):
+    from conftest import vae_block_inputs
+
+    x = vae_block_inputs()
+    p = {k: dev(x[k]) for k in ("gamma", "beta", "wo", "bo")}
+    xd = dev(x["x"])
+    out, tmp = vae_block(gpu, xd, p, 1, x["hw"], x["C"], stack_qkv(x))
+    assert_close(gpu.read(out), golden("vae_block_out"))
+    for t in (out,) + tmp:
+        t.release()
+
+
+def test_vae_block_full_size_batch(gpu):
+    """Two 32x32 images (1024 tokens x 512 channels) in one flush: per-image GroupNorm statistics,
+    against the float64 oracle."""
+    rng = np.random.default_rng(77)
+    hw, C, nimg = 1024, 512, 2
+    x = rng.standard_normal((nimg * hw, C)).astype(np.float32)
+    prm = {"gamma": (1 + 0.1 * rng.standard_normal(C)).astype(np.float32),
+           "beta": (0.1 * rng.standard_normal(C)).astype(np.float32)}
+    for nm in "qkvo":
+        prm["w" + nm] = (rng.standard_normal((C, C)) / np.sqrt(C)).astype(np.float32)
+        prm["b" + nm] = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    p = {k: dev(prm[k]) for k in ("gamma", "beta", "wo", "bo")}
+    xd = dev(x)
+    out, tmp = vae_block(gpu, xd, p, nimg, hw, C, stack_qkv(prm))
+    got = gpu.read(out).reshape(nimg, hw, C)
+    for i in range(nimg):
+        ref = oracle.vae_attention_block(x[i * hw:(i + 1) * hw], prm["gamma"], prm["beta"], prm["wq"], prm["bq"],
+                                         prm["wk"], prm["bk"], prm["wv"], prm["bv"], prm["wo"], prm["bo"])
+        assert_close(got[i], ref)
+    for t in (out,) + tmp:
+        t.release()
+
+
+def test_linear_groupnorm_silu_and_residual(gpu):
+    """The two fusions on their own, with SiLU, against oracle.groupnorm + oracle.linear."""
+    import supra_attn
+
+    rng = np.random.default_rng(88)
+    M, K, N, rows = 3 * 40, 96, 70, 40
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    gamma, beta = rng.standard_normal(K).astype(np.float32), rng.standard_normal(K).astype(np.float32)
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    r = rng.standard_normal((M, N + 3)).astype(np.float32)
+    xd, gd, bd, wd, rd = dev(x), dev(gamma), dev(beta), dev(w), dev(r)
+    y = supra_attn.linear(gpu, xd, wd, N=N, K=K, resid=rd, ldr=N + 3,
+                          groupnorm=dict(gamma=gd, beta=bd, groups=8, rows_per_image=rows, silu=True))
+    got = gpu.read(y).reshape(M, N)
+    for i in range(M // rows):
+        sl = slice(i * rows, (i + 1) * rows)
+        n = oracle.groupnorm(x[sl], gamma, beta, 8, silu=True).astype(np.float32)
+        ref = oracle.linear(n, w, rows, N, K).reshape(rows, N) + r[sl, :N]
+        assert_close(got[sl], ref)
+    y.release()

@@ -141,3 +141,16 @@ def test_context_preparation(golden):
     kv1 = kvs[1]
     out = oracle.attention_heads(x["q"], kv1[:, :576], kv1[:, 576:], 9)
     assert oracle.max_rel(out, golden("ctxprep_cross_out")) <= TOL
+
+
+def test_vae_attention_block(golden):
+    """oracle.vae_attention_block (GroupNorm, q/k/v, attention, projection, residual) against the
+    reference's linear and attention around torch's group_norm."""
+    from conftest import vae_block_inputs
+
+    x = vae_block_inputs()
+    assert hashlib.sha256(np.asarray(x["flat"], dtype="<f4").tobytes()).hexdigest() == \
+        golden.meta("vae_block_out")["input_sha256"]
+    got = oracle.vae_attention_block(x["x"], x["gamma"], x["beta"], x["wq"], x["bq"], x["wk"], x["bk"], x["wv"],
+                                     x["bv"], x["wo"], x["bo"])
+    assert oracle.max_rel(got, golden("vae_block_out")) <= TOL
