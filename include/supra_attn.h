@@ -163,10 +163,13 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  *     group of K / gn->groups channels the library computes (mean, 1/sqrt(var + eps)) in an extra
  *     launch, and the product uses (x - mean) * rstd * gamma[k] + beta[k] (then SiLU if
  *     gn->silu) in place of x. Needs x_off == 0 and ldx == K.
- *   - resid != NULL: y = x W^T + bias + resid, resid rows of stride ldr at r_off (the residual
- *     add of app/models/vae.js:91; resid may not overlap y).
- * The reference's gated residual and activations on y (app/gpu/ops.js:33-43) are not covered;
- * flags and reserved must be 0.
+ *   - resid != NULL: y = resid + (x W^T + bias), resid rows of stride ldr at r_off (the residual
+ *     add of app/models/vae.js:91). resid may be y itself (same rows: r_off == y_off and
+ *     ldr == ldy), which is the reference's in-place `out: x, resid: true` (app/models/dit.js:
+ *     175,187,193); otherwise it may not overlap y.
+ *   - gate != NULL (needs resid): y = resid + gate[g_off + n] * (x W^T + bias), the gated
+ *     residual of the DiT blocks (app/gpu/gemm.js:10,135, app/models/dit.js:175,193).
+ * Activations on y (app/gpu/ops.js:33-43) are not covered; flags and reserved must be 0.
  * Cross-attention K/V preparation (app/models/dit.js:137-144) is two calls: ctx_proj, then ONE
  * product with the 14 blocks' kv weights stacked [14*1152, 576]; block b's cross attention then
  * reads K at column 1152*b and V at 1152*b + 576 of rows of stride 14*1152, without a copy. */
@@ -192,8 +195,10 @@ typedef struct supra_attn_linear_desc {
   uint32_t flags;
   uint32_t reserved;
   const supra_attn_groupnorm* gn; /* NULL, or GroupNorm x on the way in (copied at enqueue) */
-  const float* resid;             /* NULL, or y += resid (rows of stride ldr at r_off) */
+  const float* resid;             /* NULL, or y = resid + ... (rows of stride ldr at r_off) */
   int64_t resid_size, ldr, r_off;
+  const float* gate;              /* NULL, or the product is scaled by gate[g_off + n] */
+  int64_t gate_size, g_off;
 } supra_attn_linear_desc;
 SUPRA_ATTN_API int supra_attn_enqueue_linear(supra_attn_ctx* ctx, const supra_attn_linear_desc* desc);
 /* Validates a linear descriptor as supra_attn_enqueue_linear does (pure host function). */

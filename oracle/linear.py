@@ -11,6 +11,9 @@ TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): never imported by the product
   groupnorm        -- ops.groupnorm (app/gpu/ops.js:82-92, app/gpu/kernels.js:117-162).
   vae_attention_block -- VAE.attention (app/models/vae.js:77-94): GroupNorm, q/k/v, attention,
                       output projection, residual.
+  gated_residual   -- ops.linear with { out, resid: true, gate, gOff } (app/gpu/gemm.js:10,135):
+                      out = out + gate[gOff + n] * (x W^T + bias), the DiT blocks' projections
+                      (app/models/dit.js:175,187,193; tools/reference.py:98,100,102).
 """
 
 from __future__ import annotations
@@ -77,3 +80,14 @@ def vae_attention_block(x, gn_gamma, gn_beta, wq, bq, wk, bk, wv, bv, wo, bo, gr
     p = np.exp(s)
     p /= p.sum(axis=1, keepdims=True)
     return (x64 + f(p @ v, wo, bo)).astype(np.float32)
+
+
+def gated_residual(out, x, w, M, N, K, bias=None, gate=None, g_off=0):
+    """out [M, N] + gate[g_off + n] * (x [M, K] @ W^T + bias) in float64, returned as float32
+    [M, N]; gate None is the ungated residual (app/gpu/gemm.js:135 stores C[ci] = C[ci] + r)."""
+    y = np.asarray(x, np.float64).reshape(M, K) @ np.asarray(w, np.float64).reshape(N, K).T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64).reshape(-1)[:N][None, :]
+    if gate is not None:
+        y = y * np.asarray(gate, np.float64).reshape(-1)[g_off:g_off + N][None, :]
+    return (np.asarray(out, np.float64).reshape(M, N) + y).astype(np.float32)

@@ -139,8 +139,9 @@ struct alignas(16) LinProb {
   int64_t ldx, ldw, ldy;
   int32_t M, N, K;
   int32_t n_tiles;  // column tiles of 128: ceil(N / 128)
-  const float* resid;  // y += resid[row * ldr + col], or nullptr
+  const float* resid;  // y = resid[row * ldr + col] + ..., or nullptr (may be y itself)
   int64_t ldr;
+  const float* gate;   // the product is scaled by gate[col] (offset applied), or nullptr
   // GroupNorm of x on the way in (gn_stats != nullptr): stats[image * groups + g] = (mean, rstd)
   const float2* gn_stats;
   const float* gamma;

@@ -9,9 +9,10 @@
 // throughout. Within a problem the row tiles are outer and the column tiles inner, so CTAs that
 // run together share x rows and sweep W, which stays in L2 (the 14 stacked kv weights are
 // 37 MB).
-// Two optional fusions for the VAE mid-block attention (app/models/vae.js:77-94): GroupNorm of
-// x applied to each staged x tile in shared memory before it is used (statistics from
-// gn_stats_kernel, an earlier launch in the same flush), and a residual added in the epilogue.
+// Optional fusions: GroupNorm of x applied to each staged x tile in shared memory before it is
+// used (statistics from gn_stats_kernel, an earlier launch in the same flush; the VAE mid-block
+// attention, app/models/vae.js:77-94), and a residual, optionally gated per column, added in the
+// epilogue (app/gpu/gemm.js:10,135; in place for the DiT blocks' projections).
 #include "common.cuh"
 
 namespace supra {
@@ -136,19 +137,27 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
   }
 
   // y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
-  float bias[8];
+  float bias[8], gate[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
+  for (int j = 0; j < 8; ++j) {
+    bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
+    gate[j] = (P.gate && cg + 16 * j < nc) ? __ldg(P.gate + c0 + cg + 16 * j) : 1.f;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int r = rg + 16 * i;
     if (r >= nr) continue;
     float* yrow = P.y + (int64_t)(r0 + r) * P.ldy + c0;
+    // resid may be y itself (in place): each element is read and then written by this thread only
     const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = cg + 16 * j;
-      if (c < nc) yrow[c] = acc[i][j] + bias[j] + (rrow ? __ldg(rrow + c) : 0.f);
+      if (c < nc) {
+        float v = acc[i][j] + bias[j];
+        if (P.gate) v *= gate[j];
+        yrow[c] = rrow ? rrow[c] + v : v;
+      }
     }
   }
 }

@@ -589,6 +589,8 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
     if ((int64_t)(d->M / gn->rows_per_image) * gn->groups > INT32_MAX)
       return set_err(c, SUPRA_ATTN_EINVAL, "linear: too many groupnorm groups");
   }
+  // in place: resid is y itself, element for element (the reference's out: x, resid: true)
+  const bool in_place = d->resid && d->resid == d->y && d->r_off == d->y_off && d->ldr == d->ldy;
   if (d->resid) {
     if (reinterpret_cast<uintptr_t>(d->resid) & 3u)
       return set_err(c, SUPRA_ATTN_EINVAL, "linear: resid must be a 4-byte aligned float array");
@@ -596,6 +598,13 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
       return set_err(c, SUPRA_ATTN_EINVAL, "linear: resid needs ldr >= N and a non-negative r_off");
     if (!out->empty && d->r_off + (int64_t)(d->M - 1) * d->ldr + d->N - 1 >= d->resid_size)
       return set_err(c, SUPRA_ATTN_EINVAL, "linear: resid out of bounds: resid_size=%lld", (long long)d->resid_size);
+  }
+  if (d->gate) {
+    if (!d->resid) return set_err(c, SUPRA_ATTN_EINVAL, "linear: gate needs resid (the gated residual)");
+    if (reinterpret_cast<uintptr_t>(d->gate) & 3u)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: gate must be a 4-byte aligned float array");
+    if (d->g_off < 0 || d->g_off > lim || d->g_off + d->N > d->gate_size)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: gate out of bounds: needs g_off + N <= gate_size");
   }
   auto rng = [](const float* base, int64_t first, int64_t lastidx) {
     ByteRange r;
@@ -612,7 +621,9 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
       out->reads[out->nreads++] = rng(gn->gamma, 0, d->K - 1);
       out->reads[out->nreads++] = rng(gn->beta, 0, d->K - 1);
     }
-    if (d->resid) out->reads[out->nreads++] = rng(d->resid, d->r_off, d->r_off + (int64_t)(d->M - 1) * d->ldr + d->N - 1);
+    if (d->resid && !in_place)
+      out->reads[out->nreads++] = rng(d->resid, d->r_off, d->r_off + (int64_t)(d->M - 1) * d->ldr + d->N - 1);
+    if (d->gate) out->reads[out->nreads++] = rng(d->gate, d->g_off, d->g_off + d->N - 1);
     out->write = rng(d->y, d->y_off, y_last);
     for (int i = 0; i < out->nreads; ++i)
       if (out->reads[i].b < out->write.e && out->write.b < out->reads[i].e)
@@ -634,6 +645,7 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   q.lin.n_tiles = (d->N + 127) / 128;
   q.lin.resid = d->resid ? d->resid + d->r_off : nullptr;
   q.lin.ldr = d->resid ? d->ldr : 0;
+  q.lin.gate = d->gate ? d->gate + d->g_off : nullptr;
   q.gn_eps = 0.f;
   if (gn) {
     q.lin.gamma = gn->gamma;

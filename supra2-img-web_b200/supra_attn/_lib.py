@@ -49,7 +49,7 @@ class LinearDesc(C.Structure):
         ("M", C.c_int32), ("N", C.c_int32), ("K", C.c_int32),
         ("variant", C.c_int32), ("flags", C.c_uint32), ("reserved", C.c_uint32),
         ("gn", C.POINTER(GroupNorm)), ("resid", C.c_void_p), ("resid_size", C.c_int64), ("ldr", C.c_int64),
-        ("r_off", C.c_int64),
+        ("r_off", C.c_int64), ("gate", C.c_void_p), ("gate_size", C.c_int64), ("g_off", C.c_int64),
     ]
 
 

@@ -260,10 +260,13 @@ def attention(gpu: GPU, *, q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0,
 
 
 def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
-                     groupnorm=None, resid=None, ldr=None, rOff=0, variant="fp32") -> LinearDesc:
-    """Packs one linear call y = x W^T (+ bias) (+ resid) into a supra_attn_linear_desc (validated by
-    the library). groupnorm: dict(gamma, beta, groups, rows_per_image, eps=1e-6, silu=False) to
-    GroupNorm x on the way in. The returned descriptor keeps the GroupNorm block alive."""
+                     groupnorm=None, resid=None, ldr=None, rOff=0, gate=None, gOff=0,
+                     variant="fp32") -> LinearDesc:
+    """Packs one linear call y = resid + gate * (x W^T + bias) (resid, gate and bias optional) into
+    a supra_attn_linear_desc (validated by the library). resid=True is the reference's in-place
+    residual: resid is y itself, same rows. groupnorm: dict(gamma, beta, groups, rows_per_image,
+    eps=1e-6, silu=False) to GroupNorm x on the way in. The returned descriptor keeps the GroupNorm
+    block alive."""
     d = LinearDesc()
     if groupnorm is not None:
         gnb = GroupNorm()
@@ -275,10 +278,15 @@ def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=Non
         gnb.silu = 1 if groupnorm.get("silu", False) else 0
         d._gn = gnb
         d.gn = C.pointer(gnb)
-    if resid is not None:
+    if resid is True:  # in place on y (app/gpu/gemm.js:135 reads C[ci] before it writes it)
+        resid, ldr, rOff = y, (N if ldy is None else ldy), yOff
+    if resid is not None and resid is not False:
         d.resid, d.resid_size = _as_buf(resid)
         d.ldr = int(N if ldr is None else ldr)
         d.r_off = int(rOff)
+    if gate is not None:
+        d.gate, d.gate_size = _as_buf(gate)
+        d.g_off = int(gOff)
     d.x, d.x_size = _as_buf(x)
     d.w, d.w_size = _as_buf(w)
     d.y, d.y_size = _as_buf(y)
@@ -296,22 +304,30 @@ def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=Non
 
 
 def linear(gpu: GPU, x, w, *, N, K, M=None, bias=None, out=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
-           groupnorm=None, resid=None, ldr=None, rOff=0, variant="fp32"):
+           groupnorm=None, resid=None, ldr=None, rOff=0, gate=None, gOff=0, variant="fp32"):
     """ops.linear (app/gpu/ops.js:35-43): y = x @ W^T (+ bias), recorded; returns y.
 
     x: M rows of K floats (row stride ldx, first row at xOff; M defaults to x.size / K as in the
     reference); w: [N, K] row-major weights; bias: N floats. y is allocated as gpu.empty([M, N])
     when `out` is omitted. groupnorm (dict, see make_linear_desc) normalises x on the way in
     (ops.groupnorm, app/gpu/ops.js:82-92); resid is added to y (the residual add of
-    app/models/vae.js:91). fp32 FFMA; runs at the next flush/sync/read.
+    app/models/vae.js:91). resid=True with `out` is the reference's in-place residual
+    `{ out: x, resid: true }` (app/models/dit.js:187), and gate/gOff scale the product per output
+    column first, out = out + gate[gOff + n] * (x W^T + bias) (app/gpu/gemm.js:10,135,
+    app/models/dit.js:175,193). fp32 FFMA; runs at the next flush/sync/read.
     """
+    if resid is True and out is None:
+        raise ValueError("resid=True accumulates into out: pass out")
+    if gate is not None and (resid is None or resid is False):
+        raise ValueError("gate needs resid (the gated residual)")
     if M is None:  # the reference's x.size / W.K (app/gpu/ops.js:36), from the logical size
         n = x.size if isinstance(x, Tensor) else _as_buf(x)[1]
         M = (n - int(xOff)) // int(K)
     y = out if out is not None else gpu.empty([int(M), int(N)])
     try:
         d = make_linear_desc(x=x, w=w, y=y, M=M, N=N, K=K, bias=bias, ldx=ldx, ldw=ldw, ldy=ldy, xOff=xOff,
-                             yOff=yOff, groupnorm=groupnorm, resid=resid, ldr=ldr, rOff=rOff, variant=variant)
+                             yOff=yOff, groupnorm=groupnorm, resid=resid, ldr=ldr, rOff=rOff, gate=gate, gOff=gOff,
+                             variant=variant)
         check(lib.supra_attn_enqueue_linear(gpu.ctx, C.byref(d)), gpu.ctx)
     except Exception:
         if out is None:

@@ -65,6 +65,24 @@ def ctxprep_inputs():
             "bkv": [b.numpy() for b in bkv], "q": qx[0].numpy(), "flat": flat.numpy(), "q_flat": qx.reshape(-1).numpy()}
 
 
+def dit_proj_inputs():
+    """Inputs of the golden 'dit_proj' case (the DiT block's projections around its attention),
+    regenerated from its seed in tests/golden/make_golden.py's order."""
+    import torch
+
+    g = torch.Generator().manual_seed(99)
+    B, N, D = 2, 64, 576
+    x0 = torch.randn(B, N, D, generator=g)
+    qkv = torch.randn(B, N, 3 * D, generator=g)
+    mod = 0.5 * torch.randn(6 * D, generator=g)
+    t = [torch.randn(D, D, generator=g) / D ** 0.5, 0.1 * torch.randn(D, generator=g),
+         torch.randn(D, D, generator=g) / D ** 0.5, 0.1 * torch.randn(D, generator=g)]
+    cx = torch.randn(B, N, D, generator=g)
+    flat = torch.cat([x0.reshape(-1), qkv.reshape(-1), mod] + [u.reshape(-1) for u in t] + [cx.reshape(-1)])
+    return {"B": B, "N": N, "D": D, "x0": x0.numpy(), "qkv": qkv.numpy(), "mod": mod.numpy(), "wp": t[0].numpy(),
+            "bp": t[1].numpy(), "wc": t[2].numpy(), "bc": t[3].numpy(), "c": cx.numpy(), "flat": flat.numpy()}
+
+
 @pytest.fixture(scope="session")
 def gpu():
     """One libsupra_attn context on cuda:0, running on torch's current stream."""

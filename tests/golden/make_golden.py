@@ -210,6 +210,30 @@ def main():
                                   "inputs": "torch.Generator().manual_seed(66): x [64,512]; norm weight 1+0.1*randn, "
                                             "bias 0.1*randn; q,k,v,o: W randn/sqrt(512), b 0.1*randn"}
 
+    # ---- DiT block projections around the attention (app/models/dit.js:161-187) as dit_forward
+    # runs them (tools/reference.py:96-100): self attention through the reference's oracle, the
+    # gated output projection x + g1 * proj(a), then the ungated cross projection x + cproj(c).
+    # mod is one step's modulation vector [6*576] shared by the batch (app/models/dit.js:164),
+    # g1 = mod[2*576:3*576]. Inputs regenerated from the seed; only the outputs are stored.
+    g = torch.Generator().manual_seed(99)
+    B, N, D = 2, 64, 576
+    x0 = torch.randn(B, N, D, generator=g)
+    qkv = torch.randn(B, N, 3 * D, generator=g)
+    mod = 0.5 * torch.randn(6 * D, generator=g)
+    psd = {"proj.weight": torch.randn(D, D, generator=g) / D ** 0.5, "proj.bias": 0.1 * torch.randn(D, generator=g),
+           "cproj.weight": torch.randn(D, D, generator=g) / D ** 0.5, "cproj.bias": 0.1 * torch.randn(D, generator=g)}
+    cx = torch.randn(B, N, D, generator=g)
+    v3 = qkv.view(B, N, 3, D)
+    g1 = mod[2 * D:3 * D].expand(B, D)
+    x1 = x0 + g1[:, None] * reference.linear(psd, "proj", reference.attention(v3[:, :, 0], v3[:, :, 1], v3[:, :, 2], 9))
+    x2 = x1 + reference.linear(psd, "cproj", cx)
+    ins = sha(torch.cat([x0.reshape(-1), qkv.reshape(-1), mod] + [t.reshape(-1) for t in psd.values()] + [cx.reshape(-1)]))
+    d("dit_proj_x1", x1, input_sha256=ins)
+    d("dit_proj_x2", x2)
+    meta["cases"]["dit_proj"] = {"B": B, "N": N, "D": D, "seed": 99, "g_off": 2 * D,
+                                 "inputs": "torch.Generator().manual_seed(99): x [2,64,576]; qkv [2,64,1728]; mod 0.5*randn "
+                                           "[3456]; proj, cproj: W randn/sqrt(576), b 0.1*randn; c [2,64,576]"}
+
     d.save(**meta)
     print("wrote", args.out, len(d.index), "tensors")
 

@@ -243,5 +243,30 @@ def test_linear_groupnorm_and_residual_descriptors():
     assert check_linear(ok)[0] == _lib.OK
     st, msg = check_linear(linear_desc(resid=BASE_O + 4 * 10 ** 6, resid_size=37 * 576 - 1, ldr=576))
     assert st == _lib.EINVAL and "resid" in msg
-    st, msg = check_linear(linear_desc(resid=BASE_O, resid_size=37 * 576, ldr=576))
+    # resid == y row for row is the in-place residual (app/models/dit.js:187); any other overlap is not
+    assert check_linear(linear_desc(resid=BASE_O, resid_size=37 * 576, ldr=576))[0] == _lib.OK
+    st, msg = check_linear(linear_desc(resid=BASE_O, resid_size=37 * 576 + 1, ldr=576, r_off=1))
     assert st == _lib.EINVAL and "overlaps" in msg
+    st, msg = check_linear(linear_desc(resid=BASE_O, resid_size=38 * 580, ldr=580, ldy=580, y_size=38 * 580,
+                                       r_off=0, y_off=0))
+    assert st == _lib.OK, msg
+
+
+def test_linear_gate_descriptors():
+    """The gated residual of the DiT blocks (app/gpu/gemm.js:135): gate[g_off + n], needs resid."""
+    gate = BASE_B + 4 * 800000
+    ok = dict(resid=BASE_O, resid_size=37 * 576, ldr=576, gate=gate, gate_size=6 * 576, g_off=2 * 576)
+    assert check_linear(linear_desc(**ok))[0] == _lib.OK
+    for kw, needle in [(dict(resid=0, resid_size=0), "needs resid"), (dict(g_off=5 * 576 + 1), "gate out of bounds"),
+                       (dict(g_off=-1), "gate out of bounds"), (dict(gate=gate + 2), "gate must be")]:
+        st, msg = check_linear(linear_desc(**{**ok, **kw}))
+        assert st == _lib.EINVAL and needle in msg, (kw, msg)
+
+
+def test_linear_python_argument_checks():
+    """ops.linear's own checks, made before anything is recorded: an in-place residual needs out,
+    and a gate needs a residual (app/gpu/gemm.js:135 only gates the residual form)."""
+    with pytest.raises(ValueError, match="pass out"):
+        supra_attn.linear(None, BASE_Q, BASE_B, N=4, K=4, M=1, resid=True)
+    with pytest.raises(ValueError, match="needs resid"):
+        supra_attn.linear(None, BASE_Q, BASE_B, N=4, K=4, M=1, out=BASE_O, gate=BASE_B)

@@ -203,3 +203,79 @@ def test_linear_groupnorm_silu_and_residual(gpu):
         ref = oracle.linear(n, w, rows, N, K).reshape(rows, N) + r[sl, :N]
         assert_close(got[sl], ref)
     y.release()
+
+
+# ---- DiT block projections around the attention (app/models/dit.js:161-187) -----------------------
+def test_dit_block_projections_golden(gpu, golden):
+    """The residual stream x updated in place, as the reference's DiT block does: self attention
+    into a, x += g1 * proj(a) with g1 = mod[2D:3D] (gated), then x += cproj(c) (ungated); both
+    recorded behind the attention and flushed together, against the reference's outputs."""
+    import supra_attn
+    from conftest import dit_proj_inputs
+
+    x = dit_proj_inputs()
+    B, N, D = x["B"], x["N"], x["D"]
+    xs = dev(x["x0"])
+    qkv, mod, c = dev(x["qkv"]), dev(x["mod"]), dev(x["c"])
+    wp, bp, wc, bc = dev(x["wp"]), dev(x["bp"]), dev(x["wc"]), dev(x["bc"])
+    a = gpu.empty([B * N, D])
+    for b in range(B):
+        r = b * N * 3 * D
+        supra_attn.attention(gpu, q=qkv, k=qkv, v=qkv, Lq=N, Lk=N, H=9, D=64, ldq=3 * D, ldk=3 * D, ldv=3 * D,
+                             qOff=r, kOff=r + D, vOff=r + 2 * D, oOff=b * N * D, out=a)
+    supra_attn.linear(gpu, a, wp, N=D, K=D, bias=bp, out=xs, resid=True, gate=mod, gOff=2 * D)
+    gpu.sync()
+    assert_close(host(xs), golden("dit_proj_x1"))
+    supra_attn.linear(gpu, c, wc, N=D, K=D, bias=bc, out=xs, resid=True)
+    gpu.sync()
+    assert_close(host(xs), golden("dit_proj_x2"))
+    a.release()
+
+
+@pytest.mark.parametrize("aligned", [True, False])
+def test_linear_gated_in_place_strided(gpu, aligned):
+    """In-place gated residual on a strided y with offsets (rows of ldy, first at yOff): only the
+    M x N block changes, each element to y + gate[gOff + n] * (x W^T + b)."""
+    import supra_attn
+
+    rng = np.random.default_rng(31 + aligned)
+    M, N, K = 150, 200, 64 if aligned else 61
+    ldy, yo, go = (208, 16, 40) if aligned else (203, 5, 7)
+    y0 = rng.standard_normal(yo + M * ldy).astype(np.float32)
+    xa = rng.standard_normal((M, K)).astype(np.float32)
+    wa = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    ba = rng.standard_normal(N).astype(np.float32)
+    ga = rng.standard_normal(go + N + 3).astype(np.float32)
+    yd, xd, wd, bd, gd = dev(y0), dev(xa), dev(wa), dev(ba), dev(ga)
+    supra_attn.linear(gpu, xd, wd, M=M, N=N, K=K, bias=bd, out=yd, ldy=ldy, yOff=yo, resid=True, gate=gd, gOff=go)
+    gpu.sync()
+    got = host(yd)
+    idx = yo + np.arange(M)[:, None] * ldy + np.arange(N)[None, :]
+    keep = np.ones(got.size, bool)
+    keep[idx.reshape(-1)] = False
+    np.testing.assert_array_equal(got[keep], y0[keep])
+    ref = oracle.gated_residual(y0[idx], xa, wa, M, N, K, bias=ba, gate=ga, g_off=go)
+    assert_close(got[idx], ref)
+
+
+def test_linear_in_place_is_ordered_after_readers(gpu):
+    """x is read by an attention recorded before the in-place update of x: the update waits for
+    it (write-after-read hazard), and a reader recorded after sees the updated x."""
+    import supra_attn
+
+    rng = np.random.default_rng(12)
+    L, D = 80, 576
+    xa = rng.standard_normal(L * D).astype(np.float32)
+    ca = rng.standard_normal(L * D).astype(np.float32)
+    wa = (rng.standard_normal((D, D)) / np.sqrt(D)).astype(np.float32)
+    xd, cd, wd = dev(xa), dev(ca), dev(wa)
+    o1 = supra_attn.attention(gpu, q=xd, k=xd, v=xd, Lq=L, Lk=L, H=9, D=64, ldq=D, ldk=D, ldv=D)
+    supra_attn.linear(gpu, cd, wd, N=D, K=D, out=xd, resid=True)
+    o2 = supra_attn.attention(gpu, q=xd, k=xd, v=xd, Lq=L, Lk=L, H=9, D=64, ldq=D, ldk=D, ldv=D)
+    gpu.sync()
+    x1 = oracle.gated_residual(xa, ca, wa, L, D, D).reshape(-1)
+    assert_close(gpu.read(o1), oracle.attention_ops(xa, xa, xa, L, L, 9, 64, D, D, D))
+    assert_close(host(xd), x1)
+    assert_close(gpu.read(o2), oracle.attention_ops(x1, x1, x1, L, L, 9, 64, D, D, D))
+    for t in (o1, o2):
+        t.release()

@@ -154,3 +154,22 @@ def test_vae_attention_block(golden):
     got = oracle.vae_attention_block(x["x"], x["gamma"], x["beta"], x["wq"], x["bq"], x["wk"], x["bk"], x["wv"],
                                      x["bv"], x["wo"], x["bo"])
     assert oracle.max_rel(got, golden("vae_block_out")) <= TOL
+
+
+def test_dit_block_projections(golden):
+    """oracle.gated_residual around oracle.attention_heads against the reference's dit_forward
+    lines for the gated self-attention projection and the ungated cross projection."""
+    from conftest import dit_proj_inputs
+
+    x = dit_proj_inputs()
+    assert hashlib.sha256(np.asarray(x["flat"], dtype="<f4").tobytes()).hexdigest() == \
+        golden.meta("dit_proj_x1")["input_sha256"]
+    B, N, D = x["B"], x["N"], x["D"]
+    x1, x2 = [], []
+    for b in range(B):
+        qkv = x["qkv"][b]
+        a = oracle.attention_heads(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], 9)
+        x1.append(oracle.gated_residual(x["x0"][b], a, x["wp"], N, D, D, bias=x["bp"], gate=x["mod"], g_off=2 * D))
+        x2.append(oracle.gated_residual(x1[-1], x["c"][b], x["wc"], N, D, D, bias=x["bc"]))
+    assert oracle.max_rel(np.stack(x1), golden("dit_proj_x1")) <= TOL
+    assert oracle.max_rel(np.stack(x2), golden("dit_proj_x2")) <= TOL
