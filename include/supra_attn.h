@@ -169,7 +169,14 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  *     175,187,193); otherwise it may not overlap y.
  *   - gate != NULL (needs resid): y = resid + gate[g_off + n] * (x W^T + bias), the gated
  *     residual of the DiT blocks (app/gpu/gemm.js:10,135, app/models/dit.js:175,193).
- * Activations on y (app/gpu/ops.js:33-43) are not covered; flags and reserved must be 0.
+ *   - ln != NULL (not with gn): x is LayerNorm-ed on the way in, each row over its K channels
+ *     (ops.layernorm, app/gpu/ops.js:71-79, app/gpu/kernels.js:87-114): the library computes
+ *     (mean, 1/sqrt(var + eps)) per row in an extra launch, and the product uses
+ *     (x - mean) * rstd, times (1 + mod[scale_off + k]) plus mod[shift_off + k] when ln->mod is
+ *     set (adaLN modulation; app/models/dit.js:164,179,189). Needs x_off == 0 and ldx == K.
+ *   - act: SUPRA_ATTN_ACT_NONE, _GELU (erf form), _GELU_TANH or _SILU, applied to x W^T + bias
+ *     before the gate and the residual (ops.linear's act, app/gpu/gemm.js:9,28-36,130-135).
+ * flags must be 0.
  * Cross-attention K/V preparation (app/models/dit.js:137-144) is two calls: ctx_proj, then ONE
  * product with the 14 blocks' kv weights stacked [14*1152, 576]; block b's cross attention then
  * reads K at column 1152*b and V at 1152*b + 576 of rows of stride 14*1152, without a copy. */
@@ -182,6 +189,17 @@ typedef struct supra_attn_groupnorm {
   int32_t silu;       /* nonzero: SiLU after the affine (ops.groupnorm's silu flag) */
 } supra_attn_groupnorm;
 
+enum { SUPRA_ATTN_ACT_NONE = 0, SUPRA_ATTN_ACT_GELU = 1, SUPRA_ATTN_ACT_GELU_TANH = 2, SUPRA_ATTN_ACT_SILU = 3 };
+
+typedef struct supra_attn_layernorm {
+  const float* mod;   /* NULL: plain LayerNorm; else the modulation vector (mod_size floats) */
+  int64_t mod_size;
+  int64_t shift_off;  /* LN(x) * (1 + mod[scale_off + k]) + mod[shift_off + k] */
+  int64_t scale_off;
+  float eps;          /* the reference uses 1e-6 */
+  int32_t reserved;   /* 0 */
+} supra_attn_layernorm;
+
 typedef struct supra_attn_linear_desc {
   const float* x;
   const float* w;
@@ -193,12 +211,13 @@ typedef struct supra_attn_linear_desc {
   int32_t M, N, K;
   int32_t variant;
   uint32_t flags;
-  uint32_t reserved;
+  uint32_t act;                   /* SUPRA_ATTN_ACT_* */
   const supra_attn_groupnorm* gn; /* NULL, or GroupNorm x on the way in (copied at enqueue) */
   const float* resid;             /* NULL, or y = resid + ... (rows of stride ldr at r_off) */
   int64_t resid_size, ldr, r_off;
   const float* gate;              /* NULL, or the product is scaled by gate[g_off + n] */
   int64_t gate_size, g_off;
+  const supra_attn_layernorm* ln; /* NULL, or LayerNorm x on the way in (copied at enqueue) */
 } supra_attn_linear_desc;
 SUPRA_ATTN_API int supra_attn_enqueue_linear(supra_attn_ctx* ctx, const supra_attn_linear_desc* desc);
 /* Validates a linear descriptor as supra_attn_enqueue_linear does (pure host function). */

@@ -11,6 +11,10 @@ TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): never imported by the product
   groupnorm        -- ops.groupnorm (app/gpu/ops.js:82-92, app/gpu/kernels.js:117-162).
   vae_attention_block -- VAE.attention (app/models/vae.js:77-94): GroupNorm, q/k/v, attention,
                       output projection, residual.
+  layernorm        -- ops.layernorm (app/gpu/ops.js:71-79, app/gpu/kernels.js:87-114), with the
+                      optional adaLN modulation LN(x) * (1 + scale) + shift.
+  activation       -- ops.linear's act (app/gpu/gemm.js:28-36): gelu (erf form), gelu_tanh, silu.
+  dit_block        -- one DiT block (app/models/dit.js:161-194; tools/reference.py:96-102).
   gated_residual   -- ops.linear with { out, resid: true, gate, gOff } (app/gpu/gemm.js:10,135):
                       out = out + gate[gOff + n] * (x W^T + bias), the DiT blocks' projections
                       (app/models/dit.js:175,187,193; tools/reference.py:98,100,102).
@@ -91,3 +95,55 @@ def gated_residual(out, x, w, M, N, K, bias=None, gate=None, g_off=0):
     if gate is not None:
         y = y * np.asarray(gate, np.float64).reshape(-1)[g_off:g_off + N][None, :]
     return (np.asarray(out, np.float64).reshape(M, N) + y).astype(np.float32)
+
+
+def layernorm(x, mod=None, shift_off=0, scale_off=0, eps=1e-6):
+    """ops.layernorm (app/gpu/ops.js:71-79; app/gpu/kernels.js:101-113) of x [rows, cols]: per row
+    the mean, then the variance around it (biased), (x - mean) / sqrt(var + eps), then
+    * (1 + mod[scale_off + c]) + mod[shift_off + c] when mod is given. float64."""
+    x = np.asarray(x, dtype=np.float64)
+    cols = x.shape[1]
+    mean = x.mean(axis=1, keepdims=True)
+    var = ((x - mean) ** 2).mean(axis=1, keepdims=True)
+    y = (x - mean) / np.sqrt(var + eps)
+    if mod is not None:
+        m = np.asarray(mod, dtype=np.float64).reshape(-1)
+        y = y * (1.0 + m[scale_off:scale_off + cols]) + m[shift_off:shift_off + cols]
+    return y
+
+
+def activation(x, act):
+    """ops.linear's act (app/gpu/gemm.js:28-36) in float64: "gelu" = 0.5 x (1 + erf(x / sqrt 2)),
+    "gelu_tanh" = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), "silu" = x / (1 + e^-x)."""
+    from math import erf, pi, sqrt
+
+    x = np.asarray(x, dtype=np.float64)
+    if act == "gelu":
+        return 0.5 * x * (1.0 + np.vectorize(erf)(x / sqrt(2.0)))
+    if act == "gelu_tanh":
+        return 0.5 * x * (1.0 + np.tanh(sqrt(2.0 / pi) * (x + 0.044715 * x ** 3)))
+    if act == "silu":
+        return x / (1.0 + np.exp(-x))
+    raise ValueError(act)
+
+
+def dit_block(x, mod, w, kv, heads=9):
+    """One DiT block on one image (app/models/dit.js:161-194; tools/reference.py:96-102), float64:
+    x [N, D]; mod the step's modulation vector [6D] (shift, scale, gate for the attention, then for
+    the MLP); w dict of [out, in] weights and biases qkv, proj, q, cproj, fc1, fc2; kv [L, 2D] the
+    prompt's cross-attention K|V. Returns (x after self attention, after cross attention, after
+    the MLP) as float32 [N, D]."""
+    from .attention import attention_heads
+
+    x = np.asarray(x, dtype=np.float64)
+    D = x.shape[1]
+    m = np.asarray(mod, dtype=np.float64).reshape(-1)
+    f = lambda a, nm: a @ np.asarray(w[nm], np.float64).T + np.asarray(w["b" + nm], np.float64)
+    qkv = f(layernorm(x, m, 0, D), "qkv")
+    x1 = x + m[2 * D:3 * D] * f(attention_heads(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], heads), "proj")
+    kv = np.asarray(kv, dtype=np.float64)
+    c = attention_heads(f(layernorm(x1), "q"), kv[:, :D], kv[:, D:], heads)
+    x2 = x1 + f(c, "cproj")
+    h = activation(f(layernorm(x2, m, 3 * D, 4 * D), "fc1"), "gelu_tanh")
+    x3 = x2 + m[5 * D:6 * D] * f(h, "fc2")
+    return tuple(t.astype(np.float32) for t in (x1, x2, x3))

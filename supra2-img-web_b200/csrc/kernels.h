@@ -128,6 +128,13 @@ constexpr int kFwBoxRows = 32;
 cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s);
 int attn_fp32_warp_tile_rows();
 
+// Normalisation of x in the linear prologue (LinProb::gn_mode): GroupNorm with gamma/beta,
+// LayerNorm with adaLN modulation (gamma = scale, beta = shift, applied as 1 + scale), plain
+// LayerNorm.
+constexpr int kNormAffine = 0, kNormModulated = 1, kNormPlain = 2;
+// Activation in the linear epilogue (LinProb::act), the values of SUPRA_ATTN_ACT_*.
+constexpr int kActNone = 0, kActGelu = 1, kActGeluTanh = 2, kActSilu = 3;
+
 // y = x W^T (+ bias) for one ops.linear call (app/gpu/ops.js:35-43), linear_fp32.cu. x rows of
 // stride ldx (the caller's x offset already applied), W [N, K] row-major with row stride ldw,
 // y rows of stride ldy (offset applied).
@@ -142,7 +149,10 @@ struct alignas(16) LinProb {
   const float* resid;  // y = resid[row * ldr + col] + ..., or nullptr (may be y itself)
   int64_t ldr;
   const float* gate;   // the product is scaled by gate[col] (offset applied), or nullptr
-  // GroupNorm of x on the way in (gn_stats != nullptr): stats[image * groups + g] = (mean, rstd)
+  int32_t gn_mode;     // normalisation of x: kNormAffine, kNormModulated or kNormPlain
+  int32_t act;         // activation of x W^T + bias: kActNone, kActGelu, kActGeluTanh, kActSilu
+  // normalisation of x on the way in (gn_stats != nullptr): stats[image * groups + g] = (mean,
+  // rstd); a LayerNorm is one image per row and one group
   const float2* gn_stats;
   const float* gamma;
   const float* beta;
@@ -165,6 +175,7 @@ cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cuda
 // GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
 // group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
 // mean in a second pass (app/gpu/kernels.js:117-139).
+cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s);
 cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
                             float eps, float2* stats, cudaStream_t s);
 

@@ -24,6 +24,14 @@ constexpr int kBN = 128;  // columns per tile
 constexpr int kBK = 16;   // reduction depth per stage
 constexpr int kS = kBK + 4;  // row stride of the stage buffers (conflict-free float4 reads)
 
+// ops.linear's activations (app/gpu/gemm.js:28-36): GELU in its erf form, GELU with the tanh
+// approximation 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), SiLU x / (1 + e^-x).
+__device__ __forceinline__ float activate(int act, float x) {
+  if (act == kActGelu) return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+  if (act == kActGeluTanh) return 0.5f * x * (1.f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
+  return x / (1.f + expf(-x));
+}
+
 template <bool BIAS, bool ALIGNED>
 __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
   __shared__ __align__(16) float As[2][kBM * kS];
@@ -96,8 +104,9 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
     }
     __syncthreads();
     if (P.gn_stats) {
-      // GroupNorm (+ SiLU) of the staged x tile: (x - mean) * rstd * gamma + beta per element of
-      // a valid row and column (padding stays zero); app/gpu/kernels.js:141-162
+      // GroupNorm (+ SiLU) or LayerNorm (+ modulation) of the staged x tile, per element of a
+      // valid row and column (padding stays zero): (x - mean) * rstd * g + b with g, b = gamma,
+      // beta (app/gpu/kernels.js:141-162), 1 + scale, shift (app/gpu/kernels.js:111) or 1, 0
       float* a = As[st & 1];
       const int k0 = st * kBK;
 #pragma unroll
@@ -107,7 +116,13 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
         const int k = k0 + kk;
         if (r < nr && k < K) {
           const float2 ms = __ldg(P.gn_stats + (int64_t)((r0 + r) / P.gn_rows) * P.gn_groups + k / P.gn_cg);
-          float v = (a[r * kS + kk] - ms.x) * ms.y * __ldg(P.gamma + k) + __ldg(P.beta + k);
+          float g = 1.f, b = 0.f;
+          if (P.gn_mode != kNormPlain) {
+            g = __ldg(P.gamma + k);
+            b = __ldg(P.beta + k);
+            if (P.gn_mode == kNormModulated) g = 1.f + g;
+          }
+          float v = (a[r * kS + kk] - ms.x) * ms.y * g + b;
           if (P.gn_silu) v = v / (1.f + __expf(-v));
           a[r * kS + kk] = v;
         }
@@ -155,6 +170,7 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
       const int c = cg + 16 * j;
       if (c < nc) {
         float v = acc[i][j] + bias[j];
+        if (P.act != kActNone) v = activate(P.act, v);
         if (P.gate) v *= gate[j];
         yrow[c] = rrow ? rrow[c] + v : v;
       }
@@ -197,7 +213,35 @@ __global__ void __launch_bounds__(256) gn_stats_kernel(const float* __restrict__
   if (tid == 0) stats[blockIdx.x] = make_float2(mean, rsqrtf(var + eps));
 }
 
+// One warp per row: LayerNorm statistics over the row's K channels, mean then the variance
+// around it, as the reference's layernormShader (app/gpu/kernels.js:104-110).
+__global__ void __launch_bounds__(256) ln_stats_kernel(const float* __restrict__ x, int32_t K, int32_t rows,
+                                                       float eps, float2* __restrict__ stats) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* base = x + (int64_t)row * K;
+  float s = 0.f;
+  for (int i = lane; i < K; i += 32) s += __ldg(base + i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / (float)K;
+  float v = 0.f;
+  for (int i = lane; i < K; i += 32) {
+    const float d = __ldg(base + i) - mean;
+    v = fmaf(d, d, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) stats[row] = make_float2(mean, rsqrtf(v / (float)K + eps));
+}
+
 }  // namespace
+
+cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  ln_stats_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, K, rows, eps, stats);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
                             float eps, float2* stats, cudaStream_t s) {

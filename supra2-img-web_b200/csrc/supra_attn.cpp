@@ -539,7 +539,8 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
 
 int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked* out) {
   if (!d) return set_err(c, SUPRA_ATTN_EINVAL, "linear descriptor is NULL");
-  if (d->flags || d->reserved) return set_err(c, SUPRA_ATTN_EINVAL, "linear: flags and reserved must be 0");
+  if (d->flags) return set_err(c, SUPRA_ATTN_EINVAL, "linear: flags must be 0");
+  if (d->act > SUPRA_ATTN_ACT_SILU) return set_err(c, SUPRA_ATTN_EINVAL, "linear: act=%u unknown", d->act);
   if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
     return set_err(c, SUPRA_ATTN_EINVAL, "linear: unknown variant %d", d->variant);
   if (d->M < 0 || d->M > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "linear: M=%d out of range [0, 2^30]", d->M);
@@ -589,6 +590,23 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
     if ((int64_t)(d->M / gn->rows_per_image) * gn->groups > INT32_MAX)
       return set_err(c, SUPRA_ATTN_EINVAL, "linear: too many groupnorm groups");
   }
+  const supra_attn_layernorm* ln = d->ln;
+  if (ln) {
+    if (gn) return set_err(c, SUPRA_ATTN_EINVAL, "linear: groupnorm and layernorm are exclusive");
+    if (ln->reserved) return set_err(c, SUPRA_ATTN_EINVAL, "linear: layernorm reserved must be 0");
+    if (!std::isfinite(ln->eps) || ln->eps < 0.f) return set_err(c, SUPRA_ATTN_EINVAL, "linear: layernorm eps");
+    if (d->x_off != 0 || d->ldx != d->K)
+      return set_err(c, SUPRA_ATTN_EINVAL, "linear: layernorm needs contiguous x rows (x_off == 0, ldx == K)");
+    if (ln->mod) {
+      if (reinterpret_cast<uintptr_t>(ln->mod) & 3u)
+        return set_err(c, SUPRA_ATTN_EINVAL, "linear: layernorm mod must be a 4-byte aligned float array");
+      if (ln->shift_off < 0 || ln->scale_off < 0 || ln->shift_off > lim || ln->scale_off > lim ||
+          ln->shift_off + d->K > ln->mod_size || ln->scale_off + d->K > ln->mod_size)
+        return set_err(c, SUPRA_ATTN_EINVAL,
+                       "linear: layernorm mod out of bounds: needs shift_off + K and scale_off + K <= mod_size=%lld",
+                       (long long)ln->mod_size);
+    }
+  }
   // in place: resid is y itself, element for element (the reference's out: x, resid: true)
   const bool in_place = d->resid && d->resid == d->y && d->r_off == d->y_off && d->ldr == d->ldy;
   if (d->resid) {
@@ -621,6 +639,10 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
       out->reads[out->nreads++] = rng(gn->gamma, 0, d->K - 1);
       out->reads[out->nreads++] = rng(gn->beta, 0, d->K - 1);
     }
+    if (ln && ln->mod) {
+      out->reads[out->nreads++] = rng(ln->mod, ln->shift_off, ln->shift_off + d->K - 1);
+      out->reads[out->nreads++] = rng(ln->mod, ln->scale_off, ln->scale_off + d->K - 1);
+    }
     if (d->resid && !in_place)
       out->reads[out->nreads++] = rng(d->resid, d->r_off, d->r_off + (int64_t)(d->M - 1) * d->ldr + d->N - 1);
     if (d->gate) out->reads[out->nreads++] = rng(d->gate, d->g_off, d->g_off + d->N - 1);
@@ -646,6 +668,7 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   q.lin.resid = d->resid ? d->resid + d->r_off : nullptr;
   q.lin.ldr = d->resid ? d->ldr : 0;
   q.lin.gate = d->gate ? d->gate + d->g_off : nullptr;
+  q.lin.act = (int32_t)d->act;
   q.gn_eps = 0.f;
   if (gn) {
     q.lin.gamma = gn->gamma;
@@ -654,7 +677,17 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
     q.lin.gn_cg = d->K / gn->groups;
     q.lin.gn_rows = gn->rows_per_image;
     q.lin.gn_silu = gn->silu ? 1 : 0;
+    q.lin.gn_mode = supra::kNormAffine;
     q.gn_eps = gn->eps;
+  }
+  if (ln) {  // one image per row, one group of K channels (app/gpu/kernels.js:101-113)
+    q.lin.gamma = ln->mod ? ln->mod + ln->scale_off : nullptr;
+    q.lin.beta = ln->mod ? ln->mod + ln->shift_off : nullptr;
+    q.lin.gn_groups = 1;
+    q.lin.gn_cg = d->K;
+    q.lin.gn_rows = 1;
+    q.lin.gn_mode = ln->mod ? supra::kNormModulated : supra::kNormPlain;
+    q.gn_eps = ln->eps;
   }
   q.path = PATH_LINEAR;
   q.cfg = 0;
@@ -665,7 +698,8 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   q.rows_q = q.rows_k = q.rows_v = 0;
   q.flops = 2.0 * d->M * (double)d->N * d->K;
   q.bytes = 4.0 * ((double)d->M * d->K + (double)d->N * d->K + (double)d->M * d->N + (d->bias ? d->N : 0) +
-                   (d->resid ? (double)d->M * d->N : 0.0) + (gn ? 2.0 * d->K : 0.0));
+                   (d->resid ? (double)d->M * d->N : 0.0) + ((gn || (ln && ln->mod)) ? 2.0 * d->K : 0.0) +
+                   (d->gate ? d->N : 0));
   return SUPRA_ATTN_OK;
 }
 
@@ -1050,7 +1084,7 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   // GroupNorm statistics of the problems that normalise x, in a context buffer, one launch each
   size_t nstats = 0;
   for (int i = 0; i < n; ++i)
-    if (g[i]->lin.gamma) nstats += (size_t)(g[i]->lin.M / g[i]->lin.gn_rows) * g[i]->lin.gn_groups;
+    if (g[i]->lin.gn_rows > 0) nstats += (size_t)(g[i]->lin.M / g[i]->lin.gn_rows) * g[i]->lin.gn_groups;
   if (nstats > c->gn_cap) {
     cudaError_t e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return cuda_err(c, e, "groupnorm stats: stream sync");
@@ -1067,16 +1101,18 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   size_t at = 0;
   for (int i = 0; i < n; ++i) {
     hp[i] = g[i]->lin;
-    if (hp[i].gamma) {
+    if (hp[i].gn_rows > 0) {
       const int32_t images = hp[i].M / hp[i].gn_rows;
       hp[i].gn_stats = c->gn_stats + at;
       cudaError_t e;
+      const bool ln = hp[i].gn_mode != supra::kNormAffine;
       {
-        ProfScope ps(c, "groupnorm_stats", 0.0, 4.0 * (double)hp[i].M * hp[i].K);
-        e = supra::launch_gn_stats(hp[i].x, hp[i].K, hp[i].gn_rows, images, hp[i].gn_groups, g[i]->gn_eps,
-                                   c->gn_stats + at, c->stream);
+        ProfScope ps(c, ln ? "layernorm_stats" : "groupnorm_stats", 0.0, 4.0 * (double)hp[i].M * hp[i].K);
+        e = ln ? supra::launch_ln_stats(hp[i].x, hp[i].K, hp[i].M, g[i]->gn_eps, c->gn_stats + at, c->stream)
+               : supra::launch_gn_stats(hp[i].x, hp[i].K, hp[i].gn_rows, images, hp[i].gn_groups, g[i]->gn_eps,
+                                        c->gn_stats + at, c->stream);
       }
-      if (e != cudaSuccess) return cuda_err(c, e, "groupnorm_stats");
+      if (e != cudaSuccess) return cuda_err(c, e, ln ? "layernorm_stats" : "groupnorm_stats");
       c->launches += 1;
       at += (size_t)images * hp[i].gn_groups;
     }

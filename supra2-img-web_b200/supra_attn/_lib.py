@@ -39,6 +39,13 @@ class GroupNorm(C.Structure):
                 ("eps", C.c_float), ("silu", C.c_int32)]
 
 
+class LayerNorm(C.Structure):
+    """supra_attn_layernorm (include/supra_attn.h)."""
+
+    _fields_ = [("mod", C.c_void_p), ("mod_size", C.c_int64), ("shift_off", C.c_int64), ("scale_off", C.c_int64),
+                ("eps", C.c_float), ("reserved", C.c_int32)]
+
+
 class LinearDesc(C.Structure):
     """supra_attn_linear_desc (include/supra_attn.h)."""
 
@@ -47,9 +54,10 @@ class LinearDesc(C.Structure):
         ("x_size", C.c_int64), ("w_size", C.c_int64), ("bias_size", C.c_int64), ("y_size", C.c_int64),
         ("ldx", C.c_int64), ("ldw", C.c_int64), ("ldy", C.c_int64), ("x_off", C.c_int64), ("y_off", C.c_int64),
         ("M", C.c_int32), ("N", C.c_int32), ("K", C.c_int32),
-        ("variant", C.c_int32), ("flags", C.c_uint32), ("reserved", C.c_uint32),
+        ("variant", C.c_int32), ("flags", C.c_uint32), ("act", C.c_uint32),
         ("gn", C.POINTER(GroupNorm)), ("resid", C.c_void_p), ("resid_size", C.c_int64), ("ldr", C.c_int64),
         ("r_off", C.c_int64), ("gate", C.c_void_p), ("gate_size", C.c_int64), ("g_off", C.c_int64),
+        ("ln", C.POINTER(LayerNorm)),
     ]
 
 

@@ -24,9 +24,10 @@ import math
 import numpy as np
 
 from . import _lib
-from ._lib import Desc, GroupNorm, LinearDesc, ProfileEntry, check, lib
+from ._lib import Desc, GroupNorm, LayerNorm, LinearDesc, ProfileEntry, check, lib
 
 VARIANTS = {"fp32": _lib.FP32, "tf32": _lib.TF32}
+ACTS = {None: 0, "gelu": 1, "gelu_tanh": 2, "silu": 3}  # SUPRA_ATTN_ACT_*
 
 
 class Tensor:
@@ -260,13 +261,17 @@ def attention(gpu: GPU, *, q, k, v, Lq, Lk, H, D, ldq, ldk, ldv, qOff=0, kOff=0,
 
 
 def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
-                     groupnorm=None, resid=None, ldr=None, rOff=0, gate=None, gOff=0,
+                     groupnorm=None, layernorm=None, resid=None, ldr=None, rOff=0, gate=None, gOff=0, act=None,
                      variant="fp32") -> LinearDesc:
     """Packs one linear call y = resid + gate * (x W^T + bias) (resid, gate and bias optional) into
     a supra_attn_linear_desc (validated by the library). resid=True is the reference's in-place
     residual: resid is y itself, same rows. groupnorm: dict(gamma, beta, groups, rows_per_image,
-    eps=1e-6, silu=False) to GroupNorm x on the way in. The returned descriptor keeps the GroupNorm
-    block alive."""
+    eps=1e-6, silu=False) to GroupNorm x on the way in; layernorm: dict(mod=None, shiftOff=0,
+    scaleOff=0, eps=1e-6) to LayerNorm each row of x on the way in, modulated by mod when given
+    (ops.layernorm's arguments, app/gpu/ops.js:71). act: None, "gelu", "gelu_tanh" or "silu" on
+    x W^T + bias (app/gpu/gemm.js:130-134). The returned descriptor keeps the norm blocks alive."""
+    if act not in ACTS:
+        raise ValueError(f"act must be one of {sorted(a for a in ACTS if a)} or None")
     d = LinearDesc()
     if groupnorm is not None:
         gnb = GroupNorm()
@@ -278,6 +283,16 @@ def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=Non
         gnb.silu = 1 if groupnorm.get("silu", False) else 0
         d._gn = gnb
         d.gn = C.pointer(gnb)
+    if layernorm is not None:
+        lnb = LayerNorm()
+        mod = layernorm.get("mod")
+        if mod is not None:
+            lnb.mod, lnb.mod_size = _as_buf(mod)
+            lnb.shift_off = int(layernorm.get("shiftOff", 0))
+            lnb.scale_off = int(layernorm.get("scaleOff", 0))
+        lnb.eps = float(layernorm.get("eps", 1e-6))
+        d._ln = lnb
+        d.ln = C.pointer(lnb)
     if resid is True:  # in place on y (app/gpu/gemm.js:135 reads C[ci] before it writes it)
         resid, ldr, rOff = y, (N if ldy is None else ldy), yOff
     if resid is not None and resid is not False:
@@ -300,21 +315,27 @@ def make_linear_desc(*, x, w, y, M, N, K, bias=None, ldx=None, ldw=None, ldy=Non
     if variant not in VARIANTS:
         raise ValueError(f"variant must be one of {sorted(VARIANTS)}")
     d.variant = VARIANTS[variant]
+    d.act = ACTS[act]
     return d
 
 
 def linear(gpu: GPU, x, w, *, N, K, M=None, bias=None, out=None, ldx=None, ldw=None, ldy=None, xOff=0, yOff=0,
-           groupnorm=None, resid=None, ldr=None, rOff=0, gate=None, gOff=0, variant="fp32"):
+           groupnorm=None, layernorm=None, resid=None, ldr=None, rOff=0, gate=None, gOff=0, act=None,
+           variant="fp32"):
     """ops.linear (app/gpu/ops.js:35-43): y = x @ W^T (+ bias), recorded; returns y.
 
     x: M rows of K floats (row stride ldx, first row at xOff; M defaults to x.size / K as in the
     reference); w: [N, K] row-major weights; bias: N floats. y is allocated as gpu.empty([M, N])
     when `out` is omitted. groupnorm (dict, see make_linear_desc) normalises x on the way in
-    (ops.groupnorm, app/gpu/ops.js:82-92); resid is added to y (the residual add of
+    (ops.groupnorm, app/gpu/ops.js:82-92), layernorm (dict(mod, shiftOff, scaleOff), or {} for the
+    plain norm) LayerNorms each row of x on the way in (ops.layernorm, app/gpu/ops.js:71-79, with
+    the adaLN modulation of app/models/dit.js:164,189); resid is added to y (the residual add of
     app/models/vae.js:91). resid=True with `out` is the reference's in-place residual
     `{ out: x, resid: true }` (app/models/dit.js:187), and gate/gOff scale the product per output
     column first, out = out + gate[gOff + n] * (x W^T + bias) (app/gpu/gemm.js:10,135,
-    app/models/dit.js:175,193). fp32 FFMA; runs at the next flush/sync/read.
+    app/models/dit.js:175,193). act ("gelu", "gelu_tanh", "silu") applies to x W^T + bias before
+    the gate and the residual (app/gpu/gemm.js:130-135). fp32 FFMA; runs at the next
+    flush/sync/read.
     """
     if resid is True and out is None:
         raise ValueError("resid=True accumulates into out: pass out")
@@ -326,8 +347,8 @@ def linear(gpu: GPU, x, w, *, N, K, M=None, bias=None, out=None, ldx=None, ldw=N
     y = out if out is not None else gpu.empty([int(M), int(N)])
     try:
         d = make_linear_desc(x=x, w=w, y=y, M=M, N=N, K=K, bias=bias, ldx=ldx, ldw=ldw, ldy=ldy, xOff=xOff,
-                             yOff=yOff, groupnorm=groupnorm, resid=resid, ldr=ldr, rOff=rOff, gate=gate, gOff=gOff,
-                             variant=variant)
+                             yOff=yOff, groupnorm=groupnorm, layernorm=layernorm, resid=resid, ldr=ldr, rOff=rOff,
+                             gate=gate, gOff=gOff, act=act, variant=variant)
         check(lib.supra_attn_enqueue_linear(gpu.ctx, C.byref(d)), gpu.ctx)
     except Exception:
         if out is None:

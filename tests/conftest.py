@@ -83,6 +83,26 @@ def dit_proj_inputs():
             "bp": t[1].numpy(), "wc": t[2].numpy(), "bc": t[3].numpy(), "c": cx.numpy(), "flat": flat.numpy()}
 
 
+def dit_block_inputs():
+    """Inputs of the golden 'dit_block' case (one whole DiT block), regenerated from its seed in
+    tests/golden/make_golden.py's order."""
+    import torch
+
+    g = torch.Generator().manual_seed(111)
+    B, N, D, Ls = 2, 64, 576, [5, 77]
+    x0 = torch.randn(B, N, D, generator=g)
+    mod = 0.5 * torch.randn(6 * D, generator=g)
+    w = {}
+    for nm, (o, i) in [("qkv", (3 * D, D)), ("proj", (D, D)), ("q", (D, D)), ("cproj", (D, D)),
+                       ("fc1", (4 * D, D)), ("fc2", (D, 4 * D))]:
+        w[nm] = torch.randn(o, i, generator=g) / i ** 0.5
+        w["b" + nm] = 0.1 * torch.randn(o, generator=g)
+    kvs = [torch.randn(L, 2 * D, generator=g) for L in Ls]
+    flat = torch.cat([x0.reshape(-1), mod] + [t.reshape(-1) for t in w.values()] + [t.reshape(-1) for t in kvs])
+    return {"B": B, "N": N, "D": D, "Ls": Ls, "x0": x0.numpy(), "mod": mod.numpy(),
+            "w": {k: v.numpy() for k, v in w.items()}, "kv": [t.numpy() for t in kvs], "flat": flat.numpy()}
+
+
 @pytest.fixture(scope="session")
 def gpu():
     """One libsupra_attn context on cuda:0, running on torch's current stream."""

@@ -234,6 +234,39 @@ def main():
                                  "inputs": "torch.Generator().manual_seed(99): x [2,64,576]; qkv [2,64,1728]; mod 0.5*randn "
                                            "[3456]; proj, cproj: W randn/sqrt(576), b 0.1*randn; c [2,64,576]"}
 
+    # ---- one whole DiT block (app/models/dit.js:161-194) with the reference's own modulate,
+    # layernorm, linear and attention, in dit_forward's order (tools/reference.py:96-102): the
+    # step's modulation vector mod [6*576] stands for the adaLN linear's output (chunks shift,
+    # scale, gate for the attention, then for the MLP), shared by the batch; the cross K/V of each
+    # image is given (its prompt's prepared context, lengths 5 and 77). Only outputs stored.
+    g = torch.Generator().manual_seed(111)
+    B, N, D, Ls = 2, 64, 576, [5, 77]
+    x0 = torch.randn(B, N, D, generator=g)
+    mod = 0.5 * torch.randn(6 * D, generator=g)
+    bsd = {}
+    for nm, (o, i) in [("qkv", (3 * D, D)), ("proj", (D, D)), ("q", (D, D)), ("cproj", (D, D)),
+                       ("fc1", (4 * D, D)), ("fc2", (D, 4 * D))]:
+        bsd[nm + ".weight"] = torch.randn(o, i, generator=g) / i ** 0.5
+        bsd[nm + ".bias"] = 0.1 * torch.randn(o, generator=g)
+    kvs = [torch.randn(L, 2 * D, generator=g) for L in Ls]
+    s1, c1, g1, s2, c2, g2 = (t.expand(B, D) for t in mod.view(6, D))
+    qkv = reference.linear(bsd, "qkv", reference.modulate(reference.layernorm(x0), s1, c1)).view(B, -1, 3, D)
+    x1 = x0 + g1[:, None] * reference.linear(bsd, "proj", reference.attention(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], 9))
+    q = reference.linear(bsd, "q", reference.layernorm(x1))
+    cx = torch.cat([reference.attention(q[b:b + 1], kvs[b][None, :, :D], kvs[b][None, :, D:], 9) for b in range(B)])
+    x2 = x1 + reference.linear(bsd, "cproj", cx)
+    mm = reference.linear(bsd, "fc2", F.gelu(reference.linear(bsd, "fc1", reference.modulate(reference.layernorm(x2), s2, c2)),
+                                            approximate="tanh"))
+    x3 = x2 + g2[:, None] * mm
+    ins = sha(torch.cat([x0.reshape(-1), mod] + [t.reshape(-1) for t in bsd.values()] + [t.reshape(-1) for t in kvs]))
+    d("dit_block_x1", x1, input_sha256=ins)
+    d("dit_block_x2", x2)
+    d("dit_block_x3", x3)
+    meta["cases"]["dit_block"] = {"B": B, "N": N, "D": D, "Ls": Ls, "seed": 111,
+                                  "inputs": "torch.Generator().manual_seed(111): x [2,64,576]; mod 0.5*randn [3456]; "
+                                            "qkv, proj, q, cproj, fc1, fc2: W randn/sqrt(in), b 0.1*randn; kv [L,1152] "
+                                            "per image"}
+
     d.save(**meta)
     print("wrote", args.out, len(d.index), "tensors")
 

@@ -270,3 +270,32 @@ def test_linear_python_argument_checks():
         supra_attn.linear(None, BASE_Q, BASE_B, N=4, K=4, M=1, resid=True)
     with pytest.raises(ValueError, match="needs resid"):
         supra_attn.linear(None, BASE_Q, BASE_B, N=4, K=4, M=1, out=BASE_O, gate=BASE_B)
+
+
+def test_linear_layernorm_and_act_descriptors():
+    """LayerNorm prologue (ops.layernorm's mod/shiftOff/scaleOff) and the act epilogue."""
+    ln = _lib.LayerNorm()
+    ln.eps = 1e-6
+    assert check_linear(linear_desc(ln=C.pointer(ln)))[0] == _lib.OK  # plain
+    mod = BASE_B + 4 * 900000
+    ln.mod, ln.mod_size, ln.shift_off, ln.scale_off = mod, 6 * 768, 0, 768
+    assert check_linear(linear_desc(ln=C.pointer(ln)))[0] == _lib.OK
+    for field, value, needle in [("scale_off", 5 * 768 + 1, "mod out of bounds"), ("shift_off", -1, "mod out of bounds"),
+                                 ("eps", float("nan"), "eps"), ("reserved", 1, "reserved"), ("mod", mod + 1, "aligned")]:
+        bad = _lib.LayerNorm()
+        C.pointer(bad)[0] = ln
+        setattr(bad, field, value)
+        st, msg = check_linear(linear_desc(ln=C.pointer(bad)))
+        assert st == _lib.EINVAL and needle in msg, (field, msg)
+    st, msg = check_linear(linear_desc(ln=C.pointer(ln), ldx=800, x_size=37 * 800))
+    assert st == _lib.EINVAL and "contiguous" in msg
+    gn = _lib.GroupNorm()
+    gn.gamma, gn.beta, gn.groups, gn.rows_per_image, gn.eps = BASE_B + 4 * 600000, BASE_B + 4 * 700000, 32, 37, 1e-6
+    st, msg = check_linear(linear_desc(ln=C.pointer(ln), gn=C.pointer(gn)))
+    assert st == _lib.EINVAL and "exclusive" in msg
+    for a in range(4):
+        assert check_linear(linear_desc(act=a))[0] == _lib.OK
+    st, msg = check_linear(linear_desc(act=4))
+    assert st == _lib.EINVAL and "act" in msg
+    with pytest.raises(ValueError, match="act"):
+        supra_attn.make_linear_desc(x=BASE_Q, w=BASE_B, y=BASE_O, M=1, N=4, K=4, act="relu")

@@ -279,3 +279,115 @@ def test_linear_in_place_is_ordered_after_readers(gpu):
     assert_close(gpu.read(o2), oracle.attention_ops(x1, x1, x1, L, L, 9, 64, D, D, D))
     for t in (o1, o2):
         t.release()
+
+
+# ---- one whole DiT block (app/models/dit.js:161-194) -----------------------------------------------
+def dit_block(gpu, x, mod, w, kvs, Ls, B, N, D=576):
+    """The reference's block with its LayerNorms folded into the products that follow them and its
+    residual updates done in place: 8 recorded products and attentions, no other op."""
+    import supra_attn
+
+    qkv = supra_attn.linear(gpu, x, w["qkv"], N=3 * D, K=D, bias=w["bqkv"],
+                            layernorm=dict(mod=mod, shiftOff=0, scaleOff=D))
+    a = gpu.empty([B * N, D])
+    for b in range(B):
+        r = b * N * 3 * D
+        supra_attn.attention(gpu, q=qkv, k=qkv, v=qkv, Lq=N, Lk=N, H=9, D=64, ldq=3 * D, ldk=3 * D, ldv=3 * D,
+                             qOff=r, kOff=r + D, vOff=r + 2 * D, oOff=b * N * D, out=a)
+    supra_attn.linear(gpu, a, w["proj"], N=D, K=D, bias=w["bproj"], out=x, resid=True, gate=mod, gOff=2 * D)
+    q = supra_attn.linear(gpu, x, w["q"], N=D, K=D, bias=w["bq"], layernorm={})
+    c = gpu.empty([B * N, D])
+    for b in range(B):
+        supra_attn.attention(gpu, q=q, k=kvs[b], v=kvs[b], Lq=N, Lk=Ls[b], H=9, D=64, ldq=D, ldk=2 * D, ldv=2 * D,
+                             qOff=b * N * D, kOff=0, vOff=D, oOff=b * N * D, out=c)
+    supra_attn.linear(gpu, c, w["cproj"], N=D, K=D, bias=w["bcproj"], out=x, resid=True)
+    f = supra_attn.linear(gpu, x, w["fc1"], N=4 * D, K=D, bias=w["bfc1"], act="gelu_tanh",
+                          layernorm=dict(mod=mod, shiftOff=3 * D, scaleOff=4 * D))
+    supra_attn.linear(gpu, f, w["fc2"], N=D, K=4 * D, bias=w["bfc2"], out=x, resid=True, gate=mod, gOff=5 * D)
+    return (qkv, a, q, c, f)
+
+
+def test_dit_block_golden(gpu, golden):
+    """One whole DiT block through the library against the reference's dit_forward pieces."""
+    from conftest import dit_block_inputs
+
+    x = dit_block_inputs()
+    B, N, D = x["B"], x["N"], x["D"]
+    w = {k: dev(v) for k, v in x["w"].items()}
+    mod, kvs = dev(x["mod"]), [dev(t) for t in x["kv"]]
+    xs = dev(x["x0"])
+    gpu.profile(True)
+    gpu.profile_reset()
+    tmp = dit_block(gpu, xs, mod, w, kvs, x["Ls"], B, N)
+    gpu.sync()
+    names = {r["name"] for r in gpu.profile_report()}
+    gpu.profile_reset()
+    gpu.profile(False)
+    assert {"layernorm_stats", "linear_fp32_bias"} <= names, names
+    assert_close(host(xs), golden("dit_block_x3"))
+    for t in tmp:
+        t.release()
+
+
+def test_dit_block_full_size(gpu):
+    """Four images of 256 tokens (the DiT step's shape, ragged prompts up to 128 tokens) against the
+    float64 oracle, each residual stage checked."""
+    rng = np.random.default_rng(1234)
+    B, N, D = 4, 256, 576
+    Ls = [1, 37, 128, 77]
+    wn = {}
+    for nm, (o, i) in [("qkv", (3 * D, D)), ("proj", (D, D)), ("q", (D, D)), ("cproj", (D, D)),
+                       ("fc1", (4 * D, D)), ("fc2", (D, 4 * D))]:
+        wn[nm] = (rng.standard_normal((o, i)) / np.sqrt(i)).astype(np.float32)
+        wn["b" + nm] = (0.1 * rng.standard_normal(o)).astype(np.float32)
+    x0 = rng.standard_normal((B, N, D)).astype(np.float32)
+    modn = (0.5 * rng.standard_normal(6 * D)).astype(np.float32)
+    kvn = [rng.standard_normal((L, 2 * D)).astype(np.float32) for L in Ls]
+    w = {k: dev(v) for k, v in wn.items()}
+    mod, kvs = dev(modn), [dev(t) for t in kvn]
+    xs = dev(x0)
+    tmp = dit_block(gpu, xs, mod, w, kvs, Ls, B, N)
+    gpu.sync()  # the last product is recorded until a flush; x is read outside the library
+    got = host(xs).reshape(B, N, D)
+    for b in range(B):
+        assert_close(got[b], oracle.dit_block(x0[b], modn, wn, kvn[b])[2])
+    for t in tmp:
+        t.release()
+
+
+@pytest.mark.parametrize("act", ["gelu", "gelu_tanh", "silu"])
+def test_linear_activations(gpu, act):
+    import supra_attn
+
+    rng = np.random.default_rng(len(act))
+    M, N, K = 140, 300, 72
+    xa = (2 * rng.standard_normal((M, K))).astype(np.float32)
+    wa = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    ba = rng.standard_normal(N).astype(np.float32)
+    xd, wd, bd = dev(xa), dev(wa), dev(ba)
+    y = supra_attn.linear(gpu, xd, wd, N=N, K=K, bias=bd, act=act)
+    got = gpu.read(y).reshape(M, N)
+    y.release()
+    ref = oracle.activation(oracle.linear(xa, wa, M, N, K, bias=ba).reshape(M, N).astype(np.float64), act)
+    assert_close(got, ref)
+
+
+@pytest.mark.parametrize("K", [61, 576])
+def test_linear_layernorm(gpu, K):
+    """Plain and modulated LayerNorm prologues on rows that do not fill a tile, K ragged or not."""
+    import supra_attn
+
+    rng = np.random.default_rng(K)
+    M, N = 333, 150
+    xa = (rng.standard_normal((M, K)) * 2 + 0.5).astype(np.float32)
+    wa = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    modn = rng.standard_normal(3 * K + 5).astype(np.float32)
+    xd, wd, md = dev(xa), dev(wa), dev(modn)
+    y1 = supra_attn.linear(gpu, xd, wd, N=N, K=K, layernorm={})
+    y2 = supra_attn.linear(gpu, xd, wd, N=N, K=K, layernorm=dict(mod=md, shiftOff=5, scaleOff=2 * K + 3))
+    got1, got2 = gpu.read(y1).reshape(M, N), gpu.read(y2).reshape(M, N)
+    w64 = wa.astype(np.float64)
+    assert_close(got1, oracle.layernorm(xa) @ w64.T)
+    assert_close(got2, oracle.layernorm(xa, modn, 5, 2 * K + 3) @ w64.T)
+    for t in (y1, y2):
+        t.release()

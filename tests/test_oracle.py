@@ -173,3 +173,34 @@ def test_dit_block_projections(golden):
         x2.append(oracle.gated_residual(x1[-1], x["c"][b], x["wc"], N, D, D, bias=x["bc"]))
     assert oracle.max_rel(np.stack(x1), golden("dit_proj_x1")) <= TOL
     assert oracle.max_rel(np.stack(x2), golden("dit_proj_x2")) <= TOL
+
+
+def test_dit_block(golden):
+    """oracle.dit_block (LayerNorm with adaLN modulation, q/k/v, self attention, gated projection,
+    LayerNorm, cross attention, projection, modulated LayerNorm, fc1 + GELU(tanh), gated fc2)
+    against the reference's dit_forward pieces on one whole block."""
+    from conftest import dit_block_inputs
+
+    x = dit_block_inputs()
+    assert hashlib.sha256(np.asarray(x["flat"], dtype="<f4").tobytes()).hexdigest() == \
+        golden.meta("dit_block_x1")["input_sha256"]
+    outs = [oracle.dit_block(x["x0"][b], x["mod"], x["w"], x["kv"][b]) for b in range(x["B"])]
+    for i in range(3):
+        assert oracle.max_rel(np.stack([o[i] for o in outs]), golden(f"dit_block_x{i + 1}")) <= TOL
+
+
+def test_layernorm_and_activations():
+    """oracle.layernorm / oracle.activation against torch's layer_norm and GELU / SiLU."""
+    import torch
+    import torch.nn.functional as F
+
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((7, 50)) * 3 + 1
+    mod = rng.standard_normal(200)
+    t = F.layer_norm(torch.from_numpy(x), (50,), eps=1e-6).numpy()
+    assert np.abs(oracle.layernorm(x) - t).max() < 1e-12
+    want = t * (1 + mod[100:150]) + mod[20:70]
+    assert np.abs(oracle.layernorm(x, mod, 20, 100) - want).max() < 1e-12
+    xt = torch.from_numpy(x)
+    for act, ref in [("gelu", F.gelu(xt)), ("gelu_tanh", F.gelu(xt, approximate="tanh")), ("silu", F.silu(xt))]:
+        assert np.abs(oracle.activation(x, act) - ref.numpy()).max() < 1e-12, act
