@@ -260,7 +260,7 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
 
     def run(name, units, unit_name, make_descs, flops, bytes_):
         res = {}
-        for variant in ("fp32", "tf32"):
+        for variant in ("fp32", "tf32", "tf32x3"):
             descs = make_descs(variant)
             gpu.enqueue_batch(descs)
             gpu.sync()
@@ -473,6 +473,80 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
                                      "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
                                      "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
                                      "kernels": sorted({r["name"] for r in prof})}}
+    del ctx, p, kv_all, wkv
+
+    # One whole DiT block (app/models/dit.js:161-194) for 32 images of 256 tokens with ragged
+    # prompts: LayerNorm (+ adaLN modulation) folded into the qkv / q / fc1 products, the residual
+    # updates in place with their gates, GELU(tanh) on fc1: 8 recorded calls, 6 products and the
+    # two attentions, plus the LayerNorm statistics. fp32 throughout.
+    nimg, N, D = 32, 256, 576
+    Lb = workload_lengths(nimg, seed + 7)
+    xb = torch.randn(nimg * N * D, device=dev, generator=g)
+    modb = 0.5 * torch.randn(6 * D, device=dev, generator=g)
+    wb = {}
+    for nm, (o, i) in [("qkv", (3 * D, D)), ("proj", (D, D)), ("q", (D, D)), ("cproj", (D, D)),
+                       ("fc1", (4 * D, D)), ("fc2", (D, 4 * D))]:
+        wb[nm] = torch.randn(o * i, device=dev, generator=g) * i ** -0.5
+        wb["b" + nm] = 0.1 * torch.randn(o, device=dev, generator=g)
+    kvb = [torch.randn(L * 2 * D, device=dev, generator=g) for L in Lb]
+    R = nimg * N
+    qkv_b, a_b, q_b, c_b, f_b = (torch.empty(R * n, device=dev) for n in (3 * D, D, D, D, 4 * D))
+    L = supra_attn.make_linear_desc
+    lin = [
+        L(x=xb, w=wb["qkv"], bias=wb["bqkv"], y=qkv_b, M=R, N=3 * D, K=D, layernorm=dict(mod=modb, shiftOff=0, scaleOff=D)),
+        L(x=a_b, w=wb["proj"], bias=wb["bproj"], y=xb, M=R, N=D, K=D, resid=True, gate=modb, gOff=2 * D),
+        L(x=xb, w=wb["q"], bias=wb["bq"], y=q_b, M=R, N=D, K=D, layernorm={}),
+        L(x=c_b, w=wb["cproj"], bias=wb["bcproj"], y=xb, M=R, N=D, K=D, resid=True),
+        L(x=xb, w=wb["fc1"], bias=wb["bfc1"], y=f_b, M=R, N=4 * D, K=D, act="gelu_tanh",
+          layernorm=dict(mod=modb, shiftOff=3 * D, scaleOff=4 * D)),
+        L(x=f_b, w=wb["fc2"], bias=wb["bfc2"], y=xb, M=R, N=D, K=4 * D, resid=True, gate=modb, gOff=5 * D),
+    ]
+    sa, ca = (supra_attn.Desc * nimg)(), (supra_attn.Desc * nimg)()
+    for b in range(nimg):
+        r = b * N * 3 * D
+        sa[b] = supra_attn.make_desc(q=qkv_b, k=qkv_b, v=qkv_b, out=a_b, Lq=N, Lk=N, H=9, D=64, ldq=3 * D, ldk=3 * D,
+                                     ldv=3 * D, qOff=r, kOff=r + D, vOff=r + 2 * D, oOff=b * N * D)
+        ca[b] = supra_attn.make_desc(q=q_b, k=kvb[b], v=kvb[b], out=c_b, Lq=N, Lk=Lb[b], H=9, D=64, ldq=D,
+                                     ldk=2 * D, ldv=2 * D, qOff=b * N * D, kOff=0, vOff=D, oOff=b * N * D)
+
+    def block():
+        e = lambda d: supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d)), gpu.ctx)
+        e(lin[0])
+        gpu.enqueue_batch(sa)
+        e(lin[1])
+        e(lin[2])
+        gpu.enqueue_batch(ca)
+        e(lin[3])
+        e(lin[4])
+        e(lin[5])
+        gpu.flush()
+
+    block()
+    gpu.sync()
+    gpu.profile(True)
+    gpu.profile_reset()
+    times = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        block()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    prof = gpu.profile_report()
+    gpu.profile(False)
+    ms = statistics.median(times)
+    lin_flops = 2.0 * R * D * (3 * D + D + D + D + 4 * D + 4 * D)
+    att_flops = 4.0 * N * D * (nimg * N + sum(Lb))
+    flops = lin_flops + att_flops
+    per = {}
+    for r in prof:
+        per[r["name"]] = per.get(r["name"], 0.0) + r["ms"] / reps
+    out["dit_block_32"] = {"fp32": {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                                    "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                                    "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}}
     return out
 
 
@@ -487,7 +561,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--no-tf32", action="store_true", help="skip the TF32 tensor-core pass")
+    ap.add_argument("--no-tf32", action="store_true", help="skip the tensor-core passes (tf32, tf32x3)")
     ap.add_argument("--no-sites", action="store_true", help="skip the per-call-site figures (configs[0..3])")
     args = ap.parse_args()
 
@@ -768,28 +842,28 @@ def main():
         down_gpu.close()
         del qkv2, qx2, oc2
 
-    # ---- the TF32 tensor-core variant on the same workload (its own tolerance, 2e-3) --------------
-    tf32 = None
-    if not args.no_tf32:
+    # ---- the tensor-core variants on the same workload: TF32 (its own tolerance, 2e-3) and the
+    # split-precision 3xTF32 (the FP32 bar, 1e-5) ---------------------------------------------------
+    def run_variant(code, dtype, tolerance, mma_per_flop):
         for arr in [self_d] + cross_d:
             for i in range(S):
-                arr[i].variant = supra_attn._lib.TF32
+                arr[i].variant = code
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
         if gather_stream is not None:
             gather_stream.synchronize()
-        clocks_tf = ClockSampler(uuid)
+        clocks_v = ClockSampler(uuid)
         gpu.profile(True)
         gpu.profile_reset()
         l0 = gpu.launch_count()
         barrier()
         torch.cuda.synchronize()
-        clocks_tf.start()
+        clocks_v.start()
         time.sleep(0.5)
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
-        clocks_tf.mark_begin()
+        clocks_v.mark_begin()
         t0.record()
         for _ in range(args.steps):
             step()
@@ -797,45 +871,57 @@ def main():
             torch.cuda.current_stream().wait_stream(gather_stream)
         t1.record()
         torch.cuda.synchronize()
-        clocks_tf.mark_end()
+        clocks_v.mark_end()
         time.sleep(0.3)
-        clk_tf = clocks_tf.stop()
+        clk_v = clocks_v.stop()
         barrier()
-        ltf = gpu.launch_count() - l0
-        prof_tf = gpu.profile_report()
+        lv = gpu.launch_count() - l0
+        prof_v = gpu.profile_report()
         gpu.profile(False)
         tt = torch.tensor([t0.elapsed_time(t1)], device=dev)
         if world > 1:
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_tf = float(tt.item())
-        top_tf = max(prof_tf, key=lambda r: r["ms"]) if prof_tf else None
-        roof_tf = None
-        if top_tf:
-            gbs = top_tf["bytes"] / (top_tf["ms"] / 1e3) / 1e9
+        ms_v = float(tt.item())
+        top = max(prof_v, key=lambda r: r["ms"]) if prof_v else None
+        roof = None
+        if top:
+            gbs = top["bytes"] / (top["ms"] / 1e3) / 1e9
             hbm = float(peaks.get("hbm_gbs", 6650.0))
             tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0  # TF32 dense rate is half of bf16
             traffic = None
             tf = os.path.join(ROOT, "profiles", "traffic.json")
             if os.path.exists(tf):
                 with open(tf) as f:
-                    tj = json.load(f).get(top_tf["name"])
+                    tj = json.load(f).get(top["name"])
                 if tj:
-                    traffic = tj["dram_bytes_per_alg_byte"] * top_tf["bytes"] / top_tf["count"]
-            roof_tf = {"bound": "hbm", "kernel": top_tf["name"], "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                       "frac": gbs / hbm, "traffic": traffic,
-                       "alg_bytes_per_launch": top_tf["bytes"] / top_tf["count"],
-                       "launch_ms": top_tf["ms"] / top_tf["count"],
-                       "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s",
-                       "tensor_tflops": top_tf["flops"] / (top_tf["ms"] / 1e3) / 1e12,
-                       "tensor_peak_tflops": tf_peak,
-                       "tensor_peak_source": "half of MEASURED_PEAKS.json bf16_tflops (TF32 dense = bf16 dense / 2)"}
-        tf32 = {"value": seq_calls / (ms_tf / 1e3), "unit": UNIT, "ms_per_step": ms_tf / args.steps,
-                "dtype": "tf32 operands, f32 accumulate", "tolerance": "max|d|/max|ref| and rel-L2 <= 2e-3",
-                "tflops": flops_total * args.steps / (ms_tf / 1e3) / 1e12, "gpu_launches": ltf, "clocks": clk_tf,
-                "roofline": roof_tf, "kernels": prof_tf}
+                    traffic = tj["dram_bytes_per_alg_byte"] * top["bytes"] / top["count"]
+            issued = mma_per_flop * top["flops"] / (top["ms"] / 1e3) / 1e12
+            roof = {"bound": "hbm", "kernel": top["name"], "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                    "frac": gbs / hbm, "traffic": traffic,
+                    "alg_bytes_per_launch": top["bytes"] / top["count"],
+                    "launch_ms": top["ms"] / top["count"],
+                    "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s",
+                    "tensor_tflops": issued, "tensor_peak_tflops": tf_peak, "tensor_frac": issued / tf_peak,
+                    "tensor_peak_source": "half of MEASURED_PEAKS.json bf16_tflops (TF32 dense = bf16 dense / 2)"}
+            if mma_per_flop > 1:  # tensor-bound: report the tensor roofline as the bound
+                roof.update({"bound": "tensor", "achieved": issued, "peak": tf_peak, "unit": "TFLOP/s",
+                             "frac": issued / tf_peak, "hbm_gbs_achieved": gbs, "hbm_peak_gbs": hbm,
+                             "note": f"{mma_per_flop} TF32 MMA FLOPs per algorithmic FLOP (hi/lo split)"})
+        res = {"value": seq_calls / (ms_v / 1e3), "unit": UNIT, "ms_per_step": ms_v / args.steps, "dtype": dtype,
+               "tolerance": tolerance, "tflops": flops_total * args.steps / (ms_v / 1e3) / 1e12, "gpu_launches": lv,
+               "clocks": clk_v, "roofline": roof, "kernels": prof_v}
         for arr in [self_d] + cross_d:
             for i in range(S):
                 arr[i].variant = supra_attn._lib.FP32
+        return res
+
+    variants = {}
+    if not args.no_tf32:
+        variants["tf32"] = run_variant(supra_attn._lib.TF32, "tf32 operands, f32 accumulate",
+                                       "max|d|/max|ref| and rel-L2 <= 2e-3", 1)
+        variants["tf32x3"] = run_variant(supra_attn._lib.TF32X3,
+                                         "f32 operands split hi+lo into 3 TF32 products, f32 accumulate",
+                                         "max|d|/max|ref| and rel-L2 <= 1e-5 (the FP32 bar)", 3)
 
     sites = None
     if rank == 0 and world == 1 and not args.no_sites:
@@ -863,7 +949,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
             "kernels": prof,
-            "variants": {"tf32": tf32} if tf32 else {},
+            "variants": variants,
             "call_sites": sites,
         }
         print(json.dumps(line), flush=True)

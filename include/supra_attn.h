@@ -55,6 +55,10 @@ extern "C" {
 /* ---- numeric variants -------------------------------------------------------------------- */
 #define SUPRA_ATTN_FP32 0 /* FFMA kernel, fp32 throughout: matches torch CPU fp32 to <=1e-5 */
 #define SUPRA_ATTN_TF32 1 /* tcgen05 tensor-core kernel with TF32 operands, fp32 accumulate */
+/* tcgen05 kernel with every operand split x = hi + lo (hi = TF32(x), lo = x - hi) and each
+ * product formed as lo*hi + hi*lo + hi*hi ("3xTF32"): fp32-class accuracy on the tensor cores.
+ * Same coverage as SUPRA_ATTN_TF32; other requests run the FP32 kernels. */
+#define SUPRA_ATTN_TF32X3 2
 
 /* ---- descriptor flags -------------------------------------------------------------------- */
 #define SUPRA_ATTN_F_DEFAULT_SCALE 0x1u /* ignore .scale, use 1/sqrt(D) (ops.js:109 default) */

@@ -28,6 +28,18 @@
 // 128-byte / 32-byte-atom swizzle (the MN-major TF32 operand layout); every CTA loads only its own tiles.
 // Every wait is bounded; on a timeout the CTA records the failure, drains the MMAs it issued,
 // frees its TMEM and leaves.
+//
+// Split precision (SPLIT = true, variant TF32X3): fp32-class accuracy from the same tensor cores.
+// The TMA copies the operands exactly (fp32 tensor maps). hi is x with its 13 low mantissa bits
+// cleared: the tensor core ignores those bits of a TF32 operand, so the landed K and V tiles
+// serve as their own hi parts, and two converter warps (6: K, 7: V) write lo = x - hi (exact)
+// into a second copy. The softmax threads split their Q rows into hi(Q) / lo(Q) in TMEM (the A
+// operand of S) and P the same way. K and V have separate rings, so the next K blocks land
+// while a V stage waits for its PV product. Every product is formed as
+// lo*hi + hi*lo + hi*hi (three TF32 MMAs, the small terms first), which leaves an error of about
+// 2^-21 relative per product. Each block's PV product goes into a fresh TMEM accumulator and the
+// softmax threads add it to O in fp32 registers (rounded to nearest), so the error does not grow
+// with the number of key blocks. One CTA per SM (the tiles take twice the shared memory).
 #include "tcgen05.cuh"
 
 namespace supra {
@@ -36,26 +48,47 @@ namespace {
 constexpr int kM = 128;  // query rows per tile (MMA M)
 constexpr int kN = 64;   // keys per block (MMA N of S)
 constexpr int kD = 64;   // head dim (MMA N of O)
-constexpr int kNS = 2;   // K/V stages
+constexpr int kNS = 2;   // K/V stages (split kernel: K stages)
+constexpr int kNSV = 3;  // split kernel: V stages (a V stage is held until its PV product is done)
 constexpr uint32_t kQSlab = kM * 128;   // one 32-column slab of the Q tile: 16 KB
 constexpr uint32_t kKVSlab = kN * 128;  // one 32-column slab of a K or V block: 8 KB
 constexpr uint32_t kQBytes = 2 * kQSlab;
 constexpr uint32_t kKVBytes = 2 * kKVSlab;  // one K (or V) block
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + kQBytes;
-constexpr uint32_t OFF_V = OFF_K + kNS * kKVBytes;
-constexpr uint32_t OFF_O = OFF_V + kNS * kKVBytes;  // epilogue staging: 2 KB per softmax warp
-constexpr uint32_t kOStage = 16 * 32 * 4;            // 16 rows x 32 columns of O
-constexpr uint32_t OFF_BAR = OFF_O + 4 * kOStage;
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;  // barriers + alignment slack for the 1024-B base
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kOStage = 16 * 32 * 4;   // epilogue staging: 16 rows x 32 columns of O per softmax warp
+
+// Shared memory, TMEM and threads of the plain (SPLIT = false) and split-precision kernels. The
+// split kernel keeps K and V tiles twice, hi (x with its low mantissa bits cleared) in place of
+// x and lo = x - hi beside it, in separate K and V rings: one CTA per SM, 512 TMEM columns
+// (S/hi(P) and lo(P) double buffers, a double-buffered per-block PV accumulator, hi(Q) and
+// lo(Q)), and a fourth role, the converter warps.
+template <bool SPLIT>
+struct Lay {
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t K = Q + kQBytes;
+  static constexpr uint32_t KL = K + kNS * kKVBytes;
+  static constexpr uint32_t V = SPLIT ? KL + kNS * kKVBytes : K + kNS * kKVBytes;
+  static constexpr uint32_t VL = V + kNSV * kKVBytes;
+  static constexpr uint32_t O = SPLIT ? VL + kNSV * kKVBytes : V + kNS * kKVBytes;
+  static constexpr uint32_t BAR = O + 4 * kOStage;
+  static constexpr uint32_t SMEM = BAR + 256 + 1024;  // barriers + alignment slack for the 1024-B base
+  static constexpr uint32_t TMEM_COLS = SPLIT ? 512 : 256;
+  static constexpr int THREADS = SPLIT ? 256 : 192;  // 8 warps: two per SM sub-partition, up to 255 registers
+  static constexpr int CTAS_PER_SM = SPLIT ? 1 : 2;
+};
+static_assert(Lay<true>::SMEM <= 227 * 1024 && 2 * Lay<false>::SMEM <= 228 * 1024, "shared memory");
 constexpr uint32_t COL_S0 = 0, COL_S1 = 64, COL_O = 128;
-constexpr int kThreads = 192;
+// split kernel: lo(P) double buffer, a fresh per-block PV accumulator, double-buffered (O itself
+// lives in the softmax threads' registers), and hi(Q) / lo(Q), the A operand of S
+constexpr uint32_t COL_PL0 = 128, COL_PL1 = 192, COL_OB0 = 256, COL_OB1 = 320, COL_QH = 384, COL_QL = 448;
+constexpr int kConv = 32;  // threads per converter warp (split kernel: warp 6 for K, warp 7 for V)
 
 // pv_done is double-buffered by block parity so that a waiter for PV_n never sees a barrier
 // that is two phases ahead or behind (PV_{n-2} is always complete when PV_n is awaited).
 struct Bars {
   uint64_t q_full, q_empty, kv_full[kNS], kv_empty[kNS], s_full[2], p_full[2], pv_done[2], o_empty, drain;
+  // split kernel: K and V flow through separate rings (kv_full / kv_empty / kv_conv serve K),
+  // and each landed tile is released to the MMA warp once its hi/lo parts are in place
+  uint64_t q_conv, kv_conv[kNS], v_full[kNSV], v_empty[kNSV], v_conv[kNSV];
   uint32_t tmem;
   int32_t abort;
 };
@@ -74,8 +107,20 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // Wait ids reported with a timeout (status[2]); status[3] carries the waiter's block counter.
 enum WaitId : int32_t {
   W_Q_EMPTY = 31, W_KV_EMPTY = 32, W_Q_FULL = 33, W_KV_FULL = 34, W_P_FULL = 35, W_O_EMPTY = 36,
-  W_S_FULL = 37, W_PV_RESCALE = 38, W_PV_EPILOGUE = 39,
+  W_S_FULL = 37, W_PV_RESCALE = 38, W_PV_EPILOGUE = 39, W_CONV_Q = 40, W_CONV_KV = 41,
 };
+
+// The split of the 3xTF32 scheme, x*y ~ hi(x)hi(y) + hi(x)lo(y) + lo(x)hi(y): hi = x with the
+// 13 low mantissa bits cleared (a TF32 value, so the tensor core takes it exactly) and
+// lo = x - hi, exact in fp32 and below 2^-10 |x|; the tensor core keeps 11 significant bits of
+// lo, so what is lost is below 2^-21 |x|. (Clearing bits is one logic op; a rounding convert
+// costs several instructions per element.)
+__device__ __forceinline__ float hi_of(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+__device__ __forceinline__ void split4(float4& x, float4& lo) {
+  const float4 h = make_float4(hi_of(x.x), hi_of(x.y), hi_of(x.z), hi_of(x.w));
+  lo = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+  x = h;
+}
 
 // Bounded wait that also gives up as soon as another warp of the CTA has aborted. The thread
 // whose own wait runs out reports which barrier it was and the block counter it waited for.
@@ -113,16 +158,21 @@ __device__ __forceinline__ Tile tile_of(const TmaLaunch& L, int t) {
   return r;
 }
 
-template <bool BIAS>
-__global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_constant__ TmaLaunch L) {
+template <bool BIAS, bool SPLIT>
+__global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
+    attn_tf32_kernel(const __grid_constant__ TmaLaunch L) {
+  using Y = Lay<SPLIT>;
+  constexpr uint32_t kTmemCols = Y::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned for the swizzle atoms
-  uint8_t* Qs = base + OFF_Q;
-  uint8_t* Ks = base + OFF_K;
-  uint8_t* Vs = base + OFF_V;
-  float* Os = reinterpret_cast<float*>(base + OFF_O);
-  Bars* B = reinterpret_cast<Bars*>(base + OFF_BAR);
+  uint8_t* Qs = base + Y::Q;
+  uint8_t* Ks = base + Y::K;
+  uint8_t* Vs = base + Y::V;
+  uint8_t* KLs = base + Y::KL;
+  uint8_t* VLs = base + Y::VL;
+  float* Os = reinterpret_cast<float*>(base + Y::O);
+  Bars* B = reinterpret_cast<Bars*>(base + Y::BAR);
   volatile int32_t* abort = &B->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -130,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
-    mbar_init(&B->q_empty, 1);
+    mbar_init(&B->q_empty, SPLIT ? 128 : 1);  // split kernel: the softmax threads release the Q tile
     for (int s = 0; s < kNS; ++s) {
       mbar_init(&B->kv_full[s], 1);
       mbar_init(&B->kv_empty[s], 1);
@@ -143,6 +193,13 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
     mbar_init(&B->pv_done[1], 1);
     mbar_init(&B->o_empty, 128);
     mbar_init(&B->drain, 1);
+    mbar_init(&B->q_conv, 128);  // split kernel: the softmax threads, one Q row each
+    for (int s = 0; s < kNS; ++s) mbar_init(&B->kv_conv[s], kConv);
+    for (int s = 0; s < kNSV; ++s) {
+      mbar_init(&B->v_full[s], 1);
+      mbar_init(&B->v_empty[s], 1);
+      mbar_init(&B->v_conv[s], kConv);
+    }
     B->abort = 0;
     mbar_fence_init();
   }
@@ -157,7 +214,27 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    if (SPLIT && lane == 1) {
+      // split kernel: the V ring, on its own lane so that K blocks run ahead of the V stages,
+      // which stay busy until their PV products are done
+      int n = 0;
+      for (int t = blockIdx.x; t < L.total; t += gridDim.x) {
+        const Tile T = tile_of(L, t);
+        const TmaProb* pp = T.p;
+        const CUtensorMap* mv = L.maps + pp->mv;
+        const int hx = T.h * kD;
+        bool ok = true;
+        for (int j = 0; j < T.nblk; ++j, ++n) {
+          const int s = n % kNSV;
+          if (n >= kNSV && !(ok = wait_or_abort(&B->v_empty[s], (uint32_t)(((n / kNSV) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
+          mbar_arrive_expect_tx(&B->v_full[s], kKVBytes);
+          uint8_t* vd = Vs + s * kKVBytes;
+          tc::tma_load_2d(vd, mv, pp->vx + hx, pp->vy + j * kN, &B->v_full[s]);
+          tc::tma_load_2d(vd + kKVSlab, mv, pp->vx + hx + 32, pp->vy + j * kN, &B->v_full[s]);
+        }
+        if (!ok) break;
+      }
+    } else if (lane == 0) {
       int n = 0, k = 0;
       for (int t = blockIdx.x; t < L.total; t += gridDim.x, ++k) {
         const Tile T = tile_of(L, t);
@@ -174,13 +251,15 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
         for (int j = 0; j < T.nblk; ++j, ++n) {
           const int s = n % kNS;
           if (n >= kNS && !(ok = wait_or_abort(&B->kv_empty[s], (uint32_t)(((n / kNS) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
-          mbar_arrive_expect_tx(&B->kv_full[s], 2 * kKVBytes);
+          mbar_arrive_expect_tx(&B->kv_full[s], SPLIT ? kKVBytes : 2 * kKVBytes);
           uint8_t* kd = Ks + s * kKVBytes;
           uint8_t* vd = Vs + s * kKVBytes;
           tc::tma_load_2d(kd, mk, pp->kx + hx, pp->ky + j * kN, &B->kv_full[s]);
           tc::tma_load_2d(kd + kKVSlab, mk, pp->kx + hx + 32, pp->ky + j * kN, &B->kv_full[s]);
-          tc::tma_load_2d(vd, mv, pp->vx + hx, pp->vy + j * kN, &B->kv_full[s]);
-          tc::tma_load_2d(vd + kKVSlab, mv, pp->vx + hx + 32, pp->vy + j * kN, &B->kv_full[s]);
+          if (!SPLIT) {
+            tc::tma_load_2d(vd, mv, pp->vx + hx, pp->vy + j * kN, &B->kv_full[s]);
+            tc::tma_load_2d(vd + kKVSlab, mv, pp->vx + hx + 32, pp->vy + j * kN, &B->kv_full[s]);
+          }
         }
         if (!ok) break;
       }
@@ -197,14 +276,17 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
     bool pend_first = false;
     auto issue_pv = [&]() -> bool {
       const int m = pend_n;
-      const int sp = m % kNS;
+      const int sp = m % (SPLIT ? kNSV : kNS);
       const int bp = m & 1;
       if (!__all_sync(0xffffffffu, wait_or_abort(&B->p_full[bp], (uint32_t)((m >> 1) & 1), abort, L.status, W_P_FULL, m))) return false;
-      if (pend_first && pend_k > 0 &&
+      if (SPLIT && !__all_sync(0xffffffffu, wait_or_abort(&B->v_conv[sp], (uint32_t)((m / kNSV) & 1), abort, L.status,
+                                                          W_KV_FULL, m)))
+        return false;
+      if (!SPLIT && pend_first && pend_k > 0 &&
           !__all_sync(0xffffffffu, wait_or_abort(&B->o_empty, (uint32_t)((pend_k - 1) & 1), abort, L.status, W_O_EMPTY, m)))
         return false;
       uint8_t* vb = Vs + sp * kKVBytes;
-      if (pend_nk < kN) {
+      if (!SPLIT && pend_nk < kN) {  // (the split kernel's converter zeroes these rows)
         // V rows past Lk meet P == 0; make them zeros (they may hold another sequence's data).
         // Whole 128-byte rows, so the swizzle inside a row does not matter.
         for (int idx = lane; idx < (kN - pend_nk) * 16; idx += 32) {
@@ -219,13 +301,29 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
       tc::fence_after_sync();
       if (lane == 0) {
         const uint32_t pcol = bp ? COL_S1 : COL_S0;
+        // V is MN-major: 32-column atoms kKVSlab apart (LBO), 4-key groups 512 B apart (SBO)
+        auto vdesc = [&](const uint8_t* v, int kk) {
+          return tc::smem_desc(v + kk * 1024, kKVSlab, 512, tc::kLayoutSW128Base32B);
+        };
+        if (SPLIT) {
+          // this block's P V into its own accumulator (the softmax threads add it to O in fp32):
+          // lo(P) hi(V) + hi(P) lo(V) + hi(P) hi(V), the small terms first
+          const uint32_t plcol = bp ? COL_PL1 : COL_PL0;
+          const uint32_t ob = tmem + (bp ? COL_OB1 : COL_OB0);
+          const uint8_t* vl = VLs + sp * kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < kN / 8; ++kk)
-          // V is MN-major: 32-column atoms kKVSlab apart (LBO), 4-key groups 512 B apart (SBO)
-          tc::mma_tf32_ts(tmem + COL_O, tmem + pcol + 8 * kk,
-                          tc::smem_desc(vb + kk * 1024, kKVSlab, 512, tc::kLayoutSW128Base32B), idPV,
-                          (!pend_first || kk > 0) ? 1u : 0u);
-        tc::commit(&B->kv_empty[sp]);
+          for (int kk = 0; kk < kN / 8; ++kk)
+            tc::mma_tf32_ts(ob, tmem + plcol + 8 * kk, vdesc(vb, kk), idPV, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kN / 8; ++kk) tc::mma_tf32_ts(ob, tmem + pcol + 8 * kk, vdesc(vl, kk), idPV, 1u);
+#pragma unroll
+          for (int kk = 0; kk < kN / 8; ++kk) tc::mma_tf32_ts(ob, tmem + pcol + 8 * kk, vdesc(vb, kk), idPV, 1u);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < kN / 8; ++kk)
+            tc::mma_tf32_ts(tmem + COL_O, tmem + pcol + 8 * kk, vdesc(vb, kk), idPV, (!pend_first || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(SPLIT ? &B->v_empty[sp] : &B->kv_empty[sp]);
         tc::commit(&B->pv_done[m & 1]);
       }
       __syncwarp();
@@ -235,24 +333,51 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
     for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
       const Tile T = tile_of(L, t);
       const int Lk = T.p->Lk;
-      ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)(k & 1), abort, L.status, W_Q_FULL, n));
+      // split kernel: the softmax threads split this tile's Q only after the previous tile's
+      // epilogue, which waits for that tile's last PV product: issue it first
+      if (SPLIT && pend_n >= 0) ok = issue_pv();
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, wait_or_abort(SPLIT ? &B->q_conv : &B->q_full, (uint32_t)(k & 1), abort, L.status,
+                                                 W_Q_FULL, n));
       for (int j = 0; ok && j < T.nblk; ++j, ++n) {
         const int s = n % kNS;
         const int b = n & 1;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&B->kv_full[s], (uint32_t)((n / kNS) & 1), abort, L.status, W_KV_FULL, n));
+        ok = __all_sync(0xffffffffu, wait_or_abort(SPLIT ? &B->kv_conv[s] : &B->kv_full[s], (uint32_t)((n / kNS) & 1),
+                                                   abort, L.status, W_KV_FULL, n));
         if (!ok) break;
         tc::fence_after_sync();
         if (lane == 0) {
           const uint8_t* kb = Ks + s * kKVBytes;
+          const uint32_t scol = tmem + (b ? COL_S1 : COL_S0);
+          auto s_product = [&](const uint8_t* q, const uint8_t* kk, bool first) {
 #pragma unroll
-          for (int k8 = 0; k8 < kD / 8; ++k8) {
-            const uint32_t off = (uint32_t)(k8 >> 2) * kQSlab + (uint32_t)(k8 & 3) * 32u;
-            const uint32_t offk = (uint32_t)(k8 >> 2) * kKVSlab + (uint32_t)(k8 & 3) * 32u;
-            tc::mma_tf32_ss(tmem + (b ? COL_S1 : COL_S0), tc::smem_desc(Qs + off, 16, 1024, tc::kLayoutSW128),
-                            tc::smem_desc(kb + offk, 16, 1024, tc::kLayoutSW128), idS, k8 > 0 ? 1u : 0u);
+            for (int k8 = 0; k8 < kD / 8; ++k8) {
+              const uint32_t off = (uint32_t)(k8 >> 2) * kQSlab + (uint32_t)(k8 & 3) * 32u;
+              const uint32_t offk = (uint32_t)(k8 >> 2) * kKVSlab + (uint32_t)(k8 & 3) * 32u;
+              tc::mma_tf32_ss(scol, tc::smem_desc(q + off, 16, 1024, tc::kLayoutSW128),
+                              tc::smem_desc(kk + offk, 16, 1024, tc::kLayoutSW128), idS, (!first || k8 > 0) ? 1u : 0u);
+            }
+          };
+          if (SPLIT) {
+            // S = lo(Q) hi(K) + hi(Q) lo(K) + hi(Q) hi(K), the small terms first; Q from TMEM
+            const uint8_t* kl = KLs + s * kKVBytes;
+            auto s_product_t = [&](uint32_t qcol, const uint8_t* kk, bool first) {
+#pragma unroll
+              for (int k8 = 0; k8 < kD / 8; ++k8) {
+                const uint32_t offk = (uint32_t)(k8 >> 2) * kKVSlab + (uint32_t)(k8 & 3) * 32u;
+                tc::mma_tf32_ts(scol, tmem + qcol + 8 * k8, tc::smem_desc(kk + offk, 16, 1024, tc::kLayoutSW128), idS,
+                                (!first || k8 > 0) ? 1u : 0u);
+              }
+            };
+            s_product_t(COL_QL, kb, true);
+            s_product_t(COL_QH, kl, false);
+            s_product_t(COL_QH, kb, false);
+            tc::commit(&B->kv_empty[s]);  // the K stage is free once S is done
+          } else {
+            s_product(Qs, kb, true);
           }
           tc::commit(&B->s_full[b]);
-          if (j == T.nblk - 1) tc::commit(&B->q_empty);  // the Q tile is no longer read
+          if (!SPLIT && j == T.nblk - 1) tc::commit(&B->q_empty);  // the Q tile is no longer read
         }
         __syncwarp();
         if (pend_n >= 0) ok = issue_pv();
@@ -264,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
     }
     if (ok && pend_n >= 0) ok = issue_pv();
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 21, n);
-  } else {
+  } else if (warp < 6) {
     // ---------------- softmax + epilogue (warps 2..5) ----------------
     const int q4 = warp & 3;
     const int row = 32 * q4 + lane;
@@ -272,12 +397,42 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
     bool ok = true;
     int n = 0;
     float v[64];
-    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
+    float o[SPLIT ? 64 : 1];  // split kernel: this thread's row of O
+    int kt = 0;               // this CTA's tile count
+    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++kt) {
       const Tile T = tile_of(L, t);
       const TmaProb* pp = T.p;
       const int Lk = pp->Lk, Lq = pp->Lq;
       const float sl2 = pp->scale_log2;
       float m = -INFINITY, l = 0.f;
+      if constexpr (SPLIT) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) o[c] = 0.f;
+        // this thread's Q row, split into hi / lo in TMEM (the A operand of S). The last S of
+        // the previous tile has completed (its scores were read), so the Q columns are free;
+        // the smem tile is released right after. Row r of a 32-column slab is 128 bytes at
+        // r * 128 with its 16-byte chunks swizzled by r % 8 (SWIZZLE_128B).
+        ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)(kt & 1), abort, L.status, W_CONV_Q, n));
+        if (!ok) break;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float hi[32], lo[32];
+          const uint8_t* qrow = Qs + hf * kQSlab + row * 128;
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            float4 x = *reinterpret_cast<const float4*>(qrow + ((c4 ^ (row & 7)) << 4)), l4;
+            split4(x, l4);
+            hi[4 * c4] = x.x, hi[4 * c4 + 1] = x.y, hi[4 * c4 + 2] = x.z, hi[4 * c4 + 3] = x.w;
+            lo[4 * c4] = l4.x, lo[4 * c4 + 1] = l4.y, lo[4 * c4 + 2] = l4.z, lo[4 * c4 + 3] = l4.w;
+          }
+          tc::tmem_st32(tl + COL_QH + 32 * hf, hi);
+          tc::tmem_st32(tl + COL_QL + 32 * hf, lo);
+          tc::tmem_wait_st();
+        }
+        tc::fence_before_sync();
+        mbar_arrive(&B->q_conv);
+        mbar_arrive(&B->q_empty);
+      }
       for (int j = 0; j < T.nblk; ++j, ++n) {
         const int b = n & 1;
         ok = __all_sync(0xffffffffu, wait_or_abort(&B->s_full[b], (uint32_t)((n >> 1) & 1), abort, L.status, W_S_FULL, n));
@@ -320,6 +475,51 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
           }
         }
         const bool move = mx > m + 8.f;
+        if constexpr (SPLIT) {
+          // O stays in registers: P_n goes out as hi (over S_n) and lo, then the previous
+          // block's accumulator, complete by now, is added in fp32 and the sum moved to the new
+          // offset: O = (O + OB_{n-1}) * 2^(m_old - m_new)
+          const float alpha = move ? ex2(m - mx) : 1.f;  // 0 on a tile's first block (m = -inf)
+          if (move) m = mx;
+          float ps = 0.f;
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            v[c] = ex2(v[c] - m);
+            ps += v[c];
+          }
+          l = l * alpha + ps;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float hi[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              hi[c] = hi_of(v[32 * hf + c]);
+              v[32 * hf + c] -= hi[c];
+            }
+            tc::tmem_st32(tl + scol + 32 * hf, hi);
+            tc::tmem_wait_st();
+          }
+          tc::tmem_st64(tl + (b ? COL_PL1 : COL_PL0), v);
+          tc::tmem_wait_st();
+          tc::fence_before_sync();
+          mbar_arrive(&B->p_full[b]);
+          if (j > 0) {
+            ok = __all_sync(0xffffffffu, wait_or_abort(&B->pv_done[(n - 1) & 1], (uint32_t)(((n - 1) >> 1) & 1), abort,
+                                                       L.status, W_PV_RESCALE, n));
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t ob = tl + (((n - 1) & 1) ? COL_OB1 : COL_OB0);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              float ad[32];
+              tc::tmem_ld32(ob + 32 * hf, ad);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) o[32 * hf + c] = (o[32 * hf + c] + ad[c]) * alpha;
+            }
+          }
+          continue;
+        }
         if (j > 0 && __any_sync(0xffffffffu, move)) {
           // O holds this tile's PV products up to block n-1: wait for it, rescale the moved rows
           ok = __all_sync(0xffffffffu, wait_or_abort(&B->pv_done[(n - 1) & 1], (uint32_t)(((n - 1) >> 1) & 1), abort,
@@ -356,10 +556,22 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
                                                  L.status, W_PV_EPILOGUE, n));
       if (!ok) break;
       tc::fence_after_sync();
-      tc::tmem_ld64(tl + COL_O, v);
-      tc::tmem_wait_ld();
-      tc::fence_before_sync();
-      mbar_arrive(&B->o_empty);  // the next tile's first PV may overwrite O
+      if constexpr (SPLIT) {
+        const uint32_t ob = tl + (((n - 1) & 1) ? COL_OB1 : COL_OB0);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float ad[32];
+          tc::tmem_ld32(ob + 32 * hf, ad);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[32 * hf + c] = o[32 * hf + c] + ad[c];
+        }
+      } else {
+        tc::tmem_ld64(tl + COL_O, v);
+        tc::tmem_wait_ld();
+        tc::fence_before_sync();
+        mbar_arrive(&B->o_empty);  // the next tile's first PV may overwrite O
+      }
       // O / l, stored coalesced: each thread holds its own row, so the warp's 32 x 64 block goes
       // through a 16 x 32 shared-memory slot (16-byte chunks swizzled by row) in four rounds and
       // every store instruction writes four whole 128-byte row segments.
@@ -395,6 +607,60 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
       }
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 22, n);
+  } else if (SPLIT) {
+    // ---------------- converters (split kernel): warp 6 for K, warp 7 for V ----------------
+    // Each landed tile x is its own hi part; lo = x - hi goes into the lo copy (same offsets, so
+    // the same swizzled layout). V rows past Lk become zeros in both parts: they meet P == 0 but
+    // may hold another sequence's data. Then the generic-proxy writes are made visible to the
+    // tensor core and the MMA warp is released.
+    const bool vconv = warp == 7;
+    bool ok = true;
+    int n = 0, k = 0;
+    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
+      const Tile T = tile_of(L, t);
+      const int Lk = T.p->Lk;
+      for (int j = 0; ok && j < T.nblk; ++j, ++n) {
+        const int ns = vconv ? kNSV : kNS;
+        const int s = n % ns;
+        const uint32_t par = (uint32_t)((n / ns) & 1);
+        ok = __all_sync(0xffffffffu, wait_or_abort(vconv ? &B->v_full[s] : &B->kv_full[s], par, abort, L.status,
+                                                   W_CONV_KV, n));
+        if (!ok) break;
+        const int nk = min(kN, Lk - j * kN);
+        float4* xb = reinterpret_cast<float4*>((vconv ? Vs : Ks) + s * kKVBytes);
+        float4* xl = reinterpret_cast<float4*>((vconv ? VLs : KLs) + s * kKVBytes);
+        // batches of 8 chunks per lane: all loads before any store (the stores write the same
+        // array, so the compiler would not move later loads above them). The tensor core reads a
+        // TF32 operand from the high 19 bits of its 32-bit container and ignores the 13 low
+        // mantissa bits, so the landed x already serves as hi; only lo = x - hi is written
+        // (and rows of V past Lk are zeroed in both copies).
+        constexpr int kPer = (int)(kKVBytes / 16) / kConv;  // 32 chunks per lane
+#pragma unroll 1
+        for (int b0 = 0; b0 < kPer; b0 += 8) {
+          float4 x[8], lo[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) x[r] = xb[lane + kConv * (b0 + r)];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const int i = lane + kConv * (b0 + r);
+            // a 16-byte chunk of V: slab i / 512, key row (i % 512) / 8 (128-byte rows)
+            if (!vconv || ((i & 511) >> 3) < nk) {
+              split4(x[r], lo[r]);
+            } else {
+              x[r] = lo[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            if (vconv && ((lane + kConv * (b0 + r)) & 511) >> 3 >= nk) xb[lane + kConv * (b0 + r)] = x[r];
+            xl[lane + kConv * (b0 + r)] = lo[r];
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(vconv ? &B->v_conv[s] : &B->kv_conv[s]);
+      }
+    }
+    if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 23, n);
   }
 
   tc::fence_before_sync();
@@ -417,16 +683,23 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tf32_kernel(const __grid_con
 
 int attn_tf32_tile_rows() { return kM; }
 
-cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, cudaStream_t s) {
-  if (L.total <= 0) return cudaSuccess;
-  auto k = bias ? attn_tf32_kernel<true> : attn_tf32_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+template <bool SPLIT>
+cudaError_t launch_tf32(const TmaLaunch& L, bool bias, cudaStream_t s) {
+  using Y = Lay<SPLIT>;
+  auto k = bias ? attn_tf32_kernel<true, SPLIT> : attn_tf32_kernel<false, SPLIT>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Y::SMEM);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = L.total < 2 * sms ? L.total : 2 * sms;  // persistent: two CTAs per SM
-  k<<<grid, kThreads, SMEM_BYTES, s>>>(L);
+  const int slots = Y::CTAS_PER_SM * sms;  // persistent
+  const int grid = L.total < slots ? L.total : slots;
+  k<<<grid, Y::THREADS, Y::SMEM, s>>>(L);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, bool split, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
+  return split ? launch_tf32<true>(L, bias, s) : launch_tf32<false>(L, bias, s);
 }
 
 }  // namespace supra

@@ -116,7 +116,7 @@ struct TmaLaunch {
   int32_t* status;
 };
 
-cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, cudaStream_t s);
+cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, bool split, cudaStream_t s);
 int attn_tf32_tile_rows();
 
 // Persistent FP32 kernel (attn_fp32_warp.cu): D = 64, no bias, scale > 0. Q and K tensor maps

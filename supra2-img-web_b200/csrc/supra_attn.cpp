@@ -388,7 +388,7 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   if (!d) return set_err(c, SUPRA_ATTN_EINVAL, "descriptor is NULL");
   if (d->flags & ~(SUPRA_ATTN_F_DEFAULT_SCALE | SUPRA_ATTN_F_T5_TABLE))
     return set_err(c, SUPRA_ATTN_EINVAL, "unknown flag bits 0x%x", d->flags);
-  if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
+  if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32 && d->variant != SUPRA_ATTN_TF32X3)
     return set_err(c, SUPRA_ATTN_EINVAL, "unknown variant %d", d->variant);
   if (d->Lq < 0 || d->Lq > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lq=%d out of range [0, 2^30]", d->Lq);
   if (d->Lk < 1 || d->Lk > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "Lk=%d out of range [1, 2^30]", d->Lk);
@@ -519,12 +519,12 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
                       aligned16(d->v) && d->q_off % 4 == 0 && d->k_off % 4 == 0 && d->v_off % 4 == 0 &&
                       rows_ok(d->q_off, d->ldq, q.rows_q, d->Lq, HD) && rows_ok(d->k_off, d->ldk, q.rows_k, d->Lk, HD) &&
                       rows_ok(d->v_off, d->ldv, q.rows_v, d->Lk, HD);
-  if (d->variant == SUPRA_ATTN_TF32) {
-    // Other TF32 requests run the FP32 kernels, which are at least as accurate (a bias is read
-    // directly by the tensor-core kernel).
+  if (d->variant == SUPRA_ATTN_TF32 || d->variant == SUPRA_ATTN_TF32X3) {
+    // Other tensor-core requests run the FP32 kernels, which are at least as accurate (a bias is
+    // read directly by the tensor-core kernel). cfg 1: the split-precision form.
     if (tma_ok) {
       q.path = PATH_TF32;
-      q.cfg = 0;
+      q.cfg = d->variant == SUPRA_ATTN_TF32X3 ? 1 : 0;
     }
   } else if (tma_ok && !q.bias && scale > 0.f && d->Lq > 64 && d->ldq >= supra::kFwBoxWide &&
              d->ldk >= supra::kFwBoxWide) {
@@ -541,7 +541,7 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   if (!d) return set_err(c, SUPRA_ATTN_EINVAL, "linear descriptor is NULL");
   if (d->flags) return set_err(c, SUPRA_ATTN_EINVAL, "linear: flags must be 0");
   if (d->act > SUPRA_ATTN_ACT_SILU) return set_err(c, SUPRA_ATTN_EINVAL, "linear: act=%u unknown", d->act);
-  if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32)
+  if (d->variant != SUPRA_ATTN_FP32 && d->variant != SUPRA_ATTN_TF32 && d->variant != SUPRA_ATTN_TF32X3)
     return set_err(c, SUPRA_ATTN_EINVAL, "linear: unknown variant %d", d->variant);
   if (d->M < 0 || d->M > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "linear: M=%d out of range [0, 2^30]", d->M);
   if (d->N < 1 || d->N > (1 << 30)) return set_err(c, SUPRA_ATTN_EINVAL, "linear: N=%d out of range [1, 2^30]", d->N);
@@ -937,6 +937,8 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
 // context and cached; problems refer to maps by index.
 int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   const int mrows = tf32 ? supra::attn_tf32_tile_rows() : supra::attn_fp32_warp_tile_rows();
+  // the split kernel needs the operands exactly: fp32 maps with the tensor-core swizzles
+  const bool split = tf32 && g[0]->cfg == 1;
   std::stable_sort(g.begin(), g.end(), [](const Queued* a, const Queued* b) { return a->p.Lk > b->p.Lk; });
   const int n = (int)g.size();
   std::vector<supra::TmaProb> probs((size_t)n);
@@ -946,7 +948,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   int32_t last_idx = -1;
   auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box_cols, int32_t box_rows,
                        CUtensorMapSwizzle swz, int32_t* out) -> int {
-    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, box_cols, box_rows, (int32_t)swz, tf32 ? 1 : 0};
+    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, box_cols, box_rows, (int32_t)swz, (tf32 && !split) ? 1 : 0};
     if (last_idx >= 0 && k == last_key) {
       *out = last_idx;
       return SUPRA_ATTN_OK;
@@ -1051,11 +1053,13 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     if (uni) L.uniform = (int32_t)t0;
   }
   L.status = c->d_status;
-  const char* name = !tf32 ? "attn_fp32_d64_tma" : g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64";
+  const char* name = !tf32  ? "attn_fp32_d64_tma"
+                     : split ? (g[0]->bias ? "attn_tf32x3_d64_bias" : "attn_tf32x3_d64")
+                             : (g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64");
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = tf32 ? supra::launch_attn_tf32(L, g[0]->bias, c->stream) : supra::launch_attn_fp32_warp(L, c->stream);
+    e = tf32 ? supra::launch_attn_tf32(L, g[0]->bias, split, c->stream) : supra::launch_attn_fp32_warp(L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;

@@ -13,7 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("SUPRA_ATTN_LIB", os.path.join(_HERE, "libsupra_attn.so"))
 
 OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, EDEVICE, ESTATE = range(7)
-FP32, TF32 = 0, 1
+FP32, TF32, TF32X3 = 0, 1, 2
 F_DEFAULT_SCALE = 0x1
 F_T5_TABLE = 0x2
 

@@ -26,7 +26,7 @@ import numpy as np
 from . import _lib
 from ._lib import Desc, GroupNorm, LayerNorm, LinearDesc, ProfileEntry, check, lib
 
-VARIANTS = {"fp32": _lib.FP32, "tf32": _lib.TF32}
+VARIANTS = {"fp32": _lib.FP32, "tf32": _lib.TF32, "tf32x3": _lib.TF32X3}
 ACTS = {None: 0, "gelu": 1, "gelu_tanh": 2, "silu": 3}  # SUPRA_ATTN_ACT_*
 
 
