@@ -92,7 +92,7 @@ typedef struct supra_attn_desc {
   int64_t q_off, k_off, v_off, o_off;
   int32_t Lq, Lk, H, D;
   float scale;
-  int32_t variant; /* SUPRA_ATTN_FP32 or SUPRA_ATTN_TF32 */
+  int32_t variant; /* SUPRA_ATTN_FP32, SUPRA_ATTN_TF32 or SUPRA_ATTN_TF32X3 */
   uint32_t flags;  /* SUPRA_ATTN_F_* */
   uint32_t bias_param; /* with SUPRA_ATTN_F_T5_TABLE: buckets | max_distance << 16; else 0 */
 } supra_attn_desc;
@@ -160,7 +160,7 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  * tracking, one grouped launch per flush). x: M rows of K floats, row stride ldx, first row at
  * x_off; w: [N, K] row-major with row stride ldw >= K (the reference's weight layout, x @ W^T);
  * bias: N floats or NULL; y: M rows of N floats, row stride ldy >= N, first row at y_off. All
- * counts in floats. Computed in fp32 with FFMA (a TF32 request runs the same kernel).
+ * counts in floats. Computed in fp32 with FFMA (TF32 and TF32X3 requests run the same kernel).
  * Two optional fusions (the VAE mid-block attention, app/models/vae.js:77-94):
  *   - gn != NULL: x is GroupNorm-ed on the way in (ops.groupnorm, app/gpu/ops.js:82-92,
  *     app/gpu/kernels.js:117-162): x rows form images of gn->rows_per_image rows; per image and

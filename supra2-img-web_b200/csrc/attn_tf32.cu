@@ -39,7 +39,10 @@
 // lo*hi + hi*lo + hi*hi (three TF32 MMAs, the small terms first), which leaves an error of about
 // 2^-21 relative per product. Each block's PV product goes into a fresh TMEM accumulator and the
 // softmax threads add it to O in fp32 registers (rounded to nearest), so the error does not grow
-// with the number of key blocks. One CTA per SM (the tiles take twice the shared memory).
+// with the number of key blocks. Q is double-buffered in TMEM: the next tile's Q rows are split
+// right after the current tile's last P, so the tensor core starts the next tile while the
+// epilogue runs (the MMA warp issues a tile's last PV before waiting for the next Q). One CTA
+// per SM (the tiles take twice the shared memory).
 #include "tcgen05.cuh"
 
 namespace supra {
@@ -59,8 +62,8 @@ constexpr uint32_t kOStage = 16 * 32 * 4;   // epilogue staging: 16 rows x 32 co
 // Shared memory, TMEM and threads of the plain (SPLIT = false) and split-precision kernels. The
 // split kernel keeps K and V tiles twice, hi (x with its low mantissa bits cleared) in place of
 // x and lo = x - hi beside it, in separate K and V rings: one CTA per SM, 512 TMEM columns
-// (S/hi(P) and lo(P) double buffers, a double-buffered per-block PV accumulator, hi(Q) and
-// lo(Q)), and a fourth role, the converter warps.
+// (S/hi(P) double buffer, lo(P), the per-block PV accumulator and two hi(Q) | lo(Q) buffers),
+// and a fourth role, the converter warps.
 template <bool SPLIT>
 struct Lay {
   static constexpr uint32_t Q = 0;
@@ -77,9 +80,11 @@ struct Lay {
 };
 static_assert(Lay<true>::SMEM <= 227 * 1024 && 2 * Lay<false>::SMEM <= 228 * 1024, "shared memory");
 constexpr uint32_t COL_S0 = 0, COL_S1 = 64, COL_O = 128;
-// split kernel: lo(P) double buffer, a fresh per-block PV accumulator, double-buffered (O itself
-// lives in the softmax threads' registers), and hi(Q) / lo(Q), the A operand of S
-constexpr uint32_t COL_PL0 = 128, COL_PL1 = 192, COL_OB0 = 256, COL_OB1 = 320, COL_QH = 384, COL_QL = 448;
+// split kernel: lo(P), a fresh per-block PV accumulator (O itself lives in the softmax threads'
+// registers), and two buffers of hi(Q) | lo(Q) (64 + 64 columns), the A operand of S, so the
+// next tile's Q is split before the current tile's epilogue
+constexpr uint32_t COL_PL = 128, COL_OB = 192, COL_Q0 = 256, COL_Q1 = 384;
+constexpr int kBatch = 8;  // converter: 16-byte chunks per lane loaded before any is stored
 constexpr int kConv = 32;  // threads per converter warp (split kernel: warp 6 for K, warp 7 for V)
 
 // pv_done is double-buffered by block parity so that a waiter for PV_n never sees a barrier
@@ -118,7 +123,10 @@ enum WaitId : int32_t {
 __device__ __forceinline__ float hi_of(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
 __device__ __forceinline__ void split4(float4& x, float4& lo) {
   const float4 h = make_float4(hi_of(x.x), hi_of(x.y), hi_of(x.z), hi_of(x.w));
-  lo = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+  const float2 neg1 = make_float2(-1.f, -1.f);  // x - hi as packed f32x2 FFMAs (exact)
+  const float2 a = __ffma2_rn(make_float2(h.x, h.y), neg1, make_float2(x.x, x.y));
+  const float2 b = __ffma2_rn(make_float2(h.z, h.w), neg1, make_float2(x.z, x.w));
+  lo = make_float4(a.x, a.y, b.x, b.y);
   x = h;
 }
 
@@ -156,6 +164,27 @@ __device__ __forceinline__ Tile tile_of(const TmaLaunch& L, int t) {
   r.q0 = (local - r.h * q_tiles) * kM;
   r.nblk = (r.p->Lk + kN - 1) / kN;
   return r;
+}
+
+// Split kernel, softmax threads: this thread's row of the landed Q tile (row r of a 32-column
+// slab is 128 bytes at r * 128, its 16-byte chunks swizzled by r % 8: SWIZZLE_128B) into hi(Q)
+// at column qh and lo(Q) at qh + 64 of its TMEM lane.
+__device__ __forceinline__ void split_q_row(const uint8_t* Qs, int row, uint32_t taddr_qh) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    float hi[32], lo[32];
+    const uint8_t* qrow = Qs + hf * kQSlab + row * 128;
+#pragma unroll
+    for (int c4 = 0; c4 < 8; ++c4) {
+      float4 x = *reinterpret_cast<const float4*>(qrow + ((c4 ^ (row & 7)) << 4)), l4;
+      split4(x, l4);
+      hi[4 * c4] = x.x, hi[4 * c4 + 1] = x.y, hi[4 * c4 + 2] = x.z, hi[4 * c4 + 3] = x.w;
+      lo[4 * c4] = l4.x, lo[4 * c4 + 1] = l4.y, lo[4 * c4 + 2] = l4.z, lo[4 * c4 + 3] = l4.w;
+    }
+    tc::tmem_st32(taddr_qh + 32 * hf, hi);
+    tc::tmem_st32(taddr_qh + 64 + 32 * hf, lo);
+    tc::tmem_wait_st();
+  }
 }
 
 template <bool BIAS, bool SPLIT>
@@ -308,8 +337,8 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         if (SPLIT) {
           // this block's P V into its own accumulator (the softmax threads add it to O in fp32):
           // lo(P) hi(V) + hi(P) lo(V) + hi(P) hi(V), the small terms first
-          const uint32_t plcol = bp ? COL_PL1 : COL_PL0;
-          const uint32_t ob = tmem + (bp ? COL_OB1 : COL_OB0);
+          const uint32_t plcol = COL_PL;
+          const uint32_t ob = tmem + COL_OB;
           const uint8_t* vl = VLs + sp * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < kN / 8; ++kk)
@@ -369,9 +398,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
                                 (!first || k8 > 0) ? 1u : 0u);
               }
             };
-            s_product_t(COL_QL, kb, true);
-            s_product_t(COL_QH, kl, false);
-            s_product_t(COL_QH, kb, false);
+            const uint32_t qh = (k & 1) ? COL_Q1 : COL_Q0, ql = qh + 64;
+            s_product_t(ql, kb, true);
+            s_product_t(qh, kl, false);
+            s_product_t(qh, kb, false);
             tc::commit(&B->kv_empty[s]);  // the K stage is free once S is done
           } else {
             s_product(Qs, kb, true);
@@ -408,30 +438,16 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       if constexpr (SPLIT) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) o[c] = 0.f;
-        // this thread's Q row, split into hi / lo in TMEM (the A operand of S). The last S of
-        // the previous tile has completed (its scores were read), so the Q columns are free;
-        // the smem tile is released right after. Row r of a 32-column slab is 128 bytes at
-        // r * 128 with its 16-byte chunks swizzled by r % 8 (SWIZZLE_128B).
-        ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)(kt & 1), abort, L.status, W_CONV_Q, n));
-        if (!ok) break;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float hi[32], lo[32];
-          const uint8_t* qrow = Qs + hf * kQSlab + row * 128;
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            float4 x = *reinterpret_cast<const float4*>(qrow + ((c4 ^ (row & 7)) << 4)), l4;
-            split4(x, l4);
-            hi[4 * c4] = x.x, hi[4 * c4 + 1] = x.y, hi[4 * c4 + 2] = x.z, hi[4 * c4 + 3] = x.w;
-            lo[4 * c4] = l4.x, lo[4 * c4 + 1] = l4.y, lo[4 * c4 + 2] = l4.z, lo[4 * c4 + 3] = l4.w;
-          }
-          tc::tmem_st32(tl + COL_QH + 32 * hf, hi);
-          tc::tmem_st32(tl + COL_QL + 32 * hf, lo);
-          tc::tmem_wait_st();
+        if (kt == 0) {
+          // the first tile's Q; later tiles' Q rows are split during the previous tile's last
+          // block (into the other Q buffer), and the smem tile is released right after
+          ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, 0u, abort, L.status, W_CONV_Q, n));
+          if (!ok) break;
+          split_q_row(Qs, row, tl + COL_Q0);
+          tc::fence_before_sync();
+          mbar_arrive(&B->q_conv);
+          mbar_arrive(&B->q_empty);
         }
-        tc::fence_before_sync();
-        mbar_arrive(&B->q_conv);
-        mbar_arrive(&B->q_empty);
       }
       for (int j = 0; j < T.nblk; ++j, ++n) {
         const int b = n & 1;
@@ -466,6 +482,18 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
             v[c] = x;
             mx = fmaxf(mx, x);
           }
+        } else if constexpr (!BIAS) {
+          // no bias: the scores stay raw and the scale goes into the exponent's FFMA below; with
+          // scale > 0 the raw row maximum times the scale is the scaled maximum. Keys past Lk
+          // only in a ragged block (warp-uniform test).
+          if (nk < kN) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) v[c] = (c < nk) ? v[c] : -INFINITY;
+          }
+          float rm = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 64; ++c) rm = fmaxf(rm, v[c]);
+          mx = rm * sl2;
         } else {
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
@@ -474,49 +502,79 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
             mx = fmaxf(mx, x);
           }
         }
+        const float vs = BIAS ? 1.f : sl2;  // exponent = v * vs - m
         const bool move = mx > m + 8.f;
         if constexpr (SPLIT) {
-          // O stays in registers: P_n goes out as hi (over S_n) and lo, then the previous
-          // block's accumulator, complete by now, is added in fp32 and the sum moved to the new
-          // offset: O = (O + OB_{n-1}) * 2^(m_old - m_new)
+          // O stays in registers: hi(P_n) goes over S_n; then the previous block's accumulator
+          // (its PV product is done once lo(P) may be overwritten) is added in fp32 and the sum
+          // moved to the new offset, O = (O + OB_{n-1}) * 2^(m_old - m_new); then lo(P_n).
+          // (pairs of columns go through the packed f32x2 FFMA / FADD / FMUL, same rounding)
           const float alpha = move ? ex2(m - mx) : 1.f;  // 0 on a tile's first block (m = -inf)
           if (move) m = mx;
-          float ps = 0.f;
+          const float2 vs2 = make_float2(vs, vs), nm2 = make_float2(-m, -m);
+          float2 ps2 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            v[c] = ex2(v[c] - m);
-            ps += v[c];
+          for (int c = 0; c < 64; c += 2) {
+            float2 a = __ffma2_rn(make_float2(v[c], v[c + 1]), vs2, nm2);
+            a.x = ex2(a.x);
+            a.y = ex2(a.y);
+            v[c] = a.x;
+            v[c + 1] = a.y;
+            ps2 = __fadd2_rn(ps2, a);
           }
-          l = l * alpha + ps;
+          l = l * alpha + (ps2.x + ps2.y);
+          const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             float hi[32];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              hi[c] = hi_of(v[32 * hf + c]);
-              v[32 * hf + c] -= hi[c];
+            for (int c = 0; c < 32; c += 2) {
+              const float2 x = make_float2(v[32 * hf + c], v[32 * hf + c + 1]);
+              const float2 h = make_float2(hi_of(x.x), hi_of(x.y));
+              const float2 lo = __ffma2_rn(h, neg1, x);  // x - hi, exact
+              hi[c] = h.x;
+              hi[c + 1] = h.y;
+              v[32 * hf + c] = lo.x;
+              v[32 * hf + c + 1] = lo.y;
             }
             tc::tmem_st32(tl + scol + 32 * hf, hi);
             tc::tmem_wait_st();
           }
-          tc::tmem_st64(tl + (b ? COL_PL1 : COL_PL0), v);
-          tc::tmem_wait_st();
-          tc::fence_before_sync();
-          mbar_arrive(&B->p_full[b]);
           if (j > 0) {
             ok = __all_sync(0xffffffffu, wait_or_abort(&B->pv_done[(n - 1) & 1], (uint32_t)(((n - 1) >> 1) & 1), abort,
                                                        L.status, W_PV_RESCALE, n));
             if (!ok) break;
             tc::fence_after_sync();
-            const uint32_t ob = tl + (((n - 1) & 1) ? COL_OB1 : COL_OB0);
+            const uint32_t ob = tl + COL_OB;
+            const bool moved = !__all_sync(0xffffffffu, alpha == 1.f);
+            const float2 al2 = make_float2(alpha, alpha);
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               float ad[32];
               tc::tmem_ld32(ob + 32 * hf, ad);
               tc::tmem_wait_ld();
 #pragma unroll
-              for (int c = 0; c < 32; ++c) o[32 * hf + c] = (o[32 * hf + c] + ad[c]) * alpha;
+              for (int c = 0; c < 32; c += 2) {
+                float2 x = __fadd2_rn(make_float2(o[32 * hf + c], o[32 * hf + c + 1]), make_float2(ad[c], ad[c + 1]));
+                if (moved) x = __fmul2_rn(x, al2);
+                o[32 * hf + c] = x.x;
+                o[32 * hf + c + 1] = x.y;
+              }
             }
+          }
+          tc::tmem_st64(tl + COL_PL, v);
+          tc::tmem_wait_st();
+          tc::fence_before_sync();
+          mbar_arrive(&B->p_full[b]);
+          if (j == T.nblk - 1 && t + (int)gridDim.x < L.total) {
+            // the next tile's Q, into the other buffer, before this tile's epilogue: the tensor
+            // core can start the next tile while the epilogue runs
+            ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)((kt + 1) & 1), abort, L.status, W_CONV_Q, n));
+            if (!ok) break;
+            split_q_row(Qs, row, tl + (((kt + 1) & 1) ? COL_Q1 : COL_Q0));
+            tc::fence_before_sync();
+            mbar_arrive(&B->q_conv);
+            mbar_arrive(&B->q_empty);
           }
           continue;
         }
@@ -540,7 +598,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         float ps = 0.f;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float p = tc::to_tf32(ex2(v[c] - m));
+          const float p = tc::to_tf32(ex2(fmaf(v[c], vs, -m)));
           ps += p;
           v[c] = p;
         }
@@ -557,7 +615,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       if (!ok) break;
       tc::fence_after_sync();
       if constexpr (SPLIT) {
-        const uint32_t ob = tl + (((n - 1) & 1) ? COL_OB1 : COL_OB0);
+        const uint32_t ob = tl + COL_OB;
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           float ad[32];
@@ -629,19 +687,20 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         const int nk = min(kN, Lk - j * kN);
         float4* xb = reinterpret_cast<float4*>((vconv ? Vs : Ks) + s * kKVBytes);
         float4* xl = reinterpret_cast<float4*>((vconv ? VLs : KLs) + s * kKVBytes);
-        // batches of 8 chunks per lane: all loads before any store (the stores write the same
-        // array, so the compiler would not move later loads above them). The tensor core reads a
-        // TF32 operand from the high 19 bits of its 32-bit container and ignores the 13 low
-        // mantissa bits, so the landed x already serves as hi; only lo = x - hi is written
-        // (and rows of V past Lk are zeroed in both copies).
+        // Batches of kBatch chunks per lane, every load of a batch ahead of its stores (the
+        // stores write the same array, so the compiler would not move later loads above them).
+        // (One batch of all 32 chunks was slower overall.) The tensor core reads a TF32 operand
+        // from the high 19 bits of its 32-bit container and ignores the 13 low mantissa bits,
+        // so the landed x already serves as hi; only lo = x - hi is written (and rows of V past
+        // Lk are zeroed in both copies).
         constexpr int kPer = (int)(kKVBytes / 16) / kConv;  // 32 chunks per lane
 #pragma unroll 1
-        for (int b0 = 0; b0 < kPer; b0 += 8) {
-          float4 x[8], lo[8];
+        for (int b0 = 0; b0 < kPer; b0 += kBatch) {
+          float4 x[kBatch], lo[kBatch];
 #pragma unroll
-          for (int r = 0; r < 8; ++r) x[r] = xb[lane + kConv * (b0 + r)];
+          for (int r = 0; r < kBatch; ++r) x[r] = xb[lane + kConv * (b0 + r)];
 #pragma unroll
-          for (int r = 0; r < 8; ++r) {
+          for (int r = 0; r < kBatch; ++r) {
             const int i = lane + kConv * (b0 + r);
             // a 16-byte chunk of V: slab i / 512, key row (i % 512) / 8 (128-byte rows)
             if (!vconv || ((i & 511) >> 3) < nk) {
@@ -651,7 +710,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
             }
           }
 #pragma unroll
-          for (int r = 0; r < 8; ++r) {
+          for (int r = 0; r < kBatch; ++r) {
             if (vconv && ((lane + kConv * (b0 + r)) & 511) >> 3 >= nk) xb[lane + kConv * (b0 + r)] = x[r];
             xl[lane + kConv * (b0 + r)] = lo[r];
           }

@@ -94,6 +94,13 @@ def test_valid_descriptors():
     assert check(d)[0] == _lib.OK
     # Lq = 0 records nothing and is valid
     assert check(dit_self_desc(Lq=0))[0] == _lib.OK
+    # the three numeric variants (FP32 FFMA, TF32, split-precision TF32X3); 3 is not one
+    for v in (_lib.FP32, _lib.TF32, _lib.TF32X3):
+        assert check(dit_self_desc(variant=v))[0] == _lib.OK
+    st, msg = check(dit_self_desc(variant=3))
+    assert st == _lib.EINVAL and "variant" in msg
+    # the Python mirror's names for them
+    assert supra_attn.ops.VARIANTS == {"fp32": _lib.FP32, "tf32": _lib.TF32, "tf32x3": _lib.TF32X3}
 
 
 @pytest.mark.parametrize(
