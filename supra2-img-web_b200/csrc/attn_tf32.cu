@@ -32,8 +32,8 @@
 // Split precision (SPLIT = true, variant TF32X3): fp32-class accuracy from the same tensor cores.
 // The TMA copies the operands exactly (fp32 tensor maps). hi is x with its 13 low mantissa bits
 // cleared: the tensor core ignores those bits of a TF32 operand, so the landed K and V tiles
-// serve as their own hi parts, and lo = x - hi (exact) goes into a second copy: for K by two
-// converter warps (6, 7), for V by the softmax threads just before they release P. The softmax threads split their Q rows into hi(Q) / lo(Q) in TMEM (the A
+// serve as their own hi parts, and two converter warps (6: K, 7: V) write lo = x - hi (exact)
+// into a second copy. The softmax threads split their Q rows into hi(Q) / lo(Q) in TMEM (the A
 // operand of S) and P the same way. K and V have separate rings, so the next K blocks land
 // while a V stage waits for its PV product. Every product is formed as
 // lo*hi + hi*lo + hi*hi (three TF32 MMAs, the small terms first), which leaves an error of about
@@ -85,7 +85,7 @@ constexpr uint32_t COL_S0 = 0, COL_S1 = 64, COL_O = 128;
 // next tile's Q is split before the current tile's epilogue
 constexpr uint32_t COL_PL = 128, COL_OB = 192, COL_Q0 = 256, COL_Q1 = 384;
 constexpr int kBatch = 8;  // converter: 16-byte chunks per lane loaded before any is stored
-constexpr int kConv = 32;  // threads per converter warp (split kernel: warps 6 and 7, both on K)
+constexpr int kConv = 32;  // threads per converter warp (split kernel: warp 6 for K, warp 7 for V)
 
 // pv_done is double-buffered by block parity so that a waiter for PV_n never sees a barrier
 // that is two phases ahead or behind (PV_{n-2} is always complete when PV_n is awaited).
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     mbar_init(&B->o_empty, 128);
     mbar_init(&B->drain, 1);
     mbar_init(&B->q_conv, 128);  // split kernel: the softmax threads, one Q row each
-    for (int s = 0; s < kNS; ++s) mbar_init(&B->kv_conv[s], 2 * kConv);  // both converter warps
+    for (int s = 0; s < kNS; ++s) mbar_init(&B->kv_conv[s], kConv);
     for (int s = 0; s < kNSV; ++s) {
       mbar_init(&B->v_full[s], 1);
       mbar_init(&B->v_empty[s], 1);
@@ -308,6 +308,9 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       const int sp = m % (SPLIT ? kNSV : kNS);
       const int bp = m & 1;
       if (!__all_sync(0xffffffffu, wait_or_abort(&B->p_full[bp], (uint32_t)((m >> 1) & 1), abort, L.status, W_P_FULL, m))) return false;
+      if (SPLIT && !__all_sync(0xffffffffu, wait_or_abort(&B->v_conv[sp], (uint32_t)((m / kNSV) & 1), abort, L.status,
+                                                          W_KV_FULL, m)))
+        return false;
       if (!SPLIT && pend_first && pend_k > 0 &&
           !__all_sync(0xffffffffu, wait_or_abort(&B->o_empty, (uint32_t)((pend_k - 1) & 1), abort, L.status, W_O_EMPTY, m)))
         return false;
@@ -560,33 +563,6 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
             }
           }
           tc::tmem_st64(tl + COL_PL, v);
-          {
-            // lo(V_n): the 128 softmax threads split the landed V tile (8 chunks each) before
-            // they release P_n, so p_full also means lo(V_n) is in place; V rows past Lk become
-            // zeros in both copies (they meet P == 0 but may hold another sequence's data).
-            const int sv = n % kNSV;
-            ok = __all_sync(0xffffffffu, wait_or_abort(&B->v_full[sv], (uint32_t)((n / kNSV) & 1), abort, L.status,
-                                                       W_CONV_KV, n));
-            if (!ok) break;
-            float4* vb = reinterpret_cast<float4*>(Vs + sv * kKVBytes);
-            float4* vl = reinterpret_cast<float4*>(VLs + sv * kKVBytes);
-            const int st = (int)threadIdx.x - 64;
-            float4 x[8], lo[8];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) x[r] = vb[st + 128 * r];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              // a 16-byte chunk: slab i / 512, key row (i % 512) / 8 (128-byte rows)
-              if (((st + 128 * r) & 511) >> 3 < nk) {
-                split4(x[r], lo[r]);
-              } else {
-                x[r] = lo[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-                vb[st + 128 * r] = x[r];
-              }
-              vl[st + 128 * r] = lo[r];
-            }
-            fence_proxy_async_smem();
-          }
           tc::tmem_wait_st();
           tc::fence_before_sync();
           mbar_arrive(&B->p_full[b]);
@@ -690,40 +666,57 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 22, n);
   } else if (SPLIT) {
-    // ---------------- converters (split kernel): warps 6 and 7 split each K tile ----------------
+    // ---------------- converters (split kernel): warp 6 for K, warp 7 for V ----------------
     // Each landed tile x is its own hi part; lo = x - hi goes into the lo copy (same offsets, so
-    // the same swizzled layout). Then the generic-proxy writes are made visible to the tensor
-    // core and the MMA warp is released. (V tiles are split by the softmax threads.)
-    const int ct = (int)threadIdx.x - 192;  // 0..63
+    // the same swizzled layout). V rows past Lk become zeros in both parts: they meet P == 0 but
+    // may hold another sequence's data. Then the generic-proxy writes are made visible to the
+    // tensor core and the MMA warp is released.
+    const bool vconv = warp == 7;
     bool ok = true;
-    int n = 0;
-    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
+    int n = 0, k = 0;
+    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
       const Tile T = tile_of(L, t);
+      const int Lk = T.p->Lk;
       for (int j = 0; ok && j < T.nblk; ++j, ++n) {
-        const int s = n % kNS;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&B->kv_full[s], (uint32_t)((n / kNS) & 1), abort, L.status,
+        const int ns = vconv ? kNSV : kNS;
+        const int s = n % ns;
+        const uint32_t par = (uint32_t)((n / ns) & 1);
+        ok = __all_sync(0xffffffffu, wait_or_abort(vconv ? &B->v_full[s] : &B->kv_full[s], par, abort, L.status,
                                                    W_CONV_KV, n));
         if (!ok) break;
-        float4* xb = reinterpret_cast<float4*>(Ks + s * kKVBytes);
-        float4* xl = reinterpret_cast<float4*>(KLs + s * kKVBytes);
-        // Batches of kBatch chunks per thread, every load of a batch ahead of its stores (the
+        const int nk = min(kN, Lk - j * kN);
+        float4* xb = reinterpret_cast<float4*>((vconv ? Vs : Ks) + s * kKVBytes);
+        float4* xl = reinterpret_cast<float4*>((vconv ? VLs : KLs) + s * kKVBytes);
+        // Batches of kBatch chunks per lane, every load of a batch ahead of its stores (the
         // stores write the same array, so the compiler would not move later loads above them).
-        // The tensor core reads a TF32 operand from the high 19 bits of its 32-bit container
-        // and ignores the 13 low mantissa bits, so the landed x already serves as hi; only
-        // lo = x - hi is written.
-        constexpr int kPer = (int)(kKVBytes / 16) / (2 * kConv);  // 16 chunks per thread
+        // (One batch of all 32 chunks was slower overall.) The tensor core reads a TF32 operand
+        // from the high 19 bits of its 32-bit container and ignores the 13 low mantissa bits,
+        // so the landed x already serves as hi; only lo = x - hi is written (and rows of V past
+        // Lk are zeroed in both copies).
+        constexpr int kPer = (int)(kKVBytes / 16) / kConv;  // 32 chunks per lane
 #pragma unroll 1
         for (int b0 = 0; b0 < kPer; b0 += kBatch) {
           float4 x[kBatch], lo[kBatch];
 #pragma unroll
-          for (int r = 0; r < kBatch; ++r) x[r] = xb[ct + 2 * kConv * (b0 + r)];
+          for (int r = 0; r < kBatch; ++r) x[r] = xb[lane + kConv * (b0 + r)];
 #pragma unroll
-          for (int r = 0; r < kBatch; ++r) split4(x[r], lo[r]);
+          for (int r = 0; r < kBatch; ++r) {
+            const int i = lane + kConv * (b0 + r);
+            // a 16-byte chunk of V: slab i / 512, key row (i % 512) / 8 (128-byte rows)
+            if (!vconv || ((i & 511) >> 3) < nk) {
+              split4(x[r], lo[r]);
+            } else {
+              x[r] = lo[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
 #pragma unroll
-          for (int r = 0; r < kBatch; ++r) xl[ct + 2 * kConv * (b0 + r)] = lo[r];
+          for (int r = 0; r < kBatch; ++r) {
+            if (vconv && ((lane + kConv * (b0 + r)) & 511) >> 3 >= nk) xb[lane + kConv * (b0 + r)] = x[r];
+            xl[lane + kConv * (b0 + r)] = lo[r];
+          }
         }
         fence_proxy_async_smem();
-        mbar_arrive(&B->kv_conv[s]);
+        mbar_arrive(vconv ? &B->v_conv[s] : &B->kv_conv[s]);
       }
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 23, n);
