@@ -12,10 +12,12 @@
 //   O += P_n V_n   tcgen05.mma kind::tf32, A = P_n from TMEM, B = V_n (smem, MN-major), D = O in TMEM
 // Persistent CTAs: CTA b takes tiles b, b + grid, b + 2*grid, ... of the launch's list of
 // (problem, head, 128-row query tile); the key blocks of all its tiles form one stream n = 0, 1, ...
-// that flows through a 2-stage K/V ring and a double-buffered S/P in TMEM without draining at
-// tile boundaries. 6 warps:
-//   warp 0     TMA producer: per tile the Q tile (once the previous tile's last S product has
-//              read the old one), then K/V blocks of 64 keys into the ring
+// that flows through separate K and V rings (2 stages each; a K stage is released once its S
+// product is done, a V stage once its PV product is) and a double-buffered S/P in TMEM without
+// draining at tile boundaries. 6 warps:
+//   warp 0     TMA producer: lane 0 per tile the Q tile (once the previous tile's last S product
+//              has read the old one), then the K blocks of 64 keys; lane 1 the V blocks, so K
+//              runs ahead of the V stages
 //   warp 1     TMEM allocation and the single-thread MMA issuer; S_n is issued before PV_{n-1}
 //              so the tensor core computes S_n while the softmax warps work on P_{n-1}
 //   warps 2-5  softmax and epilogue; warp w owns TMEM lanes 32*(w%4) .. +31 (query rows)
@@ -51,8 +53,8 @@ namespace {
 constexpr int kM = 128;  // query rows per tile (MMA M)
 constexpr int kN = 64;   // keys per block (MMA N of S)
 constexpr int kD = 64;   // head dim (MMA N of O)
-constexpr int kNS = 2;   // K/V stages (split kernel: K stages)
-constexpr int kNSV = 3;  // split kernel: V stages (a V stage is held until its PV product is done)
+constexpr int kNS = 2;   // K stages
+constexpr int kNSV = 3;  // V stages of the split kernel (a V stage is held until its PV product is done)
 constexpr uint32_t kQSlab = kM * 128;   // one 32-column slab of the Q tile: 16 KB
 constexpr uint32_t kKVSlab = kN * 128;  // one 32-column slab of a K or V block: 8 KB
 constexpr uint32_t kQBytes = 2 * kQSlab;
@@ -77,6 +79,7 @@ struct Lay {
   static constexpr uint32_t TMEM_COLS = SPLIT ? 512 : 256;
   static constexpr int THREADS = SPLIT ? 256 : 192;  // 8 warps: two per SM sub-partition, up to 255 registers
   static constexpr int CTAS_PER_SM = SPLIT ? 1 : 2;
+  static constexpr int NSV = SPLIT ? kNSV : kNS;  // V stages
 };
 static_assert(Lay<true>::SMEM <= 227 * 1024 && 2 * Lay<false>::SMEM <= 228 * 1024, "shared memory");
 constexpr uint32_t COL_S0 = 0, COL_S1 = 64, COL_O = 128;
@@ -91,8 +94,9 @@ constexpr int kConv = 32;  // threads per converter warp (split kernel: warp 6 f
 // that is two phases ahead or behind (PV_{n-2} is always complete when PV_n is awaited).
 struct Bars {
   uint64_t q_full, q_empty, kv_full[kNS], kv_empty[kNS], s_full[2], p_full[2], pv_done[2], o_empty, drain;
-  // split kernel: K and V flow through separate rings (kv_full / kv_empty / kv_conv serve K),
-  // and each landed tile is released to the MMA warp once its hi/lo parts are in place
+  // K and V flow through separate rings (kv_full / kv_empty serve K, released once S is done;
+  // v_full / v_empty serve V, released once PV is done); in the split kernel each landed tile
+  // is released to the MMA warp once its lo part is in place (kv_conv, v_conv)
   uint64_t q_conv, kv_conv[kNS], v_full[kNSV], v_empty[kNSV], v_conv[kNSV];
   uint32_t tmem;
   int32_t abort;
@@ -103,10 +107,6 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Wait ids reported with a timeout (status[2]); status[3] carries the waiter's block counter.
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     mbar_init(&B->drain, 1);
     mbar_init(&B->q_conv, 128);  // split kernel: the softmax threads, one Q row each
     for (int s = 0; s < kNS; ++s) mbar_init(&B->kv_conv[s], kConv);
-    for (int s = 0; s < kNSV; ++s) {
+    for (int s = 0; s < Y::NSV; ++s) {
       mbar_init(&B->v_full[s], 1);
       mbar_init(&B->v_empty[s], 1);
       mbar_init(&B->v_conv[s], kConv);
@@ -243,9 +243,9 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (SPLIT && lane == 1) {
-      // split kernel: the V ring, on its own lane so that K blocks run ahead of the V stages,
-      // which stay busy until their PV products are done
+    if (lane == 1) {
+      // the V ring, on its own lane so that K blocks run ahead of the V stages, which stay busy
+      // until their PV products are done
       int n = 0;
       for (int t = blockIdx.x; t < L.total; t += gridDim.x) {
         const Tile T = tile_of(L, t);
@@ -254,8 +254,8 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         const int hx = T.h * kD;
         bool ok = true;
         for (int j = 0; j < T.nblk; ++j, ++n) {
-          const int s = n % kNSV;
-          if (n >= kNSV && !(ok = wait_or_abort(&B->v_empty[s], (uint32_t)(((n / kNSV) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
+          const int s = n % Y::NSV;
+          if (n >= Y::NSV && !(ok = wait_or_abort(&B->v_empty[s], (uint32_t)(((n / Y::NSV) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
           mbar_arrive_expect_tx(&B->v_full[s], kKVBytes);
           uint8_t* vd = Vs + s * kKVBytes;
           tc::tma_load_2d(vd, mv, pp->vx + hx, pp->vy + j * kN, &B->v_full[s]);
@@ -270,7 +270,6 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         const TmaProb* pp = T.p;
         const CUtensorMap* mq = L.maps + pp->mq;
         const CUtensorMap* mk = L.maps + pp->mk;
-        const CUtensorMap* mv = L.maps + pp->mv;
         const int hx = T.h * kD;
         if (k > 0 && !wait_or_abort(&B->q_empty, (uint32_t)((k - 1) & 1), abort, L.status, W_Q_EMPTY, n)) break;
         mbar_arrive_expect_tx(&B->q_full, kQBytes);
@@ -280,15 +279,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         for (int j = 0; j < T.nblk; ++j, ++n) {
           const int s = n % kNS;
           if (n >= kNS && !(ok = wait_or_abort(&B->kv_empty[s], (uint32_t)(((n / kNS) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
-          mbar_arrive_expect_tx(&B->kv_full[s], SPLIT ? kKVBytes : 2 * kKVBytes);
+          mbar_arrive_expect_tx(&B->kv_full[s], kKVBytes);
           uint8_t* kd = Ks + s * kKVBytes;
-          uint8_t* vd = Vs + s * kKVBytes;
           tc::tma_load_2d(kd, mk, pp->kx + hx, pp->ky + j * kN, &B->kv_full[s]);
           tc::tma_load_2d(kd + kKVSlab, mk, pp->kx + hx + 32, pp->ky + j * kN, &B->kv_full[s]);
-          if (!SPLIT) {
-            tc::tma_load_2d(vd, mv, pp->vx + hx, pp->vy + j * kN, &B->kv_full[s]);
-            tc::tma_load_2d(vd + kKVSlab, mv, pp->vx + hx + 32, pp->vy + j * kN, &B->kv_full[s]);
-          }
         }
         if (!ok) break;
       }
@@ -305,11 +299,11 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     bool pend_first = false;
     auto issue_pv = [&]() -> bool {
       const int m = pend_n;
-      const int sp = m % (SPLIT ? kNSV : kNS);
+      const int sp = m % Y::NSV;
       const int bp = m & 1;
       if (!__all_sync(0xffffffffu, wait_or_abort(&B->p_full[bp], (uint32_t)((m >> 1) & 1), abort, L.status, W_P_FULL, m))) return false;
-      if (SPLIT && !__all_sync(0xffffffffu, wait_or_abort(&B->v_conv[sp], (uint32_t)((m / kNSV) & 1), abort, L.status,
-                                                          W_KV_FULL, m)))
+      if (!__all_sync(0xffffffffu, wait_or_abort(SPLIT ? &B->v_conv[sp] : &B->v_full[sp], (uint32_t)((m / Y::NSV) & 1),
+                                                 abort, L.status, W_KV_FULL, m)))
         return false;
       if (!SPLIT && pend_first && pend_k > 0 &&
           !__all_sync(0xffffffffu, wait_or_abort(&B->o_empty, (uint32_t)((pend_k - 1) & 1), abort, L.status, W_O_EMPTY, m)))
@@ -352,7 +346,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           for (int kk = 0; kk < kN / 8; ++kk)
             tc::mma_tf32_ts(tmem + COL_O, tmem + pcol + 8 * kk, vdesc(vb, kk), idPV, (!pend_first || kk > 0) ? 1u : 0u);
         }
-        tc::commit(SPLIT ? &B->v_empty[sp] : &B->kv_empty[sp]);
+        tc::commit(&B->v_empty[sp]);
         tc::commit(&B->pv_done[m & 1]);
       }
       __syncwarp();
@@ -402,10 +396,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
             s_product_t(ql, kb, true);
             s_product_t(qh, kl, false);
             s_product_t(qh, kb, false);
-            tc::commit(&B->kv_empty[s]);  // the K stage is free once S is done
           } else {
             s_product(Qs, kb, true);
           }
+          tc::commit(&B->kv_empty[s]);  // the K stage is free once S is done
           tc::commit(&B->s_full[b]);
           if (!SPLIT && j == T.nblk - 1) tc::commit(&B->q_empty);  // the Q tile is no longer read
         }

@@ -36,6 +36,11 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// One plain arrival (no transaction bytes).
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Makes mbarrier initialisation visible to the async proxy (the bulk-copy engine).
 __device__ __forceinline__ void mbar_fence_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -114,6 +119,15 @@ __device__ __forceinline__ float t5_table_bias(const float* __restrict__ tab_h, 
                                                int32_t rel_max, uint32_t H, int32_t rel) {
   rel = max(-rel_max, min(rel_max, rel));
   return __ldg(tab_h + (uint32_t)__ldg(lut_c + rel) * H);
+}
+
+// ops.linear's activations (app/gpu/gemm.js:28-36), kActGelu / kActGeluTanh / kActSilu: GELU in
+// its erf form, GELU with the tanh approximation 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+// SiLU x / (1 + e^-x).
+__device__ __forceinline__ float linear_act(int act, float x) {
+  if (act == kActGelu) return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+  if (act == kActGeluTanh) return 0.5f * x * (1.f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
+  return x / (1.f + expf(-x));
 }
 
 // Tile index -> problem index: the largest p with begin[p] <= t (begin[0] == 0, ascending).

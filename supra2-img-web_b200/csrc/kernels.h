@@ -175,6 +175,31 @@ cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cuda
 // GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
 // group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
 // mean in a second pass (app/gpu/kernels.js:117-139).
+// Linear on the tensor cores (linear_tc.cu) for the TF32 / TF32X3 variants: x and w are first
+// written as dense [rows, ldk] arrays (ldk = K rounded up to 4) by launch_linear_split, hi = the
+// value with its 13 low mantissa bits cleared and lo = value - hi; the product is then
+// hi(x) hi(w) (TF32) or lo(x) hi(w) + hi(x) lo(w) + hi(x) hi(w) (TF32X3) on tcgen05, with p's
+// epilogue (bias, activation, gate, residual). x and w in p are unused.
+struct alignas(16) LinTcProb {
+  LinProb p;
+  int32_t mxh, mxl, mwh, mwl;  // tensor maps of hi(x), lo(x), hi(w), lo(w) (lo: split form only)
+  int32_t m_tiles, n_tiles;    // 128-row and 128-column output tiles
+  int32_t nkb;                 // 32-deep k-blocks: ceil(K / 32)
+  int32_t pad;
+};
+static_assert(sizeof(LinTcProb) % 16 == 0, "LinTcProb is packed into the descriptor ring");
+struct LinTcLaunch {
+  const LinTcProb* probs;
+  const CUtensorMap* maps;
+  const int32_t* begin;  // first tile of each problem
+  int32_t n, total;
+  int32_t* status;
+};
+cudaError_t launch_linear_tc(const LinTcLaunch& L, bool split, cudaStream_t s);
+// rows x K floats of src (row stride ld) -> hi (and lo when non-null), dense with row stride ldd;
+// normalised first when norm.gn_stats is set (norm's GroupNorm / LayerNorm fields, x rows).
+cudaError_t launch_linear_split(const float* src, int64_t ld, int32_t rows, int32_t K, const LinProb& norm, float* hi,
+                                float* lo, int32_t ldd, cudaStream_t s);
 cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s);
 cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
                             float eps, float2* stats, cudaStream_t s);

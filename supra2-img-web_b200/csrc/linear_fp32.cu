@@ -24,14 +24,6 @@ constexpr int kBN = 128;  // columns per tile
 constexpr int kBK = 16;   // reduction depth per stage
 constexpr int kS = kBK + 4;  // row stride of the stage buffers (conflict-free float4 reads)
 
-// ops.linear's activations (app/gpu/gemm.js:28-36): GELU in its erf form, GELU with the tanh
-// approximation 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), SiLU x / (1 + e^-x).
-__device__ __forceinline__ float activate(int act, float x) {
-  if (act == kActGelu) return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
-  if (act == kActGeluTanh) return 0.5f * x * (1.f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
-  return x / (1.f + expf(-x));
-}
-
 template <bool BIAS, bool ALIGNED>
 __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
   __shared__ __align__(16) float As[2][kBM * kS];
@@ -170,7 +162,7 @@ __global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
       const int c = cg + 16 * j;
       if (c < nc) {
         float v = acc[i][j] + bias[j];
-        if (P.act != kActNone) v = activate(P.act, v);
+        if (P.act != kActNone) v = linear_act(P.act, v);
         if (P.gate) v *= gate[j];
         yrow[c] = rrow ? rrow[c] + v : v;
       }

@@ -1,0 +1,308 @@
+// ops.linear (app/gpu/ops.js:35-43, app/gpu/gemm.js:116-223) on the tensor cores, sm_100a: the
+// TF32 and split-precision (TF32X3) variants of supra_attn_enqueue_linear.
+//
+//   linear_split_kernel  x (normalised first when asked: GroupNorm / LayerNorm with the
+//                        statistics of the stats kernels, app/gpu/kernels.js:87-162) and w into
+//                        dense hi / lo arrays: hi = value with its 13 low mantissa bits cleared
+//                        (a TF32 value), lo = value - hi (exact). Elementwise, HBM-bound.
+//   linear_tc_kernel     C[128 x 128 tile] = X W^T with tcgen05.mma kind::tf32: per 32-deep
+//                        k-block the TMA brings hi(X), hi(W) (and lo(X), lo(W)) tiles
+//                        (SWIZZLE_128B, K-major), the MMA warp issues per 8-deep step one
+//                        product (TF32) or three, lo*hi + hi*lo + hi*hi (TF32X3, the small terms
+//                        first), into a TMEM accumulator. Every kFlush k-blocks the partial sum
+//                        goes to a fresh (double-buffered) accumulator and the epilogue warps add
+//                        it to the row they hold in registers, in fp32 rounded to nearest, so the
+//                        error does not grow with K as it would in one TMEM accumulator. The
+//                        epilogue then applies bias, activation, gate and residual (the
+//                        reference's order, app/gpu/gemm.js:130-135) and stores the row.
+// Persistent: CTA c takes tiles c, c + grid, ... of the launch's (problem, row tile, column tile)
+// list, column tiles innermost. 6 warps: TMA producer, MMA issuer, 4 epilogue warps (warp w owns
+// TMEM lanes 32*(w%4) .. +31, i.e. output rows). One CTA per SM (three 64 KB stages). Every wait
+// is bounded; on a timeout the CTA records the failure, drains its MMAs, frees TMEM and leaves.
+#include "tcgen05.cuh"
+
+namespace supra {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 32;
+constexpr int kStages = 3;
+constexpr int kFlush = 4;                        // k-blocks per TMEM partial sum
+constexpr uint32_t kTile = kBM * kBK * 4;        // one operand tile: 128 rows x 128 bytes = 16 KB
+constexpr uint32_t kStage = 4 * kTile;           // hi(X), hi(W), lo(X), lo(W)
+constexpr uint32_t OFF_BAR = kStages * kStage;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t kTmemCols = 256;              // two 128-column accumulators
+constexpr int kThreads = 192;
+
+struct Bars {
+  uint64_t full[kStages], empty[kStages], accf[2], acce[2], drain;
+  int32_t abort;
+  uint32_t tmem;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+enum WaitId : int32_t { W_EMPTY = 51, W_FULL = 52, W_ACCE = 53, W_ACCF = 54 };
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
+                                              int32_t* status, int32_t id, int32_t detail) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        report_error(status, DEV_TIMEOUT, id, detail);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+struct TileRef {
+  const LinTcProb* p;
+  int mt, nt;
+};
+__device__ __forceinline__ TileRef tile_ref(const LinTcLaunch& L, int t) {
+  TileRef r;
+  const int pi = find_problem(L.begin, L.n, t);
+  r.p = L.probs + pi;
+  const int local = t - __ldg(L.begin + pi);
+  r.mt = local / r.p->n_tiles;
+  r.nt = local - r.mt * r.p->n_tiles;
+  return r;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
+  tc::tma_load_2d(dst, m, x, y, bar);
+}
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_constant__ LinTcLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned for the swizzle atoms
+  Bars* B = reinterpret_cast<Bars*>(base + OFF_BAR);
+  volatile int32_t* abort = &B->abort;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&B->full[s], 1);
+      mbar_init(&B->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&B->accf[b], 1);
+      mbar_init(&B->acce[b], 128);
+    }
+    mbar_init(&B->drain, 1);
+    B->abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&B->tmem, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = B->tmem;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
+        const TileRef T = tile_ref(L, t);
+        const LinTcProb* P = T.p;
+        for (int kb = 0; kb < P->nkb; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages &&
+              !(ok = wait_or_abort(&B->empty[s], (uint32_t)(((g / kStages) - 1) & 1), abort, L.status, W_EMPTY, g)))
+            break;
+          uint8_t* st = base + s * kStage;
+          mbar_arrive_expect_tx(&B->full[s], SPLIT ? 4 * kTile : 2 * kTile);
+          tma_load_2d(st, L.maps + P->mxh, kb * kBK, T.mt * kBM, &B->full[s]);
+          tma_load_2d(st + kTile, L.maps + P->mwh, kb * kBK, T.nt * kBN, &B->full[s]);
+          if (SPLIT) {
+            tma_load_2d(st + 2 * kTile, L.maps + P->mxl, kb * kBK, T.mt * kBM, &B->full[s]);
+            tma_load_2d(st + 3 * kTile, L.maps + P->mwl, kb * kBK, T.nt * kBN, &B->full[s]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = tc::idesc_tf32(kBM, kBN, false, false);
+    int g = 0, f = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
+      const TileRef T = tile_ref(L, t);
+      const int nkb = T.p->nkb;
+      for (int kb = 0; ok && kb < nkb; ++kb, ++g) {
+        const int s = g % kStages;
+        const bool start = (kb % kFlush) == 0;
+        const bool end = (kb % kFlush) == kFlush - 1 || kb == nkb - 1;
+        if (start && f >= 2)  // the epilogue has read this accumulator's previous partial sum
+          ok = __all_sync(0xffffffffu, wait_or_abort(&B->acce[f & 1], (uint32_t)(((f >> 1) - 1) & 1), abort, L.status,
+                                                     W_ACCE, f));
+        if (!ok) break;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&B->full[s], (uint32_t)((g / kStages) & 1), abort, L.status, W_FULL, g));
+        if (!ok) break;
+        tc::fence_after_sync();
+        if (lane == 0) {
+          const uint8_t* st = base + s * kStage;
+          const uint32_t d = tmem + (uint32_t)(f & 1) * kBN;
+          auto desc = [&](const uint8_t* tile, int k8) {
+            return tc::smem_desc(tile + k8 * 32, 16, 1024, tc::kLayoutSW128);
+          };
+#pragma unroll
+          for (int k8 = 0; k8 < kBK / 8; ++k8) {
+            const uint32_t acc = (start && k8 == 0) ? 0u : 1u;
+            if (SPLIT) {
+              tc::mma_tf32_ss(d, desc(st + 2 * kTile, k8), desc(st + kTile, k8), idesc, acc);  // lo(X) hi(W)
+              tc::mma_tf32_ss(d, desc(st, k8), desc(st + 3 * kTile, k8), idesc, 1u);           // hi(X) lo(W)
+              tc::mma_tf32_ss(d, desc(st, k8), desc(st + kTile, k8), idesc, 1u);               // hi(X) hi(W)
+            } else {
+              tc::mma_tf32_ss(d, desc(st, k8), desc(st + kTile, k8), idesc, acc);
+            }
+          }
+          tc::commit(&B->empty[s]);
+          if (end) tc::commit(&B->accf[f & 1]);
+        }
+        __syncwarp();
+        if (end) ++f;
+      }
+    }
+    if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 55, g);
+  } else {
+    // ---------------- epilogue (warps 2..5): one output row per thread ----------------
+    const int q4 = warp & 3;
+    const int row = 32 * q4 + lane;
+    const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
+    int f = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
+      const TileRef T = tile_ref(L, t);
+      const LinProb& P = T.p->p;
+      const int nkb = T.p->nkb;
+      float o[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) o[c] = 0.f;
+      for (int kb0 = 0; kb0 < nkb; kb0 += kFlush, ++f) {
+        ok = __all_sync(0xffffffffu, wait_or_abort(&B->accf[f & 1], (uint32_t)((f >> 1) & 1), abort, L.status, W_ACCF, f));
+        if (!ok) break;
+        tc::fence_after_sync();
+        const uint32_t acc = tl + (uint32_t)(f & 1) * kBN;
+#pragma unroll
+        for (int c32 = 0; c32 < kBN / 32; ++c32) {
+          float ad[32];
+          tc::tmem_ld32(acc + 32 * c32, ad);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float2 x = __fadd2_rn(make_float2(o[32 * c32 + c], o[32 * c32 + c + 1]), make_float2(ad[c], ad[c + 1]));
+            o[32 * c32 + c] = x.x;
+            o[32 * c32 + c + 1] = x.y;
+          }
+        }
+        tc::fence_before_sync();
+        mbar_arrive(&B->acce[f & 1]);
+      }
+      if (!ok) break;
+      // y = resid + gate * act(o + bias), the reference's epilogue order
+      const int r = T.mt * kBM + row;
+      if (r < P.M) {
+        const int c0 = T.nt * kBN;
+        const int nc = min(kBN, P.N - c0);
+        float* yrow = P.y + (int64_t)r * P.ldy + c0;
+        const float* rrow = P.resid ? P.resid + (int64_t)r * P.ldr + c0 : nullptr;
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          if (c < nc) {
+            float v = o[c] + (P.bias ? __ldg(P.bias + c0 + c) : 0.f);
+            if (P.act != kActNone) v = linear_act(P.act, v);
+            if (P.gate) v *= __ldg(P.gate + c0 + c);
+            yrow[c] = rrow ? rrow[c] + v : v;
+          }
+        }
+      }
+    }
+    if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 56, f);
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (*abort && warp == 1) {
+    if (lane == 0) {
+      tc::commit(&B->drain);
+      mbar_wait_bounded(&B->drain, 0);
+    }
+    __syncwarp();
+  }
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// hi / lo split of rows x K (row stride ld) into dense [rows, ldd], normalised first when
+// N.gn_stats is set: (x - mean) * rstd * g + b (then SiLU if asked) with g, b = gamma, beta
+// (GroupNorm), 1 + scale, shift (modulated LayerNorm) or 1, 0 (plain LayerNorm), as the
+// linear_fp32 prologue applies them.
+__global__ void __launch_bounds__(256) linear_split_kernel(const float* __restrict__ src, int64_t ld, int32_t rows,
+                                                           int32_t K, const LinProb N, float* __restrict__ hi,
+                                                           float* __restrict__ lo, int32_t ldd) {
+  const int64_t total = (int64_t)rows * K;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t r = (int32_t)(i / K), k = (int32_t)(i - (int64_t)r * K);
+    float x = __ldg(src + (int64_t)r * ld + k);
+    if (N.gn_stats) {
+      const float2 ms = __ldg(N.gn_stats + (int64_t)(r / N.gn_rows) * N.gn_groups + k / N.gn_cg);
+      float g = 1.f, b = 0.f;
+      if (N.gn_mode != kNormPlain) {
+        g = __ldg(N.gamma + k);
+        b = __ldg(N.beta + k);
+        if (N.gn_mode == kNormModulated) g = 1.f + g;
+      }
+      x = (x - ms.x) * ms.y * g + b;
+      if (N.gn_silu) x = x / (1.f + __expf(-x));
+    }
+    const float h = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+    hi[(int64_t)r * ldd + k] = h;
+    if (lo) lo[(int64_t)r * ldd + k] = x - h;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_linear_split(const float* src, int64_t ld, int32_t rows, int32_t K, const LinProb& norm, float* hi,
+                                float* lo, int32_t ldd, cudaStream_t s) {
+  const int64_t total = (int64_t)rows * K;
+  if (total <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (total + 255) / 256;
+  const int grid = (int)(want < 8 * sms ? want : 8 * sms);
+  linear_split_kernel<<<grid, 256, 0, s>>>(src, ld, rows, K, norm, hi, lo, ldd);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_linear_tc(const LinTcLaunch& L, bool split, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
+  auto k = split ? linear_tc_kernel<true> : linear_tc_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = L.total < sms ? L.total : sms;
+  k<<<grid, kThreads, SMEM_BYTES, s>>>(L);
+  return cudaGetLastError();
+}
+
+}  // namespace supra

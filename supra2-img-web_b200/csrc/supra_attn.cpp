@@ -102,12 +102,13 @@ struct Queued {
 struct MapKey {
   uintptr_t base;
   int64_t ld, rows;
+  int64_t cols;  // the inner extent: boxes reaching past it read zeros
   int32_t box_cols, box_rows;
   int32_t swz;  // CUtensorMapSwizzle
   int32_t tf32;
   bool operator==(const MapKey& o) const {
-    return base == o.base && ld == o.ld && rows == o.rows && box_cols == o.box_cols && box_rows == o.box_rows &&
-           swz == o.swz && tf32 == o.tf32;
+    return base == o.base && ld == o.ld && rows == o.rows && cols == o.cols && box_cols == o.box_cols &&
+           box_rows == o.box_rows && swz == o.swz && tf32 == o.tf32;
   }
 };
 struct MapKeyHash {
@@ -115,6 +116,7 @@ struct MapKeyHash {
     size_t h = std::hash<uintptr_t>()(k.base);
     h ^= std::hash<int64_t>()(k.ld) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
     h ^= std::hash<int64_t>()(k.rows) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= std::hash<int64_t>()(k.cols) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
     h ^= std::hash<int64_t>()(((int64_t)k.box_cols << 32) ^ (k.box_rows * 16 + k.swz * 2 + k.tf32)) +
          0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
     return h;
@@ -166,6 +168,8 @@ struct supra_attn_ctx {
 
   float2* gn_stats = nullptr;  // GroupNorm statistics of the linear problems of a flush
   size_t gn_cap = 0;             // in float2
+  float* lin_split = nullptr;    // tensor-core linears: hi / lo copies of x and w of a flush
+  size_t lin_split_cap = 0;      // in floats
   std::map<size_t, std::vector<void*>> pool_free;
   std::unordered_map<void*, size_t> pool_live;
   std::unordered_set<void*> host_live;
@@ -216,7 +220,7 @@ EncodeTiledFn encode_fn() {
 bool encode_map(CUtensorMap* m, const MapKey& k) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)k.ld, (cuuint64_t)k.rows};
+  const cuuint64_t dims[2] = {(cuuint64_t)k.cols, (cuuint64_t)k.rows};
   const cuuint64_t strides[1] = {(cuuint64_t)k.ld * 4};
   const cuuint32_t box[2] = {(cuuint32_t)k.box_cols, (cuuint32_t)k.box_rows};
   const cuuint32_t estr[2] = {1, 1};
@@ -690,7 +694,9 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
     q.gn_eps = ln->eps;
   }
   q.path = PATH_LINEAR;
-  q.cfg = 0;
+  // TF32 / TF32X3 requests with at least one 32-deep k-block run on the tensor cores (cfg 1 / 2);
+  // FP32 requests and shallower products run the FFMA kernel
+  q.cfg = (d->variant != SUPRA_ATTN_FP32 && d->K >= 32) ? (d->variant == SUPRA_ATTN_TF32X3 ? 2 : 1) : 0;
   q.bias = d->bias != nullptr;
   q.aligned = (d->K % 4 == 0) && (d->ldx % 4 == 0) && (d->ldw % 4 == 0) && aligned16(d->x + d->x_off) &&
               aligned16(d->w);
@@ -944,11 +950,12 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   std::vector<supra::TmaProb> probs((size_t)n);
   std::vector<CUtensorMap> maps;
   std::unordered_map<MapKey, int32_t, MapKeyHash> index;
-  MapKey last_key{0, 0, 0, 0, 0, 0, 0};
+  MapKey last_key{0, 0, 0, 0, 0, 0, 0, 0};
   int32_t last_idx = -1;
   auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box_cols, int32_t box_rows,
                        CUtensorMapSwizzle swz, int32_t* out) -> int {
-    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, box_cols, box_rows, (int32_t)swz, (tf32 && !split) ? 1 : 0};
+    const MapKey k{reinterpret_cast<uintptr_t>(base), ld, rows, ld, box_cols, box_rows, (int32_t)swz,
+                   (tf32 && !split) ? 1 : 0};
     if (last_idx >= 0 && k == last_key) {
       *out = last_idx;
       return SUPRA_ATTN_OK;
@@ -1067,6 +1074,52 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
 }
 
 // Linear group: one launch over the 128x128 output tiles of every recorded problem.
+// Grows a context-owned device buffer to at least `need` elements of `esize` bytes (the stream
+// is drained first: earlier launches may still read the old buffer).
+int grow_buffer(supra_attn_ctx* c, void** buf, size_t* cap, size_t need, size_t esize, const char* what) {
+  if (need <= *cap) return SUPRA_ATTN_OK;
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return cuda_err(c, e, what);
+  if (*buf) cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  if (cudaMalloc(buf, need * esize) != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(c, SUPRA_ATTN_ENOMEM, "%s: cudaMalloc of %zu bytes failed", what, need * esize);
+  }
+  *cap = need;
+  return SUPRA_ATTN_OK;
+}
+
+// GroupNorm / LayerNorm statistics of the linear problems that normalise x, into the context's
+// statistics buffer, one launch each; sets lp[i].gn_stats (lp[i] starts as g[i]->lin).
+int norm_stats(supra_attn_ctx* c, const std::vector<const Queued*>& g, supra::LinProb* lp) {
+  const int n = (int)g.size();
+  size_t nstats = 0;
+  for (int i = 0; i < n; ++i)
+    if (lp[i].gn_rows > 0) nstats += (size_t)(lp[i].M / lp[i].gn_rows) * lp[i].gn_groups;
+  int rc = grow_buffer(c, reinterpret_cast<void**>(&c->gn_stats), &c->gn_cap, nstats, sizeof(float2), "norm stats");
+  if (rc) return rc;
+  size_t at = 0;
+  for (int i = 0; i < n; ++i) {
+    if (lp[i].gn_rows <= 0) continue;
+    const int32_t images = lp[i].M / lp[i].gn_rows;
+    lp[i].gn_stats = c->gn_stats + at;
+    cudaError_t e;
+    const bool ln = lp[i].gn_mode != supra::kNormAffine;
+    {
+      ProfScope ps(c, ln ? "layernorm_stats" : "groupnorm_stats", 0.0, 4.0 * (double)lp[i].M * lp[i].K);
+      e = ln ? supra::launch_ln_stats(lp[i].x, lp[i].K, lp[i].M, g[i]->gn_eps, c->gn_stats + at, c->stream)
+             : supra::launch_gn_stats(lp[i].x, lp[i].K, lp[i].gn_rows, images, lp[i].gn_groups, g[i]->gn_eps,
+                                      c->gn_stats + at, c->stream);
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, ln ? "layernorm_stats" : "groupnorm_stats");
+    c->launches += 1;
+    at += (size_t)images * lp[i].gn_groups;
+  }
+  return SUPRA_ATTN_OK;
+}
+
 int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   const int n = (int)g.size();
   std::vector<int32_t> begin(n + 1);
@@ -1085,42 +1138,10 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   char *h = nullptr, *dv = nullptr;
   int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
   if (rc) return rc;
-  // GroupNorm statistics of the problems that normalise x, in a context buffer, one launch each
-  size_t nstats = 0;
-  for (int i = 0; i < n; ++i)
-    if (g[i]->lin.gn_rows > 0) nstats += (size_t)(g[i]->lin.M / g[i]->lin.gn_rows) * g[i]->lin.gn_groups;
-  if (nstats > c->gn_cap) {
-    cudaError_t e = cudaStreamSynchronize(c->stream);
-    if (e != cudaSuccess) return cuda_err(c, e, "groupnorm stats: stream sync");
-    if (c->gn_stats) cudaFree(c->gn_stats);
-    c->gn_stats = nullptr;
-    c->gn_cap = 0;
-    if (cudaMalloc(&c->gn_stats, nstats * sizeof(float2)) != cudaSuccess) {
-      cudaGetLastError();
-      return set_err(c, SUPRA_ATTN_ENOMEM, "groupnorm stats: cudaMalloc failed");
-    }
-    c->gn_cap = nstats;
-  }
   supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(h);
-  size_t at = 0;
-  for (int i = 0; i < n; ++i) {
-    hp[i] = g[i]->lin;
-    if (hp[i].gn_rows > 0) {
-      const int32_t images = hp[i].M / hp[i].gn_rows;
-      hp[i].gn_stats = c->gn_stats + at;
-      cudaError_t e;
-      const bool ln = hp[i].gn_mode != supra::kNormAffine;
-      {
-        ProfScope ps(c, ln ? "layernorm_stats" : "groupnorm_stats", 0.0, 4.0 * (double)hp[i].M * hp[i].K);
-        e = ln ? supra::launch_ln_stats(hp[i].x, hp[i].K, hp[i].M, g[i]->gn_eps, c->gn_stats + at, c->stream)
-               : supra::launch_gn_stats(hp[i].x, hp[i].K, hp[i].gn_rows, images, hp[i].gn_groups, g[i]->gn_eps,
-                                        c->gn_stats + at, c->stream);
-      }
-      if (e != cudaSuccess) return cuda_err(c, e, ln ? "layernorm_stats" : "groupnorm_stats");
-      c->launches += 1;
-      at += (size_t)images * hp[i].gn_groups;
-    }
-  }
+  for (int i = 0; i < n; ++i) hp[i] = g[i]->lin;
+  rc = norm_stats(c, g, hp);
+  if (rc) return rc;
   std::memcpy(h + pbytes, begin.data(), bbytes);
   rc = ring_commit(c, h, dv, pbytes + bbytes);
   if (rc) return rc;
@@ -1141,6 +1162,135 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   return SUPRA_ATTN_OK;
 }
 
+// Tensor-core linear group (variants TF32 / TF32X3, cfg 1 / 2): the norm statistics, then the
+// hi / lo split of each problem's x (normalised) and of each distinct weight matrix into the
+// context's split buffer (dense rows of ldk = K rounded up to 4 floats), then one launch over the
+// 128x128 output tiles of every problem.
+int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
+  const int n = (int)g.size();
+  const bool split = g[0]->cfg == 2;
+  const size_t parts = split ? 2 : 1;  // hi (and lo)
+  std::vector<supra::LinProb> lp((size_t)n);
+  for (int i = 0; i < n; ++i) lp[i] = g[i]->lin;
+  int rc = norm_stats(c, g, lp.data());
+  if (rc) return rc;
+  std::vector<size_t> xoff((size_t)n), woff((size_t)n);
+  std::vector<char> wfirst((size_t)n, 0);
+  size_t need = 0;
+  for (int i = 0; i < n; ++i) {
+    const size_t kp = (size_t)((lp[i].K + 3) & ~3);
+    xoff[i] = need;
+    need += parts * (size_t)lp[i].M * kp;
+    int j = 0;
+    for (; j < i; ++j)
+      if (lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N && lp[j].K == lp[i].K) break;
+    if (j < i) {
+      woff[i] = woff[j];
+    } else {
+      woff[i] = need;
+      wfirst[i] = 1;
+      need += parts * (size_t)lp[i].N * kp;
+    }
+  }
+  rc = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, need, sizeof(float), "linear split");
+  if (rc) return rc;
+  supra::LinProb plain;
+  std::memset(&plain, 0, sizeof plain);
+  for (int i = 0; i < n; ++i) {
+    const int32_t kp = (lp[i].K + 3) & ~3;
+    float* xh = c->lin_split + xoff[i];
+    float* wh = c->lin_split + woff[i];
+    cudaError_t e;
+    {
+      ProfScope ps(c, "linear_split", 0.0, 4.0 * (1.0 + (double)parts) * lp[i].M * lp[i].K);
+      e = supra::launch_linear_split(lp[i].x, lp[i].ldx, lp[i].M, lp[i].K, lp[i], xh,
+                                     split ? xh + (size_t)lp[i].M * kp : nullptr, kp, c->stream);
+      c->launches += 1;
+      if (e == cudaSuccess && wfirst[i]) {
+        e = supra::launch_linear_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, plain, wh,
+                                       split ? wh + (size_t)lp[i].N * kp : nullptr, kp, c->stream);
+        c->launches += 1;
+      }
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, "linear_split");
+  }
+  // tensor maps over the split arrays: [rows, K] with row stride kp, 32 x 128 boxes, SWIZZLE_128B,
+  // exact fp32 (the tensor core takes the hi copies as TF32 values)
+  std::vector<CUtensorMap> maps;
+  std::unordered_map<MapKey, int32_t, MapKeyHash> index;
+  auto map_of = [&](const float* b, int64_t kp, int64_t rows, int64_t cols, int32_t* out) -> int {
+    const MapKey k{reinterpret_cast<uintptr_t>(b), kp, rows, cols, 32, 128, (int32_t)CU_TENSOR_MAP_SWIZZLE_128B, 0};
+    auto it = index.find(k);
+    if (it == index.end()) {
+      auto ct = c->map_cache.find(k);
+      if (ct == c->map_cache.end()) {
+        CUtensorMap m;
+        if (!encode_map(&m, k)) return set_err(c, SUPRA_ATTN_ECUDA, "cuTensorMapEncodeTiled failed (linear)");
+        if (c->map_cache.size() > 65536) c->map_cache.clear();
+        ct = c->map_cache.emplace(k, m).first;
+      }
+      it = index.emplace(k, (int32_t)maps.size()).first;
+      maps.push_back(ct->second);
+    }
+    *out = it->second;
+    return SUPRA_ATTN_OK;
+  };
+  std::vector<supra::LinTcProb> probs((size_t)n);
+  std::vector<int32_t> begin((size_t)n + 1);
+  int64_t total = 0;
+  double flops = 0, bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    supra::LinTcProb& t = probs[i];
+    std::memset(&t, 0, sizeof t);
+    t.p = lp[i];
+    const int64_t kp = (lp[i].K + 3) & ~3;
+    const float* xh = c->lin_split + xoff[i];
+    const float* wh = c->lin_split + woff[i];
+    rc = map_of(xh, kp, lp[i].M, lp[i].K, &t.mxh);
+    if (!rc) rc = map_of(wh, kp, lp[i].N, lp[i].K, &t.mwh);
+    if (!rc && split) rc = map_of(xh + (size_t)lp[i].M * kp, kp, lp[i].M, lp[i].K, &t.mxl);
+    if (!rc && split) rc = map_of(wh + (size_t)lp[i].N * kp, kp, lp[i].N, lp[i].K, &t.mwl);
+    if (rc) return rc;
+    t.m_tiles = (lp[i].M + 127) / 128;
+    t.n_tiles = (lp[i].N + 127) / 128;
+    t.nkb = (lp[i].K + 31) / 32;
+    begin[i] = (int32_t)total;
+    total += (int64_t)t.m_tiles * t.n_tiles;
+    if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
+    flops += g[i]->flops;
+    bytes += g[i]->bytes;
+  }
+  begin[n] = (int32_t)total;
+  const size_t mbytes = sizeof(CUtensorMap) * maps.size();
+  const size_t pbytes = align16(sizeof(supra::LinTcProb) * n);
+  const size_t bbytes = sizeof(int32_t) * (n + 1);
+  char *h = nullptr, *dv = nullptr;
+  rc = ring_reserve(c, 64 + mbytes + pbytes + bbytes, &h, &dv);
+  if (rc) return rc;
+  const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;  // tensor maps on 64 bytes
+  std::memcpy(h + pad, maps.data(), mbytes);
+  std::memcpy(h + pad + mbytes, probs.data(), sizeof(supra::LinTcProb) * n);
+  std::memcpy(h + pad + mbytes + pbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
+  if (rc) return rc;
+  supra::LinTcLaunch L;
+  L.maps = reinterpret_cast<const CUtensorMap*>(dv + pad);
+  L.probs = reinterpret_cast<const supra::LinTcProb*>(dv + pad + mbytes);
+  L.begin = reinterpret_cast<const int32_t*>(dv + pad + mbytes + pbytes);
+  L.n = n;
+  L.total = (int32_t)total;
+  L.status = c->d_status;
+  const char* name = split ? "linear_tc_tf32x3" : "linear_tc_tf32";
+  cudaError_t e;
+  {
+    ProfScope ps(c, name, flops, bytes);
+    e = supra::launch_linear_tc(L, split, c->stream);
+  }
+  if (e != cudaSuccess) return cuda_err(c, e, name);
+  c->launches += 1;
+  return SUPRA_ATTN_OK;
+}
+
 int do_flush(supra_attn_ctx* c) {
   if (c->queue.empty()) return SUPRA_ATTN_OK;
   std::map<int, std::vector<const Queued*>> groups;
@@ -1155,7 +1305,7 @@ int do_flush(supra_attn_ctx* c) {
     rc = path == PATH_FUSED ? flush_fused(c, kv.second)
          : path == PATH_TF32 ? flush_tma(c, kv.second, true)
          : path == PATH_FP32_TMA ? flush_tma(c, kv.second, false)
-         : path == PATH_LINEAR ? flush_linear(c, kv.second)
+         : path == PATH_LINEAR ? (kv.second[0]->cfg ? flush_linear_tc(c, kv.second) : flush_linear(c, kv.second))
                              : flush_gemm(c, kv.second);
     if (rc) break;
   }
@@ -1281,6 +1431,7 @@ int supra_attn_destroy(supra_attn_ctx* c) {
   for (void* p : c->host_live) cudaFreeHost(p);
   if (c->scratch) cudaFree(c->scratch);
   if (c->gn_stats) cudaFree(c->gn_stats);
+  if (c->lin_split) cudaFree(c->lin_split);
   if (c->ring_h) cudaFreeHost(c->ring_h);
   if (c->ring_d) cudaFree(c->ring_d);
   for (int i = 0; i < 2; ++i)
