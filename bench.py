@@ -396,6 +396,37 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
                                      ldk=3 * C, ldv=3 * C, qOff=r * 3 * C, kOff=r * 3 * C + C, vOff=r * 3 * C + 2 * C,
                                      oOff=r * C)
     enq = supra_attn.lib.supra_attn_enqueue_linear
+    VCODES = {"fp32": supra_attn._lib.FP32, "tf32x3": supra_attn._lib.TF32X3, "tf32": supra_attn._lib.TF32}
+
+    def timed_variants(fn, descs, per_kernel=False):
+        # each numeric variant on the same recorded calls: median ms over reps, kernels launched
+        res = {}
+        for vname, code in VCODES.items():
+            for d in descs:
+                d.variant = code
+            fn()
+            gpu.sync()
+            gpu.profile(True)
+            gpu.profile_reset()
+            times = []
+            for _ in range(reps):
+                flush.fill_(1.0)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            prof = gpu.profile_report()
+            gpu.profile(False)
+            per = {}
+            for r in prof:
+                per[r["name"]] = per.get(r["name"], 0.0) + r["ms"] / reps
+            res[vname] = (statistics.median(times), sorted(per), per)
+        for d in descs:
+            d.variant = VCODES["fp32"]
+        return res
 
     def vae_block():
         supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(dq)), gpu.ctx)
@@ -403,28 +434,11 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
         supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(do)), gpu.ctx)
         gpu.flush()
 
-    vae_block()
-    gpu.sync()
-    gpu.profile(True)
-    gpu.profile_reset()
-    times = []
-    for _ in range(reps):
-        flush.fill_(1.0)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        vae_block()
-        e1.record()
-        torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    prof = gpu.profile_report()
-    gpu.profile(False)
-    ms = statistics.median(times)
     flops = nimg * (2.0 * hw * C * 3 * C + 4.0 * hw * hw * C + 2.0 * hw * C * C)
-    out["vae_block_8"] = {"fp32": {"ms": ms, "image_per_s": nimg / (ms / 1e3),
-                                   "tflops": flops / (ms / 1e3) / 1e12,
-                                   "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
-                                   "kernels": sorted({r["name"] for r in prof})}}
+    out["vae_block_8"] = {}
+    for vname, (ms, kernels, per) in timed_variants(vae_block, [dq, do] + list(da)).items():
+        out["vae_block_8"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                                     "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak, "kernels": kernels}
     del xv, qkv_v, a_v, y_v
 
     # Cross-attention K/V preparation for configs[4]'s 2048 sequences (app/models/dit.js:137-144):
@@ -449,30 +463,19 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
         supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d2)), gpu.ctx)  # hazard: flushes d1 first
         gpu.flush()
 
-    prep()
-    gpu.sync()
-    gpu.profile(True)
-    gpu.profile_reset()
-    times = []
-    for _ in range(reps):
-        flush.fill_(1.0)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        prep()
-        e1.record()
-        torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    prof = gpu.profile_report()
-    gpu.profile(False)
-    ms = statistics.median(times)
     flops = 2.0 * rows * (768 * 576 + 576 * 14 * 1152)
     bytes_ = 4.0 * (rows * 768 + 576 * 768 + rows * 576 * 2 + 14 * 1152 * 576 + rows * 14 * 1152)
-    out["ctx_prep_2048"] = {"fp32": {"ms": ms, "seq_per_s": 2048 / (ms / 1e3), "rows": rows,
-                                     "tflops": flops / (ms / 1e3) / 1e12, "gbs": bytes_ / (ms / 1e3) / 1e9,
-                                     "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
-                                     "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
-                                     "kernels": sorted({r["name"] for r in prof})}}
+    tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0
+    out["ctx_prep_2048"] = {}
+    for vname, (ms, kernels, per) in timed_variants(prep, [d1, d2]).items():
+        r = {"ms": ms, "seq_per_s": 2048 / (ms / 1e3), "rows": rows, "tflops": flops / (ms / 1e3) / 1e12,
+             "gbs": bytes_ / (ms / 1e3) / 1e9, "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm, "kernels": kernels,
+             "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+        if vname == "fp32":
+            r["frac_fp32_peak"] = flops / (ms / 1e3) / 1e12 / fp32_peak
+        else:  # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
+            r["frac_tf32_peak"] = (3 if vname == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 / tf_peak
+        out["ctx_prep_2048"][vname] = r
     del ctx, p, kv_all, wkv
 
     # One whole DiT block (app/models/dit.js:161-194) for 32 images of 256 tokens with ragged
@@ -521,32 +524,14 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
         e(lin[5])
         gpu.flush()
 
-    block()
-    gpu.sync()
-    gpu.profile(True)
-    gpu.profile_reset()
-    times = []
-    for _ in range(reps):
-        flush.fill_(1.0)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        block()
-        e1.record()
-        torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    prof = gpu.profile_report()
-    gpu.profile(False)
-    ms = statistics.median(times)
     lin_flops = 2.0 * R * D * (3 * D + D + D + D + 4 * D + 4 * D)
     att_flops = 4.0 * N * D * (nimg * N + sum(Lb))
     flops = lin_flops + att_flops
-    per = {}
-    for r in prof:
-        per[r["name"]] = per.get(r["name"], 0.0) + r["ms"] / reps
-    out["dit_block_32"] = {"fp32": {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
-                                    "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
-                                    "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}}
+    out["dit_block_32"] = {}
+    for vname, (ms, kernels, per) in timed_variants(block, lin + list(sa) + list(ca)).items():
+        out["dit_block_32"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                                      "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                                      "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
     return out
 
 

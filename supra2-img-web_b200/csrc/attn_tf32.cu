@@ -251,15 +251,15 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         const Tile T = tile_of(L, t);
         const TmaProb* pp = T.p;
         const CUtensorMap* mv = L.maps + pp->mv;
-        const int hx = T.h * kD;
+        const int vx = pp->vx + T.h * kD, vy = pp->vy;  // in registers (the TMA asm clobbers memory)
         bool ok = true;
         for (int j = 0; j < T.nblk; ++j, ++n) {
           const int s = n % Y::NSV;
           if (n >= Y::NSV && !(ok = wait_or_abort(&B->v_empty[s], (uint32_t)(((n / Y::NSV) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
           mbar_arrive_expect_tx(&B->v_full[s], kKVBytes);
           uint8_t* vd = Vs + s * kKVBytes;
-          tc::tma_load_2d(vd, mv, pp->vx + hx, pp->vy + j * kN, &B->v_full[s]);
-          tc::tma_load_2d(vd + kKVSlab, mv, pp->vx + hx + 32, pp->vy + j * kN, &B->v_full[s]);
+          tc::tma_load_2d(vd, mv, vx, vy + j * kN, &B->v_full[s]);
+          tc::tma_load_2d(vd + kKVSlab, mv, vx + 32, vy + j * kN, &B->v_full[s]);
         }
         if (!ok) break;
       }
@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         const CUtensorMap* mq = L.maps + pp->mq;
         const CUtensorMap* mk = L.maps + pp->mk;
         const int hx = T.h * kD;
+        const int kx = pp->kx + hx, ky = pp->ky;  // in registers (the TMA asm clobbers memory)
         if (k > 0 && !wait_or_abort(&B->q_empty, (uint32_t)((k - 1) & 1), abort, L.status, W_Q_EMPTY, n)) break;
         mbar_arrive_expect_tx(&B->q_full, kQBytes);
         tc::tma_load_2d(Qs, mq, pp->qx + hx, pp->qy + T.q0, &B->q_full);
@@ -281,8 +282,8 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           if (n >= kNS && !(ok = wait_or_abort(&B->kv_empty[s], (uint32_t)(((n / kNS) - 1) & 1), abort, L.status, W_KV_EMPTY, n))) break;
           mbar_arrive_expect_tx(&B->kv_full[s], kKVBytes);
           uint8_t* kd = Ks + s * kKVBytes;
-          tc::tma_load_2d(kd, mk, pp->kx + hx, pp->ky + j * kN, &B->kv_full[s]);
-          tc::tma_load_2d(kd + kKVSlab, mk, pp->kx + hx + 32, pp->ky + j * kN, &B->kv_full[s]);
+          tc::tma_load_2d(kd, mk, kx, ky + j * kN, &B->kv_full[s]);
+          tc::tma_load_2d(kd + kKVSlab, mk, kx + 32, ky + j * kN, &B->kv_full[s]);
         }
         if (!ok) break;
       }

@@ -10,11 +10,13 @@
 //                        (SWIZZLE_128B, K-major), the MMA warp issues per 8-deep step one
 //                        product (TF32) or three, lo*hi + hi*lo + hi*hi (TF32X3, the small terms
 //                        first), into a TMEM accumulator. Every kFlush k-blocks the partial sum
-//                        goes to a fresh (double-buffered) accumulator and the epilogue warps add
+//                        goes to a fresh accumulator (four in turn) and the epilogue warps add
 //                        it to the row they hold in registers, in fp32 rounded to nearest, so the
 //                        error does not grow with K as it would in one TMEM accumulator. The
-//                        epilogue then applies bias, activation, gate and residual (the
-//                        reference's order, app/gpu/gemm.js:130-135) and stores the row.
+//                        epilogue then applies bias, activation and gate per row (the
+//                        reference's order, app/gpu/gemm.js:130-135) and passes each 32 x 32
+//                        block through a padded shared-memory slot, so the residual is read and
+//                        y written as whole 128-byte row segments.
 // Persistent: CTA c takes tiles c, c + grid, ... of the launch's (problem, row tile, column tile)
 // list, column tiles innermost. 6 warps: TMA producer, MMA issuer, 4 epilogue warps (warp w owns
 // TMEM lanes 32*(w%4) .. +31, i.e. output rows). One CTA per SM (three 64 KB stages). Every wait
@@ -29,13 +31,16 @@ constexpr int kStages = 3;
 constexpr int kFlush = 4;                        // k-blocks per TMEM partial sum
 constexpr uint32_t kTile = kBM * kBK * 4;        // one operand tile: 128 rows x 128 bytes = 16 KB
 constexpr uint32_t kStage = 4 * kTile;           // hi(X), hi(W), lo(X), lo(W)
-constexpr uint32_t OFF_BAR = kStages * kStage;
+constexpr uint32_t kSlot = 32 * 33 * 4;          // epilogue staging per warp: 32 rows x 32 columns, padded
+constexpr uint32_t OFF_EPI = kStages * kStage;
+constexpr uint32_t OFF_BAR = OFF_EPI + 4 * kSlot;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
-constexpr uint32_t kTmemCols = 256;              // two 128-column accumulators
+constexpr int kAcc = 4;                          // TMEM accumulators (partial sums in flight)
+constexpr uint32_t kTmemCols = kAcc * 128;       // 512: four 128-column accumulators
 constexpr int kThreads = 192;
 
 struct Bars {
-  uint64_t full[kStages], empty[kStages], accf[2], acce[2], drain;
+  uint64_t full[kStages], empty[kStages], accf[kAcc], acce[kAcc], drain;
   int32_t abort;
   uint32_t tmem;
 };
@@ -93,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       mbar_init(&B->full[s], 1);
       mbar_init(&B->empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       mbar_init(&B->accf[b], 1);
       mbar_init(&B->acce[b], 128);
     }
@@ -116,20 +121,28 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       int g = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
+        // the tile's fields in registers: each TMA issue below is an asm statement that clobbers
+        // memory, after which fields read through P would be loaded from global memory again
         const TileRef T = tile_ref(L, t);
         const LinTcProb* P = T.p;
-        for (int kb = 0; kb < P->nkb; ++kb, ++g) {
+        const int nkb = P->nkb;
+        const CUtensorMap* mxh = L.maps + P->mxh;
+        const CUtensorMap* mwh = L.maps + P->mwh;
+        const CUtensorMap* mxl = L.maps + P->mxl;
+        const CUtensorMap* mwl = L.maps + P->mwl;
+        const int ym = T.mt * kBM, yn = T.nt * kBN;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
           const int s = g % kStages;
           if (g >= kStages &&
               !(ok = wait_or_abort(&B->empty[s], (uint32_t)(((g / kStages) - 1) & 1), abort, L.status, W_EMPTY, g)))
             break;
           uint8_t* st = base + s * kStage;
           mbar_arrive_expect_tx(&B->full[s], SPLIT ? 4 * kTile : 2 * kTile);
-          tma_load_2d(st, L.maps + P->mxh, kb * kBK, T.mt * kBM, &B->full[s]);
-          tma_load_2d(st + kTile, L.maps + P->mwh, kb * kBK, T.nt * kBN, &B->full[s]);
+          tma_load_2d(st, mxh, kb * kBK, ym, &B->full[s]);
+          tma_load_2d(st + kTile, mwh, kb * kBK, yn, &B->full[s]);
           if (SPLIT) {
-            tma_load_2d(st + 2 * kTile, L.maps + P->mxl, kb * kBK, T.mt * kBM, &B->full[s]);
-            tma_load_2d(st + 3 * kTile, L.maps + P->mwl, kb * kBK, T.nt * kBN, &B->full[s]);
+            tma_load_2d(st + 2 * kTile, mxl, kb * kBK, ym, &B->full[s]);
+            tma_load_2d(st + 3 * kTile, mwl, kb * kBK, yn, &B->full[s]);
           }
         }
       }
@@ -147,16 +160,16 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
         const int s = g % kStages;
         const bool start = (kb % kFlush) == 0;
         const bool end = (kb % kFlush) == kFlush - 1 || kb == nkb - 1;
-        if (start && f >= 2)  // the epilogue has read this accumulator's previous partial sum
-          ok = __all_sync(0xffffffffu, wait_or_abort(&B->acce[f & 1], (uint32_t)(((f >> 1) - 1) & 1), abort, L.status,
-                                                     W_ACCE, f));
+        if (start && f >= kAcc)  // the epilogue has read this accumulator's previous partial sum
+          ok = __all_sync(0xffffffffu, wait_or_abort(&B->acce[f % kAcc], (uint32_t)(((f / kAcc) - 1) & 1), abort,
+                                                     L.status, W_ACCE, f));
         if (!ok) break;
         ok = __all_sync(0xffffffffu, wait_or_abort(&B->full[s], (uint32_t)((g / kStages) & 1), abort, L.status, W_FULL, g));
         if (!ok) break;
         tc::fence_after_sync();
         if (lane == 0) {
           const uint8_t* st = base + s * kStage;
-          const uint32_t d = tmem + (uint32_t)(f & 1) * kBN;
+          const uint32_t d = tmem + (uint32_t)(f % kAcc) * kBN;
           auto desc = [&](const uint8_t* tile, int k8) {
             return tc::smem_desc(tile + k8 * 32, 16, 1024, tc::kLayoutSW128);
           };
@@ -172,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
             }
           }
           tc::commit(&B->empty[s]);
-          if (end) tc::commit(&B->accf[f & 1]);
+          if (end) tc::commit(&B->accf[f % kAcc]);
         }
         __syncwarp();
         if (end) ++f;
@@ -181,23 +194,31 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 55, g);
   } else {
     // ---------------- epilogue (warps 2..5): one output row per thread ----------------
-    const int q4 = warp & 3;
-    const int row = 32 * q4 + lane;
+    const int q4 = warp & 3;  // this warp's 32 rows of the tile (its TMEM lanes); lane = row
     const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
     int f = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x) {
       const TileRef T = tile_ref(L, t);
-      const LinProb& P = T.p->p;
       const int nkb = T.p->nkb;
+      // the problem's epilogue fields in registers (the stores below would otherwise make the
+      // compiler reload them from global memory for every column)
+      const LinProb& P = T.p->p;
+      const float* bias = P.bias;
+      const float* gate = P.gate;
+      const float* resid = P.resid;
+      float* y = P.y;
+      const int64_t ldy = P.ldy, ldr = P.ldr;
+      const int act = P.act, M = P.M, N = P.N;
       float o[kBN];
 #pragma unroll
       for (int c = 0; c < kBN; ++c) o[c] = 0.f;
       for (int kb0 = 0; kb0 < nkb; kb0 += kFlush, ++f) {
-        ok = __all_sync(0xffffffffu, wait_or_abort(&B->accf[f & 1], (uint32_t)((f >> 1) & 1), abort, L.status, W_ACCF, f));
+        ok = __all_sync(0xffffffffu, wait_or_abort(&B->accf[f % kAcc], (uint32_t)((f / kAcc) & 1), abort, L.status,
+                                                   W_ACCF, f));
         if (!ok) break;
         tc::fence_after_sync();
-        const uint32_t acc = tl + (uint32_t)(f & 1) * kBN;
+        const uint32_t acc = tl + (uint32_t)(f % kAcc) * kBN;
 #pragma unroll
         for (int c32 = 0; c32 < kBN / 32; ++c32) {
           float ad[32];
@@ -211,25 +232,42 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
           }
         }
         tc::fence_before_sync();
-        mbar_arrive(&B->acce[f & 1]);
+        mbar_arrive(&B->acce[f % kAcc]);
       }
       if (!ok) break;
-      // y = resid + gate * act(o + bias), the reference's epilogue order
-      const int r = T.mt * kBM + row;
-      if (r < P.M) {
-        const int c0 = T.nt * kBN;
-        const int nc = min(kBN, P.N - c0);
-        float* yrow = P.y + (int64_t)r * P.ldy + c0;
-        const float* rrow = P.resid ? P.resid + (int64_t)r * P.ldr + c0 : nullptr;
+      // y = resid + gate * act(o + bias), the reference's epilogue order: gate * act(o + bias) per
+      // row in registers (bias and gate are the same column for every thread: broadcast loads),
+      // then each 32 x 32 block through the warp's slot (row stride 33: conflict-free both ways)
+      // and out as rows, lane = column, with the residual added on the way.
+      const int c0 = T.nt * kBN;
+      const int nc = min(kBN, N - c0);
+      const int r0 = T.mt * kBM + 32 * q4;   // this warp's first row
+      const int nr = min(32, M - r0);        // rows of the 32 that exist (may be <= 0)
+      float* slot = reinterpret_cast<float*>(base + OFF_EPI + q4 * kSlot);
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          if (c < nc) {
-            float v = o[c] + (P.bias ? __ldg(P.bias + c0 + c) : 0.f);
-            if (P.act != kActNone) v = linear_act(P.act, v);
-            if (P.gate) v *= __ldg(P.gate + c0 + c);
-            yrow[c] = rrow ? rrow[c] + v : v;
+      for (int cb = 0; cb < kBN / 32; ++cb) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int cc = 32 * cb + c;
+          float v = o[cc];
+          if (cc < nc) {
+            v += bias ? __ldg(bias + c0 + cc) : 0.f;
+            if (act != kActNone) v = linear_act(act, v);
+            if (gate) v *= __ldg(gate + c0 + cc);
+          }
+          slot[lane * 33 + c] = v;
+        }
+        __syncwarp();
+        const int col = 32 * cb + lane;
+        if (col < nc) {
+          for (int rr = 0; rr < nr; ++rr) {
+            const float v = slot[rr * 33 + lane];
+            const int64_t rg = r0 + rr;
+            float* yp = y + rg * ldy + c0 + col;
+            *yp = resid ? resid[rg * ldr + c0 + col] + v : v;
           }
         }
+        __syncwarp();
       }
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 56, f);
