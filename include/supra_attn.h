@@ -160,7 +160,10 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  * tracking, one grouped launch per flush). x: M rows of K floats, row stride ldx, first row at
  * x_off; w: [N, K] row-major with row stride ldw >= K (the reference's weight layout, x @ W^T);
  * bias: N floats or NULL; y: M rows of N floats, row stride ldy >= N, first row at y_off. All
- * counts in floats. Computed in fp32 with FFMA (TF32 and TF32X3 requests run the same kernel).
+ * counts in floats. SUPRA_ATTN_FP32: fp32 FFMA. SUPRA_ATTN_TF32 / SUPRA_ATTN_TF32X3 with K >= 32: on
+ * the tensor cores, TF32 products or the split form (three TF32 products per product, held to the
+ * FP32 tolerance); x (normalised when asked) and w are first copied as hi / lo parts into a
+ * context-owned buffer. Shallower products run the FFMA kernel.
  * Two optional fusions (the VAE mid-block attention, app/models/vae.js:77-94):
  *   - gn != NULL: x is GroupNorm-ed on the way in (ops.groupnorm, app/gpu/ops.js:82-92,
  *     app/gpu/kernels.js:117-162): x rows form images of gn->rows_per_image rows; per image and
