@@ -13,10 +13,9 @@
 //                        goes to a fresh accumulator (four in turn) and the epilogue warps add
 //                        it to the row they hold in registers, in fp32 rounded to nearest, so the
 //                        error does not grow with K as it would in one TMEM accumulator. The
-//                        epilogue then applies bias, activation and gate per row (the
-//                        reference's order, app/gpu/gemm.js:130-135) and passes each 32 x 32
-//                        block through a padded shared-memory slot, so the residual is read and
-//                        y written as whole 128-byte row segments.
+//                        epilogue then applies bias, activation, gate and residual (the
+//                        reference's order, app/gpu/gemm.js:130-135) and each thread stores its
+//                        row (float4 stores when the rows are 16-byte aligned).
 // Persistent: CTA c takes tiles c, c + grid, ... of the launch's (problem, row tile, column tile)
 // list, column tiles innermost. 6 warps: TMA producer, MMA issuer, 4 epilogue warps (warp w owns
 // TMEM lanes 32*(w%4) .. +31, i.e. output rows). One CTA per SM (three 64 KB stages). Every wait
@@ -31,9 +30,7 @@ constexpr int kStages = 3;
 constexpr int kFlush = 4;                        // k-blocks per TMEM partial sum
 constexpr uint32_t kTile = kBM * kBK * 4;        // one operand tile: 128 rows x 128 bytes = 16 KB
 constexpr uint32_t kStage = 4 * kTile;           // hi(X), hi(W), lo(X), lo(W)
-constexpr uint32_t kSlot = 32 * 33 * 4;          // epilogue staging per warp: 32 rows x 32 columns, padded
-constexpr uint32_t OFF_EPI = kStages * kStage;
-constexpr uint32_t OFF_BAR = OFF_EPI + 4 * kSlot;
+constexpr uint32_t OFF_BAR = kStages * kStage;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int kAcc = 4;                          // TMEM accumulators (partial sums in flight)
 constexpr uint32_t kTmemCols = kAcc * 128;       // 512: four 128-column accumulators
@@ -203,13 +200,18 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       const int nkb = T.p->nkb;
       // the problem's epilogue fields in registers (the stores below would otherwise make the
       // compiler reload them from global memory for every column)
+      // (the empty asm statements make the values opaque: at this register pressure the
+      // compiler would otherwise re-load them from the descriptor in global memory at each use,
+      // a dependent load per output column)
       const LinProb& P = T.p->p;
       const float* bias = P.bias;
       const float* gate = P.gate;
       const float* resid = P.resid;
       float* y = P.y;
-      const int64_t ldy = P.ldy, ldr = P.ldr;
-      const int act = P.act, M = P.M, N = P.N;
+      int64_t ldy = P.ldy, ldr = P.ldr;
+      int act = P.act, M = P.M, N = P.N;
+      asm volatile("" : "+l"(bias), "+l"(gate), "+l"(resid), "+l"(y), "+l"(ldy), "+l"(ldr));
+      asm volatile("" : "+r"(act), "+r"(M), "+r"(N));
       float o[kBN];
 #pragma unroll
       for (int c = 0; c < kBN; ++c) o[c] = 0.f;
@@ -235,39 +237,47 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
         mbar_arrive(&B->acce[f % kAcc]);
       }
       if (!ok) break;
-      // y = resid + gate * act(o + bias), the reference's epilogue order: gate * act(o + bias) per
-      // row in registers (bias and gate are the same column for every thread: broadcast loads),
-      // then each 32 x 32 block through the warp's slot (row stride 33: conflict-free both ways)
-      // and out as rows, lane = column, with the residual added on the way.
+      // y = resid + gate * act(o + bias), the reference's epilogue order, per row from registers
+      // (bias and gate are the same column for every thread: broadcast loads). Each thread writes
+      // its own row: float4 stores when y (and the residual) have 16-byte rows. Staging through
+      // shared memory for coalesced rows was slower: shared loads wait about a thousand cycles
+      // while the tensor core streams the next tile's operands.
       const int c0 = T.nt * kBN;
       const int nc = min(kBN, N - c0);
-      const int r0 = T.mt * kBM + 32 * q4;   // this warp's first row
-      const int nr = min(32, M - r0);        // rows of the 32 that exist (may be <= 0)
-      float* slot = reinterpret_cast<float*>(base + OFF_EPI + q4 * kSlot);
+      const int r = T.mt * kBM + 32 * q4 + lane;
+      if (bias || gate || act != kActNone) {
 #pragma unroll
-      for (int cb = 0; cb < kBN / 32; ++cb) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int cc = 32 * cb + c;
-          float v = o[cc];
-          if (cc < nc) {
-            v += bias ? __ldg(bias + c0 + cc) : 0.f;
+        for (int c = 0; c < kBN; ++c) {
+          if (c < nc) {
+            float v = o[c] + (bias ? __ldg(bias + c0 + c) : 0.f);
             if (act != kActNone) v = linear_act(act, v);
-            if (gate) v *= __ldg(gate + c0 + cc);
-          }
-          slot[lane * 33 + c] = v;
-        }
-        __syncwarp();
-        const int col = 32 * cb + lane;
-        if (col < nc) {
-          for (int rr = 0; rr < nr; ++rr) {
-            const float v = slot[rr * 33 + lane];
-            const int64_t rg = r0 + rr;
-            float* yp = y + rg * ldy + c0 + col;
-            *yp = resid ? resid[rg * ldr + c0 + col] + v : v;
+            if (gate) v *= __ldg(gate + c0 + c);
+            o[c] = v;
           }
         }
-        __syncwarp();
+      }
+      if (r < M) {
+        float* yrow = y + (int64_t)r * ldy + c0;
+        const float* rrow = resid ? resid + (int64_t)r * ldr + c0 : nullptr;
+        const bool vec = ((reinterpret_cast<uintptr_t>(yrow) & 15u) == 0) && (nc & 3) == 0 &&
+                         (!rrow || (reinterpret_cast<uintptr_t>(rrow) & 15u) == 0);
+        if (vec) {
+#pragma unroll
+          for (int c = 0; c < kBN; c += 4) {
+            if (c < nc) {
+              float4 val = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+              if (rrow) {
+                const float4 rv = *reinterpret_cast<const float4*>(rrow + c);
+                val = make_float4(rv.x + val.x, rv.y + val.y, rv.z + val.z, rv.w + val.w);
+              }
+              *reinterpret_cast<float4*>(yrow + c) = val;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (c < nc) yrow[c] = rrow ? rrow[c] + o[c] : o[c];
+        }
       }
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 56, f);
