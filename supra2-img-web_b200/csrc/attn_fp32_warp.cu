@@ -223,8 +223,9 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
   uint32_t k = 0;  // position in the CTA's tile sequence
   for (int t = t0; t < L.total; t += (int)gridDim.x, ++k) {
     const TmaProb* __restrict__ pp = T.p;
-    const int Lk = pp->Lk;
-    const float sl2 = pp->scale_log2;
+    int Lk = pp->Lk;
+    float sl2 = pp->scale_log2;
+    asm volatile("" : "+r"(Lk), "+f"(sl2));  // kept in registers, not re-loaded from the descriptor
     const int nblk = T.nblk;
     // this lane's first output row, read now rather than behind the last block
     const int64_t ldo = pp->ldo;

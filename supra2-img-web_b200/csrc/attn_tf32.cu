@@ -356,7 +356,8 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     };
     for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
       const Tile T = tile_of(L, t);
-      const int Lk = T.p->Lk;
+      int Lk = T.p->Lk;
+      asm volatile("" : "+r"(Lk));  // kept in a register (see the softmax warps)
       // split kernel: the softmax threads split this tile's Q only after the previous tile's
       // epilogue, which waits for that tile's last PV product: issue it first
       if (SPLIT && pend_n >= 0) ok = issue_pv();
@@ -427,8 +428,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++kt) {
       const Tile T = tile_of(L, t);
       const TmaProb* pp = T.p;
-      const int Lk = pp->Lk, Lq = pp->Lq;
-      const float sl2 = pp->scale_log2;
+      int Lk = pp->Lk, Lq = pp->Lq;
+      float sl2 = pp->scale_log2;
+      // opaque: kept in registers rather than re-loaded from the descriptor at each block
+      asm volatile("" : "+r"(Lk), "+r"(Lq), "+f"(sl2));
       float m = -INFINITY, l = 0.f;
       if constexpr (SPLIT) {
 #pragma unroll
@@ -671,7 +674,8 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     int n = 0, k = 0;
     for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
       const Tile T = tile_of(L, t);
-      const int Lk = T.p->Lk;
+      int Lk = T.p->Lk;
+      asm volatile("" : "+r"(Lk));  // kept in a register (see the softmax warps)
       for (int j = 0; ok && j < T.nblk; ++j, ++n) {
         const int ns = vconv ? kNSV : kNS;
         const int s = n % ns;
