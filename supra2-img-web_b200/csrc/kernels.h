@@ -185,7 +185,7 @@ struct alignas(16) LinTcProb {
   int32_t mxh, mxl, mwh, mwl;  // tensor maps of hi(x), lo(x), hi(w), lo(w) (lo: split form only)
   int32_t m_tiles, n_tiles;    // 128-row and 128-column output tiles
   int32_t nkb;                 // 32-deep k-blocks: ceil(K / 32)
-  int32_t pad;
+  int32_t my;                  // tensor map of y (32 x 32 boxes, TMA stores), or -1: per-row stores
 };
 static_assert(sizeof(LinTcProb) % 16 == 0, "LinTcProb is packed into the descriptor ring");
 struct LinTcLaunch {

@@ -17,7 +17,7 @@
 //                        reference's order, app/gpu/gemm.js:130-135) and each thread stores its
 //                        row (float4 stores when the rows are 16-byte aligned).
 // Persistent: CTA c takes tiles c, c + grid, ... of the launch's (problem, row tile, column tile)
-// list, column tiles innermost. 6 warps: TMA producer, MMA issuer, 4 epilogue warps (warp w owns
+// list, in groups of 16 row tiles with the row tile innermost. 6 warps: TMA producer, MMA issuer, 4 epilogue warps (warp w owns
 // TMEM lanes 32*(w%4) .. +31, i.e. output rows). One CTA per SM (three 64 KB stages). Every wait
 // is bounded; on a timeout the CTA records the failure, drains its MMAs, frees TMEM and leaves.
 #include "tcgen05.cuh"
@@ -30,7 +30,9 @@ constexpr int kStages = 3;
 constexpr int kFlush = 4;                        // k-blocks per TMEM partial sum
 constexpr uint32_t kTile = kBM * kBK * 4;        // one operand tile: 128 rows x 128 bytes = 16 KB
 constexpr uint32_t kStage = 4 * kTile;           // hi(X), hi(W), lo(X), lo(W)
-constexpr uint32_t OFF_BAR = kStages * kStage;
+constexpr uint32_t kSlot = 32 * 32 * 4;          // epilogue: one 32 x 32 block, 128-byte rows, swizzled
+constexpr uint32_t OFF_EPI = kStages * kStage;   // two slots per epilogue warp (TMA stores)
+constexpr uint32_t OFF_BAR = OFF_EPI + 4 * 2 * kSlot;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int kAcc = 4;                          // TMEM accumulators (partial sums in flight)
 constexpr uint32_t kTmemCols = kAcc * 128;       // 512: four 128-column accumulators
@@ -42,6 +44,7 @@ struct Bars {
   uint32_t tmem;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 
 enum WaitId : int32_t { W_EMPTY = 51, W_FULL = 52, W_ACCE = 53, W_ACCF = 54 };
 
@@ -66,13 +69,22 @@ struct TileRef {
   const LinTcProb* p;
   int mt, nt;
 };
+// Tiles walk a problem in groups of kGroup row tiles: within a group the row tile is innermost,
+// so the CTAs running at one time share a few weight column tiles (each read from memory once per
+// group) and the group's rows of x stay in L2. (Column tiles innermost over all rows made every
+// row tile read all of w again: for a [131K, 576] x [16128, 576]^T product that is 74 GB.)
+constexpr int kGroup = 16;
 __device__ __forceinline__ TileRef tile_ref(const LinTcLaunch& L, int t) {
   TileRef r;
   const int pi = find_problem(L.begin, L.n, t);
   r.p = L.probs + pi;
   const int local = t - __ldg(L.begin + pi);
-  r.mt = local / r.p->n_tiles;
-  r.nt = local - r.mt * r.p->n_tiles;
+  const int nt_all = r.p->n_tiles, mt_all = r.p->m_tiles;
+  const int g = local / (kGroup * nt_all);       // row-tile group
+  const int rem = local - g * (kGroup * nt_all);
+  const int gs = min(kGroup, mt_all - g * kGroup);  // row tiles in this group
+  r.nt = rem / gs;
+  r.mt = g * kGroup + (rem - r.nt * gs);
   return r;
 }
 
@@ -212,9 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       int act = P.act, M = P.M, N = P.N;
       asm volatile("" : "+l"(bias), "+l"(gate), "+l"(resid), "+l"(y), "+l"(ldy), "+l"(ldr));
       asm volatile("" : "+r"(act), "+r"(M), "+r"(N));
+      const int c0 = T.nt * kBN;
+      const int nc = min(kBN, N - c0);
+      // the row starts at the bias: its loads are issued here, ahead of the wait for the first
+      // partial sum (at this register pressure, loads in the epilogue loop would run one by one)
       float o[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) o[c] = 0.f;
+      for (int c = 0; c < kBN; ++c) o[c] = (bias && c < nc) ? __ldg(bias + c0 + c) : 0.f;
       for (int kb0 = 0; kb0 < nkb; kb0 += kFlush, ++f) {
         ok = __all_sync(0xffffffffu, wait_or_abort(&B->accf[f % kAcc], (uint32_t)((f / kAcc) & 1), abort, L.status,
                                                    W_ACCF, f));
@@ -238,25 +254,67 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       }
       if (!ok) break;
       // y = resid + gate * act(o + bias), the reference's epilogue order, per row from registers
-      // (bias and gate are the same column for every thread: broadcast loads). Each thread writes
+      // (o holds the bias already; gate is the same column for every thread: broadcast loads).
+      // Each thread writes
       // its own row: float4 stores when y (and the residual) have 16-byte rows. Staging through
       // shared memory for coalesced rows was slower: shared loads wait about a thousand cycles
       // while the tensor core streams the next tile's operands.
-      const int c0 = T.nt * kBN;
-      const int nc = min(kBN, N - c0);
       const int r = T.mt * kBM + 32 * q4 + lane;
-      if (bias || gate || act != kActNone) {
+      int my = T.p->my;
+      asm volatile("" : "+r"(my));
+      if (gate || act != kActNone) {
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
           if (c < nc) {
-            float v = o[c] + (bias ? __ldg(bias + c0 + c) : 0.f);
+            float v = o[c];
             if (act != kActNone) v = linear_act(act, v);
             if (gate) v *= __ldg(gate + c0 + c);
             o[c] = v;
           }
         }
       }
-      if (r < M) {
+      if (my >= 0) {
+        // TMA stores: the residual first (this thread's row), then each 32 x 32 block through one
+        // of the warp's two slots (16-byte chunks swizzled by row, SWIZZLE_128B: conflict-free
+        // float4 writes); lane 0 stores the block, and the TMA clips rows past M and columns
+        // past N. A slot is rewritten once at most one store (the other slot's) is still reading.
+        if (resid && r < M) {
+          const float* rrow = resid + (int64_t)r * ldr + c0;
+          if ((reinterpret_cast<uintptr_t>(rrow) & 15u) == 0 && (nc & 3) == 0) {
+#pragma unroll
+            for (int c = 0; c < kBN; c += 4)
+              if (c < nc) {
+                const float4 rv = *reinterpret_cast<const float4*>(rrow + c);
+                o[c] += rv.x, o[c + 1] += rv.y, o[c + 2] += rv.z, o[c + 3] += rv.w;
+              }
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBN; ++c)
+              if (c < nc) o[c] += rrow[c];
+          }
+        }
+        const CUtensorMap* ymap = L.maps + my;
+        uint8_t* slots = base + OFF_EPI + q4 * 2 * kSlot;
+#pragma unroll
+        for (int cb = 0; cb < kBN / 32; ++cb) {
+          // blocks wholly past N are skipped altogether (every block written to a slot is stored,
+          // which is what keeps "at most one store still reading" on the other slot)
+          if (32 * cb >= nc) break;
+          uint8_t* slot = slots + (cb & 1) * kSlot;
+          if (lane == 0) tc::bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            *reinterpret_cast<float4*>(slot + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
+                make_float4(o[32 * cb + 4 * c4], o[32 * cb + 4 * c4 + 1], o[32 * cb + 4 * c4 + 2], o[32 * cb + 4 * c4 + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_store_2d(ymap, slot, c0 + 32 * cb, T.mt * kBM + 32 * q4);
+            tc::bulk_commit_group();
+          }
+        }
+      } else if (r < M) {
         float* yrow = y + (int64_t)r * ldy + c0;
         const float* rrow = resid ? resid + (int64_t)r * ldr + c0 : nullptr;
         const bool vec = ((reinterpret_cast<uintptr_t>(yrow) & 15u) == 0) && (nc & 3) == 0 &&
@@ -281,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       }
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 56, f);
+    if (lane == 0) tc::bulk_wait_group_all();  // this warp's TMA stores are complete
   }
 
   tc::fence_before_sync();

@@ -1218,8 +1218,8 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   // exact fp32 (the tensor core takes the hi copies as TF32 values)
   std::vector<CUtensorMap> maps;
   std::unordered_map<MapKey, int32_t, MapKeyHash> index;
-  auto map_of = [&](const float* b, int64_t kp, int64_t rows, int64_t cols, int32_t* out) -> int {
-    const MapKey k{reinterpret_cast<uintptr_t>(b), kp, rows, cols, 32, 128, (int32_t)CU_TENSOR_MAP_SWIZZLE_128B, 0};
+  auto map_of = [&](const float* b, int64_t kp, int64_t rows, int64_t cols, int32_t* out, int32_t box_rows = 128) -> int {
+    const MapKey k{reinterpret_cast<uintptr_t>(b), kp, rows, cols, 32, box_rows, (int32_t)CU_TENSOR_MAP_SWIZZLE_128B, 0};
     auto it = index.find(k);
     if (it == index.end()) {
       auto ct = c->map_cache.find(k);
@@ -1250,6 +1250,10 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     if (!rc) rc = map_of(wh, kp, lp[i].N, lp[i].K, &t.mwh);
     if (!rc && split) rc = map_of(xh + (size_t)lp[i].M * kp, kp, lp[i].M, lp[i].K, &t.mxl);
     if (!rc && split) rc = map_of(wh + (size_t)lp[i].N * kp, kp, lp[i].N, lp[i].K, &t.mwl);
+    // y through TMA stores (32 x 32 boxes) when its rows are 16-byte aligned; else per-row stores
+    t.my = -1;
+    if (!rc && (reinterpret_cast<uintptr_t>(lp[i].y) & 15u) == 0 && (lp[i].ldy & 3) == 0)
+      rc = map_of(lp[i].y, lp[i].ldy, lp[i].M, lp[i].N, &t.my, 32);
     if (rc) return rc;
     t.m_tiles = (lp[i].M + 127) / 128;
     t.n_tiles = (lp[i].N + 127) / 128;
