@@ -242,12 +242,12 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------------------------------------
-def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
+def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
     """BASELINE.json configs[0..3] as extra figures: DiT self (B=2), DiT cross (128 ragged
     sequences), T5 (256 prompts, ragged L, bias), VAE mid-block (1, 8, 64 images). Each rep is one
     flush of the call site's calls, timed with CUDA events after the L2 is flushed; FP32 and TF32
     requests both reported with the kernels that ran (TF32 requests the tensor-core kernel does
-    not cover run the FP32 kernels)."""
+    not cover run the FP32 kernels). only: names of the call sites to run (default all)."""
     import supra_attn
 
     peaks = measured_peaks()
@@ -257,6 +257,7 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
     g = torch.Generator(device=dev).manual_seed(seed)
     gc = torch.Generator().manual_seed(seed)
     out = {}
+    want = lambda name: only is None or name in only
 
     def run(name, units, unit_name, make_descs, flops, bytes_):
         res = {}
@@ -287,114 +288,6 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
                             "kernels": sorted({p["name"] for p in prof})}
         out[name] = res
 
-    # DiT self-attention, B = 2, interleaved qkv
-    qkv = torch.randn(2 * 256 * 1728, device=dev, generator=g)
-    o1 = torch.empty(2 * 256 * 576, device=dev)
-
-    def c1(variant):
-        arr = (supra_attn.Desc * 2)()
-        for b in range(2):
-            r = b * 256 * 1728
-            arr[b] = supra_attn.make_desc(q=qkv, k=qkv, v=qkv, out=o1, Lq=256, Lk=256, H=9, D=64, ldq=1728, ldk=1728,
-                                          ldv=1728, qOff=r, kOff=r + 576, vOff=r + 1152, oOff=b * 256 * 576,
-                                          variant=variant)
-        return arr
-
-    f1 = 2 * 4.0 * 256 * 256 * 64 * 9
-    run("dit_self_b2", 2, "seq", c1, f1, 2 * 4.0 * (2 * 256 * 576 + 2 * 256 * 576))
-
-    # DiT cross-attention, 64 prompts x CFG, ragged L
-    Ls = torch.randint(1, 129, (128,), generator=gc).tolist()
-    q2 = torch.randn(128 * 256 * 576, device=dev, generator=g)
-    kv2 = [torch.randn(L * 1152, device=dev, generator=g) for L in Ls]
-    o2 = torch.empty_like(q2)
-
-    def c2(variant):
-        arr = (supra_attn.Desc * 128)()
-        for b, L in enumerate(Ls):
-            arr[b] = supra_attn.make_desc(q=q2, k=kv2[b], v=kv2[b], out=o2, Lq=256, Lk=L, H=9, D=64, ldq=576,
-                                          ldk=1152, ldv=1152, qOff=b * 256 * 576, kOff=0, vOff=576,
-                                          oOff=b * 256 * 576, variant=variant)
-        return arr
-
-    run("dit_cross_128", 128, "seq", c2, sum(4.0 * 256 * L * 64 * 9 for L in Ls),
-        sum(4.0 * (2 * 256 * 576 + 2 * L * 576) for L in Ls))
-
-    # T5 encoder attention, 256 prompts, ragged L, relative-position bias, scale 1
-    Lt = torch.randint(1, 129, (256,), generator=gc).tolist()
-    table = (torch.randn(32 * 12, generator=gc) * 0.1).to(dev)
-    qs = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
-    ks = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
-    vs = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
-    os_ = [torch.empty(L * 768, device=dev) for L in Lt]
-    biases = [gpu.wrap(torch.empty(12 * L * L, device=dev)) for L in Lt]
-    for L, bt in zip(Lt, biases):
-        supra_attn.position_bias(gpu, table, L, H=12, out=bt)
-    gpu.sync()
-
-    def c3(variant):
-        arr = (supra_attn.Desc * 256)()
-        for i, L in enumerate(Lt):
-            arr[i] = supra_attn.make_desc(q=qs[i], k=ks[i], v=vs[i], out=os_[i], bias=biases[i], Lq=L, Lk=L, H=12, D=64,
-                                          ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
-        return arr
-
-    run("t5_256", 256, "prompt", c3, sum(4.0 * L * L * 64 * 12 for L in Lt),
-        sum(4.0 * (4 * L * 768 + 12 * L * L) for L in Lt))
-
-    # the same T5 calls with the [32, 12] table in place of the expanded bias (the kernels form
-    # the bias; the host's per-prompt bias build and its 48*L^2 bytes drop out)
-    def c3t(variant):
-        arr = (supra_attn.Desc * 256)()
-        for i, L in enumerate(Lt):
-            arr[i] = supra_attn.make_desc(q=qs[i], k=ks[i], v=vs[i], out=os_[i], t5_table=table, Lq=L, Lk=L, H=12,
-                                          D=64, ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
-        return arr
-
-    run("t5_256_table", 256, "prompt", c3t, sum(4.0 * L * L * 64 * 12 for L in Lt),
-        sum(4.0 * (4 * L * 768 + 32 * 12) for L in Lt))
-
-    # VAE mid-block single-head attention, 1024 tokens x 512 channels
-    for nimg in (1, 8, 64):
-        qv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
-        kvv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
-        vv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
-        ov = torch.empty_like(qv)
-
-        def c4(variant, nimg=nimg, qv=qv, kvv=kvv, vv=vv, ov=ov):
-            arr = (supra_attn.Desc * nimg)()
-            for i in range(nimg):
-                o = i * 1024 * 512
-                arr[i] = supra_attn.make_desc(q=qv, k=kvv, v=vv, out=ov, Lq=1024, Lk=1024, H=1, D=512, ldq=512,
-                                              ldk=512, ldv=512, qOff=o, kOff=o, vOff=o, oOff=o, variant=variant)
-            return arr
-
-        run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512)
-        del qv, kvv, vv, ov
-
-    # VAE mid-block attention, whole block fused (app/models/vae.js:77-94), 8 images of 32x32:
-    # GroupNorm folded into one stacked q/k/v product, attention reading q/k/v in place, residual
-    # folded into the output projection.
-    nimg, hw, C = 8, 1024, 512
-    xv = torch.randn(nimg * hw * C, device=dev, generator=g)
-    gam = 1 + 0.1 * torch.randn(C, device=dev, generator=g)
-    bet = 0.1 * torch.randn(C, device=dev, generator=g)
-    wqkv = torch.randn(3 * C * C, device=dev, generator=g) * C ** -0.5
-    bqkv = 0.1 * torch.randn(3 * C, device=dev, generator=g)
-    wo = torch.randn(C * C, device=dev, generator=g) * C ** -0.5
-    bo = 0.1 * torch.randn(C, device=dev, generator=g)
-    qkv_v = torch.empty(nimg * hw * 3 * C, device=dev)
-    a_v = torch.empty(nimg * hw * C, device=dev)
-    y_v = torch.empty(nimg * hw * C, device=dev)
-    dq = supra_attn.make_linear_desc(x=xv, w=wqkv, bias=bqkv, y=qkv_v, M=nimg * hw, N=3 * C, K=C,
-                                     groupnorm=dict(gamma=gam, beta=bet, groups=32, rows_per_image=hw))
-    do = supra_attn.make_linear_desc(x=a_v, w=wo, bias=bo, y=y_v, M=nimg * hw, N=C, K=C, resid=xv)
-    da = (supra_attn.Desc * nimg)()
-    for i in range(nimg):
-        r = i * hw
-        da[i] = supra_attn.make_desc(q=qkv_v, k=qkv_v, v=qkv_v, out=a_v, Lq=hw, Lk=hw, H=1, D=C, ldq=3 * C,
-                                     ldk=3 * C, ldv=3 * C, qOff=r * 3 * C, kOff=r * 3 * C + C, vOff=r * 3 * C + 2 * C,
-                                     oOff=r * C)
     enq = supra_attn.lib.supra_attn_enqueue_linear
     VCODES = {"fp32": supra_attn._lib.FP32, "tf32x3": supra_attn._lib.TF32X3, "tf32": supra_attn._lib.TF32}
 
@@ -428,110 +321,227 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5):
             d.variant = VCODES["fp32"]
         return res
 
-    def vae_block():
-        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(dq)), gpu.ctx)
-        gpu.enqueue_batch(da)  # reads qkv: flushes the projection first
-        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(do)), gpu.ctx)
-        gpu.flush()
+    if want("dit_self_b2"):
+        # DiT self-attention, B = 2, interleaved qkv
+        qkv = torch.randn(2 * 256 * 1728, device=dev, generator=g)
+        o1 = torch.empty(2 * 256 * 576, device=dev)
 
-    flops = nimg * (2.0 * hw * C * 3 * C + 4.0 * hw * hw * C + 2.0 * hw * C * C)
-    out["vae_block_8"] = {}
-    for vname, (ms, kernels, per) in timed_variants(vae_block, [dq, do] + list(da)).items():
-        out["vae_block_8"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
-                                     "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak, "kernels": kernels}
-    del xv, qkv_v, a_v, y_v
+        def c1(variant):
+            arr = (supra_attn.Desc * 2)()
+            for b in range(2):
+                r = b * 256 * 1728
+                arr[b] = supra_attn.make_desc(q=qkv, k=qkv, v=qkv, out=o1, Lq=256, Lk=256, H=9, D=64, ldq=1728, ldk=1728,
+                                              ldv=1728, qOff=r, kOff=r + 576, vOff=r + 1152, oOff=b * 256 * 576,
+                                              variant=variant)
+            return arr
 
-    # Cross-attention K/V preparation for configs[4]'s 2048 sequences (app/models/dit.js:137-144):
-    # ctx_proj over every sequence's T5 rows at once, then the 14 blocks' kv projections as one
-    # product with the stacked [14*1152, 576] weights (the cross attention reads its K/V in place).
-    # Two flushes (the second reads the first's output); fp32 FFMA (a TF32 request runs the same).
-    Lc = workload_lengths(1024, seed)
-    rows = sum(Lc)
-    ctx = torch.randn(rows * 768, device=dev, generator=g)
-    wp = torch.randn(576 * 768, device=dev, generator=g) * 768 ** -0.5
-    bp = torch.randn(576, device=dev, generator=g) * 0.1
-    wkv = torch.randn(14 * 1152 * 576, device=dev, generator=g) * 576 ** -0.5
-    bkv = torch.randn(14 * 1152, device=dev, generator=g) * 0.1
-    p = torch.empty(rows * 576, device=dev)
-    kv_all = torch.empty(rows * 14 * 1152, device=dev)
-    d1 = supra_attn.make_linear_desc(x=ctx, w=wp, bias=bp, y=p, M=rows, N=576, K=768)
-    d2 = supra_attn.make_linear_desc(x=p, w=wkv, bias=bkv, y=kv_all, M=rows, N=14 * 1152, K=576)
-    enq = supra_attn.lib.supra_attn_enqueue_linear
+        f1 = 2 * 4.0 * 256 * 256 * 64 * 9
+        run("dit_self_b2", 2, "seq", c1, f1, 2 * 4.0 * (2 * 256 * 576 + 2 * 256 * 576))
 
-    def prep():
-        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d1)), gpu.ctx)
-        supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d2)), gpu.ctx)  # hazard: flushes d1 first
-        gpu.flush()
+    if want("dit_cross_128"):
+        # DiT cross-attention, 64 prompts x CFG, ragged L
+        Ls = torch.randint(1, 129, (128,), generator=gc).tolist()
+        q2 = torch.randn(128 * 256 * 576, device=dev, generator=g)
+        kv2 = [torch.randn(L * 1152, device=dev, generator=g) for L in Ls]
+        o2 = torch.empty_like(q2)
 
-    flops = 2.0 * rows * (768 * 576 + 576 * 14 * 1152)
-    bytes_ = 4.0 * (rows * 768 + 576 * 768 + rows * 576 * 2 + 14 * 1152 * 576 + rows * 14 * 1152)
-    tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0
-    out["ctx_prep_2048"] = {}
-    for vname, (ms, kernels, per) in timed_variants(prep, [d1, d2]).items():
-        r = {"ms": ms, "seq_per_s": 2048 / (ms / 1e3), "rows": rows, "tflops": flops / (ms / 1e3) / 1e12,
-             "gbs": bytes_ / (ms / 1e3) / 1e9, "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm, "kernels": kernels,
-             "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
-        if vname == "fp32":
-            r["frac_fp32_peak"] = flops / (ms / 1e3) / 1e12 / fp32_peak
-        else:  # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
-            r["frac_tf32_peak"] = (3 if vname == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 / tf_peak
-        out["ctx_prep_2048"][vname] = r
-    del ctx, p, kv_all, wkv
+        def c2(variant):
+            arr = (supra_attn.Desc * 128)()
+            for b, L in enumerate(Ls):
+                arr[b] = supra_attn.make_desc(q=q2, k=kv2[b], v=kv2[b], out=o2, Lq=256, Lk=L, H=9, D=64, ldq=576,
+                                              ldk=1152, ldv=1152, qOff=b * 256 * 576, kOff=0, vOff=576,
+                                              oOff=b * 256 * 576, variant=variant)
+            return arr
 
-    # One whole DiT block (app/models/dit.js:161-194) for 32 images of 256 tokens with ragged
-    # prompts: LayerNorm (+ adaLN modulation) folded into the qkv / q / fc1 products, the residual
-    # updates in place with their gates, GELU(tanh) on fc1: 8 recorded calls, 6 products and the
-    # two attentions, plus the LayerNorm statistics. fp32 throughout.
-    nimg, N, D = 32, 256, 576
-    Lb = workload_lengths(nimg, seed + 7)
-    xb = torch.randn(nimg * N * D, device=dev, generator=g)
-    modb = 0.5 * torch.randn(6 * D, device=dev, generator=g)
-    wb = {}
-    for nm, (o, i) in [("qkv", (3 * D, D)), ("proj", (D, D)), ("q", (D, D)), ("cproj", (D, D)),
-                       ("fc1", (4 * D, D)), ("fc2", (D, 4 * D))]:
-        wb[nm] = torch.randn(o * i, device=dev, generator=g) * i ** -0.5
-        wb["b" + nm] = 0.1 * torch.randn(o, device=dev, generator=g)
-    kvb = [torch.randn(L * 2 * D, device=dev, generator=g) for L in Lb]
-    R = nimg * N
-    qkv_b, a_b, q_b, c_b, f_b = (torch.empty(R * n, device=dev) for n in (3 * D, D, D, D, 4 * D))
-    L = supra_attn.make_linear_desc
-    lin = [
-        L(x=xb, w=wb["qkv"], bias=wb["bqkv"], y=qkv_b, M=R, N=3 * D, K=D, layernorm=dict(mod=modb, shiftOff=0, scaleOff=D)),
-        L(x=a_b, w=wb["proj"], bias=wb["bproj"], y=xb, M=R, N=D, K=D, resid=True, gate=modb, gOff=2 * D),
-        L(x=xb, w=wb["q"], bias=wb["bq"], y=q_b, M=R, N=D, K=D, layernorm={}),
-        L(x=c_b, w=wb["cproj"], bias=wb["bcproj"], y=xb, M=R, N=D, K=D, resid=True),
-        L(x=xb, w=wb["fc1"], bias=wb["bfc1"], y=f_b, M=R, N=4 * D, K=D, act="gelu_tanh",
-          layernorm=dict(mod=modb, shiftOff=3 * D, scaleOff=4 * D)),
-        L(x=f_b, w=wb["fc2"], bias=wb["bfc2"], y=xb, M=R, N=D, K=4 * D, resid=True, gate=modb, gOff=5 * D),
-    ]
-    sa, ca = (supra_attn.Desc * nimg)(), (supra_attn.Desc * nimg)()
-    for b in range(nimg):
-        r = b * N * 3 * D
-        sa[b] = supra_attn.make_desc(q=qkv_b, k=qkv_b, v=qkv_b, out=a_b, Lq=N, Lk=N, H=9, D=64, ldq=3 * D, ldk=3 * D,
-                                     ldv=3 * D, qOff=r, kOff=r + D, vOff=r + 2 * D, oOff=b * N * D)
-        ca[b] = supra_attn.make_desc(q=q_b, k=kvb[b], v=kvb[b], out=c_b, Lq=N, Lk=Lb[b], H=9, D=64, ldq=D,
-                                     ldk=2 * D, ldv=2 * D, qOff=b * N * D, kOff=0, vOff=D, oOff=b * N * D)
+        run("dit_cross_128", 128, "seq", c2, sum(4.0 * 256 * L * 64 * 9 for L in Ls),
+            sum(4.0 * (2 * 256 * 576 + 2 * L * 576) for L in Ls))
 
-    def block():
-        e = lambda d: supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d)), gpu.ctx)
-        e(lin[0])
-        gpu.enqueue_batch(sa)
-        e(lin[1])
-        e(lin[2])
-        gpu.enqueue_batch(ca)
-        e(lin[3])
-        e(lin[4])
-        e(lin[5])
-        gpu.flush()
+    if want("t5_256") or want("t5_256_table"):  # (the table form reuses these inputs)
+        # T5 encoder attention, 256 prompts, ragged L, relative-position bias, scale 1
+        Lt = torch.randint(1, 129, (256,), generator=gc).tolist()
+        table = (torch.randn(32 * 12, generator=gc) * 0.1).to(dev)
+        qs = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
+        ks = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
+        vs = [torch.randn(L * 768, device=dev, generator=g) for L in Lt]
+        os_ = [torch.empty(L * 768, device=dev) for L in Lt]
+        biases = [gpu.wrap(torch.empty(12 * L * L, device=dev)) for L in Lt]
+        for L, bt in zip(Lt, biases):
+            supra_attn.position_bias(gpu, table, L, H=12, out=bt)
+        gpu.sync()
 
-    lin_flops = 2.0 * R * D * (3 * D + D + D + D + 4 * D + 4 * D)
-    att_flops = 4.0 * N * D * (nimg * N + sum(Lb))
-    flops = lin_flops + att_flops
-    out["dit_block_32"] = {}
-    for vname, (ms, kernels, per) in timed_variants(block, lin + list(sa) + list(ca)).items():
-        out["dit_block_32"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
-                                      "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
-                                      "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+        def c3(variant):
+            arr = (supra_attn.Desc * 256)()
+            for i, L in enumerate(Lt):
+                arr[i] = supra_attn.make_desc(q=qs[i], k=ks[i], v=vs[i], out=os_[i], bias=biases[i], Lq=L, Lk=L, H=12, D=64,
+                                              ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
+            return arr
+
+        if want("t5_256"):
+            run("t5_256", 256, "prompt", c3, sum(4.0 * L * L * 64 * 12 for L in Lt),
+                sum(4.0 * (4 * L * 768 + 12 * L * L) for L in Lt))
+
+    if want("t5_256_table"):
+        # the same T5 calls with the [32, 12] table in place of the expanded bias (the kernels form
+        # the bias; the host's per-prompt bias build and its 48*L^2 bytes drop out)
+        def c3t(variant):
+            arr = (supra_attn.Desc * 256)()
+            for i, L in enumerate(Lt):
+                arr[i] = supra_attn.make_desc(q=qs[i], k=ks[i], v=vs[i], out=os_[i], t5_table=table, Lq=L, Lk=L, H=12,
+                                              D=64, ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
+            return arr
+
+        run("t5_256_table", 256, "prompt", c3t, sum(4.0 * L * L * 64 * 12 for L in Lt),
+            sum(4.0 * (4 * L * 768 + 32 * 12) for L in Lt))
+
+    if want("vae"):
+        # VAE mid-block single-head attention, 1024 tokens x 512 channels
+        for nimg in (1, 8, 64):
+            qv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
+            kvv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
+            vv = torch.randn(nimg * 1024 * 512, device=dev, generator=g)
+            ov = torch.empty_like(qv)
+
+            def c4(variant, nimg=nimg, qv=qv, kvv=kvv, vv=vv, ov=ov):
+                arr = (supra_attn.Desc * nimg)()
+                for i in range(nimg):
+                    o = i * 1024 * 512
+                    arr[i] = supra_attn.make_desc(q=qv, k=kvv, v=vv, out=ov, Lq=1024, Lk=1024, H=1, D=512, ldq=512,
+                                                  ldk=512, ldv=512, qOff=o, kOff=o, vOff=o, oOff=o, variant=variant)
+                return arr
+
+            run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512)
+            del qv, kvv, vv, ov
+
+    if want("vae_block_8"):
+        # VAE mid-block attention, whole block fused (app/models/vae.js:77-94), 8 images of 32x32:
+        # GroupNorm folded into one stacked q/k/v product, attention reading q/k/v in place, residual
+        # folded into the output projection.
+        nimg, hw, C = 8, 1024, 512
+        xv = torch.randn(nimg * hw * C, device=dev, generator=g)
+        gam = 1 + 0.1 * torch.randn(C, device=dev, generator=g)
+        bet = 0.1 * torch.randn(C, device=dev, generator=g)
+        wqkv = torch.randn(3 * C * C, device=dev, generator=g) * C ** -0.5
+        bqkv = 0.1 * torch.randn(3 * C, device=dev, generator=g)
+        wo = torch.randn(C * C, device=dev, generator=g) * C ** -0.5
+        bo = 0.1 * torch.randn(C, device=dev, generator=g)
+        qkv_v = torch.empty(nimg * hw * 3 * C, device=dev)
+        a_v = torch.empty(nimg * hw * C, device=dev)
+        y_v = torch.empty(nimg * hw * C, device=dev)
+        dq = supra_attn.make_linear_desc(x=xv, w=wqkv, bias=bqkv, y=qkv_v, M=nimg * hw, N=3 * C, K=C,
+                                         groupnorm=dict(gamma=gam, beta=bet, groups=32, rows_per_image=hw))
+        do = supra_attn.make_linear_desc(x=a_v, w=wo, bias=bo, y=y_v, M=nimg * hw, N=C, K=C, resid=xv)
+        da = (supra_attn.Desc * nimg)()
+        for i in range(nimg):
+            r = i * hw
+            da[i] = supra_attn.make_desc(q=qkv_v, k=qkv_v, v=qkv_v, out=a_v, Lq=hw, Lk=hw, H=1, D=C, ldq=3 * C,
+                                         ldk=3 * C, ldv=3 * C, qOff=r * 3 * C, kOff=r * 3 * C + C, vOff=r * 3 * C + 2 * C,
+                                         oOff=r * C)
+        def vae_block():
+            supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(dq)), gpu.ctx)
+            gpu.enqueue_batch(da)  # reads qkv: flushes the projection first
+            supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(do)), gpu.ctx)
+            gpu.flush()
+
+        flops = nimg * (2.0 * hw * C * 3 * C + 4.0 * hw * hw * C + 2.0 * hw * C * C)
+        out["vae_block_8"] = {}
+        for vname, (ms, kernels, per) in timed_variants(vae_block, [dq, do] + list(da)).items():
+            out["vae_block_8"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                                         "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak, "kernels": kernels}
+        del xv, qkv_v, a_v, y_v
+
+    if want("ctx_prep_2048"):
+        # Cross-attention K/V preparation for configs[4]'s 2048 sequences (app/models/dit.js:137-144):
+        # ctx_proj over every sequence's T5 rows at once, then the 14 blocks' kv projections as one
+        # product with the stacked [14*1152, 576] weights (the cross attention reads its K/V in place).
+        # Two flushes (the second reads the first's output); fp32 FFMA (a TF32 request runs the same).
+        Lc = workload_lengths(1024, seed)
+        rows = sum(Lc)
+        ctx = torch.randn(rows * 768, device=dev, generator=g)
+        wp = torch.randn(576 * 768, device=dev, generator=g) * 768 ** -0.5
+        bp = torch.randn(576, device=dev, generator=g) * 0.1
+        wkv = torch.randn(14 * 1152 * 576, device=dev, generator=g) * 576 ** -0.5
+        bkv = torch.randn(14 * 1152, device=dev, generator=g) * 0.1
+        p = torch.empty(rows * 576, device=dev)
+        kv_all = torch.empty(rows * 14 * 1152, device=dev)
+        d1 = supra_attn.make_linear_desc(x=ctx, w=wp, bias=bp, y=p, M=rows, N=576, K=768)
+        d2 = supra_attn.make_linear_desc(x=p, w=wkv, bias=bkv, y=kv_all, M=rows, N=14 * 1152, K=576)
+        enq = supra_attn.lib.supra_attn_enqueue_linear
+
+        def prep():
+            supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d1)), gpu.ctx)
+            supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d2)), gpu.ctx)  # hazard: flushes d1 first
+            gpu.flush()
+
+        flops = 2.0 * rows * (768 * 576 + 576 * 14 * 1152)
+        bytes_ = 4.0 * (rows * 768 + 576 * 768 + rows * 576 * 2 + 14 * 1152 * 576 + rows * 14 * 1152)
+        tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0
+        out["ctx_prep_2048"] = {}
+        for vname, (ms, kernels, per) in timed_variants(prep, [d1, d2]).items():
+            r = {"ms": ms, "seq_per_s": 2048 / (ms / 1e3), "rows": rows, "tflops": flops / (ms / 1e3) / 1e12,
+                 "gbs": bytes_ / (ms / 1e3) / 1e9, "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm, "kernels": kernels,
+                 "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+            if vname == "fp32":
+                r["frac_fp32_peak"] = flops / (ms / 1e3) / 1e12 / fp32_peak
+            else:  # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
+                r["frac_tf32_peak"] = (3 if vname == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 / tf_peak
+            out["ctx_prep_2048"][vname] = r
+        del ctx, p, kv_all, wkv
+
+    if want("dit_block_32"):
+        # One whole DiT block (app/models/dit.js:161-194) for 32 images of 256 tokens with ragged
+        # prompts: LayerNorm (+ adaLN modulation) folded into the qkv / q / fc1 products, the residual
+        # updates in place with their gates, GELU(tanh) on fc1: 8 recorded calls, 6 products and the
+        # two attentions, plus the LayerNorm statistics. fp32 throughout.
+        nimg, N, D = 32, 256, 576
+        Lb = workload_lengths(nimg, seed + 7)
+        xb = torch.randn(nimg * N * D, device=dev, generator=g)
+        modb = 0.5 * torch.randn(6 * D, device=dev, generator=g)
+        wb = {}
+        for nm, (o, i) in [("qkv", (3 * D, D)), ("proj", (D, D)), ("q", (D, D)), ("cproj", (D, D)),
+                           ("fc1", (4 * D, D)), ("fc2", (D, 4 * D))]:
+            wb[nm] = torch.randn(o * i, device=dev, generator=g) * i ** -0.5
+            wb["b" + nm] = 0.1 * torch.randn(o, device=dev, generator=g)
+        kvb = [torch.randn(L * 2 * D, device=dev, generator=g) for L in Lb]
+        R = nimg * N
+        qkv_b, a_b, q_b, c_b, f_b = (torch.empty(R * n, device=dev) for n in (3 * D, D, D, D, 4 * D))
+        L = supra_attn.make_linear_desc
+        lin = [
+            L(x=xb, w=wb["qkv"], bias=wb["bqkv"], y=qkv_b, M=R, N=3 * D, K=D, layernorm=dict(mod=modb, shiftOff=0, scaleOff=D)),
+            L(x=a_b, w=wb["proj"], bias=wb["bproj"], y=xb, M=R, N=D, K=D, resid=True, gate=modb, gOff=2 * D),
+            L(x=xb, w=wb["q"], bias=wb["bq"], y=q_b, M=R, N=D, K=D, layernorm={}),
+            L(x=c_b, w=wb["cproj"], bias=wb["bcproj"], y=xb, M=R, N=D, K=D, resid=True),
+            L(x=xb, w=wb["fc1"], bias=wb["bfc1"], y=f_b, M=R, N=4 * D, K=D, act="gelu_tanh",
+              layernorm=dict(mod=modb, shiftOff=3 * D, scaleOff=4 * D)),
+            L(x=f_b, w=wb["fc2"], bias=wb["bfc2"], y=xb, M=R, N=D, K=4 * D, resid=True, gate=modb, gOff=5 * D),
+        ]
+        sa, ca = (supra_attn.Desc * nimg)(), (supra_attn.Desc * nimg)()
+        for b in range(nimg):
+            r = b * N * 3 * D
+            sa[b] = supra_attn.make_desc(q=qkv_b, k=qkv_b, v=qkv_b, out=a_b, Lq=N, Lk=N, H=9, D=64, ldq=3 * D, ldk=3 * D,
+                                         ldv=3 * D, qOff=r, kOff=r + D, vOff=r + 2 * D, oOff=b * N * D)
+            ca[b] = supra_attn.make_desc(q=q_b, k=kvb[b], v=kvb[b], out=c_b, Lq=N, Lk=Lb[b], H=9, D=64, ldq=D,
+                                         ldk=2 * D, ldv=2 * D, qOff=b * N * D, kOff=0, vOff=D, oOff=b * N * D)
+
+        def block():
+            e = lambda d: supra_attn._lib.check(enq(gpu.ctx, supra_attn._lib.C.byref(d)), gpu.ctx)
+            e(lin[0])
+            gpu.enqueue_batch(sa)
+            e(lin[1])
+            e(lin[2])
+            gpu.enqueue_batch(ca)
+            e(lin[3])
+            e(lin[4])
+            e(lin[5])
+            gpu.flush()
+
+        lin_flops = 2.0 * R * D * (3 * D + D + D + D + 4 * D + 4 * D)
+        att_flops = 4.0 * N * D * (nimg * N + sum(Lb))
+        flops = lin_flops + att_flops
+        out["dit_block_32"] = {}
+        for vname, (ms, kernels, per) in timed_variants(block, lin + list(sa) + list(ca)).items():
+            out["dit_block_32"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                                          "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                                          "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
     return out
 
 
@@ -548,6 +558,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tf32", action="store_true", help="skip the tensor-core passes (tf32, tf32x3)")
     ap.add_argument("--no-sites", action="store_true", help="skip the per-call-site figures (configs[0..3])")
+    ap.add_argument("--sites", default=None,
+                    help="comma-separated call sites to run (dit_self_b2, dit_cross_128, t5_256, t5_256_table, vae, "
+                         "vae_block_8, ctx_prep_2048, dit_block_32); default all")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -910,7 +923,8 @@ def main():
 
     sites = None
     if rank == 0 and world == 1 and not args.no_sites:
-        sites = measure_call_sites(gpu, torch, dev, args.seed)
+        sites = measure_call_sites(gpu, torch, dev, args.seed,
+                                   only=set(args.sites.split(",")) if args.sites else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
