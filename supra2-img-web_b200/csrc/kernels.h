@@ -197,9 +197,12 @@ struct LinTcLaunch {
 };
 cudaError_t launch_linear_tc(const LinTcLaunch& L, bool split, cudaStream_t s);
 // rows x K floats of src (row stride ld) -> hi (and lo when non-null), dense with row stride ldd;
-// normalised first when norm.gn_stats is set (norm's GroupNorm / LayerNorm fields, x rows).
+// normalised first when norm.gn_stats is set (norm's GroupNorm / LayerNorm fields, x rows), or
+// row r scaled by rowscale[r] when rowscale is set (w rows times a gate; then bias_out[r] =
+// bias_in[r] * rowscale[r] too when bias_out is set).
 cudaError_t launch_linear_split(const float* src, int64_t ld, int32_t rows, int32_t K, const LinProb& norm, float* hi,
-                                float* lo, int32_t ldd, cudaStream_t s);
+                                float* lo, int32_t ldd, cudaStream_t s, const float* rowscale = nullptr,
+                                const float* bias_in = nullptr, float* bias_out = nullptr);
 cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s);
 cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
                             float eps, float2* stats, cudaStream_t s);

@@ -20,6 +20,8 @@
 // list, in groups of 16 row tiles with the row tile innermost. 6 warps: TMA producer, MMA issuer, 4 epilogue warps (warp w owns
 // TMEM lanes 32*(w%4) .. +31, i.e. output rows). One CTA per SM (three 64 KB stages). Every wait
 // is bounded; on a timeout the CTA records the failure, drains its MMAs, frees TMEM and leaves.
+#include <type_traits>
+
 #include "tcgen05.cuh"
 
 namespace supra {
@@ -231,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
       float o[kBN];
 #pragma unroll
       for (int c = 0; c < kBN; ++c) o[c] = (bias && c < nc) ? __ldg(bias + c0 + c) : 0.f;
+      int flast = f;  // the partial sum whose accumulator ends up holding the finished row
       for (int kb0 = 0; kb0 < nkb; kb0 += kFlush, ++f) {
         ok = __all_sync(0xffffffffu, wait_or_abort(&B->accf[f % kAcc], (uint32_t)((f / kAcc) & 1), abort, L.status,
                                                    W_ACCF, f));
@@ -249,64 +252,133 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
             o[32 * c32 + c + 1] = x.y;
           }
         }
-        tc::fence_before_sync();
-        mbar_arrive(&B->acce[f % kAcc]);
+        if (kb0 + kFlush < nkb) {
+          tc::fence_before_sync();
+          mbar_arrive(&B->acce[f % kAcc]);
+        } else {
+          // the finished row goes back into this accumulator, which the epilogue below reads in
+          // 32-column chunks (with the row no longer held in registers) and then releases
+#pragma unroll
+          for (int c32 = 0; c32 < kBN / 32; ++c32) {
+            float t32[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) t32[c] = o[32 * c32 + c];
+            tc::tmem_st32(acc + 32 * c32, t32);
+          }
+          tc::tmem_wait_st();
+          flast = f;
+        }
       }
       if (!ok) break;
-      // y = resid + gate * act(o + bias), the reference's epilogue order, per row from registers
-      // (o holds the bias already; gate is the same column for every thread: broadcast loads).
-      // Each thread writes
-      // its own row: float4 stores when y (and the residual) have 16-byte rows. Staging through
-      // shared memory for coalesced rows was slower: shared loads wait about a thousand cycles
-      // while the tensor core streams the next tile's operands.
+      // y = resid + gate * act(o + bias), the reference's epilogue order, in 32-column chunks read
+      // back from TMEM (the row started at the bias; gate is the same column for every thread:
+      // broadcast loads). y leaves through TMA stores, or each thread stores its own row (float4
+      // when the rows are 16-byte aligned). (Staging through shared memory for coalesced rows and
+      // reading it back was slower: shared loads wait about a thousand cycles while the tensor
+      // core streams the next tile's operands.)
+      const uint32_t accl = tl + (uint32_t)(flast % kAcc) * kBN;
       const int r = T.mt * kBM + 32 * q4 + lane;
       int my = T.p->my;
       asm volatile("" : "+r"(my));
-      if (gate || act != kActNone) {
+      const CUtensorMap* ymap = L.maps + (my >= 0 ? my : 0);
+      uint8_t* slots = base + OFF_EPI + q4 * 2 * kSlot;
+      const float* rrow = (resid && r < M) ? resid + (int64_t)r * ldr + c0 : nullptr;
+      float* yrow = y + (int64_t)r * ldy + c0;
+      const bool rvec = rrow && (reinterpret_cast<uintptr_t>(rrow) & 15u) == 0 && (nc & 3) == 0;
+      const bool yvec = (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0 && (nc & 3) == 0;
+      // Without gate and activation each 32-column block is read and written whole; with either,
+      // in a loop over 4-column groups that is not unrolled (unrolled 32-wide with the three
+      // activations' code ran about three times slower than the whole product without them).
+      const bool plain = !gate && act == kActNone;
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          if (c < nc) {
-            float v = o[c];
-            if (act != kActNone) v = linear_act(act, v);
-            if (gate) v *= __ldg(gate + c0 + c);
-            o[c] = v;
-          }
-        }
-      }
-      if (my >= 0) {
-        // TMA stores: the residual first (this thread's row), then each 32 x 32 block through one
-        // of the warp's two slots (16-byte chunks swizzled by row, SWIZZLE_128B: conflict-free
-        // float4 writes); lane 0 stores the block, and the TMA clips rows past M and columns
-        // past N. A slot is rewritten once at most one store (the other slot's) is still reading.
-        if (resid && r < M) {
-          const float* rrow = resid + (int64_t)r * ldr + c0;
-          if ((reinterpret_cast<uintptr_t>(rrow) & 15u) == 0 && (nc & 3) == 0) {
-#pragma unroll
-            for (int c = 0; c < kBN; c += 4)
-              if (c < nc) {
-                const float4 rv = *reinterpret_cast<const float4*>(rrow + c);
-                o[c] += rv.x, o[c + 1] += rv.y, o[c + 2] += rv.z, o[c + 3] += rv.w;
-              }
-          } else {
-#pragma unroll
-            for (int c = 0; c < kBN; ++c)
-              if (c < nc) o[c] += rrow[c];
-          }
-        }
-        const CUtensorMap* ymap = L.maps + my;
-        uint8_t* slots = base + OFF_EPI + q4 * 2 * kSlot;
-#pragma unroll
-        for (int cb = 0; cb < kBN / 32; ++cb) {
-          // blocks wholly past N are skipped altogether (every block written to a slot is stored,
-          // which is what keeps "at most one store still reading" on the other slot)
-          if (32 * cb >= nc) break;
-          uint8_t* slot = slots + (cb & 1) * kSlot;
+      for (int cb = 0; cb < kBN / 32; ++cb) {
+        // blocks wholly past N are skipped altogether (every block written to a slot is stored,
+        // which is what keeps "at most one store still reading" on the other slot)
+        if (32 * cb >= nc) break;
+        uint8_t* slot = slots + (cb & 1) * kSlot;
+        if (my >= 0) {
           if (lane == 0) tc::bulk_wait_group_read<1>();
           __syncwarp();
+        }
+        if (plain) {
+          float v[32];
+          tc::tmem_ld32(accl + 32 * cb, v);
+          tc::tmem_wait_ld();
+          if (rrow) {
+            if (rvec) {
 #pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4)
-            *reinterpret_cast<float4*>(slot + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
-                make_float4(o[32 * cb + 4 * c4], o[32 * cb + 4 * c4 + 1], o[32 * cb + 4 * c4 + 2], o[32 * cb + 4 * c4 + 3]);
+              for (int c = 0; c < 32; c += 4)
+                if (32 * cb + c < nc) {
+                  const float4 rv = *reinterpret_cast<const float4*>(rrow + 32 * cb + c);
+                  v[c] += rv.x, v[c + 1] += rv.y, v[c + 2] += rv.z, v[c + 3] += rv.w;
+                }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (32 * cb + c < nc) v[c] += rrow[32 * cb + c];
+            }
+          }
+          if (my >= 0) {
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4)
+              *reinterpret_cast<float4*>(slot + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+          } else if (r < M) {
+            if (yvec) {
+#pragma unroll
+              for (int c = 0; c < 32; c += 4)
+                if (32 * cb + c < nc)
+                  *reinterpret_cast<float4*>(yrow + 32 * cb + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (32 * cb + c < nc) yrow[32 * cb + c] = v[c];
+            }
+          }
+        } else {
+          // one loop per activation, chosen outside it (the activation known at compile time
+          // keeps each loop's code small)
+          auto groups = [&](auto actc) {
+            constexpr int A = decltype(actc)::value;
+#pragma unroll 2
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const int cc = 32 * cb + 4 * c4;  // first of the group's 4 columns in the tile
+              const float4 q = tc::tmem_ld4(accl + cc);
+              tc::tmem_wait_ld();
+              float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                if (cc + u < nc) {
+                  if constexpr (A != kActNone) e[u] = linear_act(A, e[u]);
+                  if (gate) e[u] *= __ldg(gate + c0 + cc + u);
+                  if (rrow) e[u] += rrow[cc + u];
+                }
+              }
+              if (my >= 0) {
+                *reinterpret_cast<float4*>(slot + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
+                    make_float4(e[0], e[1], e[2], e[3]);
+              } else if (r < M) {
+                if (yvec && cc < nc) {
+                  *reinterpret_cast<float4*>(yrow + cc) = make_float4(e[0], e[1], e[2], e[3]);
+                } else {
+#pragma unroll
+                  for (int u = 0; u < 4; ++u)
+                    if (cc + u < nc) yrow[cc + u] = e[u];
+                }
+              }
+            }
+          };
+          switch (act) {
+            case kActGelu: groups(std::integral_constant<int, kActGelu>{}); break;
+            case kActGeluTanh: groups(std::integral_constant<int, kActGeluTanh>{}); break;
+            case kActSilu: groups(std::integral_constant<int, kActSilu>{}); break;
+            default: groups(std::integral_constant<int, kActNone>{}); break;
+          }
+        }
+        if (my >= 0) {
+          // TMA store of the 32 x 32 block (16-byte chunks swizzled by row, SWIZZLE_128B); the TMA
+          // clips rows past M and columns past N. A slot is rewritten once at most one store (the
+          // other slot's) is still reading.
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -314,29 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
             tc::bulk_commit_group();
           }
         }
-      } else if (r < M) {
-        float* yrow = y + (int64_t)r * ldy + c0;
-        const float* rrow = resid ? resid + (int64_t)r * ldr + c0 : nullptr;
-        const bool vec = ((reinterpret_cast<uintptr_t>(yrow) & 15u) == 0) && (nc & 3) == 0 &&
-                         (!rrow || (reinterpret_cast<uintptr_t>(rrow) & 15u) == 0);
-        if (vec) {
-#pragma unroll
-          for (int c = 0; c < kBN; c += 4) {
-            if (c < nc) {
-              float4 val = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
-              if (rrow) {
-                const float4 rv = *reinterpret_cast<const float4*>(rrow + c);
-                val = make_float4(rv.x + val.x, rv.y + val.y, rv.z + val.z, rv.w + val.w);
-              }
-              *reinterpret_cast<float4*>(yrow + c) = val;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBN; ++c)
-            if (c < nc) yrow[c] = rrow ? rrow[c] + o[c] : o[c];
-        }
       }
+      tc::fence_before_sync();
+      mbar_arrive(&B->acce[flast % kAcc]);  // the finished row's accumulator is free again
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 56, f);
     if (lane == 0) tc::bulk_wait_group_all();  // this warp's TMA stores are complete
@@ -358,17 +410,26 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------------------------------------
-// hi / lo split of rows x K (row stride ld) into dense [rows, ldd], normalised first when
+// hi / lo split of rows x K (row stride ld) into dense [rows, ldd] (row r scaled by rowscale[r]
+// first when set: a gate folded into w, with the bias scaled alongside), normalised first when
 // N.gn_stats is set: (x - mean) * rstd * g + b (then SiLU if asked) with g, b = gamma, beta
 // (GroupNorm), 1 + scale, shift (modulated LayerNorm) or 1, 0 (plain LayerNorm), as the
 // linear_fp32 prologue applies them.
 __global__ void __launch_bounds__(256) linear_split_kernel(const float* __restrict__ src, int64_t ld, int32_t rows,
                                                            int32_t K, const LinProb N, float* __restrict__ hi,
-                                                           float* __restrict__ lo, int32_t ldd) {
+                                                           float* __restrict__ lo, int32_t ldd,
+                                                           const float* __restrict__ rowscale,
+                                                           const float* __restrict__ bias_in,
+                                                           float* __restrict__ bias_out) {
   const int64_t total = (int64_t)rows * K;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int32_t r = (int32_t)(i / K), k = (int32_t)(i - (int64_t)r * K);
     float x = __ldg(src + (int64_t)r * ld + k);
+    if (rowscale) {
+      const float g = __ldg(rowscale + r);
+      x *= g;
+      if (bias_out && k == 0) bias_out[r] = bias_in ? __ldg(bias_in + r) * g : 0.f;
+    }
     if (N.gn_stats) {
       const float2 ms = __ldg(N.gn_stats + (int64_t)(r / N.gn_rows) * N.gn_groups + k / N.gn_cg);
       float g = 1.f, b = 0.f;
@@ -389,14 +450,15 @@ __global__ void __launch_bounds__(256) linear_split_kernel(const float* __restri
 }  // namespace
 
 cudaError_t launch_linear_split(const float* src, int64_t ld, int32_t rows, int32_t K, const LinProb& norm, float* hi,
-                                float* lo, int32_t ldd, cudaStream_t s) {
+                                float* lo, int32_t ldd, cudaStream_t s, const float* rowscale, const float* bias_in,
+                                float* bias_out) {
   const int64_t total = (int64_t)rows * K;
   if (total <= 0) return cudaSuccess;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (total + 255) / 256;
   const int grid = (int)(want < 8 * sms ? want : 8 * sms);
-  linear_split_kernel<<<grid, 256, 0, s>>>(src, ld, rows, K, norm, hi, lo, ldd);
+  linear_split_kernel<<<grid, 256, 0, s>>>(src, ld, rows, K, norm, hi, lo, ldd, rowscale, bias_in, bias_out);
   return cudaGetLastError();
 }
 

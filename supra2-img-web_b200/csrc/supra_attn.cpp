@@ -1174,22 +1174,35 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   for (int i = 0; i < n; ++i) lp[i] = g[i]->lin;
   int rc = norm_stats(c, g, lp.data());
   if (rc) return rc;
-  std::vector<size_t> xoff((size_t)n), woff((size_t)n);
+  // A gate without an activation folds into the split of w: gate[n] * (x w[n] + b[n]) =
+  // x (gate[n] w[n]) + gate[n] b[n], so the product runs the plain epilogue (one extra rounding
+  // of gate * w, far inside the FP32 bar). Such a w is split per gate, with a gated bias copy.
+  std::vector<char> fold((size_t)n, 0);
+  for (int i = 0; i < n; ++i) fold[i] = lp[i].gate != nullptr && lp[i].act == supra::kActNone;
+  std::vector<size_t> xoff((size_t)n), woff((size_t)n), boff((size_t)n, 0);
   std::vector<char> wfirst((size_t)n, 0);
   size_t need = 0;
   for (int i = 0; i < n; ++i) {
     const size_t kp = (size_t)((lp[i].K + 3) & ~3);
     xoff[i] = need;
     need += parts * (size_t)lp[i].M * kp;
+    const float* gi = fold[i] ? lp[i].gate : nullptr;
     int j = 0;
     for (; j < i; ++j)
-      if (lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N && lp[j].K == lp[i].K) break;
+      if (lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N && lp[j].K == lp[i].K &&
+          (fold[j] ? lp[j].gate : nullptr) == gi && (!gi || lp[j].bias == lp[i].bias))
+        break;
     if (j < i) {
       woff[i] = woff[j];
+      boff[i] = boff[j];
     } else {
       woff[i] = need;
       wfirst[i] = 1;
       need += parts * (size_t)lp[i].N * kp;
+      if (gi) {  // the gated bias, 16-byte aligned
+        boff[i] = need;
+        need += ((size_t)lp[i].N + 3) & ~(size_t)3;
+      }
     }
   }
   rc = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, need, sizeof(float), "linear split");
@@ -1208,7 +1221,9 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
       c->launches += 1;
       if (e == cudaSuccess && wfirst[i]) {
         e = supra::launch_linear_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, plain, wh,
-                                       split ? wh + (size_t)lp[i].N * kp : nullptr, kp, c->stream);
+                                       split ? wh + (size_t)lp[i].N * kp : nullptr, kp, c->stream,
+                                       fold[i] ? lp[i].gate : nullptr, lp[i].bias,
+                                       fold[i] ? c->lin_split + boff[i] : nullptr);
         c->launches += 1;
       }
     }
@@ -1243,6 +1258,10 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     supra::LinTcProb& t = probs[i];
     std::memset(&t, 0, sizeof t);
     t.p = lp[i];
+    if (fold[i]) {  // the gate lives in the split w and the gated bias
+      t.p.gate = nullptr;
+      t.p.bias = c->lin_split + boff[i];
+    }
     const int64_t kp = (lp[i].K + 3) & ~3;
     const float* xh = c->lin_split + xoff[i];
     const float* wh = c->lin_split + woff[i];
