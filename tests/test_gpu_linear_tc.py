@@ -196,3 +196,33 @@ def test_dit_block_golden_tf32x3(gpu, golden):
     check(host(xs), golden("dit_block_x3"), "tf32x3")
     for t in (qkv, a, q, c, f):
         t.release()
+
+
+def test_gates_folded_into_weights(gpu):
+    """Gated residuals without an activation (the DiT block's proj / fc2): two problems on the same
+    weights with different gates, in place on strided outputs with offsets, one flush (tf32x3)."""
+    import supra_attn
+
+    rng = np.random.default_rng(29)
+    M, N, K = 300, 576, 576
+    ldy, yo = 580, 8
+    wa = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    ba = rng.standard_normal(N).astype(np.float32)
+    mod = rng.standard_normal(6 * N).astype(np.float32)
+    xs = [rng.standard_normal((M, K)).astype(np.float32) for _ in range(2)]
+    y0s = [rng.standard_normal(yo + M * ldy).astype(np.float32) for _ in range(2)]
+    wd, bd, md = dev(wa), dev(ba), dev(mod)
+    xds, yds = [dev(x) for x in xs], [dev(y) for y in y0s]
+    goffs = [2 * N, 5 * N]
+    for i in range(2):
+        supra_attn.linear(gpu, xds[i], wd, M=M, N=N, K=K, bias=bd, out=yds[i], ldy=ldy, yOff=yo, resid=True, gate=md,
+                          gOff=goffs[i], variant="tf32x3")
+    gpu.sync()
+    idx = yo + np.arange(M)[:, None] * ldy + np.arange(N)[None, :]
+    for i in range(2):
+        got = host(yds[i])
+        keep = np.ones(got.size, bool)
+        keep[idx.reshape(-1)] = False
+        np.testing.assert_array_equal(got[keep], y0s[i][keep])
+        ref = oracle.gated_residual(y0s[i][idx], xs[i], wa, M, N, K, bias=ba, gate=mod, g_off=goffs[i])
+        check(got[idx], ref, "tf32x3")
