@@ -446,7 +446,9 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
         out["vae_block_8"] = {}
         for vname, (ms, kernels, per) in timed_variants(vae_block, [dq, do] + list(da)).items():
             out["vae_block_8"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
-                                         "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak, "kernels": kernels}
+                                         "kernels": kernels}
+            if vname == "fp32":  # (mixed kernels in the other variants: no single peak applies)
+                out["vae_block_8"][vname]["frac_fp32_peak"] = flops / (ms / 1e3) / 1e12 / fp32_peak
         del xv, qkv_v, a_v, y_v
 
     if want("ctx_prep_2048"):
@@ -538,10 +540,15 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
         att_flops = 4.0 * N * D * (nimg * N + sum(Lb))
         flops = lin_flops + att_flops
         out["dit_block_32"] = {}
+        tfp = float(peaks.get("bf16_tflops", 1590.0)) / 2.0  # TF32 dense peak: half of measured bf16
         for vname, (ms, kernels, per) in timed_variants(block, lin + list(sa) + list(ca)).items():
-            out["dit_block_32"][vname] = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
-                                          "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
-                                          "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+            r = {"ms": ms, "image_per_s": nimg / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                 "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+            if vname == "fp32":
+                r["frac_fp32_peak"] = flops / (ms / 1e3) / 1e12 / fp32_peak
+            else:  # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
+                r["frac_tf32_peak"] = (3 if vname == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 / tfp
+            out["dit_block_32"][vname] = r
     return out
 
 
