@@ -281,11 +281,19 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
             prof = gpu.profile_report()
             gpu.profile(False)
             ms = statistics.median(times)
+            per = {}
+            for r in prof:
+                per[r["name"]] = per.get(r["name"], 0.0) + r["ms"] / reps
             res[variant] = {"ms": ms, f"{unit_name}_per_s": units / (ms / 1e3),
                             "tflops": flops / (ms / 1e3) / 1e12, "gbs": bytes_ / (ms / 1e3) / 1e9,
                             "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
                             "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
-                            "kernels": sorted({p["name"] for p in prof})}
+                            "kernels": sorted(per),
+                            "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+            if variant != "fp32" and any(k.startswith(("linear_tc", "attn_tf32")) for k in per):
+                # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
+                res[variant]["frac_tf32_peak"] = ((3 if variant == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 /
+                                                  (float(peaks.get("bf16_tflops", 1590.0)) / 2.0))
         out[name] = res
 
     enq = supra_attn.lib.supra_attn_enqueue_linear

@@ -141,7 +141,10 @@ __global__ void __launch_bounds__(kGT) gemm_qk_kernel(const GemmLaunch L) {
 
 // ------------------------------------------------------------------------------------------------
 // In-place row softmax of the unit's scores, one warp per row: max, exp and sum, normalise
-// (app/gpu/kernels.js:53-62).
+// (app/gpu/kernels.js:53-62). For the tensor-core products (L.sm_scale) the scores come unscaled
+// and the problem's scale is applied here, exp(scale s - max(scale s)); with L.lo set each
+// probability p leaves split, hi (p with its 13 low mantissa bits cleared) in place and p - hi at
+// the same offset from L.lo. Columns Lk .. ldS - 1 are zeroed.
 __global__ void __launch_bounds__(256) softmax_rows_kernel(const GemmLaunch L) {
   const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -149,21 +152,33 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const GemmLaunch L) {
   const int ui = find_unit(L.row_begin, L.n_units, wid);
   const GemmUnit u = L.units[ui];
   const int Lk = L.probs[u.prob].Lk;
-  float* row = L.scratch + u.s_off + (int64_t)(wid - u.row_begin) * u.ldS;
+  const float sc = L.sm_scale ? L.probs[u.prob].scale : 1.f;
+  const int64_t off = u.s_off + (int64_t)(wid - u.row_begin) * u.ldS;
+  float* row = L.scratch + off;
   float mx = -INFINITY;
-  for (int c = lane; c < Lk; c += 32) mx = fmaxf(mx, row[c]);
+  for (int c = lane; c < Lk; c += 32) mx = fmaxf(mx, row[c] * sc);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sm = 0.f;
   for (int c = lane; c < Lk; c += 32) {
-    const float e = expf(row[c] - mx);
+    const float e = expf(row[c] * sc - mx);
     row[c] = e;
     sm += e;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
   const float inv = 1.0f / sm;
-  for (int c = lane; c < u.ldS; c += 32) row[c] = c < Lk ? row[c] * inv : 0.f;
+  if (L.lo) {
+    float* lrow = L.lo + off;
+    for (int c = lane; c < u.ldS; c += 32) {
+      const float p = c < Lk ? row[c] * inv : 0.f;
+      const float h = __uint_as_float(__float_as_uint(p) & 0xffffe000u);
+      row[c] = h;
+      lrow[c] = p - h;
+    }
+  } else {
+    for (int c = lane; c < u.ldS; c += 32) row[c] = c < Lk ? row[c] * inv : 0.f;
+  }
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -65,6 +65,11 @@ struct GemmLaunch {
   const int32_t* pv_begin;  // n_units + 1
   const int32_t* row_begin; // n_units + 1
   float* scratch;
+  // The row softmax for the tensor-core products: with sm_scale it applies each problem's scale
+  // (the scores come unscaled); with lo set it writes the probabilities split, hi in place and
+  // lo at the same offset from lo (the operand of the split-precision P V).
+  float* lo = nullptr;
+  int32_t sm_scale = 0;
   int32_t n_units;
   int32_t qk_total, pv_total, row_total;
   int32_t* status;
@@ -175,11 +180,13 @@ cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cuda
 // GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
 // group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
 // mean in a second pass (app/gpu/kernels.js:117-139).
-// Linear on the tensor cores (linear_tc.cu) for the TF32 / TF32X3 variants: x and w are first
-// written as dense [rows, ldk] arrays (ldk = K rounded up to 4) by launch_linear_split, hi = the
-// value with its 13 low mantissa bits cleared and lo = value - hi; the product is then
-// hi(x) hi(w) (TF32) or lo(x) hi(w) + hi(x) lo(w) + hi(x) hi(w) (TF32X3) on tcgen05, with p's
-// epilogue (bias, activation, gate, residual). x and w in p are unused.
+// Linear on the tensor cores (linear_tc.cu) for the TF32 / TF32X3 variants: x and w are read
+// through tensor maps, either in place (TF32: the tensor core ignores the 13 low mantissa bits, so
+// a 16-byte aligned fp32 operand is its own TF32 part) or from dense [rows, ldk] arrays (ldk = K
+// rounded up to 4) written by launch_split, hi = the value with its 13 low mantissa bits cleared
+// and lo = value - hi; the product is then hi(x) hi(w) (TF32) or lo(x) hi(w) + hi(x) lo(w) +
+// hi(x) hi(w) (TF32X3) on tcgen05, with p's epilogue (bias, activation, gate, residual). x and w
+// in p are unused.
 struct alignas(16) LinTcProb {
   LinProb p;
   int32_t mxh, mxl, mwh, mwl;  // tensor maps of hi(x), lo(x), hi(w), lo(w) (lo: split form only)
@@ -196,13 +203,38 @@ struct LinTcLaunch {
   int32_t* status;
 };
 cudaError_t launch_linear_tc(const LinTcLaunch& L, bool split, cudaStream_t s);
-// rows x K floats of src (row stride ld) -> hi (and lo when non-null), dense with row stride ldd;
-// normalised first when norm.gn_stats is set (norm's GroupNorm / LayerNorm fields, x rows), or
-// row r scaled by rowscale[r] when rowscale is set (w rows times a gate; then bias_out[r] =
-// bias_in[r] * rowscale[r] too when bias_out is set).
-cudaError_t launch_linear_split(const float* src, int64_t ld, int32_t rows, int32_t K, const LinProb& norm, float* hi,
-                                float* lo, int32_t ldd, cudaStream_t s, const float* rowscale = nullptr,
-                                const float* bias_in = nullptr, float* bias_out = nullptr);
+constexpr int kSplitTileRows = 32, kSplitTileCols = 128;  // launch_split's tile
+// One split job: rows x K floats of src (row stride ld; with trans read as [K, rows], element
+// (r, k) at src[k * ld + r]) -> hi (and lo when non-null), dense with row stride ldd. Every value
+// is multiplied by xscale, then by rowscale[r] when rowscale is set (w rows times a gate; then
+// bias_out[r] = bias_in[r] * rowscale[r] too when bias_out is set), then normalised when gn_stats
+// is set (LinProb's GroupNorm / LayerNorm fields of x rows). trans excludes rowscale and gn_stats.
+struct alignas(16) SplitJob {
+  const float* src;
+  float* hi;
+  float* lo;
+  const float* rowscale;
+  const float* bias_in;
+  float* bias_out;
+  const float2* gn_stats;
+  const float* gamma;
+  const float* beta;
+  int64_t ld;
+  int32_t rows, K, ldd, trans;
+  int32_t gn_mode, gn_cg, gn_rows, gn_groups;
+  int32_t gn_silu;
+  float xscale;
+  int32_t ktiles;  // k tiles: ceil(K / kSplitTileCols); the job has ceil(rows / kSplitTileRows) * ktiles
+  int32_t pad_;
+};
+static_assert(sizeof(SplitJob) % 16 == 0, "SplitJob is packed into the descriptor ring");
+struct SplitLaunch {
+  const SplitJob* jobs;
+  const int32_t* begin;  // first tile of each job
+  int32_t n, total;
+};
+// All jobs of one flush in one launch (32 x 128 tiles, HBM-bound).
+cudaError_t launch_split(const SplitLaunch& L, cudaStream_t s);
 cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s);
 cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
                             float eps, float2* stats, cudaStream_t s);

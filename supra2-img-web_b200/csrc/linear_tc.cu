@@ -1,10 +1,12 @@
 // ops.linear (app/gpu/ops.js:35-43, app/gpu/gemm.js:116-223) on the tensor cores, sm_100a: the
 // TF32 and split-precision (TF32X3) variants of supra_attn_enqueue_linear.
 //
-//   linear_split_kernel  x (normalised first when asked: GroupNorm / LayerNorm with the
-//                        statistics of the stats kernels, app/gpu/kernels.js:87-162) and w into
-//                        dense hi / lo arrays: hi = value with its 13 low mantissa bits cleared
-//                        (a TF32 value), lo = value - hi (exact). Elementwise, HBM-bound.
+//   split_kernel         every operand of a flush that is not read in place (x normalised
+//                        first when asked: GroupNorm / LayerNorm with the statistics of the
+//                        stats kernels, app/gpu/kernels.js:87-162; w times a folded gate; a w
+//                        stored [K, N] transposed) into dense hi / lo arrays: hi = value with
+//                        its 13 low mantissa bits cleared (a TF32 value), lo = value - hi
+//                        (exact). One launch, HBM-bound.
 //   linear_tc_kernel     C[128 x 128 tile] = X W^T with tcgen05.mma kind::tf32: per 32-deep
 //                        k-block the TMA brings hi(X), hi(W) (and lo(X), lo(W)) tiles
 //                        (SWIZZLE_128B, K-major), the MMA warp issues per 8-deep step one
@@ -410,55 +412,95 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------------------------------------
-// hi / lo split of rows x K (row stride ld) into dense [rows, ldd] (row r scaled by rowscale[r]
-// first when set: a gate folded into w, with the bias scaled alongside), normalised first when
-// N.gn_stats is set: (x - mean) * rstd * g + b (then SiLU if asked) with g, b = gamma, beta
-// (GroupNorm), 1 + scale, shift (modulated LayerNorm) or 1, 0 (plain LayerNorm), as the
-// linear_fp32 prologue applies them.
-__global__ void __launch_bounds__(256) linear_split_kernel(const float* __restrict__ src, int64_t ld, int32_t rows,
-                                                           int32_t K, const LinProb N, float* __restrict__ hi,
-                                                           float* __restrict__ lo, int32_t ldd,
-                                                           const float* __restrict__ rowscale,
-                                                           const float* __restrict__ bias_in,
-                                                           float* __restrict__ bias_out) {
-  const int64_t total = (int64_t)rows * K;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t r = (int32_t)(i / K), k = (int32_t)(i - (int64_t)r * K);
-    float x = __ldg(src + (int64_t)r * ld + k);
-    if (rowscale) {
-      const float g = __ldg(rowscale + r);
-      x *= g;
-      if (bias_out && k == 0) bias_out[r] = bias_in ? __ldg(bias_in + r) * g : 0.f;
-    }
-    if (N.gn_stats) {
-      const float2 ms = __ldg(N.gn_stats + (int64_t)(r / N.gn_rows) * N.gn_groups + k / N.gn_cg);
-      float g = 1.f, b = 0.f;
-      if (N.gn_mode != kNormPlain) {
-        g = __ldg(N.gamma + k);
-        b = __ldg(N.beta + k);
-        if (N.gn_mode == kNormModulated) g = 1.f + g;
+// hi / lo split of every job of a flush, one 32-row x 128-column tile per block iteration. Value
+// order: x * xscale, times rowscale[r] when set (a gate folded into w, with the bias scaled
+// alongside), normalised when gn_stats is set: (x - mean) * rstd * g + b (then SiLU if asked) with
+// g, b = gamma, beta (GroupNorm), 1 + scale, shift (modulated LayerNorm) or 1, 0 (plain
+// LayerNorm), as the linear_fp32 prologue applies them. Lanes run along k, so loads and stores
+// are 128-byte rows per warp; a transposed job ([K, rows] source) goes through a shared-memory
+// tile so that its loads run along r.
+constexpr int kSplitRows = kSplitTileRows, kSplitCols = kSplitTileCols;
+
+__device__ __forceinline__ void split_store(const SplitJob& J, int32_t r, int32_t k, float x) {
+  const float h = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  J.hi[(int64_t)r * J.ldd + k] = h;
+  if (J.lo) J.lo[(int64_t)r * J.ldd + k] = x - h;
+}
+
+__global__ void __launch_bounds__(256) split_kernel(const SplitLaunch L) {
+  __shared__ float t[kSplitCols][kSplitRows + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int tile = blockIdx.x; tile < L.total; tile += gridDim.x) {
+    const int ji = find_problem(L.begin, L.n, tile);
+    const SplitJob J = L.jobs[ji];
+    const int local = tile - __ldg(L.begin + ji);
+    const int rt = local / J.ktiles, kt = local - rt * J.ktiles;
+    const int32_t r0 = rt * kSplitRows, k0 = kt * kSplitCols;
+    if (J.trans) {  // (uniform over the block: one job per tile)
+#pragma unroll 4
+      for (int kk = ty; kk < kSplitCols; kk += 8) {
+        const int32_t k = k0 + kk, r = r0 + tx;
+        t[kk][tx] = (k < J.K && r < J.rows) ? __ldg(J.src + (int64_t)k * J.ld + r) * J.xscale : 0.f;
       }
-      x = (x - ms.x) * ms.y * g + b;
-      if (N.gn_silu) x = x / (1.f + __expf(-x));
+      __syncthreads();
+      for (int rr = ty; rr < kSplitRows; rr += 8) {
+        const int32_t r = r0 + rr;
+        if (r >= J.rows) break;
+#pragma unroll
+        for (int c = 0; c < kSplitCols / 32; ++c) {
+          const int kl = 32 * c + tx;
+          if (k0 + kl < J.K) split_store(J, r, k0 + kl, t[kl][rr]);
+        }
+      }
+      __syncthreads();  // the tile buffer is rewritten by the next iteration
+      continue;
     }
-    const float h = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
-    hi[(int64_t)r * ldd + k] = h;
-    if (lo) lo[(int64_t)r * ldd + k] = x - h;
+    for (int rr = ty; rr < kSplitRows; rr += 8) {
+      const int32_t r = r0 + rr;
+      if (r >= J.rows) break;
+      const float* src = J.src + (int64_t)r * J.ld;
+      float g = J.xscale;
+      if (J.rowscale) {
+        const float rs = __ldg(J.rowscale + r);
+        g *= rs;
+        if (J.bias_out && kt == 0 && tx == 0) J.bias_out[r] = J.bias_in ? __ldg(J.bias_in + r) * rs : 0.f;
+      }
+      float x[kSplitCols / 32];
+#pragma unroll
+      for (int c = 0; c < kSplitCols / 32; ++c) {
+        const int32_t k = k0 + 32 * c + tx;
+        x[c] = k < J.K ? __ldg(src + k) : 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < kSplitCols / 32; ++c) {
+        const int32_t k = k0 + 32 * c + tx;
+        if (k >= J.K) continue;
+        float v = x[c] * g;
+        if (J.gn_stats) {
+          const float2 ms = __ldg(J.gn_stats + (int64_t)(r / J.gn_rows) * J.gn_groups + k / J.gn_cg);
+          float ga = 1.f, b = 0.f;
+          if (J.gn_mode != kNormPlain) {
+            ga = __ldg(J.gamma + k);
+            b = __ldg(J.beta + k);
+            if (J.gn_mode == kNormModulated) ga = 1.f + ga;
+          }
+          v = (v - ms.x) * ms.y * ga + b;
+          if (J.gn_silu) v = v / (1.f + __expf(-v));
+        }
+        split_store(J, r, k, v);
+      }
+    }
   }
 }
 
 }  // namespace
 
-cudaError_t launch_linear_split(const float* src, int64_t ld, int32_t rows, int32_t K, const LinProb& norm, float* hi,
-                                float* lo, int32_t ldd, cudaStream_t s, const float* rowscale, const float* bias_in,
-                                float* bias_out) {
-  const int64_t total = (int64_t)rows * K;
-  if (total <= 0) return cudaSuccess;
+cudaError_t launch_split(const SplitLaunch& L, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (total + 255) / 256;
-  const int grid = (int)(want < 8 * sms ? want : 8 * sms);
-  linear_split_kernel<<<grid, 256, 0, s>>>(src, ld, rows, K, norm, hi, lo, ldd, rowscale, bias_in, bias_out);
+  const int grid = L.total < 8 * sms ? L.total : 8 * sms;
+  split_kernel<<<grid, 256, 0, s>>>(L);
   return cudaGetLastError();
 }
 

@@ -507,7 +507,11 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
     q.cfg = supra::CFG_D128_Q64;
   } else {
     q.path = PATH_GEMM;
-    q.cfg = 0;
+    // TF32 / TF32X3 requests without a bias and with at least 32 keys run the score path's two
+    // products (Q K^T and P V) on the tensor-core linear (cfg 1 / 2); the row softmax between them
+    // stays as it is
+    const bool tc = d->variant != SUPRA_ATTN_FP32 && !q.bias && d->Lk >= 32;
+    q.cfg = tc ? (d->variant == SUPRA_ATTN_TF32X3 ? 2 : 1) : 0;
   }
   q.rows_q = d->ldq > 0 ? d->q_size / d->ldq : 0;
   q.rows_k = d->ldk > 0 ? d->k_size / d->ldk : 0;
@@ -813,10 +817,29 @@ int ensure_scratch(supra_attn_ctx* c, size_t bytes) {
   return SUPRA_ATTN_OK;
 }
 
+// A tensor-core linear job: the problem, a factor applied to x before its split (with the gate
+// folding, the only prologue the split applies to the attention operands), whether w is read as
+// [K, N] (w[k * ldw + n]: V of an attention as the weights of P V) instead of [N, K], and x given
+// ready (xh non-null: the TF32 part at xh, the remainder at xl in the split form, row stride
+// ldxs, both 16-byte aligned) instead of from p.x.
+struct TcJob {
+  supra::LinProb p;
+  float xscale;
+  bool wtrans;
+  const float* xh;
+  const float* xl;
+  int64_t ldxs;
+};
+
+int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, double flops, double bytes);
+
 int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::vector<GemmUnit>& units,
                    size_t scratch_bytes, bool bias, bool aligned) {
   if (units.empty()) return SUPRA_ATTN_OK;
-  int rc = ensure_scratch(c, scratch_bytes);
+  // cfg 1 / 2: both products on the tensor-core linear, TF32 / split form; the split form keeps
+  // the probabilities' remainders in a second region of the scratch of the same layout
+  const int tc = g[0]->cfg;
+  int rc = ensure_scratch(c, tc == 2 ? 2 * scratch_bytes : scratch_bytes);
   if (rc) return rc;
   const int np = (int)g.size();
   const int nu = (int)units.size();
@@ -880,23 +903,77 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
   L.pv_total = (int32_t)tp;
   L.row_total = (int32_t)tr;
   L.status = c->d_status;
+  L.lo = tc == 2 ? c->scratch + scratch_bytes / 4 : nullptr;
+  L.sm_scale = tc ? 1 : 0;
   cudaError_t e;
-  {
-    ProfScope ps(c, bias ? "attn_gemm_qk_bias" : "attn_gemm_qk", fl, by_qk);
-    e = supra::launch_gemm_qk(bias, aligned, L, c->stream);
+  if (tc) {
+    // S = Q_h K_h^T (unscaled: the softmax applies the scale) for each unit's rows into its
+    // scores: a linear with x = the unit's Q rows and w = K_h, both [rows, D]
+    std::vector<TcJob> jobs((size_t)nu);
+    for (int i = 0; i < nu; ++i) {
+      const GemmUnit& u = units[i];
+      const AttnProb& P = g[u.prob]->p;
+      supra::LinProb lp;
+      std::memset(&lp, 0, sizeof lp);
+      lp.x = P.q + P.q_off + (int64_t)u.row0 * P.ldq + (int64_t)u.h * P.D;
+      lp.ldx = P.ldq;
+      lp.w = P.k + P.k_off + (int64_t)u.h * P.D;
+      lp.ldw = P.ldk;
+      lp.y = c->scratch + u.s_off;
+      lp.ldy = u.ldS;
+      lp.M = u.rows;
+      lp.N = P.Lk;
+      lp.K = P.D;
+      lp.n_tiles = (P.Lk + 127) / 128;
+      jobs[i] = TcJob{lp, 1.f, false, nullptr, nullptr, 0};
+    }
+    rc = run_linear_tc(c, jobs, tc == 2, fl, by_qk);
+    if (rc) return rc;
+  } else {
+    {
+      ProfScope ps(c, bias ? "attn_gemm_qk_bias" : "attn_gemm_qk", fl, by_qk);
+      e = supra::launch_gemm_qk(bias, aligned, L, c->stream);
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, "attn_gemm_qk");
+    c->launches += 1;
   }
-  if (e != cudaSuccess) return cuda_err(c, e, "attn_gemm_qk");
   {
     ProfScope ps(c, "attn_softmax_rows", 0.0, by_sm);
     e = supra::launch_softmax_rows(L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, "attn_softmax_rows");
-  {
-    ProfScope ps(c, "attn_gemm_pv", fl, by_pv);
-    e = supra::launch_gemm_pv(aligned, L, c->stream);
+  c->launches += 1;
+  if (tc) {
+    // O_h rows = P V_h: a linear with x = the unit's probabilities, as the softmax left them (in
+    // place, or split into the scratch's two regions), and w = V_h read as [Lk, D]
+    std::vector<TcJob> jobs((size_t)nu);
+    for (int i = 0; i < nu; ++i) {
+      const GemmUnit& u = units[i];
+      const AttnProb& P = g[u.prob]->p;
+      supra::LinProb lp;
+      std::memset(&lp, 0, sizeof lp);
+      lp.x = c->scratch + u.s_off;
+      lp.ldx = u.ldS;
+      lp.w = P.v + P.v_off + (int64_t)u.h * P.D;
+      lp.ldw = P.ldv;
+      lp.y = P.o + P.o_off + (int64_t)u.row0 * P.ldo + (int64_t)u.h * P.D;
+      lp.ldy = P.ldo;
+      lp.M = u.rows;
+      lp.N = P.D;
+      lp.K = P.Lk;
+      lp.n_tiles = (P.D + 127) / 128;
+      jobs[i] = TcJob{lp, 1.f, true, c->scratch + u.s_off, L.lo ? L.lo + u.s_off : nullptr, u.ldS};
+    }
+    rc = run_linear_tc(c, jobs, tc == 2, fl, by_pv);
+    if (rc) return rc;
+  } else {
+    {
+      ProfScope ps(c, "attn_gemm_pv", fl, by_pv);
+      e = supra::launch_gemm_pv(aligned, L, c->stream);
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, "attn_gemm_pv");
+    c->launches += 1;
   }
-  if (e != cudaSuccess) return cuda_err(c, e, "attn_gemm_pv");
-  c->launches += 3;
   return SUPRA_ATTN_OK;
 }
 
@@ -1168,29 +1245,56 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
 // 128x128 output tiles of every problem.
 int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   const int n = (int)g.size();
-  const bool split = g[0]->cfg == 2;
-  const size_t parts = split ? 2 : 1;  // hi (and lo)
+  std::vector<TcJob> jobs((size_t)n);
+  for (int i = 0; i < n; ++i) jobs[i] = TcJob{g[i]->lin, 1.f, false, nullptr, nullptr, 0};
   std::vector<supra::LinProb> lp((size_t)n);
   for (int i = 0; i < n; ++i) lp[i] = g[i]->lin;
   int rc = norm_stats(c, g, lp.data());
   if (rc) return rc;
+  double flops = 0, bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    jobs[i].p = lp[i];
+    flops += g[i]->flops;
+    bytes += g[i]->bytes;
+  }
+  return run_linear_tc(c, jobs, g[0]->cfg == 2, flops, bytes);
+}
+
+int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, double flops, double bytes) {
+  const int n = (int)jobs.size();
+  if (n == 0) return SUPRA_ATTN_OK;
+  const size_t parts = split ? 2 : 1;  // hi (and lo)
+  std::vector<supra::LinProb> lp((size_t)n);
+  for (int i = 0; i < n; ++i) lp[i] = jobs[i].p;
+  int rc = SUPRA_ATTN_OK;
   // A gate without an activation folds into the split of w: gate[n] * (x w[n] + b[n]) =
   // x (gate[n] w[n]) + gate[n] b[n], so the product runs the plain epilogue (one extra rounding
   // of gate * w, far inside the FP32 bar). Such a w is split per gate, with a gated bias copy.
   std::vector<char> fold((size_t)n, 0);
   for (int i = 0; i < n; ++i) fold[i] = lp[i].gate != nullptr && lp[i].act == supra::kActNone;
-  std::vector<size_t> xoff((size_t)n), woff((size_t)n), boff((size_t)n, 0);
-  std::vector<char> wfirst((size_t)n, 0);
+  // Operands read in place: the TF32 form takes a 16-byte aligned fp32 operand with a row stride
+  // of a multiple of 4 floats as it is (the tensor core ignores the 13 low mantissa bits), unless
+  // it must be normalised, scaled, gated or transposed first. Everything else is split into
+  // lin_split (x per job; w once per distinct (w, shape, gate) in the flush).
+  std::vector<char> xin((size_t)n, 0), win((size_t)n, 0), wfirst((size_t)n, 0);
+  std::vector<size_t> xoff((size_t)n, 0), woff((size_t)n, 0), boff((size_t)n, 0);
   size_t need = 0;
   for (int i = 0; i < n; ++i) {
     const size_t kp = (size_t)((lp[i].K + 3) & ~3);
-    xoff[i] = need;
-    need += parts * (size_t)lp[i].M * kp;
+    xin[i] = jobs[i].xh != nullptr ||
+             (!split && !lp[i].gn_stats && jobs[i].xscale == 1.f && aligned16(lp[i].x) && (lp[i].ldx & 3) == 0);
+    win[i] = !split && !fold[i] && !jobs[i].wtrans && aligned16(lp[i].w) && (lp[i].ldw & 3) == 0;
+    if (!xin[i]) {
+      xoff[i] = need;
+      need += parts * (size_t)lp[i].M * kp;
+    }
+    if (win[i]) continue;
     const float* gi = fold[i] ? lp[i].gate : nullptr;
     int j = 0;
     for (; j < i; ++j)
-      if (lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N && lp[j].K == lp[i].K &&
-          (fold[j] ? lp[j].gate : nullptr) == gi && (!gi || lp[j].bias == lp[i].bias))
+      if (!win[j] && lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N && lp[j].K == lp[i].K &&
+          jobs[j].wtrans == jobs[i].wtrans && (fold[j] ? lp[j].gate : nullptr) == gi &&
+          (!gi || lp[j].bias == lp[i].bias))
         break;
     if (j < i) {
       woff[i] = woff[j];
@@ -1205,36 +1309,65 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
       }
     }
   }
-  rc = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, need, sizeof(float), "linear split");
-  if (rc) return rc;
-  supra::LinProb plain;
-  std::memset(&plain, 0, sizeof plain);
-  for (int i = 0; i < n; ++i) {
-    const int32_t kp = (lp[i].K + 3) & ~3;
-    float* xh = c->lin_split + xoff[i];
-    float* wh = c->lin_split + woff[i];
-    cudaError_t e;
-    {
-      ProfScope ps(c, "linear_split", 0.0, 4.0 * (1.0 + (double)parts) * lp[i].M * lp[i].K);
-      e = supra::launch_linear_split(lp[i].x, lp[i].ldx, lp[i].M, lp[i].K, lp[i], xh,
-                                     split ? xh + (size_t)lp[i].M * kp : nullptr, kp, c->stream);
-      c->launches += 1;
-      if (e == cudaSuccess && wfirst[i]) {
-        e = supra::launch_linear_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, plain, wh,
-                                       split ? wh + (size_t)lp[i].N * kp : nullptr, kp, c->stream,
-                                       fold[i] ? lp[i].gate : nullptr, lp[i].bias,
-                                       fold[i] ? c->lin_split + boff[i] : nullptr);
-        c->launches += 1;
-      }
-    }
-    if (e != cudaSuccess) return cuda_err(c, e, "linear_split");
+  if (need) {
+    rc = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, need, sizeof(float),
+                     "linear split");
+    if (rc) return rc;
   }
-  // tensor maps over the split arrays: [rows, K] with row stride kp, 32 x 128 boxes, SWIZZLE_128B,
-  // exact fp32 (the tensor core takes the hi copies as TF32 values)
+  // the split jobs
+  std::vector<supra::SplitJob> sj;
+  std::vector<int32_t> sbegin;
+  int64_t stotal = 0;
+  double sbytes = 0;
+  auto add_split = [&](const float* src, int64_t ld, int32_t rows, int32_t K, float* hi, bool trans, float xscale,
+                       const supra::LinProb* norm, const float* rowscale, const float* bias_in, float* bias_out) {
+    supra::SplitJob J;
+    std::memset(&J, 0, sizeof J);
+    const int32_t kp = (K + 3) & ~3;
+    J.src = src;
+    J.hi = hi;
+    J.lo = split ? hi + (size_t)rows * kp : nullptr;
+    J.rowscale = rowscale;
+    J.bias_in = bias_in;
+    J.bias_out = bias_out;
+    if (norm && norm->gn_stats) {
+      J.gn_stats = norm->gn_stats;
+      J.gamma = norm->gamma;
+      J.beta = norm->beta;
+      J.gn_mode = norm->gn_mode;
+      J.gn_cg = norm->gn_cg;
+      J.gn_rows = norm->gn_rows;
+      J.gn_groups = norm->gn_groups;
+      J.gn_silu = norm->gn_silu;
+    }
+    J.ld = ld;
+    J.rows = rows;
+    J.K = K;
+    J.ldd = kp;
+    J.trans = trans ? 1 : 0;
+    J.xscale = xscale;
+    J.ktiles = (K + supra::kSplitTileCols - 1) / supra::kSplitTileCols;
+    sbegin.push_back((int32_t)stotal);
+    stotal += (int64_t)((rows + supra::kSplitTileRows - 1) / supra::kSplitTileRows) * J.ktiles;
+    sbytes += 4.0 * (1.0 + (double)parts) * rows * (double)K;
+    sj.push_back(J);
+  };
+  for (int i = 0; i < n; ++i) {
+    if (!xin[i])
+      add_split(lp[i].x, lp[i].ldx, lp[i].M, lp[i].K, c->lin_split + xoff[i], false, jobs[i].xscale, &lp[i], nullptr,
+                nullptr, nullptr);
+    if (wfirst[i])
+      add_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, c->lin_split + woff[i], jobs[i].wtrans, 1.f, nullptr,
+                fold[i] ? lp[i].gate : nullptr, lp[i].bias, fold[i] ? c->lin_split + boff[i] : nullptr);
+  }
+  if (stotal > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many split tiles in one flush");
+  sbegin.push_back((int32_t)stotal);
+  // tensor maps: [rows, K] with row stride ld (the split arrays' kp, or the operand's own), 32 x
+  // 128 boxes, SWIZZLE_128B, exact fp32 (the tensor core takes them as TF32 values)
   std::vector<CUtensorMap> maps;
   std::unordered_map<MapKey, int32_t, MapKeyHash> index;
-  auto map_of = [&](const float* b, int64_t kp, int64_t rows, int64_t cols, int32_t* out, int32_t box_rows = 128) -> int {
-    const MapKey k{reinterpret_cast<uintptr_t>(b), kp, rows, cols, 32, box_rows, (int32_t)CU_TENSOR_MAP_SWIZZLE_128B, 0};
+  auto map_of = [&](const float* b, int64_t ld, int64_t rows, int64_t cols, int32_t* out, int32_t box_rows = 128) -> int {
+    const MapKey k{reinterpret_cast<uintptr_t>(b), ld, rows, cols, 32, box_rows, (int32_t)CU_TENSOR_MAP_SWIZZLE_128B, 0};
     auto it = index.find(k);
     if (it == index.end()) {
       auto ct = c->map_cache.find(k);
@@ -1253,7 +1386,6 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   std::vector<supra::LinTcProb> probs((size_t)n);
   std::vector<int32_t> begin((size_t)n + 1);
   int64_t total = 0;
-  double flops = 0, bytes = 0;
   for (int i = 0; i < n; ++i) {
     supra::LinTcProb& t = probs[i];
     std::memset(&t, 0, sizeof t);
@@ -1263,16 +1395,30 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
       t.p.bias = c->lin_split + boff[i];
     }
     const int64_t kp = (lp[i].K + 3) & ~3;
-    const float* xh = c->lin_split + xoff[i];
-    const float* wh = c->lin_split + woff[i];
-    rc = map_of(xh, kp, lp[i].M, lp[i].K, &t.mxh);
-    if (!rc) rc = map_of(wh, kp, lp[i].N, lp[i].K, &t.mwh);
-    if (!rc && split) rc = map_of(xh + (size_t)lp[i].M * kp, kp, lp[i].M, lp[i].K, &t.mxl);
-    if (!rc && split) rc = map_of(wh + (size_t)lp[i].N * kp, kp, lp[i].N, lp[i].K, &t.mwl);
-    // y through TMA stores (32 x 32 boxes) when its rows are 16-byte aligned; else per-row stores
+    const int64_t M = lp[i].M, N = lp[i].N, K = lp[i].K;
+    if (jobs[i].xh) {
+      rc = map_of(jobs[i].xh, jobs[i].ldxs, M, K, &t.mxh);
+      if (!rc && split) rc = map_of(jobs[i].xl, jobs[i].ldxs, M, K, &t.mxl);
+    } else if (xin[i]) {
+      rc = map_of(lp[i].x, lp[i].ldx, M, K, &t.mxh);
+    } else {
+      const float* xh = c->lin_split + xoff[i];
+      rc = map_of(xh, kp, M, K, &t.mxh);
+      if (!rc && split) rc = map_of(xh + (size_t)M * kp, kp, M, K, &t.mxl);
+    }
+    if (!rc && win[i]) {
+      rc = map_of(lp[i].w, lp[i].ldw, N, K, &t.mwh);
+    } else if (!rc) {
+      const float* wh = c->lin_split + woff[i];
+      rc = map_of(wh, kp, N, K, &t.mwh);
+      if (!rc && split) rc = map_of(wh + (size_t)N * kp, kp, N, K, &t.mwl);
+    }
+    // y through TMA stores (32 x 32 boxes) when its rows are 16-byte aligned and N is a multiple
+    // of 4 columns; else per-row stores. (A store box clipped at an inner extent that ends inside a
+    // 16-byte chunk overwrote the chunk's elements past the extent with zeros on B200: the first
+    // columns of a neighbouring head, written by another tile, came out 0.)
     t.my = -1;
-    if (!rc && (reinterpret_cast<uintptr_t>(lp[i].y) & 15u) == 0 && (lp[i].ldy & 3) == 0)
-      rc = map_of(lp[i].y, lp[i].ldy, lp[i].M, lp[i].N, &t.my, 32);
+    if (!rc && aligned16(lp[i].y) && (lp[i].ldy & 3) == 0 && (N & 3) == 0) rc = map_of(lp[i].y, lp[i].ldy, M, N, &t.my, 32);
     if (rc) return rc;
     t.m_tiles = (lp[i].M + 127) / 128;
     t.n_tiles = (lp[i].N + 127) / 128;
@@ -1280,22 +1426,43 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     begin[i] = (int32_t)total;
     total += (int64_t)t.m_tiles * t.n_tiles;
     if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
-    flops += g[i]->flops;
-    bytes += g[i]->bytes;
   }
   begin[n] = (int32_t)total;
+  // one descriptor staging for both launches: tensor maps (64-byte aligned), problems, tile
+  // starts, split jobs, split tile starts
   const size_t mbytes = sizeof(CUtensorMap) * maps.size();
   const size_t pbytes = align16(sizeof(supra::LinTcProb) * n);
-  const size_t bbytes = sizeof(int32_t) * (n + 1);
+  const size_t bbytes = align16(sizeof(int32_t) * (n + 1));
+  const size_t jbytes = sizeof(supra::SplitJob) * sj.size();
+  const size_t sbbytes = sj.empty() ? 0 : sizeof(int32_t) * sbegin.size();
+  const size_t body = mbytes + pbytes + bbytes + jbytes + sbbytes;
   char *h = nullptr, *dv = nullptr;
-  rc = ring_reserve(c, 64 + mbytes + pbytes + bbytes, &h, &dv);
+  rc = ring_reserve(c, 64 + body, &h, &dv);
   if (rc) return rc;
-  const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;  // tensor maps on 64 bytes
+  const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
   std::memcpy(h + pad, maps.data(), mbytes);
   std::memcpy(h + pad + mbytes, probs.data(), sizeof(supra::LinTcProb) * n);
-  std::memcpy(h + pad + mbytes + pbytes, begin.data(), bbytes);
-  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
+  std::memcpy(h + pad + mbytes + pbytes, begin.data(), sizeof(int32_t) * (n + 1));
+  if (!sj.empty()) {
+    std::memcpy(h + pad + mbytes + pbytes + bbytes, sj.data(), jbytes);
+    std::memcpy(h + pad + mbytes + pbytes + bbytes + jbytes, sbegin.data(), sbbytes);
+  }
+  rc = ring_commit(c, h, dv, pad + body);
   if (rc) return rc;
+  cudaError_t e;
+  if (!sj.empty()) {
+    supra::SplitLaunch S;
+    S.jobs = reinterpret_cast<const supra::SplitJob*>(dv + pad + mbytes + pbytes + bbytes);
+    S.begin = reinterpret_cast<const int32_t*>(dv + pad + mbytes + pbytes + bbytes + jbytes);
+    S.n = (int32_t)sj.size();
+    S.total = (int32_t)stotal;
+    {
+      ProfScope ps(c, "linear_split", 0.0, sbytes);
+      e = supra::launch_split(S, c->stream);
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, "linear_split");
+    c->launches += 1;
+  }
   supra::LinTcLaunch L;
   L.maps = reinterpret_cast<const CUtensorMap*>(dv + pad);
   L.probs = reinterpret_cast<const supra::LinTcProb*>(dv + pad + mbytes);
@@ -1304,7 +1471,6 @@ int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   L.total = (int32_t)total;
   L.status = c->d_status;
   const char* name = split ? "linear_tc_tf32x3" : "linear_tc_tf32";
-  cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
     e = supra::launch_linear_tc(L, split, c->stream);

@@ -153,9 +153,9 @@ def test_batch_shares_weights(gpu):
     rep = {r["name"]: r for r in gpu.profile_report()}
     gpu.profile_reset()
     gpu.profile(False)
-    assert rep["linear_tc_tf32x3"]["count"] == 1
-    # one split launch per x and one per distinct w (2), one product launch, one descriptor staging
-    assert gpu.launch_count() - n0 == len(Ms) + 2 + 1 + 1
+    assert rep["linear_tc_tf32x3"]["count"] == 1 and rep["linear_split"]["count"] == 1
+    # one split launch (every x and the 2 distinct w), one product launch, one descriptor staging
+    assert gpu.launch_count() - n0 == 3
     for i, m in enumerate(Ms):
         check(gpu.read(ys[i]), oracle.linear(xs[i], wa if i != 2 else w2, m, N, K, bias=ba), "tf32x3")
         ys[i].release()
@@ -226,3 +226,27 @@ def test_gates_folded_into_weights(gpu):
         np.testing.assert_array_equal(got[keep], y0s[i][keep])
         ref = oracle.gated_residual(y0s[i][idx], xs[i], wa, M, N, K, bias=ba, gate=mod, g_off=goffs[i])
         check(got[idx], ref, "tf32x3")
+
+
+def test_tf32_operands_read_in_place(gpu):
+    """The TF32 form reads 16-byte aligned operands (row strides a multiple of 4 floats) in place:
+    no split launch. An x at an odd offset is split first. Both at the TF32 bar; the split form
+    always splits."""
+    import supra_attn
+
+    rng = np.random.default_rng(41)
+    M, N, K = 200, 300, 576
+    xa = rng.standard_normal(1 + M * K).astype(np.float32)
+    wa = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    xd, wd = dev(xa), dev(wa)
+    for xo, variant, split in ((0, "tf32", False), (1, "tf32", True), (0, "tf32x3", True)):
+        gpu.profile(True)
+        gpu.profile_reset()
+        y = supra_attn.linear(gpu, xd, wd, M=M, N=N, K=K, xOff=xo, variant=variant)
+        got = gpu.read(y)
+        names = names_of(gpu)
+        gpu.profile_reset()
+        gpu.profile(False)
+        y.release()
+        assert f"linear_tc_{variant}" in names and ("linear_split" in names) == split, (xo, variant, names)
+        check(got, oracle.linear(xa[xo:xo + M * K], wa, M, N, K), variant)

@@ -3,8 +3,9 @@
 TF32 bar (its own stated tolerance, "<= 2e-3 relative on attention output"): rel-L2 <= 2e-3 per
 output tensor, the reference's own parity metric (tools/check.js:31-44), plus a sanity bound of
 5e-3 on the normwise max error max|got - ref| / max|ref| (TF32 operands carry 2^-11 relative
-rounding; T5's unscaled scores of standard deviation 8 turn that into ~2e-3 normwise max error). Requests the tensor-core kernel does not cover (head dim other than 64, rows that are not
-whole buffer rows) run the FP32 kernels and are held to the FP32 bar (1e-5).
+rounding; T5's unscaled scores of standard deviation 8 turn that into ~2e-3 normwise max error). Head dims above 128 run the score path's two products on the tensor-core linear (TF32 bar).
+Other requests the tensor-core attention kernel does not cover (head dims up to 128 other than 64,
+rows that are not whole buffer rows) run the FP32 kernels and are held to the FP32 bar (1e-5).
 """
 
 import numpy as np
@@ -226,3 +227,27 @@ def test_config2_cross_tf32(gpu):
     for b in range(0, 128, 7):
         kv = kvs[b].numpy().reshape(-1, 1152)
         check(got[b], oracle.attention_heads(qn[b], kv[:, :576], kv[:, 576:], 9), TOL_TF32)
+
+
+@pytest.mark.parametrize("Lq,Lk,H,D", [(64, 96, 1, 512), (33, 77, 1, 192), (130, 260, 2, 256), (70, 70, 2, 130)])
+def test_score_path_on_tensor_cores_tf32(gpu, Lq, Lk, H, D):
+    """Head dims above 128 (the VAE mid-block, app/models/vae.js:86) run S = Q K^T and O = P V on
+    the tensor-core linear with TF32 operands (Q, K and P read in place where 16-byte aligned) and
+    the row softmax between them, held to the TF32 bar."""
+    import supra_attn
+
+    rng = np.random.default_rng(Lq + Lk + D)
+    HD = H * D
+    q = rng.standard_normal(Lq * HD).astype(np.float32)
+    k = rng.standard_normal(Lk * HD).astype(np.float32)
+    v = rng.standard_normal(Lk * HD).astype(np.float32)
+    gpu.profile(True)
+    gpu.profile_reset()
+    o = supra_attn.attention(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=Lq, Lk=Lk, H=H, D=D, ldq=HD, ldk=HD, ldv=HD,
+                             variant="tf32")
+    got = gpu.read(o)
+    names = kernel_names(gpu)
+    gpu.profile(False)
+    o.release()
+    check(got, oracle.attention_ops(q, k, v, Lq, Lk, H, D, HD, HD, HD), TOL_TF32)
+    assert "linear_tc_tf32" in names and "attn_gemm_qk" not in names, names

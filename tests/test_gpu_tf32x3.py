@@ -186,3 +186,66 @@ def test_config2_cross_full_size(gpu):
     for b in range(0, 128, 7):
         kv = kvs[b].numpy().reshape(-1, 1152)
         check(got[b], oracle.attention_heads(qn[b], kv[:, :576], kv[:, 576:], 9))
+
+
+def vae_like(rng, T, nimg):
+    """Config 4's value distribution: x ~ N(0,1), Q/K/V = x W^T with W Xavier-uniform (512 x 512),
+    so scores q.k / sqrt(512) have standard deviation ~1."""
+    bound = (6.0 / 1024) ** 0.5
+    x = rng.standard_normal((nimg * T, 512)).astype(np.float32)
+    return [(x @ rng.uniform(-bound, bound, (512, 512)).astype(np.float32).T).reshape(-1) for _ in range(3)]
+
+
+@pytest.mark.parametrize(
+    "Lq,Lk,H,D",
+    [(64, 96, 1, 512), (33, 77, 1, 192), (130, 260, 2, 256), (70, 70, 2, 130), (70, 70, 4, 134), (200, 70, 2, 258),
+     (300, 31, 1, 512)],
+)
+def test_score_path_on_tensor_cores(gpu, Lq, Lk, H, D):
+    """Head dims above 128 (the VAE mid-block's one head of 512, app/models/vae.js:86) run the
+    score path's two products, S = Q K^T and O = P V, on the tensor-core linear with the split
+    operands, and the row softmax (which applies the scale and writes P split) between them;
+    ragged Lk (ld of the scores a multiple of 4 above Lk) and several heads included; head dims
+    that are not a multiple of 4 put a head's first columns in the 16-byte chunk of the previous
+    head's last ones. Lk < 32 stays on the FFMA GEMMs."""
+    import supra_attn
+
+    rng = np.random.default_rng(Lq * 3 + Lk * 5 + D)
+    HD = H * D
+    q = rng.standard_normal(Lq * HD).astype(np.float32)
+    k = rng.standard_normal(Lk * HD).astype(np.float32)
+    v = rng.standard_normal(Lk * HD).astype(np.float32)
+    gpu.profile(True)
+    gpu.profile_reset()
+    o = supra_attn.attention(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=Lq, Lk=Lk, H=H, D=D, ldq=HD, ldk=HD, ldv=HD,
+                             variant="tf32x3")
+    got = gpu.read(o)
+    names = names_of(gpu)
+    gpu.profile(False)
+    o.release()
+    check(got, oracle.attention_ops(q, k, v, Lq, Lk, H, D, HD, HD, HD))
+    if Lk >= 32:
+        assert "linear_tc_tf32x3" in names and "attn_softmax_rows" in names, names
+        assert "attn_gemm_qk" not in names and "attn_gemm_pv" not in names, names
+    else:
+        assert "attn_gemm_qk" in names, names
+
+
+def test_vae_full_size_on_tensor_cores(gpu):
+    """Config 4 at full size: 2 images of 32 x 32 latents (Lq = Lk = 1024, H = 1, D = 512) in one
+    flush, each image's rows at its own offset, at the FP32 bar per image."""
+    import supra_attn
+
+    rng = np.random.default_rng(4)
+    T, nimg = 1024, 2
+    q, k, v = vae_like(rng, T, nimg)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = dev(np.zeros(nimg * T * 512))
+    for i in range(nimg):
+        o = i * T * 512
+        supra_attn.attention(gpu, q=qd, k=kd, v=vd, Lq=T, Lk=T, H=1, D=512, ldq=512, ldk=512, ldv=512, qOff=o,
+                             kOff=o, vOff=o, oOff=o, out=out, variant="tf32x3")
+    got = gpu.read(out)
+    for i in range(nimg):
+        s = slice(i * T * 512, (i + 1) * T * 512)
+        check(got[s], oracle.attention_ops(q[s], k[s], v[s], T, T, 1, 512, 512, 512, 512))
