@@ -7,7 +7,9 @@
 //    query rows of one head of one problem; the host orders problems longest-Lk first.
 //  * 4 warps x 32 query rows. Lane (rg = lane/8, cg = lane%8) of warp w owns rows 32w + rg + 4i
 //    (i < 8), keys cg + 8j (j < 4) of each 32-key block and output columns 4*(cg + 8u) .. +3
-//    (u < 2): 8x4 score and 8x8 output register blocks (FFMA only, fp32 throughout).
+//    (u < 2): 8x4 score and 8x8 output register blocks (fp32 throughout). The products use the
+//    packed f32x2 FMA (two FMAs per issued instruction), which leaves issue slots for the
+//    fragment loads and the softmax: with scalar FFMA the kernel was issue-bound.
 //  * All operands arrive by TMA tensor copies (fp32 tensor maps, no rounding): one box per warp
 //    for its Q rows, one box each for the K and V rows of a 32-key block. Q and K boxes are 68
 //    columns wide, so their shared-memory rows are 68 floats apart and the fragment reads are
@@ -137,16 +139,17 @@ __device__ __forceinline__ void issue_q(const TmaLaunch& L, const QBox& q, float
 }
 
 // S = Q K^T for keys cg + 8jj, jj < NJ, of one block (NJ < 4 for a ragged last block: the key
-// groups past Lk are not computed). Component-major order: for each 4-deep slice of the head
-// dim, the products of one component are independent FFMAs, so no accumulator waits on its
-// previous update.
+// groups past Lk are not computed). Packed FFMA (f32x2, two FMAs per issued instruction): each
+// score accumulates the head dim's even and odd components in the two halves of one float2
+// ((x, y) and (z, w) of a float4 fragment are register pairs already), summed at the end.
 template <int NJ>
 __device__ __forceinline__ void qk_block(const float4* __restrict__ Q4, const float4* __restrict__ K4,
                                          float (&sc)[kRI][4]) {
+  float2 acc[kRI][NJ];
 #pragma unroll
   for (int i = 0; i < kRI; ++i)
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.f;
+    for (int jj = 0; jj < NJ; ++jj) acc[i][jj] = make_float2(0.f, 0.f);
 #pragma unroll 2
   for (int d4 = 0; d4 < kD / 4; ++d4) {
     float4 kf[NJ], qf[kRI];
@@ -157,20 +160,18 @@ __device__ __forceinline__ void qk_block(const float4* __restrict__ Q4, const fl
 #pragma unroll
     for (int i = 0; i < kRI; ++i)
 #pragma unroll
-      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].x, kf[jj].x, sc[i][jj]);
+      for (int jj = 0; jj < NJ; ++jj)
+        acc[i][jj] = __ffma2_rn(make_float2(qf[i].x, qf[i].y), make_float2(kf[jj].x, kf[jj].y), acc[i][jj]);
 #pragma unroll
     for (int i = 0; i < kRI; ++i)
 #pragma unroll
-      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].y, kf[jj].y, sc[i][jj]);
-#pragma unroll
-    for (int i = 0; i < kRI; ++i)
-#pragma unroll
-      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].z, kf[jj].z, sc[i][jj]);
-#pragma unroll
-    for (int i = 0; i < kRI; ++i)
-#pragma unroll
-      for (int jj = 0; jj < NJ; ++jj) sc[i][jj] = fmaf(qf[i].w, kf[jj].w, sc[i][jj]);
+      for (int jj = 0; jj < NJ; ++jj)
+        acc[i][jj] = __ffma2_rn(make_float2(qf[i].z, qf[i].w), make_float2(kf[jj].z, kf[jj].w), acc[i][jj]);
   }
+#pragma unroll
+  for (int i = 0; i < kRI; ++i)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) sc[i][jj] = jj < NJ ? acc[i][jj].x + acc[i][jj].y : 0.f;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -236,13 +237,15 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     const Tile Tn = tn < L.total ? tile_of(L, tn) : T;
     const QBox qn = qbox_of(Tn, w);
 
-    float4 o[kRI][2];
+    // output columns 4cg + (0,1), (2,3), 32 + 4cg + (0,1), (2,3): packed pairs
+    float2 o[kRI][4];
     float mo[kRI], l[kRI];
 #pragma unroll
     for (int i = 0; i < kRI; ++i) {
       mo[i] = -INFINITY;
       l[i] = 0.f;
-      o[i][0] = o[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o[i][u] = make_float2(0.f, 0.f);
     }
     if (!mbar_wait_bounded(&C->qbar[w], k & 1u)) {
       if (lane == 0) report_error(L.status, DEV_TIMEOUT, 21, (int32_t)k);
@@ -319,12 +322,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
             const float alpha = ex2(mprev[i] - mo[i]);
             l[i] *= alpha;
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              o[i][u].x *= alpha;
-              o[i][u].y *= alpha;
-              o[i][u].z *= alpha;
-              o[i][u].w *= alpha;
-            }
+            for (int u = 0; u < 4; ++u) o[i][u] = __fmul2_rn(o[i][u], make_float2(alpha, alpha));
           }
         }
       }
@@ -355,14 +353,11 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
 #pragma unroll
           for (int i = 0; i < kRI; ++i) {
             const float pe = e == 0 ? pf[i].x : e == 1 ? pf[i].y : e == 2 ? pf[i].z : pf[i].w;
-            o[i][0].x = fmaf(pe, v0.x, o[i][0].x);
-            o[i][0].y = fmaf(pe, v0.y, o[i][0].y);
-            o[i][0].z = fmaf(pe, v0.z, o[i][0].z);
-            o[i][0].w = fmaf(pe, v0.w, o[i][0].w);
-            o[i][1].x = fmaf(pe, v1.x, o[i][1].x);
-            o[i][1].y = fmaf(pe, v1.y, o[i][1].y);
-            o[i][1].z = fmaf(pe, v1.z, o[i][1].z);
-            o[i][1].w = fmaf(pe, v1.w, o[i][1].w);
+            const float2 pp = make_float2(pe, pe);
+            o[i][0] = __ffma2_rn(pp, make_float2(v0.x, v0.y), o[i][0]);
+            o[i][1] = __ffma2_rn(pp, make_float2(v0.z, v0.w), o[i][1]);
+            o[i][2] = __ffma2_rn(pp, make_float2(v1.x, v1.y), o[i][2]);
+            o[i][3] = __ffma2_rn(pp, make_float2(v1.z, v1.w), o[i][3]);
           }
         }
       };
@@ -397,8 +392,8 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         float* dst = orow + (int64_t)(4 * i) * ldo;
 #pragma unroll
         for (int u = 0; u < 2; ++u)
-          *reinterpret_cast<float4*>(dst + 32 * u) =
-              make_float4(o[i][u].x * inv, o[i][u].y * inv, o[i][u].z * inv, o[i][u].w * inv);
+          *reinterpret_cast<float4*>(dst + 32 * u) = make_float4(o[i][2 * u].x * inv, o[i][2 * u].y * inv,
+                                                                 o[i][2 * u + 1].x * inv, o[i][2 * u + 1].y * inv);
       }
     }
     T = Tn;
