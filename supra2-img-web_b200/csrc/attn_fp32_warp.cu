@@ -3,8 +3,11 @@
 //
 // Same algorithm as attn_fp32.cu (online softmax over key blocks, app/gpu/kernels.js:164-316),
 // organised so that the main loop has no block-wide barrier and no start-up gap between tiles:
-//  * Persistent CTAs (two per SM): CTA c runs tiles c, c + grid, c + 2*grid, ... A tile is 128
-//    query rows of one head of one problem; the host orders problems longest-Lk first.
+//  * Persistent CTAs (two per SM): CTA c starts with tile c and then claims tiles one at a time
+//    from the launch's counter (grid, grid + 1, ... in claim order). A tile is 128 query rows of
+//    one head of one problem; the host orders problems longest-Lk first. (With a fixed stride
+//    c, c + grid, ... the two CTAs of an SM progressed at different rates, about 4.8 against
+//    7.0 ms over a DiT self-attention launch, and the slower one finished alone on the SM.)
 //  * 4 warps x 32 query rows. Lane (rg = lane/8, cg = lane%8) of warp w owns rows 32w + rg + 4i
 //    (i < 8), keys cg + 8j (j < 4) of each 32-key block and output columns 4*(cg + 8u) .. +3
 //    (u < 2): 8x4 score and 8x8 output register blocks (fp32 throughout). The products use the
@@ -20,7 +23,9 @@
 //    out on the stage's counter; the last warp out issues the block three ahead, which may
 //    belong to the CTA's next tile, through a cursor kept in shared memory. No warp waits for
 //    a producer, warps drift freely, and the next tile's first blocks are already in flight
-//    while the current tile finishes.
+//    while the current tile finishes. The cursor claims the next tile when it issues a tile's
+//    last block and publishes it in a small shared table before that block's barrier arrive,
+//    so every warp finds it there once it has waited for the block.
 //  * Each warp fetches its Q rows of the next tile as soon as it has finished the last QK^T of
 //    the current tile (its own Q rows are read by no other warp).
 //  * Lazy rescaling: the running row maximum used as the exp2 offset is only moved when a block
@@ -69,14 +74,17 @@ static_assert((OFF_K * 4) % 128 == 0 && (OFF_V * 4) % 128 == 0 && kQBytes % 128 
 // Next K/V block of this CTA's block sequence: tile t, block b of its nblk, and the tile's TMA
 // coordinates (head column already added).
 struct Cursor {
-  int32_t t, b, nblk, mk, mv, kx, ky, vx, vy, pad;
+  int32_t t, b, nblk, mk, mv, kx, ky, vx, vy;
+  int32_t k;  // the tile's position in the CTA's tile sequence
 };
+constexpr int kTileSlots = 8;  // claimed tiles in flight: the cursor runs at most 3 blocks ahead
 struct Ctl {
   uint64_t qbar[kW];
   uint64_t full[kNS];
   int32_t cnt[kNS];
   int32_t pad;
   Cursor cur;
+  int32_t tiles[kTileSlots];  // tile k of this CTA at tiles[k % kTileSlots]
 };
 constexpr int BYTES = FLOATS * 4 + (int)sizeof(Ctl) + 128;  // + slack for the 128-byte alignment
 
@@ -110,17 +118,24 @@ __device__ __forceinline__ void cursor_at(const TmaLaunch& L, Cursor& c, int t) 
   c.vy = T.p->vy;
 }
 
-// Issues the cursor's block into stage s and advances the cursor (one thread). Past the CTA's
-// last tile it issues nothing: no warp will wait for that stage again.
+// Issues the cursor's block into stage s and advances the cursor (one thread). With a tile's
+// last block it first claims the CTA's next tile and publishes it in C->tiles; the barrier
+// arrive below releases that store to every warp that later waits for this block. Past the
+// CTA's last tile it issues nothing: no warp will wait for that stage again.
 __device__ __forceinline__ void issue_next(const TmaLaunch& L, Ctl* C, float* Ks, float* Vs, int s) {
   Cursor& c = C->cur;
   if (c.t >= L.total) return;
+  int tn = 0;
+  if (c.b + 1 == c.nblk) {
+    tn = (int)gridDim.x + atomicAdd(L.next_tile, 1);
+    C->tiles[(c.k + 1) % kTileSlots] = tn;
+  }
   uint64_t* bar = &C->full[s];
   mbar_arrive_expect_tx(bar, kKBytes + kVBytes);
   tc::tma_load_2d(Ks + s * kNK * kKS, L.maps + c.mk, c.kx, c.ky + c.b * kNK, bar);
   tc::tma_load_2d(Vs + s * kNK * kVS, L.maps + c.mv, c.vx, c.vy + c.b * kNK, bar);
   if (++c.b == c.nblk) {
-    const int tn = c.t + (int)gridDim.x;
+    ++c.k;
     if (tn < L.total) cursor_at(L, c, tn);
     else c.t = tn;
   }
@@ -209,6 +224,8 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
       C->cnt[s] = 0;
     }
     mbar_fence_init();
+    C->tiles[0] = t0;
+    C->cur.k = 0;
   }
   __syncthreads();  // the kernel's only block-wide barrier
   if (tid == 0) {
@@ -222,7 +239,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
   const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
   uint32_t g = 0;  // position in the CTA's K/V block sequence
   uint32_t k = 0;  // position in the CTA's tile sequence
-  for (int t = t0; t < L.total; t += (int)gridDim.x, ++k) {
+  for (int t = t0; t < L.total; ++k) {
     const TmaProb* __restrict__ pp = T.p;
     int Lk = pp->Lk;
     float sl2 = pp->scale_log2;
@@ -232,10 +249,11 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     const int64_t ldo = pp->ldo;
     const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
     float* const orow = pp->o + pp->o_off + ((int64_t)T.q0 + kRowsW * w + rg) * ldo + (int64_t)T.h * kD + 4 * cg;
-    // the next tile, looked up now: its Q rows are requested right after this tile's last QK^T
-    const int tn = t + (int)gridDim.x;
-    const Tile Tn = tn < L.total ? tile_of(L, tn) : T;
-    const QBox qn = qbox_of(Tn, w);
+    // the next tile: known once the wait for this tile's last block has returned (it was claimed
+    // and published before that block was issued); its Q rows are requested right after this
+    // tile's last QK^T
+    int tn = L.total;
+    Tile Tn = T;
 
     // output columns 4cg + (0,1), (2,3), 32 + 4cg + (0,1), (2,3): packed pairs
     float2 o[kRI][4];
@@ -260,6 +278,10 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         if (lane == 0) report_error(L.status, DEV_TIMEOUT, 22, (int32_t)g);
         return;
       }
+      if (j == nblk - 1) {
+        tn = *reinterpret_cast<volatile const int32_t*>(&C->tiles[(k + 1) % kTileSlots]);
+        if (tn < L.total) Tn = tile_of(L, tn);
+      }
       const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
       const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
 
@@ -278,7 +300,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         __syncwarp();
         if (lane == 0) {
           fence_proxy_async_smem();
-          issue_q(L, qn, Qw, &C->qbar[w]);
+          issue_q(L, qbox_of(Tn, w), Qw, &C->qbar[w]);
         }
       }
       if (nk < kNK) {  // ragged block (warp-uniform): keys past Lk get -inf (a select, not a product)
@@ -397,6 +419,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
       }
     }
     T = Tn;
+    t = tn;
   }
 }
 

@@ -119,6 +119,10 @@ struct TmaLaunch {
   const int32_t* begin;
   int32_t n, total, uniform;
   int32_t* status;
+  // Tiles past the first gridDim.x are handed out by this counter (zero at launch, one per
+  // launch, in the staged descriptor block): the persistent FP32 kernel's CTAs claim them one at
+  // a time, so CTAs that share an SM and progress at different rates finish together.
+  int32_t* next_tile = nullptr;
 };
 
 cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, bool split, cudaStream_t s);

@@ -1100,16 +1100,19 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     flops += q.flops;
     bytes += q.bytes;
   }
-  if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
+  // (headroom: claimed tile indices run up to total + 2 x the grid)
+  if (total > INT32_MAX - (int64_t(1) << 20))
+    return set_err(c, SUPRA_ATTN_EINVAL, "too many tiles in one flush (%lld)", (long long)total);
   begin[n] = (int32_t)total;
   std::vector<int32_t> lut;
   std::vector<int64_t> loff;
   const size_t pbytes = align16(sizeof(supra::TmaProb) * n);
   const size_t lbytes = t5_luts(g, lut, loff);
   const size_t mbytes = sizeof(CUtensorMap) * maps.size();
-  const size_t bbytes = sizeof(int32_t) * (n + 1);
+  const size_t bbytes = align16(sizeof(int32_t) * (n + 1));
+  const size_t cbytes = 16;  // the launch's tile counter, staged as zero
   char *h = nullptr, *dv = nullptr;
-  int rc = ring_reserve(c, 64 + pbytes + mbytes + lbytes + bbytes, &h, &dv);
+  int rc = ring_reserve(c, 64 + pbytes + mbytes + lbytes + bbytes + cbytes, &h, &dv);
   if (rc) return rc;
   // tensor maps must sit on a 64-byte boundary in device memory
   const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
@@ -1120,10 +1123,12 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   std::memcpy(hm, maps.data(), mbytes);
   std::memcpy(hm + mbytes, probs.data(), sizeof(supra::TmaProb) * n);
   if (!lut.empty()) std::memcpy(hm + mbytes + pbytes, lut.data(), lut.size() * sizeof(int32_t));
-  std::memcpy(hm + mbytes + pbytes + lbytes, begin.data(), bbytes);
-  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + lbytes + bbytes);
+  std::memcpy(hm + mbytes + pbytes + lbytes, begin.data(), sizeof(int32_t) * (n + 1));
+  std::memset(hm + mbytes + pbytes + lbytes + bbytes, 0, cbytes);
+  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + lbytes + bbytes + cbytes);
   if (rc) return rc;
   supra::TmaLaunch L;
+  L.next_tile = reinterpret_cast<int32_t*>(dm + mbytes + pbytes + lbytes + bbytes);
   L.maps = reinterpret_cast<const CUtensorMap*>(dm);
   L.probs = reinterpret_cast<const supra::TmaProb*>(dm + mbytes);
   L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes + lbytes);
