@@ -75,7 +75,8 @@ struct Lay {
   static constexpr uint32_t VL = V + kNSV * kKVBytes;
   static constexpr uint32_t O = SPLIT ? VL + kNSV * kKVBytes : V + kNS * kKVBytes;
   static constexpr uint32_t BAR = O + 4 * kOStage;
-  static constexpr uint32_t SMEM = BAR + 256 + 1024;  // barriers + alignment slack for the 1024-B base
+  static constexpr uint32_t TILES = BAR + 256;         // the CTA's claimed tiles (TileSlot table)
+  static constexpr uint32_t SMEM = TILES + 64 + 1024;  // + alignment slack for the 1024-B base
   static constexpr uint32_t TMEM_COLS = SPLIT ? 512 : 256;
   static constexpr int THREADS = SPLIT ? 256 : 192;  // 8 warps: two per SM sub-partition, up to 255 registers
   static constexpr int CTAS_PER_SM = SPLIT ? 1 : 2;
@@ -112,7 +113,7 @@ __device__ __forceinline__ float ex2(float x) {
 // Wait ids reported with a timeout (status[2]); status[3] carries the waiter's block counter.
 enum WaitId : int32_t {
   W_Q_EMPTY = 31, W_KV_EMPTY = 32, W_Q_FULL = 33, W_KV_FULL = 34, W_P_FULL = 35, W_O_EMPTY = 36,
-  W_S_FULL = 37, W_PV_RESCALE = 38, W_PV_EPILOGUE = 39, W_CONV_Q = 40, W_CONV_KV = 41,
+  W_S_FULL = 37, W_PV_RESCALE = 38, W_PV_EPILOGUE = 39, W_CONV_Q = 40, W_CONV_KV = 41, W_TILE = 42,
 };
 
 // The split of the 3xTF32 scheme, x*y ~ hi(x)hi(y) + hi(x)lo(y) + lo(x)hi(y): hi = x with the
@@ -147,6 +148,47 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
       }
     }
   }
+}
+
+// The CTA's tiles in claim order: tile k (k = 0, 1, ...) sits in slot k % kTileSlots with
+// seq = k + 1. Tile 0 is blockIdx.x; the Q/K producer claims each later one from the launch's
+// counter (L.next_tile) as it starts it and publishes it here, and every other role reads it
+// before working on it. (With a fixed stride blockIdx.x, + gridDim.x, ... the two CTAs that
+// share an SM progress at different rates and the slower one finishes alone.) The producer runs
+// at most a few tiles ahead of the slowest role, well inside the 8 slots; a slot that does not
+// hold the awaited tile within the wait limit is reported like any other wait.
+constexpr int kTileSlots = 8;
+struct TileSlot {
+  int32_t seq, t;
+};
+static_assert(sizeof(TileSlot) * kTileSlots <= 64, "tile table");
+
+__device__ __forceinline__ void publish_tile(TileSlot* tab, int k, int t) {
+  volatile TileSlot* s = tab + (k % kTileSlots);
+  s->t = t;
+  __threadfence_block();
+  s->seq = k + 1;
+}
+
+__device__ __forceinline__ bool tile_at(TileSlot* tab, int k, int* t, volatile int32_t* abort, int32_t* status) {
+  volatile TileSlot* s = tab + (k % kTileSlots);
+  if (s->seq != k + 1) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+      if (s->seq == k + 1) break;
+      if ((it & 63u) == 0u) {
+        if (*abort) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+          report_error(status, DEV_TIMEOUT, W_TILE, k);
+          *abort = 1;
+          return false;
+        }
+      }
+    }
+  }
+  __threadfence_block();
+  *t = s->t;
+  return true;
 }
 
 // A tile of the launch: problem, head and first query row.
@@ -203,6 +245,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
   float* Os = reinterpret_cast<float*>(base + Y::O);
   Bars* B = reinterpret_cast<Bars*>(base + Y::BAR);
   volatile int32_t* abort = &B->abort;
+  TileSlot* tab = reinterpret_cast<TileSlot*>(base + Y::TILES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,6 +273,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       mbar_init(&B->v_conv[s], kConv);
     }
     B->abort = 0;
+    TileSlot* tab0 = reinterpret_cast<TileSlot*>(base + Y::TILES);
+    for (int i = 0; i < kTileSlots; ++i) tab0[i].seq = 0;
+    tab0[0].t = (int32_t)blockIdx.x;
+    tab0[0].seq = 1;
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -247,7 +294,9 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       // the V ring, on its own lane so that K blocks run ahead of the V stages, which stay busy
       // until their PV products are done
       int n = 0;
-      for (int t = blockIdx.x; t < L.total; t += gridDim.x) {
+      for (int k = 0;; ++k) {
+        int t = 0;
+        if (!tile_at(tab, k, &t, abort, L.status) || t >= L.total) break;
         const Tile T = tile_of(L, t);
         const TmaProb* pp = T.p;
         const CUtensorMap* mv = L.maps + pp->mv;
@@ -264,8 +313,14 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         if (!ok) break;
       }
     } else if (lane == 0) {
-      int n = 0, k = 0;
-      for (int t = blockIdx.x; t < L.total; t += gridDim.x, ++k) {
+      int n = 0;
+      for (int k = 0;; ++k) {
+        int t = (int)blockIdx.x;
+        if (k > 0) {  // claim and publish the CTA's next tile (past the end: every role stops)
+          t = (int)gridDim.x + atomicAdd(L.next_tile, 1);
+          publish_tile(tab, k, t);
+        }
+        if (t >= L.total) break;
         const Tile T = tile_of(L, t);
         const TmaProb* pp = T.p;
         const CUtensorMap* mq = L.maps + pp->mq;
@@ -354,7 +409,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       pend_n = -1;
       return true;
     };
-    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
+    for (; ok; ++k) {
+      int t = 0;
+      ok = __all_sync(0xffffffffu, tile_at(tab, k, &t, abort, L.status));
+      if (!ok || t >= L.total) break;
       const Tile T = tile_of(L, t);
       int Lk = T.p->Lk;
       asm volatile("" : "+r"(Lk));  // kept in a register (see the softmax warps)
@@ -425,7 +483,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     float v[64];
     float o[SPLIT ? 64 : 1];  // split kernel: this thread's row of O
     int kt = 0;               // this CTA's tile count
-    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++kt) {
+    for (; ok; ++kt) {
+      int t = 0;
+      ok = __all_sync(0xffffffffu, tile_at(tab, kt, &t, abort, L.status));
+      if (!ok || t >= L.total) break;
       const Tile T = tile_of(L, t);
       const TmaProb* pp = T.p;
       int Lk = pp->Lk, Lq = pp->Lq;
@@ -564,7 +625,12 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           tc::tmem_wait_st();
           tc::fence_before_sync();
           mbar_arrive(&B->p_full[b]);
-          if (j == T.nblk - 1 && t + (int)gridDim.x < L.total) {
+          int tn = L.total;
+          if (j == T.nblk - 1) {  // the CTA's next tile, once the producer has claimed it
+            ok = __all_sync(0xffffffffu, tile_at(tab, kt + 1, &tn, abort, L.status));
+            if (!ok) break;
+          }
+          if (j == T.nblk - 1 && tn < L.total) {
             // the next tile's Q, into the other buffer, before this tile's epilogue: the tensor
             // core can start the next tile while the epilogue runs
             ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)((kt + 1) & 1), abort, L.status, W_CONV_Q, n));
@@ -672,7 +738,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     const bool vconv = warp == 7;
     bool ok = true;
     int n = 0, k = 0;
-    for (int t = blockIdx.x; ok && t < L.total; t += gridDim.x, ++k) {
+    for (; ok; ++k) {
+      int t = 0;
+      ok = __all_sync(0xffffffffu, tile_at(tab, k, &t, abort, L.status));
+      if (!ok || t >= L.total) break;
       const Tile T = tile_of(L, t);
       int Lk = T.p->Lk;
       asm volatile("" : "+r"(Lk));  // kept in a register (see the softmax warps)
