@@ -157,7 +157,9 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 // ---- tiled TMA store (2-D, from this CTA's shared memory), tracked by bulk async-groups -------------
-// Elements of the box outside the tensor map's extents are not written.
+// Elements of the box outside the tensor map's extents are not written, except that a box
+// clipped at an inner extent ending inside a 16-byte chunk overwrote the rest of that chunk with
+// zeros on B200: maps used for stores get an inner extent of a multiple of 16 bytes.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
