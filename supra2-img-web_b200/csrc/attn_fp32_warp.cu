@@ -1,5 +1,7 @@
-// Fused FP32 attention, persistent warp-pipelined kernel (sm_100a): D = 64, no bias, scale > 0.
-// The DiT self/cross-attention kernel (app/models/dit.js:172,184).
+// Fused FP32 attention, persistent warp-pipelined kernel (sm_100a): D = 64, scale > 0, with or
+// without a score bias (expanded [H, Lq, Lk], or the T5 [buckets, H] table formed in-kernel).
+// The DiT self/cross-attention kernel (app/models/dit.js:172,184) and, with the bias, the T5
+// encoder's (app/models/t5.js:80).
 //
 // Same algorithm as attn_fp32.cu (online softmax over key blocks, app/gpu/kernels.js:164-316),
 // organised so that the main loop has no block-wide barrier and no start-up gap between tiles:
@@ -195,6 +197,7 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+template <bool BIAS>
 __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid_constant__ TmaLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -248,6 +251,9 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     // this lane's first output row, read now rather than behind the last block
     const int64_t ldo = pp->ldo;
     const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
+    // With a bias (the T5 encoder: Lq = Lk, often below 128) a warp whose rows all lie past Lq
+    // skips the arithmetic; it still waits for its Q rows and releases every K/V stage.
+    const bool active = !BIAS || kRowsW * w < pp->Lq - T.q0;
     float* const orow = pp->o + pp->o_off + ((int64_t)T.q0 + kRowsW * w + rg) * ldo + (int64_t)T.h * kD + 4 * cg;
     // the next tile: known once the wait for this tile's last block has returned (it was claimed
     // and published before that block was issued); its Q rows are requested right after this
@@ -287,7 +293,8 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
 
       // ---- S = Q K^T
       float sc[kRI][4];
-      if (nk == kNK) {
+      if (!active) {
+      } else if (nk == kNK) {
         qk_block<4>(Q4, K4, sc);
       } else {
         const int nj = (nk + 7) >> 3;
@@ -303,90 +310,126 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
           issue_q(L, qbox_of(Tn, w), Qw, &C->qbar[w]);
         }
       }
-      if (nk < kNK) {  // ragged block (warp-uniform): keys past Lk get -inf (a select, not a product)
-#pragma unroll
-        for (int i = 0; i < kRI; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) sc[i][jj] = (cg + 8 * jj < nk) ? sc[i][jj] : -INFINITY;
-      }
+      if (active) {
+        if (nk < kNK) {  // ragged block (warp-uniform): keys past Lk get -inf (a select, not a product)
+  #pragma unroll
+          for (int i = 0; i < kRI; ++i)
+  #pragma unroll
+            for (int jj = 0; jj < 4; ++jj) sc[i][jj] = (cg + 8 * jj < nk) ? sc[i][jj] : -INFINITY;
+        }
+        if constexpr (BIAS) {
+          // scores into the exp2 domain with the bias added, s scale log2 e + b log2 e (the
+          // reference adds the bias to the scaled scores, app/gpu/kernels.js:53-62); rows past Lq
+          // and keys past Lk take none. The T5 form looks the bias up in the [buckets, H] table
+          // through the relative-position bucket table.
+          const int Lq = pp->Lq;
+          const int r0 = T.q0 + kRowsW * w + rg, c0 = j * kNK + cg;
+          if (pp->rel_lut) {
+            const float* tab_h = pp->bias + T.h;
+            const int32_t* lut_c = pp->rel_lut + pp->rel_max;
+            const int32_t rel_max = pp->rel_max;
+            const uint32_t Hu = (uint32_t)pp->H;
+  #pragma unroll
+            for (int i = 0; i < kRI; ++i)
+  #pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int r = r0 + 4 * i, c = c0 + 8 * jj;
+                const float b = (r < Lq && c < Lk) ? t5_table_bias(tab_h, lut_c, rel_max, Hu, c - r) : 0.f;
+                sc[i][jj] = fmaf(b, 1.4426950408889634f, sc[i][jj] * sl2);
+              }
+          } else {
+            const float* bh = pp->bias + (int64_t)T.h * Lq * Lk;
+  #pragma unroll
+            for (int i = 0; i < kRI; ++i)
+  #pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int r = r0 + 4 * i, c = c0 + 8 * jj;
+                const float b = (r < Lq && c < Lk) ? __ldg(bh + (int64_t)r * Lk + c) : 0.f;
+                sc[i][jj] = fmaf(b, 1.4426950408889634f, sc[i][jj] * sl2);
+              }
+          }
+        }
+        // exponent factor: the raw scores times scale log2 e, or the biased scores as they are
+        const float f = BIAS ? 1.f : sl2;
 
-      // ---- softmax with a lazily moved offset (exp2 domain). scale > 0 (host-checked), so the
-      // maximum of the raw scores times scale*log2(e) is the maximum of the scaled scores.
-      // Cheap test first: does any lane hold a score more than 8 above its row's offset? Only
-      // then (every tile's first block, rarely afterwards) are the row maxima reduced across
-      // the row's 8 lanes and the offsets moved.
-      float lmax[kRI];
-      bool need = false;
-#pragma unroll
-      for (int i = 0; i < kRI; ++i) {
-        lmax[i] = fmaxf(fmaxf(sc[i][0], sc[i][1]), fmaxf(sc[i][2], sc[i][3]));
-        need |= fmaf(lmax[i], sl2, -mo[i]) > 8.f;
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        bool moved = false;
-        float mprev[kRI];
-#pragma unroll
+        // ---- softmax with a lazily moved offset (exp2 domain). scale > 0 (host-checked), so the
+        // maximum of the raw scores times scale*log2(e) is the maximum of the scaled scores.
+        // Cheap test first: does any lane hold a score more than 8 above its row's offset? Only
+        // then (every tile's first block, rarely afterwards) are the row maxima reduced across
+        // the row's 8 lanes and the offsets moved.
+        float lmax[kRI];
+        bool need = false;
+  #pragma unroll
         for (int i = 0; i < kRI; ++i) {
-          float mr = lmax[i];
-          mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
-          mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
-          mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
-          const float mx = mr * sl2;  // the same value in all 8 lanes of the row
-          mprev[i] = mo[i];
-          if (mx > mo[i] + 8.f) {
-            mo[i] = mx;
-            moved = true;
-          }
+          lmax[i] = fmaxf(fmaxf(sc[i][0], sc[i][1]), fmaxf(sc[i][2], sc[i][3]));
+          need |= fmaf(lmax[i], f, -mo[i]) > 8.f;
         }
-        if (j > 0 && __any_sync(0xffffffffu, moved)) {  // (block 0: O and l are still zero)
-#pragma unroll
+        if (__any_sync(0xffffffffu, need)) {
+          bool moved = false;
+          float mprev[kRI];
+  #pragma unroll
           for (int i = 0; i < kRI; ++i) {
-            const float alpha = ex2(mprev[i] - mo[i]);
-            l[i] *= alpha;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) o[i][u] = __fmul2_rn(o[i][u], make_float2(alpha, alpha));
+            float mr = lmax[i];
+            mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
+            mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
+            mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
+            const float mx = mr * f;  // the same value in all 8 lanes of the row
+            mprev[i] = mo[i];
+            if (mx > mo[i] + 8.f) {
+              mo[i] = mx;
+              moved = true;
+            }
+          }
+          if (j > 0 && __any_sync(0xffffffffu, moved)) {  // (block 0: O and l are still zero)
+  #pragma unroll
+            for (int i = 0; i < kRI; ++i) {
+              const float alpha = ex2(mprev[i] - mo[i]);
+              l[i] *= alpha;
+  #pragma unroll
+              for (int u = 0; u < 4; ++u) o[i][u] = __fmul2_rn(o[i][u], make_float2(alpha, alpha));
+            }
           }
         }
-      }
-#pragma unroll
-      for (int i = 0; i < kRI; ++i) {
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const float pe = ex2(fmaf(sc[i][jj], sl2, -mo[i]));
-          l[i] += pe;
-          Pw[(rg + 4 * i) * kPS + cg + 8 * jj] = pe;
+  #pragma unroll
+        for (int i = 0; i < kRI; ++i) {
+  #pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const float pe = ex2(fmaf(sc[i][jj], f, -mo[i]));
+            l[i] += pe;
+            Pw[(rg + 4 * i) * kPS + cg + 8 * jj] = pe;
+          }
         }
-      }
-      __syncwarp();
+        __syncwarp();
 
-      // ---- O += P V: whole groups of 4 valid keys, then the ragged group, whose V rows past
-      // Lk are replaced by zeros (they may hold anything, and 0 * inf is not 0).
-      auto pv_group = [&](int k4, int valid) {
-        float4 pf[kRI];
-#pragma unroll
-        for (int i = 0; i < kRI; ++i) pf[i] = P4[i * 4 * (kPS / 4) + k4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-          if (e < valid) {
-            v0 = V4[(k4 * 4 + e) * (kVS / 4)];
-            v1 = V4[(k4 * 4 + e) * (kVS / 4) + 8];
+        // ---- O += P V: whole groups of 4 valid keys, then the ragged group, whose V rows past
+        // Lk are replaced by zeros (they may hold anything, and 0 * inf is not 0).
+        auto pv_group = [&](int k4, int valid) {
+          float4 pf[kRI];
+  #pragma unroll
+          for (int i = 0; i < kRI; ++i) pf[i] = P4[i * 4 * (kPS / 4) + k4];
+  #pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+            if (e < valid) {
+              v0 = V4[(k4 * 4 + e) * (kVS / 4)];
+              v1 = V4[(k4 * 4 + e) * (kVS / 4) + 8];
+            }
+  #pragma unroll
+            for (int i = 0; i < kRI; ++i) {
+              const float pe = e == 0 ? pf[i].x : e == 1 ? pf[i].y : e == 2 ? pf[i].z : pf[i].w;
+              const float2 pp = make_float2(pe, pe);
+              o[i][0] = __ffma2_rn(pp, make_float2(v0.x, v0.y), o[i][0]);
+              o[i][1] = __ffma2_rn(pp, make_float2(v0.z, v0.w), o[i][1]);
+              o[i][2] = __ffma2_rn(pp, make_float2(v1.x, v1.y), o[i][2]);
+              o[i][3] = __ffma2_rn(pp, make_float2(v1.z, v1.w), o[i][3]);
+            }
           }
-#pragma unroll
-          for (int i = 0; i < kRI; ++i) {
-            const float pe = e == 0 ? pf[i].x : e == 1 ? pf[i].y : e == 2 ? pf[i].z : pf[i].w;
-            const float2 pp = make_float2(pe, pe);
-            o[i][0] = __ffma2_rn(pp, make_float2(v0.x, v0.y), o[i][0]);
-            o[i][1] = __ffma2_rn(pp, make_float2(v0.z, v0.w), o[i][1]);
-            o[i][2] = __ffma2_rn(pp, make_float2(v1.x, v1.y), o[i][2]);
-            o[i][3] = __ffma2_rn(pp, make_float2(v1.z, v1.w), o[i][3]);
-          }
-        }
-      };
-      const int nfull = nk >> 2;
-#pragma unroll 2
-      for (int k4 = 0; k4 < nfull; ++k4) pv_group(k4, 4);
-      if (nk & 3) pv_group(nfull, nk & 3);
+        };
+        const int nfull = nk >> 2;
+  #pragma unroll 2
+        for (int k4 = 0; k4 < nfull; ++k4) pv_group(k4, 4);
+        if (nk & 3) pv_group(nfull, nk & 3);
+      }  // active
       __syncwarp();  // every lane is done with P and with stage s
 
       // ---- release stage s; the last warp out loads the block three ahead into it -----------
@@ -427,14 +470,15 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
 
 int attn_fp32_warp_tile_rows() { return kRows; }
 
-cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s) {
+cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, bool bias, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(attn_fp32_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+  auto kern = bias ? attn_fp32_warp_kernel<true> : attn_fp32_warp_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = L.total < 2 * sms ? L.total : 2 * sms;  // persistent: two CTAs per SM
-  attn_fp32_warp_kernel<<<grid, kW * 32, BYTES, s>>>(L);
+  kern<<<grid, kW * 32, BYTES, s>>>(L);
   return cudaGetLastError();
 }
 

@@ -128,13 +128,14 @@ struct TmaLaunch {
 cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, bool split, cudaStream_t s);
 int attn_tf32_tile_rows();
 
-// Persistent FP32 kernel (attn_fp32_warp.cu): D = 64, no bias, scale > 0. Q and K tensor maps
+// Persistent FP32 kernel (attn_fp32_warp.cu): D = 64, scale > 0, optional score bias (expanded
+// or the T5 table, as TmaProb describes it). Q and K tensor maps
 // have boxes of kFwBoxWide columns x 32 rows, V maps kFwBoxNarrow columns x 32 rows (fp32, no
 // swizzle): the 4 extra Q/K columns pad the shared-memory rows against bank conflicts.
 constexpr int kFwBoxWide = 68;
 constexpr int kFwBoxNarrow = 64;
 constexpr int kFwBoxRows = 32;
-cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, cudaStream_t s);
+cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, bool bias, cudaStream_t s);
 int attn_fp32_warp_tile_rows();
 
 // Normalisation of x in the linear prologue (LinProb::gn_mode): GroupNorm with gamma/beta,

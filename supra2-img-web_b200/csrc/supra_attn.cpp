@@ -534,9 +534,8 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
       q.path = PATH_TF32;
       q.cfg = d->variant == SUPRA_ATTN_TF32X3 ? 1 : 0;
     }
-  } else if (tma_ok && !q.bias && scale > 0.f && d->Lq > 64 && d->ldq >= supra::kFwBoxWide &&
-             d->ldk >= supra::kFwBoxWide) {
-    // persistent FP32 kernel: its Q/K boxes are kFwBoxWide columns wide
+  } else if (tma_ok && scale > 0.f && d->Lq > 64 && d->ldq >= supra::kFwBoxWide && d->ldk >= supra::kFwBoxWide) {
+    // persistent FP32 kernel (with or without a bias): its Q/K boxes are kFwBoxWide columns wide
     q.path = PATH_FP32_TMA;
     q.cfg = 0;
   }
@@ -1142,13 +1141,13 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     if (uni) L.uniform = (int32_t)t0;
   }
   L.status = c->d_status;
-  const char* name = !tf32  ? "attn_fp32_d64_tma"
+  const char* name = !tf32  ? (g[0]->bias ? "attn_fp32_d64_tma_bias" : "attn_fp32_d64_tma")
                      : split ? (g[0]->bias ? "attn_tf32x3_d64_bias" : "attn_tf32x3_d64")
                              : (g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64");
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = tf32 ? supra::launch_attn_tf32(L, g[0]->bias, split, c->stream) : supra::launch_attn_fp32_warp(L, c->stream);
+    e = tf32 ? supra::launch_attn_tf32(L, g[0]->bias, split, c->stream) : supra::launch_attn_fp32_warp(L, g[0]->bias, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;

@@ -139,6 +139,59 @@ def test_t5_table_long_and_wide(gpu, L, H, D):
         t.release()
 
 
+@pytest.mark.parametrize("L", [65, 100, 128, 300])
+def test_t5_bias_on_the_persistent_kernel(gpu, L):
+    """Lq > 64 with a bias (the T5 encoder, app/models/t5.js:80) runs the bias form of the
+    persistent FP32 kernel, table and expanded forms bit-identical to each other; L = 100 and 300
+    leave query rows past Lq in a tile (warps wholly past Lq skip the arithmetic)."""
+    import supra_attn
+
+    rng = np.random.default_rng(L)
+    H = 12
+    table = (0.5 * rng.standard_normal(32 * H)).astype(np.float32)
+    q, k, v = (rng.standard_normal(L * H * 64).astype(np.float32) for _ in range(3))
+    ref = oracle.attention_ops(q, k, v, L, L, H, 64, H * 64, H * 64, H * 64, scale=1.0,
+                               bias=oracle.position_bias(table, L, H, 32, 128).reshape(-1))
+    td = dev(table)
+    kw = dict(q=dev(q), k=dev(k), v=dev(v), Lq=L, Lk=L, H=H, D=64, ldq=H * 64, ldk=H * 64, ldv=H * 64, scale=1.0)
+    bias = supra_attn.position_bias(gpu, td, L, H=H, buckets=32, max_distance=128)
+    gpu.sync()
+    gpu.profile(True)
+    gpu.profile_reset()
+    o_tab = attn(gpu, t5_table=td, **kw)
+    gpu.flush()
+    o_exp = attn(gpu, bias=bias, **kw)
+    got = gpu.read(o_tab)
+    rep = {r["name"]: r["count"] for r in gpu.profile_report()}
+    gpu.profile(False)
+    assert rep == {"attn_fp32_d64_tma_bias": 2}, rep
+    assert_close(got, ref)
+    np.testing.assert_array_equal(got, gpu.read(o_exp))
+    for t in (o_tab, o_exp, bias):
+        t.release()
+
+
+def test_expanded_bias_scaled_on_the_persistent_kernel(gpu):
+    """A [H, Lq, Lk] bias with scale 1/8 and Lq != Lk (ragged last key block, a partial last
+    query tile) on the persistent FP32 kernel's bias form, against the oracle."""
+    rng = np.random.default_rng(9)
+    Lq, Lk, H = 200, 150, 3
+    q = rng.standard_normal(Lq * H * 64).astype(np.float32)
+    k, v = (rng.standard_normal(Lk * H * 64).astype(np.float32) for _ in range(2))
+    b = rng.standard_normal(H * Lq * Lk).astype(np.float32)
+    ref = oracle.attention_ops(q, k, v, Lq, Lk, H, 64, H * 64, H * 64, H * 64, scale=0.125, bias=b)
+    gpu.profile(True)
+    gpu.profile_reset()
+    o = attn(gpu, q=dev(q), k=dev(k), v=dev(v), Lq=Lq, Lk=Lk, H=H, D=64, ldq=H * 64, ldk=H * 64, ldv=H * 64,
+             scale=0.125, bias=dev(b))
+    got = gpu.read(o)
+    names = [r["name"] for r in gpu.profile_report()]
+    gpu.profile(False)
+    o.release()
+    assert names == ["attn_fp32_d64_tma_bias"], names
+    assert_close(got, ref)
+
+
 def test_t5_table_ragged_batch(gpu):
     """256 prompts of ragged length (config 3) in one flush, table mode, against the oracle."""
     import supra_attn
