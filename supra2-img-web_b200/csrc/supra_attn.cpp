@@ -534,7 +534,8 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
       q.path = PATH_TF32;
       q.cfg = d->variant == SUPRA_ATTN_TF32X3 ? 1 : 0;
     }
-  } else if (tma_ok && scale > 0.f && d->Lq > 64 && d->ldq >= supra::kFwBoxWide && d->ldk >= supra::kFwBoxWide) {
+  } else if (tma_ok && scale > 0.f && (d->Lq > 64 || q.bias) && d->ldq >= supra::kFwBoxWide &&
+             d->ldk >= supra::kFwBoxWide) {
     // persistent FP32 kernel (with or without a bias): its Q/K boxes are kFwBoxWide columns wide
     q.path = PATH_FP32_TMA;
     q.cfg = 0;
