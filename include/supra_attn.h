@@ -54,8 +54,12 @@ extern "C" {
 
 /* ---- numeric variants -------------------------------------------------------------------- */
 #define SUPRA_ATTN_FP32 0 /* FFMA kernel, fp32 throughout: matches torch CPU fp32 to <=1e-5 */
-#define SUPRA_ATTN_TF32 1 /* tcgen05 tensor-core kernel with TF32 operands, fp32 accumulate */
-/* tcgen05 kernel with every operand split x = hi + lo (hi = TF32(x), lo = x - hi) and each
+/* tcgen05 tensor-core kernel with TF32 operands, fp32 accumulate. Covers head dim 64 with
+ * whole-row, 16-byte aligned buffers (fused kernel, with or without a bias), and head dims above
+ * 128 without a bias and with Lk >= 32 (Q K^T and P V on the tensor-core linear, the row softmax
+ * between them); other requests run the FP32 kernels. */
+#define SUPRA_ATTN_TF32 1
+/* tcgen05 kernels with every operand split x = hi + lo (hi = TF32(x), lo = x - hi) and each
  * product formed as lo*hi + hi*lo + hi*hi ("3xTF32"): fp32-class accuracy on the tensor cores.
  * Same coverage as SUPRA_ATTN_TF32; other requests run the FP32 kernels. */
 #define SUPRA_ATTN_TF32X3 2
@@ -162,8 +166,10 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  * bias: N floats or NULL; y: M rows of N floats, row stride ldy >= N, first row at y_off. All
  * counts in floats. SUPRA_ATTN_FP32: fp32 FFMA. SUPRA_ATTN_TF32 / SUPRA_ATTN_TF32X3 with K >= 32: on
  * the tensor cores, TF32 products or the split form (three TF32 products per product, held to the
- * FP32 tolerance); x (normalised when asked) and w are first copied as hi / lo parts into a
- * context-owned buffer. Shallower products run the FFMA kernel.
+ * FP32 tolerance); operands are read through tensor maps, in place for the TF32 products when
+ * 16-byte aligned with row strides of a multiple of 4 floats, else (and always for the split
+ * form) first copied as hi / lo parts, x normalised when asked, into a context-owned buffer.
+ * Shallower products run the FFMA kernel.
  * Two optional fusions (the VAE mid-block attention, app/models/vae.js:77-94):
  *   - gn != NULL: x is GroupNorm-ed on the way in (ops.groupnorm, app/gpu/ops.js:82-92,
  *     app/gpu/kernels.js:117-162): x rows form images of gn->rows_per_image rows; per image and
