@@ -27,7 +27,7 @@ __device__ __forceinline__ int find_unit(const int32_t* begin, int n, int t) { r
 // ------------------------------------------------------------------------------------------------
 // S[r][c] = scale * sum_d Q[row0 + r][d] K[c][d] (+ bias[h][row0 + r][c])
 template <bool BIAS, bool ALIGNED>
-__global__ void __launch_bounds__(kGT) gemm_qk_kernel(const GemmLaunch L) {
+__global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
   __shared__ __align__(16) float As[2][kBM * kAS];
   __shared__ __align__(16) float Bs[2][kBN * kAS];
   const int t = blockIdx.x;

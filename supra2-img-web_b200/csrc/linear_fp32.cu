@@ -6,7 +6,8 @@
 // threads, each thread an 8x8 register block (rows rg + 16i, columns cg + 16j), x and W both
 // read along K (W is [N, K] row-major, the reference's weight layout) and staged 16 deep through
 // double-buffered padded shared memory by cp.async, zero-filled past every edge. FFMA only, fp32
-// throughout. Within a problem the row tiles are outer and the column tiles inner, so CTAs that
+// throughout. Two CTAs per SM (128 registers per thread): with the compiler's 242 registers one
+// CTA, 2 warps per scheduler, left the FMA pipe waiting (K/V preparation 75.9 -> 67.7 ms). Within a problem the row tiles are outer and the column tiles inner, so CTAs that
 // run together share x rows and sweep W, which stays in L2 (the 14 stacked kv weights are
 // 37 MB).
 // Optional fusions: GroupNorm of x applied to each staged x tile in shared memory before it is
@@ -25,7 +26,7 @@ constexpr int kBK = 16;   // reduction depth per stage
 constexpr int kS = kBK + 4;  // row stride of the stage buffers (conflict-free float4 reads)
 
 template <bool BIAS, bool ALIGNED>
-__global__ void __launch_bounds__(kT) linear_fp32_kernel(const LinLaunch L) {
+__global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
   __shared__ __align__(16) float As[2][kBM * kS];
   __shared__ __align__(16) float Bs[2][kBN * kS];
   const int t = blockIdx.x;
