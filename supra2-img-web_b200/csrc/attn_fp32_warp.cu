@@ -293,15 +293,16 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
 
       // ---- S = Q K^T
       float sc[kRI][4];
-      if (!active) {
-      } else if (nk == kNK) {
-        qk_block<4>(Q4, K4, sc);
-      } else {
-        const int nj = (nk + 7) >> 3;
-        if (nj == 1) qk_block<1>(Q4, K4, sc);
-        else if (nj == 2) qk_block<2>(Q4, K4, sc);
-        else if (nj == 3) qk_block<3>(Q4, K4, sc);
-        else qk_block<4>(Q4, K4, sc);
+      if (active) {
+        if (nk == kNK) {
+          qk_block<4>(Q4, K4, sc);
+        } else {
+          const int nj = (nk + 7) >> 3;
+          if (nj == 1) qk_block<1>(Q4, K4, sc);
+          else if (nj == 2) qk_block<2>(Q4, K4, sc);
+          else if (nj == 3) qk_block<3>(Q4, K4, sc);
+          else qk_block<4>(Q4, K4, sc);
+        }
       }
       if (j == nblk - 1 && tn < L.total) {  // this warp's Q rows are done: fetch its next ones
         __syncwarp();
