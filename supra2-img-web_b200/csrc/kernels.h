@@ -210,7 +210,8 @@ struct LinTcLaunch {
 cudaError_t launch_linear_tc(const LinTcLaunch& L, bool split, cudaStream_t s);
 constexpr int kSplitTileRows = 32, kSplitTileCols = 128;  // launch_split's tile
 // One split job: rows x K floats of src (row stride ld; with trans read as [K, rows], element
-// (r, k) at src[k * ld + r]) -> hi (and lo when non-null), dense with row stride ldd. Every value
+// (r, k) at src[k * ld + r]) -> hi and lo, each written when non-null (an operand read in place
+// as its own TF32 part needs only lo), dense with row stride ldd. Every value
 // is multiplied by xscale, then by rowscale[r] when rowscale is set (w rows times a gate; then
 // bias_out[r] = bias_in[r] * rowscale[r] too when bias_out is set), then normalised when gn_stats
 // is set (LinProb's GroupNorm / LayerNorm fields of x rows). trans excludes rowscale and gn_stats.

@@ -423,7 +423,7 @@ constexpr int kSplitRows = kSplitTileRows, kSplitCols = kSplitTileCols;
 
 __device__ __forceinline__ void split_store(const SplitJob& J, int32_t r, int32_t k, float x) {
   const float h = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
-  J.hi[(int64_t)r * J.ldd + k] = h;
+  if (J.hi) J.hi[(int64_t)r * J.ldd + k] = h;
   if (J.lo) J.lo[(int64_t)r * J.ldd + k] = x - h;
 }
 

@@ -1277,28 +1277,31 @@ int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, doubl
   // of gate * w, far inside the FP32 bar). Such a w is split per gate, with a gated bias copy.
   std::vector<char> fold((size_t)n, 0);
   for (int i = 0; i < n; ++i) fold[i] = lp[i].gate != nullptr && lp[i].act == supra::kActNone;
-  // Operands read in place: the TF32 form takes a 16-byte aligned fp32 operand with a row stride
-  // of a multiple of 4 floats as it is (the tensor core ignores the 13 low mantissa bits), unless
-  // it must be normalised, scaled, gated or transposed first. Everything else is split into
-  // lin_split (x per job; w once per distinct (w, shape, gate) in the flush).
-  std::vector<char> xin((size_t)n, 0), win((size_t)n, 0), wfirst((size_t)n, 0);
+  // Operands read in place: a 16-byte aligned fp32 operand with a row stride of a multiple of 4
+  // floats, not to be normalised, scaled, gated or transposed first, is its own TF32 part (the
+  // tensor core ignores the 13 low mantissa bits): the TF32 form reads it as it is and the split
+  // form copies only its remainder x - hi. Every other operand is copied whole (hi, and lo in the
+  // split form) into lin_split: x per job, w once per distinct (w, shape, gate) in the flush.
+  // x: 0 = given split by the caller (TcJob::xh), 1 = in place, 2 = copied; w: 1 or 2.
+  std::vector<char> xmode((size_t)n, 2), wmode((size_t)n, 2), wfirst((size_t)n, 0);
   std::vector<size_t> xoff((size_t)n, 0), woff((size_t)n, 0), boff((size_t)n, 0);
   size_t need = 0;
   for (int i = 0; i < n; ++i) {
     const size_t kp = (size_t)((lp[i].K + 3) & ~3);
-    xin[i] = jobs[i].xh != nullptr ||
-             (!split && !lp[i].gn_stats && jobs[i].xscale == 1.f && aligned16(lp[i].x) && (lp[i].ldx & 3) == 0);
-    win[i] = !split && !fold[i] && !jobs[i].wtrans && aligned16(lp[i].w) && (lp[i].ldw & 3) == 0;
-    if (!xin[i]) {
-      xoff[i] = need;
-      need += parts * (size_t)lp[i].M * kp;
-    }
-    if (win[i]) continue;
+    if (jobs[i].xh) xmode[i] = 0;
+    else if (!lp[i].gn_stats && jobs[i].xscale == 1.f && aligned16(lp[i].x) && (lp[i].ldx & 3) == 0) xmode[i] = 1;
+    if (!fold[i] && !jobs[i].wtrans && aligned16(lp[i].w) && (lp[i].ldw & 3) == 0) wmode[i] = 1;
+    // floats copied per row: none (TF32 in place), the remainder (split form in place), or all
+    const size_t xparts = xmode[i] == 0 ? 0 : xmode[i] == 1 ? (split ? 1 : 0) : parts;
+    const size_t wparts = wmode[i] == 1 ? (split ? 1 : 0) : parts;
+    xoff[i] = need;
+    need += xparts * (size_t)lp[i].M * kp;
+    if (!wparts) continue;
     const float* gi = fold[i] ? lp[i].gate : nullptr;
     int j = 0;
     for (; j < i; ++j)
-      if (!win[j] && lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N && lp[j].K == lp[i].K &&
-          jobs[j].wtrans == jobs[i].wtrans && (fold[j] ? lp[j].gate : nullptr) == gi &&
+      if (wmode[j] == wmode[i] && lp[j].w == lp[i].w && lp[j].ldw == lp[i].ldw && lp[j].N == lp[i].N &&
+          lp[j].K == lp[i].K && jobs[j].wtrans == jobs[i].wtrans && (fold[j] ? lp[j].gate : nullptr) == gi &&
           (!gi || lp[j].bias == lp[i].bias))
         break;
     if (j < i) {
@@ -1307,7 +1310,7 @@ int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, doubl
     } else {
       woff[i] = need;
       wfirst[i] = 1;
-      need += parts * (size_t)lp[i].N * kp;
+      need += wparts * (size_t)lp[i].N * kp;
       if (gi) {  // the gated bias, 16-byte aligned
         boff[i] = need;
         need += ((size_t)lp[i].N + 3) & ~(size_t)3;
@@ -1324,14 +1327,16 @@ int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, doubl
   std::vector<int32_t> sbegin;
   int64_t stotal = 0;
   double sbytes = 0;
-  auto add_split = [&](const float* src, int64_t ld, int32_t rows, int32_t K, float* hi, bool trans, float xscale,
-                       const supra::LinProb* norm, const float* rowscale, const float* bias_in, float* bias_out) {
+  // a copy job: hi and lo (either may be null: remainder only, or TF32 part only)
+  auto add_split = [&](const float* src, int64_t ld, int32_t rows, int32_t K, float* hi, float* lo, bool trans,
+                       float xscale, const supra::LinProb* norm, const float* rowscale, const float* bias_in,
+                       float* bias_out) {
     supra::SplitJob J;
     std::memset(&J, 0, sizeof J);
     const int32_t kp = (K + 3) & ~3;
     J.src = src;
     J.hi = hi;
-    J.lo = split ? hi + (size_t)rows * kp : nullptr;
+    J.lo = lo;
     J.rowscale = rowscale;
     J.bias_in = bias_in;
     J.bias_out = bias_out;
@@ -1354,16 +1359,24 @@ int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, doubl
     J.ktiles = (K + supra::kSplitTileCols - 1) / supra::kSplitTileCols;
     sbegin.push_back((int32_t)stotal);
     stotal += (int64_t)((rows + supra::kSplitTileRows - 1) / supra::kSplitTileRows) * J.ktiles;
-    sbytes += 4.0 * (1.0 + (double)parts) * rows * (double)K;
+    sbytes += 4.0 * (1.0 + (hi ? 1.0 : 0.0) + (lo ? 1.0 : 0.0)) * rows * (double)K;
     sj.push_back(J);
   };
   for (int i = 0; i < n; ++i) {
-    if (!xin[i])
-      add_split(lp[i].x, lp[i].ldx, lp[i].M, lp[i].K, c->lin_split + xoff[i], false, jobs[i].xscale, &lp[i], nullptr,
-                nullptr, nullptr);
-    if (wfirst[i])
-      add_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, c->lin_split + woff[i], jobs[i].wtrans, 1.f, nullptr,
-                fold[i] ? lp[i].gate : nullptr, lp[i].bias, fold[i] ? c->lin_split + boff[i] : nullptr);
+    const size_t kp = (size_t)((lp[i].K + 3) & ~3);
+    float* xb = c->lin_split + xoff[i];
+    if (xmode[i] == 2)
+      add_split(lp[i].x, lp[i].ldx, lp[i].M, lp[i].K, xb, split ? xb + (size_t)lp[i].M * kp : nullptr, false,
+                jobs[i].xscale, &lp[i], nullptr, nullptr, nullptr);
+    else if (xmode[i] == 1 && split)
+      add_split(lp[i].x, lp[i].ldx, lp[i].M, lp[i].K, nullptr, xb, false, 1.f, nullptr, nullptr, nullptr, nullptr);
+    if (!wfirst[i]) continue;
+    float* wb = c->lin_split + woff[i];
+    if (wmode[i] == 2)
+      add_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, wb, split ? wb + (size_t)lp[i].N * kp : nullptr, jobs[i].wtrans,
+                1.f, nullptr, fold[i] ? lp[i].gate : nullptr, lp[i].bias, fold[i] ? c->lin_split + boff[i] : nullptr);
+    else
+      add_split(lp[i].w, lp[i].ldw, lp[i].N, lp[i].K, nullptr, wb, false, 1.f, nullptr, nullptr, nullptr, nullptr);
   }
   if (stotal > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many split tiles in one flush");
   sbegin.push_back((int32_t)stotal);
@@ -1401,22 +1414,24 @@ int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, doubl
     }
     const int64_t kp = (lp[i].K + 3) & ~3;
     const int64_t M = lp[i].M, N = lp[i].N, K = lp[i].K;
-    if (jobs[i].xh) {
+    const float* xb = c->lin_split + xoff[i];
+    const float* wb = c->lin_split + woff[i];
+    if (xmode[i] == 0) {
       rc = map_of(jobs[i].xh, jobs[i].ldxs, M, K, &t.mxh);
       if (!rc && split) rc = map_of(jobs[i].xl, jobs[i].ldxs, M, K, &t.mxl);
-    } else if (xin[i]) {
+    } else if (xmode[i] == 1) {
       rc = map_of(lp[i].x, lp[i].ldx, M, K, &t.mxh);
+      if (!rc && split) rc = map_of(xb, kp, M, K, &t.mxl);
     } else {
-      const float* xh = c->lin_split + xoff[i];
-      rc = map_of(xh, kp, M, K, &t.mxh);
-      if (!rc && split) rc = map_of(xh + (size_t)M * kp, kp, M, K, &t.mxl);
+      rc = map_of(xb, kp, M, K, &t.mxh);
+      if (!rc && split) rc = map_of(xb + (size_t)M * kp, kp, M, K, &t.mxl);
     }
-    if (!rc && win[i]) {
+    if (!rc && wmode[i] == 1) {
       rc = map_of(lp[i].w, lp[i].ldw, N, K, &t.mwh);
+      if (!rc && split) rc = map_of(wb, kp, N, K, &t.mwl);
     } else if (!rc) {
-      const float* wh = c->lin_split + woff[i];
-      rc = map_of(wh, kp, N, K, &t.mwh);
-      if (!rc && split) rc = map_of(wh + (size_t)N * kp, kp, N, K, &t.mwl);
+      rc = map_of(wb, kp, N, K, &t.mwh);
+      if (!rc && split) rc = map_of(wb + (size_t)N * kp, kp, N, K, &t.mwl);
     }
     // y through TMA stores (32 x 32 boxes) when its rows are 16-byte aligned and N is a multiple
     // of 4 columns; else per-row stores. (A store box clipped at an inner extent that ends inside a
