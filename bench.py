@@ -793,37 +793,85 @@ def main():
         up, down = supra_attn.lib.supra_attn_upload, supra_attn.lib.supra_attn_download
         comp = torch.cuda.current_stream()
 
+        # The first step's inputs and the last step's output cannot hide behind other steps: those
+        # two steps run in CH sequence chunks, each chunk's compute waiting only for its own upload
+        # and each chunk's read-back starting once it is computed. The steps between them run whole.
+        CH = 4
+        cb = [S * c // CH for c in range(CH + 1)]
+        dsz = supra_attn._lib.C.sizeof(supra_attn.Desc)
+
+        def sub(arr, a, b):  # descriptors a .. b-1 of a descriptor array (no copy)
+            return (supra_attn.Desc * (b - a)).from_buffer(arr, a * dsz)
+
+        chunk_descs = []  # [set][chunk] -> (self descs, [cross descs per block])
+        for q_s, x_s, o_s, sd_s, cd_s in sets:
+            chunk_descs.append([(sub(sd_s, cb[c], cb[c + 1]), [sub(cd_s[b], cb[c], cb[c + 1]) for b in range(BLOCKS)])
+                                for c in range(CH)])
+        q_row, x_row = TOKENS * 3 * DIM, TOKENS * DIM  # floats per sequence in qkv / qx / out
+
         def run_e2e(nsteps):
             """Uploads, steps and read-backs of `nsteps` steps, pipelined over the two sets."""
-            computed = [None, None]
-            arrived = [None, None]
+            computed = [None, None]  # the last event of the step that read each set
+            arrived = [None, None]   # per set: the upload event of each chunk
+            done_chunks = [None, None]
 
             def upload(s):
                 q_s, x_s = sets[s % 2][0], sets[s % 2][1]
                 if computed[s % 2] is not None:  # step s-2 read this set
                     up_stream.wait_event(computed[s % 2])
-                supra_attn._lib.check(up(up_gpu.ctx, q_s.data_ptr(), h_qkv.data_ptr(), q_s.numel()), up_gpu.ctx)
-                supra_attn._lib.check(up(up_gpu.ctx, x_s.data_ptr(), h_qx.data_ptr(), x_s.numel()), up_gpu.ctx)
-                ev = torch.cuda.Event()
-                ev.record(up_stream)
-                arrived[s % 2] = ev
+                evs = []
+                for c in range(CH):
+                    a, b = cb[c], cb[c + 1]
+                    supra_attn._lib.check(up(up_gpu.ctx, q_s.data_ptr() + 4 * a * q_row, h_qkv.data_ptr() + 4 * a * q_row,
+                                             (b - a) * q_row), up_gpu.ctx)
+                    supra_attn._lib.check(up(up_gpu.ctx, x_s.data_ptr() + 4 * a * x_row, h_qx.data_ptr() + 4 * a * x_row,
+                                             (b - a) * x_row), up_gpu.ctx)
+                    ev = torch.cuda.Event()
+                    ev.record(up_stream)
+                    evs.append(ev)
+                arrived[s % 2] = evs
+
+            def compute(s, chunked):
+                _, _, o_s, sd_s, cd_s = sets[s % 2]
+                evs = []
+                if chunked:
+                    for c in range(CH):
+                        comp.wait_event(arrived[s % 2][c])
+                        sd_c, cd_c = chunk_descs[s % 2][c]
+                        for b in range(BLOCKS):
+                            gpu.enqueue_batch(sd_c)
+                            gpu.flush()
+                            gpu.enqueue_batch(cd_c[b])
+                            gpu.flush()
+                        ev = torch.cuda.Event()
+                        ev.record(comp)
+                        evs.append(ev)
+                    gather_step(o_s)
+                else:
+                    comp.wait_event(arrived[s % 2][-1])
+                    step(sd_s, cd_s, o_s)
+                    ev = torch.cuda.Event()
+                    ev.record(comp)
+                    evs = [ev] * CH
+                computed[s % 2] = evs[-1]
+                done_chunks[s % 2] = evs
+
+            def readback(s):  # blocks the host until the copies are issued
+                o_p = sets[s % 2][2]
+                for c in range(CH):
+                    a, b = cb[c], cb[c + 1]
+                    down_stream.wait_event(done_chunks[s % 2][c])
+                    supra_attn._lib.check(down(down_gpu.ctx, h_out.data_ptr() + 4 * a * x_row,
+                                               o_p.data_ptr() + 4 * a * x_row, (b - a) * x_row), down_gpu.ctx)
 
             upload(0)
             for s in range(nsteps + 1):
                 if s + 1 < nsteps:  # issued before step s is recorded: it lands while step s computes
                     upload(s + 1)
                 if s < nsteps:
-                    _, _, o_s, sd_s, cd_s = sets[s % 2]
-                    comp.wait_event(arrived[s % 2])
-                    step(sd_s, cd_s, o_s)
-                    done = torch.cuda.Event()
-                    done.record(comp)
-                    computed[s % 2] = done
-                if s > 0:  # read back step s-1 while step s computes (blocks the host)
-                    o_p = sets[(s - 1) % 2][2]
-                    down_stream.wait_event(computed[(s - 1) % 2])
-                    supra_attn._lib.check(down(down_gpu.ctx, h_out.data_ptr(), o_p.data_ptr(), o_p.numel()),
-                                          down_gpu.ctx)
+                    compute(s, chunked=(s == 0 or s == nsteps - 1))
+                if s > 0:  # read back step s-1 while step s computes
+                    readback(s - 1)
             comp.wait_stream(down_stream)
 
         run_e2e(2)
@@ -850,7 +898,8 @@ def main():
                "h2d_bytes_per_step": 4 * (qkv.numel() + qx.numel()) * world,
                "d2h_bytes_per_step": 4 * out_cross.numel() * world,
                "ms_per_step": float(t2.item()) / args.steps,
-               "pipeline": "inputs and outputs double-buffered; uploads, compute and read-backs on three streams"}
+               "pipeline": ("inputs and outputs double-buffered; uploads, compute and read-backs on three streams; "
+                            "the first and last steps in 4 sequence chunks")}
         up_gpu.close()
         down_gpu.close()
         del qkv2, qx2, oc2
