@@ -265,18 +265,21 @@ SUPRA_ATTN_API int supra_attn_launch_count(const supra_attn_ctx* ctx, int64_t* n
  * Runs ONE problem (validated exactly as supra_attn_enqueue validates it, any head dim) on
  * `cuda_stream` through the score-materialising kernels (QK^T GEMM, row softmax, PV GEMM),
  * without a context and without any allocation: the score scratch is a 16 MiB array of static
- * device memory inside the library, used chunk by chunk, and the per-call descriptors sit in a
- * second static array of about 123 KB. Every GPU on which the library's kernels are loaded
- * holds both until the process exits. Limit: one row of scores must fit the scratch,
- * i.e. Lk <= 4,194,304; larger Lk is rejected with SUPRA_ATTN_EINVAL and a message.
+ * device memory inside the library, used chunk by chunk, and the chunk's unit table sits in a
+ * second static array of about 62 KB, written on the device by a small kernel from values passed
+ * as kernel arguments (no host buffer is read after the call returns). Every GPU on which the
+ * library's kernels are loaded holds both until the process exits. Limit: one row of scores
+ * must fit the scratch, i.e. Lk <= 4,194,304; larger Lk is rejected with SUPRA_ATTN_EINVAL and a
+ * message. The arithmetic is always FP32 FFMA, whatever desc->variant asks for: a TF32 or
+ * TF32X3 request gets the FP32 result, which lies inside their tolerances.
  *
  * The caller passes inputs and outputs as for supra_attn_enqueue. The work is enqueued on
  * cuda_stream and the call returns without waiting for it. The first call on each device looks
  * up the arrays' device addresses (cudaGetSymbolAddress) with that device current; make that
  * first call before any stream capture. All calls share the two arrays, which keep the last
- * call's contents: every call writes each score it reads before reading it, so nothing needs
- * to start at zero. Calls that overlap on the GPU (different streams, or different host
- * threads on one device) race on the arrays; serialise them, e.g. on one stream.
+ * call's contents: every call writes each score and unit entry it reads before reading it, so
+ * nothing needs to start at zero. Calls that overlap on the GPU (different streams, or different
+ * host threads on one device) race on the arrays; serialise them, e.g. on one stream.
  * msg (cap bytes, may be NULL) receives the message of a failure. */
 SUPRA_ATTN_API int supra_attn_attention_noalloc(const supra_attn_desc* desc, void* cuda_stream, char* msg,
                                                 int32_t cap);
