@@ -162,87 +162,136 @@ def measured_peaks():
 
 
 # ---------------------------------------------------------------------------------------------
-def cpu_port_rate(seq_sample: int, seconds: float, seed: int, lengths):
-    """tools/reference.py:72-79 restated (oracle.sdpa_port) on all host cores over a bounded
-    sample: `seq_sample` sequences through one block (self + ragged cross attention), repeated
-    until `seconds` have passed. Returns (sequence-attentions/s, threads, sample text)."""
-    import torch
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            return next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), "")
+    except OSError:
+        return ""
 
-    import oracle
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(seed)
-    n = seq_sample
-    qkv = torch.randn(n, TOKENS, 3 * DIM, generator=g)
-    qx = torch.randn(n, TOKENS, DIM, generator=g)
-    kvs = [torch.randn(1, lengths[i], 2 * DIM, generator=g) for i in range(n)]
-    v3 = qkv.view(n, TOKENS, 3, DIM)
+def workload_config(args, world: int) -> dict:
+    """The configs[4] workload both arms report (the reference arm runs the same config on the CPU)."""
+    return {"workload": f"supradit_attention_step (configs[4]): {args.prompts} prompts x CFG = {2 * args.prompts} "
+                        "seqs, 14 blocks x (self 256x256 + cross 256xL, L~U{1..128}), 9x64 heads",
+            "prompts": args.prompts, "global_batch": 2 * args.prompts, "seq_len": TOKENS,
+            "parallelism": f"prompt-sharded x{world}, outputs gathered to rank 0",
+            "l2": "inputs larger than L2 (qkv 3.6 GB, K/V 8.5 GB per step at N=1)"}
 
-    def one():
-        for b in range(0, n, 2):  # CFG pairs run together as in tools/reference.py:173
-            oracle.sdpa_port(v3[b:b + 2, :, 0], v3[b:b + 2, :, 1], v3[b:b + 2, :, 2], N_HEADS)
-        for i in range(n):  # each sequence at its true length (app/models/dit.js:184)
-            oracle.sdpa_port(qx[i:i + 1], kvs[i][:, :, :DIM], kvs[i][:, :, DIM:], N_HEADS)
 
-    one()
-    reps, t0 = 0, time.perf_counter()
+class CpuStep:
+    """One configs[4] step on the host cores through the port of tools/reference.py's CPU attention
+    (oracle.sdpa_port, tools/reference.py:72-79), torch fp32 on all host threads: per block,
+    self-attention per CFG pair (the reference runs cond and uncond as one batch of 2,
+    tools/reference.py:173) and cross-attention per sequence at its true length L
+    (app/models/dit.js:184). Every one of the step's 2 x 14 x n sequence-attentions runs.
+
+    Inputs are built once from a seeded pool: sequence i reads Q/K/V rows of pool entry
+    i % pool (256 sequences, 0.6 GB, larger than the host's last-level cache) and its K/V from a
+    pool of 32768 rows at a running offset; one K/V pool serves all 14 blocks. The pools tile 8 M
+    seeded N(0,1) values; the values do not change the CPU cost of an attention call."""
+
+    POOL, KV_ROWS = 256, 32768
+
+    def __init__(self, lengths, seed: int):
+        import torch
+
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        g = torch.Generator().manual_seed(seed)
+        self.n = len(lengths)
+        self.lengths = list(lengths)
+        pool = min(self.POOL, self.n)
+        base = torch.randn(1 << 23, generator=g)  # seeded N(0,1) values, tiled into the pool
+
+        def fill(*shape):
+            n = math.prod(shape)
+            return base.repeat((n + base.numel() - 1) // base.numel())[:n].view(*shape)
+
+        self.qkv = fill(pool, TOKENS, 3, DIM)
+        self.qx = fill(pool, TOKENS, DIM)
+        self.kv = fill(self.KV_ROWS, 2 * DIM)
+        self.kv_off, off = [], 0
+        for L in self.lengths:
+            if off + L > self.KV_ROWS:
+                off = 0
+            self.kv_off.append(off)
+            off += L
+
+    def block(self):
+        import oracle
+
+        pool = self.qkv.shape[0]
+        for b in range(0, self.n, 2):  # a CFG pair is two consecutive sequences
+            p = self.qkv[b % pool:b % pool + 2]
+            oracle.sdpa_port(p[:, :, 0], p[:, :, 1], p[:, :, 2], N_HEADS)
+        for i in range(self.n):
+            kv = self.kv[self.kv_off[i]:self.kv_off[i] + self.lengths[i]][None]
+            oracle.sdpa_port(self.qx[i % pool:i % pool + 1], kv[:, :, :DIM], kv[:, :, DIM:], N_HEADS)
+
+    def step(self):
+        for _ in range(BLOCKS):
+            self.block()
+
+    def seq_calls(self) -> int:
+        return 2 * BLOCKS * self.n
+
+    def describe(self, steps: int, seconds: float) -> str:
+        return (f"{steps} whole configs[4] step(s): {self.n} sequences x {BLOCKS} blocks x (self 256x256 per CFG "
+                f"pair + cross 256xL at each sequence's true L) = {self.seq_calls()} sequence-attentions per step, "
+                f"torch CPU fp32 SDPA (tools/reference.py:72-79 port), {self.threads} threads, {seconds:.1f} s; "
+                f"CPU: {cpu_model()}")
+
+
+def cpu_baseline_leg(lengths, seed: int, seconds: float):
+    """The cpu_baseline of the GPU arm: CpuStep after a one-block warm-up, whole steps until
+    `seconds` have passed (at least one). The reference arm times the same steps the same way."""
+    cpu = CpuStep(lengths, seed)
+    cpu.block()
+    steps, t0 = 0, time.perf_counter()
     while True:
-        one()
-        reps += 1
+        cpu.step()
+        steps += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    rate = reps * 2 * n / el
-    cpu = ""
-    try:
-        with open("/proc/cpuinfo") as f:
-            cpu = next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), "")
-    except OSError:
-        pass
-    sample = (f"{n} sequences x 1 block (self 256x256 + cross 256xL, L~U{{1..128}}), 9x64 heads, "
-              f"torch CPU fp32 SDPA, {reps} repetitions in {el:.1f} s; CPU: {cpu}")
-    return rate, threads, sample
+    rate = steps * cpu.seq_calls() / el
+    return {"value": rate, "unit": UNIT, "cores": cpu.threads, "kind": "port", "ms_per_step": el / steps * 1e3,
+            "sample": cpu.describe(steps, el)}
 
 
 def run_reference(args, rank, world):
-    """`--impl reference`: the reference's CPU attention (oracle port of tools/reference.py:72-79)
-    on this host's cores, rank 0 only; each step is a bounded sample of the same workload."""
+    """`--impl reference`: the reference's CPU attention (the port of tools/reference.py:72-79,
+    oracle.sdpa_port) on this host's cores, rank 0 only. Every step is the whole configs[4] step
+    (CpuStep): W untimed warm-up steps, then K steps, each timed with the host clock."""
     if rank != 0:
         return
-    import torch
-
     lengths = workload_lengths(args.prompts, args.seed)
-    n = 32
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu = CpuStep(lengths, args.seed)
     for _ in range(args.warmup):
-        cpu_port_rate(n, 0.0, args.seed, lengths)
-    rates = []
-    t0 = time.perf_counter()
-    sample = ""
-    threads = os.cpu_count() or 1
+        cpu.step()
+    times = []
     for _ in range(args.steps):
-        r, threads, sample = cpu_port_rate(n, 0.0, args.seed, lengths)
-        rates.append(r)
-    el = time.perf_counter() - t0
-    value = statistics.median(rates)
-    per_step = 2048 * BLOCKS * 2
+        t0 = time.perf_counter()
+        cpu.step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps * cpu.seq_calls() / total
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_step / value * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "supradit_attention_step (configs[4]): 2048 seqs x 14 blocks x (self 256 + cross L~U{1..128})",
-                   "prompts": args.prompts, "global_batch": 2 * args.prompts, "seq_len": TOKENS,
-                   "parallelism": f"cpu x{threads} threads", "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, L~U{1..128})", "impl": "reference",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.threads, "kind": "port",
+                         "sample": cpu.describe(args.steps, total)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": el,
+        "step_s": {"min": min(times), "median": statistics.median(times), "max": max(times)},
     }
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------------------------
-def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
+def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu_reps: int = 3):
     """BASELINE.json configs[0..3] as extra figures: DiT self (B=2), DiT cross (128 ragged
     sequences), T5 (256 prompts, ragged L, bias), VAE mid-block (1, 8, 64 images). Each rep is one
     flush of the call site's calls, timed with CUDA events after the L2 is flushed; FP32 and TF32
@@ -259,8 +308,28 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
     out = {}
     want = lambda name: only is None or name in only
 
-    def run(name, units, unit_name, make_descs, flops, bytes_):
+    tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0  # TF32 dense peak: half of measured bf16
+
+    def run(name, units, unit_name, make_descs, flops, bytes_, cpu=None, out_fn=None):
+        """Times the call site's flush for each variant; with `cpu` (runs the site's calls through
+        the torch CPU port on all host cores and returns the flat output) also times that, and
+        compares each variant's output (`out_fn`) with it."""
+        import oracle
+
         res = {}
+        ref = None
+        if cpu is not None and cpu_reps > 0:
+            import torch as _t
+
+            cpu()  # warm-up
+            ts = []
+            for _ in range(cpu_reps):
+                t0 = time.perf_counter()
+                ref = cpu()
+                ts.append(time.perf_counter() - t0)
+            cms = statistics.median(ts) * 1e3
+            res["cpu"] = {"ms": cms, f"{unit_name}_per_s": units / (cms / 1e3), "tflops": flops / (cms / 1e3) / 1e12,
+                          "cores": _t.get_num_threads(), "kind": "port"}
         for variant in ("fp32", "tf32", "tf32x3"):
             descs = make_descs(variant)
             gpu.enqueue_batch(descs)
@@ -284,16 +353,18 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
             per = {}
             for r in prof:
                 per[r["name"]] = per.get(r["name"], 0.0) + r["ms"] / reps
-            res[variant] = {"ms": ms, f"{unit_name}_per_s": units / (ms / 1e3),
-                            "tflops": flops / (ms / 1e3) / 1e12, "gbs": bytes_ / (ms / 1e3) / 1e9,
-                            "frac_fp32_peak": flops / (ms / 1e3) / 1e12 / fp32_peak,
-                            "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
-                            "kernels": sorted(per),
-                            "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
-            if variant != "fp32" and any(k.startswith(("linear_tc", "attn_tf32")) for k in per):
-                # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
-                res[variant]["frac_tf32_peak"] = ((3 if variant == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 /
-                                                  (float(peaks.get("bf16_tflops", 1590.0)) / 2.0))
+            tensor = any(k.startswith(("linear_tc", "attn_tf32")) for k in per)
+            e = {"ms": ms, f"{unit_name}_per_s": units / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                 "gbs": bytes_ / (ms / 1e3) / 1e9, "frac_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm,
+                 "kernels": sorted(per), "ms_per_kernel": {k: round(v, 4) for k, v in sorted(per.items())}}
+            if tensor:  # issued TF32 MMA work (3 products per product in the split form) against the TF32 peak
+                e["frac_tf32_peak"] = (3 if variant == "tf32x3" else 1) * flops / (ms / 1e3) / 1e12 / tf_peak
+            else:  # the FFMA kernels ran (an FP32 request, or a tensor request they cover instead)
+                e["frac_fp32_peak"] = flops / (ms / 1e3) / 1e12 / fp32_peak
+            if ref is not None and out_fn is not None:
+                got = out_fn()
+                e["parity_vs_cpu"] = {"max_rel": oracle.max_rel(got, ref), "rel_l2": oracle.rel_l2(got, ref)}
+            res[variant] = e
         out[name] = res
 
     enq = supra_attn.lib.supra_attn_enqueue_linear
@@ -344,7 +415,14 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
             return arr
 
         f1 = 2 * 4.0 * 256 * 256 * 64 * 9
-        run("dit_self_b2", 2, "seq", c1, f1, 2 * 4.0 * (2 * 256 * 576 + 2 * 256 * 576))
+        qkv_c = qkv.cpu().view(2, 256, 3, 576)
+
+        def cpu1():  # tools/reference.py:72-79 on the CFG pair, as tools/reference.py:173 runs it
+            import oracle
+            return oracle.sdpa_port(qkv_c[:, :, 0], qkv_c[:, :, 1], qkv_c[:, :, 2], 9).reshape(-1).numpy()
+
+        run("dit_self_b2", 2, "seq", c1, f1, 2 * 4.0 * (2 * 256 * 576 + 2 * 256 * 576), cpu=cpu1,
+            out_fn=lambda: o1.cpu().numpy())
 
     if want("dit_cross_128"):
         # DiT cross-attention, 64 prompts x CFG, ragged L
@@ -361,8 +439,16 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
                                               oOff=b * 256 * 576, variant=variant)
             return arr
 
+        q2_c = q2.cpu().view(128, 256, 576)
+        kv2_c = [x.cpu().view(1, -1, 1152) for x in kv2]
+
+        def cpu2():  # one call per sequence at its true L (app/models/dit.js:184)
+            import oracle
+            return torch.cat([oracle.sdpa_port(q2_c[b:b + 1], kv2_c[b][:, :, :576], kv2_c[b][:, :, 576:], 9)
+                              for b in range(128)]).reshape(-1).numpy()
+
         run("dit_cross_128", 128, "seq", c2, sum(4.0 * 256 * L * 64 * 9 for L in Ls),
-            sum(4.0 * (2 * 256 * 576 + 2 * L * 576) for L in Ls))
+            sum(4.0 * (2 * 256 * 576 + 2 * L * 576) for L in Ls), cpu=cpu2, out_fn=lambda: o2.cpu().numpy())
 
     if want("t5_256") or want("t5_256_table"):  # (the table form reuses these inputs)
         # T5 encoder attention, 256 prompts, ragged L, relative-position bias, scale 1
@@ -384,9 +470,18 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
                                               ldq=768, ldk=768, ldv=768, scale=1.0, variant=variant)
             return arr
 
+        qs_c, ks_c, vs_c = ([x.cpu().view(-1, 768) for x in xs] for xs in (qs, ks, vs))
+        bias_c = [torch.from_numpy(gpu.read(bt)).view(12, L, L) for L, bt in zip(Lt, biases)]
+
+        def cpu3():  # transformers' T5Attention arithmetic per prompt (oracle.t5_sdpa_port)
+            import oracle
+            return torch.cat([oracle.t5_sdpa_port(qs_c[i], ks_c[i], vs_c[i], bias_c[i], 12).reshape(-1)
+                              for i in range(len(Lt))]).numpy()
+
+        out3 = lambda: torch.cat([o.reshape(-1) for o in os_]).cpu().numpy()
         if want("t5_256"):
             run("t5_256", 256, "prompt", c3, sum(4.0 * L * L * 64 * 12 for L in Lt),
-                sum(4.0 * (4 * L * 768 + 12 * L * L) for L in Lt))
+                sum(4.0 * (4 * L * 768 + 12 * L * L) for L in Lt), cpu=cpu3, out_fn=out3)
 
     if want("t5_256_table"):
         # the same T5 calls with the [32, 12] table in place of the expanded bias (the kernels form
@@ -399,7 +494,7 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
             return arr
 
         run("t5_256_table", 256, "prompt", c3t, sum(4.0 * L * L * 64 * 12 for L in Lt),
-            sum(4.0 * (4 * L * 768 + 32 * 12) for L in Lt))
+            sum(4.0 * (4 * L * 768 + 32 * 12) for L in Lt), cpu=cpu3, out_fn=out3)
 
     if want("vae"):
         # VAE mid-block single-head attention, 1024 tokens x 512 channels
@@ -417,7 +512,14 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
                                                   ldk=512, ldv=512, qOff=o, kOff=o, vOff=o, oOff=o, variant=variant)
                 return arr
 
-            run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512)
+            qc, kc, vc = (x.cpu().view(nimg, 1, 1024, 512) for x in (qv, kvv, vv))
+
+            def cpu4(nimg=nimg, qc=qc, kc=kc, vc=vc):  # the reference's attention() with one head, per image
+                import oracle
+                return torch.cat([oracle.sdpa_port(qc[i], kc[i], vc[i], 1) for i in range(nimg)]).reshape(-1).numpy()
+
+            run(f"vae_{nimg}", nimg, "image", c4, nimg * 4.0 * 1024 * 1024 * 512, nimg * 4.0 * 4 * 1024 * 512,
+                cpu=cpu4, out_fn=lambda ov=ov: ov.cpu().numpy())
             del qv, kvv, vv, ov
 
     if want("vae_block_8"):
@@ -560,6 +662,26 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None):
     return out
 
 
+def rounded(x, digits: int = 5):
+    """The JSON line's floats to `digits` significant digits (shorter lines, same information)."""
+    if isinstance(x, float):
+        return float(f"{x:.{digits}g}") if math.isfinite(x) else x
+    if isinstance(x, dict):
+        return {k: rounded(v, digits) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [rounded(v, digits) for v in x]
+    return x
+
+
+def compact_variant(v: dict) -> dict:
+    """The figures of one tensor-core variant of the step, without its kernel list."""
+    r = v.get("roofline") or {}
+    return {"value": v["value"], "ms_per_step": v["ms_per_step"], "tflops": v["tflops"],
+            "roofline": {k: r.get(k) for k in ("bound", "kernel", "achieved", "peak", "unit", "frac", "tensor_frac")},
+            "parity": {k: v["parity"][k] for k in ("max_rel", "rel_l2", "n_checked")}, "tolerance": v["tolerance"],
+            "sm_mhz": v["clocks"].get("sm_mhz"), "reasons": v["clocks"].get("reasons")}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -644,39 +766,68 @@ def main():
     for L in lengths:
         flops_total += (4.0 * TOKENS * TOKENS + 4.0 * TOKENS * L) * HEAD_DIM * N_HEADS * BLOCKS
 
-    # gather of each step's output to rank 0 (a separate stream, overlapped with the next step)
-    # (double-buffered send buffers: step s copies into buffer s%2 on the compute stream once the
-    # gather that last read that buffer has finished, then the gather stream sends it)
-    gather_stream = torch.cuda.Stream(device=dev) if world > 1 else None
+    # The only collective: after the timed steps rank 0 gathers every rank's output of the last step
+    # (NCCL gather over NVLink, one per timed run, inside the timed region and timed on its own).
+    # Prompts are independent, so nothing is exchanged between steps (app/pipeline.js:97-117 keeps
+    # each prompt's K/V with its sampler).
     shard_max = max(len(shard_prompts(lengths, world, r)) for r in range(world)) * 2 * TOKENS * DIM
-    send_bufs = [torch.empty(shard_max, device=dev) for _ in range(2)] if world > 1 else None
-    sent = [None, None]
+    send_buf = torch.empty(shard_max, device=dev) if world > 1 else None
     recv = [torch.empty(shard_max, device=dev) for _ in range(world)] if (world > 1 and rank == 0) else None
-    nstep = [0]
+    gather_ms = []
 
-    def gather_step(oc):
+    def gather_outputs(oc):
         if world == 1:
             return
-        i = nstep[0] % 2
-        nstep[0] += 1
-        cur = torch.cuda.current_stream()
-        if sent[i] is not None:
-            cur.wait_event(sent[i])
-        send_bufs[i][: oc.numel()].copy_(oc)
-        gather_stream.wait_stream(cur)
-        with torch.cuda.stream(gather_stream):
-            dist.gather(send_bufs[i], recv if rank == 0 else None, dst=0)
-            ev = torch.cuda.Event()
-            ev.record(gather_stream)
-        sent[i] = ev
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        send_buf[: oc.numel()].copy_(oc)
+        dist.gather(send_buf, recv if rank == 0 else None, dst=0)
+        g1.record()
+        gather_ms.append((g0, g1))
 
-    def step(sd=self_d, cd=cross_d, oc=out_cross):
+    def step(sd=self_d, cd=cross_d):
         for b in range(BLOCKS):
             gpu.enqueue_batch(sd)
             gpu.flush()
             gpu.enqueue_batch(cd[b])
             gpu.flush()
-        gather_step(oc)
+
+    # ---- the checker: a sample of the step's outputs against the float64 oracle (outside the
+    # timed regions). One sequence per L-bucket of 16 on each rank; the self-attention output of
+    # the last block and its cross-attention output (block 13's K/V). ---------------------------------
+    picks = []
+    for lo in range(1, 129, 16):
+        i = next((j for j, L in enumerate(Ls) if lo <= L < lo + 16 and j not in picks), None)
+        if i is not None:
+            picks.append(i)
+
+    def check_step(oself, ocross, qkv_t=qkv, qx_t=qx):
+        import numpy as np
+
+        import oracle
+
+        worst = [0.0, 0.0]
+        kvl = kv[BLOCKS - 1]
+        for i in picks:
+            qr = qkv_t[i * TOKENS * 3 * DIM:(i + 1) * TOKENS * 3 * DIM].view(TOKENS, 3 * DIM).cpu().numpy()
+            ref_s = oracle.attention_heads(qr[:, :DIM], qr[:, DIM:2 * DIM], qr[:, 2 * DIM:], N_HEADS)
+            got_s = oself[i * TOKENS * DIM:(i + 1) * TOKENS * DIM].cpu().numpy()
+            xr = qx_t[i * TOKENS * DIM:(i + 1) * TOKENS * DIM].view(TOKENS, DIM).cpu().numpy()
+            kr = kvl[kv_off[i]:kv_off[i + 1]].view(-1, 2 * DIM).cpu().numpy()
+            ref_c = oracle.attention_heads(xr, kr[:, :DIM], kr[:, DIM:], N_HEADS)
+            got_c = ocross[i * TOKENS * DIM:(i + 1) * TOKENS * DIM].cpu().numpy()
+            for got, ref in ((got_s, ref_s), (got_c, ref_c)):
+                worst[0] = max(worst[0], oracle.max_rel(got, ref))
+                worst[1] = max(worst[1], oracle.rel_l2(got, ref))
+        t = torch.tensor(worst + [2.0 * len(picks)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t[:2], op=dist.ReduceOp.MAX)
+            n = t[2:].clone()
+            dist.all_reduce(n)
+            t[2:] = n
+        return {"max_rel": float(t[0]), "rel_l2": float(t[1]), "n_checked": int(t[2]),
+                "what": "per rank one sequence per L-bucket of 16: the last block's self- and cross-attention "
+                        "output vs the float64 oracle"}
 
     def barrier():
         if world > 1:
@@ -684,9 +835,8 @@ def main():
 
     for _ in range(args.warmup):
         step()
+    gather_outputs(out_cross)
     torch.cuda.synchronize()
-    if gather_stream is not None:
-        gather_stream.synchronize()
 
     # ---- timed region (device time, max over ranks) ---------------------------------------------
     uuid = None
@@ -708,8 +858,7 @@ def main():
     ev0.record()
     for _ in range(args.steps):
         step()
-    if gather_stream is not None:
-        torch.cuda.current_stream().wait_stream(gather_stream)
+    gather_outputs(out_cross)
     ev1.record()
     torch.cuda.synchronize()
     clocks.mark_end()
@@ -717,6 +866,14 @@ def main():
     clk = clocks.stop()
     barrier()
     ms = ev0.elapsed_time(ev1)
+    gather = None
+    if world > 1:
+        gt = torch.tensor([gather_ms[-1][0].elapsed_time(gather_ms[-1][1])], device=dev)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        gather = {"ms": float(gt.item()), "bytes_to_rank0": 4 * TOKENS * DIM * 2 * args.prompts * (world - 1) // world,
+                  "what": "NCCL gather of the last step's cross-attention output to rank 0, once per timed run, "
+                          "inside the timed region"}
+    parity = check_step(out_self, out_cross)
     launches = gpu.launch_count() - launches0
     prof = gpu.profile_report()
     gpu.profile(False)
@@ -846,10 +1003,9 @@ def main():
                         ev = torch.cuda.Event()
                         ev.record(comp)
                         evs.append(ev)
-                    gather_step(o_s)
                 else:
                     comp.wait_event(arrived[s % 2][-1])
-                    step(sd_s, cd_s, o_s)
+                    step(sd_s, cd_s)
                     ev = torch.cuda.Event()
                     ev.record(comp)
                     evs = [ev] * CH
@@ -876,8 +1032,6 @@ def main():
 
         run_e2e(2)
         torch.cuda.synchronize()
-        if gather_stream is not None:
-            gather_stream.synchronize()
         barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -886,8 +1040,7 @@ def main():
         up_stream.wait_event(e0)
         down_stream.wait_event(e0)
         run_e2e(args.steps)
-        if gather_stream is not None:
-            comp.wait_stream(gather_stream)
+        gather_outputs(sets[(args.steps - 1) % 2][2])
         e1.record(comp)
         torch.cuda.synchronize()
         barrier()
@@ -899,7 +1052,11 @@ def main():
                "d2h_bytes_per_step": 4 * out_cross.numel() * world,
                "ms_per_step": float(t2.item()) / args.steps,
                "pipeline": ("inputs and outputs double-buffered; uploads, compute and read-backs on three streams; "
-                            "the first and last steps in 4 sequence chunks")}
+                            "the first and last steps in 4 sequence chunks"),
+               "copy_volume": ("per step every rank uploads its sequences' self-attention q/k/v and cross-attention q "
+                               "once and reads its cross-attention output back once; the 14 blocks of the step reuse "
+                               "those inputs (in the model the projections produce them on the device), so the "
+                               "copies are 1/14 of the bytes the step's attention reads")}
         up_gpu.close()
         down_gpu.close()
         del qkv2, qx2, oc2
@@ -913,8 +1070,6 @@ def main():
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
-        if gather_stream is not None:
-            gather_stream.synchronize()
         clocks_v = ClockSampler(uuid)
         gpu.profile(True)
         gpu.profile_reset()
@@ -929,8 +1084,7 @@ def main():
         t0.record()
         for _ in range(args.steps):
             step()
-        if gather_stream is not None:
-            torch.cuda.current_stream().wait_stream(gather_stream)
+        gather_outputs(out_cross)
         t1.record()
         torch.cuda.synchronize()
         clocks_v.mark_end()
@@ -971,7 +1125,7 @@ def main():
                              "note": f"{mma_per_flop} TF32 MMA FLOPs per algorithmic FLOP (hi/lo split)"})
         res = {"value": seq_calls / (ms_v / 1e3), "unit": UNIT, "ms_per_step": ms_v / args.steps, "dtype": dtype,
                "tolerance": tolerance, "tflops": flops_total * args.steps / (ms_v / 1e3) / 1e12, "gpu_launches": lv,
-               "clocks": clk_v, "roofline": roof, "kernels": prof_v}
+               "clocks": clk_v, "roofline": roof, "kernels": prof_v, "parity": check_step(out_self, out_cross)}
         for arr in [self_d] + cross_d:
             for i in range(S):
                 arr[i].variant = supra_attn._lib.FP32
@@ -987,35 +1141,34 @@ def main():
 
     sites = None
     if rank == 0 and world == 1 and not args.no_sites:
-        sites = measure_call_sites(gpu, torch, dev, args.seed,
-                                   only=set(args.sites.split(",")) if args.sites else None)
+        sites = measure_call_sites(gpu, torch, dev, args.seed, only=set(args.sites.split(",")) if args.sites else None,
+                                   cpu_reps=0 if args.no_cpu else 3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, threads, sample = cpu_port_rate(32, args.cpu_seconds, args.seed, lengths)
-        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+        cpu = cpu_baseline_leg(lengths, args.seed, args.cpu_seconds)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V, L~U{1..128})",
-            "config": {"workload": "supradit_attention_step (configs[4]): 1024 prompts x CFG = 2048 seqs, 14 blocks x "
-                                   "(self 256x256 + cross 256xL, L~U{1..128}), 9x64 heads, fp32 kernel",
-                       "prompts": args.prompts, "global_batch": 2 * args.prompts, "seq_len": TOKENS,
-                       "parallelism": f"prompt-sharded x{world}, outputs gathered to rank 0",
-                       "l2": "inputs larger than L2 (qkv 3.6 GB, K/V 8.5 GB per step at N=1)"},
+            "config": workload_config(args, world),
             "tflops": flops_total * args.steps / (ms_max / 1e3) / 1e12,
             "gpu_launches": launches,
             "clocks": clk,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "parity": parity,
+            "gather": gather,
             "kernels": prof,
-            "variants": variants,
+            "variants_detail": variants,
             "call_sites": sites,
+            # last, so that a reader of the line's tail sees the tensor-core step figures
+            "variants": {k: compact_variant(v) for k, v in variants.items()},
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(rounded(line)), flush=True)
 
     gpu.close()
     if world > 1:

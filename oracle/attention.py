@@ -99,6 +99,24 @@ def sdpa_port(q, k, v, heads, mask=None):
     return o.transpose(1, 2).reshape(B, N, C)
 
 
+def t5_sdpa_port(q, k, v, bias, heads):
+    """T5 encoder self-attention in torch float32 on the CPU (the timed CPU baseline of the T5 call
+    site, app/models/t5.js:80): q, k, v [L, C] torch float32, bias [heads, L, L] (positionBias,
+    app/models/t5.js:55-65). The arithmetic of transformers' T5Attention.forward (an unvendored
+    dependency of tools/reference.py:129, version 5.5.0 in this image, models/t5/modeling_t5.py):
+    scores = Q K^T with NO 1/sqrt(d) scaling (:308), plus the position bias (:327-328), softmax in
+    float (:331), times V (:334); heads split and merged as C = heads x d."""
+    import torch.nn.functional as F
+
+    L, C = q.shape
+    M = k.shape[0]
+    qh = q.view(L, heads, C // heads).transpose(0, 1)
+    kh = k.view(M, heads, C // heads).transpose(0, 1)
+    vh = v.view(M, heads, C // heads).transpose(0, 1)
+    o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=bias.view(heads, L, M), scale=1.0)
+    return o.transpose(0, 1).reshape(L, C)
+
+
 def rel_l2(got, ref):
     """Relative L2 error, the reference's parity metric (tools/check.js:31-44)."""
     g = np.asarray(got, dtype=np.float64).reshape(-1)

@@ -74,6 +74,18 @@ def test_t5_bias_and_attention(golden, L):
     assert oracle.max_rel(out, ref) < TOL
 
 
+@pytest.mark.parametrize("L", [1, 5, 37, 128])
+def test_t5_torch_port(golden, L):
+    """The torch fp32 T5 attention timed as the T5 call site's CPU baseline, against the goldens
+    from transformers' T5Attention."""
+    import torch
+
+    bias = torch.from_numpy(golden(f"t5_L{L}_bias").reshape(12, L, L).copy())
+    q, k, v = (torch.from_numpy(golden(f"t5_L{L}_{n}").reshape(L, 768).copy()) for n in "qkv")
+    out = oracle.t5_sdpa_port(q, k, v, bias, 12).numpy()
+    assert oracle.max_rel(out, golden(f"t5_L{L}_out")) < TOL
+
+
 @pytest.mark.parametrize("nb,md", [(32, 128), (32, 64), (16, 32), (64, 256)])
 def test_relative_bucket_matches_hf(golden, nb, md):
     ref = golden(f"bucket_{nb}_{md}").astype(np.int64)
