@@ -39,6 +39,11 @@
 //    read, and rows past Lq are never stored, so no value there can reach a stored output. In a
 //    ragged last block the 8-key groups wholly past Lk are skipped in QK^T and the 4-key groups
 //    in PV.
+//  * Key splits, for launches with fewer tiles than CTAs (the DiT self-attention of one image
+//    pair, 36 tiles): a tile then covers a range of key blocks of its (head, query tile) group,
+//    writes its unnormalised O rows with their exp2 offset and sum to a partial array, and the last
+//    split of each warp's 32 rows to arrive (a counter per group and warp) combines the group's
+//    partials: O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, M = max_s m_s.
 //  * All waits are bounded (2 s); a timeout sets the device status word and the CTA leaves.
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -73,12 +78,13 @@ static_assert((OFF_K * 4) % 128 == 0 && (OFF_V * 4) % 128 == 0 && kQBytes % 128 
                   kVBytes % 128 == 0,
               "TMA destinations are 128-byte aligned");
 
-// Next K/V block of this CTA's block sequence: tile t, block b of its nblk, and the tile's TMA
-// coordinates (head column already added).
+// Next K/V block of this CTA's block sequence: tile t, block b (the tile's blocks end before
+// block nblk), and the tile's TMA coordinates (head column already added).
 struct Cursor {
   int32_t t, b, nblk, mk, mv, kx, ky, vx, vy;
   int32_t k;  // the tile's position in the CTA's tile sequence
 };
+constexpr int kMaxSplits = 8;  // key splits per (head, query tile) group at most (the host caps them)
 constexpr int kTileSlots = 8;  // claimed tiles in flight: the cursor runs at most 3 blocks ahead
 struct Ctl {
   uint64_t qbar[kW];
@@ -90,28 +96,52 @@ struct Ctl {
 };
 constexpr int BYTES = FLOATS * 4 + (int)sizeof(Ctl) + 128;  // + slack for the 128-byte alignment
 
+// A tile: query rows q0 .. q0 + 127 of head h, key blocks b0 .. b1 - 1 (all of them unless the
+// problem's groups are split).
 struct Tile {
   const TmaProb* p;
-  int h, q0, nblk;
+  int h, q0, b0, b1;
 };
 
+struct TileIdx {
+  int pidx, local;
+};
+__device__ __forceinline__ TileIdx tile_idx(const TmaLaunch& L, int t) {
+  const int pidx = L.uniform > 0 ? t / L.uniform : find_problem(L.begin, L.n, t);
+  return TileIdx{pidx, t - (L.uniform > 0 ? pidx * L.uniform : __ldg(L.begin + pidx))};
+}
+
+// Within a problem, tile local = (h * q_tiles + query tile) * splits + split. SPLIT: the launch
+// may split groups (a separate kernel form, so that the unsplit form keeps its registers).
+template <bool SPLIT>
 __device__ __forceinline__ Tile tile_of(const TmaLaunch& L, int t) {
   Tile r;
-  const int pidx = L.uniform > 0 ? t / L.uniform : find_problem(L.begin, L.n, t);
-  r.p = L.probs + pidx;
-  const int local = t - (L.uniform > 0 ? pidx * L.uniform : __ldg(L.begin + pidx));
+  const TileIdx ix = tile_idx(L, t);
+  r.p = L.probs + ix.pidx;
   const int qt = r.p->q_tiles;
-  r.h = local / qt;
-  r.q0 = (local - r.h * qt) * kRows;
-  r.nblk = (r.p->Lk + kNK - 1) / kNK;
+  const int nb = (r.p->Lk + kNK - 1) / kNK;
+  if (SPLIT) {
+    const int ns = r.p->splits;
+    const int grp = ix.local / ns;
+    r.h = grp / qt;
+    r.q0 = (grp - r.h * qt) * kRows;
+    r.b0 = (ix.local - grp * ns) * r.p->bps;
+    r.b1 = min(nb, r.b0 + r.p->bps);
+  } else {
+    r.h = ix.local / qt;
+    r.q0 = (ix.local - r.h * qt) * kRows;
+    r.b0 = 0;
+    r.b1 = nb;
+  }
   return r;
 }
 
+template <bool SPLIT>
 __device__ __forceinline__ void cursor_at(const TmaLaunch& L, Cursor& c, int t) {
-  const Tile T = tile_of(L, t);
+  const Tile T = tile_of<SPLIT>(L, t);
   c.t = t;
-  c.b = 0;
-  c.nblk = T.nblk;
+  c.b = T.b0;
+  c.nblk = T.b1;
   c.mk = T.p->mk;
   c.mv = T.p->mv;
   c.kx = T.p->kx + T.h * kD;
@@ -124,6 +154,7 @@ __device__ __forceinline__ void cursor_at(const TmaLaunch& L, Cursor& c, int t) 
 // last block it first claims the CTA's next tile and publishes it in C->tiles; the barrier
 // arrive below releases that store to every warp that later waits for this block. Past the
 // CTA's last tile it issues nothing: no warp will wait for that stage again.
+template <bool SPLIT>
 __device__ __forceinline__ void issue_next(const TmaLaunch& L, Ctl* C, float* Ks, float* Vs, int s) {
   Cursor& c = C->cur;
   if (c.t >= L.total) return;
@@ -138,7 +169,7 @@ __device__ __forceinline__ void issue_next(const TmaLaunch& L, Ctl* C, float* Ks
   tc::tma_load_2d(Vs + s * kNK * kVS, L.maps + c.mv, c.vx, c.vy + c.b * kNK, bar);
   if (++c.b == c.nblk) {
     ++c.k;
-    if (tn < L.total) cursor_at(L, c, tn);
+    if (tn < L.total) cursor_at<SPLIT>(L, c, tn);
     else c.t = tn;
   }
 }
@@ -197,7 +228,110 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <bool BIAS>
+// Key-split epilogue of warp w for tile t (TmaProb::splits > 1). Lane (rg, cg) holds rows
+// 32w + rg + 4i, output columns 4cg .. 4cg + 3 and 32 + 4cg .. + 3 (o, unnormalised), the rows'
+// exp2 offsets mo (equal in the row's 8 lanes) and its share of the row sums l. The warp writes
+// its rows to the partial arrays; the last split of (group, w) to arrive reads every split's
+// rows back from L2 and stores O / l for rows < Lq.
+__device__ __forceinline__ void split_epilogue(const TmaLaunch& L, int t, int w, int lane, int rg, int cg, int rows_q,
+                                            float* orow, int64_t ldo, const float2 (&o)[kRI][4],
+                                            const float (&mo)[kRI], const float (&l)[kRI]) {
+  const TileIdx ix = tile_idx(L, t);
+  const TmaProb* p = L.probs + ix.pidx;
+  const int ns = p->splits;
+  const int grp_local = ix.local / ns;
+  const int split = ix.local - grp_local * ns;
+  const int64_t group = (int64_t)p->group0 + grp_local;
+  const int64_t base = (group * L.part_splits) * kRows;  // row index of split 0's first row
+  const int r0 = kRowsW * w + rg;
+#pragma unroll
+  for (int i = 0; i < kRI; ++i) {
+    float ls = l[i];
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+    const int64_t row = base + (int64_t)split * kRows + r0 + 4 * i;
+    float* dst = L.part_o + row * kD + 4 * cg;
+    *reinterpret_cast<float4*>(dst) = make_float4(o[i][0].x, o[i][0].y, o[i][1].x, o[i][1].y);
+    *reinterpret_cast<float4*>(dst + 32) = make_float4(o[i][2].x, o[i][2].y, o[i][3].x, o[i][3].y);
+    if (cg == 0) L.part_ml[row] = make_float2(mo[i], ls);
+  }
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence();  // this warp's partial rows before its count
+    last = atomicAdd(L.part_cnt + group * kW + w, 1) == ns - 1;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();  // every split's partial rows after the count that saw them all
+  // The row's 8 lanes share its offsets and sums: lane cg reads split cg's (offset, sum) of each
+  // of its 8 rows (all loads before any use), the row maximum M and the denominator come from
+  // shuffles across the 8 lanes, and each lane keeps the weight 2^(m_cg - M) of its split.
+  float wgt[kRI], inv[kRI];
+#pragma unroll
+  for (int i = 0; i < kRI; ++i) {
+    const float2 ml =
+        cg < ns ? __ldcg(&L.part_ml[base + (int64_t)cg * kRows + r0 + 4 * i]) : make_float2(-INFINITY, 0.f);
+    wgt[i] = ml.x;
+    inv[i] = ml.y;
+  }
+#pragma unroll
+  for (int i = 0; i < kRI; ++i) {
+    float M = wgt[i];
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
+    const float f = cg < ns ? ex2(wgt[i] - M) : 0.f;
+    float den = f * inv[i];
+    den += __shfl_xor_sync(0xffffffffu, den, 1);
+    den += __shfl_xor_sync(0xffffffffu, den, 2);
+    den += __shfl_xor_sync(0xffffffffu, den, 4);
+    wgt[i] = f;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv[i]) : "f"(den));  // den >= 1: the split holding M adds >= 1
+  }
+  // per row: every split's O fragments loaded, then summed with the weights
+#pragma unroll 1
+  for (int i = 0; i < kRI; ++i) {
+    float f[kMaxSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s) f[s] = __shfl_sync(0xffffffffu, wgt[i], (lane & ~7) | s);
+    if (4 * i < rows_q) {
+      const int64_t row0 = base + r0 + 4 * i;
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll
+      for (int s0 = 0; s0 < kMaxSplits; s0 += 4) {  // four splits' loads in flight at a time
+        if (s0 < ns) {
+          float4 x0[4], x1[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (s0 + u < ns) {
+              const float* src = L.part_o + (row0 + (int64_t)(s0 + u) * kRows) * kD + 4 * cg;
+              x0[u] = __ldcg(reinterpret_cast<const float4*>(src));
+              x1[u] = __ldcg(reinterpret_cast<const float4*>(src + 32));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (s0 + u < ns) {
+              const float w = f[s0 + u];
+              a0 = make_float4(fmaf(w, x0[u].x, a0.x), fmaf(w, x0[u].y, a0.y), fmaf(w, x0[u].z, a0.z),
+                               fmaf(w, x0[u].w, a0.w));
+              a1 = make_float4(fmaf(w, x1[u].x, a1.x), fmaf(w, x1[u].y, a1.y), fmaf(w, x1[u].z, a1.z),
+                               fmaf(w, x1[u].w, a1.w));
+            }
+          }
+        }
+      }
+      float* dst = orow + (int64_t)(4 * i) * ldo;
+      const float v = inv[i];
+      *reinterpret_cast<float4*>(dst) = make_float4(a0.x * v, a0.y * v, a0.z * v, a0.w * v);
+      *reinterpret_cast<float4*>(dst + 32) = make_float4(a1.x * v, a1.y * v, a1.z * v, a1.w * v);
+    }
+  }
+}
+
+template <bool BIAS, bool SPLIT>
 __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid_constant__ TmaLaunch L) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -232,10 +366,10 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
   }
   __syncthreads();  // the kernel's only block-wide barrier
   if (tid == 0) {
-    cursor_at(L, C->cur, t0);
-    for (int s = 0; s < kNS; ++s) issue_next(L, C, Ks, Vs, s);
+    cursor_at<SPLIT>(L, C->cur, t0);
+    for (int s = 0; s < kNS; ++s) issue_next<SPLIT>(L, C, Ks, Vs, s);
   }
-  Tile T = tile_of(L, t0);
+  Tile T = tile_of<SPLIT>(L, t0);
   if (lane == 0) issue_q(L, qbox_of(T, w), Qw, &C->qbar[w]);
 
   const float4* Q4 = reinterpret_cast<const float4*>(Qw) + rg * (kQS / 4);
@@ -247,7 +381,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     int Lk = pp->Lk;
     float sl2 = pp->scale_log2;
     asm volatile("" : "+r"(Lk), "+f"(sl2));  // kept in registers, not re-loaded from the descriptor
-    const int nblk = T.nblk;
+    const int b0 = T.b0, b1 = T.b1;
     // this lane's first output row, read now rather than behind the last block
     const int64_t ldo = pp->ldo;
     const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
@@ -276,7 +410,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
       return;
     }
 
-    for (int j = 0; j < nblk; ++j, ++g) {
+    for (int j = b0; j < b1; ++j, ++g) {
       const int s = (int)(g % kNS);
       const uint32_t par = (g / kNS) & 1u;
       const int nk = min(kNK, Lk - j * kNK);
@@ -284,9 +418,9 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         if (lane == 0) report_error(L.status, DEV_TIMEOUT, 22, (int32_t)g);
         return;
       }
-      if (j == nblk - 1) {
+      if (j == b1 - 1) {
         tn = *reinterpret_cast<volatile const int32_t*>(&C->tiles[(k + 1) % kTileSlots]);
-        if (tn < L.total) Tn = tile_of(L, tn);
+        if (tn < L.total) Tn = tile_of<SPLIT>(L, tn);
       }
       const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
       const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
@@ -304,7 +438,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
           else qk_block<4>(Q4, K4, sc);
         }
       }
-      if (j == nblk - 1 && tn < L.total) {  // this warp's Q rows are done: fetch its next ones
+      if (j == b1 - 1 && tn < L.total) {  // this warp's Q rows are done: fetch its next ones
         __syncwarp();
         if (lane == 0) {
           fence_proxy_async_smem();
@@ -381,7 +515,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
               moved = true;
             }
           }
-          if (j > 0 && __any_sync(0xffffffffu, moved)) {  // (block 0: O and l are still zero)
+          if (j > b0 && __any_sync(0xffffffffu, moved)) {  // (first block: O and l are still zero)
   #pragma unroll
             for (int i = 0; i < kRI; ++i) {
               const float alpha = ex2(mprev[i] - mo[i]);
@@ -440,26 +574,32 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
           atomicExch(&C->cnt[s], 0);
           __threadfence_block();
           fence_proxy_async_smem();
-          issue_next(L, C, Ks, Vs, s);
+          issue_next<SPLIT>(L, C, Ks, Vs, s);
         }
       }
     }
 
-    // ---- O / l, rows < Lq ------------------------------------------------------------------
+    if (SPLIT && pp->splits > 1) {
+      // ---- key split: this split's unnormalised rows, then the last split of this warp's rows
+      // combines the group (every split of a group has the same active warps)
+      if (active) split_epilogue(L, t, w, lane, rg, cg, rows_q, orow, ldo, o, mo, l);
+    } else {
+      // ---- O / l, rows < Lq ----------------------------------------------------------------
 #pragma unroll
-    for (int i = 0; i < kRI; ++i) {
-      float ls = l[i];
-      ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
-      ls += __shfl_xor_sync(0xffffffffu, ls, 4);
-      float inv;
-      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(ls));  // within 1 ulp; l >= 1 here
-      if (4 * i < rows_q) {
-        float* dst = orow + (int64_t)(4 * i) * ldo;
+      for (int i = 0; i < kRI; ++i) {
+        float ls = l[i];
+        ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+        float inv;
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(ls));  // within 1 ulp; l >= 1 here
+        if (4 * i < rows_q) {
+          float* dst = orow + (int64_t)(4 * i) * ldo;
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-          *reinterpret_cast<float4*>(dst + 32 * u) = make_float4(o[i][2 * u].x * inv, o[i][2 * u].y * inv,
-                                                                 o[i][2 * u + 1].x * inv, o[i][2 * u + 1].y * inv);
+          for (int u = 0; u < 2; ++u)
+            *reinterpret_cast<float4*>(dst + 32 * u) = make_float4(o[i][2 * u].x * inv, o[i][2 * u].y * inv,
+                                                                   o[i][2 * u + 1].x * inv, o[i][2 * u + 1].y * inv);
+        }
       }
     }
     T = Tn;
@@ -471,16 +611,25 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
 
 int attn_fp32_warp_tile_rows() { return kRows; }
 
-cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, bool bias, cudaStream_t s) {
-  if (L.total <= 0) return cudaSuccess;
-  auto kern = bias ? attn_fp32_warp_kernel<true> : attn_fp32_warp_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
-  if (e != cudaSuccess) return e;
+// SMs of the current device (the persistent grid is two CTAs per SM).
+static int fp32_warp_sms() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = L.total < 2 * sms ? L.total : 2 * sms;  // persistent: two CTAs per SM
+  return sms;
+}
+
+cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, bool bias, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
+  const bool split = L.part_splits > 1;
+  auto kern = bias ? (split ? attn_fp32_warp_kernel<true, true> : attn_fp32_warp_kernel<true, false>)
+                   : (split ? attn_fp32_warp_kernel<false, true> : attn_fp32_warp_kernel<false, false>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+  if (e != cudaSuccess) return e;
+  const int grid = L.total < 2 * fp32_warp_sms() ? L.total : 2 * fp32_warp_sms();  // persistent: two CTAs per SM
   kern<<<grid, kW * 32, BYTES, s>>>(L);
   return cudaGetLastError();
 }
+
+int attn_fp32_warp_cta_slots() { return 2 * fp32_warp_sms(); }
 
 }  // namespace supra

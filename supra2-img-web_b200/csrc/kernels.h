@@ -109,7 +109,14 @@ struct alignas(16) TmaProb {
   int32_t q_tiles;
   const int32_t* rel_lut;  // T5 table bias (as AttnProb): bias is then the [buckets, H] table
   int32_t rel_max;
-  int32_t pad;
+  // Key splits (persistent FP32 kernel only; 1 elsewhere): each (head, query tile) group of the
+  // problem is `splits` tiles, split s covering key blocks [s * bps, min((s + 1) * bps, blocks)),
+  // every split at least one block. The group's partial results meet in TmaLaunch::part_o /
+  // part_ml at group index group0 + h * q_tiles + query tile.
+  int32_t splits;
+  int32_t bps;
+  int32_t group0;
+  int32_t pad[2];
 };
 static_assert(sizeof(TmaProb) % 16 == 0, "TmaProb is packed into the descriptor ring");
 
@@ -123,6 +130,15 @@ struct TmaLaunch {
   // launch, in the staged descriptor block): the persistent FP32 kernel's CTAs claim them one at
   // a time, so CTAs that share an SM and progress at different rates finish together.
   int32_t* next_tile = nullptr;
+  // Key splits (TmaProb::splits > 1), persistent FP32 kernel: split s of group g writes its
+  // unnormalised O rows to part_o[((g * part_splits + s) * tile rows + row) * 64 + col] and the
+  // row's (exp2 offset, sum) to part_ml[(g * part_splits + s) * tile rows + row]; part_cnt holds one
+  // counter per (group, warp), zero at launch, and the last split of a warp's rows to arrive
+  // combines them.
+  float* part_o = nullptr;
+  float2* part_ml = nullptr;
+  int32_t* part_cnt = nullptr;
+  int32_t part_splits = 0;
 };
 
 cudaError_t launch_attn_tf32(const TmaLaunch& L, bool bias, bool split, cudaStream_t s);
@@ -137,6 +153,7 @@ constexpr int kFwBoxNarrow = 64;
 constexpr int kFwBoxRows = 32;
 cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, bool bias, cudaStream_t s);
 int attn_fp32_warp_tile_rows();
+int attn_fp32_warp_cta_slots();  // CTAs the persistent grid holds at most (two per SM)
 
 // Normalisation of x in the linear prologue (LinProb::gn_mode): GroupNorm with gamma/beta,
 // LayerNorm with adaLN modulation (gamma = scale, beta = shift, applied as 1 + scale), plain

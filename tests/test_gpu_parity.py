@@ -518,3 +518,84 @@ def test_config2_cross_full(gpu):
     for b in range(128):  # every sequence against the float64 oracle
         kv = kvs[b].numpy().reshape(-1, 1152)
         assert_close(got[b], oracle.attention_heads(qn[b], kv[:, :576], kv[:, 576:], 9))
+
+
+# ---- key splits of the persistent FP32 kernel (launches with few (head, query tile) groups) -----
+@pytest.mark.parametrize("Lq,Lk,H,bias", [
+    (256, 256, 9, None),      # 18 groups: 8 splits of one key block
+    (200, 37, 3, None),       # 6 groups, 2 key blocks (ragged last) -> 2 splits; a partial query tile
+    (128, 300, 2, None),      # 2 groups, 10 blocks -> splits of 2 blocks, the last one ragged
+    (65, 4096, 2, None),      # two groups of 65 query rows, 128 key blocks in 8 splits each
+    (100, 100, 12, "table"),  # one T5 prompt (app/models/t5.js:80): 12 groups, 4 splits, table bias
+    (150, 200, 3, "expanded"),
+])
+def test_fp32_key_splits(gpu, Lq, Lk, H, bias):
+    """A launch with at most half as many groups as CTA slots splits each group's key blocks
+    across CTAs and combines the partial rows in the kernel; against the float64 oracle, with
+    NaN/inf planted past Lq and Lk (boxes read those rows; nothing there may reach the output)."""
+    import supra_attn
+
+    rng = np.random.default_rng(Lq * 7 + Lk)
+    D = 64
+    ld = H * D
+    q = rng.standard_normal((Lq + 40) * ld).astype(np.float32)
+    k = rng.standard_normal((Lk + 40) * ld).astype(np.float32)
+    v = rng.standard_normal((Lk + 40) * ld).astype(np.float32)
+    q[Lq * ld:] = np.nan
+    k[Lk * ld:] = np.inf
+    v[Lk * ld:] = np.nan
+    kw = dict(q=dev(q), k=dev(k), v=dev(v), Lq=Lq, Lk=Lk, H=H, D=D, ldq=ld, ldk=ld, ldv=ld)
+    scale, b_ref = None, None
+    if bias == "table":
+        table = (0.5 * rng.standard_normal(32 * H)).astype(np.float32)
+        kw.update(t5_table=dev(table), scale=1.0)
+        scale, b_ref = 1.0, oracle.position_bias(table, Lq, H, 32, 128).reshape(-1)
+    elif bias == "expanded":
+        b_ref = rng.standard_normal(H * Lq * Lk).astype(np.float32)
+        kw.update(bias=dev(b_ref), scale=0.125)
+        scale = 0.125
+    out = dev(np.full((Lq + 40) * ld, 7.0))
+    gpu.profile(True)
+    gpu.profile_reset()
+    attn(gpu, out=out, **kw)
+    gpu.sync()
+    names = [r["name"] for r in gpu.profile_report()]
+    gpu.profile(False)
+    assert names == ["attn_fp32_d64_tma" + ("_bias" if bias else "")], names
+    got = host(out)
+    ref = oracle.attention_ops(q[: Lq * ld], k[: Lk * ld], v[: Lk * ld], Lq, Lk, H, D, ld, ld, ld, scale=scale,
+                               bias=b_ref)
+    assert_close(got[: Lq * ld], ref)
+    assert np.all(got[Lq * ld:] == 7.0), "wrote past Lq"
+
+
+def test_fp32_key_splits_deterministic_and_unsplit_batch(gpu):
+    """Split results are the same on every run (the combine sums the splits in a fixed order), and
+    a batch of the same problems large enough not to split gives the same values to the FP32 bar."""
+    import supra_attn
+
+    rng = np.random.default_rng(77)
+    n, Lq, Lk, H, D = 40, 256, 256, 9, 64
+    q = rng.standard_normal(n * Lq * H * D).astype(np.float32)
+    kv = rng.standard_normal(n * Lk * 2 * H * D).astype(np.float32)
+    qd, kvd = dev(q), dev(kv)
+    outs = []
+    for _ in range(2):  # problem 0 alone: 18 groups, split
+        o = dev(np.zeros(Lq * H * D))
+        attn(gpu, q=qd, k=kvd, v=kvd, out=o, Lq=Lq, Lk=Lk, H=H, D=D, ldq=H * D, ldk=2 * H * D, ldv=2 * H * D, kOff=0,
+             vOff=H * D)
+        gpu.sync()
+        outs.append(host(o))
+    np.testing.assert_array_equal(outs[0], outs[1])
+    big = dev(np.zeros(n * Lq * H * D))
+    descs = (supra_attn.Desc * n)()
+    for b in range(n):  # 720 groups: not split
+        descs[b] = supra_attn.make_desc(q=qd, k=kvd, v=kvd, out=big, Lq=Lq, Lk=Lk, H=H, D=D, ldq=H * D, ldk=2 * H * D,
+                                        ldv=2 * H * D, qOff=b * Lq * H * D, kOff=b * Lk * 2 * H * D,
+                                        vOff=b * Lk * 2 * H * D + H * D, oOff=b * Lq * H * D)
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    got = host(big)
+    assert_close(got[: Lq * H * D], outs[0])
+    x = kv[: Lk * 2 * H * D].reshape(Lk, 2 * H * D)
+    assert_close(outs[0], oracle.attention_heads(q[: Lq * H * D].reshape(Lq, H * D), x[:, : H * D], x[:, H * D:], H))
