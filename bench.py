@@ -3,7 +3,7 @@
 One step = one Euler step of the DiT's attention: 14 blocks x (self-attention over 256 patch
 tokens + cross-attention to the sequence's cached projected T5 K/V of ragged length L ~ U{1..128}),
 9 heads x 64, for 1024 prompts with CFG (2048 sequences), sharded by prompt across the ranks
-(strong scaling), outputs of each step gathered to rank 0. Each attention call is issued as the
+(strong scaling), the last step's outputs gathered to rank 0. Each attention call is issued as the
 reference issues it (one ops.attention per sample, app/models/dit.js:170-173,182-185) through
 the C ABI; the library groups the 2048 calls of a block into one launch. Self and cross
 attention of a block are flushed separately because the model's cross-attention query depends
@@ -63,6 +63,17 @@ def shard_prompts(lengths, world: int, rank: int):
         if r == rank:
             mine.append(p)
     return sorted(mine)
+
+
+def site_shard(n: int, rank: int, world: int, shardable: bool = True):
+    """A call site's problems on this rank: (indices, replicas). Sharded round-robin (problem i on
+    rank i % world) when the site may be split and has at least `world` problems; otherwise every
+    rank runs the whole batch as a replica."""
+    if world <= 1:
+        return list(range(n)), False
+    if not shardable or n < world:
+        return list(range(n)), True
+    return [i for i in range(n) if i % world == rank], False
 
 
 class ClockSampler:
@@ -291,13 +302,22 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------------------------------------
-def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu_reps: int = 3):
+def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu_reps: int = 3, rank: int = 0,
+                       world: int = 1, dist=None):
     """BASELINE.json configs[0..3] as extra figures: DiT self (B=2), DiT cross (128 ragged
     sequences), T5 (256 prompts, ragged L, bias), VAE mid-block (1, 8, 64 images). Each rep is one
     flush of the call site's calls, timed with CUDA events after the L2 is flushed; FP32 and TF32
     requests both reported with the kernels that ran (TF32 requests the tensor-core kernel does
-    not cover run the FP32 kernels). only: names of the call sites to run (default all)."""
+    not cover run the FP32 kernels). only: names of the call sites to run (default all).
+    With world > 1 every rank runs its share of a site's batch (problem i on rank i % world; a
+    batch smaller than world, and the B = 2 self-attention pair, run whole on every rank as
+    replicas), each rep starts after a barrier, and a rep's time is the max over ranks; the
+    f-rows (whole blocks, K/V preparation) run on one GPU only."""
     import supra_attn
+
+    if world > 1:  # the f-rows are single-GPU figures
+        keep = {"dit_self_b2", "dit_cross_128", "t5_256", "t5_256_table", "vae"}
+        only = keep if only is None else set(only) & keep
 
     peaks = measured_peaks()
     fp32_peak = 148 * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
@@ -310,13 +330,18 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
 
     tf_peak = float(peaks.get("bf16_tflops", 1590.0)) / 2.0  # TF32 dense peak: half of measured bf16
 
-    def run(name, units, unit_name, make_descs, flops, bytes_, cpu=None, out_fn=None):
+    def run(name, units, unit_name, make_descs, flops, bytes_, cpu=None, out_fn=None, shardable=True):
         """Times the call site's flush for each variant; with `cpu` (runs the site's calls through
         the torch CPU port on all host cores and returns the flat output) also times that, and
         compares each variant's output (`out_fn`) with it."""
         import oracle
 
         res = {}
+        mine, replicas = site_shard(units, rank, world, shardable)
+        if replicas:  # every rank runs the whole batch: the job does world times the work
+            units, flops, bytes_ = units * world, flops * world, bytes_ * world
+        if world > 1:
+            res["ranks"] = {"world": world, "mode": "replicas" if replicas else "sharded (problem i on rank i % N)"}
         ref = None
         if cpu is not None and cpu_reps > 0:
             import torch as _t
@@ -332,6 +357,8 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
                           "cores": _t.get_num_threads(), "kind": "port"}
         for variant in ("fp32", "tf32", "tf32x3"):
             descs = make_descs(variant)
+            if len(mine) != len(descs):
+                descs = (supra_attn.Desc * len(mine))(*[descs[i] for i in mine])
             gpu.enqueue_batch(descs)
             gpu.sync()
             gpu.profile(True)
@@ -339,6 +366,8 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
             times = []
             for _ in range(reps):
                 flush.fill_(1.0)
+                if world > 1:
+                    dist.barrier(device_ids=[dev.index])
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record()
@@ -349,6 +378,10 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
                 times.append(e0.elapsed_time(e1))
             prof = gpu.profile_report()
             gpu.profile(False)
+            if world > 1:  # each rep's time is the slowest rank's
+                tt = torch.tensor(times, device=dev)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                times = tt.tolist()
             ms = statistics.median(times)
             per = {}
             for r in prof:
@@ -422,7 +455,7 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
             return oracle.sdpa_port(qkv_c[:, :, 0], qkv_c[:, :, 1], qkv_c[:, :, 2], 9).reshape(-1).numpy()
 
         run("dit_self_b2", 2, "seq", c1, f1, 2 * 4.0 * (2 * 256 * 576 + 2 * 256 * 576), cpu=cpu1,
-            out_fn=lambda: o1.cpu().numpy())
+            out_fn=lambda: o1.cpu().numpy(), shardable=False)
 
     if want("dit_cross_128"):
         # DiT cross-attention, 64 prompts x CFG, ragged L
@@ -1140,9 +1173,9 @@ def main():
                                          "max|d|/max|ref| and rel-L2 <= 1e-5 (the FP32 bar)", 3)
 
     sites = None
-    if rank == 0 and world == 1 and not args.no_sites:
+    if not args.no_sites:  # (every rank: with N > 1 each runs its share of a site's batch)
         sites = measure_call_sites(gpu, torch, dev, args.seed, only=set(args.sites.split(",")) if args.sites else None,
-                                   cpu_reps=0 if args.no_cpu else 3)
+                                   cpu_reps=0 if (args.no_cpu or world > 1) else 3, rank=rank, world=world, dist=dist)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

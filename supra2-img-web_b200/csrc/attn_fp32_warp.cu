@@ -37,8 +37,7 @@
 //  * Boxes are always whole (32 rows). Rows past Lq or Lk hold other rows of the buffer or zero
 //    fill: scores of keys past Lk are replaced (not multiplied) by -inf, V rows past Lk are not
 //    read, and rows past Lq are never stored, so no value there can reach a stored output. In a
-//    ragged last block the 8-key groups wholly past Lk are skipped in QK^T and the 4-key groups
-//    in PV.
+//    ragged last block the 4-key groups wholly past Lk are skipped in PV.
 //  * Key splits, for launches with fewer tiles than CTAs (the DiT self-attention of one image
 //    pair, 36 tiles): a tile then covers a range of key blocks of its (head, query tile) group,
 //    writes its unnormalised O rows with their exp2 offset and sum to a partial array, and the last
@@ -186,40 +185,39 @@ __device__ __forceinline__ void issue_q(const TmaLaunch& L, const QBox& q, float
   tc::tma_load_2d(dst, L.maps + q.m, q.x, q.y, bar);
 }
 
-// S = Q K^T for keys cg + 8jj, jj < NJ, of one block (NJ < 4 for a ragged last block: the key
-// groups past Lk are not computed). Packed FFMA (f32x2, two FMAs per issued instruction): each
-// score accumulates the head dim's even and odd components in the two halves of one float2
-// ((x, y) and (z, w) of a float4 fragment are register pairs already), summed at the end.
-template <int NJ>
+// S = Q K^T for keys cg + 8jj (jj < 4) of one block. Packed FFMA (f32x2, two FMAs per issued
+// instruction): each score accumulates the head dim's even and odd components in the two halves
+// of one float2 ((x, y) and (z, w) of a float4 fragment are register pairs already), summed at the
+// end.
 __device__ __forceinline__ void qk_block(const float4* __restrict__ Q4, const float4* __restrict__ K4,
                                          float (&sc)[kRI][4]) {
-  float2 acc[kRI][NJ];
+  float2 acc[kRI][4];
 #pragma unroll
   for (int i = 0; i < kRI; ++i)
 #pragma unroll
-    for (int jj = 0; jj < NJ; ++jj) acc[i][jj] = make_float2(0.f, 0.f);
+    for (int jj = 0; jj < 4; ++jj) acc[i][jj] = make_float2(0.f, 0.f);
 #pragma unroll 2
   for (int d4 = 0; d4 < kD / 4; ++d4) {
-    float4 kf[NJ], qf[kRI];
+    float4 kf[4], qf[kRI];
 #pragma unroll
-    for (int jj = 0; jj < NJ; ++jj) kf[jj] = K4[jj * 8 * (kKS / 4) + d4];
+    for (int jj = 0; jj < 4; ++jj) kf[jj] = K4[jj * 8 * (kKS / 4) + d4];
 #pragma unroll
     for (int i = 0; i < kRI; ++i) qf[i] = Q4[i * 4 * (kQS / 4) + d4];
 #pragma unroll
     for (int i = 0; i < kRI; ++i)
 #pragma unroll
-      for (int jj = 0; jj < NJ; ++jj)
+      for (int jj = 0; jj < 4; ++jj)
         acc[i][jj] = __ffma2_rn(make_float2(qf[i].x, qf[i].y), make_float2(kf[jj].x, kf[jj].y), acc[i][jj]);
 #pragma unroll
     for (int i = 0; i < kRI; ++i)
 #pragma unroll
-      for (int jj = 0; jj < NJ; ++jj)
+      for (int jj = 0; jj < 4; ++jj)
         acc[i][jj] = __ffma2_rn(make_float2(qf[i].z, qf[i].w), make_float2(kf[jj].z, kf[jj].w), acc[i][jj]);
   }
 #pragma unroll
   for (int i = 0; i < kRI; ++i)
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) sc[i][jj] = jj < NJ ? acc[i][jj].x + acc[i][jj].y : 0.f;
+    for (int jj = 0; jj < 4; ++jj) sc[i][jj] = acc[i][jj].x + acc[i][jj].y;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -290,7 +288,8 @@ __device__ __forceinline__ void split_epilogue(const TmaLaunch& L, int t, int w,
     wgt[i] = f;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv[i]) : "f"(den));  // den >= 1: the split holding M adds >= 1
   }
-  // per row: every split's O fragments loaded, then summed with the weights
+  // per row: the row's O fragments of up to four splits loaded together, then summed with the
+  // weights (about one wait for L2 per row; splits-outer loops hold twice the registers and spill)
 #pragma unroll 1
   for (int i = 0; i < kRI; ++i) {
     float f[kMaxSplits];
@@ -300,7 +299,7 @@ __device__ __forceinline__ void split_epilogue(const TmaLaunch& L, int t, int w,
       const int64_t row0 = base + r0 + 4 * i;
       float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
 #pragma unroll
-      for (int s0 = 0; s0 < kMaxSplits; s0 += 4) {  // four splits' loads in flight at a time
+      for (int s0 = 0; s0 < kMaxSplits; s0 += 4) {
         if (s0 < ns) {
           float4 x0[4], x1[4];
 #pragma unroll
@@ -428,15 +427,9 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
       // ---- S = Q K^T
       float sc[kRI][4];
       if (active) {
-        if (nk == kNK) {
-          qk_block<4>(Q4, K4, sc);
-        } else {
-          const int nj = (nk + 7) >> 3;
-          if (nj == 1) qk_block<1>(Q4, K4, sc);
-          else if (nj == 2) qk_block<2>(Q4, K4, sc);
-          else if (nj == 3) qk_block<3>(Q4, K4, sc);
-          else qk_block<4>(Q4, K4, sc);
-        }
+        // (ragged blocks too: scores of keys past Lk are replaced below; forms that skipped the
+        // 8-key groups past Lk measured 0.2 % slower over the DiT step, their code being larger)
+        qk_block(Q4, K4, sc);
       }
       if (j == b1 - 1 && tn < L.total) {  // this warp's Q rows are done: fetch its next ones
         __syncwarp();

@@ -36,12 +36,24 @@ int norm_stats(supra_attn_ctx* c, const std::vector<const Queued*>& g, supra::Li
 
 int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   const int n = (int)g.size();
+  // Column tile width: 128 x 64 tiles cost about 0.55 of a 128 x 128 tile (a smaller register
+  // block reads more shared memory per FMA); take the width whose whole waves of the grid's CTA
+  // slots (two per SM) cost less. The DiT blocks' N = 576 products: 2 waves either way, 1.1 against
+  // 2.0 in tile costs; the stacked K/V preparation (N = 16128) keeps 128.
+  int64_t t128 = 0, t64 = 0;
+  for (int i = 0; i < n; ++i) {
+    const int64_t mt = (g[i]->lin.M + 127) / 128;
+    t128 += mt * ((g[i]->lin.N + 127) / 128);
+    t64 += mt * ((g[i]->lin.N + 63) / 64);
+  }
+  const int64_t slots = supra::attn_fp32_warp_cta_slots();
+  const int cols = 0.55 * (double)((t64 + slots - 1) / slots) < (double)((t128 + slots - 1) / slots) ? 64 : 128;
   std::vector<int32_t> begin(n + 1);
   int64_t total = 0;
   double flops = 0, bytes = 0;
   for (int i = 0; i < n; ++i) {
     begin[i] = (int32_t)total;
-    total += (int64_t)((g[i]->lin.M + 127) / 128) * g[i]->lin.n_tiles;
+    total += (int64_t)((g[i]->lin.M + 127) / 128) * ((g[i]->lin.N + cols - 1) / cols);
     flops += g[i]->flops;
     bytes += g[i]->bytes;
     if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
@@ -53,7 +65,10 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
   if (rc) return rc;
   supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(h);
-  for (int i = 0; i < n; ++i) hp[i] = g[i]->lin;
+  for (int i = 0; i < n; ++i) {
+    hp[i] = g[i]->lin;
+    hp[i].n_tiles = (hp[i].N + cols - 1) / cols;
+  }
   rc = norm_stats(c, g, hp);
   if (rc) return rc;
   std::memcpy(h + pbytes, begin.data(), bbytes);
@@ -69,7 +84,7 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = supra::launch_linear_fp32(g[0]->bias, g[0]->aligned, L, c->stream);
+    e = supra::launch_linear_fp32(g[0]->bias, g[0]->aligned, cols, L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;

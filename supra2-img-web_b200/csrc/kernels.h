@@ -172,7 +172,7 @@ struct alignas(16) LinProb {
   float* y;
   int64_t ldx, ldw, ldy;
   int32_t M, N, K;
-  int32_t n_tiles;  // column tiles of 128: ceil(N / 128)
+  int32_t n_tiles;  // column tiles: ceil(N / tile columns) (128 or 64, the FFMA kernel; 128 elsewhere)
   const float* resid;  // y = resid[row * ldr + col] + ..., or nullptr (may be y itself)
   int64_t ldr;
   const float* gate;   // the product is scaled by gate[col] (offset applied), or nullptr
@@ -198,7 +198,8 @@ struct LinLaunch {
   int32_t n, total;
   int32_t* status;
 };
-cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cudaStream_t s);
+// tile_cols: 128 or 64 columns per 128-row tile (LinProb::n_tiles counts tiles of that width)
+cudaError_t launch_linear_fp32(bool bias, bool aligned, int tile_cols, const LinLaunch& L, cudaStream_t s);
 // GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
 // group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
 // mean in a second pass (app/gpu/kernels.js:117-139).

@@ -14,6 +14,8 @@
 // used (statistics from gn_stats_kernel, an earlier launch in the same flush; the VAE mid-block
 // attention, app/models/vae.js:77-94), and a residual, optionally gated per column, added in the
 // epilogue (app/gpu/gemm.js:10,135; in place for the DiT blocks' projections).
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace supra {
@@ -21,14 +23,39 @@ namespace {
 
 constexpr int kT = 256;   // threads
 constexpr int kBM = 128;  // rows per tile
-constexpr int kBN = 128;  // columns per tile
 constexpr int kBK = 16;   // reduction depth per stage
 constexpr int kS = kBK + 4;  // row stride of the stage buffers (conflict-free float4 reads)
+// k stages in flight: the load of stage s + stages - 1 is issued while stage s is computed. With
+// two (one load ahead) a 128 x 64 tile's stage compute, about 1 us, did not cover its load's
+// latency from L2, and such a tile took as long as a 128 x 128 one; four stages for the 64-column
+// tiles, two for the 128-column tiles (whose 64 accumulators leave no registers for deeper
+// address bookkeeping under the two-CTA bound: four stages spilled ~1 KB there).
+template <int BN>
+constexpr int stages_of() { return BN == 64 ? 4 : 2; }
+// dynamic shared memory of the form (the two-stage form's arrays are static)
+template <int BN>
+constexpr int smem_bytes() { return stages_of<BN>() == 2 ? 0 : stages_of<BN>() * (kBM + BN) * kS * 4; }
 
-template <bool BIAS, bool ALIGNED>
-__global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
-  __shared__ __align__(16) float As[2][kBM * kS];
-  __shared__ __align__(16) float Bs[2][kBN * kS];
+// BN: columns per tile, 128 or 64 (the host picks per launch the width that fills the last wave
+// of tiles best: the DiT blocks' N = 576 products are 320 tiles of 128 x 128, 1.08 waves of the
+// 296 CTA slots, against 576 tiles of 128 x 64). Thread (rg, cg) owns rows rg + 16i (i < 8) and
+// columns cg + 16j (j < BN / 16).
+template <bool BIAS, bool ALIGNED, int BN>
+__global__ void __launch_bounds__(kT, BN == 64 ? 3 : 2) linear_fp32_kernel(const LinLaunch L) {
+  constexpr int NJ = BN / 16;
+  constexpr int kStages = stages_of<BN>();
+  float* As;  // [kStages][kBM * kS]
+  float* Bs;  // [kStages][BN * kS]
+  if constexpr (kStages == 2) {  // static arrays (40 KB), as the two-stage form always had
+    __shared__ __align__(16) float sA[2 * kBM * kS];
+    __shared__ __align__(16) float sB[2 * BN * kS];
+    As = sA;
+    Bs = sB;
+  } else {
+    extern __shared__ __align__(16) float lin_smem[];
+    As = lin_smem;
+    Bs = lin_smem + kStages * kBM * kS;
+  }
   const int t = blockIdx.x;
   if (t >= L.total) {
     if (threadIdx.x == 0) report_error(L.status, DEV_BAD_TILE, 30);
@@ -39,12 +66,12 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
   const int local = t - __ldg(L.begin + pi);
   const int rt = local / P.n_tiles;
   const int r0 = rt * kBM;
-  const int c0 = (local - rt * P.n_tiles) * kBN;
+  const int c0 = (local - rt * P.n_tiles) * BN;
   const int K = P.K;
   const float* abase = P.x + (int64_t)r0 * P.ldx;
   const float* bbase = P.w + (int64_t)c0 * P.ldw;
   const int nr = min(kBM, P.M - r0);
-  const int nc = min(kBN, P.N - c0);
+  const int nc = min(BN, P.N - c0);
 
   const int tid = threadIdx.x;
   const int rg = tid >> 4, cg = tid & 15;
@@ -52,16 +79,18 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
   auto load_stage = [&](int buf, int k0) {
     if (ALIGNED) {
 #pragma unroll
-      for (int it = 0; it < 2; ++it) {  // 512 float4 per operand
+      for (int it = 0; it < 2; ++it) {  // 512 float4 of x, BN * 4 of W
         const int idx = tid + it * kT;
         const int r = idx >> 2, c4 = idx & 3;
         const int k = k0 + c4 * 4;
         const bool okA = (r < nr) && (k < K);
-        cp_async16(&As[buf][r * kS + c4 * 4], okA ? (const void*)(abase + (int64_t)r * P.ldx + k) : (const void*)abase,
+        cp_async16(&As[buf * kBM * kS + r * kS + c4 * 4], okA ? (const void*)(abase + (int64_t)r * P.ldx + k) : (const void*)abase,
                    okA ? 16u : 0u);
-        const bool okB = (r < nc) && (k < K);
-        cp_async16(&Bs[buf][r * kS + c4 * 4], okB ? (const void*)(bbase + (int64_t)r * P.ldw + k) : (const void*)bbase,
-                   okB ? 16u : 0u);
+        if (it * kT < BN * 4) {
+          const bool okB = (r < nc) && (k < K);
+          cp_async16(&Bs[buf * BN * kS + r * kS + c4 * 4], okB ? (const void*)(bbase + (int64_t)r * P.ldw + k) : (const void*)bbase,
+                     okB ? 16u : 0u);
+        }
       }
     } else {
 #pragma unroll
@@ -70,70 +99,97 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
         const int r = idx >> 4, c = idx & 15;
         const int k = k0 + c;
         const bool okA = (r < nr) && (k < K);
-        cp_async4(&As[buf][r * kS + c], okA ? (const void*)(abase + (int64_t)r * P.ldx + k) : (const void*)abase,
+        cp_async4(&As[buf * kBM * kS + r * kS + c], okA ? (const void*)(abase + (int64_t)r * P.ldx + k) : (const void*)abase,
                   okA ? 4u : 0u);
-        const bool okB = (r < nc) && (k < K);
-        cp_async4(&Bs[buf][r * kS + c], okB ? (const void*)(bbase + (int64_t)r * P.ldw + k) : (const void*)bbase,
-                  okB ? 4u : 0u);
+        if (it * kT < BN * 16) {
+          const bool okB = (r < nc) && (k < K);
+          cp_async4(&Bs[buf * BN * kS + r * kS + c], okB ? (const void*)(bbase + (int64_t)r * P.ldw + k) : (const void*)bbase,
+                    okB ? 4u : 0u);
+        }
       }
     }
     cp_async_commit();
   };
 
-  float acc[8][8];
+  float acc[8][NJ];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
 
   const int nstage = (K + kBK - 1) / kBK;
-  load_stage(0, 0);
-  for (int st = 0; st < nstage; ++st) {
-    if (st + 1 < nstage) {
-      load_stage((st + 1) & 1, (st + 1) * kBK);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+  if constexpr (kStages == 2) {
+    load_stage(0, 0);
+  } else {
+#pragma unroll
+    for (int s0 = 0; s0 < kStages - 1; ++s0) {  // the first kStages - 1 stages (empty groups past K)
+      if (s0 < nstage) load_stage(s0, s0 * kBK);
+      else cp_async_commit();
     }
-    __syncthreads();
+  }
+  for (int st = 0; st < nstage; ++st) {
+    const int buf = st % kStages;
+    if constexpr (kStages == 2) {  // next stage's load first, then wait for this one
+      if (st + 1 < nstage) {
+        load_stage((st + 1) & 1, (st + 1) * kBK);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+    } else {
+      cp_async_wait<kStages - 2>();  // stage st has landed (one commit group per stage)
+      __syncthreads();               // ... for every thread; and every thread is done with stage st - 1
+      if (st + kStages - 1 < nstage) load_stage((st + kStages - 1) % kStages, (st + kStages - 1) * kBK);
+      else cp_async_commit();
+    }
     if (P.gn_stats) {
       // GroupNorm (+ SiLU) or LayerNorm (+ modulation) of the staged x tile, per element of a
       // valid row and column (padding stays zero): (x - mean) * rstd * g + b with g, b = gamma,
-      // beta (app/gpu/kernels.js:141-162), 1 + scale, shift (app/gpu/kernels.js:111) or 1, 0
-      float* a = As[st & 1];
-      const int k0 = st * kBK;
+      // beta (app/gpu/kernels.js:141-162), 1 + scale, shift (app/gpu/kernels.js:111) or 1, 0.
+      // Thread tid normalises column kk = tid % 16 of the stage in rows tid / 16 + 16 i: its
+      // column's g, b and group are one lookup per stage, its rows' images one per tile.
+      float* a = As + buf * kBM * kS;
+      const int kk = tid & 15, rb = tid >> 4;
+      const int k = st * kBK + kk;
+      if (k < K) {
+        float g = 1.f, b = 0.f;
+        if (P.gn_mode != kNormPlain) {
+          g = __ldg(P.gamma + k);
+          b = __ldg(P.beta + k);
+          if (P.gn_mode == kNormModulated) g = 1.f + g;
+        }
+        const float2* st_k = P.gn_stats + k / P.gn_cg;  // the column's group
+        // a row's image: one for the whole tile when images are whole tiles (the VAE's 1024-row
+        // images), the row itself for a LayerNorm
+        const bool one_img = P.gn_rows % kBM == 0;
+        const int img0 = one_img ? r0 / P.gn_rows : 0;
 #pragma unroll
-      for (int it = 0; it < kBM * kBK / kT; ++it) {
-        const int idx = tid + it * kT;
-        const int r = idx >> 4, kk = idx & 15;
-        const int k = k0 + kk;
-        if (r < nr && k < K) {
-          const float2 ms = __ldg(P.gn_stats + (int64_t)((r0 + r) / P.gn_rows) * P.gn_groups + k / P.gn_cg);
-          float g = 1.f, b = 0.f;
-          if (P.gn_mode != kNormPlain) {
-            g = __ldg(P.gamma + k);
-            b = __ldg(P.beta + k);
-            if (P.gn_mode == kNormModulated) g = 1.f + g;
+        for (int it = 0; it < kBM / 16; ++it) {
+          const int r = rb + 16 * it;
+          if (r < nr) {
+            const int img = one_img ? img0 : (P.gn_rows == 1 ? r0 + r : (r0 + r) / P.gn_rows);
+            const float2 ms = __ldg(st_k + (int64_t)img * P.gn_groups);
+            float v = (a[r * kS + kk] - ms.x) * (ms.y * g) + b;
+            if (P.gn_silu) v = v / (1.f + __expf(-v));
+            a[r * kS + kk] = v;
           }
-          float v = (a[r * kS + kk] - ms.x) * ms.y * g + b;
-          if (P.gn_silu) v = v / (1.f + __expf(-v));
-          a[r * kS + kk] = v;
         }
       }
       __syncthreads();
     }
-    const float4* A4 = reinterpret_cast<const float4*>(As[st & 1]) + rg * (kS / 4);
-    const float4* B4 = reinterpret_cast<const float4*>(Bs[st & 1]) + cg * (kS / 4);
+    const float4* A4 = reinterpret_cast<const float4*>(As + buf * kBM * kS) + rg * (kS / 4);
+    const float4* B4 = reinterpret_cast<const float4*>(Bs + buf * BN * kS) + cg * (kS / 4);
 #pragma unroll
     for (int k4 = 0; k4 < kBK / 4; ++k4) {
-      float4 bf[8];
+      float4 bf[NJ];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
+      for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 af = A4[i * 16 * (kS / 4) + k4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < NJ; ++j) {
           acc[i][j] = fmaf(af.x, bf[j].x, acc[i][j]);
           acc[i][j] = fmaf(af.y, bf[j].y, acc[i][j]);
           acc[i][j] = fmaf(af.z, bf[j].z, acc[i][j]);
@@ -141,13 +197,13 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
         }
       }
     }
-    __syncthreads();
+    if constexpr (kStages == 2) __syncthreads();  // the next iteration's load overwrites this buffer
   }
 
   // y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
-  float bias[8], gate[8];
+  float bias[NJ], gate[NJ];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < NJ; ++j) {
     bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
     gate[j] = (P.gate && cg + 16 * j < nc) ? __ldg(P.gate + c0 + cg + 16 * j) : 1.f;
   }
@@ -159,7 +215,7 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_kernel(const LinLaunch L) {
     // resid may be y itself (in place): each element is read and then written by this thread only
     const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < NJ; ++j) {
       const int c = cg + 16 * j;
       if (c < nc) {
         float v = acc[i][j] + bias[j];
@@ -243,16 +299,27 @@ cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, i
   return cudaGetLastError();
 }
 
-cudaError_t launch_linear_fp32(bool bias, bool aligned, const LinLaunch& L, cudaStream_t s) {
+cudaError_t launch_linear_fp32(bool bias, bool aligned, int tile_cols, const LinLaunch& L, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
-  if (bias) {
-    if (aligned) linear_fp32_kernel<true, true><<<L.total, kT, 0, s>>>(L);
-    else linear_fp32_kernel<true, false><<<L.total, kT, 0, s>>>(L);
-  } else {
-    if (aligned) linear_fp32_kernel<false, true><<<L.total, kT, 0, s>>>(L);
-    else linear_fp32_kernel<false, false><<<L.total, kT, 0, s>>>(L);
-  }
-  return cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  auto go = [&](auto kern, int bytes) {
+    if (bytes > 0) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) kern<<<L.total, kT, bytes, s>>>(L);
+  };
+  auto pick = [&](auto bn) {
+    constexpr int BN = decltype(bn)::value;
+    constexpr int bytes = smem_bytes<BN>();
+    if (bias) {
+      if (aligned) go(linear_fp32_kernel<true, true, BN>, bytes);
+      else go(linear_fp32_kernel<true, false, BN>, bytes);
+    } else {
+      if (aligned) go(linear_fp32_kernel<false, true, BN>, bytes);
+      else go(linear_fp32_kernel<false, false, BN>, bytes);
+    }
+  };
+  if (tile_cols == 64) pick(std::integral_constant<int, 64>{});
+  else pick(std::integral_constant<int, 128>{});
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace supra

@@ -599,3 +599,39 @@ def test_fp32_key_splits_deterministic_and_unsplit_batch(gpu):
     assert_close(got[: Lq * H * D], outs[0])
     x = kv[: Lk * 2 * H * D].reshape(Lk, 2 * H * D)
     assert_close(outs[0], oracle.attention_heads(q[: Lq * H * D].reshape(Lq, H * D), x[:, : H * D], x[:, H * D:], H))
+
+
+def test_batch_hazards_fall_back_to_ordered_recording(gpu):
+    """supra_attn_enqueue_batch records a conflict-free batch in one merge; a batch whose problems
+    depend on each other is recorded in order with a flush at each hazard, as single calls are:
+    (1) problem 1 reads problem 0's output (read after write), (2) problems 0 and 2 write the same
+    output (the later one wins), (3) a batch reading an output still queued from an earlier call."""
+    import supra_attn
+
+    rng = np.random.default_rng(12)
+    H, D, L = 2, 64, 70
+    ld = H * D
+    q, k, v = (rng.standard_normal(L * ld).astype(np.float32) for _ in range(3))
+    k2 = rng.standard_normal(L * ld).astype(np.float32)
+    qd, kd, vd, k2d = dev(q), dev(k), dev(v), dev(k2)
+    o1, o2, o3 = (dev(np.zeros(L * ld)) for _ in range(3))
+    kw = dict(Lq=L, Lk=L, H=H, D=D, ldq=ld, ldk=ld, ldv=ld)
+    r1 = oracle.attention_ops(q, k, v, L, L, H, D, ld, ld, ld)
+    r2 = oracle.attention_ops(r1, k, v, L, L, H, D, ld, ld, ld)
+    r3 = oracle.attention_ops(q, k2, v, L, L, H, D, ld, ld, ld)
+    # (1) and (2) in one batch: o1 = A(q); o2 = A(o1); o1 = A(q, k2) (overwrites o1 after o2 read it)
+    descs = (supra_attn.Desc * 3)(supra_attn.make_desc(q=qd, k=kd, v=vd, out=o1, **kw),
+                                  supra_attn.make_desc(q=o1, k=kd, v=vd, out=o2, **kw),
+                                  supra_attn.make_desc(q=qd, k=k2d, v=vd, out=o1, **kw))
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    assert_close(host(o2), r2)
+    assert_close(host(o1), r3)
+    # (3) a queued single call, then a batch that reads its output and a conflict-free problem
+    attn(gpu, q=qd, k=kd, v=vd, out=o3, **kw)
+    descs = (supra_attn.Desc * 2)(supra_attn.make_desc(q=o3, k=kd, v=vd, out=o2, **kw),
+                                  supra_attn.make_desc(q=qd, k=k2d, v=vd, out=o1, **kw))
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    assert_close(host(o2), r2)
+    assert_close(host(o1), r3)

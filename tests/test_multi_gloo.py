@@ -1,5 +1,5 @@
-"""Multi-rank host logic of bench.py on CPU: prompt sharding across ranks and the gather of each
-step's outputs to rank 0, run as two gloo ranks (world size 2, 127.0.0.1)."""
+"""Multi-rank host logic of bench.py on CPU: prompt sharding across ranks, the call sites' shares,
+and the gather of the outputs to rank 0, run as two gloo ranks (world size 2, 127.0.0.1)."""
 
 import os
 import socket
@@ -21,6 +21,22 @@ def test_shards_cover_every_prompt_once_and_balance_lengths():
         assert len({len(s) for s in shards}) == 1  # the same number of prompts (CFG pairs) per rank
         sums = [sum(lengths[2 * p] + lengths[2 * p + 1] for p in s) for s in shards]
         assert max(sums) - min(sums) <= 0.01 * max(sums)  # K/V work within 1 %
+
+
+def test_call_site_shards():
+    """bench.py's call sites at N GPUs: every problem on exactly one rank when sharded; batches
+    smaller than N, and the B = 2 self-attention pair, run whole on every rank (replicas)."""
+    for n in (2, 8, 64, 128, 256):
+        for world in (1, 2, 4, 8):
+            parts = [bench.site_shard(n, r, world) for r in range(world)]
+            if n >= world:
+                assert sorted(i for idx, rep in parts for i in idx) == list(range(n))
+                assert not any(rep for _, rep in parts)
+                assert max(len(p[0]) for p in parts) - min(len(p[0]) for p in parts) <= 1
+            else:
+                assert all(rep and p == list(range(n)) for p, rep in parts)
+    assert bench.site_shard(2, 1, 4, shardable=False) == ([0, 1], True)
+    assert bench.site_shard(2, 0, 1, shardable=False) == ([0, 1], False)
 
 
 def _free_port():
