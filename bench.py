@@ -65,6 +65,36 @@ def shard_prompts(lengths, world: int, rank: int):
     return sorted(mine)
 
 
+def bind_to_gpu_cpus(torch, dev_index: int):
+    """Pins this process to the host CPUs nearest its GPU (the PCI device's local_cpulist), so the
+    pinned host buffers it allocates afterwards land on that NUMA node. With N ranks each moving
+    its step's inputs over PCIe, buffers on the far socket cost the copies host-link bandwidth.
+    Returns the CPU list applied, or None when the host does not say."""
+    try:
+        p = torch.cuda.get_device_properties(dev_index)
+        path = (f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/"
+                "local_cpulist")
+        with open(path) as f:
+            spec = f.read().strip()
+        cpus = parse_cpulist(spec)
+        if not cpus or len(cpus) >= (os.cpu_count() or 1):
+            return None
+        os.sched_setaffinity(0, cpus)
+        return spec
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return None
+
+
+def parse_cpulist(spec: str) -> set:
+    """The CPUs of a sysfs CPU list such as "0-47,96-143"."""
+    cpus = set()
+    for part in spec.split(","):
+        if part.strip():
+            lo, _, hi = part.strip().partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
 def site_shard(n: int, rank: int, world: int, shardable: bool = True):
     """A call site's problems on this rank: (indices, replicas). Sharded round-robin (problem i on
     rank i % world) when the site may be split and has at least `world` problems; otherwise every
@@ -757,6 +787,9 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    # with several ranks, each keeps its host threads and pinned buffers beside its GPU (the
+    # single-GPU run keeps every core: its CPU baseline uses them all)
+    cpus_near_gpu = bind_to_gpu_cpus(torch, local_rank) if world > 1 else None
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     # one compute stream for torch's copies/events and the library's launches
@@ -1086,6 +1119,7 @@ def main():
                "ms_per_step": float(t2.item()) / args.steps,
                "pipeline": ("inputs and outputs double-buffered; uploads, compute and read-backs on three streams; "
                             "the first and last steps in 4 sequence chunks"),
+               "host_cpus": cpus_near_gpu or "all",
                "copy_volume": ("per step every rank uploads its sequences' self-attention q/k/v and cross-attention q "
                                "once and reads its cross-attention output back once; the 14 blocks of the step reuse "
                                "those inputs (in the model the projections produce them on the device), so the "

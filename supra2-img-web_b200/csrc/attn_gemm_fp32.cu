@@ -10,13 +10,14 @@
 // Both GEMMs are 128x128 tiles over 256 threads with 8x8 register blocks (thread (rg, cg) in
 // 16x16 owns rows rg + 16*i and columns cg + 16*j / float4 groups cg, cg + 16), operands staged
 // 16-deep through double-buffered padded shared memory by cp.async (zero-filled past every edge).
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace supra {
 namespace {
 
 constexpr int kGT = 256;  // threads
-constexpr int kBM = 128;  // rows per tile
 constexpr int kBN = 128;  // columns per tile
 constexpr int kBK = 16;   // reduction depth per stage
 constexpr int kAS = kBK + 4;   // row stride of the [rows][k] stage buffers
@@ -25,10 +26,13 @@ constexpr int kVS = kBN + 4;   // row stride of the [k][cols] V stage buffer
 __device__ __forceinline__ int find_unit(const int32_t* begin, int n, int t) { return find_problem(begin, n, t); }
 
 // ------------------------------------------------------------------------------------------------
-// S[r][c] = scale * sum_d Q[row0 + r][d] K[c][d] (+ bias[h][row0 + r][c])
-template <bool BIAS, bool ALIGNED>
+// S[r][c] = scale * sum_d Q[row0 + r][d] K[c][d] (+ bias[h][row0 + r][c]). BM query rows per tile
+// (128, or 64 / 32 for launches with fewer 128-row tiles than SMs: one VAE image has 64), thread
+// (rg, cg) owning rows rg + 16i (i < BM / 16) and columns cg + 16j (j < 8).
+template <bool BIAS, bool ALIGNED, int BM>
 __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
-  __shared__ __align__(16) float As[2][kBM * kAS];
+  constexpr int MI = BM / 16;
+  __shared__ __align__(16) float As[2][BM * kAS];
   __shared__ __align__(16) float Bs[2][kBN * kAS];
   const int t = blockIdx.x;
   if (t >= L.qk_total) return;
@@ -39,12 +43,12 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
   const int ktiles = (P.Lk + kBN - 1) / kBN;
   const int rt = local / ktiles;
   const int kt = local - rt * ktiles;
-  const int r0 = rt * kBM;  // within the unit
+  const int r0 = rt * BM;  // within the unit
   const int c0 = kt * kBN;
   const int D = P.D;
   const float* qbase = P.q + P.q_off + (int64_t)(u.row0 + r0) * P.ldq + (int64_t)u.h * D;
   const float* kbase = P.k + P.k_off + (int64_t)c0 * P.ldk + (int64_t)u.h * D;
-  const int nr = min(kBM, u.rows - r0);
+  const int nr = min(BM, u.rows - r0);
   const int nc = min(kBN, P.Lk - c0);
 
   const int tid = threadIdx.x;
@@ -53,13 +57,15 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
   auto load_stage = [&](int buf, int d0) {
     if (ALIGNED) {
 #pragma unroll
-      for (int it = 0; it < 2; ++it) {  // 512 float4 per operand
+      for (int it = 0; it < 2; ++it) {  // 512 float4 of K, BM * 4 of Q
         const int idx = tid + it * kGT;
         const int r = idx >> 2, c4 = idx & 3;
         const int d = d0 + c4 * 4;
-        const bool okA = (r < nr) && (d < D);
-        cp_async16(&As[buf][r * kAS + c4 * 4], okA ? (const void*)(qbase + (int64_t)r * P.ldq + d) : (const void*)qbase,
-                   okA ? 16u : 0u);
+        if (idx < BM * 4) {
+          const bool okA = (r < nr) && (d < D);
+          cp_async16(&As[buf][r * kAS + c4 * 4], okA ? (const void*)(qbase + (int64_t)r * P.ldq + d) : (const void*)qbase,
+                     okA ? 16u : 0u);
+        }
         const bool okB = (r < nc) && (d < D);
         cp_async16(&Bs[buf][r * kAS + c4 * 4], okB ? (const void*)(kbase + (int64_t)r * P.ldk + d) : (const void*)kbase,
                    okB ? 16u : 0u);
@@ -70,9 +76,11 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
         const int idx = tid + it * kGT;
         const int r = idx >> 4, c = idx & 15;
         const int d = d0 + c;
-        const bool okA = (r < nr) && (d < D);
-        cp_async4(&As[buf][r * kAS + c], okA ? (const void*)(qbase + (int64_t)r * P.ldq + d) : (const void*)qbase,
-                  okA ? 4u : 0u);
+        if (idx < BM * 16) {
+          const bool okA = (r < nr) && (d < D);
+          cp_async4(&As[buf][r * kAS + c], okA ? (const void*)(qbase + (int64_t)r * P.ldq + d) : (const void*)qbase,
+                    okA ? 4u : 0u);
+        }
         const bool okB = (r < nc) && (d < D);
         cp_async4(&Bs[buf][r * kAS + c], okB ? (const void*)(kbase + (int64_t)r * P.ldk + d) : (const void*)kbase,
                   okB ? 4u : 0u);
@@ -81,9 +89,9 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
     cp_async_commit();
   };
 
-  float acc[8][8];
+  float acc[MI][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < MI; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
@@ -105,7 +113,7 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) bf[j] = B4[j * 16 * (kAS / 4) + d4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < MI; ++i) {
         const float4 af = A4[i * 16 * (kAS / 4) + d4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -122,7 +130,7 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
   float* S = L.scratch + u.s_off;
   const float scale = P.scale;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < MI; ++i) {
     const int r = rg + 16 * i;
     if (r >= nr) continue;
     const int grow = u.row0 + r0 + r;  // query row within the problem
@@ -182,10 +190,11 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const GemmLaunch L) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// O[row0 + r][c] = sum_k P[r][k] V[k][c]
-template <bool ALIGNED>
+// O[row0 + r][c] = sum_k P[r][k] V[k][c], BM rows per tile as gemm_qk_kernel
+template <bool ALIGNED, int BM>
 __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
-  __shared__ __align__(16) float As[2][kBM * kAS];
+  constexpr int MI = BM / 16;
+  __shared__ __align__(16) float As[2][BM * kAS];
   __shared__ __align__(16) float Vt[2][kBK * kVS];
   const int t = blockIdx.x;
   if (t >= L.pv_total) return;
@@ -197,10 +206,10 @@ __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
   const int ctiles = (D + kBN - 1) / kBN;
   const int rt = local / ctiles;
   const int ct = local - rt * ctiles;
-  const int r0 = rt * kBM;
+  const int r0 = rt * BM;
   const int c0 = ct * kBN;
   const int Lk = P.Lk;
-  const int nr = min(kBM, u.rows - r0);
+  const int nr = min(BM, u.rows - r0);
   const int nc = min(kBN, D - c0);
   const float* pbase = L.scratch + u.s_off + (int64_t)r0 * u.ldS;
   const float* vbase = P.v + P.v_off + (int64_t)u.h * D + c0;
@@ -210,13 +219,15 @@ __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
 
   auto load_stage = [&](int buf, int k0) {
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {  // P tile [128][16]: scratch rows are 16-byte aligned
+    for (int it = 0; it < (BM * 4 + kGT - 1) / kGT; ++it) {  // P tile [BM][16]: scratch rows are 16-byte aligned
       const int idx = tid + it * kGT;
       const int r = idx >> 2, c4 = idx & 3;
       const int k = k0 + c4 * 4;
-      const bool ok = (r < nr) && (k < u.ldS);
-      cp_async16(&As[buf][r * kAS + c4 * 4], ok ? (const void*)(pbase + (int64_t)r * u.ldS + k) : (const void*)pbase,
-                 ok ? 16u : 0u);
+      if (idx < BM * 4) {
+        const bool ok = (r < nr) && (k < u.ldS);
+        cp_async16(&As[buf][r * kAS + c4 * 4], ok ? (const void*)(pbase + (int64_t)r * u.ldS + k) : (const void*)pbase,
+                   ok ? 16u : 0u);
+      }
     }
     if (ALIGNED) {
 #pragma unroll
@@ -240,9 +251,9 @@ __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
     cp_async_commit();
   };
 
-  float4 acc[8][2];
+  float4 acc[MI][2];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < MI; ++i) acc[i][0] = acc[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
 
   const int nstage = (Lk + kBK - 1) / kBK;
   load_stage(0, 0);
@@ -258,15 +269,15 @@ __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
     const float4* V4 = reinterpret_cast<const float4*>(Vt[st & 1]) + cg;
 #pragma unroll
     for (int k4 = 0; k4 < kBK / 4; ++k4) {
-      float4 af[8];
+      float4 af[MI];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) af[i] = A4[i * 16 * (kAS / 4) + k4];
+      for (int i = 0; i < MI; ++i) af[i] = A4[i * 16 * (kAS / 4) + k4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float4 v0 = V4[(k4 * 4 + e) * (kVS / 4)];
         const float4 v1 = V4[(k4 * 4 + e) * (kVS / 4) + 16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < MI; ++i) {
           const float pe = e == 0 ? af[i].x : e == 1 ? af[i].y : e == 2 ? af[i].z : af[i].w;
           acc[i][0].x = fmaf(pe, v0.x, acc[i][0].x);
           acc[i][0].y = fmaf(pe, v0.y, acc[i][0].y);
@@ -283,7 +294,7 @@ __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
   }
 
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < MI; ++i) {
     const int r = rg + 16 * i;
     if (r >= nr) continue;
     float* dst = P.o + P.o_off + (int64_t)(u.row0 + r0 + r) * P.ldo + (int64_t)u.h * D + c0;
@@ -307,13 +318,19 @@ __global__ void __launch_bounds__(kGT) gemm_pv_kernel(const GemmLaunch L) {
 
 cudaError_t launch_gemm_qk(bool bias, bool aligned, const GemmLaunch& L, cudaStream_t s) {
   if (L.qk_total <= 0) return cudaSuccess;
-  if (bias) {
-    if (aligned) gemm_qk_kernel<true, true><<<L.qk_total, kGT, 0, s>>>(L);
-    else gemm_qk_kernel<true, false><<<L.qk_total, kGT, 0, s>>>(L);
-  } else {
-    if (aligned) gemm_qk_kernel<false, true><<<L.qk_total, kGT, 0, s>>>(L);
-    else gemm_qk_kernel<false, false><<<L.qk_total, kGT, 0, s>>>(L);
-  }
+  auto go = [&](auto bm) {
+    constexpr int BM = decltype(bm)::value;
+    if (bias) {
+      if (aligned) gemm_qk_kernel<true, true, BM><<<L.qk_total, kGT, 0, s>>>(L);
+      else gemm_qk_kernel<true, false, BM><<<L.qk_total, kGT, 0, s>>>(L);
+    } else {
+      if (aligned) gemm_qk_kernel<false, true, BM><<<L.qk_total, kGT, 0, s>>>(L);
+      else gemm_qk_kernel<false, false, BM><<<L.qk_total, kGT, 0, s>>>(L);
+    }
+  };
+  if (L.bm == 32) go(std::integral_constant<int, 32>{});
+  else if (L.bm == 64) go(std::integral_constant<int, 64>{});
+  else go(std::integral_constant<int, 128>{});
   return cudaGetLastError();
 }
 
@@ -325,8 +342,14 @@ cudaError_t launch_softmax_rows(const GemmLaunch& L, cudaStream_t s) {
 
 cudaError_t launch_gemm_pv(bool aligned, const GemmLaunch& L, cudaStream_t s) {
   if (L.pv_total <= 0) return cudaSuccess;
-  if (aligned) gemm_pv_kernel<true><<<L.pv_total, kGT, 0, s>>>(L);
-  else gemm_pv_kernel<false><<<L.pv_total, kGT, 0, s>>>(L);
+  auto go = [&](auto bm) {
+    constexpr int BM = decltype(bm)::value;
+    if (aligned) gemm_pv_kernel<true, BM><<<L.pv_total, kGT, 0, s>>>(L);
+    else gemm_pv_kernel<false, BM><<<L.pv_total, kGT, 0, s>>>(L);
+  };
+  if (L.bm == 32) go(std::integral_constant<int, 32>{});
+  else if (L.bm == 64) go(std::integral_constant<int, 64>{});
+  else go(std::integral_constant<int, 128>{});
   return cudaGetLastError();
 }
 

@@ -104,6 +104,19 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
   if (rc) return rc;
   const int np = (int)g.size();
   const int nu = (int)units.size();
+  // FFMA score kernels: query rows per tile. A chunk with fewer Q K^T tiles of 128 rows than SMs
+  // (one VAE image: 8 x 8) takes 64- or 32-row tiles, so that every SM has work.
+  int bm = 128;
+  if (!tc) {
+    const int sms = supra::attn_fp32_warp_cta_slots() / 2;
+    auto qk_tiles = [&](int rows_per_tile) {
+      int64_t n = 0;
+      for (const GemmUnit& u : units)
+        n += (int64_t)((u.rows + rows_per_tile - 1) / rows_per_tile) * ((g[u.prob]->p.Lk + 127) / 128);
+      return n;
+    };
+    while (bm > 32 && qk_tiles(bm) < sms) bm /= 2;
+  }
   std::vector<int32_t> qk(nu + 1), pv(nu + 1), rw(nu + 1);
   int64_t tq = 0, tp = 0, tr = 0;
   double fl = 0, by_qk = 0, by_sm = 0, by_pv = 0;
@@ -116,7 +129,7 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
     qk[i] = u.qk_begin;
     pv[i] = u.pv_begin;
     rw[i] = u.row_begin;
-    const int rt = (u.rows + 127) / 128;
+    const int rt = (u.rows + bm - 1) / bm;
     tq += (int64_t)rt * ((P.Lk + 127) / 128);
     tp += (int64_t)rt * ((P.D + 127) / 128);
     tr += u.rows;
@@ -166,6 +179,7 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
   L.status = c->d_status;
   L.lo = tc == 2 ? c->scratch + scratch_bytes / 4 : nullptr;
   L.sm_scale = tc ? 1 : 0;
+  L.bm = bm;
   cudaError_t e;
   if (tc) {
     // S = Q_h K_h^T (unscaled: the softmax applies the scale) for each unit's rows into its

@@ -70,6 +70,7 @@ struct GemmLaunch {
   // lo at the same offset from lo (the operand of the split-precision P V).
   float* lo = nullptr;
   int32_t sm_scale = 0;
+  int32_t bm = 128;  // query rows per tile of the FFMA score kernels: 128, 64 or 32 (qk/pv prefixes count those)
   int32_t n_units;
   int32_t qk_total, pv_total, row_total;
   int32_t* status;

@@ -635,3 +635,15 @@ def test_batch_hazards_fall_back_to_ordered_recording(gpu):
     gpu.sync()
     assert_close(host(o2), r2)
     assert_close(host(o1), r3)
+
+
+@pytest.mark.parametrize("Lq,Lk,H,D,bias", [
+    (1024, 2048, 1, 256, False),  # 8 x 16 tiles of 128 rows: 64-row tiles (256 of them)
+    (1000, 2000, 1, 192, True),   # the same with a bias and a ragged last row tile
+    (1024, 1024, 1, 512, False),  # one VAE image: 32-row tiles
+])
+def test_score_path_small_launch_tiles(gpu, Lq, Lk, H, D, bias):
+    """The FFMA score path (head dims above 128) takes 64- or 32-row tiles when a launch has
+    fewer 128-row Q K^T tiles than SMs; against the float64 oracle."""
+    rng = np.random.default_rng(Lq + D)
+    run_and_check(gpu, rand_problem(rng, Lq, Lk, H, D, bias=bias), scale=(64.0 / D) ** 0.5 if bias else None)

@@ -39,6 +39,13 @@ def test_call_site_shards():
     assert bench.site_shard(2, 0, 1, shardable=False) == ([0, 1], False)
 
 
+def test_cpulist_parsing():
+    """bench.py pins each rank to its GPU's local CPUs, read from sysfs lists like these."""
+    assert bench.parse_cpulist("0-3,8,10-11") == {0, 1, 2, 3, 8, 10, 11}
+    assert bench.parse_cpulist("0-47,96-143\n".strip()) == set(range(48)) | set(range(96, 144))
+    assert bench.parse_cpulist("") == set()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
