@@ -59,24 +59,50 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
   }
   begin[n] = (int32_t)total;
+  // 16-byte aligned operands (the group's `aligned`) are staged by TMA: a tensor map of x [M, K]
+  // with 20 x 128 boxes and of W [N, K] with 20 x (tile columns) boxes per problem, cached per
+  // context like the attention kernels' maps
+  bool tma = g[0]->aligned;
+  std::vector<CUtensorMap> maps;
+  std::vector<supra::LinProb> lp((size_t)n);
+  ++c->map_epoch;
+  for (int i = 0; i < n; ++i) {
+    lp[i] = g[i]->lin;
+    lp[i].n_tiles = (lp[i].N + cols - 1) / cols;
+    if (tma) {
+      const supra::LinProb& q = lp[i];
+      int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.x), q.ldx, q.M, q.K, 20, 128, 0, 0}, maps, &lp[i].mx);
+      if (!rc0)
+        rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, 20, cols, 0, 0}, maps, &lp[i].mw);
+      if (rc0) {  // a shape the driver's encoder refuses: the group runs the per-thread copy form
+        tma = false;
+        maps.clear();
+        c->err.clear();
+      }
+    }
+  }
+  const size_t mbytes = sizeof(CUtensorMap) * maps.size();
   const size_t pbytes = align16(sizeof(supra::LinProb) * n);
   const size_t bbytes = sizeof(int32_t) * (n + 1);
   char *h = nullptr, *dv = nullptr;
-  int rc = ring_reserve(c, pbytes + bbytes, &h, &dv);
+  int rc = ring_reserve(c, 64 + mbytes + pbytes + bbytes, &h, &dv);
   if (rc) return rc;
-  supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(h);
-  for (int i = 0; i < n; ++i) {
-    hp[i] = g[i]->lin;
-    hp[i].n_tiles = (hp[i].N + cols - 1) / cols;
-  }
+  // tensor maps first, on a 64-byte boundary in device memory
+  const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
+  char* hm = h + pad;
+  char* dm = dv + pad;
+  if (mbytes) std::memcpy(hm, maps.data(), mbytes);
+  supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(hm + mbytes);
+  std::memcpy(hp, lp.data(), sizeof(supra::LinProb) * n);
   rc = norm_stats(c, g, hp);
   if (rc) return rc;
-  std::memcpy(h + pbytes, begin.data(), bbytes);
-  rc = ring_commit(c, h, dv, pbytes + bbytes);
+  std::memcpy(hm + mbytes + pbytes, begin.data(), bbytes);
+  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
   if (rc) return rc;
   supra::LinLaunch L;
-  L.probs = reinterpret_cast<const supra::LinProb*>(dv);
-  L.begin = reinterpret_cast<const int32_t*>(dv + pbytes);
+  L.maps = reinterpret_cast<const CUtensorMap*>(dm);
+  L.probs = reinterpret_cast<const supra::LinProb*>(dm + mbytes);
+  L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes);
   L.n = n;
   L.total = (int32_t)total;
   L.status = c->d_status;
@@ -84,7 +110,8 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = supra::launch_linear_fp32(g[0]->bias, g[0]->aligned, cols, L, c->stream);
+    e = tma ? supra::launch_linear_fp32_tma(g[0]->bias, cols, L, c->stream)
+            : supra::launch_linear_fp32(g[0]->bias, false, cols, L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;

@@ -188,6 +188,9 @@ struct alignas(16) LinProb {
   int32_t gn_rows;   // rows per image
   int32_t gn_groups;
   int32_t gn_silu;
+  int32_t mx, mw;    // the TMA-staged FFMA kernel: tensor maps of x ([M, K], boxes 20 x 128) and W
+                     // ([N, K], boxes 20 x tile columns) in LinLaunch::maps; unused elsewhere
+  int32_t pad_[2];
 };
 static_assert(sizeof(LinProb) % 16 == 0, "LinProb is packed into the descriptor ring");
 
@@ -198,9 +201,13 @@ struct LinLaunch {
   const int32_t* begin;
   int32_t n, total;
   int32_t* status;
+  const CUtensorMap* maps = nullptr;  // the TMA-staged form's tensor maps
 };
 // tile_cols: 128 or 64 columns per 128-row tile (LinProb::n_tiles counts tiles of that width)
 cudaError_t launch_linear_fp32(bool bias, bool aligned, int tile_cols, const LinLaunch& L, cudaStream_t s);
+// The same with the x and W tiles staged by TMA tensor copies (x and W 16-byte aligned, row strides
+// of a multiple of 4 floats; LinProb::mx / mw index L.maps).
+cudaError_t launch_linear_fp32_tma(bool bias, int tile_cols, const LinLaunch& L, cudaStream_t s);
 // GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
 // group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
 // mean in a second pass (app/gpu/kernels.js:117-139).

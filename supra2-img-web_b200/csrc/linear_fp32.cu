@@ -17,6 +17,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace supra {
 namespace {
@@ -35,11 +36,183 @@ constexpr int stages_of() { return BN == 64 ? 4 : 2; }
 // dynamic shared memory of the form (the two-stage form's arrays are static)
 template <int BN>
 constexpr int smem_bytes() { return stages_of<BN>() == 2 ? 0 : stages_of<BN>() * (kBM + BN) * kS * 4; }
+// the TMA-staged form: four stages in flight, 128-byte aligned boxes, one mbarrier per stage
+constexpr int kTmaStages = 4;
+template <int BN>
+constexpr int tma_smem_bytes() { return 128 + kTmaStages * (kBM + BN) * kS * 4 + kTmaStages * 8; }
+
+// GroupNorm (+ SiLU) or LayerNorm (+ modulation) of a staged x tile `a` (stage st of the tile at
+// rows r0.., nr of them valid), per element of a valid row and column (padding stays zero):
+// (x - mean) * rstd * g + b with g, b = gamma, beta (app/gpu/kernels.js:141-162), 1 + scale, shift
+// (app/gpu/kernels.js:111) or 1, 0. Thread tid normalises column kk = tid % 16 of the stage in rows
+// tid / 16 + 16 i: its column's g, b and group are one lookup per stage, its rows' images one per
+// tile. (Per element, with two integer divisions and three global loads, it cost as much as the
+// stage's FMAs.)
+__device__ __forceinline__ void norm_stage(const LinProb& P, float* a, int st, int r0, int nr, int tid) {
+  const int kk = tid & 15, rb = tid >> 4;
+  const int k = st * kBK + kk;
+  if (k >= P.K) return;
+  float g = 1.f, b = 0.f;
+  if (P.gn_mode != kNormPlain) {
+    g = __ldg(P.gamma + k);
+    b = __ldg(P.beta + k);
+    if (P.gn_mode == kNormModulated) g = 1.f + g;
+  }
+  const float2* st_k = P.gn_stats + k / P.gn_cg;  // the column's group
+  // a row's image: one for the whole tile when images are whole tiles (the VAE's 1024-row
+  // images), the row itself for a LayerNorm
+  const bool one_img = P.gn_rows % kBM == 0;
+  const int img0 = one_img ? r0 / P.gn_rows : 0;
+#pragma unroll
+  for (int it = 0; it < kBM / 16; ++it) {
+    const int r = rb + 16 * it;
+    if (r < nr) {
+      const int img = one_img ? img0 : (P.gn_rows == 1 ? r0 + r : (r0 + r) / P.gn_rows);
+      const float2 ms = __ldg(st_k + (int64_t)img * P.gn_groups);
+      float v = (a[r * kS + kk] - ms.x) * (ms.y * g) + b;
+      if (P.gn_silu) v = v / (1.f + __expf(-v));
+      a[r * kS + kk] = v;
+    }
+  }
+}
+
+// acc += the stage's x tile (rows rg + 16i) times its W tile (rows cg + 16j), kBK deep
+template <int NJ>
+__device__ __forceinline__ void mma_stage(const float* a, const float* b, int rg, int cg, float (&acc)[8][NJ]) {
+  const float4* A4 = reinterpret_cast<const float4*>(a) + rg * (kS / 4);
+  const float4* B4 = reinterpret_cast<const float4*>(b) + cg * (kS / 4);
+#pragma unroll
+  for (int k4 = 0; k4 < kBK / 4; ++k4) {
+    float4 bf[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 af = A4[i * 16 * (kS / 4) + k4];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        acc[i][j] = fmaf(af.x, bf[j].x, acc[i][j]);
+        acc[i][j] = fmaf(af.y, bf[j].y, acc[i][j]);
+        acc[i][j] = fmaf(af.z, bf[j].z, acc[i][j]);
+        acc[i][j] = fmaf(af.w, bf[j].w, acc[i][j]);
+      }
+    }
+  }
+}
+
+// y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
+template <bool BIAS, int NJ>
+__device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&acc)[8][NJ], int r0, int c0, int nr,
+                                                int nc, int rg, int cg) {
+  float bias[NJ], gate[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
+    gate[j] = (P.gate && cg + 16 * j < nc) ? __ldg(P.gate + c0 + cg + 16 * j) : 1.f;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = rg + 16 * i;
+    if (r >= nr) continue;
+    float* yrow = P.y + (int64_t)(r0 + r) * P.ldy + c0;
+    // resid may be y itself (in place): each element is read and then written by this thread only
+    const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int c = cg + 16 * j;
+      if (c < nc) {
+        float v = acc[i][j] + bias[j];
+        if (P.act != kActNone) v = linear_act(P.act, v);
+        if (P.gate) v *= gate[j];
+        yrow[c] = rrow ? rrow[c] + v : v;
+      }
+    }
+  }
+}
 
 // BN: columns per tile, 128 or 64 (the host picks per launch the width that fills the last wave
 // of tiles best: the DiT blocks' N = 576 products are 320 tiles of 128 x 128, 1.08 waves of the
 // 296 CTA slots, against 576 tiles of 128 x 64). Thread (rg, cg) owns rows rg + 16i (i < 8) and
 // columns cg + 16j (j < BN / 16).
+
+// Tiles staged by TMA (x and W 16-byte aligned with row strides of a multiple of 4 floats): per
+// stage thread 0 issues two tensor copies, a [128 x 20] box of x and a [BN x 20] box of W (the 4
+// columns past the stage's 16 pad the shared-memory rows against bank conflicts and are never
+// read; past K and past the last row the copies read zeros), completing on the stage's mbarrier,
+// kStages - 1 stages ahead. The 256 threads only compute: the per-thread cp.async form spent a
+// third of its issue slots on copy addresses and predicates.
+template <bool BIAS, int BN>
+__global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_constant__ LinLaunch L) {
+  constexpr int NJ = BN / 16;
+  extern __shared__ uint8_t lin_raw[];
+  const uint32_t raw = smem_u32(lin_raw);
+  float* const As = reinterpret_cast<float*>(lin_raw + (((raw + 127u) & ~127u) - raw));  // [kTmaStages][kBM * kS]
+  float* const Bs = As + kTmaStages * kBM * kS;                                                  // [kTmaStages][BN * kS]
+  uint64_t* const full = reinterpret_cast<uint64_t*>(Bs + kTmaStages * BN * kS);                // [kTmaStages]
+  const int t = blockIdx.x;
+  if (t >= L.total) {
+    if (threadIdx.x == 0) report_error(L.status, DEV_BAD_TILE, 30);
+    return;
+  }
+  const int pi = find_problem(L.begin, L.n, t);
+  const LinProb& P = L.probs[pi];
+  const int local = t - __ldg(L.begin + pi);
+  const int rt = local / P.n_tiles;
+  const int r0 = rt * kBM;
+  const int c0 = (local - rt * P.n_tiles) * BN;
+  const int nr = min(kBM, P.M - r0);
+  const int nc = min(BN, P.N - c0);
+  const int nstage = (P.K + kBK - 1) / kBK;
+  const CUtensorMap* mx = L.maps + P.mx;
+  const CUtensorMap* mw = L.maps + P.mw;
+  const int tid = threadIdx.x;
+  const int rg = tid >> 4, cg = tid & 15;
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kTmaStages; ++s) mbar_init(&full[s], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  auto issue = [&](int st) {  // (thread 0)
+    if (st < nstage) {
+      const int buf = st % kTmaStages;
+      mbar_arrive_expect_tx(&full[buf], (uint32_t)((kBM + BN) * kS * 4));
+      tc::tma_load_2d(As + buf * kBM * kS, mx, st * kBK, r0, &full[buf]);
+      tc::tma_load_2d(Bs + buf * BN * kS, mw, st * kBK, c0, &full[buf]);
+    }
+  };
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kTmaStages; ++s) issue(s);
+  }
+  float acc[8][NJ];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
+  for (int st = 0; st < nstage; ++st) {
+    const int buf = st % kTmaStages;
+    // every thread waits for the stage (bounded); a vote keeps the CTA together if a wait runs out
+    const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)((st / kTmaStages) & 1));
+    if (!__syncthreads_and(ok)) {
+      if (tid == 0) report_error(L.status, DEV_TIMEOUT, 31, st);
+      return;
+    }
+    float* a = As + buf * kBM * kS;
+    if (P.gn_stats) {
+      norm_stage(P, a, st, r0, nr, tid);
+      __syncthreads();
+    }
+    mma_stage<NJ>(a, Bs + buf * BN * kS, rg, cg, acc);
+    fence_proxy_async_smem();  // this thread's reads (and norm writes) of the buffer before the next copy
+    __syncthreads();           // every thread is done with the buffer
+    if (tid == 0) issue(st + kTmaStages);
+  }
+  linear_epilogue<BIAS, NJ>(P, acc, r0, c0, nr, nc, rg, cg);
+}
+
+// The same product with the tiles staged by per-thread cp.async (any alignment: 4-byte copies
+// when rows are not 16-byte aligned).
 template <bool BIAS, bool ALIGNED, int BN>
 __global__ void __launch_bounds__(kT, BN == 64 ? 3 : 2) linear_fp32_kernel(const LinLaunch L) {
   constexpr int NJ = BN / 16;
@@ -144,87 +317,13 @@ __global__ void __launch_bounds__(kT, BN == 64 ? 3 : 2) linear_fp32_kernel(const
       else cp_async_commit();
     }
     if (P.gn_stats) {
-      // GroupNorm (+ SiLU) or LayerNorm (+ modulation) of the staged x tile, per element of a
-      // valid row and column (padding stays zero): (x - mean) * rstd * g + b with g, b = gamma,
-      // beta (app/gpu/kernels.js:141-162), 1 + scale, shift (app/gpu/kernels.js:111) or 1, 0.
-      // Thread tid normalises column kk = tid % 16 of the stage in rows tid / 16 + 16 i: its
-      // column's g, b and group are one lookup per stage, its rows' images one per tile.
-      float* a = As + buf * kBM * kS;
-      const int kk = tid & 15, rb = tid >> 4;
-      const int k = st * kBK + kk;
-      if (k < K) {
-        float g = 1.f, b = 0.f;
-        if (P.gn_mode != kNormPlain) {
-          g = __ldg(P.gamma + k);
-          b = __ldg(P.beta + k);
-          if (P.gn_mode == kNormModulated) g = 1.f + g;
-        }
-        const float2* st_k = P.gn_stats + k / P.gn_cg;  // the column's group
-        // a row's image: one for the whole tile when images are whole tiles (the VAE's 1024-row
-        // images), the row itself for a LayerNorm
-        const bool one_img = P.gn_rows % kBM == 0;
-        const int img0 = one_img ? r0 / P.gn_rows : 0;
-#pragma unroll
-        for (int it = 0; it < kBM / 16; ++it) {
-          const int r = rb + 16 * it;
-          if (r < nr) {
-            const int img = one_img ? img0 : (P.gn_rows == 1 ? r0 + r : (r0 + r) / P.gn_rows);
-            const float2 ms = __ldg(st_k + (int64_t)img * P.gn_groups);
-            float v = (a[r * kS + kk] - ms.x) * (ms.y * g) + b;
-            if (P.gn_silu) v = v / (1.f + __expf(-v));
-            a[r * kS + kk] = v;
-          }
-        }
-      }
+      norm_stage(P, As + buf * kBM * kS, st, r0, nr, tid);
       __syncthreads();
     }
-    const float4* A4 = reinterpret_cast<const float4*>(As + buf * kBM * kS) + rg * (kS / 4);
-    const float4* B4 = reinterpret_cast<const float4*>(Bs + buf * BN * kS) + cg * (kS / 4);
-#pragma unroll
-    for (int k4 = 0; k4 < kBK / 4; ++k4) {
-      float4 bf[NJ];
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 af = A4[i * 16 * (kS / 4) + k4];
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          acc[i][j] = fmaf(af.x, bf[j].x, acc[i][j]);
-          acc[i][j] = fmaf(af.y, bf[j].y, acc[i][j]);
-          acc[i][j] = fmaf(af.z, bf[j].z, acc[i][j]);
-          acc[i][j] = fmaf(af.w, bf[j].w, acc[i][j]);
-        }
-      }
-    }
+    mma_stage<NJ>(As + buf * kBM * kS, Bs + buf * BN * kS, rg, cg, acc);
     if constexpr (kStages == 2) __syncthreads();  // the next iteration's load overwrites this buffer
   }
-
-  // y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
-  float bias[NJ], gate[NJ];
-#pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
-    gate[j] = (P.gate && cg + 16 * j < nc) ? __ldg(P.gate + c0 + cg + 16 * j) : 1.f;
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = rg + 16 * i;
-    if (r >= nr) continue;
-    float* yrow = P.y + (int64_t)(r0 + r) * P.ldy + c0;
-    // resid may be y itself (in place): each element is read and then written by this thread only
-    const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const int c = cg + 16 * j;
-      if (c < nc) {
-        float v = acc[i][j] + bias[j];
-        if (P.act != kActNone) v = linear_act(P.act, v);
-        if (P.gate) v *= gate[j];
-        yrow[c] = rrow ? rrow[c] + v : v;
-      }
-    }
-  }
+  linear_epilogue<BIAS, NJ>(P, acc, r0, c0, nr, nc, rg, cg);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -319,6 +418,23 @@ cudaError_t launch_linear_fp32(bool bias, bool aligned, int tile_cols, const Lin
   };
   if (tile_cols == 64) pick(std::integral_constant<int, 64>{});
   else pick(std::integral_constant<int, 128>{});
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t launch_linear_fp32_tma(bool bias, int tile_cols, const LinLaunch& L, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
+  auto go = [&](auto kern, int bytes) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) kern<<<L.total, kT, bytes, s>>>(L);
+  };
+  if (tile_cols == 64) {
+    if (bias) go(linear_fp32_tma_kernel<true, 64>, tma_smem_bytes<64>());
+    else go(linear_fp32_tma_kernel<false, 64>, tma_smem_bytes<64>());
+  } else {
+    if (bias) go(linear_fp32_tma_kernel<true, 128>, tma_smem_bytes<128>());
+    else go(linear_fp32_tma_kernel<false, 128>, tma_smem_bytes<128>());
+  }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

@@ -59,9 +59,10 @@ def test_context_preparation_golden(gpu, golden):
     "M,N,K,bias",
     [(1, 1, 1, False), (1, 1152, 576, True), (37, 576, 768, True), (130, 129, 33, True), (257, 1000, 64, False),
      (128, 128, 16, True), (300, 16128, 576, True), (1000, 7, 3, True),
-     # 288 tiles of 128 x 128 (one wave of the 296 CTA slots) against 576 of 128 x 64 (two): the
-     # 128-column form; the cases above take the 64-column one
-     (2048, 2304, 64, True), (2048, 2301, 33, False)],
+     # the 128-column tile form (one 288-tile wave), and the 64-column form chosen for the DiT
+     # blocks' N = 576 products (576 tiles against 320); the smaller cases above take the 64-column
+     # form too (one wave either way, the narrower tile cheaper)
+     (2048, 2304, 64, True), (2048, 2301, 33, False), (8192, 576, 64, True), (8192, 570, 33, False)],
 )
 def test_linear_shapes(gpu, M, N, K, bias):
     import supra_attn
