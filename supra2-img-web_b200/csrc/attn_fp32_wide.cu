@@ -1,0 +1,451 @@
+// Fused FP32 attention, persistent kernel for large unbiased launches (sm_100a): D = 64, scale > 0,
+// no score bias. The DiT self- and cross-attention launches (app/models/dit.js:172,184) when they
+// hold enough 256-row tiles to fill the device; smaller launches, and the T5 encoder's biased
+// ones, run on attn_fp32_warp.cu.
+//
+// Same algorithm as attn_fp32_warp.cu (online softmax over key blocks, app/gpu/kernels.js:164-316,
+// persistent CTAs claiming tiles from a counter, a K/V ring that runs across tiles, lazy exp2
+// offsets), with a larger register block per lane for Q K^T:
+//  * One CTA per SM, 8 warps x 32 query rows: a tile is 256 query rows of one head, so the DiT's
+//    K/V blocks are read once per (sequence, head).
+//  * 64-key blocks. Lane (rg = lane/8, cg = lane%8) of warp w owns rows 32w + rg + 4i (i < 8),
+//    keys cg + 8j (j < 8) of each block, and output columns 4cg .. +3, 32 + 4cg .. +3: 8x8 score
+//    and 8x8 output register blocks. With 8 keys per lane instead of 4, each Q fragment load feeds
+//    twice the products: per four head-dim steps a lane loads 8 Q and 8 K float4 fragments for
+//    128 packed FMAs (attn_fp32_warp.cu: 12 loads for 64), and the Q K^T loop runs at about the
+//    rate of the P V loop (80 % of the FMA pipe in isolation at two warps per scheduler, against
+//    71 % for the 8x4 block).
+//  * Row-pair packing: a packed f32x2 FMA multiplies the Q values of two of the lane's rows by one
+//    K value (broadcast) into the two rows' scores of that key, so a score needs one register.
+//    For that the warp transposes its 32 Q rows in place once per tile (Q^T [64 d][32]): the two
+//    rows of a pair must sit side by side. Position 8rg + i of a Q^T row holds row rg + 4i, so a
+//    lane's 8 rows are two float4 loads and pairs (i, i+1) are the halves of a float4.
+//  * Operands by TMA tensor copies with the same tensor maps as attn_fp32_warp.cu: a warp's Q rows
+//    as one [32 x 68] box, a K/V block as two [32 x 68] K and two [32 x 64] V boxes (the second
+//    pair only if the block has keys past 32). Two stages (211 KB of shared memory with the P
+//    rows); the last of the 8 warps to finish a stage issues the block two ahead into it.
+//  * Ragged last blocks: keys past Lk take -inf scores (a select), blocks of at most 32 keys run
+//    the Q K^T of the first 32 keys only, and P V skips the 4-key groups past Lk (V rows past Lk
+//    are never read).
+//  * All waits are bounded (2 s); a timeout sets the device status word and the warp leaves.
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace supra {
+namespace {
+
+constexpr int kW = 8;              // warps per CTA
+constexpr int kRI = 8;             // query rows per lane
+constexpr int kRowsW = 4 * kRI;    // query rows per warp
+constexpr int kRows = kW * kRowsW; // query rows per tile
+constexpr int kNK = 64;            // keys per block
+constexpr int kBox = kFwBoxRows;   // rows per TMA box (32): a block is two K and two V boxes
+constexpr int kNS = 2;             // K/V stages
+constexpr int kD = 64;             // head dim
+constexpr int kQS = kFwBoxWide;    // Q box row stride in shared memory (floats)
+constexpr int kKS = kFwBoxWide;    // K row stride
+constexpr int kVS = kFwBoxNarrow;  // V row stride
+constexpr int kTS = kRowsW;        // Q^T row stride: 32 positions (conflict-free float4 reads)
+constexpr int kPS = kNK + 8;       // P row stride: conflict-free scalar writes and float4 reads
+static_assert(kRowsW == kBox, "one Q box per warp");
+static_assert(kD * kTS <= kRowsW * kQS, "Q^T fits in the warp's Q box");
+
+constexpr uint32_t kQBytes = kRowsW * kQS * 4;
+constexpr uint32_t kKBoxBytes = kBox * kKS * 4;
+constexpr uint32_t kVBoxBytes = kBox * kVS * 4;
+
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + kW * kRowsW * kQS;
+constexpr int OFF_V = OFF_K + kNS * kNK * kKS;
+constexpr int OFF_P = OFF_V + kNS * kNK * kVS;
+constexpr int FLOATS = OFF_P + kW * kRowsW * kPS;
+static_assert((OFF_K * 4) % 128 == 0 && (OFF_V * 4) % 128 == 0 && (OFF_P * 4) % 128 == 0 && kQBytes % 128 == 0 &&
+                  kKBoxBytes % 128 == 0 && kVBoxBytes % 128 == 0,
+              "TMA destinations are 128-byte aligned");
+
+struct Cursor {
+  int32_t t, b, nblk, Lk, mk, mv, kx, ky, vx, vy;
+  int32_t k;  // the tile's position in the CTA's tile sequence
+};
+constexpr int kTileSlots = 8;
+struct Ctl {
+  uint64_t qbar[kW];
+  uint64_t full[kNS];
+  int32_t cnt[kNS];
+  Cursor cur;
+  int32_t tiles[kTileSlots];
+};
+constexpr int BYTES = FLOATS * 4 + (int)sizeof(Ctl) + 128;
+static_assert(BYTES <= 232448, "shared memory per CTA");
+
+struct Tile {
+  const TmaProb* p;
+  int h, q0;
+};
+// Within a problem, tile local = h * q_tiles + query tile (TmaProb::q_tiles counts 256-row tiles).
+__device__ __forceinline__ Tile tile_of(const TmaLaunch& L, int t) {
+  const int pidx = L.uniform > 0 ? t / L.uniform : find_problem(L.begin, L.n, t);
+  const int local = t - (L.uniform > 0 ? pidx * L.uniform : __ldg(L.begin + pidx));
+  Tile r;
+  r.p = L.probs + pidx;
+  const int qt = r.p->q_tiles;
+  r.h = local / qt;
+  r.q0 = (local - r.h * qt) * kRows;
+  return r;
+}
+
+__device__ __forceinline__ void cursor_at(const TmaLaunch& L, Cursor& c, int t) {
+  const Tile T = tile_of(L, t);
+  c.t = t;
+  c.b = 0;
+  c.Lk = T.p->Lk;
+  c.nblk = (c.Lk + kNK - 1) / kNK;
+  c.mk = T.p->mk;
+  c.mv = T.p->mv;
+  c.kx = T.p->kx + T.h * kD;
+  c.ky = T.p->ky;
+  c.vx = T.p->vx + T.h * kD;
+  c.vy = T.p->vy;
+}
+
+// Issues the cursor's block into stage s and advances the cursor (one thread); with a tile's last
+// block it first claims and publishes the CTA's next tile (as attn_fp32_warp.cu).
+__device__ __forceinline__ void issue_next(const TmaLaunch& L, Ctl* C, float* Ks, float* Vs, int s) {
+  Cursor& c = C->cur;
+  if (c.t >= L.total) return;
+  int tn = 0;
+  if (c.b + 1 == c.nblk) {
+    tn = (int)gridDim.x + atomicAdd(L.next_tile, 1);
+    C->tiles[(c.k + 1) % kTileSlots] = tn;
+  }
+  const int y0 = c.b * kNK;
+  const bool two = c.Lk - y0 > kBox;  // keys past the first 32 of the block
+  uint64_t* bar = &C->full[s];
+  mbar_arrive_expect_tx(bar, (kKBoxBytes + kVBoxBytes) * (two ? 2u : 1u));
+  float* kd = Ks + s * kNK * kKS;
+  float* vd = Vs + s * kNK * kVS;
+  tc::tma_load_2d(kd, L.maps + c.mk, c.kx, c.ky + y0, bar);
+  tc::tma_load_2d(vd, L.maps + c.mv, c.vx, c.vy + y0, bar);
+  if (two) {
+    tc::tma_load_2d(kd + kBox * kKS, L.maps + c.mk, c.kx, c.ky + y0 + kBox, bar);
+    tc::tma_load_2d(vd + kBox * kVS, L.maps + c.mv, c.vx, c.vy + y0 + kBox, bar);
+  }
+  if (++c.b == c.nblk) {
+    ++c.k;
+    if (tn < L.total) cursor_at(L, c, tn);
+    else c.t = tn;
+  }
+}
+
+__device__ __forceinline__ void issue_q(const TmaLaunch& L, const Tile& T, int w, float* dst, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, kQBytes);
+  tc::tma_load_2d(dst, L.maps + T.p->mq, T.p->qx + T.h * kD, T.p->qy + T.q0 + w * kRowsW, bar);
+}
+
+// The warp's Q box [32 rows][68] -> Q^T [64 d][32] in place: lane l holds row l's 64 values (all
+// loads before any store), then writes column d of Q^T at position 8 (l % 4) + l / 4.
+__device__ __forceinline__ void transpose_q(float* Qw, int lane) {
+  const float4* src = reinterpret_cast<const float4*>(Qw + lane * kQS);
+  float4 r[kD / 4];
+#pragma unroll
+  for (int c = 0; c < kD / 4; ++c) r[c] = src[c];
+  __syncwarp();
+  float* dst = Qw + 8 * (lane & 3) + (lane >> 2);
+#pragma unroll
+  for (int c = 0; c < kD / 4; ++c) {
+    dst[(4 * c + 0) * kTS] = r[c].x;
+    dst[(4 * c + 1) * kTS] = r[c].y;
+    dst[(4 * c + 2) * kTS] = r[c].z;
+    dst[(4 * c + 3) * kTS] = r[c].w;
+  }
+  __syncwarp();
+}
+
+// S = Q K^T for keys cg + 8j (j < NJ) of one block: acc[p][j] holds the scores of rows rg + 8p
+// (x) and rg + 8p + 4 (y) for key cg + 8j.
+template <int NJ>
+__device__ __forceinline__ void qk_block(const float4* __restrict__ QT4, const float4* __restrict__ K4,
+                                         float2 (&acc)[4][8]) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[p][j] = make_float2(0.f, 0.f);
+#pragma unroll 2
+  for (int d4 = 0; d4 < kD / 4; ++d4) {
+    float4 kf[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) kf[j] = K4[j * 8 * (kKS / 4) + d4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 q0 = QT4[(4 * d4 + e) * (kTS / 4)];
+      const float4 q1 = QT4[(4 * d4 + e) * (kTS / 4) + 1];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const float kv = e == 0 ? kf[j].x : e == 1 ? kf[j].y : e == 2 ? kf[j].z : kf[j].w;
+        const float2 k2 = make_float2(kv, kv);
+        acc[0][j] = __ffma2_rn(make_float2(q0.x, q0.y), k2, acc[0][j]);
+        acc[1][j] = __ffma2_rn(make_float2(q0.z, q0.w), k2, acc[1][j]);
+        acc[2][j] = __ffma2_rn(make_float2(q1.x, q1.y), k2, acc[2][j]);
+        acc[3][j] = __ffma2_rn(make_float2(q1.z, q1.w), k2, acc[3][j]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float score(const float2 (&acc)[4][8], int i, int j) {
+  return (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
+}
+
+__global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid_constant__ TmaLaunch L) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  float* smem = reinterpret_cast<float*>(smem_raw + (((raw + 127u) & ~127u) - raw));
+  float* Ks = smem + OFF_K;
+  float* Vs = smem + OFF_V;
+  Ctl* C = reinterpret_cast<Ctl*>(smem + FLOATS);
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  const int rg = lane >> 3;
+  const int cg = lane & 7;
+  float* Qw = smem + OFF_Q + w * kRowsW * kQS;
+  float* Pw = smem + OFF_P + w * kRowsW * kPS;
+
+  const int t0 = blockIdx.x;
+  if (t0 >= L.total) {  // the host sizes the grid to at most one CTA per tile
+    if (tid == 0) report_error(L.status, DEV_BAD_TILE, 30);
+    return;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kW; ++i) mbar_init(&C->qbar[i], 1);
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&C->full[s], 1);
+      C->cnt[s] = 0;
+    }
+    mbar_fence_init();
+    C->tiles[0] = t0;
+    C->cur.k = 0;
+  }
+  __syncthreads();  // the kernel's only block-wide barrier
+  if (tid == 0) {
+    cursor_at(L, C->cur, t0);
+    for (int s = 0; s < kNS; ++s) issue_next(L, C, Ks, Vs, s);
+  }
+  Tile T = tile_of(L, t0);
+  if (lane == 0) issue_q(L, T, w, Qw, &C->qbar[w]);
+
+  const float4* QT4 = reinterpret_cast<const float4*>(Qw) + 2 * rg;
+  const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
+  uint32_t g = 0;  // position in the CTA's K/V block sequence
+  uint32_t k = 0;  // position in the CTA's tile sequence
+  for (int t = t0; t < L.total; ++k) {
+    const TmaProb* __restrict__ pp = T.p;
+    int Lk = pp->Lk;
+    float sl2 = pp->scale_log2;
+    asm volatile("" : "+r"(Lk), "+f"(sl2));
+    const int nb = (Lk + kNK - 1) / kNK;
+    const int64_t ldo = pp->ldo;
+    const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
+    const bool active = kRowsW * w < pp->Lq - T.q0;  // (warp-uniform) the warp holds a row below Lq
+    float* const orow = pp->o + pp->o_off + ((int64_t)T.q0 + kRowsW * w + rg) * ldo + (int64_t)T.h * kD + 4 * cg;
+    int tn = L.total;
+    Tile Tn = T;
+
+    float2 o[kRI][4];
+    float mo[kRI], l[kRI];
+#pragma unroll
+    for (int i = 0; i < kRI; ++i) {
+      mo[i] = -INFINITY;
+      l[i] = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o[i][u] = make_float2(0.f, 0.f);
+    }
+    if (!mbar_wait_bounded(&C->qbar[w], k & 1u)) {
+      if (lane == 0) report_error(L.status, DEV_TIMEOUT, 31, (int32_t)k);
+      return;
+    }
+    if (active) transpose_q(Qw, lane);
+
+    for (int j = 0; j < nb; ++j, ++g) {
+      const int s = (int)(g % kNS);
+      const uint32_t par = (g / kNS) & 1u;
+      const int nk = min(kNK, Lk - j * kNK);
+      if (!mbar_wait_bounded(&C->full[s], par)) {
+        if (lane == 0) report_error(L.status, DEV_TIMEOUT, 32, (int32_t)g);
+        return;
+      }
+      if (j == nb - 1) {
+        tn = *reinterpret_cast<volatile const int32_t*>(&C->tiles[(k + 1) % kTileSlots]);
+        if (tn < L.total) Tn = tile_of(L, tn);
+      }
+      const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
+      const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
+
+      // ---- S = Q K^T (the first 32 keys only when the block has no more)
+      float2 acc[4][8];
+      if (active) {
+        if (nk > kBox) qk_block<8>(QT4, K4, acc);
+        else qk_block<4>(QT4, K4, acc);
+      }
+      if (j == nb - 1 && tn < L.total) {  // this warp's Q^T is done: fetch its next Q rows
+        __syncwarp();
+        if (lane == 0) {
+          fence_proxy_async_smem();
+          issue_q(L, Tn, w, Qw, &C->qbar[w]);
+        }
+      }
+      if (active) {
+        if (nk < kNK) {  // ragged block (warp-uniform): keys past Lk get -inf (a select, not a product)
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+              if (cg + 8 * jj >= nk) acc[p][jj] = make_float2(-INFINITY, -INFINITY);
+        }
+        // ---- softmax with a lazily moved exp2 offset (as attn_fp32_warp.cu): the row maxima are
+        // reduced across the row's 8 lanes only when some score exceeds its row's offset by 8
+        float lmax[kRI];
+        bool need = false;
+#pragma unroll
+        for (int i = 0; i < kRI; ++i) {
+          float m = score(acc, i, 0);
+#pragma unroll
+          for (int jj = 1; jj < 8; ++jj) m = fmaxf(m, score(acc, i, jj));
+          lmax[i] = m;
+          need |= fmaf(m, sl2, -mo[i]) > 8.f;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          bool moved = false;
+          float mprev[kRI];
+#pragma unroll
+          for (int i = 0; i < kRI; ++i) {
+            float mr = lmax[i];
+            mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
+            mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
+            mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
+            const float mx = mr * sl2;
+            mprev[i] = mo[i];
+            if (mx > mo[i] + 8.f) {
+              mo[i] = mx;
+              moved = true;
+            }
+          }
+          if (j > 0 && __any_sync(0xffffffffu, moved)) {
+#pragma unroll
+            for (int i = 0; i < kRI; ++i) {
+              const float alpha = ex2(mprev[i] - mo[i]);
+              l[i] *= alpha;
+#pragma unroll
+              for (int u = 0; u < 4; ++u) o[i][u] = __fmul2_rn(o[i][u], make_float2(alpha, alpha));
+            }
+          }
+        }
+        const int njw = nk > kBox ? 8 : 4;  // key groups written to P (PV reads keys < nk only)
+#pragma unroll
+        for (int i = 0; i < kRI; ++i) {
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            if (jj < njw) {
+              const float pe = ex2(fmaf(score(acc, i, jj), sl2, -mo[i]));
+              l[i] += pe;
+              Pw[(rg + 4 * i) * kPS + cg + 8 * jj] = pe;
+            }
+          }
+        }
+        __syncwarp();
+
+        // ---- O += P V: whole groups of 4 keys, then the ragged group (V rows past Lk are
+        // replaced by zeros: they may hold anything, and 0 * inf is not 0)
+        auto pv_group = [&](int k4, int valid) {
+          float4 pf[kRI];
+#pragma unroll
+          for (int i = 0; i < kRI; ++i) pf[i] = P4[i * 4 * (kPS / 4) + k4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+            if (e < valid) {
+              v0 = V4[(k4 * 4 + e) * (kVS / 4)];
+              v1 = V4[(k4 * 4 + e) * (kVS / 4) + 8];
+            }
+#pragma unroll
+            for (int i = 0; i < kRI; ++i) {
+              const float pe = e == 0 ? pf[i].x : e == 1 ? pf[i].y : e == 2 ? pf[i].z : pf[i].w;
+              const float2 p2 = make_float2(pe, pe);
+              o[i][0] = __ffma2_rn(p2, make_float2(v0.x, v0.y), o[i][0]);
+              o[i][1] = __ffma2_rn(p2, make_float2(v0.z, v0.w), o[i][1]);
+              o[i][2] = __ffma2_rn(p2, make_float2(v1.x, v1.y), o[i][2]);
+              o[i][3] = __ffma2_rn(p2, make_float2(v1.z, v1.w), o[i][3]);
+            }
+          }
+        };
+        const int nfull = nk >> 2;
+#pragma unroll 2
+        for (int k4 = 0; k4 < nfull; ++k4) pv_group(k4, 4);
+        if (nk & 3) pv_group(nfull, nk & 3);
+      }  // active
+      __syncwarp();  // every lane is done with P and with stage s
+
+      // ---- release stage s; the last warp out loads the block two ahead into it
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&C->cnt[s], 1) == kW - 1) {
+          atomicExch(&C->cnt[s], 0);
+          __threadfence_block();
+          fence_proxy_async_smem();
+          issue_next(L, C, Ks, Vs, s);
+        }
+      }
+    }
+
+    // ---- O / l, rows < Lq
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < kRI; ++i) {
+        float ls = l[i];
+        ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+        float inv;
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(ls));  // within 1 ulp; l >= 1 here
+        if (4 * i < rows_q) {
+          float* dst = orow + (int64_t)(4 * i) * ldo;
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            *reinterpret_cast<float4*>(dst + 32 * u) = make_float4(o[i][2 * u].x * inv, o[i][2 * u].y * inv,
+                                                                   o[i][2 * u + 1].x * inv, o[i][2 * u + 1].y * inv);
+        }
+      }
+    }
+    T = Tn;
+    t = tn;
+  }
+}
+
+}  // namespace
+
+int attn_fp32_wide_tile_rows() { return kRows; }
+
+int attn_fp32_wide_ctas() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+cudaError_t launch_attn_fp32_wide(const TmaLaunch& L, cudaStream_t s) {
+  if (L.total <= 0) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(attn_fp32_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+  if (e != cudaSuccess) return e;
+  const int ctas = attn_fp32_wide_ctas();
+  const int grid = L.total < ctas ? L.total : ctas;  // persistent: one CTA per SM
+  attn_fp32_wide_kernel<<<grid, kW * 32, BYTES, s>>>(L);
+  return cudaGetLastError();
+}
+
+}  // namespace supra

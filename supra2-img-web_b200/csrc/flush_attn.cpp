@@ -294,7 +294,24 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
 // kernel): one tensor map per distinct (buffer, ld, rows, box) in the flush, encoded once per
 // context and cached; problems refer to maps by index.
 int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
-  const int mrows = tf32 ? supra::attn_tf32_tile_rows() : supra::attn_fp32_warp_tile_rows();
+  // Unbiased FP32 launches that fill the device with 256-row tiles, and lose little to the larger
+  // tile (query rows rounded up to 256 at most 1/8 more than rounded up to 128), run on the
+  // 256-row kernel (8x8 register blocks, one CTA per SM); the others on the 128-row kernel.
+  bool wide = false;
+  if (!tf32 && !g[0]->bias) {
+    const int64_t wr = supra::attn_fp32_wide_tile_rows(), nr = supra::attn_fp32_warp_tile_rows();
+    int64_t tiles = 0, rows_w = 0, rows_n = 0;
+    for (const Queued* q : g) {
+      const int64_t tw = (q->p.Lq + wr - 1) / wr;
+      tiles += tw * q->p.H;
+      rows_w += tw * wr * q->p.H;
+      rows_n += (q->p.Lq + nr - 1) / nr * nr * q->p.H;
+    }
+    wide = tiles >= 2 * (int64_t)supra::attn_fp32_wide_ctas() && 8 * rows_w <= 9 * rows_n;
+  }
+  const int mrows = tf32 ? supra::attn_tf32_tile_rows()
+                    : wide ? supra::attn_fp32_wide_tile_rows()
+                           : supra::attn_fp32_warp_tile_rows();
   // the split kernel needs the operands exactly: fp32 maps with the tensor-core swizzles
   const bool split = tf32 && g[0]->cfg == 1;
   std::stable_sort(g.begin(), g.end(), [](const Queued* a, const Queued* b) { return a->p.Lk > b->p.Lk; });
@@ -326,7 +343,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   // schedulers, and fewer splits leave fewer partial rows to combine.)
   int ns_max = 1;
   int64_t groups = 0;
-  if (!tf32) {
+  if (!tf32 && !wide) {
     for (int i = 0; i < n; ++i) groups += (int64_t)((g[i]->p.Lq + mrows - 1) / mrows) * g[i]->p.H;
     const int sms = supra::attn_fp32_warp_cta_slots() / 2;
     if (groups > 0 && 2 * groups <= sms) ns_max = (int)std::min<int64_t>(8, sms / groups);
@@ -437,13 +454,16 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     L.part_ml = reinterpret_cast<float2*>(c->scratch + (size_t)group0 * used_splits * mrows * 64);
     L.part_cnt = L.next_tile + 4;  // (16 bytes past the tile counter)
   }
-  const char* name = !tf32  ? (g[0]->bias ? "attn_fp32_d64_tma_bias" : "attn_fp32_d64_tma")
+  const char* name = wide    ? "attn_fp32_d64_wide"
+                     : !tf32  ? (g[0]->bias ? "attn_fp32_d64_tma_bias" : "attn_fp32_d64_tma")
                      : split ? (g[0]->bias ? "attn_tf32x3_d64_bias" : "attn_tf32x3_d64")
                              : (g[0]->bias ? "attn_tf32_d64_bias" : "attn_tf32_d64");
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = tf32 ? supra::launch_attn_tf32(L, g[0]->bias, split, c->stream) : supra::launch_attn_fp32_warp(L, g[0]->bias, c->stream);
+    e = tf32   ? supra::launch_attn_tf32(L, g[0]->bias, split, c->stream)
+        : wide ? supra::launch_attn_fp32_wide(L, c->stream)
+               : supra::launch_attn_fp32_warp(L, g[0]->bias, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;

@@ -156,6 +156,13 @@ cudaError_t launch_attn_fp32_warp(const TmaLaunch& L, bool bias, cudaStream_t s)
 int attn_fp32_warp_tile_rows();
 int attn_fp32_warp_cta_slots();  // CTAs the persistent grid holds at most (two per SM)
 
+// Persistent FP32 kernel for large unbiased launches (attn_fp32_wide.cu): D = 64, scale > 0, no
+// bias; 256-row tiles (TmaProb::q_tiles counts those), no key splits, the same tensor maps as
+// attn_fp32_warp.cu. One CTA per SM.
+cudaError_t launch_attn_fp32_wide(const TmaLaunch& L, cudaStream_t s);
+int attn_fp32_wide_tile_rows();
+int attn_fp32_wide_ctas();
+
 // Normalisation of x in the linear prologue (LinProb::gn_mode): GroupNorm with gamma/beta,
 // LayerNorm with adaLN modulation (gamma = scale, beta = shift, applied as 1 + scale), plain
 // LayerNorm.
