@@ -46,7 +46,7 @@ constexpr int kQS = kFwBoxWide;    // Q box row stride in shared memory (floats)
 constexpr int kKS = kFwBoxWide;    // K row stride
 constexpr int kVS = kFwBoxNarrow;  // V row stride
 constexpr int kTS = kRowsW;        // Q^T row stride: 32 positions (conflict-free float4 reads)
-constexpr int kPS = kNK + 8;       // P row stride: conflict-free scalar writes and float4 reads
+constexpr int kPT = kRowsW + 4;    // P^T row stride: conflict-free float4 writes and reads
 static_assert(kRowsW == kBox, "one Q box per warp");
 static_assert(kD * kTS <= kRowsW * kQS, "Q^T fits in the warp's Q box");
 
@@ -58,7 +58,7 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + kW * kRowsW * kQS;
 constexpr int OFF_V = OFF_K + kNS * kNK * kKS;
 constexpr int OFF_P = OFF_V + kNS * kNK * kVS;
-constexpr int FLOATS = OFF_P + kW * kRowsW * kPS;
+constexpr int FLOATS = OFF_P + kW * kNK * kPT;
 static_assert((OFF_K * 4) % 128 == 0 && (OFF_V * 4) % 128 == 0 && (OFF_P * 4) % 128 == 0 && kQBytes % 128 == 0 &&
                   kKBoxBytes % 128 == 0 && kVBoxBytes % 128 == 0,
               "TMA destinations are 128-byte aligned");
@@ -201,6 +201,12 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ float score(const float2 (&acc)[4][8], int i, int j) {
   return (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
 }
+// row i of a row-pair array (x: even rows, y: odd rows)
+__device__ __forceinline__ float pick(const float2 (&a)[4], int i) { return (i & 1) ? a[i >> 1].y : a[i >> 1].x; }
+__device__ __forceinline__ void set(float2 (&a)[4], int i, float v) {
+  if (i & 1) a[i >> 1].y = v;
+  else a[i >> 1].x = v;
+}
 
 __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid_constant__ TmaLaunch L) {
   extern __shared__ uint8_t smem_raw[];
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
   const int rg = lane >> 3;
   const int cg = lane & 7;
   float* Qw = smem + OFF_Q + w * kRowsW * kQS;
-  float* Pw = smem + OFF_P + w * kRowsW * kPS;
+  float* Pw = smem + OFF_P + w * kNK * kPT;
 
   const int t0 = blockIdx.x;
   if (t0 >= L.total) {  // the host sizes the grid to at most one CTA per tile
@@ -242,7 +248,7 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
   if (lane == 0) issue_q(L, T, w, Qw, &C->qbar[w]);
 
   const float4* QT4 = reinterpret_cast<const float4*>(Qw) + 2 * rg;
-  const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
+  const float4* PT4 = reinterpret_cast<const float4*>(Pw) + 2 * rg;
   uint32_t g = 0;  // position in the CTA's K/V block sequence
   uint32_t k = 0;  // position in the CTA's tile sequence
   for (int t = t0; t < L.total; ++k) {
@@ -258,15 +264,19 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
     int tn = L.total;
     Tile Tn = T;
 
+    // per row: the negated exp2 offset and the running sum, in row pairs (i = 2p, 2p + 1) as the
+    // scores are
     float2 o[kRI][4];
-    float mo[kRI], l[kRI];
+    float2 nm2[4], l2[4];
 #pragma unroll
-    for (int i = 0; i < kRI; ++i) {
-      mo[i] = -INFINITY;
-      l[i] = 0.f;
+    for (int p = 0; p < 4; ++p) {
+      nm2[p] = make_float2(INFINITY, INFINITY);
+      l2[p] = make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < kRI; ++i)
 #pragma unroll
       for (int u = 0; u < 4; ++u) o[i][u] = make_float2(0.f, 0.f);
-    }
     if (!mbar_wait_bounded(&C->qbar[w], k & 1u)) {
       if (lane == 0) report_error(L.status, DEV_TIMEOUT, 31, (int32_t)k);
       return;
@@ -319,65 +329,59 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
 #pragma unroll
           for (int jj = 1; jj < 8; ++jj) m = fmaxf(m, score(acc, i, jj));
           lmax[i] = m;
-          need |= fmaf(m, sl2, -mo[i]) > 8.f;
+          need |= fmaf(m, sl2, pick(nm2, i)) > 8.f;
         }
         if (__any_sync(0xffffffffu, need)) {
           bool moved = false;
-          float mprev[kRI];
+          float2 nprev[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) nprev[p] = nm2[p];
 #pragma unroll
           for (int i = 0; i < kRI; ++i) {
             float mr = lmax[i];
             mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 1));
             mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 2));
             mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 4));
-            const float mx = mr * sl2;
-            mprev[i] = mo[i];
-            if (mx > mo[i] + 8.f) {
-              mo[i] = mx;
+            const float mx = mr * sl2;  // the same value in all 8 lanes of the row
+            if (mx + pick(nm2, i) > 8.f) {
+              set(nm2, i, -mx);
               moved = true;
             }
           }
           if (j > 0 && __any_sync(0xffffffffu, moved)) {
 #pragma unroll
-            for (int i = 0; i < kRI; ++i) {
-              const float alpha = ex2(mprev[i] - mo[i]);
-              l[i] *= alpha;
+            for (int p = 0; p < 4; ++p) {
+              const float2 alpha = make_float2(ex2(nm2[p].x - nprev[p].x), ex2(nm2[p].y - nprev[p].y));
+              l2[p] = __fmul2_rn(l2[p], alpha);
 #pragma unroll
-              for (int u = 0; u < 4; ++u) o[i][u] = __fmul2_rn(o[i][u], make_float2(alpha, alpha));
+              for (int u = 0; u < 4; ++u) {
+                o[2 * p][u] = __fmul2_rn(o[2 * p][u], make_float2(alpha.x, alpha.x));
+                o[2 * p + 1][u] = __fmul2_rn(o[2 * p + 1][u], make_float2(alpha.y, alpha.y));
+              }
             }
           }
         }
-        const int njw = nk > kBox ? 8 : 4;  // key groups written to P (PV reads keys < nk only)
+        // P^T [key][position]: a lane's 8 rows of one key are two float4 stores (positions 8rg..)
+        auto pv_group = [&](int k4, int valid) {  // O += P V over keys 4 k4 .. + 3
+          float4 pa[4], pb[4];
 #pragma unroll
-        for (int i = 0; i < kRI; ++i) {
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            if (jj < njw) {
-              const float pe = ex2(fmaf(score(acc, i, jj), sl2, -mo[i]));
-              l[i] += pe;
-              Pw[(rg + 4 * i) * kPS + cg + 8 * jj] = pe;
-            }
+          for (int e = 0; e < 4; ++e) {
+            pa[e] = PT4[(k4 * 4 + e) * (kPT / 4)];
+            pb[e] = PT4[(k4 * 4 + e) * (kPT / 4) + 1];
           }
-        }
-        __syncwarp();
-
-        // ---- O += P V: whole groups of 4 keys, then the ragged group (V rows past Lk are
-        // replaced by zeros: they may hold anything, and 0 * inf is not 0)
-        auto pv_group = [&](int k4, int valid) {
-          float4 pf[kRI];
-#pragma unroll
-          for (int i = 0; i < kRI; ++i) pf[i] = P4[i * 4 * (kPS / 4) + k4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-            if (e < valid) {
+            if (e < valid) {  // V rows past Lk are replaced by zeros (they may hold anything; 0 * inf is not 0)
               v0 = V4[(k4 * 4 + e) * (kVS / 4)];
               v1 = V4[(k4 * 4 + e) * (kVS / 4) + 8];
             }
 #pragma unroll
             for (int i = 0; i < kRI; ++i) {
-              const float pe = e == 0 ? pf[i].x : e == 1 ? pf[i].y : e == 2 ? pf[i].z : pf[i].w;
-              const float2 p2 = make_float2(pe, pe);
+              const float4& pq = i < 4 ? pa[e] : pb[e];
+              const int c = i & 3;
+              const float pv = c == 0 ? pq.x : c == 1 ? pq.y : c == 2 ? pq.z : pq.w;
+              const float2 p2 = make_float2(pv, pv);
               o[i][0] = __ffma2_rn(p2, make_float2(v0.x, v0.y), o[i][0]);
               o[i][1] = __ffma2_rn(p2, make_float2(v0.z, v0.w), o[i][1]);
               o[i][2] = __ffma2_rn(p2, make_float2(v1.x, v1.y), o[i][2]);
@@ -385,10 +389,49 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
             }
           }
         };
-        const int nfull = nk >> 2;
+        // probabilities of key group jj (key cg + 8 jj), row pairs 2h and 2h + 1 (rows 4h .. 4h + 3):
+        // one float4 of P^T, and the rows' sums
+        auto p_half = [&](int jj, int h) {
+          const float2 a0 = __ffma2_rn(acc[2 * h][jj], make_float2(sl2, sl2), nm2[2 * h]);
+          const float2 a1 = __ffma2_rn(acc[2 * h + 1][jj], make_float2(sl2, sl2), nm2[2 * h + 1]);
+          const float2 p0 = make_float2(ex2(a0.x), ex2(a0.y));
+          const float2 p1 = make_float2(ex2(a1.x), ex2(a1.y));
+          l2[2 * h] = __fadd2_rn(l2[2 * h], p0);
+          l2[2 * h + 1] = __fadd2_rn(l2[2 * h + 1], p1);
+          *reinterpret_cast<float4*>(Pw + (cg + 8 * jj) * kPT + 8 * rg + 4 * h) = make_float4(p0.x, p0.y, p1.x, p1.y);
+        };
+        if (nk > kBox) {
+          // keys past 32: their probabilities are formed inside the P V of keys 0..31, so that
+          // their exp2 (on the SFU) overlap the products (on the FMA pipe)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            p_half(jj, 0);
+            p_half(jj, 1);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int k4 = 0; k4 < 8; ++k4) {
+            pv_group(k4, 4);
+            p_half(4 + (k4 >> 1), k4 & 1);
+          }
+          __syncwarp();
+          if (nk == kNK) {
 #pragma unroll 2
-        for (int k4 = 0; k4 < nfull; ++k4) pv_group(k4, 4);
-        if (nk & 3) pv_group(nfull, nk & 3);
+            for (int k4 = 8; k4 < kNK / 4; ++k4) pv_group(k4, 4);
+          } else {
+#pragma unroll 2
+            for (int k4 = 8; 4 * k4 < nk; ++k4) pv_group(k4, min(4, nk - 4 * k4));
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            p_half(jj, 0);
+            p_half(jj, 1);
+          }
+          __syncwarp();
+#pragma unroll 2
+          for (int k4 = 0; 4 * k4 < nk; ++k4) pv_group(k4, min(4, nk - 4 * k4));
+        }
       }  // active
       __syncwarp();  // every lane is done with P and with stage s
 
@@ -408,7 +451,7 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
     if (active) {
 #pragma unroll
       for (int i = 0; i < kRI; ++i) {
-        float ls = l[i];
+        float ls = pick(l2, i);
         ls += __shfl_xor_sync(0xffffffffu, ls, 1);
         ls += __shfl_xor_sync(0xffffffffu, ls, 2);
         ls += __shfl_xor_sync(0xffffffffu, ls, 4);
