@@ -142,21 +142,31 @@ __device__ __forceinline__ void issue_q(const TmaLaunch& L, const Tile& T, int w
   tc::tma_load_2d(dst, L.maps + T.p->mq, T.p->qx + T.h * kD, T.p->qy + T.q0 + w * kRowsW, bar);
 }
 
-// The warp's Q box [32 rows][68] -> Q^T [64 d][32] in place: lane l holds row l's 64 values (all
-// loads before any store), then writes column d of Q^T at position 8 (l % 4) + l / 4.
+// The warp's Q box [32 rows][68] -> Q^T [64 d][32] in place, in 4x4 blocks: row r goes to
+// position 8 (r % 4) + r / 4, so rows a + 4 (b + t), t < 4, fill positions 8a + b + t. Lane (a =
+// lane % 4, x = lane / 4) moves four blocks (columns 4c .. 4c + 3 of those rows): all 16 float4
+// loads before any store, then 16 float4 stores. The choice of c and b per lane keeps the loads
+// and the stores of each quarter-warp on 8 distinct 16-byte bank groups.
 __device__ __forceinline__ void transpose_q(float* Qw, int lane) {
-  const float4* src = reinterpret_cast<const float4*>(Qw + lane * kQS);
-  float4 r[kD / 4];
+  const int a = lane & 3, x = lane >> 2;
+  float4 f[4][4];
 #pragma unroll
-  for (int c = 0; c < kD / 4; ++c) r[c] = src[c];
+  for (int m = 0; m < 4; ++m) {
+    const int c = 4 * (x & 1) + (x >> 1) + 8 * (m & 1);
+    const int b = 4 * (((m >> 1) ^ x) & 1);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) f[m][t] = *reinterpret_cast<const float4*>(Qw + (a + 4 * (b + t)) * kQS + 4 * c);
+  }
   __syncwarp();
-  float* dst = Qw + 8 * (lane & 3) + (lane >> 2);
 #pragma unroll
-  for (int c = 0; c < kD / 4; ++c) {
-    dst[(4 * c + 0) * kTS] = r[c].x;
-    dst[(4 * c + 1) * kTS] = r[c].y;
-    dst[(4 * c + 2) * kTS] = r[c].z;
-    dst[(4 * c + 3) * kTS] = r[c].w;
+  for (int m = 0; m < 4; ++m) {
+    const int c = 4 * (x & 1) + (x >> 1) + 8 * (m & 1);
+    const int b = 4 * (((m >> 1) ^ x) & 1);
+    float* dst = Qw + 4 * c * kTS + 8 * a + b;
+    *reinterpret_cast<float4*>(dst) = make_float4(f[m][0].x, f[m][1].x, f[m][2].x, f[m][3].x);
+    *reinterpret_cast<float4*>(dst + kTS) = make_float4(f[m][0].y, f[m][1].y, f[m][2].y, f[m][3].y);
+    *reinterpret_cast<float4*>(dst + 2 * kTS) = make_float4(f[m][0].z, f[m][1].z, f[m][2].z, f[m][3].z);
+    *reinterpret_cast<float4*>(dst + 3 * kTS) = make_float4(f[m][0].w, f[m][1].w, f[m][2].w, f[m][3].w);
   }
   __syncwarp();
 }
@@ -298,11 +308,13 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
       const float4* K4 = reinterpret_cast<const float4*>(Ks + s * kNK * kKS) + cg * (kKS / 4);
       const float4* V4 = reinterpret_cast<const float4*>(Vs + s * kNK * kVS) + cg;
 
-      // ---- S = Q K^T (the first 32 keys only when the block has no more)
+      // ---- S = Q K^T over the block's 16-key groups that hold a key below Lk
       float2 acc[4][8];
       if (active) {
-        if (nk > kBox) qk_block<8>(QT4, K4, acc);
-        else qk_block<4>(QT4, K4, acc);
+        if (nk > 48) qk_block<8>(QT4, K4, acc);
+        else if (nk > 32) qk_block<6>(QT4, K4, acc);
+        else if (nk > 16) qk_block<4>(QT4, K4, acc);
+        else qk_block<2>(QT4, K4, acc);
       }
       if (j == nb - 1 && tn < L.total) {  // this warp's Q^T is done: fetch its next Q rows
         __syncwarp();
