@@ -288,7 +288,10 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
 #pragma unroll
       for (int u = 0; u < 4; ++u) o[i][u] = make_float2(0.f, 0.f);
     if (!mbar_wait_bounded(&C->qbar[w], k & 1u)) {
-      if (lane == 0) report_error(L.status, DEV_TIMEOUT, 31, (int32_t)k);
+      if (lane == 0) {
+        report_error(L.status, DEV_TIMEOUT, 31, (int32_t)k);
+        tc::bulk_wait_group_all();
+      }
       return;
     }
     if (active) transpose_q(Qw, lane);
@@ -298,7 +301,10 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
       const uint32_t par = (g / kNS) & 1u;
       const int nk = min(kNK, Lk - j * kNK);
       if (!mbar_wait_bounded(&C->full[s], par)) {
-        if (lane == 0) report_error(L.status, DEV_TIMEOUT, 32, (int32_t)g);
+        if (lane == 0) {
+          report_error(L.status, DEV_TIMEOUT, 32, (int32_t)g);
+          tc::bulk_wait_group_all();
+        }
         return;
       }
       if (j == nb - 1) {
@@ -372,6 +378,10 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
               }
             }
           }
+        }
+        if (j == 0) {  // the previous tile's output copy has read the P^T buffer
+          if (lane == 0) tc::bulk_wait_group_read<0>();
+          __syncwarp();
         }
         // P^T [key][position]: a lane's 8 rows of one key are two float4 stores (positions 8rg..)
         auto pv_group = [&](int k4, int valid) {  // O += P V over keys 4 k4 .. + 3
@@ -459,8 +469,12 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
       }
     }
 
-    // ---- O / l, rows < Lq
+    // ---- O / l, rows < Lq. A warp whose 32 rows all lie below Lq stages them in its P^T buffer
+    // ([32][64]) and stores them with one TMA copy, which runs on while the next tile starts (the
+    // next write to the buffer, in the next tile's first block, first waits for the copy to have
+    // read it); other warps store their rows below Lq directly.
     if (active) {
+      const bool tma_o = pp->mo >= 0 && pp->Lq - T.q0 >= kRowsW * (w + 1);  // (warp-uniform)
 #pragma unroll
       for (int i = 0; i < kRI; ++i) {
         float ls = pick(l2, i);
@@ -469,18 +483,31 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
         ls += __shfl_xor_sync(0xffffffffu, ls, 4);
         float inv;
         asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(ls));  // within 1 ulp; l >= 1 here
-        if (4 * i < rows_q) {
+        const float4 lo = make_float4(o[i][0].x * inv, o[i][0].y * inv, o[i][1].x * inv, o[i][1].y * inv);
+        const float4 hi = make_float4(o[i][2].x * inv, o[i][2].y * inv, o[i][3].x * inv, o[i][3].y * inv);
+        if (tma_o) {
+          float* st = Pw + (rg + 4 * i) * kD + 4 * cg;
+          *reinterpret_cast<float4*>(st) = lo;
+          *reinterpret_cast<float4*>(st + 32) = hi;
+        } else if (4 * i < rows_q) {
           float* dst = orow + (int64_t)(4 * i) * ldo;
-#pragma unroll
-          for (int u = 0; u < 2; ++u)
-            *reinterpret_cast<float4*>(dst + 32 * u) = make_float4(o[i][2 * u].x * inv, o[i][2 * u].y * inv,
-                                                                   o[i][2 * u + 1].x * inv, o[i][2 * u + 1].y * inv);
+          *reinterpret_cast<float4*>(dst) = lo;
+          *reinterpret_cast<float4*>(dst + 32) = hi;
+        }
+      }
+      if (tma_o) {
+        fence_proxy_async_smem();  // this lane's staged rows, before the copy reads them
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_2d(L.maps + pp->mo, Pw, T.h * kD, pp->oy + T.q0 + kRowsW * w);
+          tc::bulk_commit_group();
         }
       }
     }
     T = Tn;
     t = tn;
   }
+  if (lane == 0) tc::bulk_wait_group_all();  // the output copies are complete
 }
 
 }  // namespace

@@ -381,6 +381,14 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
         rc = map_index(P.v, P.ldv, q.rows_v, supra::kFwBoxNarrow, supra::kFwBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE,
                        &t.mv);
     }
+    // output rows by TMA stores (256-row kernel): one map over the whole output buffer, when the
+    // problem's rows are whole rows of it
+    t.mo = -1;
+    if (!rc && wide && aligned16(P.o) && P.o_off % P.ldo == 0 && P.o_off / P.ldo + P.Lq <= q.rows_o &&
+        q.rows_o <= INT32_MAX) {
+      rc = map_index(P.o, P.ldo, q.rows_o, 64, 32, CU_TENSOR_MAP_SWIZZLE_NONE, &t.mo);
+      t.oy = (int32_t)(P.o_off / P.ldo);
+    }
     if (rc) return rc;
     t.qx = (int32_t)(P.q_off % P.ldq);
     t.qy = (int32_t)(P.q_off / P.ldq);

@@ -117,7 +117,11 @@ struct alignas(16) TmaProb {
   int32_t splits;
   int32_t bps;
   int32_t group0;
-  int32_t pad[2];
+  // The 256-row FP32 kernel: tensor map of the whole output buffer as [rows, H*D] (boxes of 64
+  // columns x 32 rows) and the problem's first output row in it, for TMA stores of whole 32-row
+  // blocks; mo = -1: plain stores only.
+  int32_t mo;
+  int32_t oy;
 };
 static_assert(sizeof(TmaProb) % 16 == 0, "TmaProb is packed into the descriptor ring");
 

@@ -100,6 +100,7 @@ struct Queued {
   double flops;
   double bytes;
   int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TMA tensor maps)
+  int64_t rows_o;                  // whole H*D-float rows of the output buffer
   int32_t t5_buckets, t5_maxd;      // T5 table bias (SUPRA_ATTN_F_T5_TABLE), else 0
   supra::LinProb lin;               // PATH_LINEAR: the linear problem (p unused)
   float gn_eps;                     // PATH_LINEAR with GroupNorm of x

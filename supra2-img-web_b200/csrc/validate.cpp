@@ -135,6 +135,7 @@ int validate(supra_attn_ctx* c, const supra_attn_desc* d, Checked* out) {
   q.rows_q = d->ldq > 0 ? d->q_size / d->ldq : 0;
   q.rows_k = d->ldk > 0 ? d->k_size / d->ldk : 0;
   q.rows_v = d->ldv > 0 ? d->v_size / d->ldv : 0;
+  q.rows_o = HD > 0 ? d->out_size / HD : 0;
   // The TMA kernels read whole boxes of full buffer rows through tensor maps: head dim 64,
   // 16-byte aligned rows, every row of the problem a whole row of its buffer, and the heads
   // inside one row.
@@ -324,7 +325,7 @@ int validate_linear(supra_attn_ctx* c, const supra_attn_linear_desc* d, Checked*
   q.aligned = (d->K % 4 == 0) && (d->ldx % 4 == 0) && (d->ldw % 4 == 0) && aligned16(d->x + d->x_off) &&
               aligned16(d->w);
   q.t5_buckets = q.t5_maxd = 0;
-  q.rows_q = q.rows_k = q.rows_v = 0;
+  q.rows_q = q.rows_k = q.rows_v = q.rows_o = 0;
   q.flops = 2.0 * d->M * (double)d->N * d->K;
   q.bytes = 4.0 * ((double)d->M * d->K + (double)d->N * d->K + (double)d->M * d->N + (d->bias ? d->N : 0) +
                    (d->resid ? (double)d->M * d->N : 0.0) + ((gn || (ln && ln->mod)) ? 2.0 * d->K : 0.0) +
