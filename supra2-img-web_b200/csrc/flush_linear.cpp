@@ -59,19 +59,38 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
     if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
   }
   begin[n] = (int32_t)total;
+  // A normalised x read by two or more column tiles is normalised once, into the context's split
+  // buffer ([M, K] dense), by a launch between its statistics and the product (which then reads it
+  // plainly): the prologue would normalise every x tile again for every column tile (the DiT
+  // block's qkv, N = 1728: 27 times). x of such problems is 16-byte aligned with K % 4 == 0.
+  std::vector<supra::LinProb> lp((size_t)n);
+  std::vector<int64_t> xn((size_t)n, -1);  // offset of the normalised x in lin_split, or -1
+  size_t xn_need = 0;
+  for (int i = 0; i < n; ++i) {
+    lp[i] = g[i]->lin;
+    lp[i].n_tiles = (lp[i].N + cols - 1) / cols;
+    if (lp[i].gn_rows > 0 && lp[i].n_tiles >= 2 && lp[i].K % 4 == 0 && (lp[i].ldx & 3) == 0 && aligned16(lp[i].x)) {
+      xn[i] = (int64_t)xn_need;
+      xn_need += align16((size_t)lp[i].M * lp[i].K * sizeof(float)) / sizeof(float);
+    }
+  }
+  if (xn_need) {
+    const int rc0 = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, xn_need, sizeof(float),
+                                "normalised x");
+    if (rc0) return rc0;
+  }
   // 16-byte aligned operands (the group's `aligned`) are staged by TMA: a tensor map of x [M, K]
   // with 20 x 128 boxes and of W [N, K] with 20 x (tile columns) boxes per problem, cached per
   // context like the attention kernels' maps
   bool tma = g[0]->aligned;
   std::vector<CUtensorMap> maps;
-  std::vector<supra::LinProb> lp((size_t)n);
   ++c->map_epoch;
   for (int i = 0; i < n; ++i) {
-    lp[i] = g[i]->lin;
-    lp[i].n_tiles = (lp[i].N + cols - 1) / cols;
     if (tma) {
       const supra::LinProb& q = lp[i];
-      int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.x), q.ldx, q.M, q.K, 20, 128, 0, 0}, maps, &lp[i].mx);
+      const float* xb = xn[i] >= 0 ? c->lin_split + xn[i] : q.x;
+      const int64_t ldx = xn[i] >= 0 ? q.K : q.ldx;
+      int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(xb), ldx, q.M, q.K, 20, 128, 0, 0}, maps, &lp[i].mx);
       if (!rc0)
         rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, 20, cols, 0, 0}, maps, &lp[i].mw);
       if (rc0) {  // a shape the driver's encoder refuses: the group runs the per-thread copy form
@@ -96,6 +115,20 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   std::memcpy(hp, lp.data(), sizeof(supra::LinProb) * n);
   rc = norm_stats(c, g, hp);
   if (rc) return rc;
+  for (int i = 0; i < n; ++i) {
+    if (xn[i] < 0) continue;
+    float* dst = c->lin_split + xn[i];
+    cudaError_t e;
+    {
+      ProfScope ps(c, "norm_apply", 0.0, 8.0 * (double)hp[i].M * hp[i].K);
+      e = supra::launch_norm_apply(hp[i], dst, c->stream);
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, "norm_apply");
+    c->launches += 1;
+    hp[i].x = dst;
+    hp[i].ldx = hp[i].K;
+    hp[i].gn_stats = nullptr;  // the product reads x as it is
+  }
   std::memcpy(hm + mbytes + pbytes, begin.data(), bbytes);
   rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
   if (rc) return rc;

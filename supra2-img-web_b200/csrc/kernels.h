@@ -279,6 +279,9 @@ struct SplitLaunch {
 // All jobs of one flush in one launch (32 x 128 tiles, HBM-bound).
 cudaError_t launch_split(const SplitLaunch& L, cudaStream_t s);
 cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s);
+// P.x (rows of stride P.ldx) normalised as the linear's prologue would (P.gn_stats set, K % 4 == 0,
+// 16-byte aligned rows) into dst as [M, K] dense.
+cudaError_t launch_norm_apply(const LinProb& P, float* dst, cudaStream_t s);
 cudaError_t launch_gn_stats(const float* x, int32_t K, int32_t rows_per_image, int32_t images, int32_t groups,
                             float eps, float2* stats, cudaStream_t s);
 

@@ -383,7 +383,41 @@ __global__ void __launch_bounds__(256) ln_stats_kernel(const float* __restrict__
   if (lane == 0) stats[row] = make_float2(mean, rsqrtf(v / (float)K + eps));
 }
 
+// x normalised once into dst ([M, K] dense), for products whose x tiles would otherwise be
+// normalised again by every column tile: the same arithmetic as norm_stage, one float4 per thread.
+__global__ void __launch_bounds__(256) norm_apply_kernel(const LinProb P, float* __restrict__ dst) {
+  const int64_t k4n = P.K / 4;
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= (int64_t)P.M * k4n) return;
+  const int r = (int)(i / k4n);
+  const int k = (int)(i - (int64_t)r * k4n) * 4;
+  const int img = P.gn_rows == 1 ? r : r / P.gn_rows;
+  const float4 x = __ldg(reinterpret_cast<const float4*>(P.x + (int64_t)r * P.ldx + k));
+  float v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    float g = 1.f, b = 0.f;
+    if (P.gn_mode != kNormPlain) {
+      g = __ldg(P.gamma + k + u);
+      b = __ldg(P.beta + k + u);
+      if (P.gn_mode == kNormModulated) g = 1.f + g;
+    }
+    const float2 ms = __ldg(P.gn_stats + (int64_t)img * P.gn_groups + (k + u) / P.gn_cg);
+    float y = (v[u] - ms.x) * (ms.y * g) + b;
+    if (P.gn_silu) y = y / (1.f + __expf(-y));
+    v[u] = y;
+  }
+  *reinterpret_cast<float4*>(dst + (int64_t)r * P.K + k) = make_float4(v[0], v[1], v[2], v[3]);
+}
+
 }  // namespace
+
+cudaError_t launch_norm_apply(const LinProb& P, float* dst, cudaStream_t s) {
+  const int64_t n = (int64_t)P.M * (P.K / 4);
+  if (n <= 0) return cudaSuccess;
+  norm_apply_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(P, dst);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ln_stats(const float* x, int32_t K, int32_t rows, float eps, float2* stats, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
