@@ -84,6 +84,9 @@ struct Lay {
 };
 static_assert(Lay<true>::SMEM <= 227 * 1024 && 2 * Lay<false>::SMEM <= 228 * 1024, "shared memory");
 constexpr uint32_t COL_S0 = 0, COL_S1 = 64, COL_O = 128;
+// plain kernel: the tile's Q rows, the A operand of S, copied from the landed smem tile by the
+// softmax threads so that the smem tile is free for the next tile's Q at once
+constexpr uint32_t COL_QP = 192;
 // split kernel: lo(P), a fresh per-block PV accumulator (O itself lives in the softmax threads'
 // registers), and two buffers of hi(Q) | lo(Q) (64 + 64 columns), the A operand of S, so the
 // next tile's Q is split before the current tile's epilogue
@@ -229,6 +232,23 @@ __device__ __forceinline__ void split_q_row(const uint8_t* Qs, int row, uint32_t
   }
 }
 
+// Plain kernel, softmax threads: this thread's row of the landed Q tile into TMEM at column qc of
+// its lane, unchanged (the tensor core reads it as TF32).
+__device__ __forceinline__ void copy_q_row(const uint8_t* Qs, int row, uint32_t taddr_q) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    float q[32];
+    const uint8_t* qrow = Qs + hf * kQSlab + row * 128;
+#pragma unroll
+    for (int c4 = 0; c4 < 8; ++c4) {
+      const float4 x = *reinterpret_cast<const float4*>(qrow + ((c4 ^ (row & 7)) << 4));
+      q[4 * c4] = x.x, q[4 * c4 + 1] = x.y, q[4 * c4 + 2] = x.z, q[4 * c4 + 3] = x.w;
+    }
+    tc::tmem_st32(taddr_q + 32 * hf, q);
+  }
+  tc::tmem_wait_st();
+}
+
 template <bool BIAS, bool SPLIT>
 __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     attn_tf32_kernel(const __grid_constant__ TmaLaunch L) {
@@ -252,7 +272,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
-    mbar_init(&B->q_empty, SPLIT ? 128 : 1);  // split kernel: the softmax threads release the Q tile
+    mbar_init(&B->q_empty, 128);  // the softmax threads release the Q tile once it is in TMEM
     for (int s = 0; s < kNS; ++s) {
       mbar_init(&B->kv_full[s], 1);
       mbar_init(&B->kv_empty[s], 1);
@@ -418,9 +438,9 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       asm volatile("" : "+r"(Lk));  // kept in a register (see the softmax warps)
       // split kernel: the softmax threads split this tile's Q only after the previous tile's
       // epilogue, which waits for that tile's last PV product: issue it first
-      if (SPLIT && pend_n >= 0) ok = issue_pv();
+      if (pend_n >= 0) ok = issue_pv();
       if (!ok) break;
-      ok = __all_sync(0xffffffffu, wait_or_abort(SPLIT ? &B->q_conv : &B->q_full, (uint32_t)(k & 1), abort, L.status,
+      ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_conv, (uint32_t)(k & 1), abort, L.status,
                                                  W_Q_FULL, n));
       for (int j = 0; ok && j < T.nblk; ++j, ++n) {
         const int s = n % kNS;
@@ -432,36 +452,27 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         if (lane == 0) {
           const uint8_t* kb = Ks + s * kKVBytes;
           const uint32_t scol = tmem + (b ? COL_S1 : COL_S0);
-          auto s_product = [&](const uint8_t* q, const uint8_t* kk, bool first) {
+          // S = Q K^T with Q from TMEM (the split kernel: lo(Q) hi(K) + hi(Q) lo(K) + hi(Q) hi(K),
+          // the small terms first)
+          auto s_product_t = [&](uint32_t qcol, const uint8_t* kk, bool first) {
 #pragma unroll
             for (int k8 = 0; k8 < kD / 8; ++k8) {
-              const uint32_t off = (uint32_t)(k8 >> 2) * kQSlab + (uint32_t)(k8 & 3) * 32u;
               const uint32_t offk = (uint32_t)(k8 >> 2) * kKVSlab + (uint32_t)(k8 & 3) * 32u;
-              tc::mma_tf32_ss(scol, tc::smem_desc(q + off, 16, 1024, tc::kLayoutSW128),
-                              tc::smem_desc(kk + offk, 16, 1024, tc::kLayoutSW128), idS, (!first || k8 > 0) ? 1u : 0u);
+              tc::mma_tf32_ts(scol, tmem + qcol + 8 * k8, tc::smem_desc(kk + offk, 16, 1024, tc::kLayoutSW128), idS,
+                              (!first || k8 > 0) ? 1u : 0u);
             }
           };
           if (SPLIT) {
-            // S = lo(Q) hi(K) + hi(Q) lo(K) + hi(Q) hi(K), the small terms first; Q from TMEM
             const uint8_t* kl = KLs + s * kKVBytes;
-            auto s_product_t = [&](uint32_t qcol, const uint8_t* kk, bool first) {
-#pragma unroll
-              for (int k8 = 0; k8 < kD / 8; ++k8) {
-                const uint32_t offk = (uint32_t)(k8 >> 2) * kKVSlab + (uint32_t)(k8 & 3) * 32u;
-                tc::mma_tf32_ts(scol, tmem + qcol + 8 * k8, tc::smem_desc(kk + offk, 16, 1024, tc::kLayoutSW128), idS,
-                                (!first || k8 > 0) ? 1u : 0u);
-              }
-            };
             const uint32_t qh = (k & 1) ? COL_Q1 : COL_Q0, ql = qh + 64;
             s_product_t(ql, kb, true);
             s_product_t(qh, kl, false);
             s_product_t(qh, kb, false);
           } else {
-            s_product(Qs, kb, true);
+            s_product_t(COL_QP, kb, true);
           }
           tc::commit(&B->kv_empty[s]);  // the K stage is free once S is done
           tc::commit(&B->s_full[b]);
-          if (!SPLIT && j == T.nblk - 1) tc::commit(&B->q_empty);  // the Q tile is no longer read
         }
         __syncwarp();
         if (pend_n >= 0) ok = issue_pv();
@@ -497,16 +508,18 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
       if constexpr (SPLIT) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) o[c] = 0.f;
-        if (kt == 0) {
-          // the first tile's Q; later tiles' Q rows are split during the previous tile's last
-          // block (into the other Q buffer), and the smem tile is released right after
-          ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, 0u, abort, L.status, W_CONV_Q, n));
-          if (!ok) break;
-          split_q_row(Qs, row, tl + COL_Q0);
-          tc::fence_before_sync();
-          mbar_arrive(&B->q_conv);
-          mbar_arrive(&B->q_empty);
-        }
+      }
+      if (kt == 0) {
+        // the first tile's Q into TMEM; later tiles' Q rows go there during the previous tile's
+        // last block (split kernel: into the other Q buffer), and the smem tile is released
+        // right after, so the next tile's Q copy is in flight while this tile runs
+        ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, 0u, abort, L.status, W_CONV_Q, n));
+        if (!ok) break;
+        if constexpr (SPLIT) split_q_row(Qs, row, tl + COL_Q0);
+        else copy_q_row(Qs, row, tl + COL_QP);
+        tc::fence_before_sync();
+        mbar_arrive(&B->q_conv);
+        mbar_arrive(&B->q_empty);
       }
       for (int j = 0; j < T.nblk; ++j, ++n) {
         const int b = n & 1;
@@ -671,6 +684,20 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         tc::tmem_wait_st();
         tc::fence_before_sync();
         mbar_arrive(&B->p_full[b]);
+        if (j == T.nblk - 1) {
+          // this tile's last S product is done: the CTA's next tile's Q rows into TMEM
+          int tn = L.total;
+          ok = __all_sync(0xffffffffu, tile_at(tab, kt + 1, &tn, abort, L.status));
+          if (!ok) break;
+          if (tn < L.total) {
+            ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)((kt + 1) & 1), abort, L.status, W_CONV_Q, n));
+            if (!ok) break;
+            copy_q_row(Qs, row, tl + COL_QP);
+            tc::fence_before_sync();
+            mbar_arrive(&B->q_conv);
+            mbar_arrive(&B->q_empty);
+          }
+        }
       }
       if (!ok) break;
       // epilogue: O of this tile is complete after its last PV product
