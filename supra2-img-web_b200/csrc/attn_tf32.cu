@@ -5,7 +5,7 @@
 //
 // Same math as the reference's fused kernel (app/gpu/kernels.js:164-316: online softmax over key
 // blocks, O / l at the end), with both contractions on the 5th-generation tensor cores:
-//   S_n = Q K_n^T   tcgen05.mma kind::tf32, A = Q (smem, K-major), B = K_n (smem, K-major),
+//   S_n = Q K_n^T   tcgen05.mma kind::tf32, A = Q (TMEM), B = K_n (smem, K-major),
 //                   D = S_n in TMEM (128 lanes = query rows x 64 columns = keys), fp32
 //   P_n            softmax warps read S_n from TMEM (one row per thread), compute
 //                   exp2(s*scale*log2e - m), round to TF32 and write P_n over S_n in TMEM
@@ -15,13 +15,17 @@
 // that flows through separate K and V rings (2 stages each; a K stage is released once its S
 // product is done, a V stage once its PV product is) and a double-buffered S/P in TMEM without
 // draining at tile boundaries. 6 warps:
-//   warp 0     TMA producer: lane 0 per tile the Q tile (once the previous tile's last S product
-//              has read the old one), then the K blocks of 64 keys; lane 1 the V blocks, so K
-//              runs ahead of the V stages
+//   warp 0     TMA producer: lane 0 per tile the Q tile (as soon as the softmax threads have
+//              copied the previous one into TMEM, so it lands while the previous tile runs),
+//              then the K blocks of 64 keys; lane 1 the V blocks, so K runs ahead of the V stages
 //   warp 1     TMEM allocation and the single-thread MMA issuer; S_n is issued before PV_{n-1}
 //              so the tensor core computes S_n while the softmax warps work on P_{n-1}
 //   warps 2-5  softmax and epilogue; warp w owns TMEM lanes 32*(w%4) .. +31 (query rows)
-// TMEM: S/P double buffer (2 x 64 columns) and O (64 columns): 256 columns, two CTAs per SM.
+// TMEM: S/P double buffer (2 x 64 columns), O (64 columns) and Q (64 columns, the softmax threads
+// copy each tile's Q rows there from the landed tile: at the start of the CTA's first tile, and
+// for later tiles right after the previous tile's last P, once its last S product is done):
+// 256 columns, two CTAs per SM. The MMA warp issues a tile's last PV before it waits for the next
+// tile's Q in TMEM.
 // The running maximum moves lazily (only when a block exceeds it by more than 8 in log2 units),
 // so O is rarely rescaled; when it is, the softmax warps wait for the previous PV product and
 // rescale O in TMEM. The first PV of a tile overwrites O once the previous tile's epilogue has
