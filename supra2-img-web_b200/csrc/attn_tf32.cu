@@ -566,9 +566,13 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
 #pragma unroll
             for (int c = 0; c < 64; ++c) v[c] = (c < nk) ? v[c] : -INFINITY;
           }
-          float rm = -INFINITY;
+          // (eight partial maxima: a 64-long chain of dependent max operations cost ~256 cycles)
+          float rp[8];
 #pragma unroll
-          for (int c = 0; c < 64; ++c) rm = fmaxf(rm, v[c]);
+          for (int u = 0; u < 8; ++u) rp[u] = v[u];
+#pragma unroll
+          for (int c = 8; c < 64; ++c) rp[c & 7] = fmaxf(rp[c & 7], v[c]);
+          const float rm = fmaxf(fmaxf(fmaxf(rp[0], rp[1]), fmaxf(rp[2], rp[3])), fmaxf(fmaxf(rp[4], rp[5]), fmaxf(rp[6], rp[7])));
           mx = rm * sl2;
         } else {
 #pragma unroll
@@ -676,14 +680,19 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           l *= alpha;
         }
         if (move) m = mx;
-        float ps = 0.f;
+        // (four packed partial sums rather than one 64-long chain of dependent adds)
+        float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 vs2 = make_float2(vs, vs), nm2 = make_float2(-m, -m);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p = tc::to_tf32(ex2(fmaf(v[c], vs, -m)));
-          ps += p;
-          v[c] = p;
+        for (int c = 0; c < 64; c += 2) {
+          const float2 a = __ffma2_rn(make_float2(v[c], v[c + 1]), vs2, nm2);
+          const float2 p = make_float2(tc::to_tf32(ex2(a.x)), tc::to_tf32(ex2(a.y)));
+          ps2[(c >> 1) & 3] = __fadd2_rn(ps2[(c >> 1) & 3], p);
+          v[c] = p.x;
+          v[c + 1] = p.y;
         }
-        l += ps;
+        const float2 pt = __fadd2_rn(__fadd2_rn(ps2[0], ps2[1]), __fadd2_rn(ps2[2], ps2[3]));
+        l += pt.x + pt.y;
         tc::tmem_st64(tl + scol, v);
         tc::tmem_wait_st();
         tc::fence_before_sync();
