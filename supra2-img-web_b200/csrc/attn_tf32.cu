@@ -236,6 +236,17 @@ __device__ __forceinline__ void split_q_row(const uint8_t* Qs, int row, uint32_t
   }
 }
 
+// Maximum of a row's 64 scores through eight partial maxima (one 64-long chain of dependent max
+// operations cost ~256 cycles per block).
+__device__ __forceinline__ float max64(const float (&v)[64]) {
+  float rp[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) rp[u] = v[u];
+#pragma unroll
+  for (int c = 8; c < 64; ++c) rp[c & 7] = fmaxf(rp[c & 7], v[c]);
+  return fmaxf(fmaxf(fmaxf(rp[0], rp[1]), fmaxf(rp[2], rp[3])), fmaxf(fmaxf(rp[4], rp[5]), fmaxf(rp[6], rp[7])));
+}
+
 // Plain kernel, softmax threads: this thread's row of the landed Q tile into TMEM at column qc of
 // its lane, unchanged (the tensor core reads it as TF32).
 __device__ __forceinline__ void copy_q_row(const uint8_t* Qs, int row, uint32_t taddr_q) {
@@ -545,19 +556,17 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
             const float b = t5_table_bias(tab_h, lut_c, rel_max, Hu, rel0 + c);
-            const float x = (c < nk) ? fmaf(b, 1.4426950408889634f, v[c] * sl2) : -INFINITY;
-            v[c] = x;
-            mx = fmaxf(mx, x);
+            v[c] = (c < nk) ? fmaf(b, 1.4426950408889634f, v[c] * sl2) : -INFINITY;
           }
+          mx = max64(v);
         } else if (BIAS && T.q0 + row < Lq) {
           // this thread's query row of the bias, keys j*64 .. j*64 + nk (exp2 domain: times log2 e)
           const float* brow = pp->bias + ((int64_t)T.h * Lq + T.q0 + row) * Lk + (int64_t)j * kN;
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
-            const float x = (c < nk) ? fmaf(__ldg(brow + c), 1.4426950408889634f, v[c] * sl2) : -INFINITY;
-            v[c] = x;
-            mx = fmaxf(mx, x);
+            v[c] = (c < nk) ? fmaf(__ldg(brow + c), 1.4426950408889634f, v[c] * sl2) : -INFINITY;
           }
+          mx = max64(v);
         } else if constexpr (!BIAS) {
           // no bias: the scores stay raw and the scale goes into the exponent's FFMA below; with
           // scale > 0 the raw row maximum times the scale is the scaled maximum. Keys past Lk
@@ -566,21 +575,13 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
 #pragma unroll
             for (int c = 0; c < 64; ++c) v[c] = (c < nk) ? v[c] : -INFINITY;
           }
-          // (eight partial maxima: a 64-long chain of dependent max operations cost ~256 cycles)
-          float rp[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) rp[u] = v[u];
-#pragma unroll
-          for (int c = 8; c < 64; ++c) rp[c & 7] = fmaxf(rp[c & 7], v[c]);
-          const float rm = fmaxf(fmaxf(fmaxf(rp[0], rp[1]), fmaxf(rp[2], rp[3])), fmaxf(fmaxf(rp[4], rp[5]), fmaxf(rp[6], rp[7])));
-          mx = rm * sl2;
+          mx = max64(v) * sl2;
         } else {
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
-            const float x = (c < nk) ? v[c] * sl2 : -INFINITY;
-            v[c] = x;
-            mx = fmaxf(mx, x);
+            v[c] = (c < nk) ? v[c] * sl2 : -INFINITY;
           }
+          mx = max64(v);
         }
         const float vs = BIAS ? 1.f : sl2;  // exponent = v * vs - m
         const bool move = mx > m + 8.f;
@@ -592,7 +593,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           const float alpha = move ? ex2(m - mx) : 1.f;  // 0 on a tile's first block (m = -inf)
           if (move) m = mx;
           const float2 vs2 = make_float2(vs, vs), nm2 = make_float2(-m, -m);
-          float2 ps2 = make_float2(0.f, 0.f);
+          float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
             float2 a = __ffma2_rn(make_float2(v[c], v[c + 1]), vs2, nm2);
@@ -600,9 +601,10 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
             a.y = ex2(a.y);
             v[c] = a.x;
             v[c + 1] = a.y;
-            ps2 = __fadd2_rn(ps2, a);
+            ps2[(c >> 1) & 3] = __fadd2_rn(ps2[(c >> 1) & 3], a);
           }
-          l = l * alpha + (ps2.x + ps2.y);
+          const float2 pt = __fadd2_rn(__fadd2_rn(ps2[0], ps2[1]), __fadd2_rn(ps2[2], ps2[3]));
+          l = l * alpha + (pt.x + pt.y);
           const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
