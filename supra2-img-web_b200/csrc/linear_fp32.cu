@@ -38,8 +38,11 @@ template <int BN>
 constexpr int smem_bytes() { return stages_of<BN>() == 2 ? 0 : stages_of<BN>() * (kBM + BN) * kS * 4; }
 // the TMA-staged form: four stages in flight, 128-byte aligned boxes, one mbarrier per stage
 constexpr int kTmaStages = 4;
+// x^T of the stage being computed: [kBK][kTS], row r of x at position 8 (r % 16) + r / 16, so a
+// thread's 8 rows (rg + 16i) are two float4 at 8rg
+constexpr int kTS = kBM + 4;
 template <int BN>
-constexpr int tma_smem_bytes() { return 128 + kTmaStages * (kBM + BN) * kS * 4 + kTmaStages * 8; }
+constexpr int tma_smem_bytes() { return 128 + (kTmaStages * (kBM + BN) * kS + kBK * kTS) * 4 + kTmaStages * 8; }
 
 // GroupNorm (+ SiLU) or LayerNorm (+ modulation) of a staged x tile `a` (stage st of the tile at
 // rows r0.., nr of them valid), per element of a valid row and column (padding stays zero):
@@ -100,6 +103,50 @@ __device__ __forceinline__ void mma_stage(const float* a, const float* b, int rg
   }
 }
 
+// The stage's x tile `a` ([kBM][kS], row-major) into x^T `at`: thread tid moves rows rg + 16 (2ip)
+// and rg + 16 (2ip + 1) (rg = tid % 16, ip = tid / 16 % 4) of k4 group tid / 64, two float4 loads
+// and four float2 stores (the two rows sit side by side in x^T).
+__device__ __forceinline__ void transpose_stage(const float* __restrict__ a, float* __restrict__ at, int tid) {
+  const int rg = tid & 15, ip = (tid >> 4) & 3, k4 = tid >> 6;
+  const int r = rg + 32 * ip;
+  const float4 x0 = *reinterpret_cast<const float4*>(a + r * kS + 4 * k4);
+  const float4 x1 = *reinterpret_cast<const float4*>(a + (r + 16) * kS + 4 * k4);
+  float* d = at + (4 * k4) * kTS + 8 * rg + 2 * ip;
+  *reinterpret_cast<float2*>(d) = make_float2(x0.x, x1.x);
+  *reinterpret_cast<float2*>(d + kTS) = make_float2(x0.y, x1.y);
+  *reinterpret_cast<float2*>(d + 2 * kTS) = make_float2(x0.z, x1.z);
+  *reinterpret_cast<float2*>(d + 3 * kTS) = make_float2(x0.w, x1.w);
+}
+
+// acc += the stage's x^T (rows rg + 16i in pairs: acc[p][j] holds rows rg + 32p (x) and
+// rg + 32p + 16 (y)) times its W tile (rows cg + 16j), kBK deep, with packed f32x2 FMAs: one W
+// value (broadcast) times the x values of two rows
+template <int NJ>
+__device__ __forceinline__ void mma_stage_t(const float* at, const float* b, int rg, int cg, float2 (&acc)[4][NJ]) {
+  const float4* A4 = reinterpret_cast<const float4*>(at) + 2 * rg;
+  const float4* B4 = reinterpret_cast<const float4*>(b) + cg * (kS / 4);
+#pragma unroll
+  for (int k4 = 0; k4 < kBK / 4; ++k4) {
+    float4 bf[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 q0 = A4[(4 * k4 + e) * (kTS / 4)];
+      const float4 q1 = A4[(4 * k4 + e) * (kTS / 4) + 1];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const float w = e == 0 ? bf[j].x : e == 1 ? bf[j].y : e == 2 ? bf[j].z : bf[j].w;
+        const float2 w2 = make_float2(w, w);
+        acc[0][j] = __ffma2_rn(make_float2(q0.x, q0.y), w2, acc[0][j]);
+        acc[1][j] = __ffma2_rn(make_float2(q0.z, q0.w), w2, acc[1][j]);
+        acc[2][j] = __ffma2_rn(make_float2(q1.x, q1.y), w2, acc[2][j]);
+        acc[3][j] = __ffma2_rn(make_float2(q1.z, q1.w), w2, acc[3][j]);
+      }
+    }
+  }
+}
+
 // y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
 template <bool BIAS, int NJ>
 __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&acc)[8][NJ], int r0, int c0, int nr,
@@ -139,8 +186,14 @@ __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&
 // stage thread 0 issues two tensor copies, a [128 x 20] box of x and a [BN x 20] box of W (the 4
 // columns past the stage's 16 pad the shared-memory rows against bank conflicts and are never
 // read; past K and past the last row the copies read zeros), completing on the stage's mbarrier,
-// kStages - 1 stages ahead. The 256 threads only compute: the per-thread cp.async form spent a
-// third of its issue slots on copy addresses and predicates.
+// three stages ahead. The 256 threads only compute: the per-thread cp.async form spent a third of
+// its issue slots on copy addresses and predicates. Each stage's x tile is first transposed in
+// shared memory (x^T, 8 values per thread), so that the products run as packed f32x2 FMAs of two
+// rows' x values by one W value: half the FMA instructions of the scalar form (which, with its
+// 16 fragment loads per 256 FMAs, kept the schedulers near their issue limit), as the 256-row
+// attention kernel's Q^T K does. Two barriers per stage: after the wait for the stage's copies
+// (every thread is also done with the previous stage, whose buffers thread 0 then refills) and
+// after the transposition.
 template <bool BIAS, int BN>
 __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_constant__ LinLaunch L) {
   constexpr int NJ = BN / 16;
@@ -148,7 +201,8 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   const uint32_t raw = smem_u32(lin_raw);
   float* const As = reinterpret_cast<float*>(lin_raw + (((raw + 127u) & ~127u) - raw));  // [kTmaStages][kBM * kS]
   float* const Bs = As + kTmaStages * kBM * kS;                                                  // [kTmaStages][BN * kS]
-  uint64_t* const full = reinterpret_cast<uint64_t*>(Bs + kTmaStages * BN * kS);                // [kTmaStages]
+  float* const At = Bs + kTmaStages * BN * kS;                                                   // [kBK][kTS]
+  uint64_t* const full = reinterpret_cast<uint64_t*>(At + kBK * kTS);                            // [kTmaStages]
   const int t = blockIdx.x;
   if (t >= L.total) {
     if (threadIdx.x == 0) report_error(L.status, DEV_BAD_TILE, 30);
@@ -185,30 +239,37 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
 #pragma unroll
     for (int s = 0; s < kTmaStages; ++s) issue(s);
   }
-  float acc[8][NJ];
+  float2 acc[4][NJ];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int p = 0; p < 4; ++p)
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < NJ; ++j) acc[p][j] = make_float2(0.f, 0.f);
   for (int st = 0; st < nstage; ++st) {
     const int buf = st % kTmaStages;
-    // every thread waits for the stage (bounded); a vote keeps the CTA together if a wait runs out
+    // every thread waits for the stage (bounded); a vote keeps the CTA together if a wait runs
+    // out. Past it every thread is done with stage st - 1, whose buffers take stage st + 3.
     const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)((st / kTmaStages) & 1));
     if (!__syncthreads_and(ok)) {
       if (tid == 0) report_error(L.status, DEV_TIMEOUT, 31, st);
       return;
     }
+    if (tid == 0 && st > 0) issue(st + kTmaStages - 1);
     float* a = As + buf * kBM * kS;
     if (P.gn_stats) {
       norm_stage(P, a, st, r0, nr, tid);
       __syncthreads();
     }
-    mma_stage<NJ>(a, Bs + buf * BN * kS, rg, cg, acc);
-    fence_proxy_async_smem();  // this thread's reads (and norm writes) of the buffer before the next copy
-    __syncthreads();           // every thread is done with the buffer
-    if (tid == 0) issue(st + kTmaStages);
+    transpose_stage(a, At, tid);
+    __syncthreads();  // x^T complete
+    mma_stage_t<NJ>(At, Bs + buf * BN * kS, rg, cg, acc);
+    fence_proxy_async_smem();  // this thread's reads (and norm writes) of the buffers before they are refilled
   }
-  linear_epilogue<BIAS, NJ>(P, acc, r0, c0, nr, nc, rg, cg);
+  float accf[8][NJ];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) accf[i][j] = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
+  linear_epilogue<BIAS, NJ>(P, accf, r0, c0, nr, nc, rg, cg);
 }
 
 // The same product with the tiles staged by per-thread cp.async (any alignment: 4-byte copies
