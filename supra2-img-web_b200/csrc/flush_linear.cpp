@@ -90,9 +90,9 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
       const supra::LinProb& q = lp[i];
       const float* xb = xn[i] >= 0 ? c->lin_split + xn[i] : q.x;
       const int64_t ldx = xn[i] >= 0 ? q.K : q.ldx;
-      int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(xb), ldx, q.M, q.K, 20, 128, 0, 0}, maps, &lp[i].mx);
+      int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(xb), ldx, q.M, q.K, supra::kLinBoxCols, 128, 0, 0}, maps, &lp[i].mx);
       if (!rc0)
-        rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, 20, cols, 0, 0}, maps, &lp[i].mw);
+        rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, supra::kLinBoxCols, cols, 0, 0}, maps, &lp[i].mw);
       if (rc0) {  // a shape the driver's encoder refuses: the group runs the per-thread copy form
         tma = false;
         maps.clear();

@@ -174,6 +174,10 @@ constexpr int kNormAffine = 0, kNormModulated = 1, kNormPlain = 2;
 // Activation in the linear epilogue (LinProb::act), the values of SUPRA_ATTN_ACT_*.
 constexpr int kActNone = 0, kActGelu = 1, kActGeluTanh = 2, kActSilu = 3;
 
+// Columns of the x and W tensor-map boxes of the TMA-staged FFMA linear: 32 of K per stage plus 4
+// that pad the shared-memory rows.
+constexpr int kLinBoxCols = 36;
+
 // y = x W^T (+ bias) for one ops.linear call (app/gpu/ops.js:35-43), linear_fp32.cu. x rows of
 // stride ldx (the caller's x offset already applied), W [N, K] row-major with row stride ldw,
 // y rows of stride ldy (offset applied).

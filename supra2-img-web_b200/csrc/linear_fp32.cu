@@ -36,13 +36,17 @@ constexpr int stages_of() { return BN == 64 ? 4 : 2; }
 // dynamic shared memory of the form (the two-stage form's arrays are static)
 template <int BN>
 constexpr int smem_bytes() { return stages_of<BN>() == 2 ? 0 : stages_of<BN>() * (kBM + BN) * kS * 4; }
-// the TMA-staged form: four stages in flight, 128-byte aligned boxes, one mbarrier per stage
-constexpr int kTmaStages = 4;
-// x^T of the stage being computed: [kBK][kTS], row r of x at position 8 (r % 16) + r / 16, so a
+// the TMA-staged form: 32-deep stages (one pair of barriers per 32 k), two in flight (a stage's
+// products take several microseconds, well over a copy's latency from L2), 128-byte aligned boxes
+// of kLinBoxCols columns, one mbarrier per stage
+constexpr int kTmaStages = 2;
+constexpr int kBKT = kLinBoxCols - 4;  // reduction depth per stage
+constexpr int kST = kLinBoxCols;       // row stride of the stage buffers
+// x^T of the stage being computed: [kBKT][kTS], row r of x at position 8 (r % 16) + r / 16, so a
 // thread's 8 rows (rg + 16i) are two float4 at 8rg
 constexpr int kTS = kBM + 4;
 template <int BN>
-constexpr int tma_smem_bytes() { return 128 + (kTmaStages * (kBM + BN) * kS + kBK * kTS) * 4 + kTmaStages * 8; }
+constexpr int tma_smem_bytes() { return 128 + (kTmaStages * (kBM + BN) * kST + kBKT * kTS) * 4 + kTmaStages * 8; }
 
 // GroupNorm (+ SiLU) or LayerNorm (+ modulation) of a staged x tile `a` (stage st of the tile at
 // rows r0.., nr of them valid), per element of a valid row and column (padding stays zero):
@@ -51,9 +55,10 @@ constexpr int tma_smem_bytes() { return 128 + (kTmaStages * (kBM + BN) * kS + kB
 // tid / 16 + 16 i: its column's g, b and group are one lookup per stage, its rows' images one per
 // tile. (Per element, with two integer divisions and three global loads, it cost as much as the
 // stage's FMAs.)
+template <int BK = kBK, int S = kS>
 __device__ __forceinline__ void norm_stage(const LinProb& P, float* a, int st, int r0, int nr, int tid) {
-  const int kk = tid & 15, rb = tid >> 4;
-  const int k = st * kBK + kk;
+  const int kk = tid % BK, rb = tid / BK;
+  const int k = st * BK + kk;
   if (k >= P.K) return;
   float g = 1.f, b = 0.f;
   if (P.gn_mode != kNormPlain) {
@@ -67,14 +72,14 @@ __device__ __forceinline__ void norm_stage(const LinProb& P, float* a, int st, i
   const bool one_img = P.gn_rows % kBM == 0;
   const int img0 = one_img ? r0 / P.gn_rows : 0;
 #pragma unroll
-  for (int it = 0; it < kBM / 16; ++it) {
-    const int r = rb + 16 * it;
+  for (int it = 0; it < kBM * BK / kT; ++it) {
+    const int r = rb + (kT / BK) * it;
     if (r < nr) {
       const int img = one_img ? img0 : (P.gn_rows == 1 ? r0 + r : (r0 + r) / P.gn_rows);
       const float2 ms = __ldg(st_k + (int64_t)img * P.gn_groups);
-      float v = (a[r * kS + kk] - ms.x) * (ms.y * g) + b;
+      float v = (a[r * S + kk] - ms.x) * (ms.y * g) + b;
       if (P.gn_silu) v = v / (1.f + __expf(-v));
-      a[r * kS + kk] = v;
+      a[r * S + kk] = v;
     }
   }
 }
@@ -107,15 +112,18 @@ __device__ __forceinline__ void mma_stage(const float* a, const float* b, int rg
 // and rg + 16 (2ip + 1) (rg = tid % 16, ip = tid / 16 % 4) of k4 group tid / 64, two float4 loads
 // and four float2 stores (the two rows sit side by side in x^T).
 __device__ __forceinline__ void transpose_stage(const float* __restrict__ a, float* __restrict__ at, int tid) {
-  const int rg = tid & 15, ip = (tid >> 4) & 3, k4 = tid >> 6;
+  const int rg = tid & 15, ip = (tid >> 4) & 3;
   const int r = rg + 32 * ip;
-  const float4 x0 = *reinterpret_cast<const float4*>(a + r * kS + 4 * k4);
-  const float4 x1 = *reinterpret_cast<const float4*>(a + (r + 16) * kS + 4 * k4);
-  float* d = at + (4 * k4) * kTS + 8 * rg + 2 * ip;
-  *reinterpret_cast<float2*>(d) = make_float2(x0.x, x1.x);
-  *reinterpret_cast<float2*>(d + kTS) = make_float2(x0.y, x1.y);
-  *reinterpret_cast<float2*>(d + 2 * kTS) = make_float2(x0.z, x1.z);
-  *reinterpret_cast<float2*>(d + 3 * kTS) = make_float2(x0.w, x1.w);
+#pragma unroll
+  for (int k4 = tid >> 6; k4 < kBKT / 4; k4 += kT / 64) {
+    const float4 x0 = *reinterpret_cast<const float4*>(a + r * kST + 4 * k4);
+    const float4 x1 = *reinterpret_cast<const float4*>(a + (r + 16) * kST + 4 * k4);
+    float* d = at + (4 * k4) * kTS + 8 * rg + 2 * ip;
+    *reinterpret_cast<float2*>(d) = make_float2(x0.x, x1.x);
+    *reinterpret_cast<float2*>(d + kTS) = make_float2(x0.y, x1.y);
+    *reinterpret_cast<float2*>(d + 2 * kTS) = make_float2(x0.z, x1.z);
+    *reinterpret_cast<float2*>(d + 3 * kTS) = make_float2(x0.w, x1.w);
+  }
 }
 
 // acc += the stage's x^T (rows rg + 16i in pairs: acc[p][j] holds rows rg + 32p (x) and
@@ -124,12 +132,12 @@ __device__ __forceinline__ void transpose_stage(const float* __restrict__ a, flo
 template <int NJ>
 __device__ __forceinline__ void mma_stage_t(const float* at, const float* b, int rg, int cg, float2 (&acc)[4][NJ]) {
   const float4* A4 = reinterpret_cast<const float4*>(at) + 2 * rg;
-  const float4* B4 = reinterpret_cast<const float4*>(b) + cg * (kS / 4);
+  const float4* B4 = reinterpret_cast<const float4*>(b) + cg * (kST / 4);
 #pragma unroll
-  for (int k4 = 0; k4 < kBK / 4; ++k4) {
+  for (int k4 = 0; k4 < kBKT / 4; ++k4) {
     float4 bf[NJ];
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kS / 4) + k4];
+    for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kST / 4) + k4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float4 q0 = A4[(4 * k4 + e) * (kTS / 4)];
@@ -183,10 +191,10 @@ __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&
 // columns cg + 16j (j < BN / 16).
 
 // Tiles staged by TMA (x and W 16-byte aligned with row strides of a multiple of 4 floats): per
-// stage thread 0 issues two tensor copies, a [128 x 20] box of x and a [BN x 20] box of W (the 4
-// columns past the stage's 16 pad the shared-memory rows against bank conflicts and are never
+// stage thread 0 issues two tensor copies, a [128 x 36] box of x and a [BN x 36] box of W (the 4
+// columns past the stage's 32 pad the shared-memory rows against bank conflicts and are never
 // read; past K and past the last row the copies read zeros), completing on the stage's mbarrier,
-// three stages ahead. The 256 threads only compute: the per-thread cp.async form spent a third of
+// one stage ahead. The 256 threads only compute: the per-thread cp.async form spent a third of
 // its issue slots on copy addresses and predicates. Each stage's x tile is first transposed in
 // shared memory (x^T, 8 values per thread), so that the products run as packed f32x2 FMAs of two
 // rows' x values by one W value: half the FMA instructions of the scalar form (which, with its
@@ -199,10 +207,10 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   constexpr int NJ = BN / 16;
   extern __shared__ uint8_t lin_raw[];
   const uint32_t raw = smem_u32(lin_raw);
-  float* const As = reinterpret_cast<float*>(lin_raw + (((raw + 127u) & ~127u) - raw));  // [kTmaStages][kBM * kS]
-  float* const Bs = As + kTmaStages * kBM * kS;                                                  // [kTmaStages][BN * kS]
-  float* const At = Bs + kTmaStages * BN * kS;                                                   // [kBK][kTS]
-  uint64_t* const full = reinterpret_cast<uint64_t*>(At + kBK * kTS);                            // [kTmaStages]
+  float* const As = reinterpret_cast<float*>(lin_raw + (((raw + 127u) & ~127u) - raw));  // [kTmaStages][kBM * kST]
+  float* const Bs = As + kTmaStages * kBM * kST;                                                 // [kTmaStages][BN * kST]
+  float* const At = Bs + kTmaStages * BN * kST;                                                  // [kBKT][kTS]
+  uint64_t* const full = reinterpret_cast<uint64_t*>(At + kBKT * kTS);                           // [kTmaStages]
   const int t = blockIdx.x;
   if (t >= L.total) {
     if (threadIdx.x == 0) report_error(L.status, DEV_BAD_TILE, 30);
@@ -216,7 +224,7 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   const int c0 = (local - rt * P.n_tiles) * BN;
   const int nr = min(kBM, P.M - r0);
   const int nc = min(BN, P.N - c0);
-  const int nstage = (P.K + kBK - 1) / kBK;
+  const int nstage = (P.K + kBKT - 1) / kBKT;
   const CUtensorMap* mx = L.maps + P.mx;
   const CUtensorMap* mw = L.maps + P.mw;
   const int tid = threadIdx.x;
@@ -230,9 +238,9 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   auto issue = [&](int st) {  // (thread 0)
     if (st < nstage) {
       const int buf = st % kTmaStages;
-      mbar_arrive_expect_tx(&full[buf], (uint32_t)((kBM + BN) * kS * 4));
-      tc::tma_load_2d(As + buf * kBM * kS, mx, st * kBK, r0, &full[buf]);
-      tc::tma_load_2d(Bs + buf * BN * kS, mw, st * kBK, c0, &full[buf]);
+      mbar_arrive_expect_tx(&full[buf], (uint32_t)((kBM + BN) * kST * 4));
+      tc::tma_load_2d(As + buf * kBM * kST, mx, st * kBKT, r0, &full[buf]);
+      tc::tma_load_2d(Bs + buf * BN * kST, mw, st * kBKT, c0, &full[buf]);
     }
   };
   if (tid == 0) {
@@ -247,21 +255,21 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   for (int st = 0; st < nstage; ++st) {
     const int buf = st % kTmaStages;
     // every thread waits for the stage (bounded); a vote keeps the CTA together if a wait runs
-    // out. Past it every thread is done with stage st - 1, whose buffers take stage st + 3.
+    // out. Past it every thread is done with stage st - 1, whose buffers take stage st + 1.
     const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)((st / kTmaStages) & 1));
     if (!__syncthreads_and(ok)) {
       if (tid == 0) report_error(L.status, DEV_TIMEOUT, 31, st);
       return;
     }
     if (tid == 0 && st > 0) issue(st + kTmaStages - 1);
-    float* a = As + buf * kBM * kS;
+    float* a = As + buf * kBM * kST;
     if (P.gn_stats) {
-      norm_stage(P, a, st, r0, nr, tid);
+      norm_stage<kBKT, kST>(P, a, st, r0, nr, tid);
       __syncthreads();
     }
     transpose_stage(a, At, tid);
     __syncthreads();  // x^T complete
-    mma_stage_t<NJ>(At, Bs + buf * BN * kS, rg, cg, acc);
+    mma_stage_t<NJ>(At, Bs + buf * BN * kST, rg, cg, acc);
     fence_proxy_async_smem();  // this thread's reads (and norm writes) of the buffers before they are refilled
   }
   float accf[8][NJ];
