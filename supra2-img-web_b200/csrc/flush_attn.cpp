@@ -117,6 +117,14 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
     };
     while (bm > 32 && qk_tiles(bm) < sms) bm /= 2;
   }
+  // FFMA path: with enough 128 x 128 score tiles to fill two CTAs per SM, S = Q K^T runs on the
+  // FFMA linear (TMA-staged, packed FMAs; the VAE at 8 or more images) rather than the score kernel
+  bool lin_qk = false;
+  if (!tc && !bias && aligned) {
+    int64_t t = 0;
+    for (const GemmUnit& u : units) t += (int64_t)((u.rows + 127) / 128) * ((g[u.prob]->p.Lk + 127) / 128);
+    lin_qk = t >= supra::attn_fp32_warp_cta_slots();
+  }
   std::vector<int32_t> qk(nu + 1), pv(nu + 1), rw(nu + 1);
   int64_t tq = 0, tp = 0, tr = 0;
   double fl = 0, by_qk = 0, by_sm = 0, by_pv = 0;
@@ -178,7 +186,7 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
   L.row_total = (int32_t)tr;
   L.status = c->d_status;
   L.lo = tc == 2 ? c->scratch + scratch_bytes / 4 : nullptr;
-  L.sm_scale = tc ? 1 : 0;
+  L.sm_scale = (tc || lin_qk) ? 1 : 0;
   L.bm = bm;
   cudaError_t e;
   if (tc) {
@@ -203,6 +211,26 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
       jobs[i] = TcJob{lp, 1.f, false, nullptr, nullptr, 0};
     }
     rc = run_linear_tc(c, jobs, tc == 2, fl, by_qk);
+    if (rc) return rc;
+  } else if (lin_qk) {
+    // the same products on the FFMA linear, unscaled (the softmax applies the scale)
+    std::vector<supra::LinProb> lps((size_t)nu);
+    for (int i = 0; i < nu; ++i) {
+      const GemmUnit& u = units[i];
+      const AttnProb& P = g[u.prob]->p;
+      supra::LinProb& lp = lps[i];
+      std::memset(&lp, 0, sizeof lp);
+      lp.x = P.q + P.q_off + (int64_t)u.row0 * P.ldq + (int64_t)u.h * P.D;
+      lp.ldx = P.ldq;
+      lp.w = P.k + P.k_off + (int64_t)u.h * P.D;
+      lp.ldw = P.ldk;
+      lp.y = c->scratch + u.s_off;
+      lp.ldy = u.ldS;
+      lp.M = u.rows;
+      lp.N = P.Lk;
+      lp.K = P.D;
+    }
+    rc = run_linear_fp32(c, lps, false, true, fl, by_qk, "attn_gemm_qk_lin");
     if (rc) return rc;
   } else {
     {

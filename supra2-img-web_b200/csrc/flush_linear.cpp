@@ -34,70 +34,53 @@ int norm_stats(supra_attn_ctx* c, const std::vector<const Queued*>& g, supra::Li
   return SUPRA_ATTN_OK;
 }
 
-int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
-  const int n = (int)g.size();
-  // Column tile width: 128 x 64 tiles cost about 0.55 of a 128 x 128 tile (a smaller register
-  // block reads more shared memory per FMA); take the width whose whole waves of the grid's CTA
-  // slots (two per SM) cost less. The DiT blocks' N = 576 products: 2 waves either way, 1.1 against
-  // 2.0 in tile costs; the stacked K/V preparation (N = 16128) keeps 128.
+// Column tile width of an FFMA linear launch: 128 x 64 tiles cost about 0.55 of a 128 x 128 tile
+// (a smaller register block reads more shared memory per FMA); take the width whose whole waves of
+// the grid's CTA slots (two per SM) cost less. The DiT blocks' N = 576 products: 2 waves either
+// way, 1.1 against 2.0 in tile costs; the stacked K/V preparation (N = 16128) keeps 128.
+static int linear_tile_cols(const std::vector<supra::LinProb>& lp) {
   int64_t t128 = 0, t64 = 0;
-  for (int i = 0; i < n; ++i) {
-    const int64_t mt = (g[i]->lin.M + 127) / 128;
-    t128 += mt * ((g[i]->lin.N + 127) / 128);
-    t64 += mt * ((g[i]->lin.N + 63) / 64);
+  for (const supra::LinProb& q : lp) {
+    const int64_t mt = (q.M + 127) / 128;
+    t128 += mt * ((q.N + 127) / 128);
+    t64 += mt * ((q.N + 63) / 64);
   }
   const int64_t slots = supra::attn_fp32_warp_cta_slots();
-  const int cols = 0.55 * (double)((t64 + slots - 1) / slots) < (double)((t128 + slots - 1) / slots) ? 64 : 128;
+  return 0.55 * (double)((t64 + slots - 1) / slots) < (double)((t128 + slots - 1) / slots) ? 64 : 128;
+}
+
+// One grouped FFMA linear launch over problems whose x is ready to be read as it is (any norm
+// prologue still set in gn_stats runs per staged tile). 16-byte aligned groups (`aligned`) stage
+// their tiles by TMA: a tensor map of x [M, K] with kLinBoxCols x 128 boxes and of W [N, K] with
+// kLinBoxCols x (tile columns) boxes per problem, cached per context like the attention kernels'
+// maps; a shape the driver's encoder refuses, or a misaligned group, takes the per-thread copy form.
+int run_linear_fp32(supra_attn_ctx* c, std::vector<supra::LinProb>& lp, bool bias, bool aligned, double flops,
+                    double bytes, const char* name) {
+  const int n = (int)lp.size();
+  const int cols = linear_tile_cols(lp);
   std::vector<int32_t> begin(n + 1);
   int64_t total = 0;
-  double flops = 0, bytes = 0;
   for (int i = 0; i < n; ++i) {
+    lp[i].n_tiles = (lp[i].N + cols - 1) / cols;
     begin[i] = (int32_t)total;
-    total += (int64_t)((g[i]->lin.M + 127) / 128) * ((g[i]->lin.N + cols - 1) / cols);
-    flops += g[i]->flops;
-    bytes += g[i]->bytes;
+    total += (int64_t)((lp[i].M + 127) / 128) * lp[i].n_tiles;
     if (total > INT32_MAX) return set_err(c, SUPRA_ATTN_EINVAL, "too many linear tiles in one flush");
   }
   begin[n] = (int32_t)total;
-  // A normalised x read by two or more column tiles is normalised once, into the context's split
-  // buffer ([M, K] dense), by a launch between its statistics and the product (which then reads it
-  // plainly): the prologue would normalise every x tile again for every column tile (the DiT
-  // block's qkv, N = 1728: 27 times). x of such problems is 16-byte aligned with K % 4 == 0.
-  std::vector<supra::LinProb> lp((size_t)n);
-  std::vector<int64_t> xn((size_t)n, -1);  // offset of the normalised x in lin_split, or -1
-  size_t xn_need = 0;
-  for (int i = 0; i < n; ++i) {
-    lp[i] = g[i]->lin;
-    lp[i].n_tiles = (lp[i].N + cols - 1) / cols;
-    if (lp[i].gn_rows > 0 && lp[i].n_tiles >= 2 && lp[i].K % 4 == 0 && (lp[i].ldx & 3) == 0 && aligned16(lp[i].x)) {
-      xn[i] = (int64_t)xn_need;
-      xn_need += align16((size_t)lp[i].M * lp[i].K * sizeof(float)) / sizeof(float);
-    }
-  }
-  if (xn_need) {
-    const int rc0 = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, xn_need, sizeof(float),
-                                "normalised x");
-    if (rc0) return rc0;
-  }
-  // 16-byte aligned operands (the group's `aligned`) are staged by TMA: a tensor map of x [M, K]
-  // with 20 x 128 boxes and of W [N, K] with 20 x (tile columns) boxes per problem, cached per
-  // context like the attention kernels' maps
-  bool tma = g[0]->aligned;
+  bool tma = aligned;
   std::vector<CUtensorMap> maps;
   ++c->map_epoch;
-  for (int i = 0; i < n; ++i) {
-    if (tma) {
-      const supra::LinProb& q = lp[i];
-      const float* xb = xn[i] >= 0 ? c->lin_split + xn[i] : q.x;
-      const int64_t ldx = xn[i] >= 0 ? q.K : q.ldx;
-      int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(xb), ldx, q.M, q.K, supra::kLinBoxCols, 128, 0, 0}, maps, &lp[i].mx);
-      if (!rc0)
-        rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, supra::kLinBoxCols, cols, 0, 0}, maps, &lp[i].mw);
-      if (rc0) {  // a shape the driver's encoder refuses: the group runs the per-thread copy form
-        tma = false;
-        maps.clear();
-        c->err.clear();
-      }
+  for (int i = 0; i < n && tma; ++i) {
+    const supra::LinProb& q = lp[i];
+    int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.x), q.ldx, q.M, q.K, supra::kLinBoxCols, 128, 0, 0},
+                       maps, &lp[i].mx);
+    if (!rc0)
+      rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, supra::kLinBoxCols, cols, 0, 0},
+                     maps, &lp[i].mw);
+    if (rc0) {
+      tma = false;
+      maps.clear();
+      c->err.clear();
     }
   }
   const size_t mbytes = sizeof(CUtensorMap) * maps.size();
@@ -111,24 +94,7 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   char* hm = h + pad;
   char* dm = dv + pad;
   if (mbytes) std::memcpy(hm, maps.data(), mbytes);
-  supra::LinProb* hp = reinterpret_cast<supra::LinProb*>(hm + mbytes);
-  std::memcpy(hp, lp.data(), sizeof(supra::LinProb) * n);
-  rc = norm_stats(c, g, hp);
-  if (rc) return rc;
-  for (int i = 0; i < n; ++i) {
-    if (xn[i] < 0) continue;
-    float* dst = c->lin_split + xn[i];
-    cudaError_t e;
-    {
-      ProfScope ps(c, "norm_apply", 0.0, 8.0 * (double)hp[i].M * hp[i].K);
-      e = supra::launch_norm_apply(hp[i], dst, c->stream);
-    }
-    if (e != cudaSuccess) return cuda_err(c, e, "norm_apply");
-    c->launches += 1;
-    hp[i].x = dst;
-    hp[i].ldx = hp[i].K;
-    hp[i].gn_stats = nullptr;  // the product reads x as it is
-  }
+  std::memcpy(hm + mbytes, lp.data(), sizeof(supra::LinProb) * n);
   std::memcpy(hm + mbytes + pbytes, begin.data(), bbytes);
   rc = ring_commit(c, h, dv, pad + mbytes + pbytes + bbytes);
   if (rc) return rc;
@@ -139,16 +105,62 @@ int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
   L.n = n;
   L.total = (int32_t)total;
   L.status = c->d_status;
-  const char* name = g[0]->bias ? "linear_fp32_bias" : "linear_fp32";
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = tma ? supra::launch_linear_fp32_tma(g[0]->bias, cols, L, c->stream)
-            : supra::launch_linear_fp32(g[0]->bias, false, cols, L, c->stream);
+    e = tma ? supra::launch_linear_fp32_tma(bias, cols, L, c->stream)
+            : supra::launch_linear_fp32(bias, false, cols, L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);
   c->launches += 1;
   return SUPRA_ATTN_OK;
+}
+
+int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g) {
+  const int n = (int)g.size();
+  std::vector<supra::LinProb> lp((size_t)n);
+  double flops = 0, bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    lp[i] = g[i]->lin;
+    flops += g[i]->flops;
+    bytes += g[i]->bytes;
+  }
+  const int cols = linear_tile_cols(lp);
+  // A normalised x read by two or more column tiles is normalised once, into the context's split
+  // buffer ([M, K] dense), by a launch between its statistics and the product (which then reads it
+  // plainly): the prologue would normalise every x tile again for every column tile (the DiT
+  // block's qkv, N = 1728: 27 times). x of such problems is 16-byte aligned with K % 4 == 0.
+  std::vector<int64_t> xn((size_t)n, -1);  // offset of the normalised x in lin_split, or -1
+  size_t xn_need = 0;
+  for (int i = 0; i < n; ++i) {
+    const int n_tiles = (lp[i].N + cols - 1) / cols;
+    if (lp[i].gn_rows > 0 && n_tiles >= 2 && lp[i].K % 4 == 0 && (lp[i].ldx & 3) == 0 && aligned16(lp[i].x)) {
+      xn[i] = (int64_t)xn_need;
+      xn_need += align16((size_t)lp[i].M * lp[i].K * sizeof(float)) / sizeof(float);
+    }
+  }
+  if (xn_need) {
+    const int rc0 = grow_buffer(c, reinterpret_cast<void**>(&c->lin_split), &c->lin_split_cap, xn_need, sizeof(float),
+                                "normalised x");
+    if (rc0) return rc0;
+  }
+  int rc = norm_stats(c, g, lp.data());
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) {
+    if (xn[i] < 0) continue;
+    float* dst = c->lin_split + xn[i];
+    cudaError_t e;
+    {
+      ProfScope ps(c, "norm_apply", 0.0, 8.0 * (double)lp[i].M * lp[i].K);
+      e = supra::launch_norm_apply(lp[i], dst, c->stream);
+    }
+    if (e != cudaSuccess) return cuda_err(c, e, "norm_apply");
+    c->launches += 1;
+    lp[i].x = dst;
+    lp[i].ldx = lp[i].K;
+    lp[i].gn_stats = nullptr;  // the product reads x as it is
+  }
+  return run_linear_fp32(c, lp, g[0]->bias, g[0]->aligned, flops, bytes, g[0]->bias ? "linear_fp32_bias" : "linear_fp32");
 }
 
 // Tensor-core linear group (variants TF32 / TF32X3, cfg 1 / 2): the norm statistics, then the

@@ -278,15 +278,22 @@ def vae_inputs(n_img, seed):
 @pytest.mark.parametrize("n_img,checked", [(2, (0, 1)), (8, tuple(range(8))), (64, (0, 9, 27, 45, 63))])
 def test_vae_full_size(gpu, n_img, checked):
     """Config 4 at batch 2, 8 (every image checked) and 64 (a sample of images checked), one call
-    per image (app/models/vae.js:86) grouped into one flush, FP32 FFMA score path."""
+    per image (app/models/vae.js:86) grouped into one flush, FP32 FFMA score path: from 8 images
+    on (enough 128 x 128 score tiles for two CTAs per SM) S = Q K^T runs on the FFMA linear."""
     q, k, v = vae_inputs(n_img, 4)
     qd, kd, vd = dev(q), dev(k), dev(v)
     out = dev(np.zeros(n_img * 1024 * 512))
+    gpu.profile(True)
+    gpu.profile_reset()
     for i in range(n_img):
         o = i * 1024 * 512
         attn(gpu, q=qd, k=kd, v=vd, Lq=1024, Lk=1024, H=1, D=512, ldq=512, ldk=512, ldv=512, qOff=o, kOff=o, vOff=o,
              oOff=o, out=out)
     gpu.sync()
+    names = {r["name"] for r in gpu.profile_report()}
+    gpu.profile(False)
+    assert names == ({"attn_gemm_qk_lin", "attn_softmax_rows", "attn_gemm_pv"} if n_img >= 8
+                     else {"attn_gemm_qk", "attn_softmax_rows", "attn_gemm_pv"}), names
     got = host(out).reshape(n_img, 1024, 512)
     for i in checked:
         assert_close(got[i], oracle.attention_heads(q[i], k[i], v[i], 1))
