@@ -119,11 +119,16 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
   }
   // FFMA path: with enough 128 x 128 score tiles to fill two CTAs per SM, S = Q K^T runs on the
   // FFMA linear (TMA-staged, packed FMAs; the VAE at 8 or more images) rather than the score kernel
-  bool lin_qk = false;
+  // and O = P V too (W = V read as [Lk, D]) when its 128 x 64 tiles fill them
+  bool lin_qk = false, lin_pv = false;
   if (!tc && !bias && aligned) {
-    int64_t t = 0;
-    for (const GemmUnit& u : units) t += (int64_t)((u.rows + 127) / 128) * ((g[u.prob]->p.Lk + 127) / 128);
+    int64_t t = 0, tv = 0;
+    for (const GemmUnit& u : units) {
+      t += (int64_t)((u.rows + 127) / 128) * ((g[u.prob]->p.Lk + 127) / 128);
+      tv += (int64_t)((u.rows + 127) / 128) * ((g[u.prob]->p.D + 63) / 64);
+    }
     lin_qk = t >= supra::attn_fp32_warp_cta_slots();
+    lin_pv = tv >= supra::attn_fp32_warp_cta_slots();
   }
   std::vector<int32_t> qk(nu + 1), pv(nu + 1), rw(nu + 1);
   int64_t tq = 0, tp = 0, tr = 0;
@@ -268,6 +273,26 @@ int run_gemm_chunk(supra_attn_ctx* c, const std::vector<const Queued*>& g, std::
       jobs[i] = TcJob{lp, 1.f, true, c->scratch + u.s_off, L.lo ? L.lo + u.s_off : nullptr, u.ldS};
     }
     rc = run_linear_tc(c, jobs, tc == 2, fl, by_pv);
+    if (rc) return rc;
+  } else if (lin_pv) {
+    // O_h rows = P V_h on the FFMA linear with W = V_h as [Lk, D] (read in place)
+    std::vector<supra::LinProb> lps((size_t)nu);
+    for (int i = 0; i < nu; ++i) {
+      const GemmUnit& u = units[i];
+      const AttnProb& P = g[u.prob]->p;
+      supra::LinProb& lp = lps[i];
+      std::memset(&lp, 0, sizeof lp);
+      lp.x = c->scratch + u.s_off;
+      lp.ldx = u.ldS;
+      lp.w = P.v + P.v_off + (int64_t)u.h * P.D;
+      lp.ldw = P.ldv;
+      lp.y = P.o + P.o_off + (int64_t)u.row0 * P.ldo + (int64_t)u.h * P.D;
+      lp.ldy = P.ldo;
+      lp.M = u.rows;
+      lp.N = P.D;
+      lp.K = P.Lk;
+    }
+    rc = run_linear_fp32(c, lps, false, true, fl, by_pv, "attn_gemm_pv_lin", true);
     if (rc) return rc;
   } else {
     {

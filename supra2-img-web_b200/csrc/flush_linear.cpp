@@ -55,7 +55,7 @@ static int linear_tile_cols(const std::vector<supra::LinProb>& lp) {
 // kLinBoxCols x (tile columns) boxes per problem, cached per context like the attention kernels'
 // maps; a shape the driver's encoder refuses, or a misaligned group, takes the per-thread copy form.
 int run_linear_fp32(supra_attn_ctx* c, std::vector<supra::LinProb>& lp, bool bias, bool aligned, double flops,
-                    double bytes, const char* name) {
+                    double bytes, const char* name, bool w_kn) {
   const int n = (int)lp.size();
   const int cols = linear_tile_cols(lp);
   std::vector<int32_t> begin(n + 1);
@@ -75,14 +75,18 @@ int run_linear_fp32(supra_attn_ctx* c, std::vector<supra::LinProb>& lp, bool bia
     int rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.x), q.ldx, q.M, q.K, supra::kLinBoxCols, 128, 0, 0},
                        maps, &lp[i].mx);
     if (!rc0)
-      rc0 = map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, supra::kLinBoxCols, cols, 0, 0},
-                     maps, &lp[i].mw);
+      rc0 = w_kn ? map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.K, q.N, cols, 32, 0, 0}, maps, &lp[i].mw)
+                 : map_slot(c, MapKey{reinterpret_cast<uintptr_t>(q.w), q.ldw, q.N, q.K, supra::kLinBoxCols, cols, 0, 0},
+                            maps, &lp[i].mw);
     if (rc0) {
       tma = false;
       maps.clear();
       c->err.clear();
     }
+    lp[i].w_kn = w_kn ? 1 : 0;
   }
+  // W as [K, N] has only the TMA-staged form (callers pass aligned operands)
+  if (w_kn && !tma) return set_err(c, SUPRA_ATTN_EINVAL, "%s: W as [K, N] needs 16-byte aligned operands", name);
   const size_t mbytes = sizeof(CUtensorMap) * maps.size();
   const size_t pbytes = align16(sizeof(supra::LinProb) * n);
   const size_t bbytes = sizeof(int32_t) * (n + 1);
@@ -108,7 +112,7 @@ int run_linear_fp32(supra_attn_ctx* c, std::vector<supra::LinProb>& lp, bool bia
   cudaError_t e;
   {
     ProfScope ps(c, name, flops, bytes);
-    e = tma ? supra::launch_linear_fp32_tma(bias, cols, L, c->stream)
+    e = tma ? supra::launch_linear_fp32_tma(bias, cols, w_kn, L, c->stream)
             : supra::launch_linear_fp32(bias, false, cols, L, c->stream);
   }
   if (e != cudaSuccess) return cuda_err(c, e, name);

@@ -203,9 +203,12 @@ struct alignas(16) LinProb {
   int32_t gn_rows;   // rows per image
   int32_t gn_groups;
   int32_t gn_silu;
-  int32_t mx, mw;    // the TMA-staged FFMA kernel: tensor maps of x ([M, K], boxes 20 x 128) and W
-                     // ([N, K], boxes 20 x tile columns) in LinLaunch::maps; unused elsewhere
-  int32_t pad_[2];
+  int32_t mx, mw;    // the TMA-staged FFMA kernel: tensor maps of x ([M, K], boxes kLinBoxCols x 128)
+                     // and W ([N, K], boxes kLinBoxCols x tile columns; with w_kn, [K, N] in boxes
+                     // of tile columns x 32) in LinLaunch::maps; unused elsewhere
+  int32_t w_kn;      // the TMA-staged FFMA kernel: W is stored [K, N] (row stride ldw along N), as
+                     // V is for O = P V; every problem of a launch alike
+  int32_t pad_;
 };
 static_assert(sizeof(LinProb) % 16 == 0, "LinProb is packed into the descriptor ring");
 
@@ -222,7 +225,7 @@ struct LinLaunch {
 cudaError_t launch_linear_fp32(bool bias, bool aligned, int tile_cols, const LinLaunch& L, cudaStream_t s);
 // The same with the x and W tiles staged by TMA tensor copies (x and W 16-byte aligned, row strides
 // of a multiple of 4 floats; LinProb::mx / mw index L.maps).
-cudaError_t launch_linear_fp32_tma(bool bias, int tile_cols, const LinLaunch& L, cudaStream_t s);
+cudaError_t launch_linear_fp32_tma(bool bias, int tile_cols, bool w_kn, const LinLaunch& L, cudaStream_t s);
 // GroupNorm statistics of x [images * rows_per_image, K] (contiguous rows): for every image and
 // group of K / groups channels, (mean, 1 / sqrt(var + eps)) with the variance taken around the
 // mean in a second pass (app/gpu/kernels.js:117-139).

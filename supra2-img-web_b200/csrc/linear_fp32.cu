@@ -45,8 +45,13 @@ constexpr int kST = kLinBoxCols;       // row stride of the stage buffers
 // x^T of the stage being computed: [kBKT][kTS], row r of x at position 8 (r % 16) + r / 16, so a
 // thread's 8 rows (rg + 16i) are two float4 at 8rg
 constexpr int kTS = kBM + 4;
-template <int BN>
-constexpr int tma_smem_bytes() { return 128 + (kTmaStages * (kBM + BN) * kST + kBKT * kTS) * 4 + kTmaStages * 8; }
+// a stage's W tile: [BN][kST] (W as [N, K]) or [kBKT][BN] (W as [K, N], w_kn)
+template <int BN, bool WKN>
+constexpr int w_stage_floats() { return WKN ? kBKT * BN : BN * kST; }
+template <int BN, bool WKN>
+constexpr int tma_smem_bytes() {
+  return 128 + (kTmaStages * (kBM * kST + w_stage_floats<BN, WKN>()) + kBKT * kTS) * 4 + kTmaStages * 8;
+}
 
 // GroupNorm (+ SiLU) or LayerNorm (+ modulation) of a staged x tile `a` (stage st of the tile at
 // rows r0.., nr of them valid), per element of a valid row and column (padding stays zero):
@@ -129,22 +134,28 @@ __device__ __forceinline__ void transpose_stage(const float* __restrict__ a, flo
 // acc += the stage's x^T (rows rg + 16i in pairs: acc[p][j] holds rows rg + 32p (x) and
 // rg + 32p + 16 (y)) times its W tile (rows cg + 16j), kBK deep, with packed f32x2 FMAs: one W
 // value (broadcast) times the x values of two rows
-template <int NJ>
+template <int NJ, bool WKN>
 __device__ __forceinline__ void mma_stage_t(const float* at, const float* b, int rg, int cg, float2 (&acc)[4][NJ]) {
   const float4* A4 = reinterpret_cast<const float4*>(at) + 2 * rg;
-  const float4* B4 = reinterpret_cast<const float4*>(b) + cg * (kST / 4);
+  const float4* B4 = reinterpret_cast<const float4*>(b) + (WKN ? cg : cg * (kST / 4));
 #pragma unroll
   for (int k4 = 0; k4 < kBKT / 4; ++k4) {
+    // W as [N, K]: column cg + 16j's 4 values of k (one float4 each); as [K, N] (w_kn): row k's
+    // columns 4cg .. 4cg + 3 and 64 + 4cg .. + 3 (one or two float4 per k)
     float4 bf[NJ];
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) bf[j] = B4[j * 16 * (kST / 4) + k4];
+    for (int j = 0; j < NJ; ++j)
+      bf[j] = WKN ? B4[(4 * k4 + (j & 3)) * (NJ * 4) + 16 * (j >> 2)] : B4[j * 16 * (kST / 4) + k4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float4 q0 = A4[(4 * k4 + e) * (kTS / 4)];
       const float4 q1 = A4[(4 * k4 + e) * (kTS / 4) + 1];
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
-        const float w = e == 0 ? bf[j].x : e == 1 ? bf[j].y : e == 2 ? bf[j].z : bf[j].w;
+        // W as [K, N]: bf[(j & 4) | e] holds row k = 4 k4 + e; column j is its component j & 3
+        const float4 bw = WKN ? bf[(j & 4) | e] : bf[j];
+        const int comp = WKN ? (j & 3) : e;
+        const float w = comp == 0 ? bw.x : comp == 1 ? bw.y : comp == 2 ? bw.z : bw.w;
         const float2 w2 = make_float2(w, w);
         acc[0][j] = __ffma2_rn(make_float2(q0.x, q0.y), w2, acc[0][j]);
         acc[1][j] = __ffma2_rn(make_float2(q0.z, q0.w), w2, acc[1][j]);
@@ -156,14 +167,22 @@ __device__ __forceinline__ void mma_stage_t(const float* at, const float* b, int
 }
 
 // y rows r0 + rg + 16i, columns c0 + cg + 16j: each store instruction writes two 64-byte row runs
-template <bool BIAS, int NJ>
+// the tile column of a thread's column j: cg + 16j, or (WKN, the form that reads W as [K, N])
+// 4cg + j for j < 4 and 64 + 4cg + j - 4 above
+template <bool WKN>
+__device__ __forceinline__ int col_of(int cg, int j) {
+  return WKN ? 4 * cg + (j & 3) + 64 * (j >> 2) : cg + 16 * j;
+}
+
+template <bool BIAS, int NJ, bool WKN = false>
 __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&acc)[8][NJ], int r0, int c0, int nr,
                                                 int nc, int rg, int cg) {
   float bias[NJ], gate[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    bias[j] = (BIAS && cg + 16 * j < nc) ? __ldg(P.bias + c0 + cg + 16 * j) : 0.f;
-    gate[j] = (P.gate && cg + 16 * j < nc) ? __ldg(P.gate + c0 + cg + 16 * j) : 1.f;
+    const int c = col_of<WKN>(cg, j);
+    bias[j] = (BIAS && c < nc) ? __ldg(P.bias + c0 + c) : 0.f;
+    gate[j] = (P.gate && c < nc) ? __ldg(P.gate + c0 + c) : 1.f;
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -174,7 +193,7 @@ __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&
     const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
-      const int c = cg + 16 * j;
+      const int c = col_of<WKN>(cg, j);
       if (c < nc) {
         float v = acc[i][j] + bias[j];
         if (P.act != kActNone) v = linear_act(P.act, v);
@@ -202,14 +221,15 @@ __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&
 // attention kernel's Q^T K does. Two barriers per stage: after the wait for the stage's copies
 // (every thread is also done with the previous stage, whose buffers thread 0 then refills) and
 // after the transposition.
-template <bool BIAS, int BN>
+template <bool BIAS, int BN, bool WKN>
 __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_constant__ LinLaunch L) {
   constexpr int NJ = BN / 16;
+  constexpr int WS = w_stage_floats<BN, WKN>();
   extern __shared__ uint8_t lin_raw[];
   const uint32_t raw = smem_u32(lin_raw);
   float* const As = reinterpret_cast<float*>(lin_raw + (((raw + 127u) & ~127u) - raw));  // [kTmaStages][kBM * kST]
-  float* const Bs = As + kTmaStages * kBM * kST;                                                 // [kTmaStages][BN * kST]
-  float* const At = Bs + kTmaStages * BN * kST;                                                  // [kBKT][kTS]
+  float* const Bs = As + kTmaStages * kBM * kST;                                                 // [kTmaStages][WS]
+  float* const At = Bs + kTmaStages * WS;                                                        // [kBKT][kTS]
   uint64_t* const full = reinterpret_cast<uint64_t*>(At + kBKT * kTS);                           // [kTmaStages]
   const int t = blockIdx.x;
   if (t >= L.total) {
@@ -238,9 +258,10 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   auto issue = [&](int st) {  // (thread 0)
     if (st < nstage) {
       const int buf = st % kTmaStages;
-      mbar_arrive_expect_tx(&full[buf], (uint32_t)((kBM + BN) * kST * 4));
+      mbar_arrive_expect_tx(&full[buf], (uint32_t)((kBM * kST + WS) * 4));
       tc::tma_load_2d(As + buf * kBM * kST, mx, st * kBKT, r0, &full[buf]);
-      tc::tma_load_2d(Bs + buf * BN * kST, mw, st * kBKT, c0, &full[buf]);
+      if (WKN) tc::tma_load_2d(Bs + buf * WS, mw, c0, st * kBKT, &full[buf]);  // [32 k][BN] of W as [K, N]
+      else tc::tma_load_2d(Bs + buf * WS, mw, st * kBKT, c0, &full[buf]);
     }
   };
   if (tid == 0) {
@@ -269,7 +290,7 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
     }
     transpose_stage(a, At, tid);
     __syncthreads();  // x^T complete
-    mma_stage_t<NJ>(At, Bs + buf * BN * kST, rg, cg, acc);
+    mma_stage_t<NJ, WKN>(At, Bs + buf * WS, rg, cg, acc);
     fence_proxy_async_smem();  // this thread's reads (and norm writes) of the buffers before they are refilled
   }
   float accf[8][NJ];
@@ -277,7 +298,7 @@ __global__ void __launch_bounds__(kT, 2) linear_fp32_tma_kernel(const __grid_con
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < NJ; ++j) accf[i][j] = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
-  linear_epilogue<BIAS, NJ>(P, accf, r0, c0, nr, nc, rg, cg);
+  linear_epilogue<BIAS, NJ, WKN>(P, accf, r0, c0, nr, nc, rg, cg);
 }
 
 // The same product with the tiles staged by per-thread cp.async (any alignment: 4-byte copies
@@ -524,19 +545,22 @@ cudaError_t launch_linear_fp32(bool bias, bool aligned, int tile_cols, const Lin
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-cudaError_t launch_linear_fp32_tma(bool bias, int tile_cols, const LinLaunch& L, cudaStream_t s) {
+cudaError_t launch_linear_fp32_tma(bool bias, int tile_cols, bool w_kn, const LinLaunch& L, cudaStream_t s) {
   if (L.total <= 0) return cudaSuccess;
   cudaError_t e = cudaSuccess;
   auto go = [&](auto kern, int bytes) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e == cudaSuccess) kern<<<L.total, kT, bytes, s>>>(L);
   };
-  if (tile_cols == 64) {
-    if (bias) go(linear_fp32_tma_kernel<true, 64>, tma_smem_bytes<64>());
-    else go(linear_fp32_tma_kernel<false, 64>, tma_smem_bytes<64>());
+  if (w_kn) {  // (the score path's O = P V: no bias)
+    if (tile_cols == 64) go(linear_fp32_tma_kernel<false, 64, true>, tma_smem_bytes<64, true>());
+    else go(linear_fp32_tma_kernel<false, 128, true>, tma_smem_bytes<128, true>());
+  } else if (tile_cols == 64) {
+    if (bias) go(linear_fp32_tma_kernel<true, 64, false>, tma_smem_bytes<64, false>());
+    else go(linear_fp32_tma_kernel<false, 64, false>, tma_smem_bytes<64, false>());
   } else {
-    if (bias) go(linear_fp32_tma_kernel<true, 128>, tma_smem_bytes<128>());
-    else go(linear_fp32_tma_kernel<false, 128>, tma_smem_bytes<128>());
+    if (bias) go(linear_fp32_tma_kernel<true, 128, false>, tma_smem_bytes<128, false>());
+    else go(linear_fp32_tma_kernel<false, 128, false>, tma_smem_bytes<128, false>());
   }
   return e != cudaSuccess ? e : cudaGetLastError();
 }

@@ -305,7 +305,7 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g);
 int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32);
 int flush_linear(supra_attn_ctx* c, std::vector<const Queued*>& g);
 int run_linear_fp32(supra_attn_ctx* c, std::vector<supra::LinProb>& lp, bool bias, bool aligned, double flops,
-                    double bytes, const char* name);
+                    double bytes, const char* name, bool w_kn = false);
 int flush_linear_tc(supra_attn_ctx* c, std::vector<const Queued*>& g);
 int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, double flops, double bytes);
 

@@ -279,7 +279,8 @@ def vae_inputs(n_img, seed):
 def test_vae_full_size(gpu, n_img, checked):
     """Config 4 at batch 2, 8 (every image checked) and 64 (a sample of images checked), one call
     per image (app/models/vae.js:86) grouped into one flush, FP32 FFMA score path: from 8 images
-    on (enough 128 x 128 score tiles for two CTAs per SM) S = Q K^T runs on the FFMA linear."""
+    on (enough tiles for two CTAs per SM) S = Q K^T and O = P V run on the FFMA linear, the
+    latter reading V as W [Lk, D]."""
     q, k, v = vae_inputs(n_img, 4)
     qd, kd, vd = dev(q), dev(k), dev(v)
     out = dev(np.zeros(n_img * 1024 * 512))
@@ -292,7 +293,7 @@ def test_vae_full_size(gpu, n_img, checked):
     gpu.sync()
     names = {r["name"] for r in gpu.profile_report()}
     gpu.profile(False)
-    assert names == ({"attn_gemm_qk_lin", "attn_softmax_rows", "attn_gemm_pv"} if n_img >= 8
+    assert names == ({"attn_gemm_qk_lin", "attn_softmax_rows", "attn_gemm_pv_lin"} if n_img >= 8
                      else {"attn_gemm_qk", "attn_softmax_rows", "attn_gemm_pv"}), names
     got = host(out).reshape(n_img, 1024, 512)
     for i in checked:
