@@ -300,6 +300,37 @@ def test_vae_full_size(gpu, n_img, checked):
         assert_close(got[i], oracle.attention_heads(q[i], k[i], v[i], 1))
 
 
+def test_score_path_on_linear_ragged(gpu):
+    """The score path's products on the FFMA linear (S = Q K^T, and O = P V reading V as W [Lk, D])
+    at sizes that are not multiples of any tile: 9 problems of 2 heads, Lq = 700, Lk = 900, D = 192,
+    each in its own buffers with padded row strides; every problem against the oracle."""
+    import supra_attn
+
+    rng = np.random.default_rng(41)
+    H, D, Lq, Lk = 2, 192, 700, 900
+    ld = H * D + 8
+    gpu.profile(True)
+    gpu.profile_reset()
+    cases = []
+    for _ in range(9):
+        q = rng.standard_normal(Lq * ld).astype(np.float32)
+        k = rng.standard_normal(Lk * ld).astype(np.float32)
+        v = rng.standard_normal(Lk * ld).astype(np.float32)
+        qd, kd, vd = dev(q), dev(k), dev(v)  # (kept alive until the flush)
+        o = supra_attn.attention(gpu, q=qd, k=kd, v=vd, Lq=Lq, Lk=Lk, H=H, D=D, ldq=ld, ldk=ld, ldv=ld)
+        cases.append((q, k, v, o, (qd, kd, vd)))
+    gpu.sync()
+    names = {r["name"] for r in gpu.profile_report()}
+    gpu.profile(False)
+    assert {"attn_gemm_qk_lin", "attn_gemm_pv_lin"} <= names, names
+    for q, k, v, o, _ in cases:
+        got = gpu.read(o).reshape(Lq, H * D)
+        ref = oracle.attention_heads(q.reshape(Lq, ld)[:, : H * D], k.reshape(Lk, ld)[:, : H * D],
+                                     v.reshape(Lk, ld)[:, : H * D], H)
+        assert_close(got, ref)
+        o.release()
+
+
 # ---- edge cases ---------------------------------------------------------------------------------
 def rand_problem(rng, Lq, Lk, H, D, ldq=None, ldk=None, ldv=None, qOff=0, kOff=0, vOff=0, oOff=0, bias=False):
     ldq = ldq or H * D
