@@ -189,8 +189,16 @@ __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&
     const int r = rg + 16 * i;
     if (r >= nr) continue;
     float* yrow = P.y + (int64_t)(r0 + r) * P.ldy + c0;
-    // resid may be y itself (in place): each element is read and then written by this thread only
+    // resid may be y itself (in place): each element is read and then written by this thread only.
+    // The row's residuals are all loaded before any of its stores (with y and resid possibly the
+    // same array, a load after a store would wait for it: one memory round trip per element).
     const float* rrow = P.resid ? P.resid + (int64_t)(r0 + r) * P.ldr + c0 : nullptr;
+    float rv[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int c = col_of<WKN>(cg, j);
+      rv[j] = (rrow && c < nc) ? rrow[c] : 0.f;
+    }
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
       const int c = col_of<WKN>(cg, j);
@@ -198,7 +206,7 @@ __device__ __forceinline__ void linear_epilogue(const LinProb& P, const float (&
         float v = acc[i][j] + bias[j];
         if (P.act != kActNone) v = linear_act(P.act, v);
         if (P.gate) v *= gate[j];
-        yrow[c] = rrow ? rrow[c] + v : v;
+        yrow[c] = rv[j] + v;
       }
     }
   }
