@@ -24,9 +24,14 @@
 //    as one [32 x 68] box, a K/V block as two [32 x 68] K and two [32 x 64] V boxes (the second
 //    pair only if the block has keys past 32). Two stages (211 KB of shared memory with the P
 //    rows); the last of the 8 warps to finish a stage issues the block two ahead into it.
-//  * Ragged last blocks: keys past Lk take -inf scores (a select), blocks of at most 32 keys run
-//    the Q K^T of the first 32 keys only, and P V skips the 4-key groups past Lk (V rows past Lk
-//    are never read).
+//  * Softmax on the row pairs (f32x2 FMA for the exp2 arguments, f32x2 adds for the sums); P goes
+//    to shared memory transposed (P^T [key][position], two float4 stores per key), and the
+//    probabilities of keys 32..63 are formed inside the P V of keys 0..31, so that their exp2 (on
+//    the SFU) overlap the products (on the FMA pipe).
+//  * Ragged last blocks: keys past Lk take -inf scores (a select), Q^T K runs over the 16-key
+//    groups that hold a key below Lk, and P V skips the 4-key groups past Lk (V rows past Lk are
+//    never read).
+//  * Whole 32-row output blocks are staged in the warp's P^T buffer and leave by TMA store.
 //  * All waits are bounded (2 s); a timeout sets the device status word and the warp leaves.
 #include "common.cuh"
 #include "tcgen05.cuh"
