@@ -168,3 +168,29 @@ def test_wide_selection(gpu, n, Lq, expect):
     qn, kvn = q.numpy().reshape(n, Lq, 576), kv.numpy().reshape(n, 77, 1152)
     for b in (0, n // 2, n - 1):
         assert_close(got[b], oracle.attention_heads(qn[b], kvn[b, :, :576], kvn[b, :, 576:], 9))
+
+
+@pytest.mark.parametrize("Lq,Lk", [(512, 300), (1000, 77)])
+def test_wide_several_query_tiles(gpu, Lq, Lk):
+    """Problems of several 256-row tiles (the last one partial at Lq = 1000), each tile claimed on
+    its own; sampled problems against the oracle, and nothing written past Lq."""
+    torch = _torch()
+    import supra_attn
+
+    n, H, C = 20, 9, 576
+    g = torch.Generator().manual_seed(35)
+    q = torch.randn(n * (Lq + 8) * C, generator=g)
+    kv = torch.randn(n * Lk * 2 * C, generator=g)
+    qd, kvd = q.cuda(), kv.cuda()
+    out = torch.full((n * (Lq + 8) * C,), 7.0, device="cuda")
+    descs = (supra_attn.Desc * n)()
+    for b in range(n):
+        descs[b] = supra_attn.make_desc(q=qd, k=kvd, v=kvd, out=out, Lq=Lq, Lk=Lk, H=H, D=64, ldq=C, ldk=2 * C,
+                                        ldv=2 * C, qOff=b * (Lq + 8) * C, kOff=b * Lk * 2 * C,
+                                        vOff=b * Lk * 2 * C + C, oOff=b * (Lq + 8) * C)
+    assert _run(gpu, descs) == ["attn_fp32_d64_wide"]
+    got = out.cpu().numpy().reshape(n, Lq + 8, C)
+    qn, kvn = q.numpy().reshape(n, Lq + 8, C), kv.numpy().reshape(n, Lk, 2 * C)
+    for b in (0, 7, n - 1):
+        assert_close(got[b, :Lq], oracle.attention_heads(qn[b, :Lq], kvn[b, :, :C], kvn[b, :, C:], H))
+    assert np.all(got[:, Lq:] == 7.0)
