@@ -509,16 +509,26 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
     float v[64];
     float o[SPLIT ? 64 : 1];  // split kernel: this thread's row of O
     int kt = 0;               // this CTA's tile count
-    for (; ok; ++kt) {
-      int t = 0;
-      ok = __all_sync(0xffffffffu, tile_at(tab, kt, &t, abort, L.status));
-      if (!ok || t >= L.total) break;
-      const Tile T = tile_of(L, t);
+    // The CTA's first tile; each later one is looked up during the previous tile's last block
+    // (its descriptor's loads then overlap that tile's epilogue).
+    int t = 0;
+    ok = __all_sync(0xffffffffu, tile_at(tab, 0, &t, abort, L.status));
+    Tile Tn = ok && t < L.total ? tile_of(L, t) : Tile{};
+    int Lkn = 0, Lqn = 0;
+    float sl2n = 0.f;
+    if (ok && t < L.total) {
+      Lkn = Tn.p->Lk;
+      Lqn = Tn.p->Lq;
+      sl2n = Tn.p->scale_log2;
+    }
+    for (; ok && t < L.total; ++kt) {
+      const Tile T = Tn;
       const TmaProb* pp = T.p;
-      int Lk = pp->Lk, Lq = pp->Lq;
-      float sl2 = pp->scale_log2;
+      int Lk = Lkn, Lq = Lqn;
+      float sl2 = sl2n;
       // opaque: kept in registers rather than re-loaded from the descriptor at each block
       asm volatile("" : "+r"(Lk), "+r"(Lq), "+f"(sl2));
+      int tnext = L.total;
       float m = -INFINITY, l = 0.f;
       if constexpr (SPLIT) {
 #pragma unroll
@@ -652,6 +662,13 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           if (j == T.nblk - 1) {  // the CTA's next tile, once the producer has claimed it
             ok = __all_sync(0xffffffffu, tile_at(tab, kt + 1, &tn, abort, L.status));
             if (!ok) break;
+            tnext = tn;
+            if (tn < L.total) {
+              Tn = tile_of(L, tn);
+              Lkn = Tn.p->Lk;
+              Lqn = Tn.p->Lq;
+              sl2n = Tn.p->scale_log2;
+            }
           }
           if (j == T.nblk - 1 && tn < L.total) {
             // the next tile's Q, into the other buffer, before this tile's epilogue: the tensor
@@ -704,7 +721,12 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           int tn = L.total;
           ok = __all_sync(0xffffffffu, tile_at(tab, kt + 1, &tn, abort, L.status));
           if (!ok) break;
+          tnext = tn;
           if (tn < L.total) {
+            Tn = tile_of(L, tn);
+            Lkn = Tn.p->Lk;
+            Lqn = Tn.p->Lq;
+            sl2n = Tn.p->scale_log2;
             ok = __all_sync(0xffffffffu, wait_or_abort(&B->q_full, (uint32_t)((kt + 1) & 1), abort, L.status, W_CONV_Q, n));
             if (!ok) break;
             copy_q_row(Qs, row, tl + COL_QP);
@@ -769,6 +791,7 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
           __syncwarp();
         }
       }
+      t = tnext;
     }
     if (!ok && lane == 0) report_error(L.status, DEV_TIMEOUT, 22, n);
   } else if (SPLIT) {
