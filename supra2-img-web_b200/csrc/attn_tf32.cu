@@ -759,37 +759,32 @@ __global__ void __launch_bounds__(Lay<SPLIT>::THREADS, Lay<SPLIT>::CTAS_PER_SM)
         mbar_arrive(&B->o_empty);  // the next tile's first PV may overwrite O
       }
       // O / l, stored coalesced: each thread holds its own row, so the warp's 32 x 64 block goes
-      // through a 16 x 32 shared-memory slot (16-byte chunks swizzled by row) in four rounds and
-      // every store instruction writes four whole 128-byte row segments.
+      // through a 32 x 16 shared-memory slot in four rounds of 16 columns: every lane writes its
+      // row's 4 chunks of 16 bytes (chunk c at position (c + r / 2) % 4 of row r: the 8 lanes of a
+      // quarter-warp on distinct bank groups), then each store instruction writes eight 64-byte
+      // row segments.
       const float inv = 1.0f / l;
       const int64_t ldo = pp->ldo;
       float* orow0 = pp->o + pp->o_off + (int64_t)(T.q0 + 32 * q4) * ldo + (int64_t)T.h * kD;
       const int vrows = Lq - (T.q0 + 32 * q4);  // rows of this warp's 32 that exist
       float* stg = Os + q4 * (kOStage / 4);
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
+      for (int hc = 0; hc < 4; ++hc) {
 #pragma unroll
-        for (int hc = 0; hc < 2; ++hc) {
-          if ((lane >> 4) == hr) {
-            const int r = lane & 15;
-#pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const int c = 32 * hc + 4 * c4;
-              *reinterpret_cast<float4*>(stg + r * 32 + ((c4 ^ (r & 7)) << 2)) =
-                  make_float4(v[c] * inv, v[c + 1] * inv, v[c + 2] * inv, v[c + 3] * inv);
-            }
-          }
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int r = 4 * i + (lane >> 3);
-            const int c4 = lane & 7;
-            const float4 val = *reinterpret_cast<const float4*>(stg + r * 32 + ((c4 ^ (r & 7)) << 2));
-            if (16 * hr + r < vrows)
-              *reinterpret_cast<float4*>(orow0 + (int64_t)(16 * hr + r) * ldo + 32 * hc + 4 * c4) = val;
-          }
-          __syncwarp();
+        for (int c = 0; c < 4; ++c) {
+          const int col = 16 * hc + 4 * c;
+          *reinterpret_cast<float4*>(stg + lane * 16 + 4 * ((c + (lane >> 1)) & 3)) =
+              make_float4(v[col] * inv, v[col + 1] * inv, v[col + 2] * inv, v[col + 3] * inv);
         }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = 8 * i + (lane >> 2);
+          const int c = lane & 3;
+          const float4 val = *reinterpret_cast<const float4*>(stg + r * 16 + 4 * ((c + (r >> 1)) & 3));
+          if (r < vrows) *reinterpret_cast<float4*>(orow0 + (int64_t)r * ldo + 16 * hc + 4 * c) = val;
+        }
+        __syncwarp();
       }
       t = tnext;
     }
