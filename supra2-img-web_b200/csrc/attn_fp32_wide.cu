@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
 
   const int t0 = blockIdx.x;
   if (t0 >= L.total) {  // the host sizes the grid to at most one CTA per tile
-    if (tid == 0) report_error(L.status, DEV_BAD_TILE, 30);
+    if (tid == 0) report_error(L.status, DEV_BAD_TILE, 60);
     return;
   }
   if (tid == 0) {
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
       for (int u = 0; u < 4; ++u) o[i][u] = make_float2(0.f, 0.f);
     if (!mbar_wait_bounded(&C->qbar[w], k & 1u)) {
       if (lane == 0) {
-        report_error(L.status, DEV_TIMEOUT, 31, (int32_t)k);
+        report_error(L.status, DEV_TIMEOUT, 61, (int32_t)k);
         tc::bulk_wait_group_all();
       }
       return;
@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(kW * 32, 1) attn_fp32_wide_kernel(const __grid
       const int nk = min(kNK, Lk - j * kNK);
       if (!mbar_wait_bounded(&C->full[s], par)) {
         if (lane == 0) {
-          report_error(L.status, DEV_TIMEOUT, 32, (int32_t)g);
+          report_error(L.status, DEV_TIMEOUT, 62, (int32_t)g);
           tc::bulk_wait_group_all();
         }
         return;
