@@ -187,6 +187,9 @@ SUPRA_ATTN_API int supra_attn_position_bias(supra_attn_ctx* ctx, const float* ta
  *     (mean, 1/sqrt(var + eps)) per row in an extra launch, and the product uses
  *     (x - mean) * rstd, times (1 + mod[scale_off + k]) plus mod[shift_off + k] when ln->mod is
  *     set (adaLN modulation; app/models/dit.js:164,179,189). Needs x_off == 0 and ldx == K.
+ *   With gn or ln on the FFMA kernel, a product whose x is read by two or more column tiles
+ *   first writes the normalised x once into a context-owned buffer (one more launch), which the
+ *   product then reads; products with one column tile normalise each staged x tile.
  *   - act: SUPRA_ATTN_ACT_NONE, _GELU (erf form), _GELU_TANH or _SILU, applied to x W^T + bias
  *     before the gate and the residual (ops.linear's act, app/gpu/gemm.js:9,28-36,130-135).
  * flags must be 0.
