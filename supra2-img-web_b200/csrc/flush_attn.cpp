@@ -347,9 +347,11 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
 // kernel): one tensor map per distinct (buffer, ld, rows, box) in the flush, encoded once per
 // context and cached; problems refer to maps by index.
 int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
-  // Unbiased FP32 launches that fill the device with 256-row tiles, and lose little to the larger
-  // tile (query rows rounded up to 256 at most 1/8 more than rounded up to 128), run on the
-  // 256-row kernel (8x8 register blocks, one CTA per SM); the others on the 128-row kernel.
+  // Unbiased FP32 launches with at least one 256-row tile per SM that lose little to the larger
+  // tile (query rows rounded up to 256 at most 1/8 more than rounded up to 128) run on the
+  // 256-row kernel (8x8 register blocks, one CTA per SM); the others on the 128-row kernel. (Past
+  // one tile per SM both kernels quantise alike: n 256-row tiles on 148 CTAs against 2n 128-row
+  // tiles on 296.)
   bool wide = false;
   if (!tf32 && !g[0]->bias) {
     const int64_t wr = supra::attn_fp32_wide_tile_rows(), nr = supra::attn_fp32_warp_tile_rows();
@@ -360,7 +362,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
       rows_w += tw * wr * q->p.H;
       rows_n += (q->p.Lq + nr - 1) / nr * nr * q->p.H;
     }
-    wide = tiles >= 2 * (int64_t)supra::attn_fp32_wide_ctas() && 8 * rows_w <= 9 * rows_n;
+    wide = tiles >= (int64_t)supra::attn_fp32_wide_ctas() && 8 * rows_w <= 9 * rows_n;
   }
   const int mrows = tf32 ? supra::attn_tf32_tile_rows()
                     : wide ? supra::attn_fp32_wide_tile_rows()

@@ -1,6 +1,6 @@
 """The 256-row persistent FP32 kernel (csrc/attn_fp32_wide.cu) against the float64 oracle.
 
-Unbiased D = 64 launches that hold at least two 256-row tiles per SM run on it (the DiT self- and
+Unbiased D = 64 launches that hold at least one 256-row tile per SM run on it (the DiT self- and
 cross-attention batches, app/models/dit.js:172,184); smaller ones on the 128-row kernel. The bar is
 the FP32 one: max_rel and rel_l2 <= 1e-5 per problem.
 """
@@ -144,8 +144,9 @@ def test_wide_mixed_heads_and_scales(gpu):
 
 
 @pytest.mark.parametrize("n,Lq,expect", [
-    (32, 256, "attn_fp32_d64_tma"),   # 288 tiles: under two per SM
-    (33, 256, "attn_fp32_d64_wide"),  # 297 tiles
+    (16, 256, "attn_fp32_d64_tma"),   # 144 tiles: under one per SM
+    (17, 256, "attn_fp32_d64_wide"),  # 153 tiles
+    (32, 256, "attn_fp32_d64_wide"),  # 288 tiles (the DiT block of 32 images)
     (40, 300, "attn_fp32_d64_tma"),   # 300 rows: 512 rows in 256-row tiles against 384 in 128-row ones
     (40, 129, "attn_fp32_d64_wide"),  # 129 rows: 256 either way
 ])
