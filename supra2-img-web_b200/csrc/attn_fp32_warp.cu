@@ -1,5 +1,6 @@
 // Fused FP32 attention, persistent warp-pipelined kernel (sm_100a): D = 64, scale > 0, with or
-// without a score bias (expanded [H, Lq, Lk], or the T5 [buckets, H] table formed in-kernel).
+// without a score bias (expanded [H, Lq, Lk], or the T5 [buckets, H] table, which the host
+// turns into a bias by relative position with one small launch before this one).
 // The DiT self/cross-attention kernel (app/models/dit.js:172,184) and, with the bias, the T5
 // encoder's (app/models/t5.js:80).
 //
@@ -38,6 +39,10 @@
 //    fill: scores of keys past Lk are replaced (not multiplied) by -inf, V rows past Lk are not
 //    read, and rows past Lq are never stored, so no value there can reach a stored output. In a
 //    ragged last block the 4-key groups wholly past Lk are skipped in PV.
+//  * With a bias, each lane copies (cp.async) the 32 bias values of its scores of the next key
+//    block into its own places of the warp's P block as soon as that block's P V is done, so
+//    the loads overlap the next block's wait and Q K^T (they used to sit in front of the
+//    softmax, one L2 round trip per block with one or two warps per scheduler).
 //  * Key splits, for launches with fewer tiles than CTAs (the DiT self-attention of one image
 //    pair, 36 tiles): a tile then covers a range of key blocks of its (head, query tile) group,
 //    writes its unnormalised O rows with their exp2 offset and sum to a partial array, and the last
@@ -371,6 +376,44 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
   Tile T = tile_of<SPLIT>(L, t0);
   if (lane == 0) issue_q(L, qbox_of(T, w), Qw, &C->qbar[w]);
 
+  // Expanded bias ([H, Lq, Lk]): the lane's 32 bias values of a key block are copied (cp.async,
+  // zero fill for rows past Lq and keys past Lk) into the places of the warp's P block that the
+  // lane itself writes, so the loads run behind the block's wait and Q K^T instead of in front
+  // of its softmax. Issued once the previous block's P V is done (the tile's first block: at the
+  // end of the previous tile, or here), waited for by the same lane before the scores take them.
+  auto warp_active = [&](const Tile& X) { return !BIAS || kRowsW * w < X.p->Lq - X.q0; };
+  // The T5 form reads the bias by relative position, [H, 2 rel_max + 1] (formed from the table
+  // before the launch), at clamp(c - r, -rel_max, rel_max).
+  auto issue_bias = [&](const Tile& X, int jx) {
+    const TmaProb* __restrict__ xp = X.p;
+    const int Lqx = xp->Lq, Lkx = xp->Lk;
+    const int r0 = X.q0 + kRowsW * w + rg, c0 = jx * kNK + cg;
+    if (xp->rel_lut == nullptr) {
+      const float* bh = xp->bias + (int64_t)X.h * Lqx * Lkx;
+#pragma unroll
+      for (int i = 0; i < kRI; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int r = r0 + 4 * i, c = c0 + 8 * jj;
+          const bool ok = r < Lqx && c < Lkx;
+          cp_async4(Pw + (rg + 4 * i) * kPS + cg + 8 * jj, ok ? bh + (int64_t)r * Lkx + c : bh, ok ? 4u : 0u);
+        }
+    } else {
+      const int rm = xp->rel_max;
+      const float* bh = xp->bias + (int64_t)X.h * (2 * rm + 1) + rm;
+#pragma unroll
+      for (int i = 0; i < kRI; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int r = r0 + 4 * i, c = c0 + 8 * jj;
+          const bool ok = r < Lqx && c < Lkx;
+          cp_async4(Pw + (rg + 4 * i) * kPS + cg + 8 * jj, bh + (ok ? max(-rm, min(rm, c - r)) : 0), ok ? 4u : 0u);
+        }
+    }
+    cp_async_commit();
+  };
+  if (BIAS && warp_active(T)) issue_bias(T, T.b0);
+
   const float4* Q4 = reinterpret_cast<const float4*>(Qw) + rg * (kQS / 4);
   const float4* P4 = reinterpret_cast<const float4*>(Pw) + rg * (kPS / 4);
   uint32_t g = 0;  // position in the CTA's K/V block sequence
@@ -386,7 +429,7 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
     const int rows_q = min(kRows, pp->Lq - T.q0) - (kRowsW * w + rg);  // rows r with r - (32w + rg) < rows_q
     // With a bias (the T5 encoder: Lq = Lk, often below 128) a warp whose rows all lie past Lq
     // skips the arithmetic; it still waits for its Q rows and releases every K/V stage.
-    const bool active = !BIAS || kRowsW * w < pp->Lq - T.q0;
+    const bool active = warp_active(T);
     float* const orow = pp->o + pp->o_off + ((int64_t)T.q0 + kRowsW * w + rg) * ldo + (int64_t)T.h * kD + 4 * cg;
     // the next tile: known once the wait for this tile's last block has returned (it was claimed
     // and published before that block was issued); its Q rows are requested right after this
@@ -448,34 +491,15 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         if constexpr (BIAS) {
           // scores into the exp2 domain with the bias added, s scale log2 e + b log2 e (the
           // reference adds the bias to the scaled scores, app/gpu/kernels.js:53-62); rows past Lq
-          // and keys past Lk take none. The T5 form looks the bias up in the [buckets, H] table
-          // through the relative-position bucket table.
-          const int Lq = pp->Lq;
-          const int r0 = T.q0 + kRowsW * w + rg, c0 = j * kNK + cg;
-          if (pp->rel_lut) {
-            const float* tab_h = pp->bias + T.h;
-            const int32_t* lut_c = pp->rel_lut + pp->rel_max;
-            const int32_t rel_max = pp->rel_max;
-            const uint32_t Hu = (uint32_t)pp->H;
+          // and keys past Lk take none (zero-filled copies)
+          cp_async_wait<0>();  // this lane's bias values of the block, copied into its P places
   #pragma unroll
-            for (int i = 0; i < kRI; ++i)
+          for (int i = 0; i < kRI; ++i)
   #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                const int r = r0 + 4 * i, c = c0 + 8 * jj;
-                const float b = (r < Lq && c < Lk) ? t5_table_bias(tab_h, lut_c, rel_max, Hu, c - r) : 0.f;
-                sc[i][jj] = fmaf(b, 1.4426950408889634f, sc[i][jj] * sl2);
-              }
-          } else {
-            const float* bh = pp->bias + (int64_t)T.h * Lq * Lk;
-  #pragma unroll
-            for (int i = 0; i < kRI; ++i)
-  #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                const int r = r0 + 4 * i, c = c0 + 8 * jj;
-                const float b = (r < Lq && c < Lk) ? __ldg(bh + (int64_t)r * Lk + c) : 0.f;
-                sc[i][jj] = fmaf(b, 1.4426950408889634f, sc[i][jj] * sl2);
-              }
-          }
+            for (int jj = 0; jj < 4; ++jj) {
+              const float b = Pw[(rg + 4 * i) * kPS + cg + 8 * jj];
+              sc[i][jj] = fmaf(b, 1.4426950408889634f, sc[i][jj] * sl2);
+            }
         }
         // exponent factor: the raw scores times scale log2 e, or the biased scores as they are
         const float f = BIAS ? 1.f : sl2;
@@ -559,6 +583,13 @@ __global__ void __launch_bounds__(kW * 32, 2) attn_fp32_warp_kernel(const __grid
         if (nk & 3) pv_group(nfull, nk & 3);
       }  // active
       __syncwarp();  // every lane is done with P and with stage s
+      if constexpr (BIAS) {  // the next block's bias values into P
+        if (j + 1 < b1) {
+          if (active) issue_bias(T, j + 1);
+        } else if (tn < L.total && warp_active(Tn)) {
+          issue_bias(Tn, Tn.b0);
+        }
+      }
 
       // ---- release stage s; the last warp out loads the block three ahead into it -----------
       if (lane == 0) {

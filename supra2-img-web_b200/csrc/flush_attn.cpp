@@ -480,22 +480,57 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     const int rc0 = ensure_scratch(c, (size_t)group0 * used_splits * mrows * (64 + 2) * sizeof(float));
     if (rc0) return rc0;
   }
+  // The FP32 kernel with a T5 table reads the bias by relative position: per distinct (table,
+  // bucket LUT, H) one [H, 2 rel_max + 1] array, formed on the device (rel_bias_kernel) in the
+  // ring space past the staged bytes, before the launch.
+  struct RelBias {
+    const float* table;
+    int64_t loff;
+    int32_t H, rel_max;
+    size_t off;
+  };
+  std::vector<RelBias> rb;
+  std::vector<int32_t> rb_of((size_t)n, -1);
+  size_t rbytes = 0;
+  if (!tf32) {
+    for (int i = 0; i < n; ++i) {
+      if (loff[i] < 0) continue;
+      const AttnProb& P = g[i]->p;
+      int k = 0;
+      for (; k < (int)rb.size(); ++k)
+        if (rb[k].table == P.bias && rb[k].loff == loff[i] && rb[k].H == P.H && rb[k].rel_max == P.rel_max) break;
+      if (k == (int)rb.size()) {
+        rb.push_back(RelBias{P.bias, loff[i], P.H, P.rel_max, rbytes});
+        rbytes += align16(sizeof(float) * (size_t)P.H * (2 * (size_t)P.rel_max + 1));
+      }
+      rb_of[i] = k;
+    }
+  }
+  const size_t staged = mbytes + pbytes + lbytes + bbytes + cbytes;
   char *h = nullptr, *dv = nullptr;
-  int rc = ring_reserve(c, 64 + pbytes + mbytes + lbytes + bbytes + cbytes, &h, &dv);
+  int rc = ring_reserve(c, 64 + staged + rbytes, &h, &dv);
   if (rc) return rc;
   // tensor maps must sit on a 64-byte boundary in device memory
   const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
   char* hm = h + pad;
   char* dm = dv + pad;
-  for (int i = 0; i < n; ++i)
+  for (int i = 0; i < n; ++i) {
     probs[i].rel_lut = loff[i] < 0 ? nullptr : reinterpret_cast<const int32_t*>(dm + mbytes + pbytes) + loff[i];
+    if (rb_of[i] >= 0) probs[i].bias = reinterpret_cast<const float*>(dm + staged + rb[rb_of[i]].off);
+  }
   std::memcpy(hm, maps.data(), mbytes);
   std::memcpy(hm + mbytes, probs.data(), sizeof(supra::TmaProb) * n);
   if (!lut.empty()) std::memcpy(hm + mbytes + pbytes, lut.data(), lut.size() * sizeof(int32_t));
   std::memcpy(hm + mbytes + pbytes + lbytes, begin.data(), sizeof(int32_t) * (n + 1));
   std::memset(hm + mbytes + pbytes + lbytes + bbytes, 0, cbytes);
-  rc = ring_commit(c, h, dv, pad + mbytes + pbytes + lbytes + bbytes + cbytes);
+  rc = ring_commit(c, h, dv, pad + staged);
   if (rc) return rc;
+  for (const RelBias& r : rb) {
+    const cudaError_t e0 = supra::launch_rel_bias(r.table, reinterpret_cast<const int32_t*>(dm + mbytes + pbytes) + r.loff,
+                                                  r.H, r.rel_max, reinterpret_cast<float*>(dm + staged + r.off), c->stream);
+    if (e0 != cudaSuccess) return cuda_err(c, e0, "rel_bias");
+    c->launches += 1;
+  }
   supra::TmaLaunch L;
   L.next_tile = reinterpret_cast<int32_t*>(dm + mbytes + pbytes + lbytes + bbytes);
   L.maps = reinterpret_cast<const CUtensorMap*>(dm);

@@ -102,7 +102,9 @@ struct alignas(16) TmaProb {
   float* o;
   int64_t o_off;
   int64_t ldo;
-  const float* bias;  // [H, Lq, Lk] additive score bias, or nullptr
+  // [H, Lq, Lk] additive score bias, or nullptr; with rel_lut set, the T5 [buckets, H] table (the
+  // TF32 kernels) or the [H, 2 rel_max + 1] bias by relative position (the 128-row FP32 kernel)
+  const float* bias;
   int32_t Lq, Lk, H, D;
   int32_t mq, mk, mv;
   int32_t qx, qy, kx, ky, vx, vy;
@@ -298,5 +300,8 @@ cudaError_t launch_stage_copy(const void* src, void* dst, size_t bytes, cudaStre
 
 cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L,
                                  float* out, cudaStream_t s);
+// [H, 2 rel_max + 1]: the T5 table bias by relative position (lut over rel = -rel_max .. rel_max)
+cudaError_t launch_rel_bias(const float* table, const int32_t* lut, int32_t H, int32_t rel_max, float* out,
+                            cudaStream_t s);
 
 }  // namespace supra

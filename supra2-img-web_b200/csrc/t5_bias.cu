@@ -23,7 +23,29 @@ __global__ void __launch_bounds__(256) position_bias_kernel(const float* __restr
   }
 }
 
+// The bias as a function of the relative position alone: out[h*R + d] = table[lut[d]*H + h],
+// d = rel + rel_max over R = 2 rel_max + 1 positions (past +-rel_max the bucket no longer
+// changes). The FP32 attention kernel reads a T5 table bias from this array, one load per score.
+__global__ void __launch_bounds__(256) rel_bias_kernel(const float* __restrict__ table, const int32_t* __restrict__ lut,
+                                                       int32_t H, int32_t R, float* __restrict__ out) {
+  const int total = H * R;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int h = e / R;
+    out[e] = __ldg(table + (int64_t)__ldg(lut + (e - h * R)) * H + h);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_rel_bias(const float* table, const int32_t* lut, int32_t H, int32_t rel_max, float* out,
+                            cudaStream_t s) {
+  const int64_t total = (int64_t)H * (2 * (int64_t)rel_max + 1);
+  if (H <= 0 || rel_max < 0 || total > (int64_t(1) << 30)) return cudaErrorInvalidValue;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148) blocks = 148;
+  rel_bias_kernel<<<(unsigned)blocks, 256, 0, s>>>(table, lut, H, (int32_t)(2 * rel_max + 1), out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_position_bias(const float* table, const int32_t* lut, int32_t H, int32_t L, float* out,
                                  cudaStream_t s) {

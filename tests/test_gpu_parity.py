@@ -218,6 +218,44 @@ def test_t5_table_ragged_batch(gpu):
                                                     bias=bias))
 
 
+def test_t5_tables_mixed_in_one_flush(gpu):
+    """T5 table problems with different tables, bucket counts, max distances and head counts in
+    one flush of the persistent kernel (each distinct (table, buckets, max distance, H) gets its
+    own bias-by-relative-position array), relative positions past max_distance included, against
+    the float64 oracle."""
+    import supra_attn
+
+    rng = np.random.default_rng(35)
+    cfgs = [(12, 32, 128), (4, 16, 40), (12, 32, 128), (4, 8, 20), (12, 16, 40)]
+    tables = {}
+    for H, nb, md in cfgs:
+        if (H, nb) not in tables:
+            tables[(H, nb)] = (0.3 * rng.standard_normal(nb * H)).astype(np.float32)
+    tdev = {key: dev(t) for key, t in tables.items()}
+    probs = []
+    for i in range(20):
+        H, nb, md = cfgs[i % len(cfgs)]
+        L = int(rng.integers(65, 200))
+        q, k, v = (rng.standard_normal(L * H * 64).astype(np.float32) for _ in range(3))
+        probs.append((H, nb, md, L, q, k, v, dev(q), dev(k), dev(v), dev(np.zeros(L * H * 64))))
+    descs = (supra_attn.Desc * len(probs))()
+    for i, (H, nb, md, L, q, k, v, qd, kd, vd, od) in enumerate(probs):
+        descs[i] = supra_attn.make_desc(q=qd, k=kd, v=vd, out=od, Lq=L, Lk=L, H=H, D=64, ldq=H * 64, ldk=H * 64,
+                                        ldv=H * 64, scale=1.0, t5_table=tdev[(H, nb)], t5_buckets=nb,
+                                        t5_max_distance=md)
+    gpu.profile(True)
+    gpu.profile_reset()
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    names = sorted(r["name"] for r in gpu.profile_report())
+    gpu.profile(False)
+    assert names == ["attn_fp32_d64_tma_bias"], names
+    for H, nb, md, L, q, k, v, qd, kd, vd, od in probs:
+        bias = oracle.position_bias(tables[(H, nb)], L, H, nb, md).reshape(-1)
+        assert_close(host(od), oracle.attention_ops(q, k, v, L, L, H, 64, H * 64, H * 64, H * 64, scale=1.0,
+                                                    bias=bias))
+
+
 def test_t5_expanded_bias_ragged_batch(gpu):
     """Config 3 as the T5 call site issues it (app/models/t5.js:73-80): 256 prompts of ragged
     length L ~ U{1..128} in one flush, each with its own expanded [12, L, L] bias from
