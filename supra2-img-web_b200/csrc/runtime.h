@@ -40,19 +40,25 @@ struct ByteRange {
 };
 
 // Disjoint, merged [begin, end) byte ranges, kept sorted in a flat vector: an overlap test is one
-// binary search, an add merges in place, and a batch of ranges sorted by begin merges in one pass
-// (no allocation per range: recording 256 separate T5 prompts took ~0.15 ms with a node-based map).
+// binary search, an add merges in place (no allocation per range: recording 256 separate T5
+// prompts took ~0.15 ms with a node-based map). Ranges added as a batch wait unsorted until the
+// set is next queried, so a batch that is flushed before the next recording is never sorted.
 class IntervalSet {
  public:
-  void clear() { v_.clear(); }
-  bool empty() const { return v_.empty(); }
+  void clear() {
+    v_.clear();
+    pend_.clear();
+  }
+  bool empty() const { return v_.empty() && pend_.empty(); }
   bool overlaps(uintptr_t b, uintptr_t e) const {
+    settle();
     if (b >= e || v_.empty()) return false;
     // the first range ending after b is the only one that can start before e
     auto it = std::upper_bound(v_.begin(), v_.end(), b, [](uintptr_t x, const ByteRange& r) { return x < r.e; });
     return it != v_.end() && it->b < e;
   }
   void add(uintptr_t b, uintptr_t e) {
+    settle();
     if (b >= e) return;
     // ranges touching [b, e] (end >= b and begin <= e) merge with it
     auto lo = std::lower_bound(v_.begin(), v_.end(), b, [](const ByteRange& r, uintptr_t x) { return r.e < x; });
@@ -70,29 +76,37 @@ class IntervalSet {
       v_.erase(lo + 1, hi);
     }
   }
-  // Adds ranges sorted by begin (they may overlap or touch each other): one merge pass.
-  void add_sorted(const std::vector<ByteRange>& in) {
-    if (in.empty()) return;
-    std::vector<ByteRange> out;
-    out.reserve(v_.size() + in.size());
-    size_t i = 0, j = 0;
-    while (i < v_.size() || j < in.size()) {
-      const ByteRange r = (j == in.size() || (i < v_.size() && v_[i].b <= in[j].b)) ? v_[i++] : in[j++];
-      if (r.b >= r.e) continue;
-      if (!out.empty() && r.b <= out.back().e) out.back().e = std::max(out.back().e, r.e);
-      else out.push_back(r);
-    }
-    v_.swap(out);
-  }
+  // Adds ranges in any order (they may overlap or touch each other).
+  void add_batch(const std::vector<ByteRange>& in) { pend_.insert(pend_.end(), in.begin(), in.end()); }
 
  private:
-  std::vector<ByteRange> v_;
+  // sorts the pending ranges and merges them into v_ in one pass
+  void settle() const {
+    if (pend_.empty()) return;
+    auto by_begin = [](const ByteRange& a, const ByteRange& b) { return a.b < b.b; };
+    if (!std::is_sorted(pend_.begin(), pend_.end(), by_begin)) std::sort(pend_.begin(), pend_.end(), by_begin);
+    tmp_.clear();
+    tmp_.reserve(v_.size() + pend_.size());
+    size_t i = 0, j = 0;
+    while (i < v_.size() || j < pend_.size()) {
+      const ByteRange r = (j == pend_.size() || (i < v_.size() && v_[i].b <= pend_[j].b)) ? v_[i++] : pend_[j++];
+      if (r.b >= r.e) continue;
+      if (!tmp_.empty() && r.b <= tmp_.back().e) tmp_.back().e = std::max(tmp_.back().e, r.e);
+      else tmp_.push_back(r);
+    }
+    v_.swap(tmp_);
+    pend_.clear();
+  }
+  mutable std::vector<ByteRange> v_, pend_, tmp_;
 };
 
 enum Path : int { PATH_FUSED = 0, PATH_GEMM = 1, PATH_TF32 = 2, PATH_FP32_TMA = 3, PATH_LINEAR = 4 };
 
 struct Queued {
-  AttnProb p;
+  union {
+    AttnProb p;          // attention problems
+    supra::LinProb lin;  // PATH_LINEAR: the linear problem
+  };
   int path;
   int cfg;
   bool bias;
@@ -102,7 +116,6 @@ struct Queued {
   int64_t rows_q, rows_k, rows_v;  // whole rows of each operand buffer (TMA tensor maps)
   int64_t rows_o;                  // whole H*D-float rows of the output buffer
   int32_t t5_buckets, t5_maxd;      // T5 table bias (SUPRA_ATTN_F_T5_TABLE), else 0
-  supra::LinProb lin;               // PATH_LINEAR: the linear problem (p unused)
   float gn_eps;                     // PATH_LINEAR with GroupNorm of x
 };
 

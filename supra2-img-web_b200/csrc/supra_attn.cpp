@@ -142,12 +142,14 @@ bool record_batch_fast(supra_attn_ctx* c, const std::vector<Checked>& cks, int32
     while (j < W.size() && W[j].e <= r.b) ++j;
     if (j < W.size() && W[j].b < r.e) return false;
   }
-  for (const ByteRange& w : W)
-    if (c->qwrites.overlaps(w.b, w.e) || c->qreads.overlaps(w.b, w.e)) return false;
-  for (const ByteRange& r : R)
-    if (c->qwrites.overlaps(r.b, r.e)) return false;
-  c->qreads.add_sorted(R);
-  c->qwrites.add_sorted(W);
+  if (!c->qwrites.empty() || !c->qreads.empty()) {  // (empty after a flush)
+    for (const ByteRange& w : W)
+      if (c->qwrites.overlaps(w.b, w.e) || c->qreads.overlaps(w.b, w.e)) return false;
+    for (const ByteRange& r : R)
+      if (c->qwrites.overlaps(r.b, r.e)) return false;
+  }
+  c->qreads.add_batch(R);
+  c->qwrites.add_batch(W);
   c->queue.reserve(c->queue.size() + (size_t)n);
   for (int32_t i = 0; i < n; ++i)
     if (!cks[i].empty) c->queue.push_back(cks[i].q);

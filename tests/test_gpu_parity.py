@@ -712,6 +712,19 @@ def test_batch_hazards_fall_back_to_ordered_recording(gpu):
     gpu.sync()
     assert_close(host(o2), r2)
     assert_close(host(o1), r3)
+    # (4) a conflict-free batch (its ranges recorded unsorted), then a single call reading its
+    # output and a batch writing what the first batch read: both must see the batch's ranges
+    descs = (supra_attn.Desc * 2)(supra_attn.make_desc(q=qd, k=k2d, v=vd, out=o3, **kw),
+                                  supra_attn.make_desc(q=qd, k=kd, v=vd, out=o1, **kw))
+    gpu.enqueue_batch(descs)
+    attn(gpu, q=o1, k=kd, v=vd, out=o2, **kw)  # reads o1 (read after write)
+    descs = (supra_attn.Desc * 1)(supra_attn.make_desc(q=o3, k=kd, v=vd, out=k2d, **kw))  # writes k2 (after read)
+    gpu.enqueue_batch(descs)
+    gpu.sync()
+    assert_close(host(o3), r3)
+    assert_close(host(o1), r1)
+    assert_close(host(o2), r2)
+    assert_close(host(k2d), oracle.attention_ops(r3, k, v, L, L, H, D, ld, ld, ld))
 
 
 @pytest.mark.parametrize("Lq,Lk,H,D,bias", [
