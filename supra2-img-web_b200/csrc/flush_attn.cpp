@@ -344,8 +344,10 @@ int flush_gemm(supra_attn_ctx* c, std::vector<const Queued*>& g) {
 }
 
 // A group read through TMA tensor maps (the TF32 tensor-core kernel or the persistent FP32
-// kernel): one tensor map per distinct (buffer, ld, rows, box) in the flush, encoded once per
-// context and cached; problems refer to maps by index.
+// kernels): one tensor map per distinct (buffer, ld, rows, box), encoded once per context and
+// kept in the context's device table of maps; problems refer to maps by their slot there, and
+// a flush stages only the maps that are new to the table (a batch of separate per-prompt
+// buffers reuses its maps call after call).
 int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   // Unbiased FP32 launches with at least one 256-row tile per SM that lose little to the larger
   // tile (query rows rounded up to 256 at most 1/8 more than rounded up to 128) run on the
@@ -372,9 +374,12 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   std::stable_sort(g.begin(), g.end(), [](const Queued* a, const Queued* b) { return a->p.Lk > b->p.Lk; });
   const int n = (int)g.size();
   std::vector<supra::TmaProb> probs((size_t)n);
-  std::vector<CUtensorMap> maps;
-  maps.reserve(3 * (size_t)n);
-  ++c->map_epoch;
+  {
+    const int rm = map_table_reserve(c, 4 * (size_t)n);  // (at most four maps per problem)
+    if (rm) return rm;
+  }
+  const int32_t fresh0 = c->map_table_used;
+  std::vector<const CUtensorMap*> fresh;  // maps new to the table, slots fresh0, fresh0 + 1, ...
   MapKey last_key{0, 0, 0, 0, 0, 0, 0, 0};
   int32_t last_idx = -1;
   auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box_cols, int32_t box_rows,
@@ -385,7 +390,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
       *out = last_idx;
       return SUPRA_ATTN_OK;
     }
-    const int rc = map_slot(c, k, maps, out);
+    const int rc = map_table_slot(c, k, fresh, out);
     if (rc) return rc;
     last_key = k;
     last_idx = *out;
@@ -472,7 +477,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   std::vector<int64_t> loff;
   const size_t pbytes = align16(sizeof(supra::TmaProb) * n);
   const size_t lbytes = t5_luts(g, lut, loff);
-  const size_t mbytes = sizeof(CUtensorMap) * maps.size();
+  const size_t fbytes = sizeof(CUtensorMap) * fresh.size();
   const size_t bbytes = align16(sizeof(int32_t) * (n + 1));
   // the launch's tile counter and, with key splits, one counter per (group, warp), staged as zero
   const size_t cbytes = 16 + (used_splits > 1 ? align16(sizeof(int32_t) * 4 * (size_t)group0) : 0);
@@ -506,36 +511,41 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
       rb_of[i] = k;
     }
   }
-  const size_t staged = mbytes + pbytes + lbytes + bbytes + cbytes;
+  // ring: problems | bucket LUTs | tile prefixes | counters (staged), then the relative-bias
+  // arrays (device only) and the new maps (host only: staged into their table slots)
+  const size_t staged = pbytes + lbytes + bbytes + cbytes;
   char *h = nullptr, *dv = nullptr;
-  int rc = ring_reserve(c, 64 + staged + rbytes, &h, &dv);
+  int rc = ring_reserve(c, staged + rbytes + fbytes, &h, &dv);
   if (rc) return rc;
-  // tensor maps must sit on a 64-byte boundary in device memory
-  const size_t pad = (64 - (reinterpret_cast<uintptr_t>(dv) & 63)) & 63;
-  char* hm = h + pad;
-  char* dm = dv + pad;
   for (int i = 0; i < n; ++i) {
-    probs[i].rel_lut = loff[i] < 0 ? nullptr : reinterpret_cast<const int32_t*>(dm + mbytes + pbytes) + loff[i];
-    if (rb_of[i] >= 0) probs[i].bias = reinterpret_cast<const float*>(dm + staged + rb[rb_of[i]].off);
+    probs[i].rel_lut = loff[i] < 0 ? nullptr : reinterpret_cast<const int32_t*>(dv + pbytes) + loff[i];
+    if (rb_of[i] >= 0) probs[i].bias = reinterpret_cast<const float*>(dv + staged + rb[rb_of[i]].off);
   }
-  std::memcpy(hm, maps.data(), mbytes);
-  std::memcpy(hm + mbytes, probs.data(), sizeof(supra::TmaProb) * n);
-  if (!lut.empty()) std::memcpy(hm + mbytes + pbytes, lut.data(), lut.size() * sizeof(int32_t));
-  std::memcpy(hm + mbytes + pbytes + lbytes, begin.data(), sizeof(int32_t) * (n + 1));
-  std::memset(hm + mbytes + pbytes + lbytes + bbytes, 0, cbytes);
-  rc = ring_commit(c, h, dv, pad + staged);
+  std::memcpy(h, probs.data(), sizeof(supra::TmaProb) * n);
+  if (!lut.empty()) std::memcpy(h + pbytes, lut.data(), lut.size() * sizeof(int32_t));
+  std::memcpy(h + pbytes + lbytes, begin.data(), sizeof(int32_t) * (n + 1));
+  std::memset(h + pbytes + lbytes + bbytes, 0, cbytes);
+  if (fbytes) {  // the new maps into their table slots (ordered before the launch by the stream)
+    char* hf = h + staged + rbytes;
+    for (size_t i = 0; i < fresh.size(); ++i) std::memcpy(hf + i * sizeof(CUtensorMap), fresh[i], sizeof(CUtensorMap));
+    const cudaError_t ef = supra::launch_stage_copy(c->ring_hd + (hf - c->ring_h), c->map_table + fresh0, fbytes,
+                                                    c->stream);
+    if (ef != cudaSuccess) return cuda_err(c, ef, "map table: stage");
+    c->launches += 1;
+  }
+  rc = ring_commit(c, h, dv, staged);  // (its event, recorded after both copies, frees the ring half)
   if (rc) return rc;
   for (const RelBias& r : rb) {
-    const cudaError_t e0 = supra::launch_rel_bias(r.table, reinterpret_cast<const int32_t*>(dm + mbytes + pbytes) + r.loff,
-                                                  r.H, r.rel_max, reinterpret_cast<float*>(dm + staged + r.off), c->stream);
+    const cudaError_t e0 = supra::launch_rel_bias(r.table, reinterpret_cast<const int32_t*>(dv + pbytes) + r.loff,
+                                                  r.H, r.rel_max, reinterpret_cast<float*>(dv + staged + r.off), c->stream);
     if (e0 != cudaSuccess) return cuda_err(c, e0, "rel_bias");
     c->launches += 1;
   }
   supra::TmaLaunch L;
-  L.next_tile = reinterpret_cast<int32_t*>(dm + mbytes + pbytes + lbytes + bbytes);
-  L.maps = reinterpret_cast<const CUtensorMap*>(dm);
-  L.probs = reinterpret_cast<const supra::TmaProb*>(dm + mbytes);
-  L.begin = reinterpret_cast<const int32_t*>(dm + mbytes + pbytes + lbytes);
+  L.next_tile = reinterpret_cast<int32_t*>(dv + pbytes + lbytes + bbytes);
+  L.maps = c->map_table;
+  L.probs = reinterpret_cast<const supra::TmaProb*>(dv);
+  L.begin = reinterpret_cast<const int32_t*>(dv + pbytes + lbytes);
   L.n = n;
   L.total = (int32_t)total;
   L.uniform = 0;

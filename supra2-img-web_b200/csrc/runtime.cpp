@@ -47,6 +47,54 @@ bool encode_map(CUtensorMap* m, const MapKey& k) {
   return false;
 }
 
+int map_table_reserve(supra_attn_ctx* c, size_t need) {
+  if (c->map_cache.size() + need > 65536) {  // (every map is encoded and staged again as it is used)
+    c->map_cache.clear();
+    ++c->map_table_epoch;
+    c->map_table_used = 0;
+  }
+  if (need > (size_t)c->map_table_cap) {
+    size_t cap = 16384;
+    while (cap < need) cap *= 2;
+    if (cap > (size_t(1) << 24)) return set_err(c, SUPRA_ATTN_EINVAL, "too many tensor maps in one flush");
+    if (c->map_table) {  // earlier launches may still read the old table
+      cudaError_t e = cudaStreamSynchronize(c->stream);
+      if (e != cudaSuccess) return cuda_err(c, e, "map table: stream sync");
+      cudaFree(c->map_table);
+      c->map_table = nullptr;
+      c->map_table_cap = 0;
+    }
+    if (cudaMalloc(&c->map_table, cap * sizeof(CUtensorMap)) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(c, SUPRA_ATTN_ENOMEM, "map table: cudaMalloc failed");
+    }
+    c->map_table_cap = (int32_t)cap;
+    ++c->map_table_epoch;
+    c->map_table_used = 0;
+  } else if ((size_t)c->map_table_used + need > (size_t)c->map_table_cap) {
+    ++c->map_table_epoch;  // (launches already on the stream read their slots before they are rewritten)
+    c->map_table_used = 0;
+  }
+  return SUPRA_ATTN_OK;
+}
+
+int map_table_slot(supra_attn_ctx* c, const MapKey& k, std::vector<const CUtensorMap*>& fresh, int32_t* out) {
+  auto ct = c->map_cache.find(k);
+  if (ct == c->map_cache.end()) {
+    CachedMap e;
+    if (!encode_map(&e.map, k)) return set_err(c, SUPRA_ATTN_ECUDA, "cuTensorMapEncodeTiled failed");
+    ct = c->map_cache.emplace(k, e).first;  // (references to entries stay valid: no trim here)
+  }
+  CachedMap& m = ct->second;
+  if (m.depoch != c->map_table_epoch) {
+    m.depoch = c->map_table_epoch;
+    m.dslot = c->map_table_used++;
+    fresh.push_back(&m.map);
+  }
+  *out = m.dslot;
+  return SUPRA_ATTN_OK;
+}
+
 int map_slot(supra_attn_ctx* c, const MapKey& k, std::vector<CUtensorMap>& maps, int32_t* out) {
   auto ct = c->map_cache.find(k);
   if (ct == c->map_cache.end()) {

@@ -170,8 +170,10 @@ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 // An encoded tensor map, and its slot in the launch being packed when it was last used there.
 struct CachedMap {
   CUtensorMap map;
-  uint64_t epoch = 0;
+  uint64_t epoch = 0;  // map_slot: the launch this map was last packed into, and its slot there
   int32_t slot = -1;
+  int32_t dslot = -1;   // map_table_slot: its slot in the context's device table ...
+  uint64_t depoch = 0;  // ... valid while this equals the table's epoch
 };
 
 // A validated problem with the byte ranges it reads and writes (hazard tracking).
@@ -229,6 +231,12 @@ struct supra_attn_ctx {
   // encoded TMA tensor maps, reused across flushes (keyed by buffer, box and element handling)
   std::unordered_map<supra::rt::MapKey, supra::rt::CachedMap, supra::rt::MapKeyHash> map_cache;
   uint64_t map_epoch = 0;  // one per launch being packed (map_slot)
+  // the attention launches' tensor maps: a device table that persists across flushes, each cached
+  // map given a slot at its first use (only maps new to the table are staged); a new epoch
+  // empties it
+  CUtensorMap* map_table = nullptr;
+  int32_t map_table_cap = 0, map_table_used = 0;
+  uint64_t map_table_epoch = 1;
 
   int64_t launches = 0;
   std::string err;
@@ -242,6 +250,13 @@ bool encode_map(CUtensorMap* m, const MapKey& k);
 // The slot in `maps` (the tensor maps of the launch being packed, map epoch c->map_epoch) of the
 // map for k: encoded once per context and cached, appended to maps at its first use in the epoch.
 int map_slot(supra_attn_ctx* c, const MapKey& k, std::vector<CUtensorMap>& maps, int32_t* out);
+// Makes room for `need` more maps in the device table (a new epoch when it is full: launches
+// already on the stream finish before the slots are written again; a larger table when one
+// launch needs more than it holds), trimming the host cache alongside.
+int map_table_reserve(supra_attn_ctx* c, size_t need);
+// The device-table slot of the map for k; a map new to the table is appended to `fresh` (the
+// slots of a flush's fresh maps are consecutive, from the table's fill level before the flush).
+int map_table_slot(supra_attn_ctx* c, const MapKey& k, std::vector<const CUtensorMap*>& fresh, int32_t* out);
 int set_err(supra_attn_ctx* c, int code, const char* fmt, ...);
 int cuda_err(supra_attn_ctx* c, cudaError_t e, const char* what);
 int ring_reserve(supra_attn_ctx* c, size_t bytes, char** host, char** dev);

@@ -235,6 +235,7 @@ int supra_attn_destroy(supra_attn_ctx* c) {
   if (c->scratch) cudaFree(c->scratch);
   if (c->gn_stats) cudaFree(c->gn_stats);
   if (c->lin_split) cudaFree(c->lin_split);
+  if (c->map_table) cudaFree(c->map_table);
   if (c->ring_h) cudaFreeHost(c->ring_h);
   if (c->ring_d) cudaFree(c->ring_d);
   for (int i = 0; i < 2; ++i)

@@ -256,6 +256,54 @@ def test_t5_tables_mixed_in_one_flush(gpu):
                                                     bias=bias))
 
 
+@pytest.mark.parametrize("variant", ["fp32", "tf32x3"])
+def test_tensor_map_table_refills_and_grows(gpu, variant):
+    """Flushes whose problems each bring their own buffers (distinct base pointers: new tensor
+    maps every flush). The context's device table of maps fills up, starts over (maps staged
+    again into reused slots while earlier launches may still be queued) and, for one flush that
+    needs more maps than it holds, grows; sampled outputs of every flush against the float64
+    oracle."""
+    import supra_attn
+
+    rng = np.random.default_rng(41)
+    H, D, ld = 2, 64, 128
+    pool = rng.standard_normal(12 * 14000 + 70 * ld + 64).astype(np.float32)
+    pd = dev(pool)
+    tol = TOL if variant == "fp32" else 1e-5
+
+    def run(first, n, L):
+        # problem i: q, k, v start 0, 4 and 8 floats after base 12 * (first + i) of the pool
+        # (overlapping reads, 16-byte aligned, each its own tensor map)
+        out = _torch().zeros(n * L * ld, device="cuda")
+        descs = (supra_attn.Desc * n)()
+        for i in range(n):
+            b = 12 * (first + i)
+            d = supra_attn.make_desc(q=pd, k=pd, v=pd, out=out, Lq=L, Lk=L, H=H, D=D, ldq=ld, ldk=ld, ldv=ld,
+                                     oOff=i * L * ld, variant=variant)
+            for name, off in (("q", b), ("k", b + 4), ("v", b + 8)):
+                setattr(d, name, pd.data_ptr() + 4 * off)
+                setattr(d, name + "_size", L * ld)
+            descs[i] = d
+        gpu.enqueue_batch(descs)
+        return out
+
+    outs = []
+    first = 0
+    for f in range(9):  # 700 problems x 3 new maps per flush: the 16384-slot table starts over
+        outs.append((first, 700, 65 + f % 3, run(first, 700, 65 + f % 3)))
+        gpu.flush()
+        first += 700
+    outs.append((first, 4200, 65, run(first, 4200, 65)))  # 12600 maps in one flush: the table grows
+    gpu.sync()
+    for first, n, L, out in outs:
+        got = host(out)
+        for i in sorted(set([0, n - 1] + list(rng.integers(0, n, 6)))):
+            b = 12 * (first + i)
+            q, k, v = (pool[o:o + L * ld] for o in (b, b + 4, b + 8))
+            ref = oracle.attention_ops(q, k, v, L, L, H, D, ld, ld, ld)
+            assert_close(got[i * L * ld:(i + 1) * L * ld], ref, tol)
+
+
 def test_t5_expanded_bias_ragged_batch(gpu):
     """Config 3 as the T5 call site issues it (app/models/t5.js:73-80): 256 prompts of ragged
     length L ~ U{1..128} in one flush, each with its own expanded [12, L, L] bias from
@@ -505,7 +553,9 @@ def test_determinism_and_profile(gpu):
     np.testing.assert_array_equal(outs[0], outs[1])
     rep = gpu.profile_report()
     gpu.profile(False)
-    assert gpu.launch_count() - n0 == 4  # per flush: descriptor staging + the attention kernel
+    # per flush: descriptor staging + the attention kernel; the first flush also stages its new
+    # tensor maps into the context's table, which the second reuses
+    assert gpu.launch_count() - n0 == 5
     names = [r["name"] for r in rep]
     assert names == ["attn_fp32_d64_tma"], names  # the persistent TMA kernel serves the DiT shapes
 
@@ -560,7 +610,9 @@ def test_fp32_tma_many_ragged_tiles(gpu):
     n0 = gpu.launch_count()
     gpu.enqueue_batch(descs)
     gpu.sync()
-    assert gpu.launch_count() - n0 == 2  # descriptor staging + one attention launch
+    # descriptor staging + one attention launch, and the staging of the batch's tensor maps (new
+    # buffers) into the context's table
+    assert gpu.launch_count() - n0 == 3
     got = host(out).reshape(n, Lq, H * D)
     qn, kvn = q.numpy().reshape(n, Lq, H * D), kv.numpy()
     for b in list(range(0, n, 37)) + [n - 1]:
