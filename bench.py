@@ -391,21 +391,23 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
                 descs = (supra_attn.Desc * len(mine))(*[descs[i] for i in mine])
             gpu.enqueue_batch(descs)
             gpu.sync()
-            gpu.profile(True)
-            gpu.profile_reset()
             times = []
-            for _ in range(reps):
-                flush.fill_(1.0)
-                if world > 1:
-                    dist.barrier(device_ids=[dev.index])
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-                gpu.enqueue_batch(descs)
-                gpu.flush()
-                e1.record()
-                torch.cuda.synchronize()
-                times.append(e0.elapsed_time(e1))
+            for prof_on in (False, True):  # timed without the profiler's events, then profiled apart
+                gpu.profile(prof_on)
+                gpu.profile_reset()
+                for _ in range(reps):
+                    flush.fill_(1.0)
+                    if world > 1:
+                        dist.barrier(device_ids=[dev.index])
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    gpu.enqueue_batch(descs)
+                    gpu.flush()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    if not prof_on:
+                        times.append(e0.elapsed_time(e1))
             prof = gpu.profile_report()
             gpu.profile(False)
             if world > 1:  # each rep's time is the slowest rank's
@@ -441,18 +443,20 @@ def measure_call_sites(gpu, torch, dev, seed: int, reps: int = 5, only=None, cpu
                 d.variant = code
             fn()
             gpu.sync()
-            gpu.profile(True)
-            gpu.profile_reset()
             times = []
-            for _ in range(reps):
-                flush.fill_(1.0)
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-                fn()
-                e1.record()
-                torch.cuda.synchronize()
-                times.append(e0.elapsed_time(e1))
+            for prof_on in (False, True):  # timed without the profiler's events, then profiled apart
+                gpu.profile(prof_on)
+                gpu.profile_reset()
+                for _ in range(reps):
+                    flush.fill_(1.0)
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    fn()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    if not prof_on:
+                        times.append(e0.elapsed_time(e1))
             prof = gpu.profile_report()
             gpu.profile(False)
             per = {}
