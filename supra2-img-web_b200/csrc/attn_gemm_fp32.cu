@@ -153,6 +153,54 @@ __global__ void __launch_bounds__(kGT, 2) gemm_qk_kernel(const GemmLaunch L) {
 // and the problem's scale is applied here, exp(scale s - max(scale s)); with L.lo set each
 // probability p leaves split, hi (p with its 13 low mantissa bits cleared) in place and p - hi at
 // the same offset from L.lo. Columns Lk .. ldS - 1 are zeroed.
+// A row of at most 128 NV keys (ldS floats, a multiple of 4, 16-byte aligned) held in registers:
+// lane l owns the float4 chunks l, l + 32, ..., so the row is read once and written once (P, and
+// its lo part for the split tensor-core product) instead of three passes over memory. Same
+// arithmetic per score as the loop form below (scale, max, expf(s - max), one reciprocal); the
+// sum is formed in another order.
+template <int NV>
+__device__ __forceinline__ void softmax_row_regs(float* __restrict__ row, float* __restrict__ lrow, int Lk, int ldS,
+                                                 float sc, int lane) {
+  float4 x[NV];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    x[k] = c < ldS ? *reinterpret_cast<const float4*>(row + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[k].x = c + 0 < Lk ? x[k].x * sc : -INFINITY;
+    x[k].y = c + 1 < Lk ? x[k].y * sc : -INFINITY;
+    x[k].z = c + 2 < Lk ? x[k].z * sc : -INFINITY;
+    x[k].w = c + 3 < Lk ? x[k].w * sc : -INFINITY;
+    mx = fmaxf(mx, fmaxf(fmaxf(x[k].x, x[k].y), fmaxf(x[k].z, x[k].w)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sm = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {  // (expf(-inf) = 0 past Lk)
+    x[k] = make_float4(expf(x[k].x - mx), expf(x[k].y - mx), expf(x[k].z - mx), expf(x[k].w - mx));
+    sm += (x[k].x + x[k].y) + (x[k].z + x[k].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+  const float inv = 1.0f / sm;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    if (c >= ldS) continue;
+    float4 p = make_float4(x[k].x * inv, x[k].y * inv, x[k].z * inv, x[k].w * inv);
+    if (lrow) {
+      const float4 h = make_float4(__uint_as_float(__float_as_uint(p.x) & 0xffffe000u),
+                                   __uint_as_float(__float_as_uint(p.y) & 0xffffe000u),
+                                   __uint_as_float(__float_as_uint(p.z) & 0xffffe000u),
+                                   __uint_as_float(__float_as_uint(p.w) & 0xffffe000u));
+      *reinterpret_cast<float4*>(lrow + c) = make_float4(p.x - h.x, p.y - h.y, p.z - h.z, p.w - h.w);
+      p = h;
+    }
+    *reinterpret_cast<float4*>(row + c) = p;
+  }
+}
+
 __global__ void __launch_bounds__(256) softmax_rows_kernel(const GemmLaunch L) {
   const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -163,6 +211,18 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(const GemmLaunch L) {
   const float sc = L.sm_scale ? L.probs[u.prob].scale : 1.f;
   const int64_t off = u.s_off + (int64_t)(wid - u.row_begin) * u.ldS;
   float* row = L.scratch + off;
+  // rows of up to 1024 keys in registers (the VAE's 32 x 32 latents): one pass each way
+  switch ((u.ldS + 127) >> 7) {
+    case 1: return softmax_row_regs<1>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 2: return softmax_row_regs<2>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 3: return softmax_row_regs<3>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 4: return softmax_row_regs<4>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 5: return softmax_row_regs<5>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 6: return softmax_row_regs<6>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 7: return softmax_row_regs<7>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    case 8: return softmax_row_regs<8>(row, L.lo ? L.lo + off : nullptr, Lk, u.ldS, sc, lane);
+    default: break;
+  }
   float mx = -INFINITY;
   for (int c = lane; c < Lk; c += 32) mx = fmaxf(mx, row[c] * sc);
 #pragma unroll

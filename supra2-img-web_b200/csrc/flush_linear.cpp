@@ -386,6 +386,8 @@ int run_linear_tc(supra_attn_ctx* c, std::vector<TcJob>& jobs, bool split, doubl
     S.begin = reinterpret_cast<const int32_t*>(dv + pad + mbytes + pbytes + bbytes + jbytes);
     S.n = (int32_t)sj.size();
     S.total = (int32_t)stotal;
+    S.trans_jobs = 0;
+    for (const supra::SplitJob& J : sj) S.trans_jobs += J.trans ? 1 : 0;
     {
       ProfScope ps(c, "linear_split", 0.0, sbytes);
       e = supra::launch_split(S, c->stream);

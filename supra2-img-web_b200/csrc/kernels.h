@@ -284,6 +284,7 @@ struct SplitLaunch {
   const SplitJob* jobs;
   const int32_t* begin;  // first tile of each job
   int32_t n, total;
+  int32_t trans_jobs;  // how many of the jobs are transposed (none: the kernel form without them)
 };
 // All jobs of one flush in one launch (32 x 128 tiles, HBM-bound).
 cudaError_t launch_split(const SplitLaunch& L, cudaStream_t s);

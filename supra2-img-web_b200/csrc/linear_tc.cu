@@ -416,9 +416,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_tc_kernel(const __grid_con
 // order: x * xscale, times rowscale[r] when set (a gate folded into w, with the bias scaled
 // alongside), normalised when gn_stats is set: (x - mean) * rstd * g + b (then SiLU if asked) with
 // g, b = gamma, beta (GroupNorm), 1 + scale, shift (modulated LayerNorm) or 1, 0 (plain
-// LayerNorm), as the linear_fp32 prologue applies them. Lanes run along k, so loads and stores
-// are 128-byte rows per warp; a transposed job ([K, rows] source) goes through a shared-memory
-// tile so that its loads run along r.
+// LayerNorm), as the linear_fp32 prologue applies them. Lanes run along k: a job whose rows are
+// 16-byte aligned moves 16 bytes per lane (512-byte rows per warp, a warp's 4 rows loaded before
+// any is stored), others 4 bytes per lane; a transposed job ([K, rows] source) goes through a
+// shared-memory tile so that its loads run along r.
 constexpr int kSplitRows = kSplitTileRows, kSplitCols = kSplitTileCols;
 
 __device__ __forceinline__ void split_store(const SplitJob& J, int32_t r, int32_t k, float x) {
@@ -427,8 +428,11 @@ __device__ __forceinline__ void split_store(const SplitJob& J, int32_t r, int32_
   if (J.lo) J.lo[(int64_t)r * J.ldd + k] = x - h;
 }
 
+// TRANS: the launch has transposed jobs (the form without them keeps fewer registers and no
+// transposition tile)
+template <bool TRANS>
 __global__ void __launch_bounds__(256) split_kernel(const SplitLaunch L) {
-  __shared__ float t[kSplitCols][kSplitRows + 1];
+  __shared__ float t[TRANS ? kSplitCols : 1][kSplitRows + 1];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int tile = blockIdx.x; tile < L.total; tile += gridDim.x) {
     const int ji = find_problem(L.begin, L.n, tile);
@@ -436,7 +440,7 @@ __global__ void __launch_bounds__(256) split_kernel(const SplitLaunch L) {
     const int local = tile - __ldg(L.begin + ji);
     const int rt = local / J.ktiles, kt = local - rt * J.ktiles;
     const int32_t r0 = rt * kSplitRows, k0 = kt * kSplitCols;
-    if (J.trans) {  // (uniform over the block: one job per tile)
+    if (TRANS && J.trans) {  // (uniform over the block: one job per tile)
 #pragma unroll 4
       for (int kk = ty; kk < kSplitCols; kk += 8) {
         const int32_t k = k0 + kk, r = r0 + tx;
@@ -453,6 +457,56 @@ __global__ void __launch_bounds__(256) split_kernel(const SplitLaunch L) {
         }
       }
       __syncthreads();  // the tile buffer is rewritten by the next iteration
+      continue;
+    }
+    // 16-byte rows (every job's copy, and sources whose rows are 16-byte aligned): lane tx owns
+    // columns k0 + 4 tx .. +3, and the 4 rows of a warp are loaded before any is stored
+    const bool vec = ((J.ld | J.K | J.ldd) & 3) == 0 && ((reinterpret_cast<uintptr_t>(J.src) |
+                                                         reinterpret_cast<uintptr_t>(J.hi) |
+                                                         reinterpret_cast<uintptr_t>(J.lo)) & 15u) == 0;
+    if (vec) {
+      constexpr int kRw = kSplitRows / 8;  // rows per warp
+      const int32_t k = k0 + 4 * tx;
+      float4 xv[kRw];
+#pragma unroll
+      for (int i = 0; i < kRw; ++i) {
+        const int32_t r = r0 + ty + 8 * i;
+        xv[i] = (r < J.rows && k < J.K) ? __ldg(reinterpret_cast<const float4*>(J.src + (int64_t)r * J.ld + k))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kRw; ++i) {
+        const int32_t r = r0 + ty + 8 * i;
+        if (r >= J.rows) break;
+        float g = J.xscale;
+        if (J.rowscale) {
+          const float rs = __ldg(J.rowscale + r);
+          g *= rs;
+          if (J.bias_out && kt == 0 && tx == 0) J.bias_out[r] = J.bias_in ? __ldg(J.bias_in + r) * rs : 0.f;
+        }
+        if (k >= J.K) continue;
+        float v[4] = {xv[i].x * g, xv[i].y * g, xv[i].z * g, xv[i].w * g};
+        if (J.gn_stats) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 ms = __ldg(J.gn_stats + (int64_t)(r / J.gn_rows) * J.gn_groups + (k + e) / J.gn_cg);
+            float ga = 1.f, b = 0.f;
+            if (J.gn_mode != kNormPlain) {
+              ga = __ldg(J.gamma + k + e);
+              b = __ldg(J.beta + k + e);
+              if (J.gn_mode == kNormModulated) ga = 1.f + ga;
+            }
+            v[e] = (v[e] - ms.x) * ms.y * ga + b;
+            if (J.gn_silu) v[e] = v[e] / (1.f + __expf(-v[e]));
+          }
+        }
+        float h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __uint_as_float(__float_as_uint(v[e]) & 0xffffe000u);
+        const int64_t o = (int64_t)r * J.ldd + k;
+        if (J.hi) *reinterpret_cast<float4*>(J.hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+        if (J.lo) *reinterpret_cast<float4*>(J.lo + o) = make_float4(v[0] - h[0], v[1] - h[1], v[2] - h[2], v[3] - h[3]);
+      }
       continue;
     }
     for (int rr = ty; rr < kSplitRows; rr += 8) {
@@ -500,7 +554,8 @@ cudaError_t launch_split(const SplitLaunch& L, cudaStream_t s) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = L.total < 8 * sms ? L.total : 8 * sms;
-  split_kernel<<<grid, 256, 0, s>>>(L);
+  if (L.trans_jobs == 0) split_kernel<false><<<grid, 256, 0, s>>>(L);
+  else split_kernel<true><<<grid, 256, 0, s>>>(L);
   return cudaGetLastError();
 }
 
