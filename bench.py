@@ -1023,7 +1023,7 @@ def main():
         # The first step's inputs and the last step's output cannot hide behind other steps: those
         # two steps run in CH sequence chunks, each chunk's compute waiting only for its own upload
         # and each chunk's read-back starting once it is computed. The steps between them run whole.
-        CH = 4
+        CH = min(4, S)
         cb = [S * c // CH for c in range(CH + 1)]
         dsz = supra_attn._lib.C.sizeof(supra_attn.Desc)
 
@@ -1122,7 +1122,7 @@ def main():
                "d2h_bytes_per_step": 4 * out_cross.numel() * world,
                "ms_per_step": float(t2.item()) / args.steps,
                "pipeline": ("inputs and outputs double-buffered; uploads, compute and read-backs on three streams; "
-                            "the first and last steps in 4 sequence chunks"),
+                            f"the first and last steps in {CH} sequence chunks"),
                "host_cpus": cpus_near_gpu or "all",
                "copy_volume": ("per step every rank uploads its sequences' self-attention q/k/v and cross-attention q "
                                "once and reads its cross-attention output back once; the 14 blocks of the step reuse "
