@@ -432,7 +432,8 @@ __device__ __forceinline__ void split_store(const SplitJob& J, int32_t r, int32_
 // transposition tile)
 template <bool TRANS>
 __global__ void __launch_bounds__(256) split_kernel(const SplitLaunch L) {
-  __shared__ float t[TRANS ? kSplitCols : 1][kSplitRows + 1];
+  static_assert(kSplitRows == 32, "the transposition tile's swizzle spans 32 columns");
+  __shared__ float t[TRANS ? kSplitCols : 1][kSplitRows];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int tile = blockIdx.x; tile < L.total; tile += gridDim.x) {
     const int ji = find_problem(L.begin, L.n, tile);
@@ -441,19 +442,39 @@ __global__ void __launch_bounds__(256) split_kernel(const SplitLaunch L) {
     const int rt = local / J.ktiles, kt = local - rt * J.ktiles;
     const int32_t r0 = rt * kSplitRows, k0 = kt * kSplitCols;
     if (TRANS && J.trans) {  // (uniform over the block: one job per tile)
+      // element (r, k) of the tile at t[k][r ^ ((k >> 2) & 31)]: the loads (one k, lanes along r)
+      // and the 16-byte stores' reads (one r, lane l reading k = 4l .. 4l + 3) both hit 32
+      // distinct banks
 #pragma unroll 4
       for (int kk = ty; kk < kSplitCols; kk += 8) {
         const int32_t k = k0 + kk, r = r0 + tx;
-        t[kk][tx] = (k < J.K && r < J.rows) ? __ldg(J.src + (int64_t)k * J.ld + r) * J.xscale : 0.f;
+        t[kk][tx ^ ((kk >> 2) & 31)] =
+            (k < J.K && r < J.rows) ? __ldg(J.src + (int64_t)k * J.ld + r) * J.xscale : 0.f;
       }
       __syncthreads();
+      const bool vec = ((J.K | J.ldd) & 3) == 0 &&
+                       ((reinterpret_cast<uintptr_t>(J.hi) | reinterpret_cast<uintptr_t>(J.lo)) & 15u) == 0;
       for (int rr = ty; rr < kSplitRows; rr += 8) {
         const int32_t r = r0 + rr;
         if (r >= J.rows) break;
+        if (vec) {  // lane tx: columns k0 + 4 tx .. +3 of row r, one 16-byte store per array
+          const int32_t k = k0 + 4 * tx;
+          if (k >= J.K) continue;
+          float v[4], h[4];
 #pragma unroll
-        for (int c = 0; c < kSplitCols / 32; ++c) {
-          const int kl = 32 * c + tx;
-          if (k0 + kl < J.K) split_store(J, r, k0 + kl, t[kl][rr]);
+          for (int e = 0; e < 4; ++e) {
+            v[e] = t[4 * tx + e][rr ^ tx];
+            h[e] = __uint_as_float(__float_as_uint(v[e]) & 0xffffe000u);
+          }
+          const int64_t o = (int64_t)r * J.ldd + k;
+          if (J.hi) *reinterpret_cast<float4*>(J.hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+          if (J.lo) *reinterpret_cast<float4*>(J.lo + o) = make_float4(v[0] - h[0], v[1] - h[1], v[2] - h[2], v[3] - h[3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < kSplitCols / 32; ++c) {
+            const int kl = 32 * c + tx;
+            if (k0 + kl < J.K) split_store(J, r, k0 + kl, t[kl][rr ^ ((kl >> 2) & 31)]);
+          }
         }
       }
       __syncthreads();  // the tile buffer is rewritten by the next iteration
