@@ -380,6 +380,18 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
   }
   const int32_t fresh0 = c->map_table_used;
   std::vector<const CUtensorMap*> fresh;  // maps new to the table, slots fresh0, fresh0 + 1, ...
+  // Slots handed out below hold their maps only once the staging copy is on the stream: a return
+  // before that starts the table over, so no later launch reads a slot that was never written.
+  struct TableGuard {
+    supra_attn_ctx* c;
+    bool armed;
+    ~TableGuard() {
+      if (armed) {
+        ++c->map_table_epoch;
+        c->map_table_used = 0;
+      }
+    }
+  } table_guard{c, true};
   MapKey last_key{0, 0, 0, 0, 0, 0, 0, 0};
   int32_t last_idx = -1;
   auto map_index = [&](const float* base, int64_t ld, int64_t rows, int32_t box_cols, int32_t box_rows,
@@ -533,6 +545,7 @@ int flush_tma(supra_attn_ctx* c, std::vector<const Queued*>& g, bool tf32) {
     if (ef != cudaSuccess) return cuda_err(c, ef, "map table: stage");
     c->launches += 1;
   }
+  table_guard.armed = false;
   rc = ring_commit(c, h, dv, staged);  // (its event, recorded after both copies, frees the ring half)
   if (rc) return rc;
   for (const RelBias& r : rb) {
