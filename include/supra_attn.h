@@ -103,7 +103,9 @@ typedef struct supra_attn_desc {
 
 /* ---- context ----------------------------------------------------------------------------- */
 /* Replaces GPU.create (app/gpu/device.js:92-118): binds a context to a CUDA device and
- * creates its stream, descriptor ring and device status word. */
+ * creates its stream, descriptor ring and device status word. Its first attention flush adds a
+ * device table of TMA tensor maps (2 MiB, kept for the context's life; larger only if one flush
+ * needs more than 16384 maps). */
 SUPRA_ATTN_API int supra_attn_create(int device, supra_attn_ctx** out);
 /* Flushes, synchronises and frees everything the context owns. NULL is a no-op. */
 SUPRA_ATTN_API int supra_attn_destroy(supra_attn_ctx* ctx);
